@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Planner benchmark: plan steps/s, candidate-steps/s and p50/p95 plan latency.
+
+Default workload: SkyJEPA learned MPPI, one vehicle, 512 candidates x 15
+steps, latent/GRU 256, state TCN [128,128,128], action TCN [4,4,4], prober
+32 x 2, f32, seeded random weights and synthetic context (figure-eight
+reference).  A "step" is one plan call.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload skyjepa|nominal]
+    python bench.py --impl reference ...   # the CPU restatement on the host cores
+
+`value` is timed with CUDA events around each plan on the device with the
+context resident (L2 flushed between steps); `e2e` times the public C-ABI
+calls with host buffers (context upload + plan + result download).  With
+--gpus N every rank plans its own vehicle ("replicas only": one vehicle's
+512-candidate plan does not shard) and `value` is the job-wide plans/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "le-wm-nv_b200"))
+
+# Algorithmic work per candidate-step (op count of the model; see the
+# workload notes in the design document): GRU 4x768 + 256x768 MAC, action TCN
+# 2,880 MAC, prober 9,696 MAC, integrator + cost ~200 FLOP.
+FLOP_PER_CANDIDATE_STEP = {
+    "skyjepa": 2 * (4 * 768 + 256 * 768 + 2880 + 256 * 32 + 32 * 32 + 32 * 15) + 200,
+    "nominal": 10 * 262 + 60,
+}
+
+
+def percentile(values, q):
+    """values[round((n-1) q)] of the sorted list (lewm-bench-skyjepa.rs:547-553)."""
+    v = sorted(values)
+    return v[int(round((len(v) - 1) * q))] if v else 0.0
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def sgemm_peak_tflops(torch):
+    """FP32 CUDA-core GEMM throughput (cuBLAS SGEMM, TF32 off), measured here:
+    the denominator for FP32 FFMA kernels (MEASURED_PEAKS has HBM and bf16 only)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(2):
+        torch.matmul(a, b)
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+# ----------------------------------------------------------------- our arm
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import lewm_b200 as L
+    from lewm_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    ctx = L.Context(local_rank)
+    stream = ctx.torch_stream()
+    kind = args.workload
+    seed = 17 + rank
+    if kind == "skyjepa":
+        w = W.skyjepa(seed=seed)
+        sc = L.SkyJepaScorer(ctx, w.model, w.weights, w.state_mean, w.state_std, w.action_mean, w.action_std, w.cost,
+                             w.dt)
+        set_ctx = lambda: sc.set_context(w.state_history, w.action_history, w.reference_states, w.reference_actions)
+        h2d = (w.state_history.nbytes + w.action_history.nbytes + w.reference_states.nbytes +
+               w.reference_actions.nbytes)
+    else:
+        w = W.nominal(seed=seed)
+        sc = L.NominalScorer(ctx, w.dt, w.trim, w.cost, w.substeps)
+        set_ctx = lambda: sc.set_context(w.initial, w.motors, w.reference_states, w.reference_actions)
+        h2d = w.initial.nbytes + w.motors.nbytes + w.reference_states.nbytes + w.reference_actions.nbytes
+    set_ctx()
+    planner = L.MppiPlanner(ctx, w.mppi)
+    planner.set_warm_start_sequence(w.warm_start)
+    S, T = w.samples, w.horizon
+    cand_steps = w.batch * S * T * w.mppi.iterations
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")  # > 126 MB L2
+
+    def flush_l2():
+        with torch.cuda.stream(stream):
+            flush.add_(1.0)
+
+    # ---- device-resident timing (value)
+    for _ in range(args.warmup):
+        planner.plan_device(sc)
+    ctx.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = ctx.launch_count()
+    times = []
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        for _ in range(args.steps):
+            flush_l2()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            planner.plan_device(sc)
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = (ctx.launch_count() - n0) // args.steps
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---- end to end through the public ABI (host context in, host result out)
+    e2e_times = []
+    for _ in range(args.warmup):
+        set_ctx()
+        planner.plan(sc)
+    for _ in range(args.steps):
+        flush_l2()
+        ctx.synchronize()
+        t0 = time.perf_counter()
+        set_ctx()
+        r = planner.plan(sc)
+        e2e_times.append((time.perf_counter() - t0) * 1e3)
+    d2h = 4 * (w.batch * 4 + w.batch * T * 4 + w.batch * S + w.batch)
+
+    # ---- dominant kernel alone (for the roofline): the rollout kernel is
+    # timed as the plan minus the context kernel by the ncu share; here the
+    # plan time bounds it from above.
+    total_ms = sum(times)
+    stats = torch.tensor([total_ms, float(np.mean(e2e_times))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    total_ms, e2e_mean = stats.tolist()
+    result = None
+    if rank == 0:
+        ms = total_ms / args.steps
+        plans_per_s = world * args.steps / (total_ms * 1e-3)
+        e2e_plans_per_s = world * 1e3 / e2e_mean
+        peaks = measured_peaks()
+        sgemm = sgemm_peak_tflops(torch)
+        flop = FLOP_PER_CANDIDATE_STEP[kind] * cand_steps
+        achieved = flop / (percentile(times, 0.5) * 1e-3) / 1e12
+        result = {
+            "metric": "plan steps/s (one plan of 512 candidates x 15 steps per step); candidate-steps/s and "
+                      "p50/p95 plan latency alongside",
+            "value": round(plans_per_s, 2),
+            "unit": "plans/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, generated figure-eight references)",
+            "config": {"workload": f"{kind} MPPI, 1 vehicle per GPU, 512 candidates x 15 steps, 1 iteration"
+                                   + (", latent 256, TCN [128,128,128]/[4,4,4], prober 32x2" if kind == "skyjepa"
+                                      else ", 10 rotor substeps"),
+                       "parallelism": f"replicas x{world}",
+                       "l2": "flushed between steps (256 MiB write outside the timed region)"},
+            "candidate_steps_per_s": round(plans_per_s * cand_steps, 1),
+            "latency_ms": {"p50": round(percentile(times, 0.5), 5), "p95": round(percentile(times, 0.95), 5),
+                           "p99": round(percentile(times, 0.99), 5), "max": round(max(times), 5)},
+            "e2e": {"value": round(e2e_plans_per_s, 2), "unit": "plans/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h),
+                    "latency_ms": {"p50": round(percentile(e2e_times, 0.5), 5),
+                                   "p95": round(percentile(e2e_times, 0.95), 5)}},
+            "gpu_launches": int(launches * args.steps),
+            "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2),
+                         "unit": "TFLOP/s", "frac": round(achieved / sgemm, 4), "traffic": None,
+                         "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
+                         "note": "achieved = algorithmic FLOP per plan / p50 plan time (both kernels)"},
+            "clocks": clocks.summary(),
+        }
+        if args.cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
+    planner.close()
+    sc.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return result
+
+
+# ----------------------------------------------------------------- CPU arm
+
+def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
+    """The oracle (C restatement of the reference's CPU path) on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from lewm_b200 import workloads as W
+    threads = threads or os.cpu_count() or 1
+    O.set_threads(threads)
+    if kind == "skyjepa":
+        w = W.skyjepa(seed=17)
+        m = O.SkyJepaModel(w.model, w.weights)
+        c = m.score_ctx((w.state_mean, w.state_std, w.action_mean, w.action_std), w.state_history,
+                        w.action_history, w.reference_states, w.reference_actions, w.cost, w.dt)
+        scorer = (O.SKYJEPA_FN, c)
+    else:
+        w = W.nominal(seed=17)
+        scorer = (O.NOMINAL_FN, O.nominal_ctx(w.initial, w.motors, w.reference_states, w.reference_actions, w.cost,
+                                              w.dt, w.trim))
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        O.mppi_plan(w.mppi, 1, scorer, seed=w.mppi.seed, warm_start=w.warm_start)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 200:
+            break
+    mean = float(np.mean(times))
+    return {"value": round(1.0 / mean, 4), "unit": "plans/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} full plans of the same workload (512 x 15, 1 iteration), "
+                      f"oracle C restatement, {threads} OpenMP threads",
+            "latency_ms": {"p50": round(percentile([t * 1e3 for t in times], 0.5), 3),
+                           "p95": round(percentile([t * 1e3 for t in times], 0.95), 3)}}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    base = cpu_baseline(args.workload, args.cpu_seconds)
+    # each timed step is one full plan on the host cores
+    return {
+        "impl": "reference",
+        "metric": "plan steps/s (one plan of 512 candidates x 15 steps per step); candidate-steps/s and "
+                  "p50/p95 plan latency alongside",
+        "value": base["value"],
+        "unit": "plans/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 / base["value"], 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded random-init weights, generated figure-eight references)",
+        "config": {"workload": f"{args.workload} MPPI, 1 vehicle, 512 candidates x 15 steps, 1 iteration",
+                   "parallelism": "host CPU"},
+        "candidate_steps_per_s": round(base["value"] * 512 * 15, 1),
+        "latency_ms": base["latency_ms"],
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["skyjepa", "nominal"], default="skyjepa")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out = run_ours(args, rank, world, local_rank)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,412 @@
+/*
+ * lewm_b200.h — C ABI of the B200-native sampling planner (MPPI / CEM / iCEM)
+ * and its candidate scorers.
+ *
+ * Every entry point replaces one piece of le-wm-nv's Rust planner API; the
+ * comment above each declaration names the reference item (path:line inside
+ * the le-wm-nv project) it stands in for.  Plain pointers and sizes only: no
+ * torch, no Candle, no Rust types.  All host pointers are read during the call
+ * and never retained.  Device pointers (the *_device entry points) refer to
+ * memory on the context's device and are used on the context's stream.
+ *
+ * Threading: every handle serialises its calls with an internal mutex.  A
+ * context owns one CUDA stream; work issued through handles created from the
+ * same context is ordered on that stream.
+ *
+ * Errors: every call returns an lwm_status.  On failure a human-readable
+ * message (matching the reference's bail! texts where one exists) is stored in
+ * thread-local storage and returned by lwm_last_error().
+ */
+#ifndef LEWM_B200_H
+#define LEWM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LWM_ABI_VERSION 1
+#define LWM_MAX_ACTION_DIM 16
+#define LWM_TCN_MAX_LEVELS 8
+#define LWM_STATE_DIM 18
+#define LWM_ROTOR_COUNT 4
+
+typedef enum lwm_status {
+    LWM_OK = 0,
+    LWM_INVALID_ARGUMENT = 1,
+    LWM_CUDA_ERROR = 2,
+    LWM_DEADLINE = 3,
+    LWM_NCCL_ERROR = 4,
+    LWM_TIMEOUT = 5,
+    LWM_UNSUPPORTED = 6,
+} lwm_status;
+
+typedef struct lwm_ctx lwm_ctx;
+typedef struct lwm_planner lwm_planner;
+typedef struct lwm_scorer lwm_scorer;
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* lwm_last_error(void);
+/* Library version string and ABI version number. */
+const char* lwm_version(void);
+int lwm_abi_version(void);
+
+/* ---------------------------------------------------------------- context */
+
+/* Device selection: replaces DeviceSpec::Cuda(index) / Device::new_cuda
+ * (src/runtime.rs:7-18).  Creates a non-blocking stream on `device`. */
+lwm_status lwm_ctx_create(int device, lwm_ctx** out);
+lwm_status lwm_ctx_destroy(lwm_ctx* ctx);
+/* The context's cudaStream_t, for callers that interleave their own work. */
+lwm_status lwm_ctx_stream(lwm_ctx* ctx, void** stream_out);
+lwm_status lwm_ctx_synchronize(lwm_ctx* ctx);
+/* Number of kernels this library has launched on the context so far. */
+lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out);
+
+/* ---------------------------------------------------------------- planners */
+
+/* ActionBounds + MppiConfig (src/planner.rs:67-103, 178-254).
+ * deadline_ns < 0 means "no deadline" (Option<Duration>::None). */
+typedef struct lwm_mppi_config {
+    uint32_t horizon;
+    uint32_t samples;
+    uint32_t iterations;
+    uint32_t action_dim;
+    float bounds_low[LWM_MAX_ACTION_DIM];
+    float bounds_high[LWM_MAX_ACTION_DIM];
+    float noise_std;
+    int32_t has_noise_std_per_action;
+    float noise_std_per_action[LWM_MAX_ACTION_DIM];
+    float temperature;
+    int64_t deadline_ns;
+    int32_t has_deadline_action;
+    float deadline_action[LWM_MAX_ACTION_DIM];
+    int32_t has_seed;
+    uint64_t seed;
+} lwm_mppi_config;
+
+/* CemConfig (src/planner.rs:107-176). */
+typedef struct lwm_cem_config {
+    uint32_t horizon;
+    uint32_t samples;
+    uint32_t elites;
+    uint32_t iterations;
+    uint32_t action_dim;
+    float bounds_low[LWM_MAX_ACTION_DIM];
+    float bounds_high[LWM_MAX_ACTION_DIM];
+    float init_std;
+    float min_std;
+    int64_t deadline_ns;
+    int32_t has_deadline_action;
+    float deadline_action[LWM_MAX_ACTION_DIM];
+    int32_t has_seed;
+    uint64_t seed;
+} lwm_cem_config;
+
+/* IcemConfig (src/planner.rs:256-346). */
+typedef struct lwm_icem_config {
+    uint32_t horizon;
+    uint32_t samples;
+    uint32_t elites;
+    uint32_t keep_elites;
+    uint32_t iterations;
+    float noise_beta;
+    float alpha;
+    uint32_t action_dim;
+    float bounds_low[LWM_MAX_ACTION_DIM];
+    float bounds_high[LWM_MAX_ACTION_DIM];
+    float init_std;
+    float min_std;
+    int32_t return_mean;
+    int64_t deadline_ns;
+    int32_t has_deadline_action;
+    float deadline_action[LWM_MAX_ACTION_DIM];
+    int32_t has_seed;
+    uint64_t seed;
+} lwm_icem_config;
+
+/* Defaults of MppiConfig::new / CemConfig::new / IcemConfig::new
+ * (src/planner.rs:193-208, 122-137, 275-295). */
+void lwm_mppi_config_default(uint32_t horizon, uint32_t samples, uint32_t action_dim,
+                             lwm_mppi_config* out);
+void lwm_cem_config_default(uint32_t horizon, uint32_t samples, uint32_t elites,
+                            uint32_t action_dim, lwm_cem_config* out);
+void lwm_icem_config_default(uint32_t horizon, uint32_t samples, uint32_t elites,
+                             uint32_t action_dim, lwm_icem_config* out);
+
+/* MppiPlanner::new / CemPlanner::new / IcemPlanner::new
+ * (src/planner.rs:553-561, 426-433, 741-749).  The configuration is validated
+ * here and again on every plan (the reference validates inside plan_device,
+ * src/planner.rs:451,591,779); the messages are the reference's. */
+lwm_status lwm_mppi_create(lwm_ctx* ctx, const lwm_mppi_config* cfg, lwm_planner** out);
+lwm_status lwm_cem_create(lwm_ctx* ctx, const lwm_cem_config* cfg, lwm_planner** out);
+lwm_status lwm_icem_create(lwm_ctx* ctx, const lwm_icem_config* cfg, lwm_planner** out);
+lwm_status lwm_planner_destroy(lwm_planner* planner);
+
+/* set_warm_start_sequence / clear_warm_start / warm_start_sequence
+ * (src/planner.rs:571-581, 759-769).  `sequence` is host [batch, horizon,
+ * action_dim] f32.  lwm_planner_warm_start writes *batch_out = 0 when no warm
+ * start is set.  CEM has no warm start (LWM_INVALID_ARGUMENT). */
+lwm_status lwm_planner_set_warm_start(lwm_planner* planner, const float* sequence,
+                                      uint32_t batch, uint32_t horizon, uint32_t action_dim);
+lwm_status lwm_planner_clear_warm_start(lwm_planner* planner);
+lwm_status lwm_planner_warm_start(lwm_planner* planner, float* sequence_out, size_t capacity,
+                                  uint32_t* batch_out);
+/* reset_rng_sequence / rng_offset (src/planner.rs:442-448, 583-589). */
+lwm_status lwm_planner_reset_rng(lwm_planner* planner);
+lwm_status lwm_planner_rng_offset(lwm_planner* planner, uint64_t* out);
+
+/* ---------------------------------------------------------------- scorers */
+
+/* SkyJepaDomain (src/skyjepa_sim.rs:28-56). */
+typedef struct lwm_domain {
+    float mass;
+    float inertia[3];
+    float motor_time_constant;
+    float drag[3];
+    float thrust_scale;
+    float torque_scale;
+    float arm_length;
+    float gravity;
+    float max_thrust_weight;
+} lwm_domain;
+void lwm_domain_default(lwm_domain* out);
+/* SkyJepaDomain::sample (src/skyjepa_sim.rs:61-86), SplitMix64 stream. */
+void lwm_domain_sample(uint64_t seed, lwm_domain* out);
+
+/* SkyJepaTrackingCost (src/models/skyjepa/control.rs:19-37). */
+typedef struct lwm_tracking_cost {
+    float position;
+    float velocity;
+    float attitude;
+    float angular_velocity;
+    float action[LWM_ROTOR_COUNT];
+} lwm_tracking_cost;
+void lwm_tracking_cost_paper(lwm_tracking_cost* out);
+
+/* SkyJepaNominalScorer::new (src/models/skyjepa/control.rs:344-375) with the
+ * rollout of nominal_physics_rollout (src/models/skyjepa/nominal.rs:17-72).
+ * `substeps` is 10 in the reference scorer (control.rs:401); the domain is
+ * SkyJepaDomain::default() there.  `domains` (nullable) gives one domain per
+ * vehicle for fleets; NULL = `domain` for every vehicle. */
+typedef struct lwm_nominal_scorer_config {
+    float dt;
+    float trim_scale;
+    uint32_t substeps;
+    lwm_tracking_cost cost;
+    lwm_domain domain;
+} lwm_nominal_scorer_config;
+lwm_status lwm_scorer_nominal_create(lwm_ctx* ctx, const lwm_nominal_scorer_config* cfg,
+                                     lwm_scorer** out);
+/* Context of one plan: host arrays initial [B,18], motors [B,4],
+ * reference_states [B,T,18], reference_actions [B,T,4]; domains [B] or NULL. */
+lwm_status lwm_scorer_nominal_set_context(lwm_scorer* scorer, uint32_t batch, uint32_t horizon,
+                                          const float* initial, const float* motors,
+                                          const float* reference_states,
+                                          const float* reference_actions,
+                                          const lwm_domain* domains);
+
+/* TemporalConvConfig (src/models/skyjepa/config.rs:9-14). */
+typedef struct lwm_tcn_config {
+    uint32_t input_dim;
+    uint32_t levels;
+    uint32_t channels[LWM_TCN_MAX_LEVELS];
+    uint32_t kernel_size;
+} lwm_tcn_config;
+
+typedef enum lwm_action_space {
+    LWM_ACTION_SPACE_BODY_RATES_THROTTLE = 0,
+    LWM_ACTION_SPACE_ROTOR_FORCES = 1,
+} lwm_action_space;
+
+/* KinematicConfig (src/models/skyjepa/kinematics.rs:18-47). */
+typedef struct lwm_kinematic_config {
+    double mass;
+    double gravity;
+    double hover_throttle;
+    int32_t action_space;
+} lwm_kinematic_config;
+
+/* SkyJepaConfig (src/models/skyjepa/config.rs:45-55) + SkyJepaProberConfig
+ * (src/models/skyjepa/prober.rs:10-16). */
+typedef struct lwm_skyjepa_config {
+    uint32_t state_dim;
+    uint32_t action_dim;
+    uint32_t history_steps;
+    uint32_t rollout_steps;
+    uint32_t latent_dim;
+    lwm_tcn_config state_encoder;
+    lwm_tcn_config action_encoder;
+    uint32_t prober_hidden_dim;
+    uint32_t prober_hidden_layers;
+    lwm_kinematic_config kinematics;
+} lwm_skyjepa_config;
+
+/* SkyJepaConfig::paper_derived (config.rs:59-77) with a rotor-force prober. */
+void lwm_skyjepa_config_paper(lwm_skyjepa_config* out);
+/* The 512-candidate learned-MPPI workload's model: latent/GRU 256, state TCN
+ * [128,128,128], action TCN [4,4,4], prober 32 x 2, rotor forces. */
+void lwm_skyjepa_config_wide(lwm_skyjepa_config* out);
+
+/* Weight blob: one f32 array, tensors concatenated in this order, each
+ * row-major with the shape of its VarBuilder path (model.rs:25-38, tcn.rs,
+ * prober.rs:54-80):
+ *   state_encoder.blocks.{l}.conv1.weight [C_l, C_{l-1}, K] .conv1.bias [C_l]
+ *   state_encoder.blocks.{l}.conv2.weight [C_l, C_l, K]     .conv2.bias [C_l]
+ *   state_encoder.blocks.{l}.residual.weight [C_l, C_{l-1}, 1] .residual.bias
+ *       (only when C_{l-1} != C_l)
+ *   state_projection.weight [latent, C_last] .bias [latent]
+ *   action_encoder.blocks.{l}.*  (as above)
+ *   predictor.weight_ih_l0 [3*latent, E] .weight_hh_l0 [3*latent, latent]
+ *   predictor.bias_ih_l0 [3*latent] .bias_hh_l0 [3*latent]
+ *   prober.input.weight [hid, latent] .bias [hid]
+ *   prober.hidden.{i}.weight [hid, hid] .bias [hid]   (hidden_layers - 1 times)
+ *   prober.output.weight [15, hid] .bias [15]
+ * Returns the element count, or 0 for an invalid configuration. */
+size_t lwm_skyjepa_weight_count(const lwm_skyjepa_config* cfg);
+/* Seeded random initialisation with Candle's default init families:
+ * Kaiming-normal conv/linear weights, U(+-1/sqrt(fan_in)) biases,
+ * Kaiming-uniform GRU weights with zero biases, N(0, 1e-3) prober output
+ * weight with zero bias.  Deterministic for (cfg, seed). */
+lwm_status lwm_skyjepa_random_weights(const lwm_skyjepa_config* cfg, uint64_t seed,
+                                      float* out, size_t count);
+
+/* SkyJepaMppiScorer::new (src/models/skyjepa/control.rs:163-240).  Copies
+ * the weights to the device once.  Normalisation stats are mean/std of length
+ * state_dim and action_dim (SkyJepaNormalization, data/skyjepa.rs:175-178). */
+lwm_status lwm_scorer_skyjepa_create(lwm_ctx* ctx, const lwm_skyjepa_config* cfg,
+                                     const float* weights, size_t weight_count,
+                                     const float* state_mean, const float* state_std,
+                                     const float* action_mean, const float* action_std,
+                                     const lwm_tracking_cost* cost, float dt,
+                                     lwm_scorer** out);
+/* Per-plan context (control.rs:163-240 arguments): host arrays
+ * state_history [B,H,18], action_history [B,H-1,4], reference_states [B,T,18],
+ * reference_actions [B,T,4].  Uploaded with one H2D copy. */
+lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* scorer, uint32_t batch, uint32_t horizon,
+                                          const float* state_history,
+                                          const float* action_history,
+                                          const float* reference_states,
+                                          const float* reference_actions);
+
+/* A scorer supplied by the caller: the CandidateScorer trait
+ * (src/planner.rs:25-32).  The callback receives device pointers on the
+ * context's stream: candidates [B,S,T,A] f32 and scores [B,S] f32 to fill,
+ * and returns 0 on success. */
+typedef int (*lwm_score_fn)(void* user, const float* candidates, uint32_t batch,
+                            uint32_t samples, uint32_t horizon, uint32_t action_dim,
+                            float* scores, void* stream);
+lwm_status lwm_scorer_callback_create(lwm_ctx* ctx, uint32_t batch, lwm_score_fn fn, void* user,
+                                      lwm_scorer** out);
+
+/* CandidateScorer::score_candidates (src/planner.rs:31) on device buffers:
+ * candidates [B,S,T,A], scores [B,S].  Asynchronous on the context stream. */
+lwm_status lwm_scorer_score_device(lwm_scorer* scorer, const float* candidates, uint32_t batch,
+                                   uint32_t samples, uint32_t horizon, uint32_t action_dim,
+                                   float* scores);
+/* SkyJepaMppiScorer::predict_candidates / SkyJepaNominalScorer::
+ * predict_metric_candidates (control.rs:246-290, 377-406): device candidates
+ * [B,S,T,4] -> device states [B,S,T,18]. */
+lwm_status lwm_scorer_predict_device(lwm_scorer* scorer, const float* candidates, uint32_t batch,
+                                     uint32_t samples, uint32_t horizon, float* states);
+lwm_status lwm_scorer_destroy(lwm_scorer* scorer);
+
+/* ---------------------------------------------------------------- planning */
+
+/* PlanDeadlineOutcome (src/planner.rs:348-353). */
+typedef enum lwm_deadline_outcome {
+    LWM_DEADLINE_NONE = 0,
+    LWM_DEADLINE_WARM_START = 1,
+    LWM_DEADLINE_CONFIGURED_ACTION = 2,
+} lwm_deadline_outcome;
+
+/* PlanResult (src/planner.rs:355-366) in caller-owned host buffers:
+ * first_action [B*A], sequence [B*T*A], scores [B*scores_cols],
+ * best_indices [B].  Any pointer may be NULL to skip that copy.
+ * `scores_capacity` is the element capacity of `scores`. */
+typedef struct lwm_plan_result {
+    float* first_action;
+    float* sequence;
+    float* scores;
+    size_t scores_capacity;
+    uint32_t* best_indices;
+    uint32_t batch;
+    uint32_t scores_cols;
+    uint32_t iterations_completed;
+    uint64_t elapsed_ns;
+    int32_t deadline_reached;
+    int32_t deadline_outcome;
+} lwm_plan_result;
+
+/* PlanDeviceResult (src/planner.rs:368-379): device pointers owned by the
+ * planner, valid until its next plan call. */
+typedef struct lwm_plan_device_result {
+    const float* first_action;
+    const float* sequence;
+    const float* scores;
+    const uint32_t* best_indices;
+    uint32_t batch;
+    uint32_t scores_cols;
+    uint32_t iterations_completed;
+    uint64_t elapsed_ns;
+    int32_t deadline_reached;
+    int32_t deadline_outcome;
+} lwm_plan_device_result;
+
+/* plan (src/planner.rs:446-448, 586-588, 774-776): runs every iteration and
+ * copies the result to host buffers (the only device synchronisation).
+ * `injected_noise` (host, nullable) replaces the seeded sampler with fixed
+ * standard-normal draws [iterations, B, S, T, A] — the parity hook. */
+lwm_status lwm_plan(lwm_planner* planner, lwm_scorer* scorer, const float* injected_noise,
+                    lwm_plan_result* out);
+/* plan_device (src/planner.rs:450, 590, 778): asynchronous; results stay on
+ * the device.  `injected_noise` is a device pointer or NULL. */
+lwm_status lwm_plan_device(lwm_planner* planner, lwm_scorer* scorer,
+                           const float* injected_noise, lwm_plan_device_result* out);
+
+/* Device copy of the candidates of the last iteration [B,S,T,A] (a debugging
+ * and parity hook with no reference counterpart in the public API). */
+lwm_status lwm_planner_last_candidates(lwm_planner* planner, const float** candidates_device,
+                                       uint32_t* samples_out);
+
+/* ---------------------------------------------------------------- planner pieces
+ * Device-buffer entry points for the building blocks the planners use; each
+ * mirrors one private function of src/planner.rs and exists so that callers
+ * with their own loop (and the parity tests) can run them alone. */
+
+/* lowest_score_indices (src/planner.rs:1647-1659 and kernel :1793-1850):
+ * ascending, NaN ranks as +inf, ties to the lower index; any sample count. */
+lwm_status lwm_lowest_k_device(lwm_ctx* ctx, const float* scores, uint32_t batch,
+                               uint32_t samples, uint32_t count, uint32_t* indices);
+/* color_temporal_noise (src/planner.rs:1516-1586, kernel :1852-1896). */
+lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, uint32_t batch,
+                                  uint32_t samples, uint32_t horizon, uint32_t action_dim,
+                                  float noise_beta);
+/* Seeded standard normals: draw i of stream (seed) is element i - offset of
+ * `out`; the sampler the planners use. */
+lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count,
+                             float* out);
+
+/* ---------------------------------------------------------------- task inputs */
+
+/* skyjepa_reference_horizon (src/skyjepa_task.rs:44-55): kind 0 hover,
+ * 1 circle, 2 figure-eight; out [horizon, 18]. */
+lwm_status lwm_skyjepa_reference_horizon(int32_t kind, float time, float dt, uint32_t horizon,
+                                         float radius, float period, float* out);
+/* skyjepa_geometric_action_prior (src/skyjepa_task.rs:118-162):
+ * current_state [18], references [horizon, 18] -> out [horizon, 4]. */
+lwm_status lwm_skyjepa_geometric_prior(const float* current_state, const float* references,
+                                       uint32_t horizon, float dt, const lwm_domain* domain,
+                                       float* out);
+/* One SkyJepaRotorPlant::step (src/skyjepa_sim.rs:206-270) on the host:
+ * state [18] and motors [4] are updated in place. */
+lwm_status lwm_rotor_plant_step(const lwm_domain* domain, float* state, float* motors,
+                                const float* commanded_forces, float dt);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEWM_B200_H */

@@ -1,0 +1,1262 @@
+// api.cpp — the C ABI (include/lewm_b200.h): contexts, planners (MPPI, CEM,
+// iCEM) and candidate scorers, written as C++ objects that mirror the
+// reference's Rust types (src/planner.rs, src/models/skyjepa/control.rs).
+//
+// Nothing here computes on the host except validation and bookkeeping; every
+// numeric step is a kernel launch on the context's stream, and the only
+// device synchronisation is in lwm_plan (the result copy to host memory).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <charconv>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/lewm_b200.h"
+#include "lwm_kernels.hpp"
+
+using lwm::MppiArgs;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+lwm_status fail(lwm_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+// Rust's `{}` formatting of an f32: shortest round-trip digits, no exponent.
+std::string fmt(float v) {
+    if (std::isnan(v)) return "NaN";
+    if (std::isinf(v)) return v > 0 ? "inf" : "-inf";
+    char buf[64];
+    auto r = std::to_chars(buf, buf + sizeof buf, v, std::chars_format::fixed);
+    return std::string(buf, r.ptr);
+}
+
+bool finite(float v) { return std::isfinite(v); }
+
+#define LWM_CUDA(expr)                                                                      \
+    do {                                                                                    \
+        cudaError_t e_ = (expr);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return fail(LWM_CUDA_ERROR, std::string(#expr) + " failed: " + cudaGetErrorString(e_)); \
+    } while (0)
+
+#define LWM_TRY(expr)                       \
+    do {                                    \
+        lwm_status s_ = (expr);             \
+        if (s_ != LWM_OK) return s_;        \
+    } while (0)
+
+// Device allocation that only grows.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    lwm_status ensure(size_t need) {
+        if (need <= bytes) return LWM_OK;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&ptr, need);
+        if (e != cudaSuccess) return fail(LWM_CUDA_ERROR, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+        bytes = need;
+        return LWM_OK;
+    }
+    template <class T> T* as() const { return static_cast<T*>(ptr); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+// Pinned host staging that only grows.
+struct HostBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    lwm_status ensure(size_t need) {
+        if (need <= bytes) return LWM_OK;
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMallocHost(&ptr, need);
+        if (e != cudaSuccess) return fail(LWM_CUDA_ERROR, std::string("cudaMallocHost failed: ") + cudaGetErrorString(e));
+        bytes = need;
+        return LWM_OK;
+    }
+    template <class T> T* as() const { return static_cast<T*>(ptr); }
+    void release() {
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+uint64_t round_even(uint64_t n) { return (n % 2 == 0) ? n : n + 1; }
+
+}  // namespace
+
+struct lwm_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::atomic<uint64_t> launches{0};
+    uint64_t unseeded_seed = 0;
+    std::atomic<uint64_t> unseeded_offset{0};
+};
+
+enum class PlannerKind { Mppi, Cem, Icem };
+enum class ScorerKind { Nominal, Skyjepa, Callback };
+
+struct lwm_scorer {
+    lwm_ctx* ctx = nullptr;
+    ScorerKind kind = ScorerKind::Callback;
+    std::mutex mu;
+    uint32_t batch = 0, horizon = 0;
+    bool has_context = false;
+    // nominal
+    lwm_nominal_scorer_config nominal{};
+    // skyjepa
+    lwm_skyjepa_config sky{};
+    lwm::SkyjepaArgs sky_args{};  // weight views + constants, context pointers set per plan
+    DevBuf weights;
+    DevBuf h0;
+    lwm_tracking_cost cost{};
+    float dt = 0.05f;
+    // context (device) and its pinned staging
+    DevBuf ctx_dev;
+    HostBuf ctx_host;
+    cudaEvent_t staged = nullptr;
+    size_t off_initial = 0, off_motors = 0, off_ref_states = 0, off_ref_actions = 0, off_domains = 0;
+    size_t off_state_hist = 0, off_action_hist = 0;
+    // callback
+    lwm_score_fn fn = nullptr;
+    void* user = nullptr;
+};
+
+struct lwm_planner {
+    lwm_ctx* ctx = nullptr;
+    PlannerKind kind = PlannerKind::Mppi;
+    std::mutex mu;
+    lwm_mppi_config mppi{};
+    lwm_cem_config cem{};
+    lwm_icem_config icem{};
+    uint32_t T = 0, S = 0, A = 0, iterations = 0;
+    std::atomic<uint64_t> rng_offset{0};
+    bool has_warm = false;
+    uint32_t warm_batch = 0;
+    // device state, sized for `cap_b` vehicles
+    uint32_t cap_b = 0;
+    DevBuf bounds, zeros, std_init, mean, stdv, cand, scores, partials, counters, sequence, first_action, warm,
+        best, best_score, carried, noise_tmp;
+    HostBuf staging;
+    uint32_t last_batch = 0, last_cols = 0;
+    bool has_result = false;
+};
+
+namespace {
+
+const char* planner_name(PlannerKind k) {
+    return k == PlannerKind::Mppi ? "MPPI" : (k == PlannerKind::Cem ? "CEM" : "iCEM");
+}
+
+// ActionBounds::validate (src/planner.rs:85-103).
+lwm_status validate_bounds(const float* low, const float* high, uint32_t action_dim) {
+    for (uint32_t i = 0; i < action_dim; ++i) {
+        if (!finite(low[i]) || !finite(high[i])) return fail(LWM_INVALID_ARGUMENT, "action bound " + std::to_string(i) + " is not finite");
+        if (low[i] > high[i])
+            return fail(LWM_INVALID_ARGUMENT, "action bound " + std::to_string(i) + " has low " + fmt(low[i]) +
+                                                  " greater than high " + fmt(high[i]));
+    }
+    return LWM_OK;
+}
+
+// validate_deadline_action (src/planner.rs:1060-1089).
+lwm_status validate_deadline(int32_t has, const float* action, uint32_t action_dim, const float* low, const float* high,
+                             const char* name) {
+    if (!has) return LWM_OK;
+    for (uint32_t i = 0; i < action_dim; ++i) {
+        if (!finite(action[i]))
+            return fail(LWM_INVALID_ARGUMENT, std::string(name) + " deadline_action[" + std::to_string(i) + "] is not finite");
+        if (action[i] < low[i] || action[i] > high[i])
+            return fail(LWM_INVALID_ARGUMENT, std::string(name) + " deadline_action[" + std::to_string(i) + "]=" + fmt(action[i]) +
+                                                  " is outside [" + fmt(low[i]) + ", " + fmt(high[i]) + "]");
+    }
+    return LWM_OK;
+}
+
+lwm_status check_dims(uint32_t horizon, uint32_t action_dim) {
+    if (action_dim > LWM_MAX_ACTION_DIM)
+        return fail(LWM_UNSUPPORTED, "action_dim " + std::to_string(action_dim) + " exceeds the supported maximum of 16");
+    if (horizon > lwm::kMaxHorizon)
+        return fail(LWM_UNSUPPORTED, "horizon " + std::to_string(horizon) + " exceeds the supported maximum of 64");
+    return LWM_OK;
+}
+
+// MppiConfig::validate (src/planner.rs:210-253).
+lwm_status validate_mppi(const lwm_mppi_config& c) {
+    if (c.horizon == 0) return fail(LWM_INVALID_ARGUMENT, "MPPI horizon must be greater than zero");
+    if (c.samples == 0) return fail(LWM_INVALID_ARGUMENT, "MPPI samples must be greater than zero");
+    if (c.iterations == 0) return fail(LWM_INVALID_ARGUMENT, "MPPI iterations must be greater than zero");
+    if (c.action_dim == 0) return fail(LWM_INVALID_ARGUMENT, "MPPI action_dim must be greater than zero");
+    LWM_TRY(check_dims(c.horizon, c.action_dim));
+    if (!finite(c.noise_std) || c.noise_std <= 0.0f)
+        return fail(LWM_INVALID_ARGUMENT, "MPPI noise_std must be finite and greater than zero");
+    if (c.has_noise_std_per_action)
+        for (uint32_t i = 0; i < c.action_dim; ++i)
+            if (!finite(c.noise_std_per_action[i]) || c.noise_std_per_action[i] <= 0.0f)
+                return fail(LWM_INVALID_ARGUMENT, "MPPI per-action noise values must be finite and greater than zero");
+    if (!finite(c.temperature) || c.temperature <= 0.0f)
+        return fail(LWM_INVALID_ARGUMENT, "MPPI temperature must be finite and greater than zero");
+    LWM_TRY(validate_bounds(c.bounds_low, c.bounds_high, c.action_dim));
+    return validate_deadline(c.has_deadline_action, c.deadline_action, c.action_dim, c.bounds_low, c.bounds_high, "MPPI");
+}
+
+// CemConfig::validate (src/planner.rs:139-175).
+lwm_status validate_cem(const lwm_cem_config& c) {
+    if (c.horizon == 0) return fail(LWM_INVALID_ARGUMENT, "CEM horizon must be greater than zero");
+    if (c.samples == 0) return fail(LWM_INVALID_ARGUMENT, "CEM samples must be greater than zero");
+    if (c.elites < 2) return fail(LWM_INVALID_ARGUMENT, "CEM elites must be at least two");
+    if (c.elites > c.samples)
+        return fail(LWM_INVALID_ARGUMENT, "CEM elites " + std::to_string(c.elites) + " cannot exceed samples " + std::to_string(c.samples));
+    if (c.iterations == 0) return fail(LWM_INVALID_ARGUMENT, "CEM iterations must be greater than zero");
+    if (c.action_dim == 0) return fail(LWM_INVALID_ARGUMENT, "CEM action_dim must be greater than zero");
+    LWM_TRY(check_dims(c.horizon, c.action_dim));
+    if (!finite(c.init_std) || c.init_std <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "CEM init_std must be finite and greater than zero");
+    if (!finite(c.min_std) || c.min_std < 0.0f) return fail(LWM_INVALID_ARGUMENT, "CEM min_std must be finite and non-negative");
+    LWM_TRY(validate_bounds(c.bounds_low, c.bounds_high, c.action_dim));
+    return validate_deadline(c.has_deadline_action, c.deadline_action, c.action_dim, c.bounds_low, c.bounds_high, "CEM");
+}
+
+// IcemConfig::validate (src/planner.rs:296-345).
+lwm_status validate_icem(const lwm_icem_config& c) {
+    if (c.horizon == 0) return fail(LWM_INVALID_ARGUMENT, "iCEM horizon must be greater than zero");
+    if (c.samples == 0) return fail(LWM_INVALID_ARGUMENT, "iCEM samples must be greater than zero");
+    if (c.elites < 2) return fail(LWM_INVALID_ARGUMENT, "iCEM elites must be at least two");
+    if (c.elites > c.samples)
+        return fail(LWM_INVALID_ARGUMENT, "iCEM elites " + std::to_string(c.elites) + " cannot exceed samples " +
+                                              std::to_string(c.samples) + " on the first iteration");
+    if (c.keep_elites > c.elites)
+        return fail(LWM_INVALID_ARGUMENT, "iCEM keep_elites " + std::to_string(c.keep_elites) + " cannot exceed elites " +
+                                              std::to_string(c.elites));
+    if (c.iterations == 0) return fail(LWM_INVALID_ARGUMENT, "iCEM iterations must be greater than zero");
+    if (!finite(c.noise_beta) || c.noise_beta < 0.0f) return fail(LWM_INVALID_ARGUMENT, "iCEM noise_beta must be finite and non-negative");
+    if (!finite(c.alpha) || c.alpha < 0.0f || c.alpha > 1.0f) return fail(LWM_INVALID_ARGUMENT, "iCEM alpha must be finite and in [0, 1]");
+    if (c.action_dim == 0) return fail(LWM_INVALID_ARGUMENT, "iCEM action_dim must be greater than zero");
+    LWM_TRY(check_dims(c.horizon, c.action_dim));
+    if (!finite(c.init_std) || c.init_std <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "iCEM init_std must be finite and greater than zero");
+    if (!finite(c.min_std) || c.min_std < 0.0f) return fail(LWM_INVALID_ARGUMENT, "iCEM min_std must be finite and non-negative");
+    LWM_TRY(validate_bounds(c.bounds_low, c.bounds_high, c.action_dim));
+    return validate_deadline(c.has_deadline_action, c.deadline_action, c.action_dim, c.bounds_low, c.bounds_high, "iCEM");
+}
+
+lwm_status validate_planner(const lwm_planner* p) {
+    switch (p->kind) {
+        case PlannerKind::Mppi: return validate_mppi(p->mppi);
+        case PlannerKind::Cem: return validate_cem(p->cem);
+        default: return validate_icem(p->icem);
+    }
+}
+
+const float* planner_low(const lwm_planner* p) {
+    return p->kind == PlannerKind::Mppi ? p->mppi.bounds_low : (p->kind == PlannerKind::Cem ? p->cem.bounds_low : p->icem.bounds_low);
+}
+const float* planner_high(const lwm_planner* p) {
+    return p->kind == PlannerKind::Mppi ? p->mppi.bounds_high : (p->kind == PlannerKind::Cem ? p->cem.bounds_high : p->icem.bounds_high);
+}
+
+lwm::CostParams cost_params(const lwm_tracking_cost& c) {
+    lwm::CostParams p;
+    p.position = c.position;
+    p.velocity = c.velocity;
+    p.attitude = c.attitude;
+    p.angular_velocity = c.angular_velocity;
+    for (int i = 0; i < 4; ++i) p.action[i] = c.action[i];
+    return p;
+}
+
+// SkyJepaTrackingCost::validate (src/models/skyjepa/control.rs:40-63).
+lwm_status validate_cost(const lwm_tracking_cost& c) {
+    const char* names[4] = {"position", "velocity", "attitude", "angular_velocity"};
+    const float vals[4] = {c.position, c.velocity, c.attitude, c.angular_velocity};
+    for (int i = 0; i < 4; ++i)
+        if (!finite(vals[i]) || vals[i] < 0.0f)
+            return fail(LWM_INVALID_ARGUMENT, std::string("SkyJEPA ") + names[i] + " cost must be finite and non-negative");
+    for (int i = 0; i < 4; ++i)
+        if (!finite(c.action[i]) || c.action[i] < 0.0f)
+            return fail(LWM_INVALID_ARGUMENT, "SkyJEPA action costs must be finite and non-negative");
+    return LWM_OK;
+}
+
+// SkyJepaDomain::validate (src/skyjepa_sim.rs:88-123).
+lwm_status validate_domain(const lwm_domain& d) {
+    if (!finite(d.mass) || d.mass <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "mass must be positive");
+    for (int i = 0; i < 3; ++i)
+        if (!finite(d.inertia[i]) || d.inertia[i] <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "inertia must be positive");
+    if (!finite(d.motor_time_constant) || d.motor_time_constant <= 0.0f)
+        return fail(LWM_INVALID_ARGUMENT, "motor time constant must be positive");
+    for (int i = 0; i < 3; ++i)
+        if (!finite(d.drag[i]) || d.drag[i] < 0.0f) return fail(LWM_INVALID_ARGUMENT, "drag must be non-negative");
+    if (!finite(d.thrust_scale) || d.thrust_scale <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "thrust scale must be positive");
+    if (!finite(d.torque_scale) || d.torque_scale <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "torque scale must be positive");
+    if (!finite(d.arm_length) || d.arm_length <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "arm length must be positive");
+    return LWM_OK;
+}
+
+lwm::DomainParams domain_params(const lwm_domain& d) {
+    lwm::DomainParams p;
+    p.mass = d.mass;
+    for (int i = 0; i < 3; ++i) { p.inertia[i] = d.inertia[i]; p.drag[i] = d.drag[i]; }
+    p.tau = d.motor_time_constant;
+    p.thrust_scale = d.thrust_scale;
+    p.torque_scale = d.torque_scale;
+    p.arm = d.arm_length;
+    p.gravity = d.gravity;
+    p.max_tw = d.max_thrust_weight;
+    return p;
+}
+
+// ------------------------------------------------------------- planner state
+
+lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
+    if (B <= p->cap_b && p->cap_b != 0) return LWM_OK;
+    const size_t seq = static_cast<size_t>(B) * p->T * p->A;
+    const size_t n = seq * p->S;
+    uint32_t P = std::max<uint32_t>(lwm::nominal_blocks_per_vehicle(p->S),
+                                    lwm::skyjepa_partials_per_vehicle(p->S, 256));
+    P = std::max<uint32_t>(P, (p->S + 255) / 256);
+    const size_t pw = (4 + static_cast<size_t>(p->T) * p->A + 3) & ~static_cast<size_t>(3);
+    LWM_TRY(p->zeros.ensure(seq * 4));
+    LWM_TRY(p->std_init.ensure(seq * 4));
+    LWM_TRY(p->mean.ensure(seq * 4));
+    LWM_TRY(p->stdv.ensure(seq * 4));
+    LWM_TRY(p->cand.ensure(n * 4));
+    LWM_TRY(p->scores.ensure(static_cast<size_t>(B) * p->S * 4));
+    LWM_TRY(p->partials.ensure(static_cast<size_t>(B) * P * pw * 4));
+    LWM_TRY(p->counters.ensure(static_cast<size_t>(B) * 4));
+    LWM_TRY(p->sequence.ensure(seq * 4));
+    LWM_TRY(p->first_action.ensure(static_cast<size_t>(B) * p->A * 4));
+    // the warm start is kept across plans: preserve it when growing
+    if (p->warm.bytes < seq * 4) {
+        DevBuf grown;
+        LWM_TRY(grown.ensure(seq * 4));
+        if (p->warm.ptr) LWM_CUDA(cudaMemcpyAsync(grown.ptr, p->warm.ptr, p->warm.bytes, cudaMemcpyDeviceToDevice, p->ctx->stream));
+        LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
+        p->warm.release();
+        p->warm = grown;
+    }
+    LWM_TRY(p->best.ensure(static_cast<size_t>(B) * 4));
+    LWM_TRY(p->best_score.ensure(static_cast<size_t>(B) * 4));
+    const uint32_t keep = p->kind == PlannerKind::Icem ? std::max<uint32_t>(p->icem.keep_elites, 1) : 1;
+    LWM_TRY(p->carried.ensure(static_cast<size_t>(B) * keep * p->T * p->A * 4));
+    LWM_TRY(p->bounds.ensure(2 * LWM_MAX_ACTION_DIM * 4));
+    LWM_TRY(p->staging.ensure(seq * 4 * 3 + static_cast<size_t>(B) * p->S * 4 + static_cast<size_t>(B) * 8 + 64));
+    LWM_CUDA(cudaMemsetAsync(p->zeros.ptr, 0, seq * 4, p->ctx->stream));
+    LWM_CUDA(cudaMemsetAsync(p->counters.ptr, 0, static_cast<size_t>(B) * 4, p->ctx->stream));
+    // bounds [low(16), high(16)] and the per-plan initial std, both constant per planner
+    float* h = p->staging.as<float>();
+    std::memcpy(h, planner_low(p), LWM_MAX_ACTION_DIM * 4);
+    std::memcpy(h + LWM_MAX_ACTION_DIM, planner_high(p), LWM_MAX_ACTION_DIM * 4);
+    LWM_CUDA(cudaMemcpyAsync(p->bounds.ptr, h, 2 * LWM_MAX_ACTION_DIM * 4, cudaMemcpyHostToDevice, p->ctx->stream));
+    LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
+    for (size_t i = 0; i < seq; ++i) {
+        const uint32_t a = static_cast<uint32_t>(i % p->A);
+        float v;
+        if (p->kind == PlannerKind::Mppi) v = p->mppi.has_noise_std_per_action ? p->mppi.noise_std_per_action[a] : p->mppi.noise_std;
+        else if (p->kind == PlannerKind::Cem) v = p->cem.init_std;
+        else v = p->icem.init_std;
+        h[i] = v;
+    }
+    LWM_CUDA(cudaMemcpyAsync(p->std_init.ptr, h, seq * 4, cudaMemcpyHostToDevice, p->ctx->stream));
+    LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
+    p->cap_b = B;
+    return LWM_OK;
+}
+
+MppiArgs mppi_args(lwm_planner* p, float temperature) {
+    MppiArgs m{};
+    m.partials = p->partials.as<float>();
+    m.counters = p->counters.as<unsigned int>();
+    m.sequence = p->sequence.as<float>();
+    m.first_action = p->first_action.as<float>();
+    m.warm_start = p->warm.as<float>();
+    m.best_index = p->best.as<uint32_t>();
+    m.best_score = p->best_score.as<float>();
+    m.T = p->T;
+    m.A = p->A;
+    m.pw = static_cast<uint32_t>((4 + static_cast<size_t>(p->T) * p->A + 3) & ~static_cast<size_t>(3));
+    m.mul = static_cast<float>(-(1.0 / static_cast<double>(temperature)));
+    return m;
+}
+
+// -------------------------------------------------------------- scorer calls
+
+lwm::NominalArgs nominal_args(lwm_scorer* sc, uint32_t S) {
+    lwm::NominalArgs a{};
+    a.B = sc->batch;
+    a.S = S;
+    a.T = sc->horizon;
+    a.substeps = sc->nominal.substeps;
+    a.h = sc->nominal.dt / static_cast<float>(sc->nominal.substeps);
+    a.inv_trim = static_cast<float>(1.0 / static_cast<double>(sc->nominal.trim_scale));
+    const char* base = sc->ctx_dev.as<char>();
+    a.domains = reinterpret_cast<const lwm::DomainParams*>(base + sc->off_domains);
+    a.initial = reinterpret_cast<const float*>(base + sc->off_initial);
+    a.motors = reinterpret_cast<const float*>(base + sc->off_motors);
+    a.ref_states = reinterpret_cast<const float*>(base + sc->off_ref_states);
+    a.ref_actions = reinterpret_cast<const float*>(base + sc->off_ref_actions);
+    a.cost = cost_params(sc->nominal.cost);
+    return a;
+}
+
+lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
+    lwm::SkyjepaArgs a = sc->sky_args;
+    a.B = sc->batch;
+    a.S = S;
+    a.T = sc->horizon;
+    const char* base = sc->ctx_dev.as<char>();
+    a.state_hist = reinterpret_cast<const float*>(base + sc->off_state_hist);
+    a.action_hist = reinterpret_cast<const float*>(base + sc->off_action_hist);
+    a.ref_states = reinterpret_cast<const float*>(base + sc->off_ref_states);
+    a.ref_actions = reinterpret_cast<const float*>(base + sc->off_ref_actions);
+    a.h0 = sc->h0.as<float>();
+    a.use_pdl = 1;
+    return a;
+}
+
+lwm_status check_scorer_shape(lwm_scorer* sc, uint32_t B, uint32_t T, uint32_t A) {
+    if (!sc->has_context && sc->kind != ScorerKind::Callback)
+        return fail(LWM_INVALID_ARGUMENT, "scorer context has not been set");
+    if (sc->kind == ScorerKind::Nominal) {
+        if (B != sc->batch || T != sc->horizon || A != 4) return fail(LWM_INVALID_ARGUMENT, "nominal candidate shape mismatch");
+    } else if (sc->kind == ScorerKind::Skyjepa) {
+        if (B != sc->batch || T != sc->horizon || A != 4)
+            return fail(LWM_INVALID_ARGUMENT, "SkyJEPA candidate actions [" + std::to_string(B) + ", S, " + std::to_string(T) + ", " +
+                                                  std::to_string(A) + "] do not match batch=" + std::to_string(sc->batch) +
+                                                  ", horizon=" + std::to_string(sc->horizon) + ", action_dim=4");
+    } else if (B != sc->batch) {
+        return fail(LWM_INVALID_ARGUMENT, "callback scorer batch mismatch");
+    }
+    return LWM_OK;
+}
+
+// CandidateScorer::score_candidates on device buffers (no sampling, no MPPI).
+lwm_status score_device(lwm_scorer* sc, const float* cand, uint32_t B, uint32_t S, uint32_t T, uint32_t A, float* scores,
+                        float* states) {
+    LWM_TRY(check_scorer_shape(sc, B, T, A));
+    cudaStream_t stream = sc->ctx->stream;
+    if (sc->kind == ScorerKind::Nominal) {
+        lwm::NominalArgs a = nominal_args(sc, S);
+        a.sample = 0;
+        a.cand_in = cand;
+        a.scores = scores;
+        a.states = states;
+        a.mppi = 0;
+        LWM_CUDA(lwm::launch_nominal(a, stream));
+        sc->ctx->launches += 1;
+    } else if (sc->kind == ScorerKind::Skyjepa) {
+        lwm::SkyjepaArgs a = skyjepa_args(sc, S);
+        a.sample = 0;
+        a.cand_in = cand;
+        a.scores = scores;
+        a.states = states;
+        a.mppi = 0;
+        int n = 0;
+        LWM_CUDA(lwm::launch_skyjepa(a, stream, &n));
+        sc->ctx->launches += static_cast<uint64_t>(n);
+    } else {
+        if (states) return fail(LWM_UNSUPPORTED, "callback scorers do not predict states");
+        const int rc = sc->fn(sc->user, cand, B, S, T, A, scores, stream);
+        if (rc != 0) return fail(LWM_INVALID_ARGUMENT, "candidate scorer callback failed with code " + std::to_string(rc));
+    }
+    return LWM_OK;
+}
+
+// ------------------------------------------------------------------ planning
+
+lwm_status deadline_result(lwm_planner* p, uint32_t B, bool use_warm, const char* name, lwm_plan_device_result* out,
+                           std::chrono::steady_clock::time_point start) {
+    const size_t seq = static_cast<size_t>(B) * p->T * p->A;
+    cudaStream_t stream = p->ctx->stream;
+    int outcome;
+    if (use_warm) {
+        LWM_CUDA(cudaMemcpyAsync(p->sequence.ptr, p->warm.ptr, seq * 4, cudaMemcpyDeviceToDevice, stream));
+        outcome = LWM_DEADLINE_WARM_START;
+    } else {
+        const float* action = p->kind == PlannerKind::Mppi ? p->mppi.deadline_action
+                              : (p->kind == PlannerKind::Cem ? p->cem.deadline_action : p->icem.deadline_action);
+        const int32_t has = p->kind == PlannerKind::Mppi ? p->mppi.has_deadline_action
+                            : (p->kind == PlannerKind::Cem ? p->cem.has_deadline_action : p->icem.has_deadline_action);
+        if (!has)
+            return fail(LWM_DEADLINE, std::string(name) +
+                                          " deadline reached before any iteration completed and no deadline_action is configured");
+        LWM_CUDA(cudaStreamSynchronize(stream));
+        float* h = p->staging.as<float>();
+        for (size_t i = 0; i < seq; ++i) h[i] = action[i % p->A];
+        LWM_CUDA(cudaMemcpyAsync(p->sequence.ptr, h, seq * 4, cudaMemcpyHostToDevice, stream));
+        outcome = LWM_DEADLINE_CONFIGURED_ACTION;
+    }
+    // first_action = sequence[:, 0, :]; scores and indices [B, 1] of zeros
+    LWM_CUDA(cudaMemcpy2DAsync(p->first_action.ptr, p->A * 4, p->sequence.ptr, static_cast<size_t>(p->T) * p->A * 4, p->A * 4, B,
+                               cudaMemcpyDeviceToDevice, stream));
+    LWM_CUDA(cudaMemsetAsync(p->scores.ptr, 0, static_cast<size_t>(B) * 4, stream));
+    LWM_CUDA(cudaMemsetAsync(p->best.ptr, 0, static_cast<size_t>(B) * 4, stream));
+    LWM_CUDA(cudaStreamSynchronize(stream));  // the staging buffer is reused by the next call
+    out->first_action = p->first_action.as<float>();
+    out->sequence = p->sequence.as<float>();
+    out->scores = p->scores.as<float>();
+    out->best_indices = p->best.as<uint32_t>();
+    out->batch = B;
+    out->scores_cols = 1;
+    out->iterations_completed = 0;
+    out->deadline_reached = 1;
+    out->deadline_outcome = outcome;
+    out->elapsed_ns = static_cast<uint64_t>(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count());
+    p->last_batch = B;
+    p->last_cols = 1;
+    p->has_result = true;
+    return LWM_OK;
+}
+
+lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
+    const auto start = std::chrono::steady_clock::now();
+    LWM_TRY(validate_planner(p));
+    const uint32_t B = sc->batch;
+    if (B == 0) return fail(LWM_INVALID_ARGUMENT, "scorer batch is zero (set its context first)");
+    LWM_TRY(check_scorer_shape(sc, B, p->T, p->A));
+    LWM_TRY(ensure_planner_buffers(p, B));
+    cudaStream_t stream = p->ctx->stream;
+    const char* name = planner_name(p->kind);
+    if (p->kind != PlannerKind::Cem && p->has_warm && p->warm_batch != B)
+        return fail(LWM_INVALID_ARGUMENT, std::string(name) + " warm-start shape [" + std::to_string(p->warm_batch) + ", " +
+                                              std::to_string(p->T) + ", " + std::to_string(p->A) + "] does not match expected [" +
+                                              std::to_string(B) + ", " + std::to_string(p->T) + ", " + std::to_string(p->A) + "]");
+    const size_t n = static_cast<size_t>(B) * p->S * p->T * p->A;
+    const uint64_t per_iter = round_even(n);
+    const bool seeded = p->kind == PlannerKind::Mppi ? p->mppi.has_seed
+                        : (p->kind == PlannerKind::Cem ? p->cem.has_seed : p->icem.has_seed);
+    const uint64_t seed = seeded ? (p->kind == PlannerKind::Mppi ? p->mppi.seed : (p->kind == PlannerKind::Cem ? p->cem.seed : p->icem.seed))
+                                 : p->ctx->unseeded_seed;
+    const uint64_t reserve = std::max<uint64_t>(per_iter * p->iterations, 1);
+    // PlannerRng::reserve_offset (src/planner.rs:1415-1422)
+    uint64_t offset;
+    if (seeded) {
+        uint64_t cur = p->rng_offset.load();
+        do {
+            if (cur > UINT64_MAX - reserve) return fail(LWM_INVALID_ARGUMENT, "planner CUDA RNG offset overflowed");
+        } while (!p->rng_offset.compare_exchange_weak(cur, cur + reserve));
+        offset = cur;
+    } else {
+        offset = p->ctx->unseeded_offset.fetch_add(reserve);
+    }
+    const int64_t deadline_ns = p->kind == PlannerKind::Mppi ? p->mppi.deadline_ns
+                                : (p->kind == PlannerKind::Cem ? p->cem.deadline_ns : p->icem.deadline_ns);
+    const float* low = p->bounds.as<float>();
+    const float* high = low + LWM_MAX_ACTION_DIM;
+    const size_t seq = static_cast<size_t>(B) * p->T * p->A;
+    // initial mean and std
+    const float* mean_in = (p->kind != PlannerKind::Cem && p->has_warm) ? p->warm.as<float>() : p->zeros.as<float>();
+    if (p->kind != PlannerKind::Mppi) {
+        LWM_CUDA(cudaMemcpyAsync(p->mean.ptr, mean_in, seq * 4, cudaMemcpyDeviceToDevice, stream));
+        LWM_CUDA(cudaMemcpyAsync(p->stdv.ptr, p->std_init.ptr, seq * 4, cudaMemcpyDeviceToDevice, stream));
+    }
+    uint32_t completed = 0;
+    bool deadline_hit = false;
+    MppiArgs m = mppi_args(p, p->kind == PlannerKind::Mppi ? p->mppi.temperature : 1.0f);
+    const uint32_t carried_keep = p->kind == PlannerKind::Icem ? p->icem.keep_elites : 0;
+    for (uint32_t it = 0; it < p->iterations; ++it) {
+        if (deadline_ns >= 0) {
+            const auto el = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count();
+            if (el >= deadline_ns) {
+                deadline_hit = true;
+                if (it == 0) return deadline_result(p, B, p->kind != PlannerKind::Cem && p->has_warm, name, out, start);
+                break;
+            }
+        }
+        const float* noise = injected ? injected + static_cast<size_t>(it) * n : nullptr;
+        const uint64_t it_offset = offset + static_cast<uint64_t>(it) * per_iter;
+        if (p->kind == PlannerKind::Mppi && sc->kind != ScorerKind::Callback) {
+            const float* mean_it = (it == 0) ? mean_in : p->sequence.as<float>();
+            if (sc->kind == ScorerKind::Nominal) {
+                lwm::NominalArgs a = nominal_args(sc, p->S);
+                a.sample = 1;
+                a.mean = mean_it;
+                a.std = p->std_init.as<float>();
+                for (int i = 0; i < 4; ++i) { a.low[i] = planner_low(p)[i]; a.high[i] = planner_high(p)[i]; }
+                a.noise = noise;
+                a.seed = seed;
+                a.offset = it_offset;
+                a.cand_out = p->cand.as<float>();
+                a.scores = p->scores.as<float>();
+                a.mppi = 1;
+                a.m = m;
+                a.m.P = lwm::nominal_blocks_per_vehicle(p->S);
+                LWM_CUDA(lwm::launch_nominal(a, stream));
+                p->ctx->launches += 1;
+            } else {
+                lwm::SkyjepaArgs a = skyjepa_args(sc, p->S);
+                a.sample = 1;
+                a.mean = mean_it;
+                a.std = p->std_init.as<float>();
+                for (int i = 0; i < 4; ++i) { a.low[i] = planner_low(p)[i]; a.high[i] = planner_high(p)[i]; }
+                a.noise = noise;
+                a.seed = seed;
+                a.offset = it_offset;
+                a.cand_out = p->cand.as<float>();
+                a.scores = p->scores.as<float>();
+                a.mppi = 1;
+                a.m = m;
+                a.m.P = lwm::skyjepa_partials_per_vehicle(p->S, a.H);
+                int launched = 0;
+                LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
+                p->ctx->launches += static_cast<uint64_t>(launched);
+            }
+        } else {
+            // sample -> score -> reduce (MPPI) / top-k refit (CEM, iCEM)
+            lwm::SampleArgs s{};
+            s.B = B; s.S = p->S; s.T = p->T; s.A = p->A;
+            s.mean = (p->kind == PlannerKind::Mppi) ? ((it == 0) ? mean_in : p->sequence.as<float>()) : p->mean.as<float>();
+            s.std = (p->kind == PlannerKind::Mppi) ? p->std_init.as<float>() : p->stdv.as<float>();
+            s.low = low;
+            s.high = high;
+            s.noise = noise;
+            s.seed = seed;
+            s.offset = it_offset;
+            s.smooth = 0.0f;
+            if (p->kind == PlannerKind::Icem && p->icem.noise_beta != 0.0f) {
+                float smooth = p->icem.noise_beta / (p->icem.noise_beta + 1.0f);
+                smooth = std::min(std::max(smooth, 0.0f), 0.98f);
+                s.smooth = smooth;
+            }
+            if (p->kind == PlannerKind::Icem && it > 0 && carried_keep > 0) {
+                s.carried = p->carried.as<float>();
+                s.carried_count = carried_keep;
+                s.inject = std::min(carried_keep, p->S - 1);
+            }
+            s.out = p->cand.as<float>();
+            LWM_CUDA(lwm::launch_sample(s, stream));
+            p->ctx->launches += 1;
+            LWM_TRY(score_device(sc, p->cand.as<float>(), B, p->S, p->T, p->A, p->scores.as<float>(), nullptr));
+            if (p->kind == PlannerKind::Mppi) {
+                MppiArgs mm = m;
+                mm.P = (p->S + 255) / 256;
+                LWM_CUDA(lwm::launch_mppi_reduce(mm, p->cand.as<float>(), p->scores.as<float>(), B, p->S, stream));
+                p->ctx->launches += 1;
+            } else {
+                lwm::RefitArgs r{};
+                r.S = p->S; r.T = p->T; r.A = p->A;
+                r.K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
+                r.keep = carried_keep;
+                r.sort_len = lwm::sort_length(p->S);
+                if (static_cast<size_t>(r.sort_len) * 8 > 200 * 1024)
+                    return fail(LWM_UNSUPPORTED, "elite selection supports at most 16384 samples");
+                r.scores = p->scores.as<float>();
+                r.cand = p->cand.as<float>();
+                r.mean = p->mean.as<float>();
+                r.std = p->stdv.as<float>();
+                r.carried = p->carried.as<float>();
+                r.icem = p->kind == PlannerKind::Icem;
+                r.return_best = p->kind == PlannerKind::Icem && !p->icem.return_mean;
+                r.alpha = p->kind == PlannerKind::Icem ? p->icem.alpha : 0.0f;
+                r.min_std = p->kind == PlannerKind::Cem ? p->cem.min_std : p->icem.min_std;
+                r.inv_k = static_cast<float>(1.0 / static_cast<double>(r.K));
+                r.inv_km1 = static_cast<float>(1.0 / static_cast<double>(r.K - 1));
+                r.sequence = p->sequence.as<float>();
+                r.first_action = p->first_action.as<float>();
+                r.warm_start = p->kind == PlannerKind::Icem ? p->warm.as<float>() : nullptr;
+                r.best_index = p->best.as<uint32_t>();
+                r.best_score = p->best_score.as<float>();
+                LWM_CUDA(lwm::launch_topk_refit(r, B, stream));
+                p->ctx->launches += 1;
+            }
+        }
+        ++completed;
+    }
+    if (p->kind != PlannerKind::Cem) {
+        p->has_warm = true;
+        p->warm_batch = B;
+    }
+    out->first_action = p->first_action.as<float>();
+    out->sequence = p->sequence.as<float>();
+    out->scores = p->scores.as<float>();
+    out->best_indices = p->best.as<uint32_t>();
+    out->batch = B;
+    out->scores_cols = p->S;
+    out->iterations_completed = completed;
+    out->deadline_reached = deadline_hit ? 1 : 0;
+    out->deadline_outcome = LWM_DEADLINE_NONE;
+    out->elapsed_ns = static_cast<uint64_t>(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count());
+    p->last_batch = B;
+    p->last_cols = p->S;
+    p->has_result = true;
+    return LWM_OK;
+}
+
+lwm_status stage_context(lwm_scorer* sc, size_t bytes) {
+    if (sc->staged) LWM_CUDA(cudaEventSynchronize(sc->staged));
+    LWM_TRY(sc->ctx_host.ensure(bytes));
+    LWM_TRY(sc->ctx_dev.ensure(bytes));
+    return LWM_OK;
+}
+
+lwm_status upload_context(lwm_scorer* sc, size_t bytes) {
+    LWM_CUDA(cudaMemcpyAsync(sc->ctx_dev.ptr, sc->ctx_host.ptr, bytes, cudaMemcpyHostToDevice, sc->ctx->stream));
+    if (!sc->staged) LWM_CUDA(cudaEventCreateWithFlags(&sc->staged, cudaEventDisableTiming));
+    LWM_CUDA(cudaEventRecord(sc->staged, sc->ctx->stream));
+    return LWM_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+void build_tcn_view(const lwm_tcn_config& t, const float* base, size_t& off, lwm::TcnView& v) {
+    std::memset(&v, 0, sizeof v);
+    v.input_dim = t.input_dim;
+    v.levels = t.levels;
+    v.k = t.kernel_size;
+    uint32_t in = t.input_dim, mx = t.input_dim;
+    for (uint32_t l = 0; l < t.levels; ++l) {
+        const uint32_t o = t.channels[l];
+        lwm::TcnBlockView& b = v.blocks[l];
+        b.in = in; b.out = o; b.dil = 1u << l;
+        b.w1 = base + off; off += static_cast<size_t>(o) * in * t.kernel_size;
+        b.b1 = base + off; off += o;
+        b.w2 = base + off; off += static_cast<size_t>(o) * o * t.kernel_size;
+        b.b2 = base + off; off += o;
+        if (in != o) {
+            b.wr = base + off; off += static_cast<size_t>(o) * in;
+            b.br = base + off; off += o;
+        }
+        in = o;
+        mx = std::max(mx, o);
+    }
+    v.out_dim = in;
+    v.max_ch = mx;
+}
+
+}  // namespace
+
+// ======================================================================= ABI
+
+extern "C" {
+
+const char* lwm_last_error(void) { return g_last_error.c_str(); }
+const char* lwm_version(void) { return "lewm-b200 0.1.0 (sm_100a)"; }
+int lwm_abi_version(void) { return LWM_ABI_VERSION; }
+
+lwm_status lwm_ctx_create(int device, lwm_ctx** out) {
+    if (!out) return fail(LWM_INVALID_ARGUMENT, "output pointer is null");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return fail(LWM_CUDA_ERROR, std::string("no CUDA device: ") + cudaGetErrorString(e));
+    if (device < 0 || device >= count)
+        return fail(LWM_INVALID_ARGUMENT, "CUDA device " + std::to_string(device) + " does not exist (" + std::to_string(count) + " visible)");
+    LWM_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    LWM_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(LWM_UNSUPPORTED, std::string("this library is built for sm_100a (B200); device is ") + prop.name);
+    auto* ctx = new lwm_ctx();
+    ctx->device = device;
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return fail(LWM_CUDA_ERROR, std::string("cudaStreamCreate failed: ") + cudaGetErrorString(e));
+    }
+    std::random_device rd;
+    ctx->unseeded_seed = (static_cast<uint64_t>(rd()) << 32) ^ rd();
+    *out = ctx;
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_destroy(lwm_ctx* ctx) {
+    if (!ctx) return LWM_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_stream(lwm_ctx* ctx, void** stream_out) {
+    if (!ctx || !stream_out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    *stream_out = ctx->stream;
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_synchronize(lwm_ctx* ctx) {
+    if (!ctx) return fail(LWM_INVALID_ARGUMENT, "null context");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(cudaStreamSynchronize(ctx->stream));
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out) {
+    if (!ctx || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    *out = ctx->launches.load();
+    return LWM_OK;
+}
+
+void lwm_mppi_config_default(uint32_t horizon, uint32_t samples, uint32_t action_dim, lwm_mppi_config* c) {
+    std::memset(c, 0, sizeof(*c));
+    c->horizon = horizon;
+    c->samples = samples;
+    c->iterations = 1;
+    c->action_dim = action_dim;
+    for (int i = 0; i < LWM_MAX_ACTION_DIM; ++i) { c->bounds_low[i] = -1.0f; c->bounds_high[i] = 1.0f; }
+    c->noise_std = 1.0f;
+    c->temperature = 1.0f;
+    c->deadline_ns = -1;
+}
+
+void lwm_cem_config_default(uint32_t horizon, uint32_t samples, uint32_t elites, uint32_t action_dim, lwm_cem_config* c) {
+    std::memset(c, 0, sizeof(*c));
+    c->horizon = horizon;
+    c->samples = samples;
+    c->elites = elites;
+    c->iterations = 4;
+    c->action_dim = action_dim;
+    for (int i = 0; i < LWM_MAX_ACTION_DIM; ++i) { c->bounds_low[i] = -1.0f; c->bounds_high[i] = 1.0f; }
+    c->init_std = 1.0f;
+    c->min_std = 1e-3f;
+    c->deadline_ns = -1;
+}
+
+void lwm_icem_config_default(uint32_t horizon, uint32_t samples, uint32_t elites, uint32_t action_dim, lwm_icem_config* c) {
+    std::memset(c, 0, sizeof(*c));
+    c->horizon = horizon;
+    c->samples = samples;
+    c->elites = elites;
+    c->keep_elites = elites;
+    c->iterations = 4;
+    c->noise_beta = 2.0f;
+    c->alpha = 0.1f;
+    c->action_dim = action_dim;
+    for (int i = 0; i < LWM_MAX_ACTION_DIM; ++i) { c->bounds_low[i] = -1.0f; c->bounds_high[i] = 1.0f; }
+    c->init_std = 1.0f;
+    c->min_std = 1e-3f;
+    c->return_mean = 1;
+    c->deadline_ns = -1;
+}
+
+static lwm_status make_planner(lwm_ctx* ctx, PlannerKind kind, lwm_planner** out) {
+    if (!ctx || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    auto* p = new lwm_planner();
+    p->ctx = ctx;
+    p->kind = kind;
+    *out = p;
+    return LWM_OK;
+}
+
+lwm_status lwm_mppi_create(lwm_ctx* ctx, const lwm_mppi_config* cfg, lwm_planner** out) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null config");
+    LWM_TRY(validate_mppi(*cfg));
+    LWM_TRY(make_planner(ctx, PlannerKind::Mppi, out));
+    (*out)->mppi = *cfg;
+    (*out)->T = cfg->horizon; (*out)->S = cfg->samples; (*out)->A = cfg->action_dim; (*out)->iterations = cfg->iterations;
+    return LWM_OK;
+}
+
+lwm_status lwm_cem_create(lwm_ctx* ctx, const lwm_cem_config* cfg, lwm_planner** out) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null config");
+    LWM_TRY(validate_cem(*cfg));
+    LWM_TRY(make_planner(ctx, PlannerKind::Cem, out));
+    (*out)->cem = *cfg;
+    (*out)->T = cfg->horizon; (*out)->S = cfg->samples; (*out)->A = cfg->action_dim; (*out)->iterations = cfg->iterations;
+    return LWM_OK;
+}
+
+lwm_status lwm_icem_create(lwm_ctx* ctx, const lwm_icem_config* cfg, lwm_planner** out) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null config");
+    LWM_TRY(validate_icem(*cfg));
+    LWM_TRY(make_planner(ctx, PlannerKind::Icem, out));
+    (*out)->icem = *cfg;
+    (*out)->T = cfg->horizon; (*out)->S = cfg->samples; (*out)->A = cfg->action_dim; (*out)->iterations = cfg->iterations;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_destroy(lwm_planner* p) {
+    if (!p) return LWM_OK;
+    cudaSetDevice(p->ctx->device);
+    cudaStreamSynchronize(p->ctx->stream);
+    for (DevBuf* b : {&p->bounds, &p->zeros, &p->std_init, &p->mean, &p->stdv, &p->cand, &p->scores, &p->partials, &p->counters,
+                      &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp})
+        b->release();
+    p->staging.release();
+    delete p;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_set_warm_start(lwm_planner* p, const float* sequence, uint32_t batch, uint32_t horizon,
+                                      uint32_t action_dim) {
+    if (!p || !sequence) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> lock(p->mu);
+    if (p->kind == PlannerKind::Cem) return fail(LWM_INVALID_ARGUMENT, "CEM planners have no warm start");
+    if (horizon != p->T || action_dim != p->A || batch == 0)
+        return fail(LWM_INVALID_ARGUMENT, std::string(planner_name(p->kind)) + " warm-start shape [" + std::to_string(batch) + ", " +
+                                              std::to_string(horizon) + ", " + std::to_string(action_dim) + "] does not match expected [B, " +
+                                              std::to_string(p->T) + ", " + std::to_string(p->A) + "]");
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    LWM_TRY(ensure_planner_buffers(p, batch));
+    const size_t bytes = static_cast<size_t>(batch) * horizon * action_dim * 4;
+    LWM_CUDA(cudaMemcpyAsync(p->warm.ptr, sequence, bytes, cudaMemcpyHostToDevice, p->ctx->stream));
+    LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
+    p->has_warm = true;
+    p->warm_batch = batch;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_clear_warm_start(lwm_planner* p) {
+    if (!p) return fail(LWM_INVALID_ARGUMENT, "null planner");
+    std::lock_guard<std::mutex> lock(p->mu);
+    p->has_warm = false;
+    p->warm_batch = 0;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_warm_start(lwm_planner* p, float* out, size_t capacity, uint32_t* batch_out) {
+    if (!p || !batch_out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> lock(p->mu);
+    *batch_out = 0;
+    if (!p->has_warm) return LWM_OK;
+    const size_t n = static_cast<size_t>(p->warm_batch) * p->T * p->A;
+    if (!out || capacity < n) return fail(LWM_INVALID_ARGUMENT, "warm-start output buffer too small");
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    LWM_CUDA(cudaMemcpyAsync(out, p->warm.ptr, n * 4, cudaMemcpyDeviceToHost, p->ctx->stream));
+    LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
+    *batch_out = p->warm_batch;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_reset_rng(lwm_planner* p) {
+    if (!p) return fail(LWM_INVALID_ARGUMENT, "null planner");
+    p->rng_offset.store(0);
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_rng_offset(lwm_planner* p, uint64_t* out) {
+    if (!p || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    *out = p->rng_offset.load();
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_last_candidates(lwm_planner* p, const float** cand, uint32_t* samples_out) {
+    if (!p || !cand || !samples_out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (!p->has_result) return fail(LWM_INVALID_ARGUMENT, "planner has not planned yet");
+    *cand = p->cand.as<float>();
+    *samples_out = p->S;
+    return LWM_OK;
+}
+
+// ----------------------------------------------------------------- scorers
+
+static lwm_scorer* new_scorer(lwm_ctx* ctx, ScorerKind kind) {
+    auto* s = new lwm_scorer();
+    s->ctx = ctx;
+    s->kind = kind;
+    return s;
+}
+
+lwm_status lwm_scorer_nominal_create(lwm_ctx* ctx, const lwm_nominal_scorer_config* cfg, lwm_scorer** out) {
+    if (!ctx || !cfg || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    LWM_TRY(validate_cost(cfg->cost));
+    if (!finite(cfg->trim_scale) || cfg->trim_scale <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "invalid nominal scorer context");
+    if (!finite(cfg->dt) || cfg->dt <= 0.0f || cfg->substeps == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid nominal physics rollout shape or timestep");
+    LWM_TRY(validate_domain(cfg->domain));
+    lwm_scorer* s = new_scorer(ctx, ScorerKind::Nominal);
+    s->nominal = *cfg;
+    *out = s;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_nominal_set_context(lwm_scorer* s, uint32_t B, uint32_t T, const float* initial, const float* motors,
+                                          const float* ref_states, const float* ref_actions, const lwm_domain* domains) {
+    if (!s || s->kind != ScorerKind::Nominal) return fail(LWM_INVALID_ARGUMENT, "not a nominal scorer");
+    if (!initial || !motors || !ref_states || !ref_actions || B == 0 || T == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid nominal scorer context");
+    if (T > lwm::kMaxHorizon) return fail(LWM_UNSUPPORTED, "horizon exceeds the supported maximum of 64");
+    if (domains)
+        for (uint32_t b = 0; b < B; ++b) LWM_TRY(validate_domain(domains[b]));
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    size_t off = 0;
+    s->off_initial = off; off = align256(off + static_cast<size_t>(B) * 18 * 4);
+    s->off_motors = off; off = align256(off + static_cast<size_t>(B) * 4 * 4);
+    s->off_ref_states = off; off = align256(off + static_cast<size_t>(B) * T * 18 * 4);
+    s->off_ref_actions = off; off = align256(off + static_cast<size_t>(B) * T * 4 * 4);
+    s->off_domains = off; off = align256(off + static_cast<size_t>(B) * sizeof(lwm::DomainParams));
+    LWM_TRY(stage_context(s, off));
+    char* h = s->ctx_host.as<char>();
+    std::memcpy(h + s->off_initial, initial, static_cast<size_t>(B) * 18 * 4);
+    std::memcpy(h + s->off_motors, motors, static_cast<size_t>(B) * 4 * 4);
+    std::memcpy(h + s->off_ref_states, ref_states, static_cast<size_t>(B) * T * 18 * 4);
+    std::memcpy(h + s->off_ref_actions, ref_actions, static_cast<size_t>(B) * T * 4 * 4);
+    auto* dp = reinterpret_cast<lwm::DomainParams*>(h + s->off_domains);
+    for (uint32_t b = 0; b < B; ++b) dp[b] = domain_params(domains ? domains[b] : s->nominal.domain);
+    LWM_TRY(upload_context(s, off));
+    s->batch = B;
+    s->horizon = T;
+    s->has_context = true;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_skyjepa_create(lwm_ctx* ctx, const lwm_skyjepa_config* cfg, const float* weights, size_t count,
+                                     const float* state_mean, const float* state_std, const float* action_mean,
+                                     const float* action_std, const lwm_tracking_cost* cost, float dt, lwm_scorer** out) {
+    if (!ctx || !cfg || !weights || !state_mean || !state_std || !action_mean || !action_std || !cost || !out)
+        return fail(LWM_INVALID_ARGUMENT, "null argument");
+    const size_t need = lwm_skyjepa_weight_count(cfg);
+    if (need == 0) return fail(LWM_INVALID_ARGUMENT, "invalid SkyJEPA configuration");
+    if (count != need)
+        return fail(LWM_INVALID_ARGUMENT, "SkyJEPA weight blob has " + std::to_string(count) + " values, expected " + std::to_string(need));
+    LWM_TRY(validate_cost(*cost));
+    if (!finite(dt) || dt <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "SkyJEPA control dt must be finite and positive");
+    // validate_stats (src/models/skyjepa/control.rs:454-472)
+    for (int i = 0; i < 18; ++i)
+        if (!finite(state_mean[i]) || !finite(state_std[i]) || state_std[i] <= 0.0f)
+            return fail(LWM_INVALID_ARGUMENT, "SkyJEPA state normalization is non-finite or has non-positive std");
+    for (int i = 0; i < 4; ++i)
+        if (!finite(action_mean[i]) || !finite(action_std[i]) || action_std[i] <= 0.0f)
+            return fail(LWM_INVALID_ARGUMENT, "SkyJEPA action normalization is non-finite or has non-positive std");
+    if (cfg->prober_hidden_layers > 5) return fail(LWM_UNSUPPORTED, "prober hidden_layers must be at most 5");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    lwm_scorer* s = new_scorer(ctx, ScorerKind::Skyjepa);
+    s->sky = *cfg;
+    s->cost = *cost;
+    s->dt = dt;
+    lwm_status st = s->weights.ensure(need * 4);
+    if (st != LWM_OK) { delete s; return st; }
+    cudaError_t e = cudaMemcpy(s->weights.ptr, weights, need * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { s->weights.release(); delete s; return fail(LWM_CUDA_ERROR, cudaGetErrorString(e)); }
+    lwm::SkyjepaArgs& a = s->sky_args;
+    std::memset(&a, 0, sizeof a);
+    const float* base = s->weights.as<float>();
+    size_t off = 0;
+    build_tcn_view(cfg->state_encoder, base, off, a.state_tcn);
+    const uint32_t H = cfg->latent_dim;
+    a.proj_w = base + off; off += static_cast<size_t>(H) * a.state_tcn.out_dim;
+    a.proj_b = base + off; off += H;
+    build_tcn_view(cfg->action_encoder, base, off, a.action_tcn);
+    const uint32_t E = a.action_tcn.out_dim;
+    a.w_ih = base + off; off += static_cast<size_t>(3) * H * E;
+    a.w_hh = base + off; off += static_cast<size_t>(3) * H * H;
+    a.b_ih = base + off; off += static_cast<size_t>(3) * H;
+    a.b_hh = base + off; off += static_cast<size_t>(3) * H;
+    const uint32_t hid = cfg->prober_hidden_dim;
+    a.p_in_w = base + off; off += static_cast<size_t>(hid) * H;
+    a.p_in_b = base + off; off += hid;
+    for (uint32_t i = 0; i + 1 < cfg->prober_hidden_layers; ++i) {
+        a.p_hid_w[i] = base + off; off += static_cast<size_t>(hid) * hid;
+        a.p_hid_b[i] = base + off; off += hid;
+    }
+    a.p_out_w = base + off; off += static_cast<size_t>(15) * hid;
+    a.p_out_b = base + off; off += 15;
+    a.A = cfg->action_dim;
+    a.Hs = cfg->history_steps;
+    a.H = H;
+    a.E = E;
+    a.hid = hid;
+    a.prober_layers = cfg->prober_hidden_layers;
+    for (int i = 0; i < 18; ++i) { a.state_mean[i] = state_mean[i]; a.state_std[i] = state_std[i]; }
+    for (int i = 0; i < 4; ++i) { a.action_mean[i] = action_mean[i]; a.action_std[i] = action_std[i]; }
+    a.mass = static_cast<float>(cfg->kinematics.mass);
+    a.gravity = static_cast<float>(cfg->kinematics.gravity);
+    a.hover_throttle = static_cast<float>(cfg->kinematics.hover_throttle);
+    a.rotor_forces = cfg->kinematics.action_space == LWM_ACTION_SPACE_ROTOR_FORCES;
+    a.dt = dt;
+    a.cost = cost_params(*cost);
+    a.T = 1;
+    const char* why = nullptr;
+    if (!lwm::skyjepa_supported(a, &why)) {
+        s->weights.release();
+        delete s;
+        return fail(LWM_UNSUPPORTED, std::string("SkyJEPA configuration not supported by the fused kernel: ") + why);
+    }
+    *out = s;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* s, uint32_t B, uint32_t T, const float* state_hist,
+                                          const float* action_hist, const float* ref_states, const float* ref_actions) {
+    if (!s || s->kind != ScorerKind::Skyjepa) return fail(LWM_INVALID_ARGUMENT, "not a SkyJEPA scorer");
+    if (!state_hist || !action_hist || !ref_states || !ref_actions || B == 0 || T == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid SkyJEPA control shapes");
+    lwm::SkyjepaArgs probe = s->sky_args;
+    probe.T = T;
+    const char* why = nullptr;
+    if (!lwm::skyjepa_supported(probe, &why)) return fail(LWM_UNSUPPORTED, why);
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    const uint32_t Hs = s->sky.history_steps;
+    size_t off = 0;
+    s->off_state_hist = off; off = align256(off + static_cast<size_t>(B) * Hs * 18 * 4);
+    s->off_action_hist = off; off = align256(off + static_cast<size_t>(B) * (Hs - 1) * 4 * 4);
+    s->off_ref_states = off; off = align256(off + static_cast<size_t>(B) * T * 18 * 4);
+    s->off_ref_actions = off; off = align256(off + static_cast<size_t>(B) * T * 4 * 4);
+    LWM_TRY(stage_context(s, off));
+    LWM_TRY(s->h0.ensure(static_cast<size_t>(B) * s->sky.latent_dim * 4));
+    char* h = s->ctx_host.as<char>();
+    std::memcpy(h + s->off_state_hist, state_hist, static_cast<size_t>(B) * Hs * 18 * 4);
+    std::memcpy(h + s->off_action_hist, action_hist, static_cast<size_t>(B) * (Hs - 1) * 4 * 4);
+    std::memcpy(h + s->off_ref_states, ref_states, static_cast<size_t>(B) * T * 18 * 4);
+    std::memcpy(h + s->off_ref_actions, ref_actions, static_cast<size_t>(B) * T * 4 * 4);
+    LWM_TRY(upload_context(s, off));
+    s->batch = B;
+    s->horizon = T;
+    s->has_context = true;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_callback_create(lwm_ctx* ctx, uint32_t batch, lwm_score_fn fn, void* user, lwm_scorer** out) {
+    if (!ctx || !fn || !out || batch == 0) return fail(LWM_INVALID_ARGUMENT, "invalid callback scorer arguments");
+    lwm_scorer* s = new_scorer(ctx, ScorerKind::Callback);
+    s->batch = batch;
+    s->fn = fn;
+    s->user = user;
+    *out = s;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_score_device(lwm_scorer* s, const float* cand, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
+                                   float* scores) {
+    if (!s || !cand || !scores || S == 0) return fail(LWM_INVALID_ARGUMENT, "invalid score arguments");
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    return score_device(s, cand, B, S, T, A, scores, nullptr);
+}
+
+lwm_status lwm_scorer_predict_device(lwm_scorer* s, const float* cand, uint32_t B, uint32_t S, uint32_t T, float* states) {
+    if (!s || !cand || !states || S == 0) return fail(LWM_INVALID_ARGUMENT, "invalid predict arguments");
+    if (s->kind == ScorerKind::Callback) return fail(LWM_UNSUPPORTED, "callback scorers do not predict states");
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    DevBuf tmp;
+    LWM_TRY(tmp.ensure(static_cast<size_t>(B) * S * 4));
+    lwm_status st = score_device(s, cand, B, S, T, 4, tmp.as<float>(), states);
+    cudaStreamSynchronize(s->ctx->stream);
+    tmp.release();
+    return st;
+}
+
+lwm_status lwm_scorer_destroy(lwm_scorer* s) {
+    if (!s) return LWM_OK;
+    cudaSetDevice(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+    if (s->staged) cudaEventDestroy(s->staged);
+    s->weights.release();
+    s->h0.release();
+    s->ctx_dev.release();
+    s->ctx_host.release();
+    delete s;
+    return LWM_OK;
+}
+
+// ------------------------------------------------------------------ planning
+
+lwm_status lwm_plan_device(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
+    if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    std::lock_guard<std::mutex> lock(p->mu);
+    std::lock_guard<std::mutex> lock2(sc->mu);
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    return plan_device_locked(p, sc, injected, out);
+}
+
+lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_result* out) {
+    if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    const auto start = std::chrono::steady_clock::now();
+    std::lock_guard<std::mutex> lock(p->mu);
+    std::lock_guard<std::mutex> lock2(sc->mu);
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    const float* dev_noise = nullptr;
+    if (injected) {
+        const size_t n = static_cast<size_t>(sc->batch) * p->S * p->T * p->A * p->iterations;
+        LWM_TRY(p->noise_tmp.ensure(n * 4));
+        LWM_CUDA(cudaMemcpyAsync(p->noise_tmp.ptr, injected, n * 4, cudaMemcpyHostToDevice, p->ctx->stream));
+        dev_noise = p->noise_tmp.as<float>();
+    }
+    lwm_plan_device_result d{};
+    LWM_TRY(plan_device_locked(p, sc, dev_noise, &d));
+    const size_t B = d.batch;
+    const size_t seq = B * p->T * p->A;
+    const size_t nsc = B * d.scores_cols;
+    // one D2H burst through the planner's pinned staging
+    char* h = p->staging.as<char>();
+    const size_t off_fa = 0, off_seq = align256(B * p->A * 4), off_sc = align256(off_seq + seq * 4),
+                 off_best = align256(off_sc + nsc * 4), total = off_best + B * 4;
+    LWM_TRY(p->staging.ensure(total));
+    h = p->staging.as<char>();
+    cudaStream_t stream = p->ctx->stream;
+    if (out->first_action) LWM_CUDA(cudaMemcpyAsync(h + off_fa, d.first_action, B * p->A * 4, cudaMemcpyDeviceToHost, stream));
+    if (out->sequence) LWM_CUDA(cudaMemcpyAsync(h + off_seq, d.sequence, seq * 4, cudaMemcpyDeviceToHost, stream));
+    if (out->scores) {
+        if (out->scores_capacity < nsc) return fail(LWM_INVALID_ARGUMENT, "scores buffer too small");
+        LWM_CUDA(cudaMemcpyAsync(h + off_sc, d.scores, nsc * 4, cudaMemcpyDeviceToHost, stream));
+    }
+    if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
+    LWM_CUDA(cudaStreamSynchronize(stream));
+    if (out->first_action) std::memcpy(out->first_action, h + off_fa, B * p->A * 4);
+    if (out->sequence) std::memcpy(out->sequence, h + off_seq, seq * 4);
+    if (out->scores) std::memcpy(out->scores, h + off_sc, nsc * 4);
+    if (out->best_indices) std::memcpy(out->best_indices, h + off_best, B * 4);
+    out->batch = d.batch;
+    out->scores_cols = d.scores_cols;
+    out->iterations_completed = d.iterations_completed;
+    out->deadline_reached = d.deadline_reached;
+    out->deadline_outcome = d.deadline_outcome;
+    out->elapsed_ns = static_cast<uint64_t>(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count());
+    return LWM_OK;
+}
+
+// --------------------------------------------------------- planner pieces
+
+lwm_status lwm_lowest_k_device(lwm_ctx* ctx, const float* scores, uint32_t B, uint32_t S, uint32_t K, uint32_t* out) {
+    if (!ctx || !scores || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (K == 0) return fail(LWM_INVALID_ARGUMENT, "top-k count must be greater than zero");
+    if (S == 0) return fail(LWM_INVALID_ARGUMENT, "score tensor must contain at least one sample");
+    if (K > S) return fail(LWM_INVALID_ARGUMENT, "top-k count " + std::to_string(K) + " cannot exceed samples " + std::to_string(S));
+    if (S > 16384) return fail(LWM_UNSUPPORTED, "lowest-k supports at most 16384 samples");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(lwm::launch_lowest_k(scores, out, B, S, K, ctx->stream));
+    ctx->launches += 1;
+    return LWM_OK;
+}
+
+lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
+                                  float beta) {
+    if (!ctx || !noise || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (!finite(beta) || beta < 0.0f) return fail(LWM_INVALID_ARGUMENT, "iCEM noise_beta must be finite and non-negative");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    const size_t n = static_cast<size_t>(B) * S * T * A;
+    if (beta == 0.0f || T <= 1) {
+        if (out != noise) LWM_CUDA(cudaMemcpyAsync(out, noise, n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+        return LWM_OK;
+    }
+    float smooth = std::min(std::max(beta / (beta + 1.0f), 0.0f), 0.98f);
+    LWM_CUDA(lwm::launch_color_noise(noise, out, B, S, T, A, smooth, ctx->stream));
+    ctx->launches += 1;
+    return LWM_OK;
+}
+
+lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count, float* out) {
+    if (!ctx || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (count == 0) return LWM_OK;
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(lwm::launch_normal_fill(seed, offset, count, out, ctx->stream));
+    ctx->launches += 1;
+    return LWM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,282 @@
+// kernels_planner.cu — the planner's own kernels (sampling, MPPI reduction,
+// top-k elite selection and refit, colored noise), used by CEM / iCEM and by
+// MPPI with a caller-supplied scorer.  The built-in scorers fuse sampling and
+// the MPPI reduction into their rollout kernels instead (kernels_nominal.cu,
+// kernels_skyjepa.cu).
+#include <cstdint>
+
+#include "lwm_device.cuh"
+#include "lwm_kernels.hpp"
+#include "lwm_mppi.cuh"
+
+namespace lwm {
+
+// ----------------------------------------------------------------- sampling
+//
+// One thread per (vehicle, sample, action) lane over the horizon:
+//   sample_candidates / sample_candidates_with_temporal_noise
+//   (src/planner.rs:1152-1196): eps ~ N(0,1) (injected or Philox), optional
+//   colored-noise EMA + standardisation (:1516-1586, kernel :1852-1896),
+//   cand = mean + eps*std, slot 0 = mean (:1198-1208), clamp (:1614-1616),
+//   then inject_carried_elites (:1210-1235) into slots 1..1+inject.
+__global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
+    const uint64_t lane_id = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint64_t lanes = static_cast<uint64_t>(a.B) * a.S * a.A;
+    if (lane_id >= lanes) return;
+    const uint32_t act = static_cast<uint32_t>(lane_id % a.A);
+    const uint64_t row = lane_id / a.A;  // b * S + s
+    const uint32_t s = static_cast<uint32_t>(row % a.S);
+    const uint32_t b = static_cast<uint32_t>(row / a.S);
+    const uint64_t base = row * a.T * a.A + act;
+    float eps[kMaxHorizon];
+    for (uint32_t t = 0; t < a.T; ++t) {
+        const uint64_t idx = base + static_cast<uint64_t>(t) * a.A;
+        eps[t] = a.noise ? a.noise[idx] : normal_at(a.seed, a.offset + idx);
+    }
+    if (a.smooth > 0.0f && a.T > 1) {
+        // swm_temporal_color_noise_f32 (src/planner.rs:1852-1896)
+        const float keep = 1.0f - a.smooth;
+        float prev = eps[0], mean = 0.0f;
+        for (uint32_t t = 0; t < a.T; ++t) {
+            prev = (t == 0) ? eps[t] : fmaf(a.smooth, prev, keep * eps[t]);
+            eps[t] = prev;
+            mean += prev;
+        }
+        mean /= static_cast<float>(a.T);
+        float var = 0.0f;
+        for (uint32_t t = 0; t < a.T; ++t) {
+            const float c = eps[t] - mean;
+            eps[t] = c;
+            var += c * c;
+        }
+        const float inv_std = 1.0f / sqrtf(var / static_cast<float>(a.T) + 1.0e-6f);
+        for (uint32_t t = 0; t < a.T; ++t) eps[t] *= inv_std;
+    }
+    const bool carried = a.carried && s >= 1 && s <= a.inject;
+    const float lo = a.low[act], hi = a.high[act];
+    for (uint32_t t = 0; t < a.T; ++t) {
+        const size_t mi = (static_cast<size_t>(b) * a.T + t) * a.A + act;
+        float v;
+        if (carried) {
+            v = a.carried[((static_cast<size_t>(b) * a.carried_count + (s - 1)) * a.T + t) * a.A + act];
+        } else {
+            v = (s == 0) ? a.mean[mi] : __fadd_rn(a.mean[mi], __fmul_rn(eps[t], a.std[mi]));
+            v = cmin(cmax(v, lo), hi);
+        }
+        a.out[base + static_cast<uint64_t>(t) * a.A] = v;
+    }
+}
+
+// --------------------------------------------------- MPPI reduce (generic)
+__global__ void __launch_bounds__(256) mppi_reduce_kernel(MppiArgs m, const float* cand,
+                                                          const float* scores, uint32_t S) {
+    constexpr int NT = 256;
+    __shared__ float s_score[NT];
+    __shared__ float s_w[NT];
+    const uint32_t b = blockIdx.y, p = blockIdx.x;
+    const uint32_t first = p * NT;
+    const uint32_t nrows = min(static_cast<uint32_t>(NT), S - first);
+    if (threadIdx.x < nrows) s_score[threadIdx.x] = scores[static_cast<size_t>(b) * S + first + threadIdx.x];
+    __syncthreads();
+    const size_t TA = static_cast<size_t>(m.T) * m.A;
+    mppi_reduce_rows<NT>(m, b, p, nrows, s_score, first,
+                         cand + (static_cast<size_t>(b) * S + first) * TA, TA, s_w);
+}
+
+// ------------------------------------------------ top-k + elite refit
+//
+// One block per vehicle.  Keys (score, index) are sorted ascending with a
+// shared-memory bitonic network, which gives lowest_score_indices
+// (src/planner.rs:1647-1659) for any count; then select_elites +
+// gather_candidate_sequences (:1730-1754) and the refit of
+//   CEM  (:516-517):  mean = elites.mean(1), std = max(sqrt(var_unbiased), min_std)
+//   iCEM (:859-868):  mean = momentum(mean, elite_mean, alpha),
+//                     std = max(momentum(std, max(sqrt(var), min_std), alpha), min_std)
+// plus carried elites (:869-873), the best index and the returned sequence.
+__device__ __forceinline__ void bitonic_sort_keys(uint64_t* keys, uint32_t n) {
+    for (uint32_t width = 2; width <= n; width <<= 1) {
+        for (uint32_t stride = width >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+                const uint32_t peer = i ^ stride;
+                if (peer > i) {
+                    const uint64_t x = keys[i], y = keys[peer];
+                    const bool ascending = (i & width) == 0;
+                    if ((x > y) == ascending) {
+                        keys[i] = y;
+                        keys[peer] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
+    extern __shared__ uint64_t s_keys[];
+    const uint32_t b = blockIdx.x;
+    for (uint32_t i = threadIdx.x; i < a.sort_len; i += blockDim.x)
+        s_keys[i] = i < a.S ? score_key(a.scores[static_cast<size_t>(b) * a.S + i], i) : ~0ull;
+    __syncthreads();
+    bitonic_sort_keys(s_keys, a.sort_len);
+    const uint32_t TA = a.T * a.A;
+    const size_t seq = static_cast<size_t>(b) * TA;
+    const float* cb = a.cand + static_cast<size_t>(b) * a.S * TA;
+    if (a.elite_index)
+        for (uint32_t j = threadIdx.x; j < a.K; j += blockDim.x)
+            a.elite_index[static_cast<size_t>(b) * a.K + j] = static_cast<uint32_t>(s_keys[j]);
+    const float inv_k = a.inv_k, inv_km1 = a.inv_km1;
+    const uint32_t best = static_cast<uint32_t>(s_keys[0]);
+    for (uint32_t e = threadIdx.x; e < TA; e += blockDim.x) {
+        float sum = 0.0f;
+        for (uint32_t j = 0; j < a.K; ++j) sum += cb[static_cast<size_t>(static_cast<uint32_t>(s_keys[j])) * TA + e];
+        const float m = sum * inv_k;
+        float sq = 0.0f;
+        for (uint32_t j = 0; j < a.K; ++j) {
+            const float d = cb[static_cast<size_t>(static_cast<uint32_t>(s_keys[j])) * TA + e] - m;
+            sq += d * d;
+        }
+        float sd = sqrtf(sq * inv_km1);
+        if (a.min_std != 0.0f) sd = cmax(sd, a.min_std);
+        float new_mean = m, new_std = sd;
+        if (a.icem) {
+            const float pm = a.mean[seq + e], ps = a.std[seq + e];
+            if (a.alpha == 0.0f) {
+                new_mean = m; new_std = sd;
+            } else if (a.alpha == 1.0f) {
+                new_mean = pm; new_std = ps;
+            } else {
+                const float beta = 1.0f - a.alpha;
+                new_mean = __fadd_rn(__fmul_rn(pm, a.alpha), __fmul_rn(m, beta));
+                new_std = __fadd_rn(__fmul_rn(ps, a.alpha), __fmul_rn(sd, beta));
+            }
+            if (a.min_std != 0.0f) new_std = cmax(new_std, a.min_std);
+        }
+        a.mean[seq + e] = new_mean;
+        a.std[seq + e] = new_std;
+        for (uint32_t j = 0; j < a.keep; ++j)
+            a.carried[(static_cast<size_t>(b) * a.keep + j) * TA + e] =
+                cb[static_cast<size_t>(static_cast<uint32_t>(s_keys[j])) * TA + e];
+        const float out = a.return_best ? cb[static_cast<size_t>(best) * TA + e] : new_mean;
+        const uint32_t t = e / a.A, act = e - t * a.A;
+        a.sequence[seq + e] = out;
+        if (t == 0) a.first_action[static_cast<size_t>(b) * a.A + act] = out;
+        if (a.warm_start) {
+            if (t >= 1) a.warm_start[seq + e - a.A] = out;
+            if (t == a.T - 1) a.warm_start[seq + e] = out;
+        }
+    }
+    if (threadIdx.x == 0) {
+        a.best_index[b] = best;
+        a.best_score[b] = key_score(s_keys[0]);
+    }
+}
+
+// lowest_score_indices alone (the swm_lowest_k_indices_f32 replacement).
+__global__ void __launch_bounds__(1024) lowest_k_kernel(const float* scores, uint32_t* out,
+                                                        uint32_t S, uint32_t sort_len, uint32_t K) {
+    extern __shared__ uint64_t s_keys[];
+    const uint32_t b = blockIdx.x;
+    for (uint32_t i = threadIdx.x; i < sort_len; i += blockDim.x)
+        s_keys[i] = i < S ? score_key(scores[static_cast<size_t>(b) * S + i], i) : ~0ull;
+    __syncthreads();
+    bitonic_sort_keys(s_keys, sort_len);
+    for (uint32_t j = threadIdx.x; j < K; j += blockDim.x)
+        out[static_cast<size_t>(b) * K + j] = static_cast<uint32_t>(s_keys[j]);
+}
+
+// color_temporal_noise alone (src/planner.rs:1852-1896), one thread per lane.
+__global__ void __launch_bounds__(256) color_noise_kernel(const float* in, float* out, uint64_t sequences,
+                                                          uint32_t T, uint32_t A, float smooth) {
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= sequences) return;
+    const uint64_t action = idx % A, sample = idx / A;
+    const uint64_t base = sample * T * A + action;
+    const float keep = 1.0f - smooth;
+    float prev = in[base], mean = 0.0f;
+    for (uint32_t t = 0; t < T; ++t) {
+        const uint64_t o = base + static_cast<uint64_t>(t) * A;
+        prev = (t == 0) ? in[o] : fmaf(smooth, prev, keep * in[o]);
+        out[o] = prev;
+        mean += prev;
+    }
+    mean /= static_cast<float>(T);
+    float var = 0.0f;
+    for (uint32_t t = 0; t < T; ++t) {
+        const uint64_t o = base + static_cast<uint64_t>(t) * A;
+        const float c = out[o] - mean;
+        out[o] = c;
+        var += c * c;
+    }
+    const float inv_std = 1.0f / sqrtf(var / static_cast<float>(T) + 1.0e-6f);
+    for (uint32_t t = 0; t < T; ++t) out[base + static_cast<uint64_t>(t) * A] *= inv_std;
+}
+
+__global__ void __launch_bounds__(256) normal_fill_kernel(uint64_t seed, uint64_t offset, uint64_t count,
+                                                          float* out) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < count) out[i] = normal_at(seed, offset + i);
+}
+
+// ----------------------------------------------------------------- launchers
+
+static inline uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uint32_t>((a + b - 1) / b); }
+
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream) {
+    const uint64_t lanes = static_cast<uint64_t>(a.B) * a.S * a.A;
+    sample_kernel<<<ceil_div(lanes, 256), 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
+                               uint32_t S, cudaStream_t stream) {
+    dim3 grid(ceil_div(S, 256), B);
+    mppi_reduce_kernel<<<grid, 256, 0, stream>>>(m, cand, scores, S);
+    return cudaGetLastError();
+}
+
+uint32_t sort_length(uint32_t S) {
+    uint32_t n = 1;
+    while (n < S) n <<= 1;
+    return n;
+}
+
+cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream) {
+    const size_t smem = static_cast<size_t>(a.sort_len) * sizeof(uint64_t);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(topk_refit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const uint32_t threads = a.sort_len < 1024 ? (a.sort_len < 64 ? 64 : a.sort_len) : 1024;
+    topk_refit_kernel<<<B, threads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint32_t S, uint32_t K,
+                            cudaStream_t stream) {
+    const uint32_t n = sort_length(S);
+    const size_t smem = static_cast<size_t>(n) * sizeof(uint64_t);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(lowest_k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const uint32_t threads = n < 1024 ? (n < 64 ? 64 : n) : 1024;
+    lowest_k_kernel<<<B, threads, smem, stream>>>(scores, out, S, n, K);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_color_noise(const float* in, float* out, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
+                               float smooth, cudaStream_t stream) {
+    const uint64_t seqs = static_cast<uint64_t>(B) * S * A;
+    color_noise_kernel<<<ceil_div(seqs, 256), 256, 0, stream>>>(in, out, seqs, T, A, smooth);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_normal_fill(uint64_t seed, uint64_t offset, uint64_t count, float* out, cudaStream_t stream) {
+    normal_fill_kernel<<<ceil_div(count, 256), 256, 0, stream>>>(seed, offset, count, out);
+    return cudaGetLastError();
+}
+
+}  // namespace lwm

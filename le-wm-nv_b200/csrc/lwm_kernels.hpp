@@ -1,0 +1,154 @@
+// lwm_kernels.hpp — argument blocks and launchers of the library's kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+
+namespace lwm {
+
+// Output and scratch of the one-pass MPPI reduction (lwm_mppi.cuh).
+struct MppiArgs {
+    float* partials;          // [B][P][pw]
+    unsigned int* counters;   // [B], zero between launches
+    float* sequence;          // [B][T][A]; also the next iteration's mean
+    float* first_action;      // [B][A]
+    float* warm_start;        // [B][T][A], shifted sequence
+    uint32_t* best_index;     // [B]
+    float* best_score;        // [B]
+    uint32_t T, A, P, pw;     // pw = partial row width in floats (4 + T*A, padded)
+    float mul;                // -1 / temperature
+};
+
+constexpr uint32_t kMaxHorizon = 64;
+constexpr uint32_t kMaxActionDim = 16;
+
+struct SampleArgs {
+    uint32_t B, S, T, A;
+    const float* mean;     // [B,T,A]
+    const float* std;      // [B,T,A]
+    const float* low;      // [A] (device)
+    const float* high;     // [A] (device)
+    const float* noise;    // injected [B,S,T,A] or nullptr
+    uint64_t seed, offset;
+    float smooth;          // colored-noise EMA factor; 0 = white noise
+    const float* carried;  // [B,carried_count,T,A] or nullptr
+    uint32_t carried_count, inject;
+    float* out;            // [B,S,T,A]
+};
+
+struct RefitArgs {
+    uint32_t S, T, A, K, keep, sort_len;
+    const float* scores;   // [B,S]
+    const float* cand;     // [B,S,T,A]
+    float* mean;           // [B,T,A] in/out
+    float* std;            // [B,T,A] in/out
+    float* carried;        // [B,keep,T,A]
+    uint32_t* elite_index; // [B,K] or nullptr
+    int icem, return_best;
+    float alpha, min_std, inv_k, inv_km1;
+    float* sequence;       // [B,T,A]
+    float* first_action;   // [B,A]
+    float* warm_start;     // [B,T,A] or nullptr
+    uint32_t* best_index;  // [B]
+    float* best_score;     // [B]
+};
+
+// SkyJepaDomain (src/skyjepa_sim.rs:28-40) as laid out on the device.
+struct DomainParams {
+    float mass, inertia[3], tau, drag[3], thrust_scale, torque_scale, arm, gravity, max_tw;
+};
+
+struct CostParams {
+    float position, velocity, attitude, angular_velocity, action[4];
+};
+
+struct NominalArgs {
+    uint32_t B, S, T, substeps;
+    float h;          // dt / substeps
+    float inv_trim;   // (float)(1 / trim_scale)
+    const DomainParams* domains;  // [B]
+    const float* initial;         // [B,18]
+    const float* motors;          // [B,4]
+    const float* ref_states;      // [B,T,18]
+    const float* ref_actions;     // [B,T,4]
+    CostParams cost;
+    int sample;                   // 1: sample candidates in-kernel; 0: read cand_in
+    const float* mean;            // [B,T,4]
+    const float* std;             // [B,T,4]
+    float low[4], high[4];
+    const float* noise;           // injected [B,S,T,4] or nullptr
+    uint64_t seed, offset;
+    const float* cand_in;         // [B,S,T,4] when sample == 0
+    float* cand_out;              // [B,S,T,4] or nullptr
+    float* scores;                // [B,S]
+    float* states;                // [B,S,T,18] or nullptr
+    int mppi;                     // 1: fused MPPI reduction
+    MppiArgs m;
+};
+
+// SkyJEPA learned scorer: device weight views (see the weight-blob layout in
+// include/lewm_b200.h) and per-plan context.
+struct TcnBlockView {
+    const float *w1, *b1, *w2, *b2, *wr, *br;
+    uint32_t in, out, dil;
+};
+struct TcnView {
+    uint32_t input_dim, levels, k, out_dim, max_ch;
+    TcnBlockView blocks[8];
+};
+
+struct SkyjepaArgs {
+    uint32_t B, S, T, A, Hs, H, E, hid, prober_layers;
+    TcnView state_tcn, action_tcn;
+    const float *proj_w, *proj_b;
+    const float *w_ih, *w_hh, *b_ih, *b_hh;
+    const float *p_in_w, *p_in_b, *p_hid_w[4], *p_hid_b[4], *p_out_w, *p_out_b;
+    float state_mean[18], state_std[18], action_mean[4], action_std[4];
+    float mass, gravity, hover_throttle;
+    int rotor_forces;
+    float dt;
+    CostParams cost;
+    const float* state_hist;      // [B,Hs,18] raw
+    const float* action_hist;     // [B,Hs-1,4] raw
+    const float* ref_states;      // [B,T,18]
+    const float* ref_actions;     // [B,T,4]
+    float* h0;                    // [B,H] written by the context kernel
+    int sample;
+    const float* mean;            // [B,T,4]
+    const float* std;             // [B,T,4]
+    float low[4], high[4];
+    const float* noise;
+    uint64_t seed, offset;
+    const float* cand_in;
+    float* cand_out;
+    float* scores;
+    float* states;
+    int mppi;
+    MppiArgs m;
+    int use_pdl;
+};
+
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
+cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
+                               uint32_t S, cudaStream_t stream);
+uint32_t sort_length(uint32_t S);
+cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream);
+cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint32_t S, uint32_t K,
+                            cudaStream_t stream);
+cudaError_t launch_color_noise(const float* in, float* out, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
+                               float smooth, cudaStream_t stream);
+cudaError_t launch_normal_fill(uint64_t seed, uint64_t offset, uint64_t count, float* out, cudaStream_t stream);
+
+// Number of blocks (MPPI partials per vehicle) the nominal kernel uses.
+uint32_t nominal_blocks_per_vehicle(uint32_t S);
+cudaError_t launch_nominal(const NominalArgs& a, cudaStream_t stream);
+
+// Rows per cluster and partials per vehicle of the fused SkyJEPA kernel.
+uint32_t skyjepa_partials_per_vehicle(uint32_t S, uint32_t H);
+bool skyjepa_supported(const SkyjepaArgs& a, const char** why);
+// Launches the context kernel (state TCN -> h0) and the fused rollout kernel.
+cudaError_t launch_skyjepa(const SkyjepaArgs& a, cudaStream_t stream, int* launches);
+
+}  // namespace lwm

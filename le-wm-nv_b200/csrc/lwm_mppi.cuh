@@ -1,0 +1,136 @@
+// lwm_mppi.cuh — MPPI weighting as a one-pass, multi-block reduction.
+//
+// Reference: mppi_weighted_sequence (src/planner.rs:1588-1602) computes
+//   w_s = softmax_s(-(score_s - min score) / lambda),  mean' = sum_s w_s cand_s
+// and lowest_score_indices(scores, 1) (src/planner.rs:1647) the argmin with
+// NaN ranked as +inf and ties to the lower index.
+//
+// Here every block reduces its own rows to a tuple
+//   (m_p = local min, W_p = sum exp((s - m_p) * mul), V_p[e] = sum exp(..) cand[e],
+//    key_p = smallest (score, index) key)
+// with mul = -1/lambda, and the last block of a vehicle to arrive rescales the
+// tuples by exp((m_p - M) * mul), M = global min, and writes mean' = V / W.
+// exp((s-m_p)mul) * exp((m_p-M)mul) = exp((s-M)mul), so this equals the
+// reference's softmax up to f32 rounding.
+#pragma once
+
+#include <cstdint>
+
+#include "lwm_device.cuh"
+#include "lwm_kernels.hpp"
+
+namespace lwm {
+
+template <int NT>
+__device__ __forceinline__ uint64_t block_min_u64(uint64_t v, uint64_t* scratch) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const uint64_t o = __shfl_xor_sync(0xffffffffu, v, off);
+        v = o < v ? o : v;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    uint64_t r = scratch[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w) r = scratch[w] < r ? scratch[w] : r;
+    return r;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum_f32(float v, float* scratch) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float r = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) r += scratch[w];
+    return r;
+}
+
+// All NT threads of the block call this.  Rows r in [0, nrows) of this block
+// have score s_score[r] (smem) and sample index first_sample + r; candidate
+// element e of row r is cand[r * row_stride + e] (smem or global).  s_w is
+// smem scratch of >= nrows floats.  Writes partial p of vehicle b and, if this
+// block is the last of the vehicle, the final outputs.
+template <int NT>
+__device__ void mppi_reduce_rows(const MppiArgs& a, uint32_t b, uint32_t p, uint32_t nrows,
+                                 const float* s_score, uint32_t first_sample, const float* cand,
+                                 size_t row_stride, float* s_w) {
+    __shared__ uint64_t s_key_scratch[NT / 32];
+    __shared__ float s_f_scratch[NT / 32];
+    __shared__ int s_is_last;
+    const uint32_t TA = a.T * a.A;
+
+    uint64_t key = ~0ull;
+    for (uint32_t r = threadIdx.x; r < nrows; r += NT) {
+        const uint64_t k = score_key(s_score[r], first_sample + r);
+        key = k < key ? k : key;
+    }
+    key = block_min_u64<NT>(key, s_key_scratch);
+    const float m = key_score(key);
+    float wsum = 0.0f;
+    for (uint32_t r = threadIdx.x; r < nrows; r += NT) {
+        const float w = expf((s_score[r] - m) * a.mul);
+        s_w[r] = w;
+        wsum += w;
+    }
+    wsum = block_sum_f32<NT>(wsum, s_f_scratch);  // contains __syncthreads: s_w visible
+    float* part = a.partials + (static_cast<size_t>(b) * a.P + p) * a.pw;
+    for (uint32_t e = threadIdx.x; e < TA; e += NT) {
+        float acc = 0.0f;
+        for (uint32_t r = 0; r < nrows; ++r) acc += s_w[r] * cand[r * row_stride + e];
+        part[4 + e] = acc;
+    }
+    if (threadIdx.x == 0) {
+        part[0] = m;
+        part[1] = wsum;
+        reinterpret_cast<uint64_t*>(part)[1] = key;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int done = atomicAdd(&a.counters[b], 1u);
+        s_is_last = (done == a.P - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_is_last) return;
+    __threadfence();
+
+    const float* base = a.partials + static_cast<size_t>(b) * a.P * a.pw;
+    uint64_t gkey = ~0ull;
+    for (uint32_t q = threadIdx.x; q < a.P; q += NT) {
+        const uint64_t k = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(q) * a.pw)[1];
+        gkey = k < gkey ? k : gkey;
+    }
+    gkey = block_min_u64<NT>(gkey, s_key_scratch);
+    const float M = key_score(gkey);
+    for (uint32_t e = threadIdx.x; e < TA; e += NT) {
+        float W = 0.0f, V = 0.0f;
+        for (uint32_t q = 0; q < a.P; ++q) {
+            const volatile float* pq = base + static_cast<size_t>(q) * a.pw;
+            if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;  // block without rows
+            const float f = expf((pq[0] - M) * a.mul);
+            W += pq[1] * f;
+            V += pq[4 + e] * f;
+        }
+        const float value = V / W;
+        const uint32_t t = e / a.A, act = e - t * a.A;
+        const size_t seq = static_cast<size_t>(b) * TA;
+        a.sequence[seq + e] = value;
+        if (t == 0) a.first_action[static_cast<size_t>(b) * a.A + act] = value;
+        if (t >= 1) a.warm_start[seq + e - a.A] = value;
+        if (t == a.T - 1) a.warm_start[seq + e] = value;
+    }
+    if (threadIdx.x == 0) {
+        a.best_index[b] = static_cast<uint32_t>(gkey & 0xffffffffu);
+        a.best_score[b] = M;
+        a.counters[b] = 0u;
+    }
+}
+
+}  // namespace lwm

@@ -1,0 +1,729 @@
+"""Python binding of liblewm_b200.so, the B200 sampling planner.
+
+Mirrors le-wm-nv's planner API (src/planner.rs) and SkyJEPA scorers
+(src/models/skyjepa/control.rs) over the C ABI declared in
+include/lewm_b200.h: ``MppiPlanner`` / ``CemPlanner`` / ``IcemPlanner`` with
+``plan`` and ``plan_device``, warm-start and RNG-offset methods, and the
+``NominalScorer``, ``SkyJepaScorer`` and ``CallbackScorer`` candidate scorers.
+
+The shared library is required: importing this module raises ImportError if it
+has not been built (``make -C le-wm-nv_b200``).  There is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import os
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblewm_b200.so")
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C le-wm-nv_b200`")
+lib = C.CDLL(LIB_PATH)
+
+MAX_ACTION_DIM = 16
+TCN_MAX_LEVELS = 8
+STATUS = {0: "OK", 1: "INVALID_ARGUMENT", 2: "CUDA_ERROR", 3: "DEADLINE", 4: "NCCL_ERROR", 5: "TIMEOUT", 6: "UNSUPPORTED"}
+
+F = C.c_float
+U32 = C.c_uint32
+U64 = C.c_uint64
+I32 = C.c_int32
+FP = C.POINTER(C.c_float)
+VP = C.c_void_p
+
+
+class LwmError(RuntimeError):
+    """A failing lwm_* call: .status is the lwm_status name."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = STATUS.get(status, str(status))
+        self.message = message
+
+
+# ------------------------------------------------------------------ structs
+
+class _MppiConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("iterations", U32), ("action_dim", U32),
+                ("bounds_low", F * MAX_ACTION_DIM), ("bounds_high", F * MAX_ACTION_DIM), ("noise_std", F),
+                ("has_noise_std_per_action", I32), ("noise_std_per_action", F * MAX_ACTION_DIM), ("temperature", F),
+                ("deadline_ns", C.c_int64), ("has_deadline_action", I32), ("deadline_action", F * MAX_ACTION_DIM),
+                ("has_seed", I32), ("seed", U64)]
+
+
+class _CemConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("elites", U32), ("iterations", U32), ("action_dim", U32),
+                ("bounds_low", F * MAX_ACTION_DIM), ("bounds_high", F * MAX_ACTION_DIM), ("init_std", F),
+                ("min_std", F), ("deadline_ns", C.c_int64), ("has_deadline_action", I32),
+                ("deadline_action", F * MAX_ACTION_DIM), ("has_seed", I32), ("seed", U64)]
+
+
+class _IcemConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("elites", U32), ("keep_elites", U32), ("iterations", U32),
+                ("noise_beta", F), ("alpha", F), ("action_dim", U32), ("bounds_low", F * MAX_ACTION_DIM),
+                ("bounds_high", F * MAX_ACTION_DIM), ("init_std", F), ("min_std", F), ("return_mean", I32),
+                ("deadline_ns", C.c_int64), ("has_deadline_action", I32), ("deadline_action", F * MAX_ACTION_DIM),
+                ("has_seed", I32), ("seed", U64)]
+
+
+class Domain(C.Structure):
+    """SkyJepaDomain (src/skyjepa_sim.rs:28-56)."""
+    _fields_ = [("mass", F), ("inertia", F * 3), ("motor_time_constant", F), ("drag", F * 3), ("thrust_scale", F),
+                ("torque_scale", F), ("arm_length", F), ("gravity", F), ("max_thrust_weight", F)]
+
+    @staticmethod
+    def default() -> "Domain":
+        d = Domain()
+        lib.lwm_domain_default(C.byref(d))
+        return d
+
+    @staticmethod
+    def sample(seed: int) -> "Domain":
+        d = Domain()
+        lib.lwm_domain_sample(U64(seed), C.byref(d))
+        return d
+
+    def hover_force(self) -> float:
+        return float(np.float32(self.mass) * np.float32(self.gravity) / (np.float32(4.0) * np.float32(self.thrust_scale)))
+
+
+class TrackingCost(C.Structure):
+    """SkyJepaTrackingCost (src/models/skyjepa/control.rs:19-37)."""
+    _fields_ = [("position", F), ("velocity", F), ("attitude", F), ("angular_velocity", F), ("action", F * 4)]
+
+    @staticmethod
+    def paper() -> "TrackingCost":
+        c = TrackingCost()
+        lib.lwm_tracking_cost_paper(C.byref(c))
+        return c
+
+    @staticmethod
+    def make(position, velocity, attitude, angular_velocity, action) -> "TrackingCost":
+        return TrackingCost(position, velocity, attitude, angular_velocity, (F * 4)(*action))
+
+
+class NominalScorerConfig(C.Structure):
+    _fields_ = [("dt", F), ("trim_scale", F), ("substeps", U32), ("cost", TrackingCost), ("domain", Domain)]
+
+
+class TcnConfig(C.Structure):
+    _fields_ = [("input_dim", U32), ("levels", U32), ("channels", U32 * TCN_MAX_LEVELS), ("kernel_size", U32)]
+
+
+class KinematicConfig(C.Structure):
+    _fields_ = [("mass", C.c_double), ("gravity", C.c_double), ("hover_throttle", C.c_double), ("action_space", I32)]
+
+
+class SkyJepaConfig(C.Structure):
+    """SkyJepaConfig + SkyJepaProberConfig (config.rs:45-55, prober.rs:10-16)."""
+    _fields_ = [("state_dim", U32), ("action_dim", U32), ("history_steps", U32), ("rollout_steps", U32),
+                ("latent_dim", U32), ("state_encoder", TcnConfig), ("action_encoder", TcnConfig),
+                ("prober_hidden_dim", U32), ("prober_hidden_layers", U32), ("kinematics", KinematicConfig)]
+
+    @staticmethod
+    def paper() -> "SkyJepaConfig":
+        c = SkyJepaConfig()
+        lib.lwm_skyjepa_config_paper(C.byref(c))
+        return c
+
+    @staticmethod
+    def wide() -> "SkyJepaConfig":
+        c = SkyJepaConfig()
+        lib.lwm_skyjepa_config_wide(C.byref(c))
+        return c
+
+    def weight_count(self) -> int:
+        return int(lib.lwm_skyjepa_weight_count(C.byref(self)))
+
+    def random_weights(self, seed: int) -> np.ndarray:
+        n = self.weight_count()
+        if n == 0:
+            raise LwmError(1, "invalid SkyJEPA configuration")
+        out = np.empty(n, dtype=np.float32)
+        _check(lib.lwm_skyjepa_random_weights(C.byref(self), U64(seed), _fp(out), C.c_size_t(n)))
+        return out
+
+
+class _PlanResult(C.Structure):
+    _fields_ = [("first_action", FP), ("sequence", FP), ("scores", FP), ("scores_capacity", C.c_size_t),
+                ("best_indices", C.POINTER(U32)), ("batch", U32), ("scores_cols", U32),
+                ("iterations_completed", U32), ("elapsed_ns", U64), ("deadline_reached", I32),
+                ("deadline_outcome", I32)]
+
+
+class _PlanDeviceResult(C.Structure):
+    _fields_ = [("first_action", VP), ("sequence", VP), ("scores", VP), ("best_indices", VP), ("batch", U32),
+                ("scores_cols", U32), ("iterations_completed", U32), ("elapsed_ns", U64),
+                ("deadline_reached", I32), ("deadline_outcome", I32)]
+
+
+SCORE_FN = C.CFUNCTYPE(C.c_int, VP, VP, U32, U32, U32, U32, VP, VP)
+
+# ------------------------------------------------------------- signatures
+
+def _sig(name, restype, *argtypes):
+    fn = getattr(lib, name)
+    fn.restype = restype
+    fn.argtypes = list(argtypes)
+    return fn
+
+
+_sig("lwm_last_error", C.c_char_p)
+_sig("lwm_version", C.c_char_p)
+_sig("lwm_abi_version", C.c_int)
+_sig("lwm_ctx_create", C.c_int, C.c_int, C.POINTER(VP))
+_sig("lwm_ctx_destroy", C.c_int, VP)
+_sig("lwm_ctx_stream", C.c_int, VP, C.POINTER(VP))
+_sig("lwm_ctx_synchronize", C.c_int, VP)
+_sig("lwm_ctx_launch_count", C.c_int, VP, C.POINTER(U64))
+_sig("lwm_mppi_config_default", None, U32, U32, U32, C.POINTER(_MppiConfig))
+_sig("lwm_cem_config_default", None, U32, U32, U32, U32, C.POINTER(_CemConfig))
+_sig("lwm_icem_config_default", None, U32, U32, U32, U32, C.POINTER(_IcemConfig))
+_sig("lwm_mppi_create", C.c_int, VP, C.POINTER(_MppiConfig), C.POINTER(VP))
+_sig("lwm_cem_create", C.c_int, VP, C.POINTER(_CemConfig), C.POINTER(VP))
+_sig("lwm_icem_create", C.c_int, VP, C.POINTER(_IcemConfig), C.POINTER(VP))
+_sig("lwm_planner_destroy", C.c_int, VP)
+_sig("lwm_planner_set_warm_start", C.c_int, VP, FP, U32, U32, U32)
+_sig("lwm_planner_clear_warm_start", C.c_int, VP)
+_sig("lwm_planner_warm_start", C.c_int, VP, FP, C.c_size_t, C.POINTER(U32))
+_sig("lwm_planner_reset_rng", C.c_int, VP)
+_sig("lwm_planner_rng_offset", C.c_int, VP, C.POINTER(U64))
+_sig("lwm_planner_last_candidates", C.c_int, VP, C.POINTER(VP), C.POINTER(U32))
+_sig("lwm_domain_default", None, C.POINTER(Domain))
+_sig("lwm_domain_sample", None, U64, C.POINTER(Domain))
+_sig("lwm_tracking_cost_paper", None, C.POINTER(TrackingCost))
+_sig("lwm_scorer_nominal_create", C.c_int, VP, C.POINTER(NominalScorerConfig), C.POINTER(VP))
+_sig("lwm_scorer_nominal_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP, C.POINTER(Domain))
+_sig("lwm_skyjepa_config_paper", None, C.POINTER(SkyJepaConfig))
+_sig("lwm_skyjepa_config_wide", None, C.POINTER(SkyJepaConfig))
+_sig("lwm_skyjepa_weight_count", C.c_size_t, C.POINTER(SkyJepaConfig))
+_sig("lwm_skyjepa_random_weights", C.c_int, C.POINTER(SkyJepaConfig), U64, FP, C.c_size_t)
+_sig("lwm_scorer_skyjepa_create", C.c_int, VP, C.POINTER(SkyJepaConfig), FP, C.c_size_t, FP, FP, FP, FP,
+     C.POINTER(TrackingCost), F, C.POINTER(VP))
+_sig("lwm_scorer_skyjepa_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP)
+_sig("lwm_scorer_callback_create", C.c_int, VP, U32, SCORE_FN, VP, C.POINTER(VP))
+_sig("lwm_scorer_score_device", C.c_int, VP, VP, U32, U32, U32, U32, VP)
+_sig("lwm_scorer_predict_device", C.c_int, VP, VP, U32, U32, U32, VP)
+_sig("lwm_scorer_destroy", C.c_int, VP)
+_sig("lwm_plan", C.c_int, VP, VP, FP, C.POINTER(_PlanResult))
+_sig("lwm_plan_device", C.c_int, VP, VP, VP, C.POINTER(_PlanDeviceResult))
+_sig("lwm_lowest_k_device", C.c_int, VP, VP, U32, U32, U32, VP)
+_sig("lwm_color_noise_device", C.c_int, VP, VP, VP, U32, U32, U32, U32, F)
+_sig("lwm_normal_device", C.c_int, VP, U64, U64, C.c_size_t, VP)
+_sig("lwm_skyjepa_reference_horizon", C.c_int, I32, F, F, U32, F, F, FP)
+_sig("lwm_skyjepa_geometric_prior", C.c_int, FP, FP, U32, F, C.POINTER(Domain), FP)
+_sig("lwm_rotor_plant_step", C.c_int, C.POINTER(Domain), FP, FP, FP, F)
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise LwmError(status, lib.lwm_last_error().decode())
+
+
+def _fp(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(FP)
+
+
+def _f32(x, shape=None) -> np.ndarray:
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    if shape is not None:
+        a = a.reshape(shape)
+    return a
+
+
+def version() -> str:
+    return lib.lwm_version().decode()
+
+
+# ------------------------------------------------------------------- context
+
+class Context:
+    """A CUDA device and stream (Device::new_cuda, src/runtime.rs:7-18)."""
+
+    def __init__(self, device: int = 0):
+        h = VP()
+        _check(lib.lwm_ctx_create(device, C.byref(h)))
+        self.handle = h
+        self.device = device
+
+    @property
+    def stream(self) -> int:
+        s = VP()
+        _check(lib.lwm_ctx_stream(self.handle, C.byref(s)))
+        return int(s.value or 0)
+
+    def synchronize(self) -> None:
+        _check(lib.lwm_ctx_synchronize(self.handle))
+
+    def launch_count(self) -> int:
+        n = U64()
+        _check(lib.lwm_ctx_launch_count(self.handle, C.byref(n)))
+        return int(n.value)
+
+    def torch_stream(self):
+        import torch
+        return torch.cuda.ExternalStream(self.stream, device=torch.device("cuda", self.device))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib.lwm_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------- configs
+
+def _bounds(arr, action_dim, default):
+    out = (F * MAX_ACTION_DIM)()
+    vals = list(arr) if arr is not None else [default] * action_dim
+    for i, v in enumerate(vals[:MAX_ACTION_DIM]):
+        out[i] = v
+    return out
+
+
+@dataclass
+class ActionBounds:
+    """ActionBounds (src/planner.rs:67-83)."""
+    low: List[float]
+    high: List[float]
+
+    @staticmethod
+    def symmetric(action_dim: int, limit: float) -> "ActionBounds":
+        return ActionBounds([-limit] * action_dim, [limit] * action_dim)
+
+    @staticmethod
+    def scalar(action_dim: int, low: float, high: float) -> "ActionBounds":
+        return ActionBounds([low] * action_dim, [high] * action_dim)
+
+
+@dataclass
+class MppiConfig:
+    """MppiConfig (src/planner.rs:178-208); deadline in seconds."""
+    horizon: int
+    samples: int
+    action_dim: int
+    iterations: int = 1
+    action_bounds: Optional[ActionBounds] = None
+    noise_std: float = 1.0
+    noise_std_per_action: Optional[Sequence[float]] = None
+    temperature: float = 1.0
+    deadline: Optional[float] = None
+    deadline_action: Optional[Sequence[float]] = None
+    seed: Optional[int] = None
+
+    def _c(self) -> _MppiConfig:
+        c = _MppiConfig()
+        lib.lwm_mppi_config_default(self.horizon, self.samples, self.action_dim, C.byref(c))
+        c.iterations = self.iterations
+        b = self.action_bounds or ActionBounds.symmetric(self.action_dim, 1.0)
+        c.bounds_low = _bounds(b.low, self.action_dim, -1.0)
+        c.bounds_high = _bounds(b.high, self.action_dim, 1.0)
+        c.noise_std = self.noise_std
+        if self.noise_std_per_action is not None:
+            if len(self.noise_std_per_action) != self.action_dim:
+                raise LwmError(1, f"MPPI per-action noise length {len(self.noise_std_per_action)} must match "
+                                  f"action_dim {self.action_dim}")
+            c.has_noise_std_per_action = 1
+            c.noise_std_per_action = _bounds(self.noise_std_per_action, self.action_dim, 1.0)
+        c.temperature = self.temperature
+        c.deadline_ns = -1 if self.deadline is None else int(self.deadline * 1e9)
+        if self.deadline_action is not None:
+            if len(self.deadline_action) != self.action_dim:
+                raise LwmError(1, f"MPPI deadline_action length {len(self.deadline_action)} must match "
+                                  f"action_dim {self.action_dim}")
+            c.has_deadline_action = 1
+            c.deadline_action = _bounds(self.deadline_action, self.action_dim, 0.0)
+        if self.seed is not None:
+            c.has_seed = 1
+            c.seed = self.seed
+        return c
+
+
+@dataclass
+class CemConfig:
+    """CemConfig (src/planner.rs:107-137)."""
+    horizon: int
+    samples: int
+    elites: int
+    action_dim: int
+    iterations: int = 4
+    action_bounds: Optional[ActionBounds] = None
+    init_std: float = 1.0
+    min_std: float = 1e-3
+    deadline: Optional[float] = None
+    deadline_action: Optional[Sequence[float]] = None
+    seed: Optional[int] = None
+
+    def _c(self) -> _CemConfig:
+        c = _CemConfig()
+        lib.lwm_cem_config_default(self.horizon, self.samples, self.elites, self.action_dim, C.byref(c))
+        c.iterations = self.iterations
+        b = self.action_bounds or ActionBounds.symmetric(self.action_dim, 1.0)
+        c.bounds_low = _bounds(b.low, self.action_dim, -1.0)
+        c.bounds_high = _bounds(b.high, self.action_dim, 1.0)
+        c.init_std = self.init_std
+        c.min_std = self.min_std
+        c.deadline_ns = -1 if self.deadline is None else int(self.deadline * 1e9)
+        if self.deadline_action is not None:
+            c.has_deadline_action = 1
+            c.deadline_action = _bounds(self.deadline_action, self.action_dim, 0.0)
+        if self.seed is not None:
+            c.has_seed = 1
+            c.seed = self.seed
+        return c
+
+
+@dataclass
+class IcemConfig:
+    """IcemConfig (src/planner.rs:256-295)."""
+    horizon: int
+    samples: int
+    elites: int
+    action_dim: int
+    keep_elites: Optional[int] = None
+    iterations: int = 4
+    noise_beta: float = 2.0
+    alpha: float = 0.1
+    action_bounds: Optional[ActionBounds] = None
+    init_std: float = 1.0
+    min_std: float = 1e-3
+    return_mean: bool = True
+    deadline: Optional[float] = None
+    deadline_action: Optional[Sequence[float]] = None
+    seed: Optional[int] = None
+
+    def _c(self) -> _IcemConfig:
+        c = _IcemConfig()
+        lib.lwm_icem_config_default(self.horizon, self.samples, self.elites, self.action_dim, C.byref(c))
+        c.keep_elites = self.elites if self.keep_elites is None else self.keep_elites
+        c.iterations = self.iterations
+        c.noise_beta = self.noise_beta
+        c.alpha = self.alpha
+        b = self.action_bounds or ActionBounds.symmetric(self.action_dim, 1.0)
+        c.bounds_low = _bounds(b.low, self.action_dim, -1.0)
+        c.bounds_high = _bounds(b.high, self.action_dim, 1.0)
+        c.init_std = self.init_std
+        c.min_std = self.min_std
+        c.return_mean = 1 if self.return_mean else 0
+        c.deadline_ns = -1 if self.deadline is None else int(self.deadline * 1e9)
+        if self.deadline_action is not None:
+            c.has_deadline_action = 1
+            c.deadline_action = _bounds(self.deadline_action, self.action_dim, 0.0)
+        if self.seed is not None:
+            c.has_seed = 1
+            c.seed = self.seed
+        return c
+
+
+# ------------------------------------------------------------------- results
+
+@dataclass
+class PlanResult:
+    """PlanResult (src/planner.rs:355-366) as numpy arrays."""
+    first_action: np.ndarray
+    sequence: np.ndarray
+    scores: np.ndarray
+    best_indices: List[int]
+    iterations_completed: int
+    elapsed: float
+    deadline_reached: bool
+    deadline_outcome: str
+
+
+@dataclass
+class PlanDeviceResult:
+    """PlanDeviceResult (src/planner.rs:368-379): device addresses owned by the
+    planner, valid until its next plan call."""
+    first_action: int
+    sequence: int
+    scores: int
+    best_indices: int
+    batch: int
+    scores_cols: int
+    iterations_completed: int
+    elapsed: float
+    deadline_reached: bool
+    deadline_outcome: str
+
+
+_OUTCOME = {0: "None", 1: "WarmStart", 2: "ConfiguredAction"}
+
+
+# ------------------------------------------------------------------- scorers
+
+class Scorer:
+    handle = None
+    batch = 0
+    ctx: Context
+
+    def score_device(self, candidates_ptr: int, batch: int, samples: int, horizon: int, action_dim: int,
+                     scores_ptr: int) -> None:
+        _check(lib.lwm_scorer_score_device(self.handle, VP(candidates_ptr), batch, samples, horizon, action_dim,
+                                           VP(scores_ptr)))
+
+    def predict_device(self, candidates_ptr: int, batch: int, samples: int, horizon: int, states_ptr: int) -> None:
+        _check(lib.lwm_scorer_predict_device(self.handle, VP(candidates_ptr), batch, samples, horizon,
+                                             VP(states_ptr)))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib.lwm_scorer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class NominalScorer(Scorer):
+    """SkyJepaNominalScorer (src/models/skyjepa/control.rs:332-428)."""
+
+    def __init__(self, ctx: Context, dt: float, trim_scale: float, cost: TrackingCost, substeps: int = 10,
+                 domain: Optional[Domain] = None):
+        self.ctx = ctx
+        cfg = NominalScorerConfig(dt, trim_scale, substeps, cost, domain or Domain.default())
+        h = VP()
+        _check(lib.lwm_scorer_nominal_create(ctx.handle, C.byref(cfg), C.byref(h)))
+        self.handle = h
+
+    def set_context(self, initial, motors, reference_states, reference_actions, domains=None) -> None:
+        initial = _f32(initial)
+        B = initial.shape[0]
+        ref = _f32(reference_states)
+        T = ref.shape[1]
+        dom = None
+        if domains is not None:
+            dom = (Domain * B)(*domains)
+        _check(lib.lwm_scorer_nominal_set_context(self.handle, B, T, _fp(initial), _fp(_f32(motors)), _fp(ref),
+                                                  _fp(_f32(reference_actions)), dom))
+        self.batch = B
+
+
+class SkyJepaScorer(Scorer):
+    """SkyJepaMppiScorer (src/models/skyjepa/control.rs:146-317)."""
+
+    def __init__(self, ctx: Context, config: SkyJepaConfig, weights: np.ndarray, state_mean, state_std,
+                 action_mean, action_std, cost: TrackingCost, dt: float):
+        self.ctx = ctx
+        self.config = config
+        w = _f32(weights)
+        h = VP()
+        _check(lib.lwm_scorer_skyjepa_create(ctx.handle, C.byref(config), _fp(w), C.c_size_t(w.size),
+                                             _fp(_f32(state_mean)), _fp(_f32(state_std)), _fp(_f32(action_mean)),
+                                             _fp(_f32(action_std)), C.byref(cost), F(dt), C.byref(h)))
+        self.handle = h
+
+    def set_context(self, state_history, action_history, reference_states, reference_actions) -> None:
+        sh = _f32(state_history)
+        ref = _f32(reference_states)
+        _check(lib.lwm_scorer_skyjepa_set_context(self.handle, sh.shape[0], ref.shape[1], _fp(sh),
+                                                  _fp(_f32(action_history)), _fp(ref), _fp(_f32(reference_actions))))
+        self.batch = sh.shape[0]
+
+
+class _CudaArray:
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_tensor(ptr: int, shape, dtype: str = "f4"):
+    """A torch view of device memory owned by the library (no copy)."""
+    import torch
+    return torch.as_tensor(_CudaArray(ptr, shape, "<" + dtype), device="cuda")
+
+
+class CallbackScorer(Scorer):
+    """The CandidateScorer trait (src/planner.rs:25-32) implemented by a
+    Python callable ``fn(candidates: torch.Tensor[B,S,T,A]) -> torch.Tensor[B,S]``
+    that runs on the context stream."""
+
+    def __init__(self, ctx: Context, batch: int, fn: Callable):
+        import torch
+        self.ctx = ctx
+        self.batch = batch
+        self._fn = fn
+
+        def trampoline(user, cand, B, S, T, A, scores, stream):
+            try:
+                with torch.cuda.stream(torch.cuda.ExternalStream(stream)):
+                    cands = device_tensor(cand, (B, S, T, A))
+                    out = device_tensor(scores, (B, S))
+                    out.copy_(fn(cands).reshape(B, S).to(torch.float32))
+                return 0
+            except Exception as exc:  # surfaced as LwmError by the caller
+                self.error = exc
+                return 1
+
+        self._cb = SCORE_FN(trampoline)
+        h = VP()
+        _check(lib.lwm_scorer_callback_create(ctx.handle, batch, self._cb, None, C.byref(h)))
+        self.handle = h
+
+
+# ------------------------------------------------------------------- planners
+
+class _Planner:
+    kind = ""
+
+    def __init__(self, ctx: Context, config):
+        self.ctx = ctx
+        self.config = config
+        self._cfg = config._c()
+        h = VP()
+        _check(self._create(ctx.handle, C.byref(self._cfg), C.byref(h)))
+        self.handle = h
+
+    def plan(self, scorer: Scorer, injected_noise: Optional[np.ndarray] = None, batch: Optional[int] = None) -> PlanResult:
+        cfg = self.config
+        B = batch or scorer.batch
+        T, A, S = cfg.horizon, cfg.action_dim, cfg.samples
+        fa = np.empty((B, A), np.float32)
+        seq = np.empty((B, T, A), np.float32)
+        sc = np.empty((B, S), np.float32)
+        best = np.empty((B,), np.uint32)
+        r = _PlanResult(_fp(fa), _fp(seq), _fp(sc), C.c_size_t(sc.size), best.ctypes.data_as(C.POINTER(U32)))
+        noise = None if injected_noise is None else _f32(injected_noise)
+        _check(lib.lwm_plan(self.handle, scorer.handle, _fp(noise), C.byref(r)))
+        cols = r.scores_cols
+        return PlanResult(fa, seq, sc.reshape(-1)[: B * cols].reshape(B, cols).copy(), [int(x) for x in best],
+                          int(r.iterations_completed), r.elapsed_ns * 1e-9, bool(r.deadline_reached),
+                          _OUTCOME[r.deadline_outcome])
+
+    def plan_device(self, scorer: Scorer, injected_noise_ptr: Optional[int] = None) -> PlanDeviceResult:
+        r = _PlanDeviceResult()
+        _check(lib.lwm_plan_device(self.handle, scorer.handle, VP(injected_noise_ptr) if injected_noise_ptr else None,
+                                   C.byref(r)))
+        return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
+                                r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
+                                _OUTCOME[r.deadline_outcome])
+
+    def last_candidates_ptr(self) -> int:
+        p = VP()
+        s = U32()
+        _check(lib.lwm_planner_last_candidates(self.handle, C.byref(p), C.byref(s)))
+        return int(p.value)
+
+    def set_warm_start_sequence(self, sequence) -> None:
+        seq = _f32(sequence)
+        if seq.ndim != 3:
+            raise LwmError(1, f"{self.kind} warm-start must be [batch, horizon, action_dim], got {list(seq.shape)}")
+        _check(lib.lwm_planner_set_warm_start(self.handle, _fp(seq), seq.shape[0], seq.shape[1], seq.shape[2]))
+
+    def clear_warm_start(self) -> None:
+        _check(lib.lwm_planner_clear_warm_start(self.handle))
+
+    def warm_start_sequence(self, max_batch: int = 4096) -> Optional[np.ndarray]:
+        cfg = self.config
+        buf = np.empty((max_batch, cfg.horizon, cfg.action_dim), np.float32)
+        b = U32()
+        _check(lib.lwm_planner_warm_start(self.handle, _fp(buf), C.c_size_t(buf.size), C.byref(b)))
+        return None if b.value == 0 else buf[: b.value].copy()
+
+    def reset_rng_sequence(self) -> None:
+        _check(lib.lwm_planner_reset_rng(self.handle))
+
+    def rng_offset(self) -> int:
+        o = U64()
+        _check(lib.lwm_planner_rng_offset(self.handle, C.byref(o)))
+        return int(o.value)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib.lwm_planner_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MppiPlanner(_Planner):
+    """MppiPlanner (src/planner.rs:544-729)."""
+    kind = "MPPI"
+    _create = staticmethod(lib.lwm_mppi_create)
+
+
+class CemPlanner(_Planner):
+    """CemPlanner (src/planner.rs:418-541)."""
+    kind = "CEM"
+    _create = staticmethod(lib.lwm_cem_create)
+
+    def set_warm_start_sequence(self, sequence) -> None:  # CEM has no warm start in the reference
+        raise LwmError(1, "CEM planners have no warm start")
+
+
+class IcemPlanner(_Planner):
+    """IcemPlanner (src/planner.rs:731-1053)."""
+    kind = "iCEM"
+    _create = staticmethod(lib.lwm_icem_create)
+
+
+# ------------------------------------------------------- device building blocks
+
+def lowest_k_device(ctx: Context, scores_ptr: int, batch: int, samples: int, count: int, out_ptr: int) -> None:
+    _check(lib.lwm_lowest_k_device(ctx.handle, VP(scores_ptr), batch, samples, count, VP(out_ptr)))
+
+
+def color_noise_device(ctx: Context, in_ptr: int, out_ptr: int, batch: int, samples: int, horizon: int,
+                       action_dim: int, beta: float) -> None:
+    _check(lib.lwm_color_noise_device(ctx.handle, VP(in_ptr), VP(out_ptr), batch, samples, horizon, action_dim,
+                                      F(beta)))
+
+
+def normal_device(ctx: Context, seed: int, offset: int, count: int, out_ptr: int) -> None:
+    _check(lib.lwm_normal_device(ctx.handle, U64(seed), U64(offset), C.c_size_t(count), VP(out_ptr)))
+
+
+# ----------------------------------------------------------------- task inputs
+
+REFERENCE_KINDS = {"hover": 0, "circle": 1, "figure-eight": 2, "figure8": 2}
+
+
+def reference_horizon(kind: str, time: float, dt: float, horizon: int, radius: float, period: float) -> np.ndarray:
+    """skyjepa_reference_horizon (src/skyjepa_task.rs:44-55)."""
+    out = np.empty((horizon, 18), np.float32)
+    _check(lib.lwm_skyjepa_reference_horizon(REFERENCE_KINDS[kind], F(time), F(dt), horizon, F(radius), F(period),
+                                             _fp(out)))
+    return out
+
+
+def geometric_prior(current_state, references, dt: float, domain: Optional[Domain] = None) -> np.ndarray:
+    """skyjepa_geometric_action_prior (src/skyjepa_task.rs:118-162)."""
+    refs = _f32(references)
+    out = np.empty((refs.shape[0], 4), np.float32)
+    d = domain or Domain.default()
+    _check(lib.lwm_skyjepa_geometric_prior(_fp(_f32(current_state)), _fp(refs), refs.shape[0], F(dt), C.byref(d),
+                                           _fp(out)))
+    return out
+
+
+def plant_step(domain: Domain, state: np.ndarray, motors: np.ndarray, command, dt: float) -> None:
+    """SkyJepaRotorPlant::step (src/skyjepa_sim.rs:206-270), in place."""
+    _check(lib.lwm_rotor_plant_step(C.byref(domain), _fp(state), _fp(motors), _fp(_f32(command)), F(dt)))
+
+
+def hover_state() -> np.ndarray:
+    """SkyJepaRotorState::hover().as_state18() (src/skyjepa_sim.rs:134-154)."""
+    s = np.zeros(18, np.float32)
+    s[2] = 1.0
+    s[6] = s[10] = s[14] = 1.0
+    return s
+

@@ -1,0 +1,393 @@
+"""ctypes wrapper of the CPU oracle (liblewm_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by __graft_entry__.smoke() as the
+checker, and by bench.py's CPU-baseline / reference leg.  The product library
+(le-wm-nv_b200) never imports, links or calls this module.
+
+The library is built by oracle/Makefile (`make -C oracle`).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import sys
+from typing import Optional
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblewm_oracle.so")
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C oracle`")
+lib = C.CDLL(LIB_PATH)
+
+sys.path.insert(0, os.path.join(os.path.dirname(_HERE), "le-wm-nv_b200"))
+# Struct layouts only (ctypes mirrors of include/lewm_b200.h); no product call.
+from lewm_b200 import (  # noqa: E402
+    Domain, TrackingCost, SkyJepaConfig, KinematicConfig, _MppiConfig, _CemConfig, _IcemConfig,
+)
+
+F = C.c_float
+U32 = C.c_uint32
+U64 = C.c_uint64
+FP = C.POINTER(C.c_float)
+UP = C.POINTER(C.c_uint32)
+VP = C.c_void_p
+SCORE_FN = C.CFUNCTYPE(None, VP, FP, U32, U32, U32, U32, FP)
+
+
+class NominalCtx(C.Structure):
+    _fields_ = [("initial", FP), ("motors", FP), ("ref_states", FP), ("ref_actions", FP), ("cost", TrackingCost),
+                ("dt", F), ("trim_scale", F), ("substeps", U32), ("domain", Domain), ("domains", C.POINTER(Domain))]
+
+
+class SkyCtx(C.Structure):
+    _fields_ = [("model", VP), ("state_mean", FP), ("state_std", FP), ("action_mean", FP), ("action_std", FP),
+                ("state_hist", FP), ("action_hist", FP), ("ref_states", FP), ("ref_actions", FP),
+                ("cost", TrackingCost), ("dt", F)]
+
+
+def _sig(name, restype, *args):
+    f = getattr(lib, name)
+    f.restype = restype
+    f.argtypes = list(args)
+
+
+_sig("orc_set_threads", None, C.c_int)
+_sig("orc_get_threads", C.c_int)
+_sig("orc_philox4x32_10", None, U64, U64, UP)
+_sig("orc_normal_at", F, U64, U64)
+_sig("orc_normals", None, U64, U64, C.c_size_t, FP)
+_sig("orc_sample", None, FP, FP, FP, FP, FP, U32, U32, U32, U32, FP)
+_sig("orc_color_noise", None, FP, FP, U32, U32, U32, U32, F)
+_sig("orc_inject_carried", None, FP, FP, U32, U32, U32, U32, U32, U32)
+_sig("orc_mppi_weighted", None, FP, FP, U32, U32, U32, U32, F, FP)
+_sig("orc_lowest_k", None, FP, U32, U32, U32, UP)
+_sig("orc_gather", None, FP, UP, U32, U32, U32, U32, U32, FP)
+_sig("orc_refit", None, FP, U32, U32, U32, U32, F, FP, FP)
+_sig("orc_momentum", None, FP, FP, C.c_size_t, F, FP)
+_sig("orc_shift", None, FP, U32, U32, U32, FP)
+_sig("orc_plant_step", None, C.POINTER(Domain), FP, FP, FP, F)
+_sig("orc_nominal_rollout", None, FP, FP, FP, U32, U32, F, U32, C.POINTER(Domain), FP)
+_sig("orc_nominal_rollout_k4", None, FP, FP, FP, U32, U32, F, U32, C.POINTER(Domain), FP)
+_sig("orc_tracking_scores", None, FP, FP, FP, FP, C.POINTER(TrackingCost), U32, U32, U32, FP)
+_sig("orc_nominal_scores", None, FP, FP, FP, FP, C.POINTER(TrackingCost), F, F, U32, C.POINTER(Domain),
+     C.POINTER(Domain), FP, U32, U32, U32, FP, FP)
+_sig("orc_skyjepa_new", VP, C.POINTER(SkyJepaConfig), FP, C.c_size_t)
+_sig("orc_skyjepa_free", None, VP)
+_sig("orc_skyjepa_weight_count", C.c_size_t, C.POINTER(SkyJepaConfig))
+_sig("orc_tcn_forward_last", None, VP, C.c_int, FP, U32, U32, FP)
+_sig("orc_initial_latent", None, VP, FP, U32, FP)
+_sig("orc_gru_step", None, VP, FP, FP, U32, FP)
+_sig("orc_rollout_latents", None, VP, FP, FP, FP, U32, U32, U32, FP)
+_sig("orc_prober", None, VP, FP, U32, FP)
+_sig("orc_integrate_k3", None, FP, FP, FP, FP, FP, U32, U32, C.POINTER(KinematicConfig), FP)
+_sig("orc_integrate_reference", None, FP, FP, FP, FP, FP, U32, U32, C.POINTER(KinematicConfig), FP)
+_sig("orc_so3_exp", None, FP, FP)
+_sig("orc_skyjepa_scores", None, VP, FP, FP, FP, FP, FP, FP, FP, FP, C.POINTER(TrackingCost), F, FP, U32, U32,
+     U32, FP, FP)
+_sig("orc_mppi_plan", C.c_int, C.POINTER(_MppiConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
+_sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, FP, FP, UP, FP)
+_sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
+_sig("orc_reference_state", None, C.c_int, F, F, F, FP)
+_sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
+
+NOMINAL_FN = C.cast(lib.orc_nominal_score_fn, VP)
+SKYJEPA_FN = C.cast(lib.orc_skyjepa_score_fn, VP)
+
+
+def f32(x) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+
+
+def fp(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"], (a.dtype, a.flags)
+    return a.ctypes.data_as(FP)
+
+
+def up(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.dtype == np.uint32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(UP)
+
+
+def set_threads(n: int) -> None:
+    lib.orc_set_threads(n)
+
+
+def normals(seed: int, offset: int, count: int) -> np.ndarray:
+    out = np.empty(count, np.float32)
+    lib.orc_normals(seed, offset, count, fp(out))
+    return out
+
+
+def philox(counter: int, key: int) -> np.ndarray:
+    out = np.empty(4, np.uint32)
+    lib.orc_philox4x32_10(counter, key, up(out))
+    return out
+
+
+def sample(mean, std, noise, low, high):
+    noise = f32(noise)
+    B, S, T, A = noise.shape
+    out = np.empty_like(noise)
+    lib.orc_sample(fp(f32(mean)), fp(f32(std)), fp(noise), fp(f32(low)), fp(f32(high)), B, S, T, A, fp(out))
+    return out
+
+
+def color_noise(noise, beta):
+    noise = f32(noise)
+    out = np.empty_like(noise)
+    lib.orc_color_noise(fp(noise), fp(out), *noise.shape, F(beta))
+    return out
+
+
+def inject_carried(cand, carried, keep):
+    cand = f32(cand).copy()
+    carried = f32(carried)
+    B, S, T, A = cand.shape
+    lib.orc_inject_carried(fp(cand), fp(carried), carried.shape[1], keep, B, S, T, A)
+    return cand
+
+
+def mppi_weighted(cand, scores, temperature):
+    cand = f32(cand)
+    B, S, T, A = cand.shape
+    out = np.empty((B, T, A), np.float32)
+    lib.orc_mppi_weighted(fp(cand), fp(f32(scores)), B, S, T, A, F(temperature), fp(out))
+    return out
+
+
+def lowest_k(scores, k):
+    scores = f32(scores)
+    B, S = scores.shape
+    out = np.empty((B, k), np.uint32)
+    lib.orc_lowest_k(fp(scores), B, S, k, up(out))
+    return out
+
+
+def gather(cand, idx):
+    cand = f32(cand)
+    idx = np.ascontiguousarray(idx, dtype=np.uint32)
+    B, S, T, A = cand.shape
+    k = idx.shape[1]
+    out = np.empty((B, k, T, A), np.float32)
+    lib.orc_gather(fp(cand), up(idx), B, S, k, T, A, fp(out))
+    return out
+
+
+def refit(elites, min_std):
+    elites = f32(elites)
+    B, k, T, A = elites.shape
+    mean = np.empty((B, T, A), np.float32)
+    std = np.empty((B, T, A), np.float32)
+    lib.orc_refit(fp(elites), B, k, T, A, F(min_std), fp(mean), fp(std))
+    return mean, std
+
+
+def shift(seq):
+    seq = f32(seq)
+    out = np.empty_like(seq)
+    lib.orc_shift(fp(seq), *seq.shape, fp(out))
+    return out
+
+
+def plant_step(domain, state, motors, cmd, dt):
+    lib.orc_plant_step(C.byref(domain), fp(state), fp(motors), fp(f32(cmd)), F(dt))
+
+
+def nominal_rollout(initial, actions, motors, dt, substeps, domain, kernel_form=False):
+    actions = f32(actions)
+    N, T, _ = actions.shape
+    out = np.empty((N, T, 18), np.float32)
+    fn = lib.orc_nominal_rollout_k4 if kernel_form else lib.orc_nominal_rollout
+    fn(fp(f32(initial)), fp(actions), fp(f32(motors)), N, T, F(dt), substeps, C.byref(domain), fp(out))
+    return out
+
+
+def tracking_scores(pred, actions, ref_states, ref_actions, cost):
+    pred = f32(pred)
+    B, S, T, _ = pred.shape
+    out = np.empty((B, S), np.float32)
+    lib.orc_tracking_scores(fp(pred), fp(f32(actions)), fp(f32(ref_states)), fp(f32(ref_actions)), C.byref(cost),
+                            B, S, T, fp(out))
+    return out
+
+
+def nominal_scores(initial, motors, ref_states, ref_actions, cost, dt, trim, cand, substeps=10, domain=None,
+                   domains=None, with_states=False):
+    cand = f32(cand)
+    B, S, T, _ = cand.shape
+    scores = np.empty((B, S), np.float32)
+    states = np.empty((B, S, T, 18), np.float32) if with_states else None
+    d = domain or Domain.default()
+    dd = (Domain * B)(*domains) if domains is not None else None
+    lib.orc_nominal_scores(fp(f32(initial)), fp(f32(motors)), fp(f32(ref_states)), fp(f32(ref_actions)),
+                           C.byref(cost), F(dt), F(trim), substeps, C.byref(d), dd, fp(cand), B, S, T, fp(scores),
+                           fp(states))
+    return (scores, states) if with_states else scores
+
+
+class SkyJepaModel:
+    """Oracle SkyJEPA model over a weight blob (the layout of include/lewm_b200.h)."""
+
+    def __init__(self, cfg: SkyJepaConfig, weights: np.ndarray):
+        self.cfg = cfg
+        self.weights = f32(weights)
+        n = lib.orc_skyjepa_weight_count(C.byref(cfg))
+        if n != self.weights.size:
+            raise ValueError(f"weight blob has {self.weights.size} values, oracle layout needs {n}")
+        self.handle = lib.orc_skyjepa_new(C.byref(cfg), fp(self.weights), self.weights.size)
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib.orc_skyjepa_free(self.handle)
+            self.handle = None
+
+    def tcn_last(self, which: int, x):
+        x = f32(x)
+        N, time, _ = x.shape
+        enc = self.cfg.action_encoder if which else self.cfg.state_encoder
+        out = np.empty((N, enc.channels[enc.levels - 1]), np.float32)
+        lib.orc_tcn_forward_last(self.handle, which, fp(x), N, time, fp(out))
+        return out
+
+    def initial_latent(self, norm_state_hist):
+        x = f32(norm_state_hist)
+        out = np.empty((x.shape[0], self.cfg.latent_dim), np.float32)
+        lib.orc_initial_latent(self.handle, fp(x), x.shape[0], fp(out))
+        return out
+
+    def gru_step(self, x, h):
+        x, h = f32(x), f32(h)
+        out = np.empty_like(h)
+        lib.orc_gru_step(self.handle, fp(x), fp(h), h.shape[0], fp(out))
+        return out
+
+    def rollout_latents(self, nsh, nah, ncand):
+        ncand = f32(ncand)
+        B, S, T, _ = ncand.shape
+        out = np.empty((B, S, T, self.cfg.latent_dim), np.float32)
+        lib.orc_rollout_latents(self.handle, fp(f32(nsh)), fp(f32(nah)), fp(ncand), B, S, T, fp(out))
+        return out
+
+    def prober(self, latents):
+        lat = f32(latents)
+        N = lat.size // self.cfg.latent_dim
+        out = np.empty((N, 15), np.float32)
+        lib.orc_prober(self.handle, fp(lat), N, fp(out))
+        return out
+
+    def scores(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt, cand, with_states=False):
+        cand = f32(cand)
+        B, S, T, _ = cand.shape
+        scores = np.empty((B, S), np.float32)
+        states = np.empty((B, S, T, 18), np.float32) if with_states else None
+        sm, ss, am, as_ = (f32(v) for v in norm)
+        lib.orc_skyjepa_scores(self.handle, fp(sm), fp(ss), fp(am), fp(as_), fp(f32(state_hist)),
+                               fp(f32(action_hist)), fp(f32(ref_states)), fp(f32(ref_actions)), C.byref(cost),
+                               F(dt), fp(cand), B, S, T, fp(scores), fp(states))
+        return (scores, states) if with_states else scores
+
+    def score_ctx(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt):
+        keep = [f32(v) for v in norm] + [f32(state_hist), f32(action_hist), f32(ref_states), f32(ref_actions)]
+        ctx = SkyCtx(self.handle, *(fp(v) for v in keep), cost, dt)
+        ctx._keep = keep
+        return ctx
+
+
+def integrate(initial, actions, dt, residual, maps, kin, reference_form=False):
+    actions = f32(actions)
+    N, T, _ = actions.shape
+    out = np.empty((N, T, 18), np.float32)
+    fn = lib.orc_integrate_reference if reference_form else lib.orc_integrate_k3
+    fn(fp(f32(initial)), fp(actions), fp(f32(dt)), fp(f32(residual)), fp(f32(maps)), N, T, C.byref(kin), fp(out))
+    return out
+
+
+def so3_exp(w):
+    out = np.empty(9, np.float32)
+    lib.orc_so3_exp(fp(f32(w)), fp(out))
+    return out.reshape(3, 3)
+
+
+def nominal_ctx(initial, motors, ref_states, ref_actions, cost, dt, trim, substeps=10, domain=None, domains=None):
+    keep = [f32(initial), f32(motors), f32(ref_states), f32(ref_actions)]
+    dd = (Domain * len(domains))(*domains) if domains is not None else None
+    ctx = NominalCtx(*(fp(v) for v in keep), cost, dt, trim, substeps, domain or Domain.default(), dd)
+    ctx._keep = (keep, dd)
+    return ctx
+
+
+def _plan_common(fn_user, B, S, T, A):
+    if isinstance(fn_user, tuple):
+        fn, user = fn_user
+        return C.cast(fn, VP), C.cast(C.pointer(user), VP), None
+
+    def cb(_user, cand, b, s, t, a, scores):
+        c = np.ctypeslib.as_array(cand, shape=(b, s, t, a))
+        out = np.ctypeslib.as_array(scores, shape=(b, s))
+        out[...] = fn_user(c.copy())
+    cfn = SCORE_FN(cb)
+    return C.cast(cfn, VP), None, cfn
+
+
+def mppi_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
+    """scorer: python fn(cand)->scores, or (NOMINAL_FN, NominalCtx) / (SKYJEPA_FN, SkyCtx)."""
+    c = cfg._c()
+    S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
+    fnp, user, keep = _plan_common(scorer, B, S, T, A)
+    seq = np.empty((B, T, A), np.float32)
+    scores = np.empty((B, S), np.float32)
+    best = np.empty(B, np.uint32)
+    warm = np.empty((B, T, A), np.float32)
+    cand = np.empty((B, S, T, A), np.float32)
+    lib.orc_mppi_plan(C.byref(c), fp(f32(warm_start)) if warm_start is not None else None, B,
+                      fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq), fp(scores),
+                      up(best), fp(warm), fp(cand))
+    return dict(sequence=seq, scores=scores, best=best, warm=warm, candidates=cand)
+
+
+def cem_plan(cfg, B, scorer, noise=None, seed=0, offset=0):
+    c = cfg._c()
+    S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
+    fnp, user, keep = _plan_common(scorer, B, S, T, A)
+    seq = np.empty((B, T, A), np.float32)
+    scores = np.empty((B, S), np.float32)
+    best = np.empty(B, np.uint32)
+    cand = np.empty((B, S, T, A), np.float32)
+    lib.orc_cem_plan(C.byref(c), B, fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq),
+                     fp(scores), up(best), fp(cand))
+    return dict(sequence=seq, scores=scores, best=best, candidates=cand)
+
+
+def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
+    c = cfg._c()
+    S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
+    fnp, user, keep = _plan_common(scorer, B, S, T, A)
+    seq = np.empty((B, T, A), np.float32)
+    scores = np.empty((B, S), np.float32)
+    best = np.empty(B, np.uint32)
+    warm = np.empty((B, T, A), np.float32)
+    cand = np.empty((B, S, T, A), np.float32)
+    lib.orc_icem_plan(C.byref(c), fp(f32(warm_start)) if warm_start is not None else None, B,
+                      fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq), fp(scores),
+                      up(best), fp(warm), fp(cand))
+    return dict(sequence=seq, scores=scores, best=best, warm=warm, candidates=cand)
+
+
+def reference_state(kind: int, time: float, radius: float, period: float):
+    out = np.empty(18, np.float32)
+    lib.orc_reference_state(kind, F(time), F(radius), F(period), fp(out))
+    return out
+
+
+def geometric_prior(current, refs, dt, domain=None):
+    refs = f32(refs)
+    out = np.empty((refs.shape[0], 4), np.float32)
+    lib.orc_geometric_prior(fp(f32(current)), fp(refs), refs.shape[0], F(dt), C.byref(domain or Domain.default()),
+                            fp(out))
+    return out
