@@ -357,7 +357,11 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     const uint32_t keep = p->kind == PlannerKind::Icem ? std::max<uint32_t>(p->icem.keep_elites, 1) : 1;
     LWM_TRY(p->carried.ensure(static_cast<size_t>(B) * keep * p->T * p->A * 4));
     LWM_TRY(p->bounds.ensure(2 * LWM_MAX_ACTION_DIM * 4));
-    LWM_TRY(p->staging.ensure(seq * 4 * 3 + static_cast<size_t>(B) * p->S * 4 + static_cast<size_t>(B) * 8 + 64));
+    // staging carries the bounds (2 x 16 floats), the initial std, deadline
+    // sequences and the result burst of lwm_plan
+    const size_t staging = std::max<size_t>(seq * 4 * 3 + static_cast<size_t>(B) * p->S * 4 + static_cast<size_t>(B) * 8 + 1024,
+                                            2 * LWM_MAX_ACTION_DIM * 4);
+    LWM_TRY(p->staging.ensure(staging));
     LWM_CUDA(cudaMemsetAsync(p->zeros.ptr, 0, seq * 4, p->ctx->stream));
     LWM_CUDA(cudaMemsetAsync(p->counters.ptr, 0, static_cast<size_t>(B) * 4, p->ctx->stream));
     // bounds [low(16), high(16)] and the per-plan initial std, both constant per planner
@@ -528,6 +532,7 @@ lwm_status deadline_result(lwm_planner* p, uint32_t B, bool use_warm, const char
 
 lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
     const auto start = std::chrono::steady_clock::now();
+    (void)cudaGetLastError();  // drop a stale non-sticky error of an earlier failed call
     LWM_TRY(validate_planner(p));
     const uint32_t B = sc->batch;
     if (B == 0) return fail(LWM_INVALID_ARGUMENT, "scorer batch is zero (set its context first)");
