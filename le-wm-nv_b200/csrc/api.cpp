@@ -127,7 +127,6 @@ struct lwm_scorer {
     lwm_skyjepa_config sky{};
     lwm::SkyjepaArgs sky_args{};  // weight views + constants, context pointers set per plan
     DevBuf weights;
-    DevBuf h0;
     lwm_tracking_cost cost{};
     float dt = 0.05f;
     // context (device) and its pinned staging
@@ -330,7 +329,7 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     const size_t seq = static_cast<size_t>(B) * p->T * p->A;
     const size_t n = seq * p->S;
     uint32_t P = std::max<uint32_t>(lwm::nominal_blocks_per_vehicle(p->S),
-                                    lwm::skyjepa_partials_per_vehicle(p->S, 256));
+                                    lwm::skyjepa_partials_per_vehicle(p->S, 32));
     P = std::max<uint32_t>(P, (p->S + 255) / 256);
     const size_t pw = (4 + static_cast<size_t>(p->T) * p->A + 3) & ~static_cast<size_t>(3);
     LWM_TRY(p->zeros.ensure(seq * 4));
@@ -430,8 +429,7 @@ lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
     a.action_hist = reinterpret_cast<const float*>(base + sc->off_action_hist);
     a.ref_states = reinterpret_cast<const float*>(base + sc->off_ref_states);
     a.ref_actions = reinterpret_cast<const float*>(base + sc->off_ref_actions);
-    a.h0 = sc->h0.as<float>();
-    a.use_pdl = 1;
+    a.rows = lwm::skyjepa_rows_per_cluster(a);
     return a;
 }
 
@@ -619,7 +617,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 a.scores = p->scores.as<float>();
                 a.mppi = 1;
                 a.m = m;
-                a.m.P = lwm::skyjepa_partials_per_vehicle(p->S, a.H);
+                a.m.P = lwm::skyjepa_partials_per_vehicle(p->S, a.rows);
                 int launched = 0;
                 LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
                 p->ctx->launches += static_cast<uint64_t>(launched);
@@ -1109,7 +1107,6 @@ lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* s, uint32_t B, uint32_t T,
     s->off_ref_states = off; off = align256(off + static_cast<size_t>(B) * T * 18 * 4);
     s->off_ref_actions = off; off = align256(off + static_cast<size_t>(B) * T * 4 * 4);
     LWM_TRY(stage_context(s, off));
-    LWM_TRY(s->h0.ensure(static_cast<size_t>(B) * s->sky.latent_dim * 4));
     char* h = s->ctx_host.as<char>();
     std::memcpy(h + s->off_state_hist, state_hist, static_cast<size_t>(B) * Hs * 18 * 4);
     std::memcpy(h + s->off_action_hist, action_hist, static_cast<size_t>(B) * (Hs - 1) * 4 * 4);
@@ -1159,7 +1156,6 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     cudaStreamSynchronize(s->ctx->stream);
     if (s->staged) cudaEventDestroy(s->staged);
     s->weights.release();
-    s->h0.release();
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;

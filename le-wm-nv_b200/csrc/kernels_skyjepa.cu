@@ -7,20 +7,27 @@
 //   prober MLP -> residual accel + angular map; explicit-Euler SO(3)
 //   integrator; tracking cost averaged over the horizon.
 //
-// B200 mapping.  Two kernels per plan:
-//  * skyjepa_context_kernel — one 8-CTA cluster per vehicle computes the
-//    state-history TCN and projection (h0).  It triggers programmatic launch
-//    completion at entry so the rollout kernel's prologue overlaps it.
-//  * skyjepa_rollout_kernel — one 8-CTA cluster per 32 candidates.  CTA c of
-//    the cluster owns hidden units [c*H/8, (c+1)*H/8): its slice of W_hh (all
-//    three gates, all k) lives in REGISTERS for the whole kernel (96 floats a
-//    thread at H = 256), so the recurrent GEMM reads only h from shared
-//    memory.  Every step each CTA computes its units' new hidden values for
-//    all 32 rows and writes them into every CTA's next-h buffer through
-//    distributed shared memory, then the cluster barrier publishes them.
-//    Each CTA also owns 4 of the 32 rows for sampling, the action TCN, the
-//    prober, the integrator and the cost; the MPPI tuple of its rows feeds
-//    the one-pass reduction (lwm_mppi.cuh).
+// B200 mapping: one kernel per plan iteration, one 8-CTA thread-block
+// cluster per M candidate rows (M = 8 x groups, chosen so that the whole grid
+// is resident in one wave).  Each CTA runs 8 "GEMM" warps and 1 "prober" warp.
+//  * Prologue (all warps): sampling of the CTA's M/8 own rows; the action TCN
+//    of their rolling windows (one warp-local group of lanes per window), the
+//    window embeddings broadcast to every CTA through distributed shared
+//    memory (DSMEM); the state-history TCN + projection (h0), each CTA
+//    computing 1/8 of the output channels of every convolution, k-sliced over
+//    its threads and reduced in shared memory, broadcast through DSMEM.
+//  * GRU loop (GEMM warps): CTA c owns hidden units [c*H/8, (c+1)*H/8); its
+//    slice of W_hh (all three gates, all k) lives in REGISTERS for the whole
+//    loop (96 floats a thread at H = 256), so the recurrent GEMM reads only h
+//    from shared memory.  Each step the CTA computes its units' new hidden
+//    values for all M rows and stores them into every CTA's next-h buffer
+//    through DSMEM; a split cluster barrier (arrive.release / wait.acquire)
+//    publishes them.
+//  * Prober warp: while the GEMM warps compute step t+1, it runs the prober
+//    MLP, the SO(3) integrator and the tracking cost of step t for the CTA's
+//    own rows, so that work is off the critical path.
+//  * Epilogue: the MPPI tuple of the own rows feeds the one-pass reduction
+//    (lwm_mppi.cuh).
 // No intermediate tensor ([B,S,T,latent], [B,S,T,18]) touches HBM.
 //
 // Numerics are f32 throughout.  Dot products use fused multiply-add
@@ -40,134 +47,448 @@ namespace cg = cooperative_groups;
 namespace lwm {
 
 constexpr int kCluster = 8;
-constexpr int kRows = 32;          // candidate rows per cluster
-constexpr int kThreads = 256;
-constexpr int kRowsPerCta = kRows / kCluster;
+constexpr int kGemmWarps = 8;
+constexpr int kGemmThreads = kGemmWarps * 32;
+constexpr int kThreads = kGemmThreads + 32;  // + the prober warp
+constexpr int kProberWarp = kGemmWarps;
 constexpr int kMaxTcnCh = 8;       // action-encoder channel bound
 constexpr int kMaxHist = 16;
+constexpr int kMaxRowsPerCta = 8;  // M <= 64 rows per cluster
+constexpr int kMaxHid = 64;
 
 template <int H>
 struct Geom {
-    static constexpr int U = H / kCluster;      // hidden units per CTA
-    static constexpr int PAIRS = U / 2;         // unit pairs per CTA
-    static constexpr int KG = kThreads / PAIRS; // k-groups (lanes per pair)
-    static constexpr int KPT = H / KG;          // k values per thread
-    static constexpr int KQ = KPT / 4;          // float4 loads per row
-    static constexpr int R = KG / 2;            // rows per GEMM group
-    static constexpr int GROUPS = kRows / R;
-    static constexpr int PPW = 32 / KG;         // pairs per warp
-    static constexpr int VEC = 2 * PPW;         // hidden units per warp
-    static constexpr int LPR = 32 / R;          // lanes per row in the store
-    static constexpr int DPL = kCluster / LPR;  // destination CTAs per lane
+    static constexpr int U = H / kCluster;          // hidden units per CTA
+    static constexpr int PAIRS = U / 2;             // unit pairs per CTA
+    static constexpr int KG = kGemmThreads / PAIRS; // k-groups (lanes per pair)
+    static constexpr int KPT = H / KG;              // k values per thread
+    static constexpr int KQ = KPT / 4;              // float4 loads per row
+    static constexpr int R = 4;                     // rows per GEMM group
+    static constexpr int COMBOS = 2 * R;            // (unit-in-pair, row) combos
+    static constexpr int PPW = 32 / KG;             // pairs per warp
+    static constexpr int VEC = 2 * PPW;             // hidden units per warp
     static_assert(KPT % 4 == 0, "k interleave needs float4 granularity");
-    static_assert(KG <= 32 && KG >= 2, "k-groups must fit a warp");
-    static_assert(kRows % R == 0, "row groups");
+    static_assert(KG <= 32 && KG >= COMBOS, "k-groups must fit a warp and cover the combos");
+    static_assert(32 / R == kCluster, "one destination CTA per lane in the store");
 };
+
+__host__ __device__ inline uint32_t pow2_at_least(uint32_t v) {
+    uint32_t p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
 
 struct SkySmem {
     // Offsets in floats inside the dynamic shared-memory block.
-    uint32_t h0, h1, emb, cand, tcn, w1, wih, a1, a2, out, x, score, w, total;
+    uint32_t hA, hB, emb, cand, w1, wih, pw2, pw3, pb, a1, a2, pout, x, score, w, h0v, total;
+    uint32_t w1_stride, pw_stride;
 };
 
-__host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t T, uint32_t E, uint32_t A, uint32_t hid,
-                                                   uint32_t tcn_ch, uint32_t Hs) {
+// rows = M rows per cluster; Cs = widest state-TCN layer; Ca = action-TCN
+// lanes per window (power of two).
+__host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, uint32_t T, uint32_t E, uint32_t A,
+                                                   uint32_t hid, uint32_t layers, uint32_t Cs, uint32_t Ca,
+                                                   uint32_t Hs) {
     SkySmem s;
     uint32_t off = 0;
     auto take = [&](uint32_t n) { uint32_t o = off; off += (n + 3u) & ~3u; return o; };
-    s.h0 = take(kRows * H);
-    s.h1 = take(kRows * H);
-    s.emb = take(kRows * T * E);
-    s.cand = take(kRowsPerCta * T * A);
-    const uint32_t windows = kRowsPerCta * T;
-    s.tcn = take(windows * 3 * tcn_ch * Hs);
-    s.w1 = take(hid * H);
+    const uint32_t rpc = rows / kCluster;
+    // hA doubles as the state-TCN scratch, hB as the action-TCN scratch
+    const uint32_t per = (Cs + kCluster - 1) / kCluster;
+    const uint32_t ks = kThreads / per;
+    const uint32_t state_scratch = 3 * Cs * Hs + ks * per * Hs + 8;
+    const uint32_t action_scratch = (kThreads / Ca) * 3 * Ca * Hs;
+    s.hA = take(rows * H > state_scratch ? rows * H : state_scratch);
+    s.hB = take(rows * H > action_scratch ? rows * H : action_scratch);
+    s.emb = take(rows * T * E);
+    s.cand = take(rpc * T * A);
+    s.w1_stride = H + 4;
+    s.w1 = take(hid * s.w1_stride);
     s.wih = take(3 * (H / kCluster) * E);
-    s.a1 = take(kRowsPerCta * hid);
-    s.a2 = take(kRowsPerCta * hid);
-    s.out = take(kRowsPerCta * 16);
-    s.x = take(kRowsPerCta * 20);
-    s.score = take(kRowsPerCta);
-    s.w = take(kRowsPerCta);
+    s.pw_stride = hid + 1;
+    s.pw2 = take((layers > 1 ? layers - 1 : 1) * hid * s.pw_stride);
+    s.pw3 = take(15 * s.pw_stride);
+    s.pb = take(hid * layers + 16);
+    s.a1 = take(rpc * hid);
+    s.a2 = take(rpc * hid);
+    s.pout = take(rpc * 16);
+    s.x = take(rpc * 20);
+    s.score = take(rpc);
+    s.w = take(rpc);
+    s.h0v = take(H);
     s.total = off;
     return s;
 }
 
-// ------------------------------------------------------------ context kernel
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// --------------------------------------------------------------- prologue
 //
 // SkyJepaModel::encode_state_history (model.rs:57-61): normalised state
-// history -> TemporalConvEncoder::forward_last (tcn.rs:155-160) ->
-// state_projection.  Cluster of 8 CTAs per vehicle; CTA c computes output
-// channels [c*C/8, (c+1)*C/8) of every convolution and broadcasts them.
-__device__ __forceinline__ float conv_at(const float* x, uint32_t in, uint32_t Hs, const float* w,
-                                         uint32_t o, uint32_t K, uint32_t dil, uint32_t t) {
-    float acc = 0.0f;
-    for (uint32_t i = 0; i < in; ++i) {
-        const float* wr = w + (static_cast<size_t>(o) * in + i) * K;
-        const float* xr = x + i * Hs;
-        for (uint32_t j = 0; j < K; ++j) {
-            const int src = static_cast<int>(t) - static_cast<int>((K - 1 - j) * dil);
-            if (src >= 0) acc = fmaf(__ldg(wr + j), xr[src], acc);
-        }
-    }
-    return acc;
-}
-
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
-skyjepa_context_kernel(SkyjepaArgs a) {
-#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 900)
-    cudaTriggerProgrammaticLaunchCompletion();
-#endif
-    extern __shared__ float smem[];
-    cg::cluster_group cluster = cg::this_cluster();
-    const uint32_t c = cluster.block_rank();
-    const uint32_t b = blockIdx.y;
+// history -> TemporalConvEncoder::forward_last (tcn.rs:138-160) ->
+// state_projection.  CTA c computes output channels [c*per, (c+1)*per) of
+// every convolution: thread (o, slice) sums its slice of input channels for
+// all time steps, the slices are reduced in shared memory, and the result is
+// broadcast to every CTA's activation buffer.
+__device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
+                                  float* scratch, float* h0v) {
     const TcnView& tcn = a.state_tcn;
-    const uint32_t Hs = a.Hs, C = tcn.max_ch;
-    float* xa = smem;
-    float* xb = smem + C * Hs;
-    float* h1 = smem + 2 * C * Hs;
-    // normalised state history, [channel][time]
-    for (uint32_t q = threadIdx.x; q < tcn.input_dim * Hs; q += blockDim.x) {
+    const uint32_t Hs = a.Hs, C = tcn.max_ch, tid = threadIdx.x;
+    const uint32_t per = (C + kCluster - 1) / kCluster;
+    const uint32_t KS = kThreads / per;
+    float* xa = scratch;
+    float* xb = scratch + C * Hs;
+    float* hb = scratch + 2 * C * Hs;
+    float* red = scratch + 3 * C * Hs;  // [KS][per][Hs], local
+    for (uint32_t q = tid; q < tcn.input_dim * Hs; q += kThreads) {
         const uint32_t i = q / Hs, t = q % Hs;
         const float v = a.state_hist[(static_cast<size_t>(b) * Hs + t) * 18 + i];
         xa[q] = (v - a.state_mean[i]) / a.state_std[i];
     }
-    cluster.sync();
+    __syncthreads();
     float* cur = xa;
     float* nxt = xb;
+    const uint32_t o_local = tid % per, slice = tid / per;
     for (uint32_t l = 0; l < tcn.levels; ++l) {
         const TcnBlockView& bk = tcn.blocks[l];
-        const uint32_t per = (bk.out + kCluster - 1) / kCluster;
-        const uint32_t o0 = c * per, o1 = min(bk.out, o0 + per);
-        const uint32_t n_out = (o1 > o0 ? o1 - o0 : 0) * Hs;
-        for (uint32_t q = threadIdx.x; q < n_out; q += blockDim.x) {
-            const uint32_t o = o0 + q / Hs, t = q % Hs;
-            const float v = gelu_tanh(conv_at(cur, bk.in, Hs, bk.w1, o, tcn.k, bk.dil, t) + __ldg(bk.b1 + o));
-            for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(h1, d)[o * Hs + t] = v;
+        const uint32_t o0 = c * per;
+        const uint32_t o = o0 + o_local;
+        for (int conv = 0; conv < 2; ++conv) {
+            const float* src = conv == 0 ? cur : hb;
+            const uint32_t cin = conv == 0 ? bk.in : bk.out;
+            const float* W = conv == 0 ? bk.w1 : bk.w2;
+            if (slice < KS && o < bk.out) {
+                float acc[kMaxHist];
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
+                for (uint32_t i = slice; i < cin; i += KS) {
+                    const float* xr = src + i * Hs;
+                    for (uint32_t j = 0; j < tcn.k; ++j) {
+                        const float wv = __ldg(W + (static_cast<size_t>(o) * cin + i) * tcn.k + j);
+                        const int sh = static_cast<int>((tcn.k - 1 - j) * bk.dil);
+#pragma unroll
+                        for (int t = 0; t < kMaxHist; ++t)
+                            if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, xr[t - sh], acc[t]);
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t)
+                    if (t < static_cast<int>(Hs)) red[(slice * per + o_local) * Hs + t] = acc[t];
+            }
+            __syncthreads();
+            for (uint32_t q = tid; q < per * Hs; q += kThreads) {
+                const uint32_t ol = q / Hs, t = q % Hs, oo = o0 + ol;
+                if (oo >= bk.out) continue;
+                float s = 0.0f;
+                for (uint32_t k = 0; k < KS; ++k) s += red[(k * per + ol) * Hs + t];
+                float v;
+                if (conv == 0) {
+                    v = gelu_tanh(s + __ldg(bk.b1 + oo));
+                } else {
+                    const float h2 = gelu_tanh(s + __ldg(bk.b2 + oo));
+                    float res;
+                    if (bk.wr) {
+                        float r = 0.0f;
+                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(__ldg(bk.wr + static_cast<size_t>(oo) * bk.in + i), cur[i * Hs + t], r);
+                        res = r + __ldg(bk.br + oo);
+                    } else {
+                        res = cur[oo * Hs + t];
+                    }
+                    v = gelu_tanh(h2 + res);
+                }
+                float* dst = conv == 0 ? hb : nxt;
+                for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(dst, d)[oo * Hs + t] = v;
+            }
+            cluster.sync();
         }
-        cluster.sync();
-        for (uint32_t q = threadIdx.x; q < n_out; q += blockDim.x) {
-            const uint32_t o = o0 + q / Hs, t = q % Hs;
-            const float h2 = gelu_tanh(conv_at(h1, bk.out, Hs, bk.w2, o, tcn.k, bk.dil, t) + __ldg(bk.b2 + o));
-            float res;
-            if (bk.wr) res = conv_at(cur, bk.in, Hs, bk.wr, o, 1, 1, t) + __ldg(bk.br + o);
-            else res = cur[o * Hs + t];
-            const float v = gelu_tanh(h2 + res);
-            for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(nxt, d)[o * Hs + t] = v;
-        }
-        cluster.sync();
         float* tmp = cur; cur = nxt; nxt = tmp;
     }
-    // state_projection on the last time step: CTA c writes H/8 outputs.
-    const uint32_t per = (a.H + kCluster - 1) / kCluster;
-    const uint32_t Cl = tcn.out_dim;
-    for (uint32_t q = threadIdx.x; q < per; q += blockDim.x) {
-        const uint32_t o = c * per + q;
-        if (o >= a.H) break;
-        float acc = 0.0f;
-        for (uint32_t i = 0; i < Cl; ++i) acc = fmaf(cur[i * Hs + Hs - 1], __ldg(a.proj_w + static_cast<size_t>(o) * Cl + i), acc);
-        a.h0[static_cast<size_t>(b) * a.H + o] = acc + __ldg(a.proj_b + o);
+    // state_projection of the last time step: CTA c writes H/8 outputs to every CTA
+    const uint32_t hper = a.H / kCluster, Cl = tcn.out_dim;
+    for (uint32_t q = tid; q < hper; q += kThreads) {
+        const uint32_t oo = c * hper + q;
+        const float* wrow = a.proj_w + static_cast<size_t>(oo) * Cl;
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        uint32_t i = 0;
+        for (; i + 4 <= Cl; i += 4) {
+            s0 = fmaf(cur[(i + 0) * Hs + Hs - 1], __ldg(wrow + i + 0), s0);
+            s1 = fmaf(cur[(i + 1) * Hs + Hs - 1], __ldg(wrow + i + 1), s1);
+            s2 = fmaf(cur[(i + 2) * Hs + Hs - 1], __ldg(wrow + i + 2), s2);
+            s3 = fmaf(cur[(i + 3) * Hs + Hs - 1], __ldg(wrow + i + 3), s3);
+        }
+        for (; i < Cl; ++i) s0 = fmaf(cur[i * Hs + Hs - 1], __ldg(wrow + i), s0);
+        const float v = ((s0 + s1) + (s2 + s3)) + __ldg(a.proj_b + oo);
+        for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(h0v, d)[oo] = v;
     }
+}
+
+// SkyJepaModel::rollout_candidates window encoding (model.rs:192-215) with
+// TemporalBlock::forward (tcn.rs:88-96): window (row rr, step t0) is
+// [history(Hs-1) ++ candidates][t0 .. t0+Hs), each window zero-padded on its
+// own.  `ca` lanes of one warp own a window, one output channel each, all
+// time steps in registers; warp-level syncs between convolutions.
+__device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
+                                   uint32_t rpc, const float* s_cand, float* scratch, float* s_emb) {
+    const TcnView& tcn = a.action_tcn;
+    const uint32_t Hs = a.Hs, T = a.T, A = a.A, E = a.E, TA = T * A;
+    const uint32_t ca = pow2_at_least(tcn.max_ch);
+    const uint32_t wpp = kThreads / ca;
+    const uint32_t slot = threadIdx.x / ca, o = threadIdx.x % ca;
+    const uint32_t windows = rpc * T;
+    const uint32_t Cm = ca;
+    float* cur = scratch + slot * 3 * Cm * Hs;
+    float* hb = cur + Cm * Hs;
+    for (uint32_t w0 = 0; w0 < windows; w0 += wpp) {
+        const uint32_t win = w0 + slot;
+        const bool active = win < windows;
+        const uint32_t rr = active ? win / T : 0, t0 = active ? win % T : 0;
+        if (active && o < tcn.input_dim) {
+            for (uint32_t w = 0; w < Hs; ++w) {
+                const uint32_t pos = t0 + w;
+                const float v = pos < Hs - 1 ? a.action_hist[(static_cast<size_t>(b) * (Hs - 1) + pos) * A + o]
+                                             : s_cand[rr * TA + (pos - (Hs - 1)) * A + o];
+                cur[o * Hs + w] = (v - a.action_mean[o]) / a.action_std[o];
+            }
+        }
+        __syncwarp();
+        for (uint32_t l = 0; l < tcn.levels; ++l) {
+            const TcnBlockView& bk = tcn.blocks[l];
+            const bool mine = active && o < bk.out;
+            float h2[kMaxHist];
+            for (int conv = 0; conv < 2; ++conv) {
+                const float* src = conv == 0 ? cur : hb;
+                const uint32_t cin = conv == 0 ? bk.in : bk.out;
+                const float* W = conv == 0 ? bk.w1 : bk.w2;
+                float acc[kMaxHist];
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
+                if (mine) {
+                    for (uint32_t i = 0; i < cin; ++i)
+                        for (uint32_t j = 0; j < tcn.k; ++j) {
+                            const float wv = __ldg(W + (static_cast<size_t>(o) * cin + i) * tcn.k + j);
+                            const int sh = static_cast<int>((tcn.k - 1 - j) * bk.dil);
+#pragma unroll
+                            for (int t = 0; t < kMaxHist; ++t)
+                                if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, src[i * Hs + t - sh], acc[t]);
+                        }
+                }
+                const float bias = mine ? __ldg((conv == 0 ? bk.b1 : bk.b2) + o) : 0.0f;
+                if (conv == 0) {
+                    if (mine)
+#pragma unroll
+                        for (int t = 0; t < kMaxHist; ++t)
+                            if (t < static_cast<int>(Hs)) hb[o * Hs + t] = gelu_tanh(acc[t] + bias);
+                } else {
+#pragma unroll
+                    for (int t = 0; t < kMaxHist; ++t) h2[t] = gelu_tanh(acc[t] + bias);
+                }
+                __syncwarp();
+            }
+            float res[kMaxHist];
+#pragma unroll
+            for (int t = 0; t < kMaxHist; ++t) res[t] = 0.0f;
+            if (mine) {
+                if (bk.wr) {
+                    const float br = __ldg(bk.br + o);
+#pragma unroll
+                    for (int t = 0; t < kMaxHist; ++t) {
+                        if (t >= static_cast<int>(Hs)) break;
+                        float r = 0.0f;
+                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(__ldg(bk.wr + static_cast<size_t>(o) * bk.in + i), cur[i * Hs + t], r);
+                        res[t] = r + br;
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < kMaxHist; ++t)
+                        if (t < static_cast<int>(Hs)) res[t] = cur[o * Hs + t];
+                }
+            }
+            __syncwarp();
+            if (mine)
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t)
+                    if (t < static_cast<int>(Hs)) cur[o * Hs + t] = gelu_tanh(h2[t] + res[t]);
+            __syncwarp();
+        }
+        if (active && o < E) {
+            const float v = cur[o * Hs + Hs - 1];
+            const uint32_t m = c * rpc + rr;
+            for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(s_emb, d)[(m * T + t0) * E + o] = v;
+        }
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------- the prober warp
+//
+// SkyJepaProber::forward (prober.rs:84-102) for the CTA's own rows, then one
+// step of lewm_skyjepa_integrate_f32 (kinematics.rs:377-484) and the tracking
+// cost (control.rs:430-452) of that step.
+__device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem, const float* hn, uint32_t c,
+                            uint32_t b, uint32_t rpc, uint32_t own0, uint32_t t, uint32_t H) {
+    const uint32_t lane = threadIdx.x & 31, hid = a.hid, T = a.T, A = a.A, TA = T * A;
+    float* s_a1 = smem + L.a1;
+    float* s_a2 = smem + L.a2;
+    float* s_pout = smem + L.pout;
+    const float* w1 = smem + L.w1;
+    const float* pb = smem + L.pb;
+    // layer 1: lane owns outputs lane and lane + 32
+    {
+        float acc[2][kMaxRowsPerCta];
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int r = 0; r < kMaxRowsPerCta; ++r) acc[q][r] = 0.0f;
+        const bool two = hid > 32;
+        const float* wr0 = w1 + lane * L.w1_stride;
+        const float* wr1 = w1 + (lane + 32) * L.w1_stride;
+        const bool has0 = lane < hid;
+        for (uint32_t k = 0; k < H; k += 4) {
+            const float4 w0 = has0 ? *reinterpret_cast<const float4*>(wr0 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 w1v = two && lane + 32 < hid ? *reinterpret_cast<const float4*>(wr1 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < kMaxRowsPerCta; ++r) {
+                if (static_cast<uint32_t>(r) >= rpc) break;
+                const float4 hv = *reinterpret_cast<const float4*>(hn + (c * rpc + r) * H + k);
+                float s = acc[0][r];
+                s = fmaf(w0.x, hv.x, s); s = fmaf(w0.y, hv.y, s); s = fmaf(w0.z, hv.z, s); s = fmaf(w0.w, hv.w, s);
+                acc[0][r] = s;
+                if (two) {
+                    float u = acc[1][r];
+                    u = fmaf(w1v.x, hv.x, u); u = fmaf(w1v.y, hv.y, u); u = fmaf(w1v.z, hv.z, u); u = fmaf(w1v.w, hv.w, u);
+                    acc[1][r] = u;
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxRowsPerCta; ++r) {
+            if (static_cast<uint32_t>(r) >= rpc) break;
+            if (has0) s_a1[r * hid + lane] = gelu_tanh(acc[0][r] + pb[lane]);
+            if (two && lane + 32 < hid) s_a1[r * hid + lane + 32] = gelu_tanh(acc[1][r] + pb[lane + 32]);
+        }
+    }
+    __syncwarp();
+    // hidden layers
+    float* pin = s_a1;
+    float* pout = s_a2;
+    for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
+        const float* W = smem + L.pw2 + l * hid * L.pw_stride;
+        const float* bias = pb + (l + 1) * hid;
+        for (uint32_t o = lane; o < hid; o += 32) {
+            float acc[kMaxRowsPerCta];
+#pragma unroll
+            for (int r = 0; r < kMaxRowsPerCta; ++r) acc[r] = 0.0f;
+            for (uint32_t i = 0; i < hid; ++i) {
+                const float wv = W[o * L.pw_stride + i];
+#pragma unroll
+                for (int r = 0; r < kMaxRowsPerCta; ++r)
+                    if (static_cast<uint32_t>(r) < rpc) acc[r] = fmaf(pin[r * hid + i], wv, acc[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxRowsPerCta; ++r)
+                if (static_cast<uint32_t>(r) < rpc) pout[r * hid + o] = gelu_tanh(acc[r] + bias[o]);
+        }
+        __syncwarp();
+        float* tmp = pin; pin = pout; pout = tmp;
+    }
+    // output layer: 15 values per row
+    if (lane < 15) {
+        const float* W = smem + L.pw3 + lane * L.pw_stride;
+        const float bias = pb[a.prober_layers * hid + lane];
+        float acc[kMaxRowsPerCta];
+#pragma unroll
+        for (int r = 0; r < kMaxRowsPerCta; ++r) acc[r] = 0.0f;
+        for (uint32_t i = 0; i < hid; ++i) {
+            const float wv = W[i];
+#pragma unroll
+            for (int r = 0; r < kMaxRowsPerCta; ++r)
+                if (static_cast<uint32_t>(r) < rpc) acc[r] = fmaf(pin[r * hid + i], wv, acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxRowsPerCta; ++r)
+            if (static_cast<uint32_t>(r) < rpc) s_pout[r * 16 + lane] = acc[r] + bias;
+    }
+    __syncwarp();
+    // integrator + cost: lane r owns row r
+    if (lane < rpc) {
+        float* xs = smem + L.x + lane * 20;
+        float x[18];
+#pragma unroll
+        for (int i = 0; i < 18; ++i) x[i] = xs[i];
+        const float* act = smem + L.cand + lane * TA + t * A;
+        const float* po = s_pout + lane * 16;
+        const float sdt = a.dt;
+        float ta;
+        if (a.rotor_forces) {
+            ta = (act[0] + act[1] + act[2] + act[3]) / a.mass;
+        } else {
+            const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
+            ta = th * a.gravity / a.hover_throttle;
+        }
+        const float acc[3] = {x[8] * ta + po[0], x[11] * ta + po[1], x[14] * ta - a.gravity + po[2]};
+        float ang[3];
+#pragma unroll
+        for (int row = 0; row < 3; ++row)
+            ang[row] = po[3 + row * 4] * act[0] + po[4 + row * 4] * act[1] + po[5 + row * 4] * act[2] +
+                       po[6 + row * 4] * act[3];
+#pragma unroll
+        for (int ax = 0; ax < 3; ++ax) { x[ax] += x[3 + ax] * sdt; x[3 + ax] += acc[ax] * sdt; }
+        const float wx = x[15] * sdt, wy = x[16] * sdt, wz = x[17] * sdt;
+        const float th2 = wx * wx + wy * wy + wz * wz;
+        float ca, cb;
+        if (th2 < 1.0e-6f) {
+            const float th4 = th2 * th2;
+            ca = 1.0f - th2 / 6.0f + th4 / 120.0f;
+            cb = 0.5f - th2 / 24.0f + th4 / 720.0f;
+        } else {
+            const float th = sqrtf(th2);
+            float sn, cs;
+            sincosf(th, &sn, &cs);
+            ca = sn / th;
+            cb = (1.0f - cs) / th2;
+        }
+        const float dl[9] = {1.0f - cb * (wy * wy + wz * wz), cb * wx * wy - ca * wz, cb * wx * wz + ca * wy,
+                             cb * wy * wx + ca * wz, 1.0f - cb * (wx * wx + wz * wz), cb * wy * wz - ca * wx,
+                             cb * wz * wx - ca * wy, cb * wz * wy + ca * wx, 1.0f - cb * (wx * wx + wy * wy)};
+        float nr[9];
+#pragma unroll
+        for (int row = 0; row < 3; ++row)
+#pragma unroll
+            for (int col = 0; col < 3; ++col)
+                nr[row * 3 + col] = x[6 + row * 3] * dl[col] + x[7 + row * 3] * dl[3 + col] + x[8 + row * 3] * dl[6 + col];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
+#pragma unroll
+        for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
+        const uint32_t s = own0 + lane;
+        if (a.states && s < a.S) {
+            float* o = a.states + ((static_cast<size_t>(b) * a.S + s) * T + t) * 18;
+#pragma unroll
+            for (int i = 0; i < 18; ++i) o[i] = x[i];
+        }
+        const float* ref = a.ref_states + (static_cast<size_t>(b) * T + t) * 18;
+        float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) { const float dd = x[i] - ref[i]; g0 += dd * dd; }
+#pragma unroll
+        for (int i = 3; i < 6; ++i) { const float dd = x[i] - ref[i]; g1 += dd * dd; }
+#pragma unroll
+        for (int i = 6; i < 15; ++i) { const float dd = x[i] - ref[i]; g2 += dd * dd; }
+#pragma unroll
+        for (int i = 15; i < 18; ++i) { const float dd = x[i] - ref[i]; g3 += dd * dd; }
+        const float* ra = a.ref_actions + (static_cast<size_t>(b) * T + t) * 4;
+        float ac = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { const float dd = act[i] - ra[i]; ac += (dd * dd) * a.cost.action[i]; }
+        float st = g0 * a.cost.position + g1 * a.cost.velocity;
+        st = st + g2 * a.cost.attitude;
+        st = st + g3 * a.cost.angular_velocity;
+#pragma unroll
+        for (int i = 0; i < 18; ++i) xs[i] = x[i];
+        xs[18] += st + ac;
+    }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------ rollout kernel
@@ -182,60 +503,40 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     const uint32_t rb = blockIdx.x / kCluster;  // row block of this cluster
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t T = a.T, A = a.A, E = a.E, Hs = a.Hs, hid = a.hid;
-    const SkySmem L = sky_smem_layout(H, T, E, A, hid, a.action_tcn.max_ch, Hs);
-    float* s_emb = smem + L.emb;     // [kRows][T][E]
-    float* s_cand = smem + L.cand;   // [kRowsPerCta][T][A]
-    float* s_tcn = smem + L.tcn;
-    float* s_w1 = smem + L.w1;       // [hid][H]
+    const uint32_t rows = a.rows, rpc = rows / kCluster, groups = rows / G::R;
+    const uint32_t ca = pow2_at_least(a.action_tcn.max_ch);
+    const SkySmem L = sky_smem_layout(H, rows, T, E, A, hid, a.prober_layers, a.state_tcn.max_ch, ca, Hs);
+    float* s_emb = smem + L.emb;     // [rows][T][E]
+    float* s_cand = smem + L.cand;   // [rpc][T][A]
     float* s_wih = smem + L.wih;     // [3][U][E] for this CTA's units
-    float* s_a1 = smem + L.a1;
-    float* s_a2 = smem + L.a2;
-    float* s_out = smem + L.out;     // [kRowsPerCta][16]
-    float* s_x = smem + L.x;         // [kRowsPerCta][20]: state18, running cost
     float* s_score = smem + L.score;
     float* s_w = smem + L.w;
-    const uint32_t row0 = rb * kRows;              // first sample of the cluster
-    const uint32_t own0 = row0 + c * kRowsPerCta;  // first sample this CTA owns
+    float* s_h0 = smem + L.h0v;
+    const uint32_t own0 = rb * rows + c * rpc;  // first sample this CTA owns
     const uint32_t TA = T * A;
 
-    // ---- registers: this thread's W_hh slice (independent of the context)
-    const uint32_t pl = lane / G::KG, kg = lane % G::KG;
-    const uint32_t pair = warp * G::PPW + pl;
-    float wr[2][3][G::KPT];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const uint32_t j = c * G::U + pair * 2 + q;
-#pragma unroll
-        for (int g = 0; g < 3; ++g) {
-            const float* row = a.w_hh + (static_cast<size_t>(g) * H + j) * H;
-#pragma unroll
-            for (int i = 0; i < G::KQ; ++i) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(row + kg * 4 + 4 * G::KG * i));
-                wr[q][g][4 * i + 0] = v.x; wr[q][g][4 * i + 1] = v.y;
-                wr[q][g][4 * i + 2] = v.z; wr[q][g][4 * i + 3] = v.w;
-            }
-        }
+    // ---- shared copies of the small weights
+    for (uint32_t q = tid; q < hid * H / 4; q += kThreads) {
+        const uint32_t o = q / (H / 4), k4 = q % (H / 4);
+        *reinterpret_cast<float4*>(smem + L.w1 + o * L.w1_stride + 4 * k4) =
+            __ldg(reinterpret_cast<const float4*>(a.p_in_w) + q);
     }
-    // gate epilogue of this lane: combo kg = (unit-in-pair, row-in-group)
-    const uint32_t my_q = kg / G::R, my_r = kg % G::R;
-    const uint32_t my_local = pair * 2 + my_q;
-    const uint32_t my_unit = c * G::U + my_local;
-    float bih[3], bhh[3];
-#pragma unroll
-    for (int g = 0; g < 3; ++g) {
-        bih[g] = __ldg(a.b_ih + g * H + my_unit);
-        bhh[g] = __ldg(a.b_hh + g * H + my_unit);
-    }
-    // shared copies: prober layer-1 weight, W_ih rows of this CTA's units
-    for (uint32_t q = tid; q < hid * H / 4; q += kThreads)
-        reinterpret_cast<float4*>(s_w1)[q] = __ldg(reinterpret_cast<const float4*>(a.p_in_w) + q);
     for (uint32_t q = tid; q < 3 * G::U * E; q += kThreads) {
         const uint32_t g = q / (G::U * E), rem = q % (G::U * E), u = rem / E, e = rem % E;
         s_wih[q] = __ldg(a.w_ih + (static_cast<size_t>(g) * H + c * G::U + u) * E + e);
     }
+    for (uint32_t l = 0; l + 1 < a.prober_layers; ++l)
+        for (uint32_t q = tid; q < hid * hid; q += kThreads)
+            smem[L.pw2 + l * hid * L.pw_stride + (q / hid) * L.pw_stride + q % hid] = __ldg(a.p_hid_w[l] + q);
+    for (uint32_t q = tid; q < 15 * hid; q += kThreads)
+        smem[L.pw3 + (q / hid) * L.pw_stride + q % hid] = __ldg(a.p_out_w + q);
+    for (uint32_t q = tid; q < hid; q += kThreads) smem[L.pb + q] = __ldg(a.p_in_b + q);
+    for (uint32_t l = 0; l + 1 < a.prober_layers; ++l)
+        for (uint32_t q = tid; q < hid; q += kThreads) smem[L.pb + (l + 1) * hid + q] = __ldg(a.p_hid_b[l] + q);
+    for (uint32_t q = tid; q < 15; q += kThreads) smem[L.pb + a.prober_layers * hid + q] = __ldg(a.p_out_b + q);
 
     // ---- sampling of the CTA's own rows (as sample_kernel)
-    for (uint32_t q = tid; q < kRowsPerCta * TA; q += kThreads) {
+    for (uint32_t q = tid; q < rpc * TA; q += kThreads) {
         const uint32_t rr = q / TA, e = q % TA, act = e % A;
         const uint32_t s = own0 + rr;
         const uint64_t ci = (static_cast<uint64_t>(b) * a.S + s) * TA + e;
@@ -255,317 +556,155 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
         }
         s_cand[q] = v;
     }
-    if (tid < kRowsPerCta) {
-        for (int i = 0; i < 18; ++i) s_x[tid * 20 + i] = a.state_hist[(static_cast<size_t>(b) * Hs + Hs - 1) * 18 + i];
-        s_x[tid * 20 + 18] = 0.0f;
+    for (uint32_t q = tid; q < rpc * 20; q += kThreads) {
+        const uint32_t i = q % 20;
+        smem[L.x + q] = i < 18 ? a.state_hist[(static_cast<size_t>(b) * Hs + Hs - 1) * 18 + i] : 0.0f;
     }
     // every CTA of the cluster must be running before any DSMEM access
     cluster.sync();
 
-    // ---- action TCN over the rolling windows of the own rows
+    // ---- window embeddings of the own rows -> every CTA; h0 -> every CTA
+    action_tcn_windows(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb);
+    state_tcn_cluster(a, cluster, c, b, smem + L.hA, s_h0);
+    cluster.sync();  // embeddings of all rows and h0 are complete everywhere
     {
-        const TcnView& tcn = a.action_tcn;
-        const uint32_t Cm = tcn.max_ch;
-        const uint32_t wpp = kThreads / Cm;           // windows per pass
-        const uint32_t slot = tid / Cm, ch = tid % Cm;
-        const uint32_t windows = kRowsPerCta * T;
-        for (uint32_t w0 = 0; w0 < windows; w0 += wpp) {
-            const uint32_t win = w0 + slot;
-            const bool active = slot < wpp && win < windows;
-            float* cur = s_tcn + (active ? slot : 0) * 3 * Cm * Hs;
-            float* h1 = cur + Cm * Hs;
-            float* h2 = h1 + Cm * Hs;
-            const uint32_t rr = active ? win / T : 0, t0 = active ? win % T : 0;
-            if (active && ch < tcn.input_dim) {
-                for (uint32_t w = 0; w < Hs; ++w) {
-                    const uint32_t pos = t0 + w;
-                    float v;
-                    if (pos < Hs - 1) v = a.action_hist[(static_cast<size_t>(b) * (Hs - 1) + pos) * A + ch];
-                    else v = s_cand[rr * TA + (pos - (Hs - 1)) * A + ch];
-                    cur[ch * Hs + w] = (v - a.action_mean[ch]) / a.action_std[ch];
-                }
-            }
-            __syncthreads();
-            for (uint32_t l = 0; l < tcn.levels; ++l) {
-                const TcnBlockView& bk = tcn.blocks[l];
-                const bool mine = active && ch < bk.out;
-                if (mine)
-                    for (uint32_t t = 0; t < Hs; ++t)
-                        h1[ch * Hs + t] = gelu_tanh(conv_at(cur, bk.in, Hs, bk.w1, ch, tcn.k, bk.dil, t) + __ldg(bk.b1 + ch));
-                __syncthreads();
-                if (mine)
-                    for (uint32_t t = 0; t < Hs; ++t)
-                        h2[ch * Hs + t] = gelu_tanh(conv_at(h1, bk.out, Hs, bk.w2, ch, tcn.k, bk.dil, t) + __ldg(bk.b2 + ch));
-                __syncthreads();
-                if (mine)
-                    for (uint32_t t = 0; t < Hs; ++t) {
-                        float res;
-                        if (bk.wr) res = conv_at(cur, bk.in, Hs, bk.wr, ch, 1, 1, t) + __ldg(bk.br + ch);
-                        else res = cur[ch * Hs + t];
-                        h1[ch * Hs + t] = gelu_tanh(h2[ch * Hs + t] + res);
-                    }
-                __syncthreads();
-                if (mine)
-                    for (uint32_t t = 0; t < Hs; ++t) cur[ch * Hs + t] = h1[ch * Hs + t];
-                __syncthreads();
-            }
-            if (active && ch < E) {
-                const float v = cur[ch * Hs + Hs - 1];
-                const uint32_t m = c * kRowsPerCta + rr;
-                for (uint32_t d = 0; d < kCluster; ++d)
-                    cluster.map_shared_rank(s_emb, d)[(m * T + t0) * E + ch] = v;
-            }
-            __syncthreads();
-        }
-    }
-    cluster.sync();  // every CTA now holds all 32 rows' window embeddings
-
-    // ---- wait for h0 from the context kernel, broadcast it to all rows
-#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 900)
-    if (a.use_pdl) cudaGridDependencySynchronize();
-#endif
-    {
-        const float4* src = reinterpret_cast<const float4*>(a.h0 + static_cast<size_t>(b) * H);
-        float4* dst = reinterpret_cast<float4*>(smem + L.h0);
-        for (uint32_t q = tid; q < kRows * H / 4; q += kThreads) dst[q] = src[q % (H / 4)];
+        const float4* src = reinterpret_cast<const float4*>(s_h0);
+        float4* dst = reinterpret_cast<float4*>(smem + L.hA);
+        for (uint32_t q = tid; q < rows * H / 4; q += kThreads) dst[q] = src[q % (H / 4)];
     }
     __syncthreads();
 
-    constexpr int KR4 = H / 128;  // float4 per lane in prober layer 1
-    const uint32_t opw = hid / 8;
-    for (uint32_t t = 0; t < T; ++t) {
-        const float* hc = smem + ((t & 1) ? L.h1 : L.h0);
-        float* hn = smem + ((t & 1) ? L.h0 : L.h1);
-        // ---- recurrent GEMM + GRU gates for this CTA's hidden units
-#pragma unroll 1
-        for (int grp = 0; grp < G::GROUPS; ++grp) {
-            float acc[2 * G::R][3];
+    if (warp == kProberWarp) {
+        // ---- prober warp: step t's prober / integrator / cost while the GEMM
+        // warps compute step t+1.  Arrival at phase t means "done with h_t".
+        for (uint32_t t = 0; t < T; ++t) {
+            cluster_arrive();
+            cluster_wait();
+            const float* hn = smem + ((t & 1) ? L.hA : L.hB);
+            prober_step(a, L, smem, hn, c, b, rpc, own0, t, H);
+        }
+    } else {
+        // ---- GEMM warps: registers hold this thread's W_hh slice
+        const uint32_t pl = lane / G::KG, kg = lane % G::KG;
+        const uint32_t pair = warp * G::PPW + pl;
+        float wr[2][3][G::KPT];
 #pragma unroll
-            for (int q = 0; q < 2 * G::R; ++q) { acc[q][0] = 0.0f; acc[q][1] = 0.0f; acc[q][2] = 0.0f; }
-#pragma unroll
-            for (int r = 0; r < G::R; ++r) {
-                const float* hrow = hc + (grp * G::R + r) * H + kg * 4;
-#pragma unroll
-                for (int i = 0; i < G::KQ; ++i) {
-                    const float4 hv = *reinterpret_cast<const float4*>(hrow + 4 * G::KG * i);
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)
-#pragma unroll
-                        for (int g = 0; g < 3; ++g) {
-                            float s = acc[q * G::R + r][g];
-                            s = fmaf(wr[q][g][4 * i + 0], hv.x, s);
-                            s = fmaf(wr[q][g][4 * i + 1], hv.y, s);
-                            s = fmaf(wr[q][g][4 * i + 2], hv.z, s);
-                            s = fmaf(wr[q][g][4 * i + 3], hv.w, s);
-                            acc[q * G::R + r][g] = s;
-                        }
-                }
-            }
-            // reduce-scatter over the KG lanes of the pair: lane kg ends with combo kg
-#pragma unroll
-            for (int m = G::KG / 2; m >= 1; m >>= 1) {
-                const bool upper = (kg & m) != 0;
-#pragma unroll
-                for (int cc = 0; cc < m; ++cc)
-#pragma unroll
-                    for (int g = 0; g < 3; ++g) {
-                        const float send = upper ? acc[cc][g] : acc[cc + m][g];
-                        const float keep = upper ? acc[cc + m][g] : acc[cc][g];
-                        acc[cc][g] = keep + __shfl_xor_sync(0xffffffffu, send, m);
-                    }
-            }
-            // candle GRU step for (row mrow, unit my_unit)
-            const uint32_t mrow = grp * G::R + my_r;
-            const float* xe = s_emb + (mrow * T + t) * E;
-            float gi[3];
+        for (int q = 0; q < 2; ++q) {
+            const uint32_t j = c * G::U + pair * 2 + q;
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
-                const float* wi = s_wih + (g * G::U + my_local) * E;
-                float s = 0.0f;
-                for (uint32_t e = 0; e < E; ++e) s = fmaf(xe[e], wi[e], s);
-                gi[g] = s + bih[g];
+                const float* row = a.w_hh + (static_cast<size_t>(g) * H + j) * H;
+#pragma unroll
+                for (int i = 0; i < G::KQ; ++i) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(row + kg * 4 + 4 * G::KG * i));
+                    wr[q][g][4 * i + 0] = v.x; wr[q][g][4 * i + 1] = v.y;
+                    wr[q][g][4 * i + 2] = v.z; wr[q][g][4 * i + 3] = v.w;
+                }
             }
-            const float ghr = acc[0][0] + bhh[0], ghz = acc[0][1] + bhh[1], ghn = acc[0][2] + bhh[2];
-            const float rg = sigmoid(gi[0] + ghr);
-            const float zg = sigmoid(gi[1] + ghz);
-            const float ng = tanhf(gi[2] + rg * ghn);
-            const float hp = hc[mrow * H + my_unit];
-            const float hnew = zg * hp - (zg - 1.0f) * ng;
-            // gather G::VEC consecutive units of one row, store to every CTA
-            float vals[G::VEC];
+        }
+        const uint32_t combo = kg % G::COMBOS;
+        const uint32_t my_q = combo / G::R, my_r = combo % G::R;
+        const uint32_t my_local = pair * 2 + my_q;
+        const uint32_t my_unit = c * G::U + my_local;
+        float bih[3], bhh[3];
 #pragma unroll
-            for (int v = 0; v < G::VEC; ++v) vals[v] = __shfl_sync(0xffffffffu, hnew, v * G::R + (lane % G::R));
-            const uint32_t srow = grp * G::R + (lane % G::R);
-            const uint32_t slot = lane / G::R;
-            float* local = hn + srow * H + c * G::U + warp * G::VEC;
+        for (int g = 0; g < 3; ++g) {
+            bih[g] = __ldg(a.b_ih + g * H + my_unit);
+            bhh[g] = __ldg(a.b_hh + g * H + my_unit);
+        }
+        for (uint32_t t = 0; t < T; ++t) {
+            const float* hc = smem + ((t & 1) ? L.hB : L.hA);
+            float* hn = smem + ((t & 1) ? L.hA : L.hB);
+#pragma unroll 1
+            for (uint32_t grp = 0; grp < groups; ++grp) {
+                float acc[2 * G::R][3];
 #pragma unroll
-            for (int dd = 0; dd < G::DPL; ++dd) {
-                float* dst = cluster.map_shared_rank(local, slot * G::DPL + dd);
+                for (int q = 0; q < 2 * G::R; ++q) { acc[q][0] = 0.0f; acc[q][1] = 0.0f; acc[q][2] = 0.0f; }
+#pragma unroll
+                for (int r = 0; r < G::R; ++r) {
+                    const float* hrow = hc + (grp * G::R + r) * H + kg * 4;
+#pragma unroll
+                    for (int i = 0; i < G::KQ; ++i) {
+                        const float4 hv = *reinterpret_cast<const float4*>(hrow + 4 * G::KG * i);
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+#pragma unroll
+                            for (int g = 0; g < 3; ++g) {
+                                float s = acc[q * G::R + r][g];
+                                s = fmaf(wr[q][g][4 * i + 0], hv.x, s);
+                                s = fmaf(wr[q][g][4 * i + 1], hv.y, s);
+                                s = fmaf(wr[q][g][4 * i + 2], hv.z, s);
+                                s = fmaf(wr[q][g][4 * i + 3], hv.w, s);
+                                acc[q * G::R + r][g] = s;
+                            }
+                    }
+                }
+                // reduce-scatter over the low 3 lane bits (lane kg ends with
+                // combo kg & 7), then all-reduce over the remaining k-group bits
+#pragma unroll
+                for (int m = G::COMBOS / 2; m >= 1; m >>= 1) {
+                    const bool upper = (kg & m) != 0;
+#pragma unroll
+                    for (int cc = 0; cc < m; ++cc)
+#pragma unroll
+                        for (int g = 0; g < 3; ++g) {
+                            const float send = upper ? acc[cc][g] : acc[cc + m][g];
+                            const float keep = upper ? acc[cc + m][g] : acc[cc][g];
+                            acc[cc][g] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                        }
+                }
+#pragma unroll
+                for (int m = G::COMBOS; m < G::KG; m <<= 1)
+#pragma unroll
+                    for (int g = 0; g < 3; ++g) acc[0][g] += __shfl_xor_sync(0xffffffffu, acc[0][g], m);
+                // candle GRU step for (row mrow, unit my_unit)
+                const uint32_t mrow = grp * G::R + my_r;
+                const float* xe = s_emb + (mrow * T + t) * E;
+                float gi[3];
+#pragma unroll
+                for (int g = 0; g < 3; ++g) {
+                    const float* wi = s_wih + (g * G::U + my_local) * E;
+                    float s = 0.0f;
+                    for (uint32_t e = 0; e < E; ++e) s = fmaf(xe[e], wi[e], s);
+                    gi[g] = s + bih[g];
+                }
+                const float ghr = acc[0][0] + bhh[0], ghz = acc[0][1] + bhh[1], ghn = acc[0][2] + bhh[2];
+                const float rg = sigmoid(gi[0] + ghr);
+                const float zg = sigmoid(gi[1] + ghz);
+                const float ng = tanhf(gi[2] + rg * ghn);
+                const float hp = hc[mrow * H + my_unit];
+                const float hnew = zg * hp - (zg - 1.0f) * ng;
+                // lane L stores row L & 3 (G::VEC consecutive units of this
+                // warp) into CTA L >> 2
+                const uint32_t srow_l = lane & (G::R - 1);
+                float vals[G::VEC];
+#pragma unroll
+                for (int v = 0; v < G::VEC; ++v)
+                    vals[v] = __shfl_sync(0xffffffffu, hnew, (v / 2) * G::KG + (v % 2) * G::R + srow_l);
+                float* local = hn + (grp * G::R + srow_l) * H + c * G::U + warp * G::VEC;
+                float* dst = cluster.map_shared_rank(local, lane / G::R);
                 if constexpr (G::VEC == 4) {
                     *reinterpret_cast<float4*>(dst) = make_float4(vals[0], vals[1], vals[2], vals[3]);
                 } else {
                     *reinterpret_cast<float2*>(dst) = make_float2(vals[0], vals[1]);
                 }
             }
-        }
-        cluster.sync();  // h_{t+1} complete in every CTA
-
-        // ---- prober layer 1 for the own rows: lane = k slice, warp = output group.
-        // 32 (output, row) combos are reduce-scattered over the 32 lanes.
-        {
-            float v[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) v[q] = 0.0f;
-#pragma unroll
-            for (int k4 = 0; k4 < KR4; ++k4) {
-                const uint32_t k = lane * 4 + 128 * k4;
-                float4 wv[8];
-#pragma unroll
-                for (int o = 0; o < 8; ++o)
-                    wv[o] = (static_cast<uint32_t>(o) < opw) ? *reinterpret_cast<const float4*>(s_w1 + (warp * opw + o) * H + k)
-                                                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                for (int rr = 0; rr < kRowsPerCta; ++rr) {
-                    const float4 hv = *reinterpret_cast<const float4*>(hn + (c * kRowsPerCta + rr) * H + k);
-#pragma unroll
-                    for (int o = 0; o < 8; ++o) {
-                        float s = v[o * kRowsPerCta + rr];
-                        s = fmaf(wv[o].x, hv.x, s);
-                        s = fmaf(wv[o].y, hv.y, s);
-                        s = fmaf(wv[o].z, hv.z, s);
-                        s = fmaf(wv[o].w, hv.w, s);
-                        v[o * kRowsPerCta + rr] = s;
-                    }
-                }
-            }
-#pragma unroll
-            for (int m = 16; m >= 1; m >>= 1) {
-                const bool upper = (lane & m) != 0;
-#pragma unroll
-                for (int cc = 0; cc < m; ++cc) {
-                    const float send = upper ? v[cc] : v[cc + m];
-                    const float keep = upper ? v[cc + m] : v[cc];
-                    v[cc] = keep + __shfl_xor_sync(0xffffffffu, send, m);
-                }
-            }
-            const uint32_t o = lane / kRowsPerCta, rr = lane % kRowsPerCta;
-            if (o < opw) {
-                const uint32_t oo = warp * opw + o;
-                s_a1[rr * hid + oo] = gelu_tanh(v[0] + __ldg(a.p_in_b + oo));
-            }
-        }
-        __syncthreads();
-        // ---- hidden prober layers and output layer (small)
-        float* pin = s_a1;
-        float* pout = s_a2;
-        for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
-            for (uint32_t q = tid; q < kRowsPerCta * hid; q += kThreads) {
-                const uint32_t rr = q / hid, o = q % hid;
-                const float* wrow = a.p_hid_w[l] + static_cast<size_t>(o) * hid;
-                float s = 0.0f;
-                for (uint32_t i = 0; i < hid; ++i) s = fmaf(pin[rr * hid + i], __ldg(wrow + i), s);
-                pout[q] = gelu_tanh(s + __ldg(a.p_hid_b[l] + o));
-            }
-            __syncthreads();
-            float* tmp = pin; pin = pout; pout = tmp;
-        }
-        for (uint32_t q = tid; q < kRowsPerCta * 15; q += kThreads) {
-            const uint32_t rr = q / 15, o = q % 15;
-            const float* wrow = a.p_out_w + static_cast<size_t>(o) * hid;
-            float s = 0.0f;
-            for (uint32_t i = 0; i < hid; ++i) s = fmaf(pin[rr * hid + i], __ldg(wrow + i), s);
-            s_out[rr * 16 + o] = s + __ldg(a.p_out_b + o);
-        }
-        __syncthreads();
-        // ---- integrator step (lewm_skyjepa_integrate_f32) + tracking cost
-        if (tid < kRowsPerCta) {
-            float x[18];
-#pragma unroll
-            for (int i = 0; i < 18; ++i) x[i] = s_x[tid * 20 + i];
-            const float* act = s_cand + tid * TA + t * A;
-            const float* po = s_out + tid * 16;
-            const float sdt = a.dt;
-            float ta;
-            if (a.rotor_forces) {
-                ta = (act[0] + act[1] + act[2] + act[3]) / a.mass;
-            } else {
-                const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
-                ta = th * a.gravity / a.hover_throttle;
-            }
-            const float acc[3] = {x[8] * ta + po[0], x[11] * ta + po[1], x[14] * ta - a.gravity + po[2]};
-            float ang[3];
-#pragma unroll
-            for (int row = 0; row < 3; ++row)
-                ang[row] = po[3 + row * 4] * act[0] + po[4 + row * 4] * act[1] + po[5 + row * 4] * act[2] +
-                           po[6 + row * 4] * act[3];
-#pragma unroll
-            for (int ax = 0; ax < 3; ++ax) { x[ax] += x[3 + ax] * sdt; x[3 + ax] += acc[ax] * sdt; }
-            const float wx = x[15] * sdt, wy = x[16] * sdt, wz = x[17] * sdt;
-            const float th2 = wx * wx + wy * wy + wz * wz;
-            float ca, cb;
-            if (th2 < 1.0e-6f) {
-                const float th4 = th2 * th2;
-                ca = 1.0f - th2 / 6.0f + th4 / 120.0f;
-                cb = 0.5f - th2 / 24.0f + th4 / 720.0f;
-            } else {
-                const float th = sqrtf(th2);
-                float sn, cs;
-                sincosf(th, &sn, &cs);
-                ca = sn / th;
-                cb = (1.0f - cs) / th2;
-            }
-            const float dl[9] = {1.0f - cb * (wy * wy + wz * wz), cb * wx * wy - ca * wz, cb * wx * wz + ca * wy,
-                                 cb * wy * wx + ca * wz, 1.0f - cb * (wx * wx + wz * wz), cb * wy * wz - ca * wx,
-                                 cb * wz * wx - ca * wy, cb * wz * wy + ca * wx, 1.0f - cb * (wx * wx + wy * wy)};
-            float nr[9];
-#pragma unroll
-            for (int row = 0; row < 3; ++row)
-#pragma unroll
-                for (int col = 0; col < 3; ++col)
-                    nr[row * 3 + col] = x[6 + row * 3] * dl[col] + x[7 + row * 3] * dl[3 + col] + x[8 + row * 3] * dl[6 + col];
-#pragma unroll
-            for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
-#pragma unroll
-            for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
-            const uint32_t s = own0 + tid;
-            if (a.states && s < a.S) {
-                float* o = a.states + ((static_cast<size_t>(b) * a.S + s) * T + t) * 18;
-#pragma unroll
-                for (int i = 0; i < 18; ++i) o[i] = x[i];
-            }
-            const float* ref = a.ref_states + (static_cast<size_t>(b) * T + t) * 18;
-            float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 3; ++i) { const float dd = x[i] - ref[i]; g0 += dd * dd; }
-#pragma unroll
-            for (int i = 3; i < 6; ++i) { const float dd = x[i] - ref[i]; g1 += dd * dd; }
-#pragma unroll
-            for (int i = 6; i < 15; ++i) { const float dd = x[i] - ref[i]; g2 += dd * dd; }
-#pragma unroll
-            for (int i = 15; i < 18; ++i) { const float dd = x[i] - ref[i]; g3 += dd * dd; }
-            const float* ra = a.ref_actions + (static_cast<size_t>(b) * T + t) * 4;
-            float ac = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) { const float dd = act[i] - ra[i]; ac += (dd * dd) * a.cost.action[i]; }
-            float st = g0 * a.cost.position + g1 * a.cost.velocity;
-            st = st + g2 * a.cost.attitude;
-            st = st + g3 * a.cost.angular_velocity;
-#pragma unroll
-            for (int i = 0; i < 18; ++i) s_x[tid * 20 + i] = x[i];
-            s_x[tid * 20 + 18] += st + ac;
+            cluster_arrive();  // h_{t+1} stored everywhere
+            cluster_wait();
         }
     }
+    __syncthreads();  // the prober warp has finished the last step
 
     // ---- scores of the own rows, then the MPPI tuple
-    if (tid < kRowsPerCta) {
-        const float score = s_x[tid * 20 + 18] * static_cast<float>(1.0 / static_cast<double>(T));
+    if (tid < rpc) {
+        const float score = smem[L.x + tid * 20 + 18] * static_cast<float>(1.0 / static_cast<double>(T));
         s_score[tid] = score;
         const uint32_t s = own0 + tid;
         if (s < a.S) a.scores[static_cast<size_t>(b) * a.S + s] = score;
     }
     __syncthreads();
     if (a.mppi) {
-        const uint32_t nvalid = own0 >= a.S ? 0u : min(static_cast<uint32_t>(kRowsPerCta), a.S - own0);
+        const uint32_t nvalid = own0 >= a.S ? 0u : min(rpc, a.S - own0);
         const uint32_t p = rb * kCluster + c;
         mppi_reduce_rows<kThreads>(a.m, b, p, nvalid, s_score, own0, s_cand, TA, s_w);
     }
@@ -573,8 +712,61 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
 
 // ------------------------------------------------------------------ host side
 
-uint32_t skyjepa_partials_per_vehicle(uint32_t S, uint32_t /*H*/) {
-    return ((S + kRows - 1) / kRows) * kCluster;
+static SkySmem layout_for(const SkyjepaArgs& a, uint32_t rows) {
+    return sky_smem_layout(a.H, rows, a.T, a.E, a.A, a.hid, a.prober_layers, a.state_tcn.max_ch,
+                           pow2_at_least(a.action_tcn.max_ch), a.Hs);
+}
+
+template <int H>
+static int max_active_clusters(size_t smem) {
+    static int cached[2] = {-1, -1};
+    static size_t cached_smem[2] = {0, 0};
+    const int slot = H == 256 ? 0 : 1;
+    if (cached[slot] >= 0 && cached_smem[slot] == smem) return cached[slot];
+    if (cudaFuncSetAttribute(skyjepa_rollout_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kCluster, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, skyjepa_rollout_kernel<H>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    cached[slot] = n;
+    cached_smem[slot] = smem;
+    return n;
+}
+
+// Rows per cluster: the smallest multiple of 8 (>= 32) whose grid fits in one
+// wave of co-resident clusters; 32 when even 64 rows would not fit (large
+// fleets run as several waves).
+uint32_t skyjepa_rows_per_cluster(const SkyjepaArgs& a) {
+    const uint32_t R = a.H == 256 ? Geom<256>::R : Geom<128>::R;
+    SkySmem big = layout_for(a, kMaxRowsPerCta * kCluster);
+    const size_t smem = big.total * sizeof(float);
+    const int maxc = a.H == 256 ? max_active_clusters<256>(smem) : max_active_clusters<128>(smem);
+    for (uint32_t rows = 32; rows <= kMaxRowsPerCta * kCluster; rows += 8) {
+        if (rows % R != 0) continue;
+        const uint64_t clusters = static_cast<uint64_t>(a.B) * ((a.S + rows - 1) / rows);
+        if (maxc > 0 && clusters <= static_cast<uint64_t>(maxc)) return rows;
+    }
+    return 32;
+}
+
+uint32_t skyjepa_partials_per_vehicle(uint32_t S, uint32_t rows) {
+    return ((S + rows - 1) / rows) * kCluster;
 }
 
 bool skyjepa_supported(const SkyjepaArgs& a, const char** why) {
@@ -582,51 +774,41 @@ bool skyjepa_supported(const SkyjepaArgs& a, const char** why) {
     if (a.A != 4) { *why = "action_dim must be 4"; return false; }
     if (a.E > kMaxTcnCh || a.action_tcn.max_ch > kMaxTcnCh) { *why = "action encoder channels must be <= 8"; return false; }
     if (a.Hs > kMaxHist || a.Hs < 2) { *why = "history_steps must be in [2, 16]"; return false; }
-    if (a.hid % 8 != 0 || a.hid > 64 || a.hid == 0) { *why = "prober hidden_dim must be a multiple of 8 and <= 64"; return false; }
+    if (a.hid % 4 != 0 || a.hid > kMaxHid || a.hid == 0) { *why = "prober hidden_dim must be a multiple of 4 and <= 64"; return false; }
     if (a.prober_layers < 1 || a.prober_layers > 5) { *why = "prober hidden_layers must be in [1, 5]"; return false; }
     if (a.T == 0 || a.T > kMaxHorizon) { *why = "horizon must be in [1, 64]"; return false; }
     if (a.state_tcn.max_ch > 256) { *why = "state encoder channels must be <= 256"; return false; }
-    const SkySmem L = sky_smem_layout(a.H, a.T, a.E, a.A, a.hid, a.action_tcn.max_ch, a.Hs);
-    if (L.total * sizeof(float) > 200 * 1024) { *why = "shared memory budget exceeded"; return false; }
+    const SkySmem L = layout_for(a, kMaxRowsPerCta * kCluster);
+    if (L.total * sizeof(float) > 220 * 1024) { *why = "shared memory budget exceeded"; return false; }
     return true;
 }
 
 template <int H>
 static cudaError_t launch_rollout(const SkyjepaArgs& a, cudaStream_t stream) {
-    const SkySmem L = sky_smem_layout(H, a.T, a.E, a.A, a.hid, a.action_tcn.max_ch, a.Hs);
+    const SkySmem L = layout_for(a, a.rows);
     const size_t smem = L.total * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(skyjepa_rollout_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(((a.S + kRows - 1) / kRows) * kCluster, a.B, 1);
+    cfg.gridDim = dim3(((a.S + a.rows - 1) / a.rows) * kCluster, a.B, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attrs[2];
+    cudaLaunchAttribute attrs[1];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
     attrs[0].val.clusterDim.x = kCluster;
     attrs[0].val.clusterDim.y = 1;
     attrs[0].val.clusterDim.z = 1;
-    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
-    cfg.numAttrs = a.use_pdl ? 2 : 1;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, skyjepa_rollout_kernel<H>, a);
 }
 
 cudaError_t launch_skyjepa(const SkyjepaArgs& a, cudaStream_t stream, int* launches) {
-    const size_t ctx_smem = static_cast<size_t>(3) * a.state_tcn.max_ch * a.Hs * sizeof(float);
-    if (ctx_smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(skyjepa_context_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(ctx_smem));
-        if (e != cudaSuccess) return e;
-    }
-    skyjepa_context_kernel<<<dim3(kCluster, a.B, 1), kThreads, ctx_smem, stream>>>(a);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    e = (a.H == 256) ? launch_rollout<256>(a, stream) : launch_rollout<128>(a, stream);
-    if (launches) *launches = 2;
+    if (a.rows % kCluster != 0 || a.rows < 32 || a.rows > kMaxRowsPerCta * kCluster) return cudaErrorInvalidValue;
+    const cudaError_t e = (a.H == 256) ? launch_rollout<256>(a, stream) : launch_rollout<128>(a, stream);
+    if (launches) *launches = 1;
     return e;
 }
 

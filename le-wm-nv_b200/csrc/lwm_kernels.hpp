@@ -114,7 +114,7 @@ struct SkyjepaArgs {
     const float* action_hist;     // [B,Hs-1,4] raw
     const float* ref_states;      // [B,T,18]
     const float* ref_actions;     // [B,T,4]
-    float* h0;                    // [B,H] written by the context kernel
+    uint32_t rows;                // candidate rows per cluster (multiple of 8, 32..64)
     int sample;
     const float* mean;            // [B,T,4]
     const float* std;             // [B,T,4]
@@ -127,7 +127,6 @@ struct SkyjepaArgs {
     float* states;
     int mppi;
     MppiArgs m;
-    int use_pdl;
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
@@ -145,10 +144,12 @@ cudaError_t launch_normal_fill(uint64_t seed, uint64_t offset, uint64_t count, f
 uint32_t nominal_blocks_per_vehicle(uint32_t S);
 cudaError_t launch_nominal(const NominalArgs& a, cudaStream_t stream);
 
-// Rows per cluster and partials per vehicle of the fused SkyJEPA kernel.
-uint32_t skyjepa_partials_per_vehicle(uint32_t S, uint32_t H);
+// Rows per cluster (one wave of co-resident clusters when possible) and MPPI
+// partials per vehicle of the fused SkyJEPA kernel.
+uint32_t skyjepa_rows_per_cluster(const SkyjepaArgs& a);
+uint32_t skyjepa_partials_per_vehicle(uint32_t S, uint32_t rows);
 bool skyjepa_supported(const SkyjepaArgs& a, const char** why);
-// Launches the context kernel (state TCN -> h0) and the fused rollout kernel.
+// Launches the fused rollout kernel (a.rows must be set).
 cudaError_t launch_skyjepa(const SkyjepaArgs& a, cudaStream_t stream, int* launches);
 
 }  // namespace lwm

@@ -11,10 +11,11 @@ has not been built (``make -C le-wm-nv_b200``).  There is no CPU fallback.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes as C
-import dataclasses
 import os
-from dataclasses import dataclass, field
+import weakref
+from dataclasses import dataclass
 from typing import Callable, List, Optional, Sequence
 
 import numpy as np
@@ -243,6 +244,22 @@ def version() -> str:
     return lib.lwm_version().decode()
 
 
+# Handles still alive at interpreter exit are released in dependency order
+# (planners and scorers before the contexts they use), before the CUDA
+# runtime is torn down.
+_LIVE = {"planner": weakref.WeakSet(), "scorer": weakref.WeakSet(), "ctx": weakref.WeakSet()}
+
+
+@atexit.register
+def _close_all() -> None:
+    for kind in ("planner", "scorer", "ctx"):
+        for obj in list(_LIVE[kind]):
+            try:
+                obj.close()
+            except Exception:
+                pass
+
+
 # ------------------------------------------------------------------- context
 
 class Context:
@@ -253,6 +270,7 @@ class Context:
         _check(lib.lwm_ctx_create(device, C.byref(h)))
         self.handle = h
         self.device = device
+        _LIVE["ctx"].add(self)
 
     @property
     def stream(self) -> int:
@@ -274,6 +292,10 @@ class Context:
 
     def close(self) -> None:
         if getattr(self, "handle", None):
+            for kind in ("planner", "scorer"):
+                for obj in list(_LIVE[kind]):
+                    if getattr(obj, "ctx", None) is self:
+                        obj.close()
             lib.lwm_ctx_destroy(self.handle)
             self.handle = None
 
@@ -480,7 +502,8 @@ class Scorer:
 
     def close(self) -> None:
         if getattr(self, "handle", None):
-            lib.lwm_scorer_destroy(self.handle)
+            if getattr(self.ctx, "handle", None):
+                lib.lwm_scorer_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
@@ -500,6 +523,7 @@ class NominalScorer(Scorer):
         h = VP()
         _check(lib.lwm_scorer_nominal_create(ctx.handle, C.byref(cfg), C.byref(h)))
         self.handle = h
+        _LIVE["scorer"].add(self)
 
     def set_context(self, initial, motors, reference_states, reference_actions, domains=None) -> None:
         initial = _f32(initial)
@@ -527,6 +551,7 @@ class SkyJepaScorer(Scorer):
                                              _fp(_f32(state_mean)), _fp(_f32(state_std)), _fp(_f32(action_mean)),
                                              _fp(_f32(action_std)), C.byref(cost), F(dt), C.byref(h)))
         self.handle = h
+        _LIVE["scorer"].add(self)
 
     def set_context(self, state_history, action_history, reference_states, reference_actions) -> None:
         sh = _f32(state_history)
@@ -574,6 +599,7 @@ class CallbackScorer(Scorer):
         h = VP()
         _check(lib.lwm_scorer_callback_create(ctx.handle, batch, self._cb, None, C.byref(h)))
         self.handle = h
+        _LIVE["scorer"].add(self)
 
 
 # ------------------------------------------------------------------- planners
@@ -588,6 +614,7 @@ class _Planner:
         h = VP()
         _check(self._create(ctx.handle, C.byref(self._cfg), C.byref(h)))
         self.handle = h
+        _LIVE["planner"].add(self)
 
     def plan(self, scorer: Scorer, injected_noise: Optional[np.ndarray] = None, batch: Optional[int] = None) -> PlanResult:
         cfg = self.config
@@ -645,7 +672,8 @@ class _Planner:
 
     def close(self) -> None:
         if getattr(self, "handle", None):
-            lib.lwm_planner_destroy(self.handle)
+            if getattr(self.ctx, "handle", None):
+                lib.lwm_planner_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
