@@ -49,8 +49,11 @@ namespace lwm {
 constexpr int kCluster = 8;
 constexpr int kGemmWarps = 8;
 constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kThreads = kGemmThreads + 32;  // + the prober warp
-constexpr int kProberWarp = kGemmWarps;
+constexpr int kProberWarps = 4;               // one per SM sub-partition
+constexpr int kProberThreads = kProberWarps * 32;
+constexpr int kThreads = kGemmThreads + kProberThreads;
+constexpr int kProberWarp0 = kGemmWarps;
+constexpr int kProberBarrier = 1;             // named barrier of the prober warps
 constexpr int kMaxTcnCh = 8;       // action-encoder channel bound
 constexpr int kMaxHist = 16;
 constexpr int kMaxRowsPerCta = 8;  // M <= 64 rows per cluster
@@ -80,15 +83,27 @@ __host__ __device__ inline uint32_t pow2_at_least(uint32_t v) {
 
 struct SkySmem {
     // Offsets in floats inside the dynamic shared-memory block.
-    uint32_t hA, hB, emb, cand, w1, wih, pw2, pw3, pb, a1, a2, pout, x, score, w, h0v, total;
-    uint32_t w1_stride, pw_stride;
+    uint32_t hA, hB, emb, cand, w1, wih, pw2, pw3, pb, red1, a1, a2, pout, x, score, w, h0v, aw, sw, total;
+    uint32_t w1_stride, pw_stride, sw_half;
 };
+
+// Floats of the action encoder's weights (contiguous in the blob).
+__host__ __device__ inline uint32_t tcn_weight_floats(const TcnView& t) {
+    uint32_t n = 0;
+    for (uint32_t l = 0; l < t.levels; ++l) {
+        const TcnBlockView& b = t.blocks[l];
+        n += b.out * b.in * t.k + b.out + b.out * b.out * t.k + b.out;
+        if (b.in != b.out) n += b.out * b.in + b.out;
+    }
+    return n;
+}
 
 // rows = M rows per cluster; Cs = widest state-TCN layer; Ca = action-TCN
 // lanes per window (power of two).
 __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, uint32_t T, uint32_t E, uint32_t A,
                                                    uint32_t hid, uint32_t layers, uint32_t Cs, uint32_t Ca,
-                                                   uint32_t Hs) {
+                                                   uint32_t Hs, uint32_t aw_floats, uint32_t Ks, uint32_t Cl,
+                                                   uint32_t Cs0, uint32_t levels) {
     SkySmem s;
     uint32_t off = 0;
     auto take = [&](uint32_t n) { uint32_t o = off; off += (n + 3u) & ~3u; return o; };
@@ -98,8 +113,26 @@ __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, ui
     const uint32_t ks = kThreads / per;
     const uint32_t state_scratch = 3 * Cs * Hs + ks * per * Hs + 8;
     const uint32_t action_scratch = (kThreads / Ca) * 3 * Ca * Hs;
+    // the state-TCN weight slices (largest: conv2 + residual of level 0, or
+    // the projection) stream through two halves overlaid on hB
+    uint32_t wmax = (H / kCluster) * Cl;
+    {
+        uint32_t cin = Cs0;
+        for (uint32_t l = 0; l < 8 && l < levels; ++l) {
+            const uint32_t w1n = per * cin * Ks;
+            const uint32_t w2n = per * Cs * Ks + (cin != Cs ? per * cin : 0);
+            wmax = w1n > wmax ? w1n : wmax;
+            wmax = w2n > wmax ? w2n : wmax;
+            cin = Cs;
+        }
+    }
+    s.sw_half = (wmax + 3u) & ~3u;
+    uint32_t hb_need = rows * H;
+    hb_need = action_scratch > hb_need ? action_scratch : hb_need;
+    hb_need = 2 * s.sw_half > hb_need ? 2 * s.sw_half : hb_need;
     s.hA = take(rows * H > state_scratch ? rows * H : state_scratch);
-    s.hB = take(rows * H > action_scratch ? rows * H : action_scratch);
+    s.hB = take(hb_need);
+    s.sw = s.hB;
     s.emb = take(rows * T * E);
     s.cand = take(rpc * T * A);
     s.w1_stride = H + 4;
@@ -109,6 +142,7 @@ __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, ui
     s.pw2 = take((layers > 1 ? layers - 1 : 1) * hid * s.pw_stride);
     s.pw3 = take(15 * s.pw_stride);
     s.pb = take(hid * layers + 16);
+    s.red1 = take(kProberWarps * rpc * hid);
     s.a1 = take(rpc * hid);
     s.a2 = take(rpc * hid);
     s.pout = take(rpc * 16);
@@ -116,12 +150,30 @@ __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, ui
     s.score = take(rpc);
     s.w = take(rpc);
     s.h0v = take(H);
+    s.aw = take(aw_floats);
     s.total = off;
     return s;
 }
 
+__host__ __device__ inline SkySmem layout_for(const SkyjepaArgs& a, uint32_t rows) {
+    return sky_smem_layout(a.H, rows, a.T, a.E, a.A, a.hid, a.prober_layers, a.state_tcn.max_ch,
+                           pow2_at_least(a.action_tcn.max_ch), a.Hs, tcn_weight_floats(a.action_tcn), a.state_tcn.k,
+                           a.state_tcn.out_dim, a.state_tcn.input_dim, a.state_tcn.levels);
+}
+
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void prober_sync() { asm volatile("bar.sync %0, %1;" :: "n"(kProberBarrier), "n"(kProberThreads) : "memory"); }
+
+// Asynchronous global->shared copy of n floats (4-byte granularity, any alignment).
+__device__ __forceinline__ void async_copy(float* dst, const float* src, uint32_t n) {
+    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + i));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(src + i) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void async_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // --------------------------------------------------------------- prologue
 //
@@ -132,41 +184,75 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 // all time steps, the slices are reduced in shared memory, and the result is
 // broadcast to every CTA's activation buffer.
 __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
-                                  float* scratch, float* h0v) {
+                                  float* scratch, float* h0v, float* sw, uint32_t sw_half) {
     const TcnView& tcn = a.state_tcn;
-    const uint32_t Hs = a.Hs, C = tcn.max_ch, tid = threadIdx.x;
+    const uint32_t Hs = a.Hs, C = tcn.max_ch, tid = threadIdx.x, K = tcn.k;
     const uint32_t per = (C + kCluster - 1) / kCluster;
     const uint32_t KS = kThreads / per;
+    const uint32_t o0 = c * per;
+    const uint32_t hper = a.H / kCluster, Cl = tcn.out_dim;
     float* xa = scratch;
     float* xb = scratch + C * Hs;
     float* hb = scratch + 2 * C * Hs;
     float* red = scratch + 3 * C * Hs;  // [KS][per][Hs], local
+    // Weight slices of the convolutions in order (conv1, conv2 + residual of
+    // every level, then the projection) stream through two shared buffers.
+    const uint32_t nstage = 2 * tcn.levels + 1;
+    auto stage = [&](uint32_t n) {
+        float* dst = sw + (n & 1) * sw_half;
+        if (n >= nstage) { asm volatile("cp.async.commit_group;" ::: "memory"); return; }
+        if (n == nstage - 1) {
+            async_copy(dst, a.proj_w + static_cast<size_t>(c * hper) * Cl, hper * Cl);
+            return;
+        }
+        const TcnBlockView& bk = tcn.blocks[n / 2];
+        const uint32_t cnt = min(per, bk.out > o0 ? bk.out - o0 : 0u);
+        if (n % 2 == 0) {
+            async_copy(dst, bk.w1 + static_cast<size_t>(o0) * bk.in * K, cnt * bk.in * K);
+        } else {
+            // conv2 slice, then the residual 1x1 slice right after it
+            for (uint32_t i = tid; i < cnt * bk.out * K; i += kThreads) {
+                const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + i));
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(bk.w2 + static_cast<size_t>(o0) * bk.out * K + i) : "memory");
+            }
+            if (bk.wr)
+                for (uint32_t i = tid; i < cnt * bk.in; i += kThreads) {
+                    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + per * C * K + i));
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(bk.wr + static_cast<size_t>(o0) * bk.in + i) : "memory");
+                }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+    };
+    __syncthreads();  // the weight buffers overlay the action-TCN scratch
+    stage(0);
     for (uint32_t q = tid; q < tcn.input_dim * Hs; q += kThreads) {
         const uint32_t i = q / Hs, t = q % Hs;
         const float v = a.state_hist[(static_cast<size_t>(b) * Hs + t) * 18 + i];
         xa[q] = (v - a.state_mean[i]) / a.state_std[i];
     }
-    __syncthreads();
     float* cur = xa;
     float* nxt = xb;
     const uint32_t o_local = tid % per, slice = tid / per;
+    uint32_t n = 0;
     for (uint32_t l = 0; l < tcn.levels; ++l) {
         const TcnBlockView& bk = tcn.blocks[l];
-        const uint32_t o0 = c * per;
         const uint32_t o = o0 + o_local;
-        for (int conv = 0; conv < 2; ++conv) {
+        for (int conv = 0; conv < 2; ++conv, ++n) {
+            stage(n + 1);
+            async_wait_all_but_one();
+            __syncthreads();
+            const float* Ws = sw + (n & 1) * sw_half;
             const float* src = conv == 0 ? cur : hb;
             const uint32_t cin = conv == 0 ? bk.in : bk.out;
-            const float* W = conv == 0 ? bk.w1 : bk.w2;
             if (slice < KS && o < bk.out) {
                 float acc[kMaxHist];
 #pragma unroll
                 for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
                 for (uint32_t i = slice; i < cin; i += KS) {
                     const float* xr = src + i * Hs;
-                    for (uint32_t j = 0; j < tcn.k; ++j) {
-                        const float wv = __ldg(W + (static_cast<size_t>(o) * cin + i) * tcn.k + j);
-                        const int sh = static_cast<int>((tcn.k - 1 - j) * bk.dil);
+                    for (uint32_t j = 0; j < K; ++j) {
+                        const float wv = Ws[(o_local * cin + i) * K + j];
+                        const int sh = static_cast<int>((K - 1 - j) * bk.dil);
 #pragma unroll
                         for (int t = 0; t < kMaxHist; ++t)
                             if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, xr[t - sh], acc[t]);
@@ -189,9 +275,15 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
                     const float h2 = gelu_tanh(s + __ldg(bk.b2 + oo));
                     float res;
                     if (bk.wr) {
-                        float r = 0.0f;
-                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(__ldg(bk.wr + static_cast<size_t>(oo) * bk.in + i), cur[i * Hs + t], r);
-                        res = r + __ldg(bk.br + oo);
+                        const float* wrs = Ws + per * C * K + ol * bk.in;
+                        float r0 = 0.0f, r1 = 0.0f;
+                        uint32_t i = 0;
+                        for (; i + 2 <= bk.in; i += 2) {
+                            r0 = fmaf(wrs[i], cur[i * Hs + t], r0);
+                            r1 = fmaf(wrs[i + 1], cur[(i + 1) * Hs + t], r1);
+                        }
+                        if (i < bk.in) r0 = fmaf(wrs[i], cur[i * Hs + t], r0);
+                        res = (r0 + r1) + __ldg(bk.br + oo);
                     } else {
                         res = cur[oo * Hs + t];
                     }
@@ -204,23 +296,24 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
         }
         float* tmp = cur; cur = nxt; nxt = tmp;
     }
-    // state_projection of the last time step: CTA c writes H/8 outputs to every CTA
-    const uint32_t hper = a.H / kCluster, Cl = tcn.out_dim;
-    for (uint32_t q = tid; q < hper; q += kThreads) {
-        const uint32_t oo = c * hper + q;
-        const float* wrow = a.proj_w + static_cast<size_t>(oo) * Cl;
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        uint32_t i = 0;
-        for (; i + 4 <= Cl; i += 4) {
-            s0 = fmaf(cur[(i + 0) * Hs + Hs - 1], __ldg(wrow + i + 0), s0);
-            s1 = fmaf(cur[(i + 1) * Hs + Hs - 1], __ldg(wrow + i + 1), s1);
-            s2 = fmaf(cur[(i + 2) * Hs + Hs - 1], __ldg(wrow + i + 2), s2);
-            s3 = fmaf(cur[(i + 3) * Hs + Hs - 1], __ldg(wrow + i + 3), s3);
+    // state_projection of the last time step: CTA c writes H/8 outputs to
+    // every CTA; four lanes per output, reduced with shuffles.
+    stage(n + 1);
+    async_wait_all_but_one();
+    __syncthreads();
+    const float* Wp = sw + (n & 1) * sw_half;
+    for (uint32_t q = tid; q < hper * 4; q += kThreads) {
+        const uint32_t ol = q / 4, part = q % 4, oo = c * hper + ol;
+        float s = 0.0f;
+        for (uint32_t i = part; i < Cl; i += 4) s = fmaf(cur[i * Hs + Hs - 1], Wp[ol * Cl + i], s);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (part == 0) {
+            const float v = s + __ldg(a.proj_b + oo);
+            for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(h0v, d)[oo] = v;
         }
-        for (; i < Cl; ++i) s0 = fmaf(cur[i * Hs + Hs - 1], __ldg(wrow + i), s0);
-        const float v = ((s0 + s1) + (s2 + s3)) + __ldg(a.proj_b + oo);
-        for (uint32_t d = 0; d < kCluster; ++d) cluster.map_shared_rank(h0v, d)[oo] = v;
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // SkyJepaModel::rollout_candidates window encoding (model.rs:192-215) with
@@ -229,8 +322,10 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
 // own.  `ca` lanes of one warp own a window, one output channel each, all
 // time steps in registers; warp-level syncs between convolutions.
 __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
-                                   uint32_t rpc, const float* s_cand, float* scratch, float* s_emb) {
+                                   uint32_t rpc, const float* s_cand, float* scratch, float* s_emb, const float* aw) {
     const TcnView& tcn = a.action_tcn;
+    const float* wbase = tcn.blocks[0].w1;  // the encoder's weights are contiguous from here
+    auto sm = [&](const float* p) { return aw + (p - wbase); };
     const uint32_t Hs = a.Hs, T = a.T, A = a.A, E = a.E, TA = T * A;
     const uint32_t ca = pow2_at_least(tcn.max_ch);
     const uint32_t wpp = kThreads / ca;
@@ -259,21 +354,21 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
             for (int conv = 0; conv < 2; ++conv) {
                 const float* src = conv == 0 ? cur : hb;
                 const uint32_t cin = conv == 0 ? bk.in : bk.out;
-                const float* W = conv == 0 ? bk.w1 : bk.w2;
+                const float* W = sm(conv == 0 ? bk.w1 : bk.w2);
                 float acc[kMaxHist];
 #pragma unroll
                 for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
                 if (mine) {
                     for (uint32_t i = 0; i < cin; ++i)
                         for (uint32_t j = 0; j < tcn.k; ++j) {
-                            const float wv = __ldg(W + (static_cast<size_t>(o) * cin + i) * tcn.k + j);
+                            const float wv = W[(o * cin + i) * tcn.k + j];
                             const int sh = static_cast<int>((tcn.k - 1 - j) * bk.dil);
 #pragma unroll
                             for (int t = 0; t < kMaxHist; ++t)
                                 if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, src[i * Hs + t - sh], acc[t]);
                         }
                 }
-                const float bias = mine ? __ldg((conv == 0 ? bk.b1 : bk.b2) + o) : 0.0f;
+                const float bias = mine ? sm(conv == 0 ? bk.b1 : bk.b2)[o] : 0.0f;
                 if (conv == 0) {
                     if (mine)
 #pragma unroll
@@ -290,12 +385,13 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
             for (int t = 0; t < kMaxHist; ++t) res[t] = 0.0f;
             if (mine) {
                 if (bk.wr) {
-                    const float br = __ldg(bk.br + o);
+                    const float br = sm(bk.br)[o];
+                    const float* wr = sm(bk.wr) + o * bk.in;
 #pragma unroll
                     for (int t = 0; t < kMaxHist; ++t) {
                         if (t >= static_cast<int>(Hs)) break;
                         float r = 0.0f;
-                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(__ldg(bk.wr + static_cast<size_t>(o) * bk.in + i), cur[i * Hs + t], r);
+                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(wr[i], cur[i * Hs + t], r);
                         res[t] = r + br;
                     }
                 } else {
@@ -320,33 +416,37 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
     }
 }
 
-// ------------------------------------------------------- the prober warp
+// ------------------------------------------------------- the prober warps
 //
 // SkyJepaProber::forward (prober.rs:84-102) for the CTA's own rows, then one
 // step of lewm_skyjepa_integrate_f32 (kinematics.rs:377-484) and the tracking
-// cost (control.rs:430-452) of that step.
+// cost (control.rs:430-452) of that step.  Four warps: layer 1 is split over
+// k (warp pw sums k in [pw*H/4, (pw+1)*H/4)), the later layers over
+// (row, output) pairs; the integrator runs on lanes 0..rpc-1 of the first.
 __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem, const float* hn, uint32_t c,
                             uint32_t b, uint32_t rpc, uint32_t own0, uint32_t t, uint32_t H) {
-    const uint32_t lane = threadIdx.x & 31, hid = a.hid, T = a.T, A = a.A, TA = T * A;
+    const uint32_t ptid = threadIdx.x - kGemmThreads;  // 0..127
+    const uint32_t pw = ptid >> 5, lane = ptid & 31, hid = a.hid, T = a.T, A = a.A, TA = T * A;
     float* s_a1 = smem + L.a1;
     float* s_a2 = smem + L.a2;
     float* s_pout = smem + L.pout;
+    float* red1 = smem + L.red1;  // [kProberWarps][rpc][hid]
     const float* w1 = smem + L.w1;
     const float* pb = smem + L.pb;
-    // layer 1: lane owns outputs lane and lane + 32
+    // layer 1 partial sums: lane owns outputs lane and lane + 32
     {
         float acc[2][kMaxRowsPerCta];
 #pragma unroll
         for (int q = 0; q < 2; ++q)
 #pragma unroll
             for (int r = 0; r < kMaxRowsPerCta; ++r) acc[q][r] = 0.0f;
-        const bool two = hid > 32;
+        const bool has0 = lane < hid, has1 = lane + 32 < hid;
         const float* wr0 = w1 + lane * L.w1_stride;
         const float* wr1 = w1 + (lane + 32) * L.w1_stride;
-        const bool has0 = lane < hid;
-        for (uint32_t k = 0; k < H; k += 4) {
+        const uint32_t k0 = pw * (H / kProberWarps), k1 = k0 + H / kProberWarps;
+        for (uint32_t k = k0; k < k1; k += 4) {
             const float4 w0 = has0 ? *reinterpret_cast<const float4*>(wr0 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 w1v = two && lane + 32 < hid ? *reinterpret_cast<const float4*>(wr1 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 w1v = has1 ? *reinterpret_cast<const float4*>(wr1 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int r = 0; r < kMaxRowsPerCta; ++r) {
                 if (static_cast<uint32_t>(r) >= rpc) break;
@@ -354,7 +454,7 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
                 float s = acc[0][r];
                 s = fmaf(w0.x, hv.x, s); s = fmaf(w0.y, hv.y, s); s = fmaf(w0.z, hv.z, s); s = fmaf(w0.w, hv.w, s);
                 acc[0][r] = s;
-                if (two) {
+                if (has1) {
                     float u = acc[1][r];
                     u = fmaf(w1v.x, hv.x, u); u = fmaf(w1v.y, hv.y, u); u = fmaf(w1v.z, hv.z, u); u = fmaf(w1v.w, hv.w, u);
                     acc[1][r] = u;
@@ -364,60 +464,58 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
 #pragma unroll
         for (int r = 0; r < kMaxRowsPerCta; ++r) {
             if (static_cast<uint32_t>(r) >= rpc) break;
-            if (has0) s_a1[r * hid + lane] = gelu_tanh(acc[0][r] + pb[lane]);
-            if (two && lane + 32 < hid) s_a1[r * hid + lane + 32] = gelu_tanh(acc[1][r] + pb[lane + 32]);
+            if (has0) red1[(pw * rpc + r) * hid + lane] = acc[0][r];
+            if (has1) red1[(pw * rpc + r) * hid + lane + 32] = acc[1][r];
         }
     }
-    __syncwarp();
-    // hidden layers
+    prober_sync();
+    for (uint32_t q = ptid; q < rpc * hid; q += kProberThreads) {
+        const uint32_t r = q / hid, o = q % hid;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kProberWarps; ++w) s += red1[(w * rpc + r) * hid + o];
+        s_a1[r * hid + o] = gelu_tanh(s + pb[o]);
+    }
+    prober_sync();
+    // hidden layers: one (row, output) pair per thread
     float* pin = s_a1;
     float* pout = s_a2;
     for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
         const float* W = smem + L.pw2 + l * hid * L.pw_stride;
         const float* bias = pb + (l + 1) * hid;
-        for (uint32_t o = lane; o < hid; o += 32) {
-            float acc[kMaxRowsPerCta];
-#pragma unroll
-            for (int r = 0; r < kMaxRowsPerCta; ++r) acc[r] = 0.0f;
-            for (uint32_t i = 0; i < hid; ++i) {
-                const float wv = W[o * L.pw_stride + i];
-#pragma unroll
-                for (int r = 0; r < kMaxRowsPerCta; ++r)
-                    if (static_cast<uint32_t>(r) < rpc) acc[r] = fmaf(pin[r * hid + i], wv, acc[r]);
-            }
-#pragma unroll
-            for (int r = 0; r < kMaxRowsPerCta; ++r)
-                if (static_cast<uint32_t>(r) < rpc) pout[r * hid + o] = gelu_tanh(acc[r] + bias[o]);
+        for (uint32_t q = ptid; q < rpc * hid; q += kProberThreads) {
+            const uint32_t r = q / hid, o = q % hid;
+            const float* ar = pin + r * hid;
+            const float* wr = W + o * L.pw_stride;
+            float s0 = 0.0f, s1 = 0.0f;
+            uint32_t i = 0;
+            for (; i + 2 <= hid; i += 2) { s0 = fmaf(ar[i], wr[i], s0); s1 = fmaf(ar[i + 1], wr[i + 1], s1); }
+            if (i < hid) s0 = fmaf(ar[i], wr[i], s0);
+            pout[q] = gelu_tanh((s0 + s1) + bias[o]);
         }
-        __syncwarp();
+        prober_sync();
         float* tmp = pin; pin = pout; pout = tmp;
     }
     // output layer: 15 values per row
-    if (lane < 15) {
-        const float* W = smem + L.pw3 + lane * L.pw_stride;
-        const float bias = pb[a.prober_layers * hid + lane];
-        float acc[kMaxRowsPerCta];
-#pragma unroll
-        for (int r = 0; r < kMaxRowsPerCta; ++r) acc[r] = 0.0f;
-        for (uint32_t i = 0; i < hid; ++i) {
-            const float wv = W[i];
-#pragma unroll
-            for (int r = 0; r < kMaxRowsPerCta; ++r)
-                if (static_cast<uint32_t>(r) < rpc) acc[r] = fmaf(pin[r * hid + i], wv, acc[r]);
-        }
-#pragma unroll
-        for (int r = 0; r < kMaxRowsPerCta; ++r)
-            if (static_cast<uint32_t>(r) < rpc) s_pout[r * 16 + lane] = acc[r] + bias;
+    for (uint32_t q = ptid; q < rpc * 15; q += kProberThreads) {
+        const uint32_t r = q / 15, o = q % 15;
+        const float* ar = pin + r * hid;
+        const float* wr = smem + L.pw3 + o * L.pw_stride;
+        float s0 = 0.0f, s1 = 0.0f;
+        uint32_t i = 0;
+        for (; i + 2 <= hid; i += 2) { s0 = fmaf(ar[i], wr[i], s0); s1 = fmaf(ar[i + 1], wr[i + 1], s1); }
+        if (i < hid) s0 = fmaf(ar[i], wr[i], s0);
+        s_pout[r * 16 + o] = (s0 + s1) + pb[a.prober_layers * hid + o];
     }
-    __syncwarp();
-    // integrator + cost: lane r owns row r
-    if (lane < rpc) {
-        float* xs = smem + L.x + lane * 20;
+    prober_sync();
+    // integrator + cost: thread r of the first prober warp owns row r
+    if (ptid < rpc) {
+        float* xs = smem + L.x + ptid * 20;
         float x[18];
 #pragma unroll
         for (int i = 0; i < 18; ++i) x[i] = xs[i];
-        const float* act = smem + L.cand + lane * TA + t * A;
-        const float* po = s_pout + lane * 16;
+        const float* act = smem + L.cand + ptid * TA + t * A;
+        const float* po = s_pout + ptid * 16;
         const float sdt = a.dt;
         float ta;
         if (a.rotor_forces) {
@@ -461,7 +559,7 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
         for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
 #pragma unroll
         for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
-        const uint32_t s = own0 + lane;
+        const uint32_t s = own0 + ptid;
         if (a.states && s < a.S) {
             float* o = a.states + ((static_cast<size_t>(b) * a.S + s) * T + t) * 18;
 #pragma unroll
@@ -488,7 +586,6 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
         for (int i = 0; i < 18; ++i) xs[i] = x[i];
         xs[18] += st + ac;
     }
-    __syncwarp();
 }
 
 // ------------------------------------------------------------ rollout kernel
@@ -504,8 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t T = a.T, A = a.A, E = a.E, Hs = a.Hs, hid = a.hid;
     const uint32_t rows = a.rows, rpc = rows / kCluster, groups = rows / G::R;
-    const uint32_t ca = pow2_at_least(a.action_tcn.max_ch);
-    const SkySmem L = sky_smem_layout(H, rows, T, E, A, hid, a.prober_layers, a.state_tcn.max_ch, ca, Hs);
+    const SkySmem L = layout_for(a, rows);
     float* s_emb = smem + L.emb;     // [rows][T][E]
     float* s_cand = smem + L.cand;   // [rpc][T][A]
     float* s_wih = smem + L.wih;     // [3][U][E] for this CTA's units
@@ -534,6 +630,11 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     for (uint32_t l = 0; l + 1 < a.prober_layers; ++l)
         for (uint32_t q = tid; q < hid; q += kThreads) smem[L.pb + (l + 1) * hid + q] = __ldg(a.p_hid_b[l] + q);
     for (uint32_t q = tid; q < 15; q += kThreads) smem[L.pb + a.prober_layers * hid + q] = __ldg(a.p_out_b + q);
+    {
+        const uint32_t n = tcn_weight_floats(a.action_tcn);
+        const float* src = a.action_tcn.blocks[0].w1;
+        for (uint32_t q = tid; q < n; q += kThreads) smem[L.aw + q] = __ldg(src + q);
+    }
 
     // ---- sampling of the CTA's own rows (as sample_kernel)
     for (uint32_t q = tid; q < rpc * TA; q += kThreads) {
@@ -564,8 +665,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     cluster.sync();
 
     // ---- window embeddings of the own rows -> every CTA; h0 -> every CTA
-    action_tcn_windows(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb);
-    state_tcn_cluster(a, cluster, c, b, smem + L.hA, s_h0);
+    action_tcn_windows(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb, smem + L.aw);
+    state_tcn_cluster(a, cluster, c, b, smem + L.hA, s_h0, smem + L.sw, L.sw_half);
     cluster.sync();  // embeddings of all rows and h0 are complete everywhere
     {
         const float4* src = reinterpret_cast<const float4*>(s_h0);
@@ -574,8 +675,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     }
     __syncthreads();
 
-    if (warp == kProberWarp) {
-        // ---- prober warp: step t's prober / integrator / cost while the GEMM
+    if (warp >= kProberWarp0) {
+        // ---- prober warps: step t's prober / integrator / cost while the GEMM
         // warps compute step t+1.  Arrival at phase t means "done with h_t".
         for (uint32_t t = 0; t < T; ++t) {
             cluster_arrive();
@@ -693,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
             cluster_wait();
         }
     }
-    __syncthreads();  // the prober warp has finished the last step
+    __syncthreads();  // the prober warps have finished the last step
 
     // ---- scores of the own rows, then the MPPI tuple
     if (tid < rpc) {
@@ -712,10 +813,6 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
 
 // ------------------------------------------------------------------ host side
 
-static SkySmem layout_for(const SkyjepaArgs& a, uint32_t rows) {
-    return sky_smem_layout(a.H, rows, a.T, a.E, a.A, a.hid, a.prober_layers, a.state_tcn.max_ch,
-                           pow2_at_least(a.action_tcn.max_ch), a.Hs);
-}
 
 template <int H>
 static int max_active_clusters(size_t smem) {
