@@ -389,6 +389,51 @@ lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, 
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count,
                              float* out);
 
+/* ---------------------------------------------------------------- allocation-free iteration */
+
+/* Device buffers of lwm_nominal_mppi_noalloc, all owned by the caller. */
+typedef struct lwm_nominal_mppi_io {
+    const float* initial;            /* [B,18] */
+    const float* motors;             /* [B,4] */
+    const float* reference_states;   /* [B,T,18] */
+    const float* reference_actions;  /* [B,T,4] */
+    const lwm_domain* domains;       /* [B] */
+    const float* mean;               /* [B,T,4] sampling mean (e.g. the warm start) */
+    const float* std;                /* [B,T,4] sampling std */
+    const float* injected_noise;     /* [B,S,T,4] standard normals, or NULL for Philox(seed, offset) */
+    float* scores;                   /* [B,S] */
+    float* sequence;                 /* [B,T,4] MPPI-weighted sequence */
+    float* first_action;             /* [B,4] */
+    float* warm_start;               /* [B,T,4] sequence shifted by one step */
+    uint32_t* best_indices;          /* [B] */
+} lwm_nominal_mppi_io;
+
+/* One fused nominal-physics MPPI iteration (sample, rotor rollout, tracking
+ * cost, weighted sequence, best index) that allocates no memory: no
+ * cudaMalloc, no cudaFree, no allocating library call.  No counterpart in the
+ * reference; it exists for callers that cannot allocate device memory once
+ * they run — real-time control loops and runtimes that reserve all memory up
+ * front, where an allocation may synchronise the device or block.
+ *
+ * The caller owns every input and output (`io`, device pointers on `device`)
+ * and the stream (NULL = the default stream).  The iteration's scratch — the
+ * per-block MPPI tuples, per-vehicle arrival counters and best scores — is a
+ * 1 MiB array in device memory that every GPU loading this library keeps
+ * until the process exits.  Limits: batch <= 1024 vehicles and
+ * batch * ceil(samples / 64) * (4 + 4 * horizon, rounded up to 4) * 4 bytes
+ * <= 1,040,384 bytes; larger requests fail with LWM_INVALID_ARGUMENT and do
+ * no GPU work.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the one array and each call clears its counters
+ * first, so two calls whose work overlaps on the GPU (different streams, or
+ * different threads) race on it: serialise them.  Results equal
+ * lwm_plan_device's for an MPPI planner with the nominal scorer given the
+ * same mean, std, noise and context. */
+lwm_status lwm_nominal_mppi_noalloc(int device, void* stream, const lwm_nominal_scorer_config* cfg,
+                                    uint32_t batch, uint32_t samples, uint32_t horizon,
+                                    const float* bounds_low, const float* bounds_high, float temperature,
+                                    uint64_t seed, uint64_t offset, const lwm_nominal_mppi_io* io);
+
 /* ---------------------------------------------------------------- task inputs */
 
 /* skyjepa_reference_horizon (src/skyjepa_task.rs:44-55): kind 0 hover,

@@ -104,6 +104,11 @@ uint64_t round_even(uint64_t n) { return (n % 2 == 0) ? n : n + 1; }
 
 }  // namespace
 
+namespace lwm {
+// Records the thread's last error for entry points defined in other files.
+lwm_status set_last_error(lwm_status status, const std::string& message) { return fail(status, message); }
+}  // namespace lwm
+
 struct lwm_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
