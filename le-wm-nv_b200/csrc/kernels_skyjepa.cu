@@ -75,6 +75,9 @@ struct Geom {
     static_assert(32 / R == kCluster, "one destination CTA per lane in the store");
 };
 
+// Odd row strides put consecutive rows in different shared-memory banks.
+__host__ __device__ inline uint32_t odd_stride(uint32_t n) { return n | 1u; }
+
 __host__ __device__ inline uint32_t pow2_at_least(uint32_t v) {
     uint32_t p = 1;
     while (p < v) p <<= 1;
@@ -83,7 +86,7 @@ __host__ __device__ inline uint32_t pow2_at_least(uint32_t v) {
 
 struct SkySmem {
     // Offsets in floats inside the dynamic shared-memory block.
-    uint32_t hA, hB, emb, cand, w1, wih, pw2, pw3, pb, red1, a1, a2, pout, x, score, w, h0v, aw, sw, total;
+    uint32_t hA, hB, emb, cand, w1, wih, gb, pw2, pw3, pb, red1, a1, a2, pout, x, score, w, h0v, aw, sw, total;
     uint32_t w1_stride, pw_stride, sw_half;
 };
 
@@ -115,12 +118,12 @@ __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, ui
     const uint32_t action_scratch = (kThreads / Ca) * 3 * Ca * Hs;
     // the state-TCN weight slices (largest: conv2 + residual of level 0, or
     // the projection) stream through two halves overlaid on hB
-    uint32_t wmax = (H / kCluster) * Cl;
+    uint32_t wmax = (H / kCluster) * (Cl + 4);
     {
         uint32_t cin = Cs0;
         for (uint32_t l = 0; l < 8 && l < levels; ++l) {
-            const uint32_t w1n = per * cin * Ks;
-            const uint32_t w2n = per * Cs * Ks + (cin != Cs ? per * cin : 0);
+            const uint32_t w1n = per * odd_stride(cin * Ks);
+            const uint32_t w2n = per * odd_stride(Cs * Ks) + (cin != Cs ? per * cin : 0);
             wmax = w1n > wmax ? w1n : wmax;
             wmax = w2n > wmax ? w2n : wmax;
             cin = Cs;
@@ -138,6 +141,7 @@ __host__ __device__ inline SkySmem sky_smem_layout(uint32_t H, uint32_t rows, ui
     s.w1_stride = H + 4;
     s.w1 = take(hid * s.w1_stride);
     s.wih = take(3 * (H / kCluster) * E);
+    s.gb = take(2 * 3 * (H / kCluster));
     s.pw_stride = hid + 1;
     s.pw2 = take((layers > 1 ? layers - 1 : 1) * hid * s.pw_stride);
     s.pw3 = take(15 * s.pw_stride);
@@ -159,6 +163,47 @@ __host__ __device__ inline SkySmem layout_for(const SkyjepaArgs& a, uint32_t row
     return sky_smem_layout(a.H, rows, a.T, a.E, a.A, a.hid, a.prober_layers, a.state_tcn.max_ch,
                            pow2_at_least(a.action_tcn.max_ch), a.Hs, tcn_weight_floats(a.action_tcn), a.state_tcn.k,
                            a.state_tcn.out_dim, a.state_tcn.input_dim, a.state_tcn.levels);
+}
+
+// acc[t] += sum_j w[j] * x[t - (K-1-j)*DIL] for t < HS (taps before the
+// window start read the causal zero padding and are skipped).  HS == 0 is the
+// runtime-shape fallback.
+template <int HS, int K, int DIL>
+__device__ __forceinline__ void conv_taps(float (&acc)[kMaxHist], const float* x, const float* w, uint32_t Hs,
+                                          uint32_t Kr, uint32_t dil) {
+    if constexpr (HS > 0) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            const float wv = w[j];
+            const int sh = (K - 1 - j) * DIL;
+#pragma unroll
+            for (int t = sh; t < HS; ++t) acc[t] = fmaf(wv, x[t - sh], acc[t]);
+        }
+    } else {
+        for (uint32_t j = 0; j < Kr; ++j) {
+            const float wv = w[j];
+            const int sh = static_cast<int>((Kr - 1 - j) * dil);
+#pragma unroll
+            for (int t = 0; t < kMaxHist; ++t)
+                if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, x[t - sh], acc[t]);
+        }
+    }
+}
+
+// Dispatch on the dilation (1, 2, 4, 8 specialised) for one input channel.
+template <int HS, int K>
+__device__ __forceinline__ void conv_channel(float (&acc)[kMaxHist], const float* x, const float* w, uint32_t Hs,
+                                             uint32_t Kr, uint32_t dil) {
+    if constexpr (HS > 0) {
+        switch (dil) {
+            case 1: conv_taps<HS, K, 1>(acc, x, w, Hs, Kr, dil); return;
+            case 2: conv_taps<HS, K, 2>(acc, x, w, Hs, Kr, dil); return;
+            case 4: conv_taps<HS, K, 4>(acc, x, w, Hs, Kr, dil); return;
+            case 8: conv_taps<HS, K, 8>(acc, x, w, Hs, Kr, dil); return;
+            default: break;
+        }
+    }
+    conv_taps<0, 0, 0>(acc, x, w, Hs, Kr, dil);
 }
 
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
@@ -183,6 +228,7 @@ __device__ __forceinline__ void async_wait_all_but_one() { asm volatile("cp.asyn
 // every convolution: thread (o, slice) sums its slice of input channels for
 // all time steps, the slices are reduced in shared memory, and the result is
 // broadcast to every CTA's activation buffer.
+template <int HS, int KT>
 __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
                                   float* scratch, float* h0v, float* sw, uint32_t sw_half) {
     const TcnView& tcn = a.state_tcn;
@@ -198,30 +244,33 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
     // Weight slices of the convolutions in order (conv1, conv2 + residual of
     // every level, then the projection) stream through two shared buffers.
     const uint32_t nstage = 2 * tcn.levels + 1;
+    // rows of `row_len` floats land `dst_stride` apart (odd strides: no bank conflicts)
+    auto copy_rows = [&](float* dst, const float* src, uint32_t rows_n, uint32_t row_len, uint32_t dst_stride) {
+        for (uint32_t q = tid; q < rows_n * row_len; q += kThreads) {
+            const uint32_t r = q / row_len, e = q - r * row_len;
+            const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + r * dst_stride + e));
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(src + q) : "memory");
+        }
+    };
     auto stage = [&](uint32_t n) {
         float* dst = sw + (n & 1) * sw_half;
-        if (n >= nstage) { asm volatile("cp.async.commit_group;" ::: "memory"); return; }
-        if (n == nstage - 1) {
-            async_copy(dst, a.proj_w + static_cast<size_t>(c * hper) * Cl, hper * Cl);
-            return;
-        }
-        const TcnBlockView& bk = tcn.blocks[n / 2];
-        const uint32_t cnt = min(per, bk.out > o0 ? bk.out - o0 : 0u);
-        if (n % 2 == 0) {
-            async_copy(dst, bk.w1 + static_cast<size_t>(o0) * bk.in * K, cnt * bk.in * K);
-        } else {
-            // conv2 slice, then the residual 1x1 slice right after it
-            for (uint32_t i = tid; i < cnt * bk.out * K; i += kThreads) {
-                const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + i));
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(bk.w2 + static_cast<size_t>(o0) * bk.out * K + i) : "memory");
-            }
-            if (bk.wr)
-                for (uint32_t i = tid; i < cnt * bk.in; i += kThreads) {
-                    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + per * C * K + i));
-                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(d), "l"(bk.wr + static_cast<size_t>(o0) * bk.in + i) : "memory");
+        if (n < nstage) {
+            if (n == nstage - 1) {
+                copy_rows(dst, a.proj_w + static_cast<size_t>(c * hper) * Cl, hper, Cl, Cl + 4);
+            } else {
+                const TcnBlockView& bk = tcn.blocks[n / 2];
+                const uint32_t cnt = min(per, bk.out > o0 ? bk.out - o0 : 0u);
+                if (n % 2 == 0) {
+                    copy_rows(dst, bk.w1 + static_cast<size_t>(o0) * bk.in * K, cnt, bk.in * K, odd_stride(bk.in * K));
+                } else {
+                    // conv2 slice, then the residual 1x1 slice after it
+                    copy_rows(dst, bk.w2 + static_cast<size_t>(o0) * bk.out * K, cnt, bk.out * K, odd_stride(bk.out * K));
+                    if (bk.wr)
+                        copy_rows(dst + per * odd_stride(bk.out * K), bk.wr + static_cast<size_t>(o0) * bk.in, cnt, bk.in, bk.in);
                 }
-            asm volatile("cp.async.commit_group;" ::: "memory");
+            }
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
     __syncthreads();  // the weight buffers overlay the action-TCN scratch
     stage(0);
@@ -244,20 +293,13 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
             const float* Ws = sw + (n & 1) * sw_half;
             const float* src = conv == 0 ? cur : hb;
             const uint32_t cin = conv == 0 ? bk.in : bk.out;
+            const uint32_t wstride = odd_stride(cin * K);
             if (slice < KS && o < bk.out) {
                 float acc[kMaxHist];
 #pragma unroll
                 for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
-                for (uint32_t i = slice; i < cin; i += KS) {
-                    const float* xr = src + i * Hs;
-                    for (uint32_t j = 0; j < K; ++j) {
-                        const float wv = Ws[(o_local * cin + i) * K + j];
-                        const int sh = static_cast<int>((K - 1 - j) * bk.dil);
-#pragma unroll
-                        for (int t = 0; t < kMaxHist; ++t)
-                            if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, xr[t - sh], acc[t]);
-                    }
-                }
+                for (uint32_t i = slice; i < cin; i += KS)
+                    conv_channel<HS, KT>(acc, src + i * Hs, Ws + o_local * wstride + i * K, Hs, K, bk.dil);
 #pragma unroll
                 for (int t = 0; t < kMaxHist; ++t)
                     if (t < static_cast<int>(Hs)) red[(slice * per + o_local) * Hs + t] = acc[t];
@@ -275,7 +317,7 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
                     const float h2 = gelu_tanh(s + __ldg(bk.b2 + oo));
                     float res;
                     if (bk.wr) {
-                        const float* wrs = Ws + per * C * K + ol * bk.in;
+                        const float* wrs = Ws + per * odd_stride(bk.out * K) + ol * bk.in;
                         float r0 = 0.0f, r1 = 0.0f;
                         uint32_t i = 0;
                         for (; i + 2 <= bk.in; i += 2) {
@@ -305,7 +347,7 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
     for (uint32_t q = tid; q < hper * 4; q += kThreads) {
         const uint32_t ol = q / 4, part = q % 4, oo = c * hper + ol;
         float s = 0.0f;
-        for (uint32_t i = part; i < Cl; i += 4) s = fmaf(cur[i * Hs + Hs - 1], Wp[ol * Cl + i], s);
+        for (uint32_t i = part; i < Cl; i += 4) s = fmaf(cur[i * Hs + Hs - 1], Wp[ol * (Cl + 4) + i], s);
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         if (part == 0) {
@@ -321,6 +363,7 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
 // [history(Hs-1) ++ candidates][t0 .. t0+Hs), each window zero-padded on its
 // own.  `ca` lanes of one warp own a window, one output channel each, all
 // time steps in registers; warp-level syncs between convolutions.
+template <int HS, int KT>
 __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
                                    uint32_t rpc, const float* s_cand, float* scratch, float* s_emb, const float* aw) {
     const TcnView& tcn = a.action_tcn;
@@ -358,16 +401,9 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
                 float acc[kMaxHist];
 #pragma unroll
                 for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
-                if (mine) {
+                if (mine)
                     for (uint32_t i = 0; i < cin; ++i)
-                        for (uint32_t j = 0; j < tcn.k; ++j) {
-                            const float wv = W[(o * cin + i) * tcn.k + j];
-                            const int sh = static_cast<int>((tcn.k - 1 - j) * bk.dil);
-#pragma unroll
-                            for (int t = 0; t < kMaxHist; ++t)
-                                if (t < static_cast<int>(Hs) && t >= sh) acc[t] = fmaf(wv, src[i * Hs + t - sh], acc[t]);
-                        }
-                }
+                        conv_channel<HS, KT>(acc, src + i * Hs, W + (o * cin + i) * tcn.k, Hs, tcn.k, bk.dil);
                 const float bias = mine ? sm(conv == 0 ? bk.b1 : bk.b2)[o] : 0.0f;
                 if (conv == 0) {
                     if (mine)
@@ -621,6 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
         const uint32_t g = q / (G::U * E), rem = q % (G::U * E), u = rem / E, e = rem % E;
         s_wih[q] = __ldg(a.w_ih + (static_cast<size_t>(g) * H + c * G::U + u) * E + e);
     }
+    for (uint32_t q = tid; q < 3 * G::U; q += kThreads) {
+        const uint32_t g = q / G::U, u = q % G::U;
+        smem[L.gb + q] = __ldg(a.b_ih + g * H + c * G::U + u);           // b_ih [3][U]
+        smem[L.gb + 3 * G::U + q] = __ldg(a.b_hh + g * H + c * G::U + u);  // b_hh [3][U]
+    }
     for (uint32_t l = 0; l + 1 < a.prober_layers; ++l)
         for (uint32_t q = tid; q < hid * hid; q += kThreads)
             smem[L.pw2 + l * hid * L.pw_stride + (q / hid) * L.pw_stride + q % hid] = __ldg(a.p_hid_w[l] + q);
@@ -665,8 +706,10 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     cluster.sync();
 
     // ---- window embeddings of the own rows -> every CTA; h0 -> every CTA
-    action_tcn_windows(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb, smem + L.aw);
-    state_tcn_cluster(a, cluster, c, b, smem + L.hA, s_h0, smem + L.sw, L.sw_half);
+    if (Hs == 10 && a.action_tcn.k == 3) action_tcn_windows<10, 3>(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb, smem + L.aw);
+    else action_tcn_windows<0, 0>(a, cluster, c, b, rpc, s_cand, smem + L.hB, s_emb, smem + L.aw);
+    if (Hs == 10 && a.state_tcn.k == 3) state_tcn_cluster<10, 3>(a, cluster, c, b, smem + L.hA, s_h0, smem + L.sw, L.sw_half);
+    else state_tcn_cluster<0, 0>(a, cluster, c, b, smem + L.hA, s_h0, smem + L.sw, L.sw_half);
     cluster.sync();  // embeddings of all rows and h0 are complete everywhere
     {
         const float4* src = reinterpret_cast<const float4*>(s_h0);
@@ -707,38 +750,34 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
         const uint32_t my_q = combo / G::R, my_r = combo % G::R;
         const uint32_t my_local = pair * 2 + my_q;
         const uint32_t my_unit = c * G::U + my_local;
-        float bih[3], bhh[3];
-#pragma unroll
-        for (int g = 0; g < 3; ++g) {
-            bih[g] = __ldg(a.b_ih + g * H + my_unit);
-            bhh[g] = __ldg(a.b_hh + g * H + my_unit);
-        }
+        const float* s_bih = smem + L.gb + my_local;             // stride U per gate
+        const float* s_bhh = smem + L.gb + 3 * G::U + my_local;
         for (uint32_t t = 0; t < T; ++t) {
             const float* hc = smem + ((t & 1) ? L.hB : L.hA);
             float* hn = smem + ((t & 1) ? L.hA : L.hB);
 #pragma unroll 1
             for (uint32_t grp = 0; grp < groups; ++grp) {
+                // one group = 4 rows x this thread's 2 units x 3 gates
                 float acc[2 * G::R][3];
 #pragma unroll
                 for (int q = 0; q < 2 * G::R; ++q) { acc[q][0] = 0.0f; acc[q][1] = 0.0f; acc[q][2] = 0.0f; }
 #pragma unroll
-                for (int r = 0; r < G::R; ++r) {
-                    const float* hrow = hc + (grp * G::R + r) * H + kg * 4;
+                for (int i = 0; i < G::KQ; ++i) {
+                    float4 hv[G::R];
 #pragma unroll
-                    for (int i = 0; i < G::KQ; ++i) {
-                        const float4 hv = *reinterpret_cast<const float4*>(hrow + 4 * G::KG * i);
+                    for (int r = 0; r < G::R; ++r)
+                        hv[r] = *reinterpret_cast<const float4*>(hc + (grp * G::R + r) * H + kg * 4 + 4 * G::KG * i);
 #pragma unroll
-                        for (int q = 0; q < 2; ++q)
+                    for (int comp = 0; comp < 4; ++comp)
 #pragma unroll
-                            for (int g = 0; g < 3; ++g) {
-                                float s = acc[q * G::R + r][g];
-                                s = fmaf(wr[q][g][4 * i + 0], hv.x, s);
-                                s = fmaf(wr[q][g][4 * i + 1], hv.y, s);
-                                s = fmaf(wr[q][g][4 * i + 2], hv.z, s);
-                                s = fmaf(wr[q][g][4 * i + 3], hv.w, s);
-                                acc[q * G::R + r][g] = s;
-                            }
-                    }
+                        for (int r = 0; r < G::R; ++r) {
+                            const float hcomp = comp == 0 ? hv[r].x : comp == 1 ? hv[r].y : comp == 2 ? hv[r].z : hv[r].w;
+#pragma unroll
+                            for (int q = 0; q < 2; ++q)
+#pragma unroll
+                                for (int g = 0; g < 3; ++g)
+                                    acc[q * G::R + r][g] = fmaf(wr[q][g][4 * i + comp], hcomp, acc[q * G::R + r][g]);
+                        }
                 }
                 // reduce-scatter over the low 3 lane bits (lane kg ends with
                 // combo kg & 7), then all-reduce over the remaining k-group bits
@@ -766,10 +805,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
                 for (int g = 0; g < 3; ++g) {
                     const float* wi = s_wih + (g * G::U + my_local) * E;
                     float s = 0.0f;
-                    for (uint32_t e = 0; e < E; ++e) s = fmaf(xe[e], wi[e], s);
-                    gi[g] = s + bih[g];
+#pragma unroll
+                    for (int e = 0; e < kMaxTcnCh; ++e)
+                        if (static_cast<uint32_t>(e) < E) s = fmaf(xe[e], wi[e], s);
+                    gi[g] = s + s_bih[g * G::U];
                 }
-                const float ghr = acc[0][0] + bhh[0], ghz = acc[0][1] + bhh[1], ghn = acc[0][2] + bhh[2];
+                const float ghr = acc[0][0] + s_bhh[0], ghz = acc[0][1] + s_bhh[G::U], ghn = acc[0][2] + s_bhh[2 * G::U];
                 const float rg = sigmoid(gi[0] + ghr);
                 const float zg = sigmoid(gi[1] + ghz);
                 const float ng = tanhf(gi[2] + rg * ghn);

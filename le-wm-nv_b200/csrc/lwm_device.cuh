@@ -56,7 +56,8 @@ __device__ __forceinline__ float gelu_tanh(float v) {
                                             1.0f + __fmul_rn(__fmul_rn(0.044715f, v), v))));
 }
 
-__device__ __forceinline__ float sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
+// 1 / (1 + exp(-v)); the correctly rounded reciprocal equals IEEE 1/x exactly.
+__device__ __forceinline__ float sigmoid(float v) { return __frcp_rn(1.0f + expf(-v)); }
 
 // Orderable key of a score: NaN ranks as +inf, -0 as +0; ascending keys give
 // ascending scores.  Low word = sample index, so ties resolve to the lower
