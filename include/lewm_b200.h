@@ -389,6 +389,51 @@ lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, 
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count,
                              float* out);
 
+/* ---------------------------------------------------------------- image preprocessing */
+
+/* PackedImageFormat (src/media/mod.rs:59-83) and Nv12ColorSpace (:131-148). */
+typedef enum lwm_packed_format {
+    LWM_PACKED_RGB = 0,
+    LWM_PACKED_BGR = 1,
+    LWM_PACKED_RGBA = 2,
+    LWM_PACKED_BGRA = 3,
+} lwm_packed_format;
+typedef enum lwm_nv12_color_space {
+    LWM_NV12_BT601_VIDEO = 0,
+    LWM_NV12_BT709_VIDEO = 1,
+    LWM_NV12_BT601_FULL = 2,
+    LWM_NV12_BT709_FULL = 3,
+} lwm_nv12_color_space;
+
+/* ImagePreprocess (src/media/mod.rs:168-193). */
+typedef struct lwm_image_preprocess {
+    uint32_t output_height;
+    uint32_t output_width;
+    float mean[3];
+    float std[3];
+} lwm_image_preprocess;
+/* ImagePreprocess::imagenet_224 (src/media/mod.rs:175-183). */
+void lwm_image_preprocess_imagenet_224(lwm_image_preprocess* out);
+
+/* ImagePreprocessor::preprocess_packed_u8 and
+ * ImageHistoryPreprocessor::preprocess_packed_u8_into_slot
+ * (src/media/mod.rs:275-343, 470-543; kernel :1113-1194).  `input` is a
+ * device [B,H,W,C] u8 frame batch (C = 3 or 4 by `format`); `output` is a
+ * device [B,3,oh,ow] buffer (history_len == 0) or [B,history_len,3,oh,ow]
+ * with slot `history_slot` written; out_bf16 selects bf16 instead of f32. */
+lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint32_t batch, uint32_t height,
+                                        uint32_t width, int32_t format, const lwm_image_preprocess* cfg,
+                                        uint32_t history_len, uint32_t history_slot, int32_t out_bf16,
+                                        void* output);
+/* Nv12Preprocessor::preprocess_nv12 and Nv12HistoryPreprocessor::
+ * preprocess_nv12_into_slot (src/media/mod.rs:196-273, 345-468; kernel
+ * :1196-1333).  Device Y plane [B,H,W] and interleaved UV plane
+ * [B,H/2,W/2,2]; H and W must be even. */
+lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane,
+                                      uint32_t batch, uint32_t height, uint32_t width, int32_t color_space,
+                                      const lwm_image_preprocess* cfg, uint32_t history_len,
+                                      uint32_t history_slot, int32_t out_bf16, void* output);
+
 /* ---------------------------------------------------------------- allocation-free iteration */
 
 /* Device buffers of lwm_nominal_mppi_noalloc, all owned by the caller. */

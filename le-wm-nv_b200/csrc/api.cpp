@@ -1256,6 +1256,82 @@ lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, 
     return LWM_OK;
 }
 
+void lwm_image_preprocess_imagenet_224(lwm_image_preprocess* out) {
+    out->output_height = 224;
+    out->output_width = 224;
+    out->mean[0] = 0.485f; out->mean[1] = 0.456f; out->mean[2] = 0.406f;
+    out->std[0] = 0.229f; out->std[1] = 0.224f; out->std[2] = 0.225f;
+}
+
+// ImagePreprocess::validate (src/media/mod.rs:185-193) and the history-slot check.
+static lwm_status validate_preprocess(const lwm_image_preprocess* cfg, uint32_t history_len, uint32_t slot,
+                                      const char* kind) {
+    if (cfg->output_height == 0 || cfg->output_width == 0)
+        return fail(LWM_INVALID_ARGUMENT, "CUDA preprocess output dimensions must be greater than zero");
+    for (int i = 0; i < 3; ++i)
+        if (cfg->std[i] == 0.0f) return fail(LWM_INVALID_ARGUMENT, "CUDA preprocess std values must be non-zero");
+    if (history_len > 0 && slot >= history_len)
+        return fail(LWM_INVALID_ARGUMENT, std::string("CUDA ") + kind + " history slot " + std::to_string(slot) +
+                                              " is outside history_len " + std::to_string(history_len));
+    return LWM_OK;
+}
+
+static lwm::MediaArgs media_args(const lwm_image_preprocess* cfg, uint32_t B, uint32_t H, uint32_t W,
+                                 uint32_t history_len, uint32_t slot, int32_t bf16, void* out) {
+    lwm::MediaArgs a{};
+    a.out = out;
+    a.batch = B; a.in_h = H; a.in_w = W;
+    a.out_h = cfg->output_height; a.out_w = cfg->output_width;
+    a.history_len = history_len; a.history_slot = slot;
+    a.bf16 = bf16 ? 1 : 0;
+    for (int i = 0; i < 3; ++i) { a.mean[i] = cfg->mean[i]; a.std[i] = cfg->std[i]; }
+    return a;
+}
+
+lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uint32_t H, uint32_t W,
+                                        int32_t format, const lwm_image_preprocess* cfg, uint32_t history_len,
+                                        uint32_t slot, int32_t out_bf16, void* output) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (format < 0 || format > 3)
+        return fail(LWM_INVALID_ARGUMENT, "unknown packed image format " + std::to_string(format) +
+                                              "; expected 0=RGB, 1=BGR, 2=RGBA, or 3=BGRA");
+    if (B == 0 || H == 0 || W == 0) return fail(LWM_INVALID_ARGUMENT, "packed CUDA image dimensions must be greater than zero");
+    LWM_TRY(validate_preprocess(cfg, history_len, slot, "image"));
+    if (!ctx || !input || !output) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    lwm::MediaArgs a = media_args(cfg, B, H, W, history_len, slot, out_bf16, output);
+    a.a = input;
+    a.channels = format >= 2 ? 4 : 3;
+    a.format = static_cast<uint32_t>(format);
+    LWM_CUDA(lwm::launch_media(a, false, ctx->stream));
+    ctx->launches += 1;
+    return LWM_OK;
+}
+
+lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B,
+                                      uint32_t H, uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg,
+                                      uint32_t history_len, uint32_t slot, int32_t out_bf16, void* output) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (color_space < 0 || color_space > 3)
+        return fail(LWM_INVALID_ARGUMENT, "unknown NV12 color space " + std::to_string(color_space) +
+                                              "; expected 0=BT.601 video, 1=BT.709 video, 2=BT.601 full, or 3=BT.709 full");
+    if (B == 0 || H == 0 || W == 0) return fail(LWM_INVALID_ARGUMENT, "NV12 CUDA image dimensions must be greater than zero");
+    if (H % 2 != 0 || W % 2 != 0)
+        return fail(LWM_INVALID_ARGUMENT, "NV12 CUDA image dimensions must be even, got " + std::to_string(H) + "x" +
+                                              std::to_string(W));
+    LWM_TRY(validate_preprocess(cfg, history_len, slot, "NV12"));
+    if (!ctx || !y_plane || !uv_plane || !output) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    lwm::MediaArgs a = media_args(cfg, B, H, W, history_len, slot, out_bf16, output);
+    a.a = y_plane;
+    a.uv = uv_plane;
+    a.channels = 1;
+    a.format = static_cast<uint32_t>(color_space);
+    LWM_CUDA(lwm::launch_media(a, true, ctx->stream));
+    ctx->launches += 1;
+    return LWM_OK;
+}
+
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count, float* out) {
     if (!ctx || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (count == 0) return LWM_OK;

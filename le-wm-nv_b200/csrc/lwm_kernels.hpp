@@ -144,6 +144,18 @@ cudaError_t launch_normal_fill(uint64_t seed, uint64_t offset, uint64_t count, f
 uint32_t nominal_blocks_per_vehicle(uint32_t S);
 cudaError_t launch_nominal(const NominalArgs& a, cudaStream_t stream);
 
+struct MediaArgs {
+    const uint8_t* a;   // packed pixels, or the Y plane
+    const uint8_t* uv;  // NV12 interleaved UV plane (nullptr for packed input)
+    void* out;
+    uint32_t batch, in_h, in_w, channels, out_h, out_w;
+    uint32_t format;    // packed: 0 RGB, 1 BGR, 2 RGBA, 3 BGRA; NV12: colour space 0..3
+    uint32_t history_len, history_slot;
+    int bf16;
+    float mean[3], std[3];
+};
+cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream);
+
 // Rows per cluster (one wave of co-resident clusters when possible) and MPPI
 // partials per vehicle of the fused SkyJEPA kernel.
 uint32_t skyjepa_rows_per_cluster(const SkyjepaArgs& a);

@@ -93,6 +93,22 @@ class Domain(C.Structure):
         return float(np.float32(self.mass) * np.float32(self.gravity) / (np.float32(4.0) * np.float32(self.thrust_scale)))
 
 
+class ImagePreprocess(C.Structure):
+    """ImagePreprocess (src/media/mod.rs:168-193)."""
+    _fields_ = [("output_height", C.c_uint32), ("output_width", C.c_uint32), ("mean", C.c_float * 3),
+                ("std", C.c_float * 3)]
+
+    @classmethod
+    def make(cls, output_height: int, output_width: int, mean=(0.0, 0.0, 0.0), std=(1.0, 1.0, 1.0)):
+        return cls(output_height, output_width, (C.c_float * 3)(*mean), (C.c_float * 3)(*std))
+
+    @classmethod
+    def imagenet_224(cls):
+        out = cls()
+        lib.lwm_image_preprocess_imagenet_224(C.byref(out))
+        return out
+
+
 class TrackingCost(C.Structure):
     """SkyJepaTrackingCost (src/models/skyjepa/control.rs:19-37)."""
     _fields_ = [("position", F), ("velocity", F), ("attitude", F), ("angular_velocity", F), ("action", F * 4)]
@@ -219,6 +235,11 @@ _sig("lwm_normal_device", C.c_int, VP, U64, U64, C.c_size_t, VP)
 _sig("lwm_skyjepa_reference_horizon", C.c_int, I32, F, F, U32, F, F, FP)
 _sig("lwm_skyjepa_geometric_prior", C.c_int, FP, FP, U32, F, C.POINTER(Domain), FP)
 _sig("lwm_rotor_plant_step", C.c_int, C.POINTER(Domain), FP, FP, FP, F)
+_sig("lwm_image_preprocess_imagenet_224", None, C.POINTER(ImagePreprocess))
+_sig("lwm_preprocess_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32, I32,
+     VP)
+_sig("lwm_preprocess_nv12_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32,
+     I32, VP)
 
 
 def _check(status: int) -> None:
@@ -718,6 +739,35 @@ def color_noise_device(ctx: Context, in_ptr: int, out_ptr: int, batch: int, samp
 
 def normal_device(ctx: Context, seed: int, offset: int, count: int, out_ptr: int) -> None:
     _check(lib.lwm_normal_device(ctx.handle, U64(seed), U64(offset), C.c_size_t(count), VP(out_ptr)))
+
+
+# ------------------------------------------------------------ image preprocessing
+
+PACKED_FORMATS = {"rgb": 0, "bgr": 1, "rgba": 2, "bgra": 3}
+NV12_COLOR_SPACES = {"bt601-video": 0, "bt709-video": 1, "bt601-full": 2, "bt709-full": 3}
+
+
+def _ptr(x) -> int:
+    return x.data_ptr() if hasattr(x, "data_ptr") else int(x)
+
+
+def preprocess_packed_device(ctx: Context, frames, batch: int, height: int, width: int, fmt, cfg: ImagePreprocess,
+                             out, history_len: int = 0, history_slot: int = 0, bf16: bool = False) -> None:
+    """Packed u8 [B,H,W,C] device frames -> normalized NCHW (or a history slot) on the context stream
+    (ImagePreprocessor / ImageHistoryPreprocessor, src/media/mod.rs:275-343, 470-543)."""
+    f = PACKED_FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    _check(lib.lwm_preprocess_packed_device(ctx.handle, VP(_ptr(frames)), batch, height, width, f, C.byref(cfg),
+                                            history_len, history_slot, int(bf16), VP(_ptr(out))))
+
+
+def preprocess_nv12_device(ctx: Context, y_plane, uv_plane, batch: int, height: int, width: int, color_space,
+                           cfg: ImagePreprocess, out, history_len: int = 0, history_slot: int = 0,
+                           bf16: bool = False) -> None:
+    """NV12 device planes -> normalized NCHW (or a history slot) on the context stream
+    (Nv12Preprocessor / Nv12HistoryPreprocessor, src/media/mod.rs:196-273, 345-468)."""
+    cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
+    _check(lib.lwm_preprocess_nv12_device(ctx.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), batch, height, width,
+                                          cs, C.byref(cfg), history_len, history_slot, int(bf16), VP(_ptr(out))))
 
 
 # ----------------------------------------------------------------- task inputs

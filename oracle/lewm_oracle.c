@@ -1309,3 +1309,99 @@ void orc_geometric_prior(const float* cur, const float* refs, uint32_t T, float 
         }
     }
 }
+
+/* ------------------------------------------------------------------ image preprocessing */
+
+static float orc_clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+
+/* swm_sample_plane (src/media/mod.rs:1201-1230): clamped bilinear tap. */
+static float orc_sample_plane(const uint8_t* plane, size_t b, uint32_t h, uint32_t w, uint32_t channels,
+                              uint32_t channel, float sy, float sx) {
+    sy = orc_clampf(sy, 0.0f, (float)(h - 1u));
+    sx = orc_clampf(sx, 0.0f, (float)(w - 1u));
+    uint32_t y0 = (uint32_t)floorf(sy), x0 = (uint32_t)floorf(sx);
+    uint32_t y1 = y0 + 1u < h ? y0 + 1u : y0, x1 = x0 + 1u < w ? x0 + 1u : x0;
+    float wy = sy - (float)y0, wx = sx - (float)x0;
+    float v00 = (float)plane[((b * h + y0) * w + x0) * channels + channel];
+    float v01 = (float)plane[((b * h + y0) * w + x1) * channels + channel];
+    float v10 = (float)plane[((b * h + y1) * w + x0) * channels + channel];
+    float v11 = (float)plane[((b * h + y1) * w + x1) * channels + channel];
+    float top = v00 + (v01 - v00) * wx;
+    float bottom = v10 + (v11 - v10) * wx;
+    return top + (bottom - top) * wy;
+}
+
+static size_t orc_media_index(size_t b, uint32_t c, uint32_t y, uint32_t x, uint32_t oh, uint32_t ow,
+                              uint32_t history_len, uint32_t slot) {
+    if (history_len == 0u) return ((b * 3u + c) * oh + y) * ow + x;
+    return (((b * history_len + slot) * 3u + c) * oh + y) * ow + x;
+}
+
+/* One output element (b, c, y, x) at a time, in the kernel's order
+ * (src/media/mod.rs:1134-1193). */
+void orc_preprocess_packed(const uint8_t* input, uint32_t B, uint32_t H, uint32_t W, uint32_t format,
+                           uint32_t oh, uint32_t ow, const float* mean, const float* stdv, uint32_t history_len,
+                           uint32_t slot, float* out) {
+    const uint32_t channels = format >= 2u ? 4u : 3u;
+    for (size_t b = 0; b < B; ++b)
+        for (uint32_t c = 0; c < 3u; ++c)
+            for (uint32_t y = 0; y < oh; ++y)
+                for (uint32_t x = 0; x < ow; ++x) {
+                    float sy = ((float)y + 0.5f) * ((float)H / (float)oh) - 0.5f;
+                    float sx = ((float)x + 0.5f) * ((float)W / (float)ow) - 0.5f;
+                    if (sy < 0.0f) sy = 0.0f;
+                    if (sx < 0.0f) sx = 0.0f;
+                    uint32_t y0 = (uint32_t)floorf(sy), x0 = (uint32_t)floorf(sx);
+                    uint32_t y1 = y0 + 1u < H ? y0 + 1u : y0, x1 = x0 + 1u < W ? x0 + 1u : x0;
+                    float wy = sy - (float)y0, wx = sx - (float)x0;
+                    uint32_t sc = (format == 1u || format == 3u) ? 2u - c : c;
+                    float v00 = (float)input[((b * H + y0) * W + x0) * channels + sc];
+                    float v01 = (float)input[((b * H + y0) * W + x1) * channels + sc];
+                    float v10 = (float)input[((b * H + y1) * W + x0) * channels + sc];
+                    float v11 = (float)input[((b * H + y1) * W + x1) * channels + sc];
+                    float top = v00 + (v01 - v00) * wx;
+                    float bottom = v10 + (v11 - v10) * wx;
+                    float value = (top + (bottom - top) * wy) * 0.00392156862745098f;
+                    out[orc_media_index(b, c, y, x, oh, ow, history_len, slot)] = (value - mean[c]) / stdv[c];
+                }
+}
+
+/* src/media/mod.rs:1232-1332; colour matrices :1298-1318. */
+void orc_preprocess_nv12(const uint8_t* yp, const uint8_t* uvp, uint32_t B, uint32_t H, uint32_t W,
+                         uint32_t cs, uint32_t oh, uint32_t ow, const float* mean, const float* stdv,
+                         uint32_t history_len, uint32_t slot, float* out) {
+    for (size_t b = 0; b < B; ++b)
+        for (uint32_t y = 0; y < oh; ++y)
+            for (uint32_t x = 0; x < ow; ++x) {
+                float sy = ((float)y + 0.5f) * ((float)H / (float)oh) - 0.5f;
+                float sx = ((float)x + 0.5f) * ((float)W / (float)ow) - 0.5f;
+                float yv = orc_sample_plane(yp, b, H, W, 1u, 0u, sy, sx);
+                float u = orc_sample_plane(uvp, b, H / 2u, W / 2u, 2u, 0u, sy * 0.5f, sx * 0.5f) - 128.0f;
+                float v = orc_sample_plane(uvp, b, H / 2u, W / 2u, 2u, 1u, sy * 0.5f, sx * 0.5f) - 128.0f;
+                float r, g, bl;
+                if (cs == 0u) {
+                    float yy = fmaxf(yv - 16.0f, 0.0f) * 1.16438356f;
+                    r = yy + 1.59602678f * v;
+                    g = yy - 0.39176229f * u - 0.81296765f * v;
+                    bl = yy + 2.01723214f * u;
+                } else if (cs == 1u) {
+                    float yy = fmaxf(yv - 16.0f, 0.0f) * 1.16438356f;
+                    r = yy + 1.79274107f * v;
+                    g = yy - 0.21324861f * u - 0.53290933f * v;
+                    bl = yy + 2.11240179f * u;
+                } else if (cs == 2u) {
+                    r = yv + 1.402f * v;
+                    g = yv - 0.344136f * u - 0.714136f * v;
+                    bl = yv + 1.772f * u;
+                } else {
+                    r = yv + 1.5748f * v;
+                    g = yv - 0.187324f * u - 0.468124f * v;
+                    bl = yv + 1.8556f * u;
+                }
+                const float vals[3] = {orc_clampf(r, 0.0f, 255.0f) * 0.00392156862745098f,
+                                       orc_clampf(g, 0.0f, 255.0f) * 0.00392156862745098f,
+                                       orc_clampf(bl, 0.0f, 255.0f) * 0.00392156862745098f};
+                for (uint32_t c = 0; c < 3u; ++c)
+                    out[orc_media_index(b, c, y, x, oh, ow, history_len, slot)] = (vals[c] - mean[c]) / stdv[c];
+            }
+}

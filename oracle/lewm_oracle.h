@@ -160,6 +160,19 @@ void orc_reference_state(int kind, float time, float radius, float period, float
 void orc_geometric_prior(const float* current, const float* refs, uint32_t T, float dt,
                          const lwm_domain* d, float* out);
 
+/* ---- image preprocessing (src/media/mod.rs) ---- */
+/* swm_packed_u8_to_nchw_f32 (src/media/mod.rs:1113-1194): format 0 RGB,
+ * 1 BGR, 2 RGBA, 3 BGRA; history_len 0 writes [B,3,oh,ow], otherwise slot
+ * `history_slot` of [B,history_len,3,oh,ow]. */
+void orc_preprocess_packed(const uint8_t* input, uint32_t B, uint32_t H, uint32_t W, uint32_t format,
+                           uint32_t out_h, uint32_t out_w, const float* mean3, const float* std3,
+                           uint32_t history_len, uint32_t history_slot, float* out);
+/* swm_nv12_to_nchw_f32 (src/media/mod.rs:1196-1333): colour space 0
+ * BT.601 video, 1 BT.709 video, 2 BT.601 full, 3 BT.709 full. */
+void orc_preprocess_nv12(const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B, uint32_t H, uint32_t W,
+                         uint32_t color_space, uint32_t out_h, uint32_t out_w, const float* mean3,
+                         const float* std3, uint32_t history_len, uint32_t history_slot, float* out);
+
 #ifdef __cplusplus
 }
 #endif

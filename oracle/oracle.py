@@ -91,6 +91,8 @@ _sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, 
 _sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_reference_state", None, C.c_int, F, F, F, FP)
 _sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
+_sig("orc_preprocess_packed", None, C.c_void_p, U32, U32, U32, U32, U32, U32, FP, FP, U32, U32, FP)
+_sig("orc_preprocess_nv12", None, C.c_void_p, C.c_void_p, U32, U32, U32, U32, U32, U32, FP, FP, U32, U32, FP)
 
 NOMINAL_FN = C.cast(lib.orc_nominal_score_fn, VP)
 SKYJEPA_FN = C.cast(lib.orc_skyjepa_score_fn, VP)
@@ -391,3 +393,34 @@ def geometric_prior(current, refs, dt, domain=None):
     lib.orc_geometric_prior(fp(f32(current)), fp(refs), refs.shape[0], F(dt), C.byref(domain or Domain.default()),
                             fp(out))
     return out
+
+
+def _media_out(B, oh, ow, history_len, out):
+    shape = (B, 3, oh, ow) if history_len == 0 else (B, history_len, 3, oh, ow)
+    if out is None:
+        return np.zeros(shape, np.float32)
+    assert out.shape == shape and out.dtype == np.float32 and out.flags.c_contiguous
+    return out
+
+
+def preprocess_packed(frames, fmt, out_h, out_w, mean=(0, 0, 0), std=(1, 1, 1), history_len=0, slot=0, out=None):
+    """frames: u8 [B,H,W,C]; returns f32 [B,3,oh,ow] or [B,history,3,oh,ow]."""
+    frames = np.ascontiguousarray(frames, np.uint8)
+    B, H, W, _ = frames.shape
+    res = _media_out(B, out_h, out_w, history_len, out)
+    lib.orc_preprocess_packed(frames.ctypes.data, B, H, W, fmt, out_h, out_w, fp(f32(mean)), fp(f32(std)),
+                              history_len, slot, fp(res))
+    return res
+
+
+def preprocess_nv12(y_plane, uv_plane, color_space, out_h, out_w, mean=(0, 0, 0), std=(1, 1, 1), history_len=0,
+                    slot=0, out=None):
+    """y_plane: u8 [B,H,W]; uv_plane: u8 [B,H/2,W/2,2]."""
+    y_plane = np.ascontiguousarray(y_plane, np.uint8)
+    uv_plane = np.ascontiguousarray(uv_plane, np.uint8)
+    B, H, W = y_plane.shape
+    assert uv_plane.shape == (B, H // 2, W // 2, 2)
+    res = _media_out(B, out_h, out_w, history_len, out)
+    lib.orc_preprocess_nv12(y_plane.ctypes.data, uv_plane.ctypes.data, B, H, W, color_space, out_h, out_w,
+                            fp(f32(mean)), fp(f32(std)), history_len, slot, fp(res))
+    return res

@@ -1,0 +1,115 @@
+"""Image preprocessing on the GPU through the C ABI against the oracle
+(swm_packed_u8_to_nchw_f32 / swm_nv12_to_nchw_f32, src/media/mod.rs:1113-1333).
+
+The kernels are built with -fmad=false and IEEE division, and the oracle with
+-ffp-contract=off, so f32 outputs are expected bit-identical; bf16 outputs are
+the oracle's f32 values rounded to nearest-even."""
+import zlib
+
+import numpy as np
+import pytest
+
+import lewm_b200 as L
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+IMAGENET = dict(mean=(0.485, 0.456, 0.406), std=(0.229, 0.224, 0.225))
+
+
+def _bf16_of(x: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+
+
+def _run_packed(ctx, frames, fmt, oh, ow, history_len=0, slot=0, bf16=False, **norm):
+    B, H, W, _ = frames.shape
+    cfg = L.ImagePreprocess.make(oh, ow, **norm) if norm else L.ImagePreprocess.make(oh, ow)
+    dev = torch.from_numpy(frames).cuda()
+    shape = (B, 3, oh, ow) if history_len == 0 else (B, history_len, 3, oh, ow)
+    out = torch.full(shape, 7.0, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
+    torch.cuda.synchronize()
+    L.preprocess_packed_device(ctx, dev, B, H, W, fmt, cfg, out, history_len, slot, bf16)
+    ctx.synchronize()
+    return out.float().cpu().numpy()
+
+
+def _run_nv12(ctx, y, uv, cs, oh, ow, history_len=0, slot=0, bf16=False, **norm):
+    B, H, W = y.shape
+    cfg = L.ImagePreprocess.make(oh, ow, **norm) if norm else L.ImagePreprocess.make(oh, ow)
+    shape = (B, 3, oh, ow) if history_len == 0 else (B, history_len, 3, oh, ow)
+    out = torch.full(shape, 7.0, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
+    torch.cuda.synchronize()
+    L.preprocess_nv12_device(ctx, torch.from_numpy(y).cuda(), torch.from_numpy(uv).cuda(), B, H, W, cs, cfg, out,
+                             history_len, slot, bf16)
+    ctx.synchronize()
+    return out.float().cpu().numpy()
+
+
+def test_reference_known_answers_on_gpu(ctx):
+    # the four tests of src/media/mod.rs:1336-1464, on the CUDA path
+    rgb = np.array([255, 0, 0, 0, 255, 0, 0, 0, 255, 255, 255, 255], np.uint8).reshape(1, 2, 2, 3)
+    got = _run_packed(ctx, rgb, "rgb", 2, 2).ravel()
+    assert np.abs(got - [1, 0, 0, 1, 0, 1, 0, 1, 0, 0, 1, 1]).max() <= 1e-6
+    bgr = np.array([0, 128, 255], np.uint8).reshape(1, 1, 1, 3)
+    got = _run_packed(ctx, bgr, "bgr", 1, 1, history_len=3, slot=1).ravel()
+    want = np.array([7, 7, 7, 1, 128 / 255, 0, 7, 7, 7])  # other slots untouched
+    assert np.abs(got - want).max() <= 1e-6
+    y0 = np.zeros((1, 2, 2), np.uint8)
+    uv = np.full((1, 1, 1, 2), 128, np.uint8)
+    assert np.abs(_run_nv12(ctx, y0, uv, "bt601-full", 2, 2)).max() <= 1e-6
+    y1 = np.full((1, 2, 2), 255, np.uint8)
+    got = _run_nv12(ctx, y1, uv, "bt709-full", 2, 2, history_len=2, slot=1).ravel()
+    assert np.abs(got[12:] - 1.0).max() <= 1e-6 and (got[:12] == 7.0).all()
+
+
+@pytest.mark.parametrize("fmt", ["rgb", "bgr", "rgba", "bgra"])
+@pytest.mark.parametrize("size", [(3, 480, 640, 224, 224), (2, 7, 5, 16, 12), (1, 1, 1, 3, 2), (2, 333, 517, 224, 224)])
+def test_packed_matches_oracle_bit_exact(ctx, fmt, size):
+    B, H, W, oh, ow = size
+    rng = np.random.default_rng(zlib.crc32(repr((fmt, size)).encode()))
+    frames = rng.integers(0, 256, (B, H, W, 4 if fmt.endswith("a") else 3), dtype=np.uint8)
+    got = _run_packed(ctx, frames, fmt, oh, ow, **IMAGENET)
+    ref = O.preprocess_packed(frames, L.PACKED_FORMATS[fmt], oh, ow, **IMAGENET)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("cs", ["bt601-video", "bt709-video", "bt601-full", "bt709-full"])
+@pytest.mark.parametrize("size", [(2, 720, 1280, 224, 224), (1, 4, 6, 9, 7), (3, 2, 2, 1, 1)])
+def test_nv12_matches_oracle_bit_exact(ctx, cs, size):
+    B, H, W, oh, ow = size
+    rng = np.random.default_rng(zlib.crc32(repr((cs, size)).encode()))
+    y = rng.integers(0, 256, (B, H, W), dtype=np.uint8)
+    uv = rng.integers(0, 256, (B, H // 2, W // 2, 2), dtype=np.uint8)
+    got = _run_nv12(ctx, y, uv, cs, oh, ow, **IMAGENET)
+    ref = O.preprocess_nv12(y, uv, L.NV12_COLOR_SPACES[cs], oh, ow, **IMAGENET)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_history_slots_fill_independently(ctx):
+    rng = np.random.default_rng(5)
+    B, H, W, hist = 2, 96, 128, 4
+    out_ref = np.zeros((B, hist, 3, 64, 64), np.float32)
+    cfg = L.ImagePreprocess.make(64, 64, **IMAGENET)
+    out = torch.zeros((B, hist, 3, 64, 64), device="cuda")
+    for slot in (2, 0, 3, 1):
+        frames = rng.integers(0, 256, (B, H, W, 3), dtype=np.uint8)
+        torch.cuda.synchronize()
+        L.preprocess_packed_device(ctx, torch.from_numpy(frames).cuda(), B, H, W, "rgb", cfg, out, hist, slot)
+        O.preprocess_packed(frames, 0, 64, 64, history_len=hist, slot=slot, out=out_ref, **IMAGENET)
+    ctx.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), out_ref)
+
+
+def test_bf16_output_is_rounded_oracle(ctx):
+    rng = np.random.default_rng(9)
+    frames = rng.integers(0, 256, (2, 300, 400, 3), dtype=np.uint8)
+    got = _run_packed(ctx, frames, "rgb", 224, 224, bf16=True, **IMAGENET)
+    ref = O.preprocess_packed(frames, 0, 224, 224, **IMAGENET)
+    np.testing.assert_array_equal(got, _bf16_of(ref))
+    y = rng.integers(0, 256, (2, 360, 640), dtype=np.uint8)
+    uv = rng.integers(0, 256, (2, 180, 320, 2), dtype=np.uint8)
+    got = _run_nv12(ctx, y, uv, "bt709-video", 224, 224, history_len=3, slot=2, bf16=True, **IMAGENET)
+    ref = O.preprocess_nv12(y, uv, 1, 224, 224, **IMAGENET)
+    np.testing.assert_array_equal(got[:, 2], _bf16_of(ref))
+    assert (got[:, :2] == 7.0).all()
