@@ -8,6 +8,7 @@ reference).  A "step" is one plan call.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload skyjepa|nominal]
     python bench.py --impl reference ...   # the CPU restatement on the host cores
+    python bench.py --workload fleet [--shard auto|vehicles|candidates] [--vehicles V --samples S --horizon T]
 
 `value` is timed with CUDA events around each plan on the device with the
 context resident (L2 flushed between steps); `e2e` times the public C-ABI
@@ -37,6 +38,7 @@ FLOP_PER_CANDIDATE_STEP = {
     "skyjepa": 2 * (4 * 768 + 256 * 768 + 2880 + 256 * 32 + 32 * 32 + 32 * 15) + 200,
     "nominal": 10 * 262 + 60,
 }
+FLOP_PER_CANDIDATE_STEP["fleet"] = FLOP_PER_CANDIDATE_STEP["skyjepa"]
 
 
 def percentile(values, q):
@@ -268,6 +270,160 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
+# ------------------------------------------------------------ fleet workload
+
+def run_fleet(args, rank, world, local_rank):
+    """Fleet-scale learned MPPI: V vehicles x S candidates x T steps with
+    per-vehicle physical parameters, split over the ranks by vehicles and/or
+    candidate ranges (lewm_b200.fleet); one step = one plan of the whole fleet."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import lewm_b200 as L
+    from lewm_b200 import fleet as F
+    from lewm_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    V, S, T = args.vehicles, args.samples, args.horizon
+    parts = F.partition(V, S, world, args.shard)
+    group = F.new_groups(parts) if world > 1 else None
+    part = parts[rank]
+    v0, v1 = part.vehicles
+    full = W.fleet(seed=23, vehicles=V, samples=S, horizon=T)
+    ctx = L.Context(local_rank)
+    stream = ctx.torch_stream()
+    sl = slice(v0, v1)
+    sc = L.SkyJepaScorer(ctx, full.model, full.weights, full.state_mean, full.state_std, full.action_mean,
+                         full.action_std, full.cost, full.dt)
+    hist, act, refs, ref_a, masses = (full.state_history[sl].copy(), full.action_history[sl].copy(),
+                                      full.reference_states[sl].copy(), full.reference_actions[sl].copy(),
+                                      full.masses[sl].copy())
+    set_ctx = lambda: sc.set_context(hist, act, refs, ref_a, vehicle_mass=masses)
+    set_ctx()
+    fp = F.FleetPlanner(ctx, part, sc, full.mppi, group)
+    fp.planner.set_warm_start_sequence(full.warm_start[sl])
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def one_plan():
+        return fp.plan_device()
+
+    for _ in range(args.warmup):
+        one_plan()
+    ctx.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = ctx.launch_count()
+    times = []
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.add_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            one_plan()
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = (ctx.launch_count() - n0) // args.steps
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    # end to end: host context in, host first actions out
+    e2e_times = []
+    for _ in range(args.steps):
+        ctx.synchronize()
+        t0 = time.perf_counter()
+        set_ctx()
+        r = one_plan()
+        with torch.cuda.stream(stream):  # the copy waits for the plan on the library's stream
+            first = L.device_tensor(r.first_action, (v1 - v0, 4)).cpu()
+        e2e_times.append((time.perf_counter() - t0) * 1e3)
+    h2d = hist.nbytes + act.nbytes + refs.nbytes + ref_a.nbytes + masses.nbytes
+    d2h = first.numel() * 4
+    stats = torch.tensor([max(times), sum(times), float(np.mean(e2e_times))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    _, total_ms, e2e_mean = stats.tolist()
+    result = None
+    if rank == 0:
+        cand_steps = V * S * T
+        ms = total_ms / args.steps
+        plans_per_s = 1e3 / ms
+        sgemm = sgemm_peak_tflops(torch)
+        achieved = FLOP_PER_CANDIDATE_STEP["fleet"] * cand_steps / (ms * 1e-3) / 1e12
+        result = {
+            "metric": f"fleet plan steps/s ({V} vehicles x {S} candidates x {T} steps per step); "
+                      "candidate-steps/s alongside",
+            "value": round(plans_per_s, 4),
+            "unit": "fleet plans/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, sampled vehicle masses/arms/motor constants)",
+            "config": {"workload": f"fleet SkyJEPA learned MPPI, {V} vehicles x {S} candidates x {T} steps, "
+                                   "latent 256, TCN [128,128,128]/[4,4,4], prober 32x2, per-vehicle mass",
+                       "parallelism": f"{part.vehicle_groups} vehicle groups x {part.candidate_shards} candidate "
+                                      f"shards ({args.shard})",
+                       "l2": "flushed between steps (256 MiB write outside the timed region)"},
+            "candidate_steps_per_s": round(plans_per_s * cand_steps, 1),
+            "latency_ms": {"p50": round(percentile(times, 0.5), 3), "p95": round(percentile(times, 0.95), 3)},
+            "e2e": {"value": round(1e3 / e2e_mean, 4), "unit": "fleet plans/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches * args.steps),
+            "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2),
+                         "unit": "TFLOP/s", "frac": round(achieved / (sgemm * world), 4), "traffic": None,
+                         "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run, x n_gpus"},
+            "clocks": clocks.summary(),
+        }
+        if args.cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_fleet(full, args.cpu_seconds)
+    fp.close()
+    sc.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return result
+
+
+def cpu_baseline_fleet(w, budget_s: float):
+    """The oracle on a bounded sample of the fleet: whole-vehicle plans (all S
+    candidates x T steps) one vehicle at a time until the budget is spent;
+    reported as candidate-steps/s and the fleet plans/s it implies."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import dataclasses
+    import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    m = O.SkyJepaModel(w.model, w.weights)
+    done, t_used = 0, 0.0
+    while t_used < budget_s and done < w.batch:
+        b = slice(done, done + 1)
+        c = m.score_ctx((w.state_mean, w.state_std, w.action_mean, w.action_std), w.state_history[b],
+                        w.action_history[b], w.reference_states[b], w.reference_actions[b], w.cost, w.dt,
+                        masses=w.masses[b])
+        t0 = time.perf_counter()
+        O.mppi_plan(dataclasses.replace(w.mppi), 1, (O.SKYJEPA_FN, c), seed=w.mppi.seed,
+                    warm_start=w.warm_start[b])
+        t_used += time.perf_counter() - t0
+        done += 1
+    per_vehicle = t_used / done
+    cand_steps = w.samples * w.horizon
+    return {"value": round(1.0 / (per_vehicle * w.batch), 6), "unit": "fleet plans/s", "cores": threads,
+            "kind": "port", "candidate_steps_per_s": round(cand_steps / per_vehicle, 1),
+            "sample": f"{done} whole-vehicle plans ({w.samples} x {w.horizon}) of the fleet, oracle C "
+                      f"restatement, {threads} OpenMP threads; fleet rate = vehicle rate / {w.batch}"}
+
+
 # ----------------------------------------------------------------- CPU arm
 
 def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
@@ -306,6 +462,21 @@ def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
+    if args.workload == "fleet":
+        from lewm_b200 import workloads as W
+        base = cpu_baseline_fleet(W.fleet(seed=23, vehicles=args.vehicles, samples=args.samples,
+                                          horizon=args.horizon), args.cpu_seconds)
+        return {"impl": "reference",
+                "metric": f"fleet plan steps/s ({args.vehicles} vehicles x {args.samples} candidates x "
+                          f"{args.horizon} steps per step); candidate-steps/s alongside",
+                "value": base["value"], "unit": "fleet plans/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init weights, sampled vehicle masses/arms/motor constants)",
+                "config": {"workload": "fleet SkyJEPA learned MPPI", "parallelism": "host CPU"},
+                "candidate_steps_per_s": base["candidate_steps_per_s"], "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "fleet plans/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     base = cpu_baseline(args.workload, args.cpu_seconds)
     # each timed step is one full plan on the host cores
     return {
@@ -338,7 +509,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["skyjepa", "nominal"], default="skyjepa")
+    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet"], default="skyjepa")
+    ap.add_argument("--shard", choices=["auto", "vehicles", "candidates"], default="auto")
+    ap.add_argument("--vehicles", type=int, default=256)
+    ap.add_argument("--samples", type=int, default=4096)
+    ap.add_argument("--horizon", type=int, default=30)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
@@ -348,6 +523,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         out = run_reference(args, rank, world)
+    elif args.workload == "fleet":
+        out = run_fleet(args, rank, world, local_rank)
     else:
         out = run_ours(args, rank, world, local_rank)
     if rank == 0 and out is not None:

@@ -290,6 +290,17 @@ lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* scorer, uint32_t batch, ui
                                           const float* action_history,
                                           const float* reference_states,
                                           const float* reference_actions);
+/* As lwm_scorer_skyjepa_set_context, plus an optional per-vehicle mass [B]
+ * (NULL: the model's kinematics.mass for every vehicle).  The mass enters
+ * the rotor-forces integrator (src/models/skyjepa/kinematics.rs:411-413);
+ * the reference needs one scorer per vehicle for a fleet whose vehicles
+ * differ in mass. */
+lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* scorer, uint32_t batch, uint32_t horizon,
+                                             const float* state_history,
+                                             const float* action_history,
+                                             const float* reference_states,
+                                             const float* reference_actions,
+                                             const float* vehicle_mass);
 
 /* A scorer supplied by the caller: the CandidateScorer trait
  * (src/planner.rs:25-32).  The callback receives device pointers on the
@@ -388,6 +399,27 @@ lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, 
  * `out`; the sampler the planners use. */
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count,
                              float* out);
+
+/* ---------------------------------------------------------------- candidate-range sharding */
+
+/* Multi-GPU MPPI over one vehicle batch: each GPU's planner owns samples
+ * [sample_base, sample_base + samples) of sample_total.  It draws the same
+ * Philox noise as an unsharded planner of sample_total samples and only the
+ * shard holding sample 0 carries the mean candidate.  lwm_plan_device_shard
+ * scores the shard and reduces it to one tuple per vehicle, [B][tuple_width]
+ * floats on the device: (min score, sum of weights, best (score, global index)
+ * key as 8 bytes, weighted action sums [T*A]).  The caller gathers the tuples
+ * of all shards ([shards][B][tuple_width], e.g. one NCCL all-gather) and
+ * lwm_mppi_combine_device rescales them to the global minimum and finishes
+ * the plan as mppi_weighted_sequence (src/planner.rs:1588-1602) would over
+ * all samples, warm start included.  MPPI with one iteration only.
+ * sample_total 0 makes the planner unsharded again.  No reference
+ * counterpart: the reference plans on one device. */
+lwm_status lwm_planner_set_shard(lwm_planner* planner, uint32_t sample_base, uint32_t sample_total);
+lwm_status lwm_plan_device_shard(lwm_planner* planner, lwm_scorer* scorer, const float* injected_noise,
+                                 const float** tuples, uint32_t* tuple_width);
+lwm_status lwm_mppi_combine_device(lwm_planner* planner, const float* tuples, uint32_t shards,
+                                   lwm_plan_device_result* out);
 
 /* ---------------------------------------------------------------- image preprocessing */
 

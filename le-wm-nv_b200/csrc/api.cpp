@@ -139,7 +139,8 @@ struct lwm_scorer {
     HostBuf ctx_host;
     cudaEvent_t staged = nullptr;
     size_t off_initial = 0, off_motors = 0, off_ref_states = 0, off_ref_actions = 0, off_domains = 0;
-    size_t off_state_hist = 0, off_action_hist = 0;
+    size_t off_state_hist = 0, off_action_hist = 0, off_masses = 0;
+    bool has_masses = false;
     // callback
     lwm_score_fn fn = nullptr;
     void* user = nullptr;
@@ -162,6 +163,9 @@ struct lwm_planner {
         best, best_score, carried, noise_tmp;
     HostBuf staging;
     uint32_t last_batch = 0, last_cols = 0;
+    // candidate-range shard (shard_total 0: unsharded) and its combined tuples
+    uint32_t shard_base = 0, shard_total = 0;
+    DevBuf shard_tuples;
     bool has_result = false;
 };
 
@@ -358,6 +362,7 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     }
     LWM_TRY(p->best.ensure(static_cast<size_t>(B) * 4));
     LWM_TRY(p->best_score.ensure(static_cast<size_t>(B) * 4));
+    LWM_TRY(p->shard_tuples.ensure(static_cast<size_t>(B) * pw * 4));
     const uint32_t keep = p->kind == PlannerKind::Icem ? std::max<uint32_t>(p->icem.keep_elites, 1) : 1;
     LWM_TRY(p->carried.ensure(static_cast<size_t>(B) * keep * p->T * p->A * 4));
     LWM_TRY(p->bounds.ensure(2 * LWM_MAX_ACTION_DIM * 4));
@@ -434,6 +439,7 @@ lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
     a.action_hist = reinterpret_cast<const float*>(base + sc->off_action_hist);
     a.ref_states = reinterpret_cast<const float*>(base + sc->off_ref_states);
     a.ref_actions = reinterpret_cast<const float*>(base + sc->off_ref_actions);
+    a.masses = sc->has_masses ? reinterpret_cast<const float*>(base + sc->off_masses) : nullptr;
     a.rows = lwm::skyjepa_rows_per_cluster(a);
     return a;
 }
@@ -548,7 +554,10 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                                               std::to_string(p->T) + ", " + std::to_string(p->A) + "] does not match expected [" +
                                               std::to_string(B) + ", " + std::to_string(p->T) + ", " + std::to_string(p->A) + "]");
     const size_t n = static_cast<size_t>(B) * p->S * p->T * p->A;
-    const uint64_t per_iter = round_even(n);
+    const bool sharded = p->shard_total != 0;
+    // a shard reserves the draws of the whole (unsharded) plan, so every
+    // shard's Philox indices line up with the single-GPU stream
+    const uint64_t per_iter = round_even(sharded ? static_cast<size_t>(B) * p->shard_total * p->T * p->A : n);
     const bool seeded = p->kind == PlannerKind::Mppi ? p->mppi.has_seed
                         : (p->kind == PlannerKind::Cem ? p->cem.has_seed : p->icem.has_seed);
     const uint64_t seed = seeded ? (p->kind == PlannerKind::Mppi ? p->mppi.seed : (p->kind == PlannerKind::Cem ? p->cem.seed : p->icem.seed))
@@ -579,6 +588,10 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
     uint32_t completed = 0;
     bool deadline_hit = false;
     MppiArgs m = mppi_args(p, p->kind == PlannerKind::Mppi ? p->mppi.temperature : 1.0f);
+    if (sharded) {
+        m.sample_base = p->shard_base;
+        m.shard_tuple = p->shard_tuples.as<float>();
+    }
     const uint32_t carried_keep = p->kind == PlannerKind::Icem ? p->icem.keep_elites : 0;
     for (uint32_t it = 0; it < p->iterations; ++it) {
         if (deadline_ns >= 0) {
@@ -602,6 +615,8 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 a.noise = noise;
                 a.seed = seed;
                 a.offset = it_offset;
+                a.sample_base = p->shard_base;
+                a.sample_total = p->shard_total;
                 a.cand_out = p->cand.as<float>();
                 a.scores = p->scores.as<float>();
                 a.mppi = 1;
@@ -618,6 +633,8 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 a.noise = noise;
                 a.seed = seed;
                 a.offset = it_offset;
+                a.sample_base = p->shard_base;
+                a.sample_total = p->shard_total;
                 a.cand_out = p->cand.as<float>();
                 a.scores = p->scores.as<float>();
                 a.mppi = 1;
@@ -638,6 +655,8 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
             s.noise = noise;
             s.seed = seed;
             s.offset = it_offset;
+            s.sample_base = p->shard_base;
+            s.sample_total = p->shard_total;
             s.smooth = 0.0f;
             if (p->kind == PlannerKind::Icem && p->icem.noise_beta != 0.0f) {
                 float smooth = p->icem.noise_beta / (p->icem.noise_beta + 1.0f);
@@ -687,6 +706,23 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
             }
         }
         ++completed;
+    }
+    if (sharded) {
+        // the outputs (and the warm start) come from lwm_mppi_combine_device
+        out->first_action = nullptr;
+        out->sequence = nullptr;
+        out->best_indices = nullptr;
+        out->scores = p->scores.as<float>();
+        out->batch = B;
+        out->scores_cols = p->S;
+        out->iterations_completed = completed;
+        out->deadline_reached = 0;
+        out->deadline_outcome = LWM_DEADLINE_NONE;
+        out->elapsed_ns = static_cast<uint64_t>(
+            std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count());
+        p->last_batch = B;
+        p->last_cols = p->S;
+        return LWM_OK;
     }
     if (p->kind != PlannerKind::Cem) {
         p->has_warm = true;
@@ -1096,9 +1132,19 @@ lwm_status lwm_scorer_skyjepa_create(lwm_ctx* ctx, const lwm_skyjepa_config* cfg
 
 lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* s, uint32_t B, uint32_t T, const float* state_hist,
                                           const float* action_hist, const float* ref_states, const float* ref_actions) {
+    return lwm_scorer_skyjepa_set_context_ex(s, B, T, state_hist, action_hist, ref_states, ref_actions, nullptr);
+}
+
+lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* s, uint32_t B, uint32_t T, const float* state_hist,
+                                             const float* action_hist, const float* ref_states,
+                                             const float* ref_actions, const float* masses) {
     if (!s || s->kind != ScorerKind::Skyjepa) return fail(LWM_INVALID_ARGUMENT, "not a SkyJEPA scorer");
     if (!state_hist || !action_hist || !ref_states || !ref_actions || B == 0 || T == 0)
         return fail(LWM_INVALID_ARGUMENT, "invalid SkyJEPA control shapes");
+    if (masses)
+        for (uint32_t b = 0; b < B; ++b)
+            if (!(masses[b] > 0.0f) || !std::isfinite(masses[b]))
+                return fail(LWM_INVALID_ARGUMENT, "vehicle mass " + std::to_string(b) + " must be finite and positive");
     lwm::SkyjepaArgs probe = s->sky_args;
     probe.T = T;
     const char* why = nullptr;
@@ -1111,8 +1157,10 @@ lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* s, uint32_t B, uint32_t T,
     s->off_action_hist = off; off = align256(off + static_cast<size_t>(B) * (Hs - 1) * 4 * 4);
     s->off_ref_states = off; off = align256(off + static_cast<size_t>(B) * T * 18 * 4);
     s->off_ref_actions = off; off = align256(off + static_cast<size_t>(B) * T * 4 * 4);
+    s->off_masses = off; off = align256(off + (masses ? static_cast<size_t>(B) * 4 : 0));
     LWM_TRY(stage_context(s, off));
     char* h = s->ctx_host.as<char>();
+    if (masses) std::memcpy(h + s->off_masses, masses, static_cast<size_t>(B) * 4);
     std::memcpy(h + s->off_state_hist, state_hist, static_cast<size_t>(B) * Hs * 18 * 4);
     std::memcpy(h + s->off_action_hist, action_hist, static_cast<size_t>(B) * (Hs - 1) * 4 * 4);
     std::memcpy(h + s->off_ref_states, ref_states, static_cast<size_t>(B) * T * 18 * 4);
@@ -1120,6 +1168,7 @@ lwm_status lwm_scorer_skyjepa_set_context(lwm_scorer* s, uint32_t B, uint32_t T,
     LWM_TRY(upload_context(s, off));
     s->batch = B;
     s->horizon = T;
+    s->has_masses = masses != nullptr;
     s->has_context = true;
     return LWM_OK;
 }
@@ -1172,15 +1221,77 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
 lwm_status lwm_plan_device(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
     if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    if (p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
     std::lock_guard<std::mutex> lock(p->mu);
     std::lock_guard<std::mutex> lock2(sc->mu);
     LWM_CUDA(cudaSetDevice(p->ctx->device));
     return plan_device_locked(p, sc, injected, out);
 }
 
+lwm_status lwm_planner_set_shard(lwm_planner* p, uint32_t sample_base, uint32_t sample_total) {
+    if (!p) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> lock(p->mu);
+    if (sample_total == 0) {
+        p->shard_base = 0;
+        p->shard_total = 0;
+        return LWM_OK;
+    }
+    if (p->kind != PlannerKind::Mppi || p->iterations != 1)
+        return fail(LWM_UNSUPPORTED, "candidate sharding supports MPPI planners with one iteration");
+    if (static_cast<uint64_t>(sample_base) + p->S > sample_total)
+        return fail(LWM_INVALID_ARGUMENT, "shard samples [" + std::to_string(sample_base) + ", " +
+                                              std::to_string(static_cast<uint64_t>(sample_base) + p->S) +
+                                              ") exceed sample_total " + std::to_string(sample_total));
+    p->shard_base = sample_base;
+    p->shard_total = sample_total;
+    return LWM_OK;
+}
+
+lwm_status lwm_plan_device_shard(lwm_planner* p, lwm_scorer* sc, const float* injected, const float** tuples,
+                                 uint32_t* tuple_width) {
+    if (!p || !sc || !tuples || !tuple_width) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    if (!p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is not a candidate shard (lwm_planner_set_shard)");
+    std::lock_guard<std::mutex> lock(p->mu);
+    std::lock_guard<std::mutex> lock2(sc->mu);
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    lwm_plan_device_result r{};
+    LWM_TRY(plan_device_locked(p, sc, injected, &r));
+    *tuples = p->shard_tuples.as<float>();
+    *tuple_width = mppi_args(p, p->mppi.temperature).pw;
+    return LWM_OK;
+}
+
+lwm_status lwm_mppi_combine_device(lwm_planner* p, const float* tuples, uint32_t shards, lwm_plan_device_result* out) {
+    if (!p || !tuples || !out || shards == 0) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (p->kind != PlannerKind::Mppi) return fail(LWM_UNSUPPORTED, "only MPPI tuples can be combined");
+    std::lock_guard<std::mutex> lock(p->mu);
+    const uint32_t B = p->last_batch;
+    if (B == 0) return fail(LWM_INVALID_ARGUMENT, "no shard plan to combine");
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    MppiArgs m = mppi_args(p, p->mppi.temperature);
+    LWM_CUDA(lwm::launch_mppi_combine(m, tuples, B, shards, p->ctx->stream));
+    p->ctx->launches += 1;
+    p->has_warm = true;
+    p->warm_batch = B;
+    out->first_action = p->first_action.as<float>();
+    out->sequence = p->sequence.as<float>();
+    out->scores = p->scores.as<float>();
+    out->best_indices = p->best.as<uint32_t>();
+    out->batch = B;
+    out->scores_cols = p->S;
+    out->iterations_completed = 1;
+    out->elapsed_ns = 0;
+    out->deadline_reached = 0;
+    out->deadline_outcome = LWM_DEADLINE_NONE;
+    p->has_result = true;
+    return LWM_OK;
+}
+
 lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_result* out) {
     if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    if (p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
     const auto start = std::chrono::steady_clock::now();
     std::lock_guard<std::mutex> lock(p->mu);
     std::lock_guard<std::mutex> lock2(sc->mu);

@@ -128,10 +128,11 @@ __global__ void __launch_bounds__(kNominalThreads) nominal_mppi_kernel(NominalAr
             if (a.sample) {
                 const uint32_t act = e & 3u;
                 const size_t mi = static_cast<size_t>(b) * TA + e;
-                if (s == 0) {
+                if (a.sample_base + s == 0) {
                     v = a.mean[mi];
                 } else {
-                    const float eps = a.noise ? a.noise[ci] : normal_at(a.seed, a.offset + ci);
+                    const uint64_t gi = global_row(b, s, a.sample_base, a.sample_total, a.S) * TA + e;
+                    const float eps = a.noise ? a.noise[ci] : normal_at(a.seed, a.offset + gi);
                     v = a.mean[mi] + eps * a.std[mi];
                 }
                 v = cmin(cmax(v, a.low[act]), a.high[act]);

@@ -28,10 +28,11 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
     const uint32_t s = static_cast<uint32_t>(row % a.S);
     const uint32_t b = static_cast<uint32_t>(row / a.S);
     const uint64_t base = row * a.T * a.A + act;
+    const uint64_t gbase = global_row(b, s, a.sample_base, a.sample_total, a.S) * a.T * a.A + act;
     float eps[kMaxHorizon];
     for (uint32_t t = 0; t < a.T; ++t) {
         const uint64_t idx = base + static_cast<uint64_t>(t) * a.A;
-        eps[t] = a.noise ? a.noise[idx] : normal_at(a.seed, a.offset + idx);
+        eps[t] = a.noise ? a.noise[idx] : normal_at(a.seed, a.offset + gbase + static_cast<uint64_t>(t) * a.A);
     }
     if (a.smooth > 0.0f && a.T > 1) {
         // swm_temporal_color_noise_f32 (src/planner.rs:1852-1896)
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
         if (carried) {
             v = a.carried[((static_cast<size_t>(b) * a.carried_count + (s - 1)) * a.T + t) * a.A + act];
         } else {
-            v = (s == 0) ? a.mean[mi] : __fadd_rn(a.mean[mi], __fmul_rn(eps[t], a.std[mi]));
+            v = (a.sample_base + s == 0) ? a.mean[mi] : __fadd_rn(a.mean[mi], __fmul_rn(eps[t], a.std[mi]));
             v = cmin(cmax(v, lo), hi);
         }
         a.out[base + static_cast<uint64_t>(t) * a.A] = v;
@@ -81,6 +82,18 @@ __global__ void __launch_bounds__(256) mppi_reduce_kernel(MppiArgs m, const floa
     const size_t TA = static_cast<size_t>(m.T) * m.A;
     mppi_reduce_rows<NT>(m, b, p, nrows, s_score, first,
                          cand + (static_cast<size_t>(b) * S + first) * TA, TA, s_w);
+}
+
+// ------------------------------------------- MPPI combine across shards
+// One block per vehicle: the tuples of every candidate-range shard
+// ([shards][B][pw], gathered from the GPUs that scored them) are rescaled to
+// the global minimum and summed, exactly as the per-block partials are.
+__global__ void __launch_bounds__(256) mppi_combine_kernel(MppiArgs m, const float* tuples, uint32_t B,
+                                                           uint32_t shards) {
+    __shared__ uint64_t s_key_scratch[256 / 32];
+    const uint32_t b = blockIdx.x;
+    mppi_finish<256>(m, b, tuples + static_cast<size_t>(b) * m.pw, shards, static_cast<size_t>(B) * m.pw,
+                     s_key_scratch);
 }
 
 // ------------------------------------------------ top-k + elite refit
@@ -232,6 +245,14 @@ cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float
                                uint32_t S, cudaStream_t stream) {
     dim3 grid(ceil_div(S, 256), B);
     mppi_reduce_kernel<<<grid, 256, 0, stream>>>(m, cand, scores, S);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mppi_combine(const MppiArgs& m, const float* tuples, uint32_t B, uint32_t shards,
+                                cudaStream_t stream) {
+    MppiArgs mm = m;
+    mm.shard_tuple = nullptr;
+    mppi_combine_kernel<<<B, 256, 0, stream>>>(mm, tuples, B, shards);
     return cudaGetLastError();
 }
 

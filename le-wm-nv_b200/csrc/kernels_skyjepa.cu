@@ -555,7 +555,7 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
         const float sdt = a.dt;
         float ta;
         if (a.rotor_forces) {
-            ta = (act[0] + act[1] + act[2] + act[3]) / a.mass;
+            ta = (act[0] + act[1] + act[2] + act[3]) / (a.masses ? __ldg(a.masses + b) : a.mass);
         } else {
             const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
             ta = th * a.gravity / a.hover_throttle;
@@ -685,10 +685,11 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
         float v;
         if (a.sample) {
             const size_t mi = static_cast<size_t>(b) * TA + e;
-            if (s == 0 || s >= a.S) {
+            if (a.sample_base + s == 0 || s >= a.S) {
                 v = a.mean[mi];
             } else {
-                const float eps = a.noise ? a.noise[ci] : normal_at(a.seed, a.offset + ci);
+                const uint64_t gi = global_row(b, s, a.sample_base, a.sample_total, a.S) * TA + e;
+                const float eps = a.noise ? a.noise[ci] : normal_at(a.seed, a.offset + gi);
                 v = a.mean[mi] + eps * a.std[mi];
             }
             v = cmin(cmax(v, a.low[act]), a.high[act]);

@@ -19,7 +19,20 @@ struct MppiArgs {
     float* best_score;        // [B]
     uint32_t T, A, P, pw;     // pw = partial row width in floats (4 + T*A, padded)
     float mul;                // -1 / temperature
+    uint32_t sample_base;     // global index of this shard's first sample (best-index keys)
+    float* shard_tuple;       // [B][pw]: when set, the vehicle's combined tuple is written
+                              // here (for a cross-GPU combine) instead of the final outputs
 };
+
+// Candidate-range shards: a planner that owns samples [sample_base,
+// sample_base + S) of sample_total draws the same noise as an unsharded
+// planner of sample_total samples (Philox index of the global sample) and
+// only the shard holding sample 0 carries the mean candidate.
+__host__ __device__ inline uint64_t global_row(uint32_t b, uint32_t s, uint32_t sample_base, uint32_t sample_total,
+                                               uint32_t S) {
+    const uint32_t total = sample_total ? sample_total : S;
+    return static_cast<uint64_t>(b) * total + sample_base + s;
+}
 
 constexpr uint32_t kMaxHorizon = 64;
 constexpr uint32_t kMaxActionDim = 16;
@@ -33,6 +46,7 @@ struct SampleArgs {
     const float* noise;    // injected [B,S,T,A] or nullptr
     uint64_t seed, offset;
     float smooth;          // colored-noise EMA factor; 0 = white noise
+    uint32_t sample_base, sample_total;  // candidate-range shard (sample_total 0: unsharded)
     const float* carried;  // [B,carried_count,T,A] or nullptr
     uint32_t carried_count, inject;
     float* out;            // [B,S,T,A]
@@ -80,6 +94,7 @@ struct NominalArgs {
     float low[4], high[4];
     const float* noise;           // injected [B,S,T,4] or nullptr
     uint64_t seed, offset;
+    uint32_t sample_base, sample_total;  // candidate-range shard (sample_total 0: unsharded)
     const float* cand_in;         // [B,S,T,4] when sample == 0
     float* cand_out;              // [B,S,T,4] or nullptr
     float* scores;                // [B,S]
@@ -114,6 +129,8 @@ struct SkyjepaArgs {
     const float* action_hist;     // [B,Hs-1,4] raw
     const float* ref_states;      // [B,T,18]
     const float* ref_actions;     // [B,T,4]
+    const float* masses;          // [B] per-vehicle mass, or nullptr (use `mass`)
+    uint32_t sample_base, sample_total;  // candidate-range shard (sample_total 0: unsharded)
     uint32_t rows;                // candidate rows per cluster (multiple of 8, 32..64)
     int sample;
     const float* mean;            // [B,T,4]
@@ -132,6 +149,9 @@ struct SkyjepaArgs {
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
 cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
                                uint32_t S, cudaStream_t stream);
+// Combine `shards` per-vehicle tuples [shards][B][pw] into the final outputs.
+cudaError_t launch_mppi_combine(const MppiArgs& m, const float* tuples, uint32_t B, uint32_t shards,
+                                cudaStream_t stream);
 uint32_t sort_length(uint32_t S);
 cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream);
 cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint32_t S, uint32_t K,

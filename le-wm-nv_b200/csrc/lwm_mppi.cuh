@@ -52,6 +52,56 @@ __device__ __forceinline__ float block_sum_f32(float v, float* scratch) {
     return r;
 }
 
+// Combines `count` tuples (stride `stride` floats apart, starting at `base`)
+// of vehicle b into the final outputs, or into a.shard_tuple.  All NT threads
+// call it.
+template <int NT>
+__device__ void mppi_finish(const MppiArgs& a, uint32_t b, const float* base, uint32_t count, size_t stride,
+                            uint64_t* s_key_scratch) {
+    const uint32_t TA = a.T * a.A;
+    uint64_t gkey = ~0ull;
+    for (uint32_t q = threadIdx.x; q < count; q += NT) {
+        const uint64_t k = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(q) * stride)[1];
+        gkey = k < gkey ? k : gkey;
+    }
+    gkey = block_min_u64<NT>(gkey, s_key_scratch);
+    const float M = key_score(gkey);
+    float* tuple = a.shard_tuple ? a.shard_tuple + static_cast<size_t>(b) * a.pw : nullptr;
+    float Wtot = 0.0f;
+    for (uint32_t e = threadIdx.x; e < TA; e += NT) {
+        float W = 0.0f, V = 0.0f;
+        for (uint32_t q = 0; q < count; ++q) {
+            const volatile float* pq = base + static_cast<size_t>(q) * stride;
+            if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;  // tuple without rows
+            const float f = expf((pq[0] - M) * a.mul);
+            W += pq[1] * f;
+            V += pq[4 + e] * f;
+        }
+        Wtot = W;
+        if (tuple) {
+            tuple[4 + e] = V;
+            continue;
+        }
+        const float value = V / W;
+        const uint32_t t = e / a.A, act = e - t * a.A;
+        const size_t seq = static_cast<size_t>(b) * TA;
+        a.sequence[seq + e] = value;
+        if (t == 0) a.first_action[static_cast<size_t>(b) * a.A + act] = value;
+        if (t >= 1) a.warm_start[seq + e - a.A] = value;
+        if (t == a.T - 1) a.warm_start[seq + e] = value;
+    }
+    if (threadIdx.x == 0) {
+        if (tuple) {
+            tuple[0] = M;
+            tuple[1] = Wtot;
+            reinterpret_cast<uint64_t*>(tuple)[1] = gkey;
+        } else {
+            a.best_index[b] = static_cast<uint32_t>(gkey & 0xffffffffu);
+            a.best_score[b] = M;
+        }
+    }
+}
+
 // All NT threads of the block call this.  Rows r in [0, nrows) of this block
 // have score s_score[r] (smem) and sample index first_sample + r; candidate
 // element e of row r is cand[r * row_stride + e] (smem or global).  s_w is
@@ -68,7 +118,7 @@ __device__ void mppi_reduce_rows(const MppiArgs& a, uint32_t b, uint32_t p, uint
 
     uint64_t key = ~0ull;
     for (uint32_t r = threadIdx.x; r < nrows; r += NT) {
-        const uint64_t k = score_key(s_score[r], first_sample + r);
+        const uint64_t k = score_key(s_score[r], a.sample_base + first_sample + r);
         key = k < key ? k : key;
     }
     key = block_min_u64<NT>(key, s_key_scratch);
@@ -101,36 +151,8 @@ __device__ void mppi_reduce_rows(const MppiArgs& a, uint32_t b, uint32_t p, uint
     if (!s_is_last) return;
     __threadfence();
 
-    const float* base = a.partials + static_cast<size_t>(b) * a.P * a.pw;
-    uint64_t gkey = ~0ull;
-    for (uint32_t q = threadIdx.x; q < a.P; q += NT) {
-        const uint64_t k = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(q) * a.pw)[1];
-        gkey = k < gkey ? k : gkey;
-    }
-    gkey = block_min_u64<NT>(gkey, s_key_scratch);
-    const float M = key_score(gkey);
-    for (uint32_t e = threadIdx.x; e < TA; e += NT) {
-        float W = 0.0f, V = 0.0f;
-        for (uint32_t q = 0; q < a.P; ++q) {
-            const volatile float* pq = base + static_cast<size_t>(q) * a.pw;
-            if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;  // block without rows
-            const float f = expf((pq[0] - M) * a.mul);
-            W += pq[1] * f;
-            V += pq[4 + e] * f;
-        }
-        const float value = V / W;
-        const uint32_t t = e / a.A, act = e - t * a.A;
-        const size_t seq = static_cast<size_t>(b) * TA;
-        a.sequence[seq + e] = value;
-        if (t == 0) a.first_action[static_cast<size_t>(b) * a.A + act] = value;
-        if (t >= 1) a.warm_start[seq + e - a.A] = value;
-        if (t == a.T - 1) a.warm_start[seq + e] = value;
-    }
-    if (threadIdx.x == 0) {
-        a.best_index[b] = static_cast<uint32_t>(gkey & 0xffffffffu);
-        a.best_score[b] = M;
-        a.counters[b] = 0u;
-    }
+    mppi_finish<NT>(a, b, a.partials + static_cast<size_t>(b) * a.P * a.pw, a.P, a.pw, s_key_scratch);
+    if (threadIdx.x == 0) a.counters[b] = 0u;
 }
 
 }  // namespace lwm

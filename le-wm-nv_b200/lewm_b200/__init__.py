@@ -223,6 +223,7 @@ _sig("lwm_skyjepa_random_weights", C.c_int, C.POINTER(SkyJepaConfig), U64, FP, C
 _sig("lwm_scorer_skyjepa_create", C.c_int, VP, C.POINTER(SkyJepaConfig), FP, C.c_size_t, FP, FP, FP, FP,
      C.POINTER(TrackingCost), F, C.POINTER(VP))
 _sig("lwm_scorer_skyjepa_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP)
+_sig("lwm_scorer_skyjepa_set_context_ex", C.c_int, VP, U32, U32, FP, FP, FP, FP, FP)
 _sig("lwm_scorer_callback_create", C.c_int, VP, U32, SCORE_FN, VP, C.POINTER(VP))
 _sig("lwm_scorer_score_device", C.c_int, VP, VP, U32, U32, U32, U32, VP)
 _sig("lwm_scorer_predict_device", C.c_int, VP, VP, U32, U32, U32, VP)
@@ -235,6 +236,9 @@ _sig("lwm_normal_device", C.c_int, VP, U64, U64, C.c_size_t, VP)
 _sig("lwm_skyjepa_reference_horizon", C.c_int, I32, F, F, U32, F, F, FP)
 _sig("lwm_skyjepa_geometric_prior", C.c_int, FP, FP, U32, F, C.POINTER(Domain), FP)
 _sig("lwm_rotor_plant_step", C.c_int, C.POINTER(Domain), FP, FP, FP, F)
+_sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
+_sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
+_sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
 _sig("lwm_image_preprocess_imagenet_224", None, C.POINTER(ImagePreprocess))
 _sig("lwm_preprocess_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32, I32,
      VP)
@@ -574,11 +578,15 @@ class SkyJepaScorer(Scorer):
         self.handle = h
         _LIVE["scorer"].add(self)
 
-    def set_context(self, state_history, action_history, reference_states, reference_actions) -> None:
+    def set_context(self, state_history, action_history, reference_states, reference_actions,
+                    vehicle_mass=None) -> None:
+        """Per-plan context; `vehicle_mass` [B] overrides kinematics.mass per vehicle."""
         sh = _f32(state_history)
         ref = _f32(reference_states)
-        _check(lib.lwm_scorer_skyjepa_set_context(self.handle, sh.shape[0], ref.shape[1], _fp(sh),
-                                                  _fp(_f32(action_history)), _fp(ref), _fp(_f32(reference_actions))))
+        m = None if vehicle_mass is None else _f32(vehicle_mass)
+        _check(lib.lwm_scorer_skyjepa_set_context_ex(self.handle, sh.shape[0], ref.shape[1], _fp(sh),
+                                                     _fp(_f32(action_history)), _fp(ref),
+                                                     _fp(_f32(reference_actions)), _fp(m)))
         self.batch = sh.shape[0]
 
 
@@ -657,6 +665,28 @@ class _Planner:
         r = _PlanDeviceResult()
         _check(lib.lwm_plan_device(self.handle, scorer.handle, VP(injected_noise_ptr) if injected_noise_ptr else None,
                                    C.byref(r)))
+        return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
+                                r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
+                                _OUTCOME[r.deadline_outcome])
+
+    # ------------------------------------------------ candidate-range shards
+    def set_shard(self, sample_base: int, sample_total: int) -> None:
+        """Own samples [sample_base, sample_base + samples) of sample_total (0: unsharded)."""
+        _check(lib.lwm_planner_set_shard(self.handle, sample_base, sample_total))
+
+    def plan_device_shard(self, scorer: Scorer, injected_noise_ptr: Optional[int] = None):
+        """Score this shard; returns (device address of the [B, width] tuples, width)."""
+        t = VP()
+        w = U32()
+        _check(lib.lwm_plan_device_shard(self.handle, scorer.handle,
+                                         VP(injected_noise_ptr) if injected_noise_ptr else None, C.byref(t),
+                                         C.byref(w)))
+        return int(t.value), int(w.value)
+
+    def combine_device(self, tuples_ptr: int, shards: int) -> PlanDeviceResult:
+        """Finish the plan from the gathered tuples [shards, B, width] of every shard."""
+        r = _PlanDeviceResult()
+        _check(lib.lwm_mppi_combine_device(self.handle, VP(tuples_ptr), shards, C.byref(r)))
         return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
                                 r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
                                 _OUTCOME[r.deadline_outcome])

@@ -152,3 +152,30 @@ def fleet_domains(seed: int, vehicles: int) -> List[Domain]:
 def prior_warm_start(w: NominalWorkload) -> np.ndarray:
     """Geometric prior of every vehicle (the session's warm start)."""
     return np.stack([geometric_prior(w.initial[b], w.reference_states[b], w.dt) for b in range(w.batch)])
+
+
+def fleet(seed: int = 0, vehicles: int = 256, samples: int = 4096, horizon: int = 30, dt: float = 0.05,
+          config: Optional[SkyJepaConfig] = None) -> SkyJepaWorkload:
+    """Fleet-scale learned MPPI: `vehicles` independent vehicles with sampled
+    physical parameters (fleet_domains), each planning `samples` candidates x
+    `horizon` steps with the learned SkyJEPA scorer.  Each vehicle's history
+    is flown at its own hover thrust; `masses` carries the per-vehicle mass
+    for the scorer's rotor-forces integrator."""
+    w = skyjepa(seed, batch=vehicles, samples=samples, horizon=horizon, dt=dt, config=config)
+    doms = fleet_domains(seed, vehicles)
+    Hs = w.model.history_steps
+    for b, d in enumerate(doms):
+        hover = d.hover_force()
+        x = w.state_history[b, 0].copy()
+        states = [x.copy()]
+        m = np.full(4, hover, np.float32)
+        for _ in range(Hs - 1):
+            for _ in range(10):
+                plant_step(d, x, m, np.full(4, hover, np.float32), dt / 10)
+            states.append(x.copy())
+        w.state_history[b] = np.stack(states)
+        w.action_history[b] = hover
+    w.initial = w.state_history[:, -1].copy()
+    w.masses = np.array([d.mass for d in doms], np.float32)
+    w.domains = doms
+    return w

@@ -1023,7 +1023,7 @@ void orc_skyjepa_scores(const orc_skyjepa* m, const float* state_mean, const flo
                         const float* state_hist, const float* action_hist,
                         const float* ref_states, const float* ref_actions,
                         const lwm_tracking_cost* cost, float dt, const float* cand, uint32_t B,
-                        uint32_t S, uint32_t T, float* scores, float* states_out) {
+                        uint32_t S, uint32_t T, const float* masses, float* scores, float* states_out) {
     uint32_t Hs = m->cfg.history_steps, A = m->cfg.action_dim, D = m->cfg.state_dim, H = m->cfg.latent_dim;
     size_t rows = (size_t)B * S;
     float* nsh = (float*)malloc(sizeof(float) * (size_t)B * Hs * D);
@@ -1047,7 +1047,15 @@ void orc_skyjepa_scores(const orc_skyjepa* m, const float* state_mean, const flo
     float* dts = (float*)malloc(sizeof(float) * rows * T);
     for (size_t i = 0; i < rows * T; ++i) dts[i] = dt;
     float* states = states_out ? states_out : (float*)malloc(sizeof(float) * rows * T * 18);
-    orc_integrate_k3(init, cand, dts, res, mp, (uint32_t)rows, T, &m->cfg.kinematics, states);
+    /* one integrator call per vehicle: the reference runs one scorer (one
+     * kinematics config) per vehicle when vehicles differ in mass */
+    for (uint32_t b = 0; b < B; ++b) {
+        lwm_kinematic_config kin = m->cfg.kinematics;
+        if (masses) kin.mass = masses[b];
+        size_t r0 = (size_t)b * S;
+        orc_integrate_k3(init + r0 * 18, cand + r0 * T * A, dts + r0 * T, res + r0 * T * 3, mp + r0 * T * 12, S, T,
+                         &kin, states + r0 * T * 18);
+    }
     orc_tracking_scores(states, cand, ref_states, ref_actions, cost, B, S, T, scores);
     if (!states_out) free(states);
     free(dts); free(init); free(mp); free(res); free(pr); free(lat); free(nc); free(nah); free(nsh);
@@ -1059,7 +1067,7 @@ void orc_skyjepa_score_fn(void* user, const float* cand, uint32_t B, uint32_t S,
     const orc_skyjepa_ctx* c = (const orc_skyjepa_ctx*)user;
     orc_skyjepa_scores(c->model, c->state_mean, c->state_std, c->action_mean, c->action_std, c->state_hist,
                        c->action_hist, c->ref_states, c->ref_actions, &c->cost, c->dt, cand, B, S, T,
-                       scores, NULL);
+                       c->masses, scores, NULL);
 }
 
 /* ---------------------------------------------------------------- planners */

@@ -102,7 +102,7 @@ void orc_skyjepa_scores(const orc_skyjepa* m, const float* state_mean, const flo
                         const float* state_hist, const float* action_hist,
                         const float* ref_states, const float* ref_actions,
                         const lwm_tracking_cost* cost, float dt, const float* cand, uint32_t B,
-                        uint32_t S, uint32_t T, float* scores, float* states_out);
+                        uint32_t S, uint32_t T, const float* masses, float* scores, float* states_out);
 
 /* ---- planners ---- */
 typedef void (*orc_score_fn)(void* user, const float* cand, uint32_t B, uint32_t S, uint32_t T,
@@ -151,6 +151,7 @@ typedef struct orc_skyjepa_ctx {
     const float* ref_actions;
     lwm_tracking_cost cost;
     float dt;
+    const float* masses; /* [B] per-vehicle mass or NULL */
 } orc_skyjepa_ctx;
 void orc_skyjepa_score_fn(void* user, const float* cand, uint32_t B, uint32_t S, uint32_t T,
                           uint32_t A, float* scores);

@@ -44,7 +44,7 @@ class NominalCtx(C.Structure):
 class SkyCtx(C.Structure):
     _fields_ = [("model", VP), ("state_mean", FP), ("state_std", FP), ("action_mean", FP), ("action_std", FP),
                 ("state_hist", FP), ("action_hist", FP), ("ref_states", FP), ("ref_actions", FP),
-                ("cost", TrackingCost), ("dt", F)]
+                ("cost", TrackingCost), ("dt", F), ("masses", FP)]
 
 
 def _sig(name, restype, *args):
@@ -85,7 +85,7 @@ _sig("orc_integrate_k3", None, FP, FP, FP, FP, FP, U32, U32, C.POINTER(Kinematic
 _sig("orc_integrate_reference", None, FP, FP, FP, FP, FP, U32, U32, C.POINTER(KinematicConfig), FP)
 _sig("orc_so3_exp", None, FP, FP)
 _sig("orc_skyjepa_scores", None, VP, FP, FP, FP, FP, FP, FP, FP, FP, C.POINTER(TrackingCost), F, FP, U32, U32,
-     U32, FP, FP)
+     U32, FP, FP, FP)
 _sig("orc_mppi_plan", C.c_int, C.POINTER(_MppiConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, FP, FP, UP, FP)
 _sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
@@ -283,20 +283,24 @@ class SkyJepaModel:
         lib.orc_prober(self.handle, fp(lat), N, fp(out))
         return out
 
-    def scores(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt, cand, with_states=False):
+    def scores(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt, cand, with_states=False,
+               masses=None):
         cand = f32(cand)
+        masses = None if masses is None else f32(masses)
         B, S, T, _ = cand.shape
         scores = np.empty((B, S), np.float32)
         states = np.empty((B, S, T, 18), np.float32) if with_states else None
         sm, ss, am, as_ = (f32(v) for v in norm)
         lib.orc_skyjepa_scores(self.handle, fp(sm), fp(ss), fp(am), fp(as_), fp(f32(state_hist)),
                                fp(f32(action_hist)), fp(f32(ref_states)), fp(f32(ref_actions)), C.byref(cost),
-                               F(dt), fp(cand), B, S, T, fp(scores), fp(states))
+                               F(dt), fp(cand), B, S, T, fp(masses), fp(scores), fp(states))
         return (scores, states) if with_states else scores
 
-    def score_ctx(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt):
+    def score_ctx(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt, masses=None):
         keep = [f32(v) for v in norm] + [f32(state_hist), f32(action_hist), f32(ref_states), f32(ref_actions)]
-        ctx = SkyCtx(self.handle, *(fp(v) for v in keep), cost, dt)
+        m = None if masses is None else f32(masses)
+        ctx = SkyCtx(self.handle, *(fp(v) for v in keep), cost, dt, fp(m))
+        keep.append(m)
         ctx._keep = keep
         return ctx
 
