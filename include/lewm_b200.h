@@ -400,6 +400,120 @@ lwm_status lwm_color_noise_device(lwm_ctx* ctx, const float* noise, float* out, 
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count,
                              float* out);
 
+/* ---------------------------------------------------------------- LeWM world-model scorer */
+
+/* LeWM / WorldModel (src/models/lewm/{config,model,modules,vit}.rs,
+ * src/models/world_model/{config,model}.rs): an observation encoder (vector
+ * MLP or ViT + projector MLP), an action embedder, an AdaLN-conditioned
+ * causal transformer predictor and a pred_proj MLP; candidates are scored by
+ * the squared L2 distance of the last predicted embedding to a goal
+ * embedding (LeWmSession::score_candidates, src/session.rs:46-66). */
+typedef enum lwm_norm_kind {
+    LWM_NORM_BATCH = 0, /* BatchNorm1d in eval mode (running statistics), eps 1e-5 */
+    LWM_NORM_LAYER = 1, /* LayerNorm, eps 1e-5 */
+    LWM_NORM_NONE = 2,
+} lwm_norm_kind;
+typedef enum lwm_encoder_kind {
+    LWM_ENCODER_VECTOR_MLP = 0,
+    LWM_ENCODER_VIT = 1,
+} lwm_encoder_kind;
+typedef struct lwm_lewm_config {
+    uint32_t embed_dim;        /* D: encoder output = predictor input/output */
+    uint32_t action_dim;       /* ActionEmbedderConfig (src/models/lewm/config.rs:69-88) */
+    uint32_t smoothed_dim;
+    uint32_t action_mlp_scale;
+    uint32_t history_size;     /* rollout window (LeWmConfig::history_size) */
+    uint32_t num_frames;       /* PredictorConfig (config.rs:42-67) */
+    uint32_t pred_hidden_dim;
+    uint32_t depth;
+    uint32_t heads;
+    uint32_t dim_head;
+    uint32_t mlp_dim;
+    uint32_t pred_proj_hidden; /* pred_proj MlpConfig (config.rs:90-107) */
+    int32_t pred_proj_norm;    /* lwm_norm_kind */
+    int32_t encoder;           /* lwm_encoder_kind */
+    /* VectorMlpConfig (src/models/world_model/config.rs:22-44) */
+    uint32_t obs_dim;
+    uint32_t obs_hidden_dim;
+    uint32_t obs_depth;
+    int32_t obs_norm;          /* LayerNorm or None (BatchNorm maps to LayerNorm, model.rs:297-305) */
+    /* VitEncoderConfig (src/models/lewm/config.rs:14-40) + projector MLP */
+    uint32_t image_size;
+    uint32_t patch_size;
+    uint32_t vit_hidden;
+    uint32_t vit_layers;
+    uint32_t vit_heads;
+    uint32_t vit_mlp;
+    float vit_eps;
+    uint32_t channels;
+    int32_t qkv_bias;
+    uint32_t projector_hidden;
+    int32_t projector_norm;
+} lwm_lewm_config;
+
+/* The vector-observation CEM workload's model: VectorMlp 16 -> 512 (depth 3,
+ * LayerNorm) -> 192, ActionEmbedder(2 -> 192), predictor depth 4, 8 heads x
+ * 32, MLP 768, one frame, pred_proj 192 -> 512 -> 192 LayerNorm. */
+void lwm_lewm_config_vector(lwm_lewm_config* out);
+/* The image MPPI workload's model: ViT-Tiny (224, patch 16, 12 layers, 192,
+ * 3 heads, MLP 768, eps 1e-12) + projector 192 -> 2048 -> 192 BatchNorm,
+ * ActionEmbedder(2 -> 192), predictor depth 6, 16 heads x 64, MLP 2048
+ * (PredictorConfig::lewm_tiny), one frame, pred_proj as the projector. */
+void lwm_lewm_config_image(lwm_lewm_config* out);
+/* Weight blob: one f32 array in this order (VarBuilder paths; Linear weights
+ * [out, in], then bias):
+ *   action_encoder.patch_embed.weight [sm, A, 1] .bias [sm]
+ *   action_encoder.embed.0 [scale*D, sm] + bias, .embed.2 [D, scale*D] + bias
+ *   predictor.pos_embedding [1, num_frames, D]
+ *   predictor.transformer.input_proj [hid, D] + bias   (only when hid != D)
+ *   predictor.transformer.cond_proj [hid, D] + bias    (only when hid != D)
+ *   predictor.transformer.layers.{i}:
+ *     attn.norm.weight [hid] .bias [hid], attn.to_qkv.weight [3*heads*dh, hid],
+ *     attn.to_out.0.weight [hid, heads*dh] .bias [hid],
+ *     mlp.net.0.weight [hid] .bias [hid], mlp.net.1 [mlp, hid] + bias,
+ *     mlp.net.4 [hid, mlp] + bias, adaLN_modulation.1 [6*hid, hid] + bias
+ *   predictor.transformer.norm.weight [hid] .bias [hid]
+ *   predictor.transformer.output_proj [D, hid] + bias   (only when hid != D)
+ *   pred_proj: net.0 [ph, D] + bias, net.1 (BatchNorm: weight, bias,
+ *     running_mean, running_var [ph]; LayerNorm: weight, bias; None: nothing),
+ *     net.3 [D, ph] + bias
+ *   observation encoder, vector: layers.0 [oh, obs] + bias, norms.0 (LayerNorm
+ *     weight, bias when obs_norm != None), layers.{j} [oh, oh] + bias and
+ *     norms.{j} for j = 1 .. depth-2, layers.{depth-1} [D, oh] + bias
+ *   observation encoder, ViT: embeddings.cls_token [1,1,vh],
+ *     embeddings.position_embeddings [1, 1 + (img/p)^2, vh],
+ *     embeddings.patch_embeddings.projection.weight [vh, C, p, p] .bias [vh],
+ *     per layer: layernorm_before (w, b), attention.query/key/value [vh, vh]
+ *     (+ bias when qkv_bias), attention.output.dense [vh, vh] + bias,
+ *     layernorm_after (w, b), intermediate.dense [vmlp, vh] + bias,
+ *     output.dense [vh, vmlp] + bias; then layernorm (w, b); then the
+ *     projector MLP laid out as pred_proj (input vh, hidden projector_hidden). */
+size_t lwm_lewm_weight_count(const lwm_lewm_config* cfg);
+/* Seeded random init: Linear weights N(0, 2/fan_in) (Kaiming normal, candle's
+ * linear default), biases U(+-1/sqrt(fan_in)), norm weights 1 / biases 0,
+ * BatchNorm running mean 0 / var 1, position embeddings and CLS N(0, 0.02^2). */
+lwm_status lwm_lewm_random_weights(const lwm_lewm_config* cfg, uint64_t seed, float* out, size_t count);
+
+/* LeWmSession / WorldModel scorer (src/session.rs:46-66): weights in the
+ * blob order above.  Fails with the reference's validation texts. */
+lwm_status lwm_scorer_lewm_create(lwm_ctx* ctx, const lwm_lewm_config* cfg, const float* weights, size_t count,
+                                  lwm_scorer** out);
+/* Per-plan context: history embeddings [B, h, D] (LeWmSession::reset_pixels
+ * caches them) shared by every sample of a vehicle, and the goal embedding
+ * [B, D] (goal_cost, src/models/lewm/model.rs:149-165).  `history` is the
+ * rollout window (rollout_embeddings_with_history); 0 uses h, as the session
+ * does.  Host arrays, or device arrays with the _device variant. */
+lwm_status lwm_scorer_lewm_set_context(lwm_scorer* scorer, uint32_t batch, uint32_t h, uint32_t history,
+                                       const float* emb, const float* goal);
+lwm_status lwm_scorer_lewm_set_context_device(lwm_scorer* scorer, uint32_t batch, uint32_t h, uint32_t history,
+                                              const float* emb, const float* goal);
+/* WorldModel::encode_vector (src/models/world_model/model.rs:48-50):
+ * device obs [n, obs_dim] -> device embeddings [n, D]. */
+lwm_status lwm_lewm_encode_vector_device(lwm_scorer* scorer, const float* obs, uint32_t n, float* out);
+/* LeWm::encode_pixels (src/models/lewm/model.rs:41-55): device normalised
+ * pixels [n, C, image, image] -> device embeddings [n, D]. */
+lwm_status lwm_lewm_encode_pixels_device(lwm_scorer* scorer, const float* pixels, uint32_t n, float* out);
+
 /* ---------------------------------------------------------------- candidate-range sharding */
 
 /* Multi-GPU MPPI over one vehicle batch: each GPU's planner owns samples

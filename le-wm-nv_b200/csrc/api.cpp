@@ -13,6 +13,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <random>
 #include <string>
@@ -20,6 +21,7 @@
 
 #include "../../include/lewm_b200.h"
 #include "lwm_kernels.hpp"
+#include "lwm_lewm.hpp"
 
 using lwm::MppiArgs;
 
@@ -118,7 +120,7 @@ struct lwm_ctx {
 };
 
 enum class PlannerKind { Mppi, Cem, Icem };
-enum class ScorerKind { Nominal, Skyjepa, Callback };
+enum class ScorerKind { Nominal, Skyjepa, Callback, Lewm };
 
 struct lwm_scorer {
     lwm_ctx* ctx = nullptr;
@@ -144,6 +146,8 @@ struct lwm_scorer {
     // callback
     lwm_score_fn fn = nullptr;
     void* user = nullptr;
+    // LeWM world model
+    std::unique_ptr<lwm::LewmModel> lewm;
 };
 
 struct lwm_planner {
@@ -449,6 +453,14 @@ lwm_status check_scorer_shape(lwm_scorer* sc, uint32_t B, uint32_t T, uint32_t A
         return fail(LWM_INVALID_ARGUMENT, "scorer context has not been set");
     if (sc->kind == ScorerKind::Nominal) {
         if (B != sc->batch || T != sc->horizon || A != 4) return fail(LWM_INVALID_ARGUMENT, "nominal candidate shape mismatch");
+    } else if (sc->kind == ScorerKind::Lewm) {
+        if (B != sc->batch || A != sc->lewm->c.action_dim)
+            return fail(LWM_INVALID_ARGUMENT, "LeWM candidate actions [" + std::to_string(B) + ", S, T, " + std::to_string(A) +
+                                                  "] do not match batch=" + std::to_string(sc->batch) +
+                                                  ", action_dim=" + std::to_string(sc->lewm->c.action_dim));
+        if (T < sc->lewm->h)
+            return fail(LWM_INVALID_ARGUMENT, "action horizon " + std::to_string(T) + " is shorter than history " +
+                                                  std::to_string(sc->lewm->h));
     } else if (sc->kind == ScorerKind::Skyjepa) {
         if (B != sc->batch || T != sc->horizon || A != 4)
             return fail(LWM_INVALID_ARGUMENT, "SkyJEPA candidate actions [" + std::to_string(B) + ", S, " + std::to_string(T) + ", " +
@@ -484,6 +496,9 @@ lwm_status score_device(lwm_scorer* sc, const float* cand, uint32_t B, uint32_t 
         int n = 0;
         LWM_CUDA(lwm::launch_skyjepa(a, stream, &n));
         sc->ctx->launches += static_cast<uint64_t>(n);
+    } else if (sc->kind == ScorerKind::Lewm) {
+        LWM_CUDA(sc->lewm->score(cand, S, T, scores, states, stream));
+        sc->ctx->launches += static_cast<uint64_t>(sc->lewm->launches);
     } else {
         if (states) return fail(LWM_UNSUPPORTED, "callback scorers do not predict states");
         const int rc = sc->fn(sc->user, cand, B, S, T, A, scores, stream);
@@ -1173,6 +1188,95 @@ lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* s, uint32_t B, uint32_t
     return LWM_OK;
 }
 
+lwm_status lwm_scorer_lewm_create(lwm_ctx* ctx, const lwm_lewm_config* cfg, const float* weights, size_t count,
+                                  lwm_scorer** out) {
+    if (!ctx || !cfg || !weights || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    const char* why = nullptr;
+    if (!lwm::lewm_config_valid(*cfg, &why)) return fail(LWM_INVALID_ARGUMENT, why);
+    const size_t n = lwm::lewm_walk(*cfg, nullptr, nullptr);
+    if (count != n)
+        return fail(LWM_INVALID_ARGUMENT, "LeWM weight blob has " + std::to_string(count) + " floats, expected " +
+                                              std::to_string(n));
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    auto model = std::make_unique<lwm::LewmModel>();
+    model->c = *cfg;
+    LWM_CUDA(cudaMalloc(&model->blob, n * sizeof(float)));
+    LWM_CUDA(cudaMemcpy(model->blob, weights, n * sizeof(float), cudaMemcpyHostToDevice));
+    lwm::lewm_walk(*cfg, model->blob, &model->w);
+    lwm_scorer* s = new_scorer(ctx, ScorerKind::Lewm);
+    s->lewm = std::move(model);
+    *out = s;
+    return LWM_OK;
+}
+
+static lwm_status lewm_set_context(lwm_scorer* s, uint32_t B, uint32_t h, uint32_t history, const float* emb,
+                                   const float* goal, cudaMemcpyKind kind) {
+    if (!s || s->kind != ScorerKind::Lewm) return fail(LWM_INVALID_ARGUMENT, "not a LeWM scorer");
+    if (!emb || !goal || B == 0 || h == 0) return fail(LWM_INVALID_ARGUMENT, "invalid LeWM context shapes");
+    lwm::LewmModel& m = *s->lewm;
+    const uint32_t window = history ? history : h;
+    if (window > m.c.num_frames)
+        return fail(LWM_INVALID_ARGUMENT, "rollout window " + std::to_string(window) + " exceeds predictor.num_frames " +
+                                              std::to_string(m.c.num_frames));
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    const size_t D = m.c.embed_dim;
+    const size_t need = static_cast<size_t>(B) * h * D;
+    if (need > m.ctx_cap || static_cast<size_t>(B) * D > m.ctx_cap) {
+        LWM_CUDA(cudaStreamSynchronize(s->ctx->stream));
+        if (m.emb) cudaFree(m.emb);
+        if (m.goal) cudaFree(m.goal);
+        m.emb = m.goal = nullptr;
+        m.ctx_cap = 0;
+        const size_t cap = std::max(need, static_cast<size_t>(B) * D);
+        LWM_CUDA(cudaMalloc(&m.emb, cap * sizeof(float)));
+        LWM_CUDA(cudaMalloc(&m.goal, cap * sizeof(float)));
+        m.ctx_cap = cap;
+    }
+    LWM_CUDA(cudaMemcpyAsync(m.emb, emb, need * sizeof(float), kind, s->ctx->stream));
+    LWM_CUDA(cudaMemcpyAsync(m.goal, goal, static_cast<size_t>(B) * D * sizeof(float), kind, s->ctx->stream));
+    if (kind == cudaMemcpyHostToDevice) LWM_CUDA(cudaStreamSynchronize(s->ctx->stream));  // host arrays may go away
+    m.B = B;
+    m.h = h;
+    m.history = window;
+    s->batch = B;
+    s->has_context = true;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_lewm_set_context(lwm_scorer* s, uint32_t B, uint32_t h, uint32_t history, const float* emb,
+                                       const float* goal) {
+    return lewm_set_context(s, B, h, history, emb, goal, cudaMemcpyHostToDevice);
+}
+
+lwm_status lwm_scorer_lewm_set_context_device(lwm_scorer* s, uint32_t B, uint32_t h, uint32_t history,
+                                              const float* emb, const float* goal) {
+    return lewm_set_context(s, B, h, history, emb, goal, cudaMemcpyDeviceToDevice);
+}
+
+lwm_status lwm_lewm_encode_vector_device(lwm_scorer* s, const float* obs, uint32_t n, float* out) {
+    if (!s || s->kind != ScorerKind::Lewm || !obs || !out || n == 0) return fail(LWM_INVALID_ARGUMENT, "invalid encode arguments");
+    if (s->lewm->c.encoder != LWM_ENCODER_VECTOR_MLP)
+        return fail(LWM_INVALID_ARGUMENT, "encode_vector called on non-vector observation encoder");
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    LWM_CUDA(s->lewm->encode_vector(obs, n, out, s->ctx->stream));
+    s->ctx->launches += static_cast<uint64_t>(s->lewm->launches);
+    return LWM_OK;
+}
+
+lwm_status lwm_lewm_encode_pixels_device(lwm_scorer* s, const float* pixels, uint32_t n, float* out) {
+    if (!s || s->kind != ScorerKind::Lewm || !pixels || !out || n == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid encode arguments");
+    if (s->lewm->c.encoder != LWM_ENCODER_VIT)
+        return fail(LWM_INVALID_ARGUMENT, "encode_pixels called on non-image observation encoder");
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    LWM_CUDA(s->lewm->encode_pixels(pixels, n, out, s->ctx->stream));
+    s->ctx->launches += static_cast<uint64_t>(s->lewm->launches);
+    return LWM_OK;
+}
+
 lwm_status lwm_scorer_callback_create(lwm_ctx* ctx, uint32_t batch, lwm_score_fn fn, void* user, lwm_scorer** out) {
     if (!ctx || !fn || !out || batch == 0) return fail(LWM_INVALID_ARGUMENT, "invalid callback scorer arguments");
     lwm_scorer* s = new_scorer(ctx, ScorerKind::Callback);
@@ -1198,7 +1302,8 @@ lwm_status lwm_scorer_predict_device(lwm_scorer* s, const float* cand, uint32_t 
     LWM_CUDA(cudaSetDevice(s->ctx->device));
     DevBuf tmp;
     LWM_TRY(tmp.ensure(static_cast<size_t>(B) * S * 4));
-    lwm_status st = score_device(s, cand, B, S, T, 4, tmp.as<float>(), states);
+    const uint32_t A = s->kind == ScorerKind::Lewm ? s->lewm->c.action_dim : 4;
+    lwm_status st = score_device(s, cand, B, S, T, A, tmp.as<float>(), states);
     cudaStreamSynchronize(s->ctx->stream);
     tmp.release();
     return st;
@@ -1208,6 +1313,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     if (!s) return LWM_OK;
     cudaSetDevice(s->ctx->device);
     cudaStreamSynchronize(s->ctx->stream);
+    s->lewm.reset();
     if (s->staged) cudaEventDestroy(s->staged);
     s->weights.release();
     s->ctx_dev.release();

@@ -1,0 +1,418 @@
+// kernels_lewm.cu — kernels of the LeWM / WorldModel scorer (f32).
+//
+// The scorer runs the reference's rollout (src/models/lewm/model.rs:94-147,
+// modules.rs:9-399) as a short sequence of launches per predictor step over
+// ALL candidates at once (rows = B*S*window tokens):
+//   gemm_f32<EPI>   y = x W^T + b with a fused epilogue (GELU, SiLU, gated
+//                   residual x += gate * y with the gate read from the
+//                   precomputed AdaLN table through a row map)
+//   ada_ln_kernel   LN_noaffine -> modulate(shift, scale) -> LN_affine, one
+//                   warp per row (ConditionalBlock::forward, modules.rs:317-330)
+//   attention_kernel causal softmax attention of a short window, one warp per
+//                   (sequence, head, query); a one-token window needs no
+//                   kernel at all (softmax over one key is exactly 1, so the
+//                   attention output is V and only V is projected)
+//   norm_act_kernel  BatchNorm(eval)/LayerNorm + GELU of the MLP hidden layer
+//   + window assembly, goal cost, ViT patchify/assemble/attention.
+// Everything stays in HBM-resident f32 buffers owned by the scorer.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "lwm_device.cuh"
+#include "lwm_lewm.hpp"
+
+namespace lwm {
+
+// ------------------------------------------------------------------ GEMM
+//
+// C[M,N] = A[M,K] (row stride lda) . W[N,K]^T (+ bias), 64x64 tile per
+// 256-thread block, 4x4 outputs per thread, K staged 16 at a time through
+// shared memory (A transposed so a thread's 4 rows are one float4 read).
+// Each output's dot product runs in k order (as the reference's matmul).
+constexpr int kBM = 64, kBN = 64, kBK = 16;
+
+__device__ __forceinline__ float apply_act(int act, float v) {
+    switch (act) {
+        case kActGeluTanh: return gelu_tanh(v);
+        case kActGeluErf: return (0.5f * v) * (1.0f + erff(v * 0.7071067811865476f));
+        case kActSilu: return v / (1.0f + expf(-v));
+        default: return v;
+    }
+}
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
+    __shared__ __align__(16) float As[2][kBK][kBM + 4];
+    __shared__ __align__(16) float Ws[2][kBK][kBN + 4];
+    const int tid = threadIdx.x;
+    const int tx = tid % 16, ty = tid / 16;  // 16 x 16 threads, 4 x 4 outputs each
+    const uint32_t m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    float acc[4][4] = {};
+    // loader mapping: 64 rows x 16 k = 1024 elements per tile, 4 per thread
+    const int lr = tid / 4, lk = (tid % 4) * 4;
+    auto load = [&](int buf, uint32_t k0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t k = k0 + lk + q;
+            const uint32_t m = m0 + lr, n = n0 + lr;
+            As[buf][lk + q][lr] = (m < g.M && k < g.K) ? __ldg(g.A + static_cast<size_t>(m) * g.lda + k) : 0.0f;
+            Ws[buf][lk + q][lr] = (n < g.N && k < g.K) ? __ldg(g.W + static_cast<size_t>(n) * g.ldw + k) : 0.0f;
+        }
+    };
+    load(0, 0);
+    __syncthreads();
+    int buf = 0;
+    for (uint32_t k0 = 0; k0 < g.K; k0 += kBK) {
+        if (k0 + kBK < g.K) load(buf ^ 1, k0 + kBK);
+#pragma unroll
+        for (int kk = 0; kk < kBK; ++kk) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            const float4 w = *reinterpret_cast<const float4*>(&Ws[buf][kk][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+        }
+        __syncthreads();
+        buf ^= 1;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t m = m0 + ty * 4 + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t n = n0 + tx * 4 + j;
+            if (n >= g.N) continue;
+            float v = acc[i][j];
+            if (g.bias) v = v + g.bias[n];
+            float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
+            if (g.residual) {
+                // x = x + gate * y (ConditionalBlock) or x = y + x (ViT layer)
+                if (g.gate) v = g.gate[g.map.row(m) * g.ldg + n] * v;
+                *c = *c + v;
+            } else {
+                *c = apply_act(g.act, v);
+            }
+        }
+    }
+}
+
+cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t stream) {
+    if (g.M == 0 || g.N == 0) return cudaSuccess;
+    dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM);
+    gemm_f32_kernel<<<grid, 256, 0, stream>>>(g);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ row kernels
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Per-row LayerNorm statistics over d elements held by one warp (x in global
+// or shared memory): mean = sum / d, var = sum((x - mean)^2) / d.
+__device__ __forceinline__ void row_stats(const float* x, uint32_t d, float& mean, float& den, float eps) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.0f;
+    for (uint32_t i = lane; i < d; i += 32) s += x[i];
+    mean = warp_sum(s) / static_cast<float>(d);
+    float v = 0.0f;
+    for (uint32_t i = lane; i < d; i += 32) {
+        const float c = x[i] - mean;
+        v += c * c;
+    }
+    den = sqrtf(warp_sum(v) / static_cast<float>(d) + eps);
+}
+
+// y = LN_affine(LN_noaffine(x, 1e-6) * (scale + 1) + shift, 1e-5)
+// shift/scale come from the AdaLN table row map.row(r) at column offsets
+// shift_off / scale_off (modules.rs:317-330, 9-27).
+__global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
+                              uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b) {
+    extern __shared__ float s_row[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    float* t = s_row + static_cast<size_t>(warp) * d;
+    const float* xr = x + static_cast<size_t>(r) * d;
+    float mean, den;
+    row_stats(xr, d, mean, den, 1e-6f);
+    const float* a = ada + map.row(r) * ld_ada;
+    for (uint32_t i = lane; i < d; i += 32) {
+        const float n = (xr[i] - mean) / den;
+        t[i] = n * (a[scale_off + i] + 1.0f) + a[shift_off + i];
+    }
+    __syncwarp();
+    row_stats(t, d, mean, den, 1e-5f);
+    float* yr = y + static_cast<size_t>(r) * d;
+    for (uint32_t i = lane; i < d; i += 32) yr[i] = (t[i] - mean) / den * w[i] + b[i];
+}
+
+// LayerNorm (affine, eps) of rows gathered from src row (r * t_in + pick).
+__global__ void layernorm_kernel(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
+                                 const float* w, const float* b, float eps) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    const float* xr = x + (static_cast<size_t>(r) * t_in + pick) * d;
+    float mean, den;
+    row_stats(xr, d, mean, den, eps);
+    float* yr = y + static_cast<size_t>(r) * d;
+    for (uint32_t i = lane; i < d; i += 32) yr[i] = (xr[i] - mean) / den * w[i] + b[i];
+}
+
+// In place: norm (BatchNorm eval / LayerNorm / none) then GELU (tanh) of an
+// MLP hidden layer (Mlp::forward, modules.rs:108-115; VectorMlpEncoder).
+__global__ void norm_act_kernel(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
+                                const float* rm, const float* rv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    float* xr = x + static_cast<size_t>(r) * d;
+    float mean = 0.0f, den = 1.0f;
+    if (kind == kNormLayer) row_stats(xr, d, mean, den, 1e-5f);
+    __syncwarp();
+    for (uint32_t i = lane; i < d; i += 32) {
+        float v = xr[i];
+        if (kind == kNormLayer) v = (v - mean) / den * w[i] + b[i];
+        else if (kind == kNormBatch) v = (v - rm[i]) / sqrtf(rv[i] + 1e-5f) * w[i] + b[i];
+        xr[i] = gelu_tanh(v);
+    }
+}
+
+__global__ void silu_kernel(const float* x, float* y, size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float v = x[i];
+        y[i] = v / (1.0f + expf(-v));
+    }
+}
+
+// Window tokens of one predictor step: X[(r, w)] = frames[r, lo + w] + pos[w]
+// (rollout_embeddings_with_history, model.rs:128-141; Predictor::forward_last).
+__global__ void window_kernel(const float* frames, uint32_t nframes, const float* pos, float* X, uint32_t rows,
+                              uint32_t w_len, uint32_t lo, uint32_t d) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t total = static_cast<size_t>(rows) * w_len * d;
+    if (i >= total) return;
+    const uint32_t c = static_cast<uint32_t>(i % d);
+    const size_t tok = i / d;
+    const uint32_t w = static_cast<uint32_t>(tok % w_len);
+    const size_t r = tok / w_len;
+    X[i] = frames[(r * nframes + lo + w) * d + c] + pos[static_cast<size_t>(w) * d + c];
+}
+
+// frames[r, slot] = src[r]; frames[r, j] = hist[r / S, j] for j < h (init).
+__global__ void frames_init_kernel(const float* hist, uint32_t h, uint32_t S, float* frames, uint32_t nframes,
+                                   size_t rows, uint32_t d) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * h * d) return;
+    const uint32_t c = static_cast<uint32_t>(i % d);
+    const size_t t = i / d;
+    const uint32_t j = static_cast<uint32_t>(t % h);
+    const size_t r = t / h;
+    frames[(r * nframes + j) * d + c] = hist[((r / S) * h + j) * d + c];
+}
+
+__global__ void frames_put_kernel(const float* src, float* frames, uint32_t nframes, uint32_t slot, size_t rows,
+                                  uint32_t d) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * d) return;
+    const size_t r = i / d;
+    frames[(r * nframes + slot) * d + i % d] = src[i];
+}
+
+// Causal softmax attention of short windows (Attention::forward,
+// modules.rs:245-275): qkv [seqs*t, 3*H*dh] -> out [seqs*t, H*dh]; one warp
+// per (sequence, head, query); q scaled before the dot product as the
+// reference does (q * scale).
+__global__ void attention_kernel(const float* qkv, float* out, uint32_t seqs, uint32_t t, uint32_t H, uint32_t dh,
+                                 float scale, int causal, int scale_q_first) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t gw = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    const size_t total = static_cast<size_t>(seqs) * H * t;
+    if (gw >= total) return;
+    const uint32_t i = static_cast<uint32_t>(gw % t);
+    const uint32_t h = static_cast<uint32_t>((gw / t) % H);
+    const size_t s = gw / (static_cast<size_t>(t) * H);
+    const uint32_t inner = H * dh;
+    const float* base = qkv + s * t * 3 * inner;
+    const float* q = base + static_cast<size_t>(i) * 3 * inner + h * dh;
+    const uint32_t jmax = causal ? i + 1 : t;
+    // pass 1: max score
+    float mx = -INFINITY;
+    for (uint32_t j = 0; j < jmax; ++j) {
+        const float* k = base + static_cast<size_t>(j) * 3 * inner + inner + h * dh;
+        float acc = 0.0f;
+        for (uint32_t d = lane; d < dh; d += 32) acc += (scale_q_first ? q[d] * scale : q[d]) * k[d];
+        acc = warp_sum(acc);
+        if (!scale_q_first) acc *= scale;
+        mx = fmaxf(mx, acc);
+    }
+    // pass 2: weights and output (dh <= 128: 4 accumulators per lane)
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float sum = 0.0f;
+    for (uint32_t j = 0; j < jmax; ++j) {
+        const float* k = base + static_cast<size_t>(j) * 3 * inner + inner + h * dh;
+        float acc = 0.0f;
+        for (uint32_t d = lane; d < dh; d += 32) acc += (scale_q_first ? q[d] * scale : q[d]) * k[d];
+        acc = warp_sum(acc);
+        if (!scale_q_first) acc *= scale;
+        const float p = expf(acc - mx);
+        sum += p;
+        const float* v = base + static_cast<size_t>(j) * 3 * inner + 2 * inner + h * dh;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t d = lane + 32 * u;
+            if (d < dh) o[u] += p * v[d];
+        }
+    }
+    float* orow = out + (s * t + i) * inner + h * dh;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const uint32_t d = lane + 32 * u;
+        if (d < dh) orow[d] = o[u] / sum;
+    }
+}
+
+// Goal cost (goal_cost, model.rs:149-165): sum_d (pred - goal[r / S])^2.
+__global__ void goal_cost_kernel(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
+                                 float* scores) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t r = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    const float* p = pred + r * d;
+    const float* g = goal + (r / S) * d;
+    float acc = 0.0f;
+    for (uint32_t i = lane; i < d; i += 32) {
+        const float e = p[i] - g[i];
+        acc += e * e;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) scores[r] = acc;
+}
+
+// ViT: patches [n, np, C*p*p] from pixels [n, C, img, img] (conv k = stride = p).
+__global__ void patchify_kernel(const float* pix, float* patches, uint32_t n, uint32_t C, uint32_t img, uint32_t p) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t side = img / p, kdim = C * p * p;
+    const size_t total = static_cast<size_t>(n) * side * side * kdim;
+    if (i >= total) return;
+    const uint32_t k = static_cast<uint32_t>(i % kdim);
+    const size_t pt = i / kdim;
+    const uint32_t pidx = static_cast<uint32_t>(pt % (side * side));
+    const size_t im = pt / (side * side);
+    const uint32_t ch = k / (p * p), ky = (k / p) % p, kx = k % p;
+    const uint32_t py = pidx / side, px = pidx % side;
+    patches[i] = pix[((im * C + ch) * img + py * p + ky) * img + px * p + kx];
+}
+
+// tokens [n, 1 + np, vh] = [cls ; patch embeddings] + position embeddings.
+__global__ void vit_assemble_kernel(const float* patch_out, const float* cls, const float* pos, float* x, uint32_t n,
+                                    uint32_t np, uint32_t vh) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t total = static_cast<size_t>(n) * (np + 1) * vh;
+    if (i >= total) return;
+    const uint32_t c = static_cast<uint32_t>(i % vh);
+    const size_t tok = i / vh;
+    const uint32_t t = static_cast<uint32_t>(tok % (np + 1));
+    const size_t im = tok / (np + 1);
+    const float v = t == 0 ? cls[c] : patch_out[(im * np + t - 1) * vh + c];
+    x[i] = v + pos[static_cast<size_t>(t) * vh + c];
+}
+
+// ------------------------------------------------------------- launchers
+
+static inline uint32_t blocks_for(size_t n, uint32_t per) { return static_cast<uint32_t>((n + per - 1) / per); }
+
+cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
+                          uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b,
+                          cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    constexpr int kWarps = 8;
+    ada_ln_kernel<<<blocks_for(rows, kWarps), kWarps * 32, kWarps * d * sizeof(float), s>>>(
+        x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
+                             const float* w, const float* b, float eps, cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    layernorm_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, y, rows, d, t_in, pick, w, b, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm_act(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
+                            const float* rm, const float* rv, cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    norm_act_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, rows, d, kind, w, b, rm, rv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_silu(const float* x, float* y, size_t n, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    silu_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_window(const float* frames, uint32_t nframes, const float* pos, float* X, uint32_t rows,
+                          uint32_t w_len, uint32_t lo, uint32_t d, cudaStream_t s) {
+    const size_t n = static_cast<size_t>(rows) * w_len * d;
+    if (!n) return cudaSuccess;
+    window_kernel<<<blocks_for(n, 256), 256, 0, s>>>(frames, nframes, pos, X, rows, w_len, lo, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_frames_init(const float* hist, uint32_t h, uint32_t S, float* frames, uint32_t nframes,
+                               size_t rows, uint32_t d, cudaStream_t s) {
+    const size_t n = rows * h * d;
+    if (!n) return cudaSuccess;
+    frames_init_kernel<<<blocks_for(n, 256), 256, 0, s>>>(hist, h, S, frames, nframes, rows, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_frames_put(const float* src, float* frames, uint32_t nframes, uint32_t slot, size_t rows,
+                              uint32_t d, cudaStream_t s) {
+    const size_t n = rows * d;
+    if (!n) return cudaSuccess;
+    frames_put_kernel<<<blocks_for(n, 256), 256, 0, s>>>(src, frames, nframes, slot, rows, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32_t t, uint32_t H, uint32_t dh,
+                             float scale, int causal, int scale_q_first, cudaStream_t s) {
+    const size_t warps = static_cast<size_t>(seqs) * H * t;
+    if (!warps) return cudaSuccess;
+    attention_kernel<<<blocks_for(warps, 8), 256, 0, s>>>(qkv, out, seqs, t, H, dh, scale, causal, scale_q_first);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_goal_cost(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
+                             float* scores, cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    goal_cost_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(pred, goal, S, rows, d, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_patchify(const float* pix, float* patches, uint32_t n, uint32_t C, uint32_t img, uint32_t p,
+                            cudaStream_t s) {
+    const size_t total = static_cast<size_t>(n) * (img / p) * (img / p) * C * p * p;
+    if (!total) return cudaSuccess;
+    patchify_kernel<<<blocks_for(total, 256), 256, 0, s>>>(pix, patches, n, C, img, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_vit_assemble(const float* patch_out, const float* cls, const float* pos, float* x, uint32_t n,
+                                uint32_t np, uint32_t vh, cudaStream_t s) {
+    const size_t total = static_cast<size_t>(n) * (np + 1) * vh;
+    if (!total) return cudaSuccess;
+    vit_assemble_kernel<<<blocks_for(total, 256), 256, 0, s>>>(patch_out, cls, pos, x, n, np, vh);
+    return cudaGetLastError();
+}
+
+}  // namespace lwm

@@ -1,0 +1,508 @@
+// lewm_model.cpp — host side of the LeWM / WorldModel scorer: model presets,
+// the weight-blob layout and seeded init, and the launch sequence of one
+// scoring call (every candidate of every vehicle in each launch).
+//
+// Reference: LeWm / WorldModel (src/models/lewm/model.rs:20-165,
+// src/models/world_model/model.rs:19-160), LeWmSession::score_candidates
+// (src/session.rs:46-66), modules.rs:9-399, vit.rs:7-57.
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "lwm_lewm.hpp"
+
+namespace lwm {
+
+namespace {
+
+struct Spec {
+    size_t off, n;
+    int kind;      // 0 Linear weight (Kaiming normal), 1 bias U(+-1/sqrt(fan)), 2 ones, 3 zeros, 4 N(0, 0.02^2)
+    uint32_t fan;
+};
+
+struct Walker {
+    const float* base;
+    size_t off = 0;
+    std::vector<Spec>* specs;
+    const float* take(size_t n, int kind, uint32_t fan) {
+        if (specs) specs->push_back({off, n, kind, fan});
+        const float* p = base ? base + off : nullptr;
+        off += n;
+        return p;
+    }
+    Lin lin(uint32_t out, uint32_t in, bool bias) {
+        Lin l;
+        l.out = out;
+        l.in = in;
+        l.w = take(static_cast<size_t>(out) * in, 0, in);
+        l.b = bias ? take(out, 1, in) : nullptr;
+        return l;
+    }
+    Norm norm(int kind, uint32_t d) {
+        Norm n;
+        n.kind = kind;
+        if (kind == kNormBatch) {
+            n.w = take(d, 2, 0);
+            n.b = take(d, 3, 0);
+            n.rm = take(d, 3, 0);
+            n.rv = take(d, 2, 0);
+        } else if (kind == kNormLayer) {
+            n.w = take(d, 2, 0);
+            n.b = take(d, 3, 0);
+        }
+        return n;
+    }
+    MlpW mlp(uint32_t in, uint32_t hid, uint32_t out, int norm_kind) {
+        MlpW m;
+        m.fc1 = lin(hid, in, true);
+        m.norm = norm(norm_kind, hid);
+        m.fc2 = lin(out, hid, true);
+        return m;
+    }
+};
+
+size_t walk(const lwm_lewm_config& c, const float* base, LewmWeights* out, std::vector<Spec>* specs) {
+    LewmWeights w;
+    Walker k{base, 0, specs};
+    const uint32_t D = c.embed_dim, hid = c.pred_hidden_dim, inner = c.heads * c.dim_head;
+    w.act_conv = k.lin(c.smoothed_dim, c.action_dim, true);
+    w.act_fc1 = k.lin(c.action_mlp_scale * D, c.smoothed_dim, true);
+    w.act_fc2 = k.lin(D, c.action_mlp_scale * D, true);
+    w.pos = k.take(static_cast<size_t>(c.num_frames) * D, 4, 0);
+    w.has_proj = hid != D;
+    if (w.has_proj) {
+        w.input_proj = k.lin(hid, D, true);
+        w.cond_proj = k.lin(hid, D, true);
+    }
+    w.blocks.resize(c.depth);
+    for (uint32_t l = 0; l < c.depth; ++l) {
+        BlockW& b = w.blocks[l];
+        b.attn_norm = k.norm(kNormLayer, hid);
+        b.qkv = k.lin(3 * inner, hid, false);
+        b.to_out = k.lin(hid, inner, true);
+        b.mlp_norm = k.norm(kNormLayer, hid);
+        b.fc1 = k.lin(c.mlp_dim, hid, true);
+        b.fc2 = k.lin(hid, c.mlp_dim, true);
+        b.ada = k.lin(6 * hid, hid, true);
+    }
+    w.final_norm = k.norm(kNormLayer, hid);
+    if (w.has_proj) w.output_proj = k.lin(D, hid, true);
+    w.pred_proj = k.mlp(D, c.pred_proj_hidden, D, c.pred_proj_norm);
+    if (c.encoder == LWM_ENCODER_VECTOR_MLP) {
+        const int nk = c.obs_norm == LWM_NORM_NONE ? kNormNone : kNormLayer;
+        w.enc_lin.resize(c.obs_depth);
+        w.enc_norm.resize(c.obs_depth);
+        for (uint32_t j = 0; j < c.obs_depth; ++j) {
+            const uint32_t in = j == 0 ? c.obs_dim : c.obs_hidden_dim;
+            const uint32_t o = j + 1 == c.obs_depth ? D : c.obs_hidden_dim;
+            w.enc_lin[j] = k.lin(o, in, true);
+            if (j + 1 < c.obs_depth) w.enc_norm[j] = k.norm(nk, c.obs_hidden_dim);
+        }
+    } else {
+        const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p;
+        w.cls = k.take(vh, 4, 0);
+        w.vpos = k.take(static_cast<size_t>(side * side + 1) * vh, 4, 0);
+        w.patch = k.lin(vh, c.channels * p * p, true);
+        w.vit.resize(c.vit_layers);
+        for (uint32_t l = 0; l < c.vit_layers; ++l) {
+            VitBlockW& b = w.vit[l];
+            b.ln1 = k.norm(kNormLayer, vh);
+            b.q = k.lin(vh, vh, c.qkv_bias != 0);
+            b.k = k.lin(vh, vh, c.qkv_bias != 0);
+            b.v = k.lin(vh, vh, c.qkv_bias != 0);
+            b.o = k.lin(vh, vh, true);
+            b.ln2 = k.norm(kNormLayer, vh);
+            b.fc1 = k.lin(c.vit_mlp, vh, true);
+            b.fc2 = k.lin(vh, c.vit_mlp, true);
+        }
+        w.vit_norm = k.norm(kNormLayer, vh);
+        w.projector = k.mlp(vh, c.projector_hidden, D, c.projector_norm);
+    }
+    w.count = k.off;
+    if (out) *out = w;
+    return k.off;
+}
+
+// SplitMix64 stream and Box-Muller normals for the seeded init.
+struct Mix {
+    uint64_t s;
+    uint64_t next() {
+        s += 0x9E3779B97F4A7C15ull;
+        uint64_t v = s;
+        v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ull;
+        v = (v ^ (v >> 27)) * 0x94D049BB133111EBull;
+        return v ^ (v >> 31);
+    }
+    double unit() { return (static_cast<double>(next() >> 11) + 0.5) * (1.0 / 9007199254740992.0); }
+    double normal() { return std::sqrt(-2.0 * std::log(unit())) * std::cos(6.283185307179586 * unit()); }
+};
+
+}  // namespace
+
+size_t lewm_walk(const lwm_lewm_config& c, const float* base, LewmWeights* out) { return walk(c, base, out, nullptr); }
+
+bool lewm_config_valid(const lwm_lewm_config& c, const char** why) {
+    auto bad = [&](const char* m) { *why = m; return false; };
+    if (!c.embed_dim || !c.action_dim || !c.smoothed_dim || !c.action_mlp_scale) return bad("LeWM dims must be > 0");
+    if (!c.history_size || c.num_frames < c.history_size)
+        return bad("predictor.num_frames must be >= history_size > 0");
+    if (!c.pred_hidden_dim || !c.depth || !c.heads || !c.dim_head || !c.mlp_dim || !c.pred_proj_hidden)
+        return bad("LeWM predictor dims must be > 0");
+    if (c.dim_head > 128) return bad("dim_head must be <= 128");
+    if (c.pred_hidden_dim > 1024 || c.embed_dim > 2048) return bad("pred_hidden_dim must be <= 1024 and embed_dim <= 2048");
+    if (c.pred_proj_norm < 0 || c.pred_proj_norm > 2) return bad("unknown pred_proj norm");
+    if (c.encoder == LWM_ENCODER_VECTOR_MLP) {
+        if (c.obs_depth < 2) return bad("VectorMlp depth must be at least 2");
+        if (!c.obs_dim || !c.obs_hidden_dim) return bad("VectorMlp dims must be > 0");
+    } else if (c.encoder == LWM_ENCODER_VIT) {
+        if (!c.patch_size || c.image_size % c.patch_size) return bad("image_size must be a multiple of patch_size");
+        if (!c.vit_heads || c.vit_hidden % c.vit_heads) return bad("vit_hidden must be a multiple of vit_heads");
+        if (c.vit_hidden / c.vit_heads > 128) return bad("ViT head dim must be <= 128");
+        if (!c.channels || !c.vit_layers || !c.vit_mlp || !c.projector_hidden) return bad("ViT dims must be > 0");
+        if (c.projector_norm < 0 || c.projector_norm > 2) return bad("unknown projector norm");
+    } else {
+        return bad("unknown observation encoder");
+    }
+    return true;
+}
+
+cudaError_t Arena::ensure(size_t n) {
+    if (n <= floats) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&ptr, n * sizeof(float));
+    if (e == cudaSuccess) floats = n;
+    return e;
+}
+
+void Arena::release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    floats = 0;
+}
+
+LewmModel::~LewmModel() {
+    ws.release();
+    enc.release();
+    if (blob) cudaFree(blob);
+    if (emb) cudaFree(emb);
+    if (goal) cudaFree(goal);
+}
+
+namespace {
+
+#define LWM_CU(x)                              \
+    do {                                       \
+        const cudaError_t e_ = (x);            \
+        if (e_ != cudaSuccess) return e_;      \
+    } while (0)
+
+GemmArgs gemm(const float* A, uint32_t lda, const Lin& l, float* C, uint32_t ldc, uint32_t M, int act = kActNone) {
+    GemmArgs g{};
+    g.A = A;
+    g.W = l.w;
+    g.bias = l.b;
+    g.C = C;
+    g.M = M;
+    g.N = l.out;
+    g.K = l.in;
+    g.lda = lda;
+    g.ldw = l.in;
+    g.ldc = ldc;
+    g.act = act;
+    return g;
+}
+
+// Mlp::forward on the device: fc1 -> norm + GELU -> fc2.
+cudaError_t mlp(const MlpW& m, const float* x, uint32_t n, float* hid, float* out, cudaStream_t s, int& launches) {
+    LWM_CU(gemm_f32(gemm(x, m.fc1.in, m.fc1, hid, m.fc1.out, n), s));
+    LWM_CU(launch_norm_act(hid, n, m.fc1.out, m.norm.kind, m.norm.w, m.norm.b, m.norm.rm, m.norm.rv, s));
+    LWM_CU(gemm_f32(gemm(hid, m.fc1.out, m.fc2, out, m.fc2.out, n), s));
+    launches += 3;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb,
+                             cudaStream_t s) {
+    const uint32_t D = c.embed_dim, hid = c.pred_hidden_dim, inner = c.heads * c.dim_head, A = c.action_dim;
+    const uint32_t sm = c.smoothed_dim, ah = c.action_mlp_scale * D, ph = c.pred_proj_hidden;
+    const size_t bs = static_cast<size_t>(B) * S, all = bs * T;
+    const uint32_t W = history;  // window tokens per sequence (at most)
+    const uint32_t nframes = T + 1;
+    // workspace layout (floats)
+    size_t off = 0;
+    auto take = [&](size_t n) { const size_t o = off; off += (n + 63) & ~static_cast<size_t>(63); return o; };
+    const size_t o_sm = take(all * sm), o_ah = take(all * ah), o_act = take(all * D), o_cond = take(all * hid);
+    const size_t o_ada = take(static_cast<size_t>(c.depth) * all * 6 * hid);
+    const size_t o_frames = take(bs * nframes * D), o_X = take(bs * W * D), o_x = take(bs * W * hid);
+    const size_t o_y = take(bs * W * hid), o_qkv = take(bs * W * 3 * inner), o_att = take(bs * W * inner);
+    const size_t o_f = take(bs * W * c.mlp_dim), o_last = take(bs * hid), o_po = take(bs * D);
+    const size_t o_p1 = take(bs * ph), o_pred = take(bs * D);
+    LWM_CU(ws.ensure(off));
+    float* base = ws.ptr;
+    float *f_sm = base + o_sm, *f_ah = base + o_ah, *f_act = base + o_act, *f_cond = base + o_cond;
+    float *f_ada = base + o_ada, *f_frames = base + o_frames, *f_X = base + o_X, *f_x = base + o_x;
+    float *f_y = base + o_y, *f_qkv = base + o_qkv, *f_att = base + o_att, *f_f = base + o_f;
+    float *f_last = base + o_last, *f_po = base + o_po, *f_p1 = base + o_p1, *f_pred = base + o_pred;
+    int n = 0;
+    const uint32_t rows_all = static_cast<uint32_t>(all);
+    // ActionEmbedder over every (sample, time) token (modules.rs:150-158)
+    LWM_CU(gemm_f32(gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
+    LWM_CU(gemm_f32(gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
+    LWM_CU(gemm_f32(gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
+    n += 3;
+    // cond -> SiLU -> AdaLN table of every layer (ConditionalBlock::forward, modules.rs:317-320);
+    // the condition of a token depends only on its action, so the table is
+    // built once per scoring call for all (sample, time) tokens.
+    const float* cond = f_act;
+    if (w.has_proj) {
+        LWM_CU(gemm_f32(gemm(f_act, D, w.cond_proj, f_cond, hid, rows_all), s));
+        ++n;
+        cond = f_cond;
+    }
+    LWM_CU(launch_silu(cond, f_cond, all * hid, s));
+    ++n;
+    for (uint32_t l = 0; l < c.depth; ++l) {
+        LWM_CU(gemm_f32(gemm(f_cond, hid, w.blocks[l].ada, f_ada + static_cast<size_t>(l) * all * 6 * hid, 6 * hid,
+                             rows_all), s));
+        ++n;
+    }
+    LWM_CU(launch_frames_init(emb, h, S, f_frames, nframes, bs, D, s));
+    ++n;
+    const float scale = static_cast<float>(std::pow(static_cast<double>(c.dim_head), -0.5));
+    uint32_t count = h;
+    for (uint32_t step = 0; step + h <= T; ++step) {
+        const uint32_t upper = h + step, lo = upper > history ? upper - history : 0, wl = upper - lo;
+        const uint32_t rows = static_cast<uint32_t>(bs * wl);
+        RowMap map;
+        map.t = wl;
+        map.T = T;
+        map.lo = lo;
+        LWM_CU(launch_window(f_frames, nframes, w.pos, f_X, static_cast<uint32_t>(bs), wl, lo, D, s));
+        ++n;
+        float* x = f_X;
+        if (w.has_proj) {
+            LWM_CU(gemm_f32(gemm(f_X, D, w.input_proj, f_x, hid, rows), s));
+            ++n;
+            x = f_x;
+        }
+        for (uint32_t l = 0; l < c.depth; ++l) {
+            const BlockW& b = w.blocks[l];
+            const float* ada = f_ada + static_cast<size_t>(l) * all * 6 * hid;
+            LWM_CU(launch_ada_ln(x, f_y, rows, hid, ada, 6 * hid, 0, hid, map, b.attn_norm.w, b.attn_norm.b, s));
+            const float* att;
+            uint32_t ld_att;
+            if (wl == 1) {
+                // softmax over a single key is exactly 1: the attention output is V
+                Lin v = b.qkv;
+                v.w = b.qkv.w + static_cast<size_t>(2) * inner * hid;
+                v.out = inner;
+                LWM_CU(gemm_f32(gemm(f_y, hid, v, f_att, inner, rows), s));
+                n += 2;
+                att = f_att;
+                ld_att = inner;
+            } else {
+                LWM_CU(gemm_f32(gemm(f_y, hid, b.qkv, f_qkv, 3 * inner, rows), s));
+                LWM_CU(launch_attention(f_qkv, f_att, static_cast<uint32_t>(bs), wl, c.heads, c.dim_head, scale, 1, 1,
+                                        s));
+                n += 3;
+                att = f_att;
+                ld_att = inner;
+            }
+            GemmArgs go = gemm(att, ld_att, b.to_out, x, hid, rows);
+            go.residual = 1;
+            go.gate = ada + 2 * hid;
+            go.ldg = 6 * hid;
+            go.map = map;
+            LWM_CU(gemm_f32(go, s));
+            LWM_CU(launch_ada_ln(x, f_y, rows, hid, ada, 6 * hid, 3 * hid, 4 * hid, map, b.mlp_norm.w, b.mlp_norm.b,
+                                 s));
+            LWM_CU(gemm_f32(gemm(f_y, hid, b.fc1, f_f, c.mlp_dim, rows, kActGeluTanh), s));
+            GemmArgs g2 = gemm(f_f, c.mlp_dim, b.fc2, x, hid, rows);
+            g2.residual = 1;
+            g2.gate = ada + 5 * hid;
+            g2.ldg = 6 * hid;
+            g2.map = map;
+            LWM_CU(gemm_f32(g2, s));
+            n += 4;
+        }
+        // last token -> norm -> output_proj -> pred_proj (Transformer::forward_last, modules.rs:369-380)
+        LWM_CU(launch_layernorm(x, f_last, static_cast<uint32_t>(bs), hid, wl, wl - 1, w.final_norm.w, w.final_norm.b,
+                                1e-5f, s));
+        ++n;
+        const float* pin = f_last;
+        if (w.has_proj) {
+            LWM_CU(gemm_f32(gemm(f_last, hid, w.output_proj, f_po, D, static_cast<uint32_t>(bs)), s));
+            ++n;
+            pin = f_po;
+        }
+        LWM_CU(mlp(w.pred_proj, pin, static_cast<uint32_t>(bs), f_p1, f_pred, s, n));
+        LWM_CU(launch_frames_put(f_pred, f_frames, nframes, count, bs, D, s));
+        ++n;
+        ++count;
+    }
+    LWM_CU(launch_goal_cost(f_pred, goal, S, bs, D, scores, s));
+    ++n;
+    if (last_emb) LWM_CU(cudaMemcpyAsync(last_emb, f_pred, bs * D * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    launches = n;
+    return cudaSuccess;
+}
+
+cudaError_t LewmModel::encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s) {
+    const uint32_t oh = c.obs_hidden_dim;
+    LWM_CU(enc.ensure(static_cast<size_t>(2) * n * oh));
+    float *a = enc.ptr, *b = enc.ptr + static_cast<size_t>(n) * oh;
+    int k = 0;
+    LWM_CU(gemm_f32(gemm(obs, c.obs_dim, w.enc_lin[0], a, oh, n), s));
+    ++k;
+    for (uint32_t j = 0; j + 1 < c.obs_depth; ++j) {
+        const Norm& nm = w.enc_norm[j];
+        LWM_CU(launch_norm_act(a, n, oh, nm.kind, nm.w, nm.b, nullptr, nullptr, s));
+        ++k;
+        if (j + 2 < c.obs_depth) {
+            LWM_CU(gemm_f32(gemm(a, oh, w.enc_lin[j + 1], b, oh, n), s));
+            ++k;
+            float* t = a;
+            a = b;
+            b = t;
+        }
+    }
+    LWM_CU(gemm_f32(gemm(a, oh, w.enc_lin[c.obs_depth - 1], out, c.embed_dim, n), s));
+    launches = k + 1;
+    return cudaSuccess;
+}
+
+cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, cudaStream_t s) {
+    const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p, np = side * side, t = np + 1;
+    const uint32_t kdim = c.channels * p * p, H = c.vit_heads, dh = vh / H;
+    size_t off = 0;
+    auto take = [&](size_t k) { const size_t o = off; off += (k + 63) & ~static_cast<size_t>(63); return o; };
+    const size_t o_patch = take(static_cast<size_t>(n) * np * kdim), o_pe = take(static_cast<size_t>(n) * np * vh);
+    const size_t o_x = take(static_cast<size_t>(n) * t * vh), o_y = take(static_cast<size_t>(n) * t * vh);
+    const size_t o_qkv = take(static_cast<size_t>(n) * t * 3 * vh), o_att = take(static_cast<size_t>(n) * t * vh);
+    const size_t o_f = take(static_cast<size_t>(n) * t * c.vit_mlp), o_cls = take(static_cast<size_t>(n) * vh);
+    const size_t o_ph = take(static_cast<size_t>(n) * c.projector_hidden);
+    LWM_CU(enc.ensure(off));
+    float* e = enc.ptr;
+    float *f_patch = e + o_patch, *f_pe = e + o_pe, *f_x = e + o_x, *f_y = e + o_y, *f_qkv = e + o_qkv;
+    float *f_att = e + o_att, *f_f = e + o_f, *f_cls = e + o_cls, *f_ph = e + o_ph;
+    const uint32_t rows = n * t;
+    int k = 0;
+    LWM_CU(launch_patchify(pix, f_patch, n, c.channels, c.image_size, p, s));
+    LWM_CU(gemm_f32(gemm(f_patch, kdim, w.patch, f_pe, vh, n * np), s));
+    LWM_CU(launch_vit_assemble(f_pe, w.cls, w.vpos, f_x, n, np, vh, s));
+    k += 3;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
+    for (uint32_t l = 0; l < c.vit_layers; ++l) {
+        const VitBlockW& b = w.vit[l];
+        LWM_CU(launch_layernorm(f_x, f_y, rows, vh, 1, 0, b.ln1.w, b.ln1.b, c.vit_eps, s));
+        LWM_CU(gemm_f32(gemm(f_y, vh, b.q, f_qkv, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(gemm(f_y, vh, b.k, f_qkv + vh, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(gemm(f_y, vh, b.v, f_qkv + 2 * vh, 3 * vh, rows), s));
+        LWM_CU(launch_attention(f_qkv, f_att, n, t, H, dh, scale, 0, 0, s));
+        GemmArgs go = gemm(f_att, vh, b.o, f_x, vh, rows);
+        go.residual = 1;
+        LWM_CU(gemm_f32(go, s));
+        LWM_CU(launch_layernorm(f_x, f_y, rows, vh, 1, 0, b.ln2.w, b.ln2.b, c.vit_eps, s));
+        LWM_CU(gemm_f32(gemm(f_y, vh, b.fc1, f_f, c.vit_mlp, rows, kActGeluErf), s));
+        GemmArgs g2 = gemm(f_f, c.vit_mlp, b.fc2, f_x, vh, rows);
+        g2.residual = 1;
+        LWM_CU(gemm_f32(g2, s));
+        k += 9;
+    }
+    LWM_CU(launch_layernorm(f_x, f_cls, n, vh, t, 0, w.vit_norm.w, w.vit_norm.b, c.vit_eps, s));
+    ++k;
+    LWM_CU(mlp(w.projector, f_cls, n, f_ph, out, s, k));
+    launches = k;
+    return cudaSuccess;
+}
+
+}  // namespace lwm
+
+// ----------------------------------------------------------------- C ABI
+
+extern "C" {
+
+void lwm_lewm_config_vector(lwm_lewm_config* o) {
+    std::memset(o, 0, sizeof *o);
+    o->embed_dim = 192;
+    o->action_dim = 2;
+    o->smoothed_dim = 2;
+    o->action_mlp_scale = 4;
+    o->history_size = 1;
+    o->num_frames = 1;
+    o->pred_hidden_dim = 192;
+    o->depth = 4;
+    o->heads = 8;
+    o->dim_head = 32;
+    o->mlp_dim = 768;
+    o->pred_proj_hidden = 512;
+    o->pred_proj_norm = LWM_NORM_LAYER;
+    o->encoder = LWM_ENCODER_VECTOR_MLP;
+    o->obs_dim = 16;
+    o->obs_hidden_dim = 512;
+    o->obs_depth = 3;
+    o->obs_norm = LWM_NORM_LAYER;
+}
+
+void lwm_lewm_config_image(lwm_lewm_config* o) {
+    std::memset(o, 0, sizeof *o);
+    o->embed_dim = 192;
+    o->action_dim = 2;
+    o->smoothed_dim = 2;
+    o->action_mlp_scale = 4;
+    o->history_size = 1;
+    o->num_frames = 1;
+    o->pred_hidden_dim = 192;
+    o->depth = 6;
+    o->heads = 16;
+    o->dim_head = 64;
+    o->mlp_dim = 2048;
+    o->pred_proj_hidden = 2048;
+    o->pred_proj_norm = LWM_NORM_BATCH;
+    o->encoder = LWM_ENCODER_VIT;
+    o->image_size = 224;
+    o->patch_size = 16;
+    o->vit_hidden = 192;
+    o->vit_layers = 12;
+    o->vit_heads = 3;
+    o->vit_mlp = 768;
+    o->vit_eps = 1e-12f;
+    o->channels = 3;
+    o->qkv_bias = 1;
+    o->projector_hidden = 2048;
+    o->projector_norm = LWM_NORM_BATCH;
+}
+
+size_t lwm_lewm_weight_count(const lwm_lewm_config* c) {
+    const char* why = nullptr;
+    if (!c || !lwm::lewm_config_valid(*c, &why)) return 0;
+    return lwm::lewm_walk(*c, nullptr, nullptr);
+}
+
+lwm_status lwm_lewm_random_weights(const lwm_lewm_config* c, uint64_t seed, float* out, size_t count) {
+    const char* why = nullptr;
+    if (!c || !out || !lwm::lewm_config_valid(*c, &why)) return LWM_INVALID_ARGUMENT;
+    std::vector<lwm::Spec> specs;
+    const size_t n = lwm::walk(*c, nullptr, nullptr, &specs);
+    if (count != n) return LWM_INVALID_ARGUMENT;
+    lwm::Mix rng{seed ^ 0x6C65776D2D776D31ull};
+    for (const lwm::Spec& sp : specs) {
+        for (size_t j = 0; j < sp.n; ++j) {
+            double v = 0.0;
+            switch (sp.kind) {
+                case 0: v = rng.normal() * std::sqrt(2.0 / sp.fan); break;
+                case 1: v = (2.0 * rng.unit() - 1.0) / std::sqrt(static_cast<double>(sp.fan)); break;
+                case 2: v = 1.0; break;
+                case 3: v = 0.0; break;
+                default: v = rng.normal() * 0.02; break;
+            }
+            out[sp.off + j] = static_cast<float>(v);
+        }
+    }
+    return LWM_OK;
+}
+
+}  // extern "C"

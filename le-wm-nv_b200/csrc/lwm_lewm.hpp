@@ -1,0 +1,138 @@
+// lwm_lewm.hpp — the LeWM / WorldModel scorer: kernel interfaces and the
+// host-side model (device weight views, workspaces, the launch sequence).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "../../include/lewm_b200.h"
+
+namespace lwm {
+
+constexpr int kActNone = 0, kActGeluTanh = 1, kActGeluErf = 2, kActSilu = 3;
+constexpr int kNormBatch = LWM_NORM_BATCH, kNormLayer = LWM_NORM_LAYER, kNormNone = LWM_NORM_NONE;
+
+// Row r of a window batch ([seqs, t] tokens) -> row of a per-(sample, time)
+// table ([seqs, T] rows): (r / t) * T + lo + r % t.  t == 0: identity.
+struct RowMap {
+    uint32_t t = 0, T = 0, lo = 0;
+    __host__ __device__ size_t row(size_t r) const {
+        return t == 0 ? r : (r / t) * T + lo + r % t;
+    }
+};
+
+struct GemmArgs {
+    const float* A;       // [M, K], row stride lda
+    const float* W;       // [N, K], row stride ldw
+    const float* bias;    // [N] or nullptr
+    float* C;             // [M, N], row stride ldc
+    uint32_t M, N, K, lda, ldw, ldc;
+    int act;              // kAct* (ignored with residual)
+    int residual;         // C += (gate ?) * (A W^T + b)
+    const float* gate;    // gate table, row map.row(m), stride ldg, or nullptr
+    uint32_t ldg;
+    RowMap map;
+};
+
+cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t s);
+cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
+                          uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b,
+                          cudaStream_t s);
+cudaError_t launch_layernorm(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
+                             const float* w, const float* b, float eps, cudaStream_t s);
+cudaError_t launch_norm_act(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
+                            const float* rm, const float* rv, cudaStream_t s);
+cudaError_t launch_silu(const float* x, float* y, size_t n, cudaStream_t s);
+cudaError_t launch_window(const float* frames, uint32_t nframes, const float* pos, float* X, uint32_t rows,
+                          uint32_t w_len, uint32_t lo, uint32_t d, cudaStream_t s);
+cudaError_t launch_frames_init(const float* hist, uint32_t h, uint32_t S, float* frames, uint32_t nframes,
+                               size_t rows, uint32_t d, cudaStream_t s);
+cudaError_t launch_frames_put(const float* src, float* frames, uint32_t nframes, uint32_t slot, size_t rows,
+                              uint32_t d, cudaStream_t s);
+cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32_t t, uint32_t H, uint32_t dh,
+                             float scale, int causal, int scale_q_first, cudaStream_t s);
+cudaError_t launch_goal_cost(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
+                             float* scores, cudaStream_t s);
+cudaError_t launch_patchify(const float* pix, float* patches, uint32_t n, uint32_t C, uint32_t img, uint32_t p,
+                            cudaStream_t s);
+cudaError_t launch_vit_assemble(const float* patch_out, const float* cls, const float* pos, float* x, uint32_t n,
+                                uint32_t np, uint32_t vh, cudaStream_t s);
+
+// ------------------------------------------------------------ host model
+
+struct Lin {
+    const float* w = nullptr;
+    const float* b = nullptr;
+    uint32_t out = 0, in = 0;
+};
+struct Norm {
+    int kind = kNormNone;
+    const float *w = nullptr, *b = nullptr, *rm = nullptr, *rv = nullptr;
+};
+struct MlpW {
+    Lin fc1;
+    Norm norm;
+    Lin fc2;
+};
+struct BlockW {
+    Norm attn_norm, mlp_norm;
+    Lin qkv, to_out, fc1, fc2, ada;
+};
+struct VitBlockW {
+    Norm ln1, ln2;
+    Lin q, k, v, o, fc1, fc2;
+};
+
+// Tensor views into one weight blob (host walk of the documented order); with
+// base == nullptr only the float count is computed.
+struct LewmWeights {
+    Lin act_conv, act_fc1, act_fc2;
+    const float* pos = nullptr;
+    bool has_proj = false;
+    Lin input_proj, cond_proj, output_proj;
+    std::vector<BlockW> blocks;
+    Norm final_norm;
+    MlpW pred_proj;
+    std::vector<Lin> enc_lin;
+    std::vector<Norm> enc_norm;
+    const float *cls = nullptr, *vpos = nullptr;
+    Lin patch;
+    std::vector<VitBlockW> vit;
+    Norm vit_norm;
+    MlpW projector;
+    size_t count = 0;
+};
+size_t lewm_walk(const lwm_lewm_config& c, const float* base, LewmWeights* out);
+bool lewm_config_valid(const lwm_lewm_config& c, const char** why);
+
+// Grow-only device workspace.
+struct Arena {
+    float* ptr = nullptr;
+    size_t floats = 0;
+    cudaError_t ensure(size_t n);
+    void release();
+};
+
+struct LewmModel {
+    lwm_lewm_config c{};
+    LewmWeights w;
+    float* blob = nullptr;  // device weights
+    // per-plan context
+    uint32_t B = 0, h = 0, history = 0;
+    float* emb = nullptr;   // [B, h, D]
+    float* goal = nullptr;  // [B, D]
+    size_t ctx_cap = 0;
+    Arena ws;               // rollout workspace
+    Arena enc;              // encoder workspace
+    int launches = 0;
+    ~LewmModel();
+    // scores [B,S] of candidates [B,S,T,A] (all device)
+    cudaError_t score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
+    cudaError_t encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s);
+    cudaError_t encode_pixels(const float* pixels, uint32_t n, float* out, cudaStream_t s);
+};
+
+}  // namespace lwm

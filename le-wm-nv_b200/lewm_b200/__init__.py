@@ -166,6 +166,43 @@ class SkyJepaConfig(C.Structure):
         return out
 
 
+class LewmConfig(C.Structure):
+    """LeWmConfig / WorldModelConfig (src/models/lewm/config.rs, src/models/world_model/config.rs)."""
+    _fields_ = [(n, U32) for n in ("embed_dim", "action_dim", "smoothed_dim", "action_mlp_scale", "history_size",
+                                   "num_frames", "pred_hidden_dim", "depth", "heads", "dim_head", "mlp_dim",
+                                   "pred_proj_hidden")] + \
+               [("pred_proj_norm", I32), ("encoder", I32), ("obs_dim", U32), ("obs_hidden_dim", U32),
+                ("obs_depth", U32), ("obs_norm", I32), ("image_size", U32), ("patch_size", U32),
+                ("vit_hidden", U32), ("vit_layers", U32), ("vit_heads", U32), ("vit_mlp", U32), ("vit_eps", F),
+                ("channels", U32), ("qkv_bias", I32), ("projector_hidden", U32), ("projector_norm", I32)]
+
+    @staticmethod
+    def vector() -> "LewmConfig":
+        c = LewmConfig()
+        lib.lwm_lewm_config_vector(C.byref(c))
+        return c
+
+    @staticmethod
+    def image() -> "LewmConfig":
+        c = LewmConfig()
+        lib.lwm_lewm_config_image(C.byref(c))
+        return c
+
+    def weight_count(self) -> int:
+        return int(lib.lwm_lewm_weight_count(C.byref(self)))
+
+    def random_weights(self, seed: int) -> np.ndarray:
+        n = self.weight_count()
+        if n == 0:
+            raise LwmError(1, "invalid LeWM configuration")
+        out = np.empty(n, dtype=np.float32)
+        _check(lib.lwm_lewm_random_weights(C.byref(self), U64(seed), _fp(out), C.c_size_t(n)))
+        return out
+
+
+NORM_KINDS = {"batch": 0, "layer": 1, "none": 2}
+
+
 class _PlanResult(C.Structure):
     _fields_ = [("first_action", FP), ("sequence", FP), ("scores", FP), ("scores_capacity", C.c_size_t),
                 ("best_indices", C.POINTER(U32)), ("batch", U32), ("scores_cols", U32),
@@ -236,6 +273,15 @@ _sig("lwm_normal_device", C.c_int, VP, U64, U64, C.c_size_t, VP)
 _sig("lwm_skyjepa_reference_horizon", C.c_int, I32, F, F, U32, F, F, FP)
 _sig("lwm_skyjepa_geometric_prior", C.c_int, FP, FP, U32, F, C.POINTER(Domain), FP)
 _sig("lwm_rotor_plant_step", C.c_int, C.POINTER(Domain), FP, FP, FP, F)
+_sig("lwm_lewm_config_vector", None, C.POINTER(LewmConfig))
+_sig("lwm_lewm_config_image", None, C.POINTER(LewmConfig))
+_sig("lwm_lewm_weight_count", C.c_size_t, C.POINTER(LewmConfig))
+_sig("lwm_lewm_random_weights", C.c_int, C.POINTER(LewmConfig), U64, FP, C.c_size_t)
+_sig("lwm_scorer_lewm_create", C.c_int, VP, C.POINTER(LewmConfig), FP, C.c_size_t, C.POINTER(VP))
+_sig("lwm_scorer_lewm_set_context", C.c_int, VP, U32, U32, U32, FP, FP)
+_sig("lwm_scorer_lewm_set_context_device", C.c_int, VP, U32, U32, U32, VP, VP)
+_sig("lwm_lewm_encode_vector_device", C.c_int, VP, VP, U32, VP)
+_sig("lwm_lewm_encode_pixels_device", C.c_int, VP, VP, U32, VP)
 _sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
 _sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
@@ -588,6 +634,49 @@ class SkyJepaScorer(Scorer):
                                                      _fp(_f32(action_history)), _fp(ref),
                                                      _fp(_f32(reference_actions)), _fp(m)))
         self.batch = sh.shape[0]
+
+
+class LewmScorer(Scorer):
+    """LeWmSession::score_candidates (src/session.rs:46-66) over a LeWM /
+    WorldModel: goal-embedding L2 cost of the rolled-out embeddings."""
+
+    def __init__(self, ctx: Context, config: LewmConfig, weights: np.ndarray):
+        self.ctx = ctx
+        self.config = config
+        w = _f32(weights)
+        h = VP()
+        _check(lib.lwm_scorer_lewm_create(ctx.handle, C.byref(config), _fp(w), C.c_size_t(w.size), C.byref(h)))
+        self.handle = h
+        _LIVE["scorer"].add(self)
+
+    def set_context(self, emb_history, goal, history: int = 0) -> None:
+        """emb_history [B, h, D] and goal [B, D] host arrays; history 0 = h (the session's window)."""
+        e = _f32(emb_history)
+        _check(lib.lwm_scorer_lewm_set_context(self.handle, e.shape[0], e.shape[1], history, _fp(e),
+                                               _fp(_f32(goal))))
+        self.batch = e.shape[0]
+
+    def set_context_device(self, emb_history, goal, history: int = 0) -> None:
+        """torch CUDA tensors emb_history [B, h, D], goal [B, D] (copied on the context stream)."""
+        _check(lib.lwm_scorer_lewm_set_context_device(self.handle, emb_history.shape[0], emb_history.shape[1],
+                                                      history, VP(emb_history.data_ptr()), VP(goal.data_ptr())))
+        self.batch = emb_history.shape[0]
+
+    def encode_vector(self, obs):
+        """WorldModel::encode_vector: torch CUDA [n, obs_dim] -> [n, D] (on the context stream)."""
+        import torch
+        out = torch.empty((obs.shape[0], self.config.embed_dim), device=obs.device, dtype=torch.float32)
+        _check(lib.lwm_lewm_encode_vector_device(self.handle, VP(obs.data_ptr()), obs.shape[0],
+                                                 VP(out.data_ptr())))
+        return out
+
+    def encode_pixels(self, pixels):
+        """LeWm::encode_pixels: torch CUDA [n, C, H, W] normalised -> [n, D] (on the context stream)."""
+        import torch
+        out = torch.empty((pixels.shape[0], self.config.embed_dim), device=pixels.device, dtype=torch.float32)
+        _check(lib.lwm_lewm_encode_pixels_device(self.handle, VP(pixels.data_ptr()), pixels.shape[0],
+                                                 VP(out.data_ptr())))
+        return out
 
 
 class _CudaArray:

@@ -179,3 +179,52 @@ def fleet(seed: int = 0, vehicles: int = 256, samples: int = 4096, horizon: int 
     w.masses = np.array([d.mass for d in doms], np.float32)
     w.domains = doms
     return w
+
+
+@dataclass
+class LewmWorkload:
+    config: object            # LewmConfig
+    weights: np.ndarray
+    batch: int
+    samples: int
+    horizon: int
+    planner: object           # CemConfig or MppiConfig
+    obs: Optional[np.ndarray] = None        # vector observations [B, obs_dim]
+    goal_obs: Optional[np.ndarray] = None
+    y_plane: Optional[np.ndarray] = None    # NV12 observation / goal frames [B, H, W], [B, H/2, W/2, 2]
+    uv_plane: Optional[np.ndarray] = None
+    goal_y: Optional[np.ndarray] = None
+    goal_uv: Optional[np.ndarray] = None
+
+
+def lewm_vector(seed: int = 0, batch: int = 1, samples: int = 300, horizon: int = 5, elites: int = 30,
+                iterations: int = 3, config=None) -> LewmWorkload:
+    """Vector-observation LeWM CEM: 16-d observation and goal ~ N(0, 1),
+    300 candidates x 5 steps, 30 elites, 3 iterations, initial std 1 in a
+    [-1, 1] box, action dim 2."""
+    from . import ActionBounds, CemConfig, LewmConfig
+    cfg = config or LewmConfig.vector()
+    rng = np.random.default_rng(seed + 4000)
+    obs = rng.standard_normal((batch, cfg.obs_dim)).astype(np.float32)
+    goal = rng.standard_normal((batch, cfg.obs_dim)).astype(np.float32)
+    cem = CemConfig(horizon=horizon, samples=samples, elites=elites, action_dim=cfg.action_dim,
+                    iterations=iterations, action_bounds=ActionBounds.symmetric(cfg.action_dim, 1.0), init_std=1.0,
+                    min_std=1e-3, seed=seed + 1)
+    return LewmWorkload(cfg, cfg.random_weights(seed + 5000), batch, samples, horizon, cem, obs=obs, goal_obs=goal)
+
+
+def lewm_image(seed: int = 0, batch: int = 1, samples: int = 1024, horizon: int = 10, config=None) -> LewmWorkload:
+    """Image LeWM MPPI: seeded uniform-noise NV12 observation and goal frames
+    at the model's image size, 1024 candidates x 10 steps, action dim 2,
+    temperature 0.5, std 1 in a [-1, 1] box."""
+    from . import ActionBounds, LewmConfig, MppiConfig
+    cfg = config or LewmConfig.image()
+    rng = np.random.default_rng(seed + 6000)
+    s = cfg.image_size
+    planes = [rng.integers(0, 256, shape, dtype=np.uint8)
+              for shape in ((batch, s, s), (batch, s // 2, s // 2, 2), (batch, s, s), (batch, s // 2, s // 2, 2))]
+    mppi = MppiConfig(horizon=horizon, samples=samples, action_dim=cfg.action_dim, iterations=1,
+                      action_bounds=ActionBounds.symmetric(cfg.action_dim, 1.0), noise_std=1.0, temperature=0.5,
+                      seed=seed + 1)
+    return LewmWorkload(cfg, cfg.random_weights(seed + 7000), batch, samples, horizon, mppi, y_plane=planes[0],
+                        uv_plane=planes[1], goal_y=planes[2], goal_uv=planes[3])

@@ -161,6 +161,28 @@ void orc_reference_state(int kind, float time, float radius, float period, float
 void orc_geometric_prior(const float* current, const float* refs, uint32_t T, float dt,
                          const lwm_domain* d, float* out);
 
+/* ---- LeWM / WorldModel scorer (lewm_world.c) ---- */
+typedef struct orc_lewm orc_lewm;
+size_t orc_lewm_weight_count(const lwm_lewm_config* cfg);
+orc_lewm* orc_lewm_new(const lwm_lewm_config* cfg, const float* weights, size_t count);
+void orc_lewm_free(orc_lewm* m);
+void orc_lewm_action_embed(const orc_lewm* m, const float* act, uint32_t n, float* out);
+void orc_lewm_predict_last(const orc_lewm* m, const float* frames, const float* act_emb, uint32_t seqs, uint32_t t,
+                           float* out);
+void orc_lewm_scores(const orc_lewm* m, const float* emb, uint32_t h, const float* goal, const float* cand,
+                     uint32_t B, uint32_t S, uint32_t T, uint32_t history, float* scores, float* last_out);
+void orc_lewm_encode_vector(const orc_lewm* m, const float* obs, uint32_t n, float* out);
+void orc_lewm_encode_pixels(const orc_lewm* m, const float* pixels, uint32_t n, float* out);
+typedef struct orc_lewm_ctx {
+    const orc_lewm* model;
+    const float* emb;  /* [B, h, D] */
+    const float* goal; /* [B, D] */
+    uint32_t h;
+    uint32_t history;
+} orc_lewm_ctx;
+void orc_lewm_score_fn(void* user, const float* cand, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
+                       float* scores);
+
 /* ---- image preprocessing (src/media/mod.rs) ---- */
 /* swm_packed_u8_to_nchw_f32 (src/media/mod.rs:1113-1194): format 0 RGB,
  * 1 BGR, 2 RGBA, 3 BGRA; history_len 0 writes [B,3,oh,ow], otherwise slot

@@ -91,6 +91,14 @@ _sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, 
 _sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_reference_state", None, C.c_int, F, F, F, FP)
 _sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
+_sig("orc_lewm_weight_count", C.c_size_t, C.c_void_p)
+_sig("orc_lewm_new", VP, C.c_void_p, FP, C.c_size_t)
+_sig("orc_lewm_free", None, VP)
+_sig("orc_lewm_action_embed", None, VP, FP, U32, FP)
+_sig("orc_lewm_predict_last", None, VP, FP, FP, U32, U32, FP)
+_sig("orc_lewm_scores", None, VP, FP, U32, FP, FP, U32, U32, U32, U32, FP, FP)
+_sig("orc_lewm_encode_vector", None, VP, FP, U32, FP)
+_sig("orc_lewm_encode_pixels", None, VP, FP, U32, FP)
 _sig("orc_preprocess_packed", None, C.c_void_p, U32, U32, U32, U32, U32, U32, FP, FP, U32, U32, FP)
 _sig("orc_preprocess_nv12", None, C.c_void_p, C.c_void_p, U32, U32, U32, U32, U32, U32, FP, FP, U32, U32, FP)
 
@@ -428,3 +436,67 @@ def preprocess_nv12(y_plane, uv_plane, color_space, out_h, out_w, mean=(0, 0, 0)
     lib.orc_preprocess_nv12(y_plane.ctypes.data, uv_plane.ctypes.data, B, H, W, color_space, out_h, out_w,
                             fp(f32(mean)), fp(f32(std)), history_len, slot, fp(res))
     return res
+
+
+class LewmCtx(C.Structure):
+    _fields_ = [("model", VP), ("emb", FP), ("goal", FP), ("h", U32), ("history", U32)]
+
+
+LEWM_FN = C.cast(lib.orc_lewm_score_fn, VP)
+
+
+class LewmModel:
+    """orc_lewm: LeWM / WorldModel restated in C (lewm_world.c)."""
+
+    def __init__(self, cfg, weights: np.ndarray):
+        self.cfg = cfg
+        w = f32(weights)
+        self.handle = lib.orc_lewm_new(C.byref(cfg), fp(w), w.size)
+        if not self.handle:
+            raise ValueError("LeWM weight count mismatch")
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib.orc_lewm_free(self.handle)
+            self.handle = None
+
+    def action_embed(self, act):
+        act = f32(act)
+        n = act.size // self.cfg.action_dim
+        out = np.empty((n, self.cfg.embed_dim), np.float32)
+        lib.orc_lewm_action_embed(self.handle, fp(act), n, fp(out))
+        return out
+
+    def predict_last(self, frames, act_emb):
+        frames, act_emb = f32(frames), f32(act_emb)
+        seqs, t, _ = frames.shape
+        out = np.empty((seqs, self.cfg.embed_dim), np.float32)
+        lib.orc_lewm_predict_last(self.handle, fp(frames), fp(act_emb), seqs, t, fp(out))
+        return out
+
+    def scores(self, emb, goal, cand, history=0, with_last=False):
+        emb, goal, cand = f32(emb), f32(goal), f32(cand)
+        B, h, _ = emb.shape
+        _, S, T, _ = cand.shape
+        scores = np.empty((B, S), np.float32)
+        last = np.empty((B, S, self.cfg.embed_dim), np.float32) if with_last else None
+        lib.orc_lewm_scores(self.handle, fp(emb), h, fp(goal), fp(cand), B, S, T, history or h, fp(scores), fp(last))
+        return (scores, last) if with_last else scores
+
+    def encode_vector(self, obs):
+        obs = f32(obs)
+        out = np.empty((obs.shape[0], self.cfg.embed_dim), np.float32)
+        lib.orc_lewm_encode_vector(self.handle, fp(obs), obs.shape[0], fp(out))
+        return out
+
+    def encode_pixels(self, pixels):
+        pixels = f32(pixels)
+        out = np.empty((pixels.shape[0], self.cfg.embed_dim), np.float32)
+        lib.orc_lewm_encode_pixels(self.handle, fp(pixels), pixels.shape[0], fp(out))
+        return out
+
+    def score_ctx(self, emb, goal, history=0):
+        emb, goal = f32(emb), f32(goal)
+        ctx = LewmCtx(self.handle, fp(emb), fp(goal), emb.shape[1], history or emb.shape[1])
+        ctx._keep = (emb, goal)
+        return ctx
