@@ -9,6 +9,7 @@ reference).  A "step" is one plan call.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload skyjepa|nominal]
     python bench.py --impl reference ...   # the CPU restatement on the host cores
     python bench.py --workload fleet [--shard auto|vehicles|candidates] [--vehicles V --samples S --horizon T]
+    python bench.py --workload lewm-vector|lewm-image    # LeWM CEM (vector obs) / MPPI (NV12 frames + ViT)
 
 `value` is timed with CUDA events around each plan on the device with the
 context resident (L2 flushed between steps); `e2e` times the public C-ABI
@@ -424,6 +425,191 @@ def cpu_baseline_fleet(w, budget_s: float):
                       f"restatement, {threads} OpenMP threads; fleet rate = vehicle rate / {w.batch}"}
 
 
+# ------------------------------------------------------------ LeWM workloads
+
+def lewm_flop_per_candidate_step(c) -> float:
+    """Algorithmic FLOP of one rolled-out candidate step (one-frame window:
+    the attention output is V, so only the V projection is counted)."""
+    D, hid, inner = c.embed_dim, c.pred_hidden_dim, c.heads * c.dim_head
+    mac = c.action_dim * c.smoothed_dim + c.smoothed_dim * c.action_mlp_scale * D + c.action_mlp_scale * D * D
+    mac += c.depth * (6 * hid * hid + 2 * inner * hid + 2 * c.mlp_dim * hid)
+    mac += 2 * D * c.pred_proj_hidden
+    return 2.0 * mac
+
+
+def run_lewm(args, rank, world, local_rank):
+    """LeWM planning: `lewm-vector` = CEM over 300 x 5 candidates with a
+    16-d observation; `lewm-image` = MPPI over 1024 x 10 candidates whose
+    observation and goal are NV12 frames preprocessed and encoded by the ViT
+    inside every plan.  Replicas for N > 1 (one vehicle does not shard)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import lewm_b200 as L
+    from lewm_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    image = args.workload == "lewm-image"
+    w = W.lewm_image(seed=31 + rank) if image else W.lewm_vector(seed=31 + rank)
+    ctx = L.Context(local_rank)
+    stream = ctx.torch_stream()
+    sc = L.LewmScorer(ctx, w.config, w.weights)
+    planner = (L.MppiPlanner if image else L.CemPlanner)(ctx, w.planner)
+    D = w.config.embed_dim
+    if image:
+        prep = L.ImagePreprocess.imagenet_224()
+        s_img = w.config.image_size
+        host_y = torch.from_numpy(np.concatenate([w.y_plane, w.goal_y])).pin_memory()
+        host_uv = torch.from_numpy(np.concatenate([w.uv_plane, w.goal_uv])).pin_memory()
+        dev_y = torch.empty(host_y.shape, dtype=torch.uint8, device="cuda")
+        dev_uv = torch.empty(host_uv.shape, dtype=torch.uint8, device="cuda")
+        pix = torch.empty((2, 3, s_img, s_img), device="cuda")
+        h2d = host_y.numel() + host_uv.numel()
+    else:
+        host_obs = torch.from_numpy(np.concatenate([w.obs, w.goal_obs])).pin_memory()
+        dev_obs = torch.empty(host_obs.shape, device="cuda")
+        h2d = host_obs.numel() * 4
+    with torch.cuda.stream(stream):
+        if image:
+            dev_y.copy_(host_y)
+            dev_uv.copy_(host_uv)
+        else:
+            dev_obs.copy_(host_obs)
+    ctx.synchronize()
+
+    def encode_and_plan(upload: bool):
+        with torch.cuda.stream(stream):
+            if image:
+                if upload:
+                    dev_y.copy_(host_y, non_blocking=True)
+                    dev_uv.copy_(host_uv, non_blocking=True)
+                L.preprocess_nv12_device(ctx, dev_y, dev_uv, 2, s_img, s_img, "bt601-video", prep, pix)
+                emb = sc.encode_pixels(pix)
+            else:
+                if upload:
+                    dev_obs.copy_(host_obs, non_blocking=True)
+                emb = sc.encode_vector(dev_obs)
+            sc.set_context_device(emb[:1, None, :].contiguous(), emb[1:].contiguous())
+        return planner.plan_device(sc)
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    for _ in range(args.warmup):
+        encode_and_plan(False)
+    ctx.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = ctx.launch_count()
+    times = []
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.add_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            encode_and_plan(False)
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = (ctx.launch_count() - n0) // args.steps
+    e2e_times = []
+    for _ in range(args.steps):
+        ctx.synchronize()
+        t0 = time.perf_counter()
+        r = encode_and_plan(True)
+        with torch.cuda.stream(stream):
+            seq = L.device_tensor(r.sequence, (1, w.horizon, w.config.action_dim)).cpu()
+        e2e_times.append((time.perf_counter() - t0) * 1e3)
+    stats = torch.tensor([sum(times), float(np.mean(e2e_times))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    total_ms, e2e_mean = stats.tolist()
+    result = None
+    if rank == 0:
+        iters = w.planner.iterations
+        cand_steps = w.samples * w.horizon * iters
+        ms = total_ms / args.steps
+        plans_per_s = world * 1e3 / ms
+        sgemm = sgemm_peak_tflops(torch)
+        flop = lewm_flop_per_candidate_step(w.config) * cand_steps
+        achieved = flop / (percentile(times, 0.5) * 1e-3) / 1e12
+        name = ("LeWM image MPPI: NV12 224x224 obs + goal -> preprocess -> ViT-Tiny (patch 16, 12 x 192) -> "
+                "projector; predictor depth 6, 16 x 64 heads, MLP 2048; 1024 candidates x 10 steps, lambda 0.5"
+                if image else
+                "LeWM vector CEM: 16-d obs + goal -> VectorMlp 512 -> 192; predictor depth 4, 8 x 32 heads, MLP 768; "
+                "300 candidates x 5 steps, 30 elites, 3 iterations")
+        result = {
+            "metric": "plan steps/s (one plan per step, observation/goal encoding included); candidate-steps/s "
+                      "and p50/p95 plan latency alongside",
+            "value": round(plans_per_s, 3), "unit": "plans/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, seeded observations / NV12 noise frames)",
+            "config": {"workload": name, "parallelism": f"replicas x{world}",
+                       "l2": "flushed between steps (256 MiB write outside the timed region)"},
+            "candidate_steps_per_s": round(plans_per_s * cand_steps, 1),
+            "latency_ms": {"p50": round(percentile(times, 0.5), 4), "p95": round(percentile(times, 0.95), 4)},
+            "e2e": {"value": round(world * 1e3 / e2e_mean, 3), "unit": "plans/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(seq.numel() * 4)},
+            "gpu_launches": int(launches * args.steps),
+            "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2), "unit": "TFLOP/s",
+                         "frac": round(achieved / sgemm, 4), "traffic": None,
+                         "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
+                         "note": "achieved = predictor FLOP per plan (encoders excluded) / p50 plan time"},
+            "clocks": clocks.summary(),
+        }
+        if args.cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_lewm(w, image, args.cpu_seconds)
+    # pinned host buffers used on the library's stream must be released while
+    # that stream still exists (the host allocator records events on it)
+    ctx.synchronize()
+    if image:
+        del host_y, host_uv, dev_y, dev_uv, pix
+    else:
+        del host_obs, dev_obs
+    del seq, r
+    torch.cuda.synchronize()
+    planner.close()
+    sc.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return result
+
+
+def cpu_baseline_lewm(w, image: bool, budget_s: float):
+    """The oracle's LeWM plan on the host cores (encoding included)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    m = O.LewmModel(w.config, w.weights)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        if image:
+            pix = O.preprocess_nv12(np.concatenate([w.y_plane, w.goal_y]), np.concatenate([w.uv_plane, w.goal_uv]), 0,
+                                    224, 224, mean=(0.485, 0.456, 0.406), std=(0.229, 0.224, 0.225))
+            emb = m.encode_pixels(pix)
+            ctxo = m.score_ctx(emb[:1, None, :], emb[1:])
+            O.mppi_plan(w.planner, 1, (O.LEWM_FN, ctxo), seed=w.planner.seed)
+        else:
+            emb = m.encode_vector(np.concatenate([w.obs, w.goal_obs]))
+            ctxo = m.score_ctx(emb[:1, None, :], emb[1:])
+            O.cem_plan(w.planner, 1, (O.LEWM_FN, ctxo), seed=w.planner.seed)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 50:
+            break
+    mean = float(np.mean(times))
+    return {"value": round(1.0 / mean, 5), "unit": "plans/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} full plans (encoding included), oracle C restatement, {threads} OpenMP threads"}
+
+
 # ----------------------------------------------------------------- CPU arm
 
 def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
@@ -477,6 +663,21 @@ def run_reference(args, rank, world):
                 "candidate_steps_per_s": base["candidate_steps_per_s"], "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "fleet plans/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload.startswith("lewm"):
+        from lewm_b200 import workloads as W
+        image = args.workload == "lewm-image"
+        w = W.lewm_image(seed=31) if image else W.lewm_vector(seed=31)
+        base = cpu_baseline_lewm(w, image, args.cpu_seconds)
+        return {"impl": "reference", "metric": "plan steps/s (one plan per step, observation/goal encoding "
+                "included); candidate-steps/s and p50/p95 plan latency alongside",
+                "value": base["value"], "unit": "plans/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init weights, seeded observations / NV12 noise frames)",
+                "config": {"workload": args.workload, "parallelism": "host CPU"},
+                "candidate_steps_per_s": round(base["value"] * w.samples * w.horizon * w.planner.iterations, 1),
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     base = cpu_baseline(args.workload, args.cpu_seconds)
     # each timed step is one full plan on the host cores
     return {
@@ -509,7 +710,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet"], default="skyjepa")
+    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet", "lewm-vector", "lewm-image"],
+                    default="skyjepa")
     ap.add_argument("--shard", choices=["auto", "vehicles", "candidates"], default="auto")
     ap.add_argument("--vehicles", type=int, default=256)
     ap.add_argument("--samples", type=int, default=4096)
@@ -525,6 +727,8 @@ def main():
         out = run_reference(args, rank, world)
     elif args.workload == "fleet":
         out = run_fleet(args, rank, world, local_rank)
+    elif args.workload.startswith("lewm"):
+        out = run_lewm(args, rank, world, local_rank)
     else:
         out = run_ours(args, rank, world, local_rank)
     if rank == 0 and out is not None:

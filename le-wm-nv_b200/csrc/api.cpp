@@ -619,7 +619,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
         }
         const float* noise = injected ? injected + static_cast<size_t>(it) * n : nullptr;
         const uint64_t it_offset = offset + static_cast<uint64_t>(it) * per_iter;
-        if (p->kind == PlannerKind::Mppi && sc->kind != ScorerKind::Callback) {
+        if (p->kind == PlannerKind::Mppi && (sc->kind == ScorerKind::Nominal || sc->kind == ScorerKind::Skyjepa)) {
             const float* mean_it = (it == 0) ? mean_in : p->sequence.as<float>();
             if (sc->kind == ScorerKind::Nominal) {
                 lwm::NominalArgs a = nominal_args(sc, p->S);

@@ -27,10 +27,12 @@ namespace lwm {
 // ------------------------------------------------------------------ GEMM
 //
 // C[M,N] = A[M,K] (row stride lda) . W[N,K]^T (+ bias), 64x64 tile per
-// 256-thread block, 4x4 outputs per thread, K staged 16 at a time through
-// shared memory (A transposed so a thread's 4 rows are one float4 read).
-// Each output's dot product runs in k order (as the reference's matmul).
-constexpr int kBM = 64, kBN = 64, kBK = 16;
+// 256-thread block, 4x4 outputs per thread, K staged 32 at a time through
+// shared memory (A transposed so a thread's 4 rows are one float4 read).  The
+// next K tile is fetched into registers before the current one is multiplied,
+// so its global-load latency overlaps the FMAs.  Each output's dot product
+// runs in k order (as the reference's matmul).
+constexpr int kBM = 64, kBN = 64, kBK = 32;
 
 __device__ __forceinline__ float apply_act(int act, float v) {
     switch (act) {
@@ -41,6 +43,16 @@ __device__ __forceinline__ float apply_act(int act, float v) {
     }
 }
 
+__device__ __forceinline__ float epilogue_value(const GemmArgs& g, uint32_t m, uint32_t n, float v, float* c) {
+    if (g.bias) v = v + g.bias[n];
+    if (g.residual) {
+        // x = x + gate * y (ConditionalBlock) or x = y + x (ViT layer)
+        if (g.gate) v = g.gate[g.map.row(m) * g.ldg + n] * v;
+        return *c + v;
+    }
+    return apply_act(g.act, v);
+}
+
 __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
     __shared__ __align__(16) float As[2][kBK][kBM + 4];
     __shared__ __align__(16) float Ws[2][kBK][kBN + 4];
@@ -48,22 +60,38 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
     const int tx = tid % 16, ty = tid / 16;  // 16 x 16 threads, 4 x 4 outputs each
     const uint32_t m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
     float acc[4][4] = {};
-    // loader mapping: 64 rows x 16 k = 1024 elements per tile, 4 per thread
-    const int lr = tid / 4, lk = (tid % 4) * 4;
-    auto load = [&](int buf, uint32_t k0) {
+    // this CTA's K range (split-K over blockIdx.z)
+    const uint32_t kb = blockIdx.z * g.k_chunk;
+    const uint32_t ke = min(g.K, kb + g.k_chunk);
+    // loader mapping: 64 rows x 32 k = 2048 elements per tile, 8 per thread
+    // (a lane reads 8 consecutive k of one row)
+    const int lr = tid / 4, lk = (tid % 4) * 8;
+    const uint32_t am = m0 + lr, wn = n0 + lr;
+    const float* arow = g.A + static_cast<size_t>(am < g.M ? am : 0) * g.lda;
+    const float* wrow = g.W + static_cast<size_t>(wn < g.N ? wn : 0) * g.ldw;
+    float ra[8], rw[8];
+    auto fetch = [&](uint32_t k0) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
             const uint32_t k = k0 + lk + q;
-            const uint32_t m = m0 + lr, n = n0 + lr;
-            As[buf][lk + q][lr] = (m < g.M && k < g.K) ? __ldg(g.A + static_cast<size_t>(m) * g.lda + k) : 0.0f;
-            Ws[buf][lk + q][lr] = (n < g.N && k < g.K) ? __ldg(g.W + static_cast<size_t>(n) * g.ldw + k) : 0.0f;
+            ra[q] = (am < g.M && k < ke) ? __ldg(arow + k) : 0.0f;
+            rw[q] = (wn < g.N && k < ke) ? __ldg(wrow + k) : 0.0f;
         }
     };
-    load(0, 0);
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            As[buf][lk + q][lr] = ra[q];
+            Ws[buf][lk + q][lr] = rw[q];
+        }
+    };
+    fetch(kb);
+    stash(0);
     __syncthreads();
     int buf = 0;
-    for (uint32_t k0 = 0; k0 < g.K; k0 += kBK) {
-        if (k0 + kBK < g.K) load(buf ^ 1, k0 + kBK);
+    for (uint32_t k0 = kb; k0 < ke; k0 += kBK) {
+        const bool more = k0 + kBK < ke;
+        if (more) fetch(k0 + kBK);  // in flight during the FMAs below
 #pragma unroll
         for (int kk = 0; kk < kBK; ++kk) {
             const float4 a = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
@@ -74,34 +102,81 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
         }
+        if (more) stash(buf ^ 1);
         __syncthreads();
         buf ^= 1;
     }
+    if (g.splits <= 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t m = m0 + ty * 4 + i;
+            if (m >= g.M) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t n = n0 + tx * 4 + j;
+                if (n >= g.N) continue;
+                float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
+                *c = epilogue_value(g, m, n, acc[i][j], c);
+            }
+        }
+        return;
+    }
+    // split-K: park this split's tile, the last split of the tile to arrive
+    // adds the partial tiles in split order (deterministic) and runs the epilogue
+    const size_t tile = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+    float* mine = g.partial + (tile * g.splits + blockIdx.z) * (kBM * kBN);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<float4*>(mine + (ty * 4 + i) * kBN + tx * 4) =
+            make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (tid == 0) s_last = atomicAdd(&g.counters[tile], 1u) == g.splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* parts = g.partial + tile * g.splits * (kBM * kBN);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint32_t m = m0 + ty * 4 + i;
-        if (m >= g.M) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t n = n0 + tx * 4 + j;
-            if (n >= g.N) continue;
-            float v = acc[i][j];
-            if (g.bias) v = v + g.bias[n];
-            float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
-            if (g.residual) {
-                // x = x + gate * y (ConditionalBlock) or x = y + x (ViT layer)
-                if (g.gate) v = g.gate[g.map.row(m) * g.ldg + n] * v;
-                *c = *c + v;
-            } else {
-                *c = apply_act(g.act, v);
+            float v = 0.0f;
+            for (uint32_t z = 0; z < g.splits; ++z)
+                v += __ldcg(parts + z * (kBM * kBN) + (ty * 4 + i) * kBN + tx * 4 + j);
+            if (m < g.M && n < g.N) {
+                float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
+                *c = epilogue_value(g, m, n, v, c);
             }
         }
     }
+    if (tid == 0) g.counters[tile] = 0u;
 }
 
-cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t stream) {
-    if (g.M == 0 || g.N == 0) return cudaSuccess;
-    dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM);
+// Split K when the output tiles alone leave most SMs idle: aim for about two
+// waves of CTAs, at least 64 K per split, at most 16 splits.
+cudaError_t gemm_f32(const GemmArgs& in, cudaStream_t stream, const SplitScratch* sp) {
+    if (in.M == 0 || in.N == 0) return cudaSuccess;
+    GemmArgs g = in;
+    const uint32_t tx = (g.N + kBN - 1) / kBN, ty = (g.M + kBM - 1) / kBM;
+    const size_t tiles = static_cast<size_t>(tx) * ty;
+    uint32_t splits = 1;
+    if (sp && sp->partial && tiles < 296 && g.K >= 128) {
+        splits = static_cast<uint32_t>((296 + tiles - 1) / tiles);
+        splits = min(splits, min(16u, g.K / 64));
+        while (splits > 1 && tiles * splits * kBM * kBN > sp->floats) --splits;
+        if (tiles > sp->n_counters) splits = 1;
+    }
+    g.splits = splits;
+    g.k_chunk = splits > 1 ? ((g.K + splits - 1) / splits + kBK - 1) / kBK * kBK : g.K;
+    if (splits > 1) {
+        g.splits = (g.K + g.k_chunk - 1) / g.k_chunk;  // no empty split
+        g.partial = sp->partial;
+        g.counters = sp->counters;
+    }
+    dim3 grid(tx, ty, g.splits);
     gemm_f32_kernel<<<grid, 256, 0, stream>>>(g);
     return cudaGetLastError();
 }
@@ -132,25 +207,58 @@ __device__ __forceinline__ void row_stats(const float* x, uint32_t d, float& mea
 // y = LN_affine(LN_noaffine(x, 1e-6) * (scale + 1) + shift, 1e-5)
 // shift/scale come from the AdaLN table row map.row(r) at column offsets
 // shift_off / scale_off (modules.rs:317-330, 9-27).
+// The row (d <= 1024) is held in registers, 32 values per lane at most;
+// shift/scale are fetched together with it.
+constexpr int kRowRegs = 32;
 __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
                               uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b) {
-    extern __shared__ float s_row[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
     if (r >= rows) return;
-    float* t = s_row + static_cast<size_t>(warp) * d;
     const float* xr = x + static_cast<size_t>(r) * d;
-    float mean, den;
-    row_stats(xr, d, mean, den, 1e-6f);
     const float* a = ada + map.row(r) * ld_ada;
-    for (uint32_t i = lane; i < d; i += 32) {
-        const float n = (xr[i] - mean) / den;
-        t[i] = n * (a[scale_off + i] + 1.0f) + a[shift_off + i];
+    float v[kRowRegs], sh[kRowRegs], sc[kRowRegs];
+    float s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q) {
+        const uint32_t i = lane + 32 * q;
+        const bool in = i < d;
+        v[q] = in ? xr[i] : 0.0f;
+        sh[q] = in ? a[shift_off + i] : 0.0f;
+        sc[q] = in ? a[scale_off + i] : 0.0f;
+        s += v[q];
     }
-    __syncwarp();
-    row_stats(t, d, mean, den, 1e-5f);
+    float mean = warp_sum(s) / static_cast<float>(d);
+    float var = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q)
+        if (lane + 32 * q < d) {
+            const float c = v[q] - mean;
+            var += c * c;
+        }
+    float den = sqrtf(warp_sum(var) / static_cast<float>(d) + 1e-6f);
+    s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q)
+        if (lane + 32 * q < d) {
+            v[q] = (v[q] - mean) / den * (sc[q] + 1.0f) + sh[q];
+            s += v[q];
+        }
+    mean = warp_sum(s) / static_cast<float>(d);
+    var = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q)
+        if (lane + 32 * q < d) {
+            const float c = v[q] - mean;
+            var += c * c;
+        }
+    den = sqrtf(warp_sum(var) / static_cast<float>(d) + 1e-5f);
     float* yr = y + static_cast<size_t>(r) * d;
-    for (uint32_t i = lane; i < d; i += 32) yr[i] = (t[i] - mean) / den * w[i] + b[i];
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q) {
+        const uint32_t i = lane + 32 * q;
+        if (i < d) yr[i] = (v[q] - mean) / den * w[i] + b[i];
+    }
 }
 
 // LayerNorm (affine, eps) of rows gathered from src row (r * t_in + pick).
@@ -335,7 +443,7 @@ cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, c
                           cudaStream_t s) {
     if (!rows) return cudaSuccess;
     constexpr int kWarps = 8;
-    ada_ln_kernel<<<blocks_for(rows, kWarps), kWarps * 32, kWarps * d * sizeof(float), s>>>(
+    ada_ln_kernel<<<blocks_for(rows, kWarps), kWarps * 32, 0, s>>>(
         x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b);
     return cudaGetLastError();
 }

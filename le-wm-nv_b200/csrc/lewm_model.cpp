@@ -182,6 +182,10 @@ void Arena::release() {
 }
 
 LewmModel::~LewmModel() {
+    g_score.reset();
+    g_enc.reset();
+    if (split.partial) cudaFree(split.partial);
+    if (split.counters) cudaFree(split.counters);
     ws.release();
     enc.release();
     if (blob) cudaFree(blob);
@@ -196,6 +200,8 @@ namespace {
         const cudaError_t e_ = (x);            \
         if (e_ != cudaSuccess) return e_;      \
     } while (0)
+
+cudaError_t gemm_f32(const SplitScratch* sp, const GemmArgs& g, cudaStream_t s) { return lwm::gemm_f32(g, s, sp); }
 
 GemmArgs gemm(const float* A, uint32_t lda, const Lin& l, float* C, uint32_t ldc, uint32_t M, int act = kActNone) {
     GemmArgs g{};
@@ -214,18 +220,20 @@ GemmArgs gemm(const float* A, uint32_t lda, const Lin& l, float* C, uint32_t ldc
 }
 
 // Mlp::forward on the device: fc1 -> norm + GELU -> fc2.
-cudaError_t mlp(const MlpW& m, const float* x, uint32_t n, float* hid, float* out, cudaStream_t s, int& launches) {
-    LWM_CU(gemm_f32(gemm(x, m.fc1.in, m.fc1, hid, m.fc1.out, n), s));
+cudaError_t mlp(const SplitScratch* sp, const MlpW& m, const float* x, uint32_t n, float* hid, float* out,
+                cudaStream_t s, int& launches) {
+    LWM_CU(gemm_f32(sp, gemm(x, m.fc1.in, m.fc1, hid, m.fc1.out, n), s));
     LWM_CU(launch_norm_act(hid, n, m.fc1.out, m.norm.kind, m.norm.w, m.norm.b, m.norm.rm, m.norm.rv, s));
-    LWM_CU(gemm_f32(gemm(hid, m.fc1.out, m.fc2, out, m.fc2.out, n), s));
+    LWM_CU(gemm_f32(sp, gemm(hid, m.fc1.out, m.fc2, out, m.fc2.out, n), s));
     launches += 3;
     return cudaSuccess;
 }
 
 }  // namespace
 
-cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb,
-                             cudaStream_t s) {
+cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb,
+                                  cudaStream_t s) {
+    const SplitScratch* sp = &split;
     const uint32_t D = c.embed_dim, hid = c.pred_hidden_dim, inner = c.heads * c.dim_head, A = c.action_dim;
     const uint32_t sm = c.smoothed_dim, ah = c.action_mlp_scale * D, ph = c.pred_proj_hidden;
     const size_t bs = static_cast<size_t>(B) * S, all = bs * T;
@@ -249,23 +257,23 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
     int n = 0;
     const uint32_t rows_all = static_cast<uint32_t>(all);
     // ActionEmbedder over every (sample, time) token (modules.rs:150-158)
-    LWM_CU(gemm_f32(gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
-    LWM_CU(gemm_f32(gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
-    LWM_CU(gemm_f32(gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
+    LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
+    LWM_CU(gemm_f32(sp, gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
+    LWM_CU(gemm_f32(sp, gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
     n += 3;
     // cond -> SiLU -> AdaLN table of every layer (ConditionalBlock::forward, modules.rs:317-320);
     // the condition of a token depends only on its action, so the table is
     // built once per scoring call for all (sample, time) tokens.
     const float* cond = f_act;
     if (w.has_proj) {
-        LWM_CU(gemm_f32(gemm(f_act, D, w.cond_proj, f_cond, hid, rows_all), s));
+        LWM_CU(gemm_f32(sp, gemm(f_act, D, w.cond_proj, f_cond, hid, rows_all), s));
         ++n;
         cond = f_cond;
     }
     LWM_CU(launch_silu(cond, f_cond, all * hid, s));
     ++n;
     for (uint32_t l = 0; l < c.depth; ++l) {
-        LWM_CU(gemm_f32(gemm(f_cond, hid, w.blocks[l].ada, f_ada + static_cast<size_t>(l) * all * 6 * hid, 6 * hid,
+        LWM_CU(gemm_f32(sp, gemm(f_cond, hid, w.blocks[l].ada, f_ada + static_cast<size_t>(l) * all * 6 * hid, 6 * hid,
                              rows_all), s));
         ++n;
     }
@@ -284,7 +292,7 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
         ++n;
         float* x = f_X;
         if (w.has_proj) {
-            LWM_CU(gemm_f32(gemm(f_X, D, w.input_proj, f_x, hid, rows), s));
+            LWM_CU(gemm_f32(sp, gemm(f_X, D, w.input_proj, f_x, hid, rows), s));
             ++n;
             x = f_x;
         }
@@ -299,12 +307,12 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
                 Lin v = b.qkv;
                 v.w = b.qkv.w + static_cast<size_t>(2) * inner * hid;
                 v.out = inner;
-                LWM_CU(gemm_f32(gemm(f_y, hid, v, f_att, inner, rows), s));
+                LWM_CU(gemm_f32(sp, gemm(f_y, hid, v, f_att, inner, rows), s));
                 n += 2;
                 att = f_att;
                 ld_att = inner;
             } else {
-                LWM_CU(gemm_f32(gemm(f_y, hid, b.qkv, f_qkv, 3 * inner, rows), s));
+                LWM_CU(gemm_f32(sp, gemm(f_y, hid, b.qkv, f_qkv, 3 * inner, rows), s));
                 LWM_CU(launch_attention(f_qkv, f_att, static_cast<uint32_t>(bs), wl, c.heads, c.dim_head, scale, 1, 1,
                                         s));
                 n += 3;
@@ -316,16 +324,16 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
             go.gate = ada + 2 * hid;
             go.ldg = 6 * hid;
             go.map = map;
-            LWM_CU(gemm_f32(go, s));
+            LWM_CU(gemm_f32(sp, go, s));
             LWM_CU(launch_ada_ln(x, f_y, rows, hid, ada, 6 * hid, 3 * hid, 4 * hid, map, b.mlp_norm.w, b.mlp_norm.b,
                                  s));
-            LWM_CU(gemm_f32(gemm(f_y, hid, b.fc1, f_f, c.mlp_dim, rows, kActGeluTanh), s));
+            LWM_CU(gemm_f32(sp, gemm(f_y, hid, b.fc1, f_f, c.mlp_dim, rows, kActGeluTanh), s));
             GemmArgs g2 = gemm(f_f, c.mlp_dim, b.fc2, x, hid, rows);
             g2.residual = 1;
             g2.gate = ada + 5 * hid;
             g2.ldg = 6 * hid;
             g2.map = map;
-            LWM_CU(gemm_f32(g2, s));
+            LWM_CU(gemm_f32(sp, g2, s));
             n += 4;
         }
         // last token -> norm -> output_proj -> pred_proj (Transformer::forward_last, modules.rs:369-380)
@@ -334,11 +342,11 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
         ++n;
         const float* pin = f_last;
         if (w.has_proj) {
-            LWM_CU(gemm_f32(gemm(f_last, hid, w.output_proj, f_po, D, static_cast<uint32_t>(bs)), s));
+            LWM_CU(gemm_f32(sp, gemm(f_last, hid, w.output_proj, f_po, D, static_cast<uint32_t>(bs)), s));
             ++n;
             pin = f_po;
         }
-        LWM_CU(mlp(w.pred_proj, pin, static_cast<uint32_t>(bs), f_p1, f_pred, s, n));
+        LWM_CU(mlp(sp, w.pred_proj, pin, static_cast<uint32_t>(bs), f_p1, f_pred, s, n));
         LWM_CU(launch_frames_put(f_pred, f_frames, nframes, count, bs, D, s));
         ++n;
         ++count;
@@ -351,30 +359,33 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
 }
 
 cudaError_t LewmModel::encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s) {
+    LWM_CU(ensure_split());
+    const SplitScratch* sp = &split;
     const uint32_t oh = c.obs_hidden_dim;
     LWM_CU(enc.ensure(static_cast<size_t>(2) * n * oh));
     float *a = enc.ptr, *b = enc.ptr + static_cast<size_t>(n) * oh;
     int k = 0;
-    LWM_CU(gemm_f32(gemm(obs, c.obs_dim, w.enc_lin[0], a, oh, n), s));
+    LWM_CU(gemm_f32(sp, gemm(obs, c.obs_dim, w.enc_lin[0], a, oh, n), s));
     ++k;
     for (uint32_t j = 0; j + 1 < c.obs_depth; ++j) {
         const Norm& nm = w.enc_norm[j];
         LWM_CU(launch_norm_act(a, n, oh, nm.kind, nm.w, nm.b, nullptr, nullptr, s));
         ++k;
         if (j + 2 < c.obs_depth) {
-            LWM_CU(gemm_f32(gemm(a, oh, w.enc_lin[j + 1], b, oh, n), s));
+            LWM_CU(gemm_f32(sp, gemm(a, oh, w.enc_lin[j + 1], b, oh, n), s));
             ++k;
             float* t = a;
             a = b;
             b = t;
         }
     }
-    LWM_CU(gemm_f32(gemm(a, oh, w.enc_lin[c.obs_depth - 1], out, c.embed_dim, n), s));
+    LWM_CU(gemm_f32(sp, gemm(a, oh, w.enc_lin[c.obs_depth - 1], out, c.embed_dim, n), s));
     launches = k + 1;
     return cudaSuccess;
 }
 
-cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, cudaStream_t s) {
+cudaError_t LewmModel::encode_pixels_body(const float* pix, uint32_t n, float* out, cudaStream_t s) {
+    const SplitScratch* sp = &split;
     const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p, np = side * side, t = np + 1;
     const uint32_t kdim = c.channels * p * p, H = c.vit_heads, dh = vh / H;
     size_t off = 0;
@@ -391,32 +402,103 @@ cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, c
     const uint32_t rows = n * t;
     int k = 0;
     LWM_CU(launch_patchify(pix, f_patch, n, c.channels, c.image_size, p, s));
-    LWM_CU(gemm_f32(gemm(f_patch, kdim, w.patch, f_pe, vh, n * np), s));
+    LWM_CU(gemm_f32(sp, gemm(f_patch, kdim, w.patch, f_pe, vh, n * np), s));
     LWM_CU(launch_vit_assemble(f_pe, w.cls, w.vpos, f_x, n, np, vh, s));
     k += 3;
     const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
     for (uint32_t l = 0; l < c.vit_layers; ++l) {
         const VitBlockW& b = w.vit[l];
         LWM_CU(launch_layernorm(f_x, f_y, rows, vh, 1, 0, b.ln1.w, b.ln1.b, c.vit_eps, s));
-        LWM_CU(gemm_f32(gemm(f_y, vh, b.q, f_qkv, 3 * vh, rows), s));
-        LWM_CU(gemm_f32(gemm(f_y, vh, b.k, f_qkv + vh, 3 * vh, rows), s));
-        LWM_CU(gemm_f32(gemm(f_y, vh, b.v, f_qkv + 2 * vh, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.q, f_qkv, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.k, f_qkv + vh, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.v, f_qkv + 2 * vh, 3 * vh, rows), s));
         LWM_CU(launch_attention(f_qkv, f_att, n, t, H, dh, scale, 0, 0, s));
         GemmArgs go = gemm(f_att, vh, b.o, f_x, vh, rows);
         go.residual = 1;
-        LWM_CU(gemm_f32(go, s));
+        LWM_CU(gemm_f32(sp, go, s));
         LWM_CU(launch_layernorm(f_x, f_y, rows, vh, 1, 0, b.ln2.w, b.ln2.b, c.vit_eps, s));
-        LWM_CU(gemm_f32(gemm(f_y, vh, b.fc1, f_f, c.vit_mlp, rows, kActGeluErf), s));
+        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.fc1, f_f, c.vit_mlp, rows, kActGeluErf), s));
         GemmArgs g2 = gemm(f_f, c.vit_mlp, b.fc2, f_x, vh, rows);
         g2.residual = 1;
-        LWM_CU(gemm_f32(g2, s));
+        LWM_CU(gemm_f32(sp, g2, s));
         k += 9;
     }
     LWM_CU(launch_layernorm(f_x, f_cls, n, vh, t, 0, w.vit_norm.w, w.vit_norm.b, c.vit_eps, s));
     ++k;
-    LWM_CU(mlp(w.projector, f_cls, n, f_ph, out, s, k));
+    LWM_CU(mlp(sp, w.projector, f_cls, n, f_ph, out, s, k));
     launches = k;
     return cudaSuccess;
+}
+
+void GraphCache::reset() {
+    if (exec) cudaGraphExecDestroy(exec);
+    exec = nullptr;
+    seen = false;
+}
+
+cudaError_t LewmModel::ensure_split() {
+    // 4 M floats of partial tiles (16 splits of 64 tiles) and 64 K tile counters
+    if (split.partial) return cudaSuccess;
+    constexpr size_t kPartial = static_cast<size_t>(4) << 20, kCounters = 65536;
+    LWM_CU(cudaMalloc(&split.partial, kPartial * sizeof(float)));
+    LWM_CU(cudaMalloc(&split.counters, kCounters * sizeof(unsigned int)));
+    LWM_CU(cudaMemset(split.counters, 0, kCounters * sizeof(unsigned int)));
+    split.floats = kPartial;
+    split.n_counters = kCounters;
+    return cudaSuccess;
+}
+
+namespace {
+
+// Runs `body` through `cache`: the first call of a key runs it directly (so
+// its workspaces get allocated), the second captures it into a CUDA graph,
+// later calls replay the graph.
+template <class F>
+cudaError_t run_graphed(GraphCache& cache, const uint64_t (&key)[GraphCache::kKey], cudaStream_t s, int& launches,
+                        F&& body) {
+    const bool same = cache.seen && std::memcmp(cache.key, key, sizeof key) == 0;
+    if (same && cache.exec) {
+        launches = cache.launches;
+        return cudaGraphLaunch(cache.exec, s);
+    }
+    if (!same) {
+        cache.reset();
+        std::memcpy(cache.key, key, sizeof key);
+        LWM_CU(body());
+        cache.seen = true;
+        return cudaSuccess;
+    }
+    cudaGraph_t graph = nullptr;
+    LWM_CU(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t e = body();
+    const cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return e != cudaSuccess ? e : e2;
+    }
+    const cudaError_t e3 = cudaGraphInstantiate(&cache.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    LWM_CU(e3);
+    cache.launches = launches;
+    return cudaGraphLaunch(cache.exec, s);
+}
+
+inline uint64_t u(const void* p) { return reinterpret_cast<uint64_t>(p); }
+
+}  // namespace
+
+cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb,
+                             cudaStream_t s) {
+    LWM_CU(ensure_split());
+    const uint64_t key[GraphCache::kKey] = {u(cand), u(scores), u(last_emb), S, T, B, u(emb), u(goal), h, history,
+                                            u(ws.ptr), ws.floats, u(s), 1};
+    return run_graphed(g_score, key, s, launches, [&] { return score_body(cand, S, T, scores, last_emb, s); });
+}
+
+cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, cudaStream_t s) {
+    LWM_CU(ensure_split());
+    const uint64_t key[GraphCache::kKey] = {u(pix), n, u(out), u(enc.ptr), enc.floats, u(s), 2};
+    return run_graphed(g_enc, key, s, launches, [&] { return encode_pixels_body(pix, n, out, s); });
 }
 
 }  // namespace lwm

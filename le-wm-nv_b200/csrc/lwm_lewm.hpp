@@ -35,9 +35,23 @@ struct GemmArgs {
     const float* gate;    // gate table, row map.row(m), stride ldg, or nullptr
     uint32_t ldg;
     RowMap map;
+    // split-K (set by gemm_f32): partial tiles and per-tile arrival counters
+    uint32_t splits, k_chunk;
+    float* partial;
+    unsigned int* counters;
 };
 
-cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t s);
+// Split-K scratch shared by the GEMMs of one stream (they run in order).
+struct SplitScratch {
+    float* partial = nullptr;
+    size_t floats = 0;
+    unsigned int* counters = nullptr;  // zero between GEMMs (the last CTA of a tile resets its counter)
+    size_t n_counters = 0;
+};
+
+// Launches C = A W^T (+ epilogue); splits K over CTAs (deterministically) when
+// `split` is given and the output tiles alone would leave most SMs idle.
+cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t s, const SplitScratch* split);
 cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
                           uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b,
                           cudaStream_t s);
@@ -116,6 +130,17 @@ struct Arena {
     void release();
 };
 
+// One captured launch sequence, replayed while its key (shapes and every
+// buffer address it touches) stays the same.
+struct GraphCache {
+    static constexpr int kKey = 14;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t key[kKey] = {};
+    bool seen = false;  // the key ran once uncaptured (workspaces allocated)
+    int launches = 0;
+    void reset();
+};
+
 struct LewmModel {
     lwm_lewm_config c{};
     LewmWeights w;
@@ -127,8 +152,13 @@ struct LewmModel {
     size_t ctx_cap = 0;
     Arena ws;               // rollout workspace
     Arena enc;              // encoder workspace
+    SplitScratch split;     // split-K partial tiles
+    GraphCache g_score, g_enc;
     int launches = 0;
     ~LewmModel();
+    cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
+    cudaError_t encode_pixels_body(const float* pixels, uint32_t n, float* out, cudaStream_t s);
+    cudaError_t ensure_split();
     // scores [B,S] of candidates [B,S,T,A] (all device)
     cudaError_t score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s);

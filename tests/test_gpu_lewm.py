@@ -126,3 +126,19 @@ def test_lewm_validation(ctx):
     sc.set_context(np.zeros((1, 1, 192), np.float32), np.zeros((1, 192), np.float32))
     with pytest.raises(L.LwmError, match="do not match"):
         _score(ctx, sc, np.zeros((1, 4, 5, 3), np.float32))
+
+
+def test_vector_mppi_matches_oracle(ctx):
+    # MPPI over the LeWM scorer takes the generic sample -> score -> reduce path
+    w = W.lewm_vector(seed=12)
+    sc, emb, goal = _vector_context(ctx, w)
+    e, g = emb.cpu().numpy()[:, None, :], goal.cpu().numpy()
+    sc.set_context(e, g)
+    cfg = L.MppiConfig(horizon=5, samples=256, action_dim=2, iterations=2,
+                       action_bounds=L.ActionBounds.symmetric(2, 1.0), noise_std=1.0, temperature=0.5)
+    noise = normals(57, (2, 1, 256, 5, 2))
+    r = L.MppiPlanner(ctx, cfg).plan(sc, injected_noise=noise)
+    m = O.LewmModel(w.config, w.weights)
+    ref = O.mppi_plan(cfg, 1, (O.LEWM_FN, m.score_ctx(e, g)), noise=noise)
+    assert_costs_close(r.scores, ref["scores"])
+    assert_actions_close(r.sequence, ref["sequence"])
