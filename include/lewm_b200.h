@@ -302,6 +302,20 @@ lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* scorer, uint32_t batch,
                                              const float* reference_actions,
                                              const float* vehicle_mass);
 
+/* Arithmetic of the learned scorer's fused MPPI iterations.
+ * LWM_PRECISION_F32 (default): the f32 CUDA-core rollout.
+ * LWM_PRECISION_BF16: bf16 weights and recurrent state on the tcgen05 tensor
+ * cores with f32 accumulation, f32 gates / prober tail / integrator, for
+ * plans whose sample count is a multiple of 128 (latent 256, 4 actions,
+ * 4-channel action encoder with kernel 3 over a 10-step history, prober
+ * hidden 32); other shapes keep the f32 rollout.  Costs agree with f32
+ * within about 2e-2 relative. */
+typedef enum lwm_precision {
+    LWM_PRECISION_F32 = 0,
+    LWM_PRECISION_BF16 = 1,
+} lwm_precision;
+lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* scorer, int32_t precision);
+
 /* A scorer supplied by the caller: the CandidateScorer trait
  * (src/planner.rs:25-32).  The callback receives device pointers on the
  * context's stream: candidates [B,S,T,A] f32 and scores [B,S] f32 to fill,

@@ -148,6 +148,10 @@ struct lwm_scorer {
     void* user = nullptr;
     // LeWM world model
     std::unique_ptr<lwm::LewmModel> lewm;
+    // learned scorer on tensor cores (bf16): packed weights, per-vehicle h0, wait-timeout flag
+    int32_t precision = LWM_PRECISION_F32;
+    DevBuf tc_packed, tc_h0, tc_err;
+    bool tc_ready = false;
 };
 
 struct lwm_planner {
@@ -433,6 +437,18 @@ lwm::NominalArgs nominal_args(lwm_scorer* sc, uint32_t S) {
     return a;
 }
 
+// Packed bf16 weights (once per scorer), per-vehicle h0 and the error flag.
+lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B) {
+    if (!sc->tc_ready) {
+        LWM_TRY(sc->tc_packed.ensure(lwm::skyjepa_tc_packed_bytes()));
+        LWM_CUDA(lwm::skyjepa_tc_pack(a, sc->tc_packed.as<uint8_t>(), sc->ctx->stream));
+        LWM_TRY(sc->tc_err.ensure(256));
+        sc->tc_ready = true;
+    }
+    LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    return LWM_OK;
+}
+
 lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
     lwm::SkyjepaArgs a = sc->sky_args;
     a.B = sc->batch;
@@ -656,7 +672,16 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 a.m = m;
                 a.m.P = lwm::skyjepa_partials_per_vehicle(p->S, a.rows);
                 int launched = 0;
-                LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
+                const char* why = nullptr;
+                if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
+                    LWM_TRY(ensure_tc(sc, a, B));
+                    a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
+                    LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
+                                                    sc->tc_err.as<int>(), stream, &launched));
+                } else {
+                    LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
+                }
                 p->ctx->launches += static_cast<uint64_t>(launched);
             }
         } else {
@@ -1277,6 +1302,15 @@ lwm_status lwm_lewm_encode_pixels_device(lwm_scorer* s, const float* pixels, uin
     return LWM_OK;
 }
 
+lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* s, int32_t precision) {
+    if (!s || s->kind != ScorerKind::Skyjepa) return fail(LWM_INVALID_ARGUMENT, "not a SkyJEPA scorer");
+    if (precision != LWM_PRECISION_F32 && precision != LWM_PRECISION_BF16)
+        return fail(LWM_INVALID_ARGUMENT, "unknown precision " + std::to_string(precision));
+    std::lock_guard<std::mutex> lock(s->mu);
+    s->precision = precision;
+    return LWM_OK;
+}
+
 lwm_status lwm_scorer_callback_create(lwm_ctx* ctx, uint32_t batch, lwm_score_fn fn, void* user, lwm_scorer** out) {
     if (!ctx || !fn || !out || batch == 0) return fail(LWM_INVALID_ARGUMENT, "invalid callback scorer arguments");
     lwm_scorer* s = new_scorer(ctx, ScorerKind::Callback);
@@ -1316,6 +1350,9 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->lewm.reset();
     if (s->staged) cudaEventDestroy(s->staged);
     s->weights.release();
+    s->tc_packed.release();
+    s->tc_h0.release();
+    s->tc_err.release();
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;
@@ -1428,7 +1465,13 @@ lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_p
         LWM_CUDA(cudaMemcpyAsync(h + off_sc, d.scores, nsc * 4, cudaMemcpyDeviceToHost, stream));
     }
     if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
+    int tc_err[4] = {0, 0, 0, 0};
+    if (sc->tc_err.ptr) LWM_CUDA(cudaMemcpyAsync(tc_err, sc->tc_err.ptr, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
     LWM_CUDA(cudaStreamSynchronize(stream));
+    if (tc_err[0])
+        return fail(LWM_TIMEOUT, "a tensor-core pipeline wait timed out on the device (site " + std::to_string(tc_err[0]) +
+                                     ", block " + std::to_string(tc_err[1]) + ", index " + std::to_string(tc_err[2]) +
+                                     ", parity " + std::to_string(tc_err[3]) + ")");
     if (out->first_action) std::memcpy(out->first_action, h + off_fa, B * p->A * 4);
     if (out->sequence) std::memcpy(out->sequence, h + off_seq, seq * 4);
     if (out->scores) std::memcpy(out->scores, h + off_sc, nsc * 4);

@@ -90,16 +90,6 @@ struct SkySmem {
     uint32_t w1_stride, pw_stride, sw_half;
 };
 
-// Floats of the action encoder's weights (contiguous in the blob).
-__host__ __device__ inline uint32_t tcn_weight_floats(const TcnView& t) {
-    uint32_t n = 0;
-    for (uint32_t l = 0; l < t.levels; ++l) {
-        const TcnBlockView& b = t.blocks[l];
-        n += b.out * b.in * t.k + b.out + b.out * b.out * t.k + b.out;
-        if (b.in != b.out) n += b.out * b.in + b.out;
-    }
-    return n;
-}
 
 // rows = M rows per cluster; Cs = widest state-TCN layer; Ca = action-TCN
 // lanes per window (power of two).

@@ -1,0 +1,855 @@
+// kernels_skyjepa_tc.cu — learned SkyJEPA MPPI on the 5th-generation tensor
+// cores (tcgen05, bf16 operands, f32 accumulation in TMEM) for large
+// candidate counts (the fleet: hundreds of vehicles x thousands of samples).
+//
+// Same computation as skyjepa_rollout_kernel (SkyJepaMppiScorer,
+// src/models/skyjepa/control.rs:146-317; GRU rollout model.rs:105-223; TCN
+// tcn.rs; prober prober.rs:84-138; integrator kinematics.rs:377-484; cost
+// control.rs:430-452; MPPI src/planner.rs:1588-1602) with the recurrent GEMM
+// on tensor cores:
+//
+//   per CTA, persistent over 128-candidate tiles of one vehicle; per step t
+//   and per chunk of 32 hidden units (8 chunks):
+//     D[128 x 128] = X_t[128 x 16] . Wx_c^T          (r | z | n_h | n_x cols)
+//     D[:, 0:96]  += H_t[128 x 256] . Whh_c^T         (16 MMAs, K = 256)
+//   then the GRU gates of those 32 units for the 128 rows (f32), with h_t in
+//   TMEM (f32) and in shared memory (bf16, the next step's A operand).
+//   The prober's first layer is one more MMA per step (A = h_{t+1}).
+//
+// Roles (448 threads): warp 0 streams the weight chunks (bulk copies, two
+// slots); warp 1 issues the MMAs and owns TMEM; warps 2-9 run the GRU
+// epilogue (two warps per TMEM lane quadrant, 16 units each); warps 10-13
+// (one thread per candidate) sample the candidates, compute the action-TCN
+// input of the next step, finish the prober, integrate, accumulate the cost
+// and reduce the tile to an MPPI tuple.  All hand-offs are mbarriers with
+// bounded waits; a wait that gives up raises *err and the kernel unwinds.
+//
+// TMEM (512 columns): accumulator slots 0 and 1 = columns [0,128) and
+// [128,256); h_t (f32) = columns [256,512).  Weights are bf16 (packed once
+// per scorer by pack_tc_weights_kernel); biases, the prober's later layers,
+// the TCN and the integrator stay f32.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "lwm_device.cuh"
+#include "lwm_kernels.hpp"
+#include "lwm_tc.cuh"
+
+namespace lwm {
+
+namespace {
+
+constexpr uint32_t kRows = 128, kH = 256, kChunks = 8;
+constexpr uint32_t kChunkHBytes = 4 * 96 * 128;  // 4 K-blocks x 96 rows (r, z, n_h) x 128 B
+constexpr uint32_t kChunkXBytes = 128 * 32;      // 128 rows (r, z, n_h, n_x) x 16 k (SW32)
+constexpr uint32_t kChunkBytes = kChunkHBytes + kChunkXBytes;
+constexpr uint32_t kABytes = 4 * 128 * 128;
+constexpr uint32_t kXBytes = 128 * 32;
+constexpr uint32_t kMaxHid = 32, kMaxLayers = 3;
+constexpr uint32_t kP1Bytes = 4 * kMaxHid * 128;
+constexpr uint32_t kPwFloats = kMaxHid + (kMaxLayers - 1) * (kMaxHid * kMaxHid + kMaxHid) + 16 * kMaxHid + 16;
+constexpr uint32_t kTcnFloats = 1024;
+constexpr int kThreadsTc = 448;
+constexpr uint32_t kAuxWarp0 = 10, kEpiWarp0 = 2;
+constexpr uint32_t kAuxBarrier = 3, kAuxThreads = 128;
+constexpr uint32_t kMaxHistTc = 16;
+
+struct __align__(1024) TcSmem {
+    uint8_t A[kABytes];
+    uint8_t W[2][kChunkBytes];
+    uint8_t X[2][kXBytes];
+    uint8_t P1[kP1Bytes];
+    float gbias[4][kH];   // r (b_ir + b_hr), z (b_iz + b_hz), n_x (b_in), n_h (b_hn)
+    float pw[kPwFloats];  // prober: b1, hidden layers (W, b), output (W, b)
+    float tcn[kTcnFloats];
+    float red_w[kRows];
+    uint64_t red_key[4];
+    float red_f[4];
+    // accumulator slots are shared by two consumer groups (0: GRU epilogue,
+    // 1: prober/aux); each group has its own full/empty barrier per slot so
+    // every waiter sees every phase of the barriers it waits on
+    uint64_t w_full[2], w_empty[2], full[2][2], empty[2][2], x_full[2], x_empty[2], h_full, a_read, done;
+    uint32_t tmem;
+    int last;
+};
+
+__device__ __forceinline__ void aux_sync() {
+    asm volatile("bar.sync %0, %1;" ::"n"(kAuxBarrier), "n"(kAuxThreads) : "memory");
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) { return __frcp_rn(1.0f + __expf(-v)); }
+
+// Two f32 -> packed bf16x2 (the first value at the lower address).
+__device__ __forceinline__ uint32_t bf2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// 16 f32 values as bf16 into two 16-byte chunks of a K-major tile row.
+__device__ __forceinline__ void store_bf16x16(uint8_t* dst0, uint8_t* dst1, const float (&v)[16]) {
+    *reinterpret_cast<uint4*>(dst0) = make_uint4(bf2(v[0], v[1]), bf2(v[2], v[3]), bf2(v[4], v[5]), bf2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(dst1) =
+        make_uint4(bf2(v[8], v[9]), bf2(v[10], v[11]), bf2(v[12], v[13]), bf2(v[14], v[15]));
+}
+
+// The element (row, k) of the prober / recurrent weights in the packed layouts.
+__host__ __device__ inline uint32_t packed_h_offset(uint32_t j, uint32_t k, uint32_t rows) {
+    return (k >> 6) * rows * 128u + tc::sw128_offset(j, k & 63u);
+}
+
+}  // namespace
+
+// ------------------------------------------------------- weight packing
+//
+// Wc[chunk]: H part (rows r_u, z_u, n_u of the chunk's 32 units, K = 256 of
+// weight_hh) in SW128 K-blocks, then the X part (rows r, z, 0, n of
+// weight_ih, K = E <= 16) in SW32.  P1: prober input layer [hid x 256].
+__global__ void pack_tc_weights_kernel(SkyjepaArgs a, uint8_t* wc, uint8_t* p1) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t n_h = static_cast<size_t>(kChunks) * 96 * kH;
+    const size_t n_x = static_cast<size_t>(kChunks) * 128 * 16;
+    const size_t n_p = static_cast<size_t>(a.hid) * kH;
+    if (i < n_h) {
+        const uint32_t c = static_cast<uint32_t>(i / (96 * kH)), rem = static_cast<uint32_t>(i % (96 * kH));
+        const uint32_t j = rem / kH, k = rem % kH, g = j / 32, u = c * 32 + j % 32;
+        const float v = a.w_hh[static_cast<size_t>(g * kH + u) * kH + k];
+        *reinterpret_cast<__nv_bfloat16*>(wc + static_cast<size_t>(c) * kChunkBytes + packed_h_offset(j, k, 96)) =
+            __float2bfloat16_rn(v);
+    } else if (i < n_h + n_x) {
+        const size_t q = i - n_h;
+        const uint32_t c = static_cast<uint32_t>(q / (128 * 16)), rem = static_cast<uint32_t>(q % (128 * 16));
+        const uint32_t j = rem / 16, k = rem % 16, g = j / 32, u = c * 32 + j % 32;
+        float v = 0.0f;
+        if (k < a.E && g != 2) {
+            const uint32_t gate = g == 3 ? 2u : g;  // n_x uses weight_ih's n rows
+            v = a.w_ih[static_cast<size_t>(gate * kH + u) * a.E + k];
+        }
+        *reinterpret_cast<__nv_bfloat16*>(wc + static_cast<size_t>(c) * kChunkBytes + kChunkHBytes +
+                                          tc::sw32_offset(j, k)) = __float2bfloat16_rn(v);
+    } else if (i < n_h + n_x + n_p) {
+        const size_t q = i - n_h - n_x;
+        const uint32_t j = static_cast<uint32_t>(q / kH), k = static_cast<uint32_t>(q % kH);
+        *reinterpret_cast<__nv_bfloat16*>(p1 + packed_h_offset(j, k, a.hid)) =
+            __float2bfloat16_rn(a.p_in_w[static_cast<size_t>(j) * kH + k]);
+    }
+}
+
+// --------------------------------------------------- initial latent h0
+//
+// encode_state_history (model.rs:57-61): the state TCN over the normalised
+// history, last step, state_projection.  One block per vehicle.
+__global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h0) {
+    extern __shared__ float sh[];
+    const uint32_t b = blockIdx.x, tid = threadIdx.x, Hs = a.Hs;
+    const TcnView& tcn = a.state_tcn;
+    const uint32_t C = tcn.max_ch;
+    float* cur = sh;                 // [C][Hs]
+    float* h1 = cur + C * Hs;        // [C][Hs]
+    float* h2 = h1 + C * Hs;         // [C][Hs]
+    for (uint32_t q = tid; q < 18 * Hs; q += blockDim.x) {
+        const uint32_t i = q / Hs, t = q % Hs;
+        const float v = a.state_hist[(static_cast<size_t>(b) * Hs + t) * 18 + i];
+        cur[i * Hs + t] = (v - a.state_mean[i]) / a.state_std[i];
+    }
+    __syncthreads();
+    for (uint32_t l = 0; l < tcn.levels; ++l) {
+        const TcnBlockView& bk = tcn.blocks[l];
+        for (int conv = 0; conv < 2; ++conv) {
+            const float* src = conv == 0 ? cur : h1;
+            float* dst = conv == 0 ? h1 : h2;
+            const uint32_t cin = conv == 0 ? bk.in : bk.out;
+            const float* W = conv == 0 ? bk.w1 : bk.w2;
+            const float* bias = conv == 0 ? bk.b1 : bk.b2;
+            for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) {
+                const uint32_t o = q / Hs, t = q % Hs;
+                float acc = 0.0f;
+                for (uint32_t i = 0; i < cin; ++i)
+                    for (uint32_t j = 0; j < tcn.k; ++j) {
+                        const int src_t = static_cast<int>(t) - static_cast<int>((tcn.k - 1 - j) * bk.dil);
+                        if (src_t >= 0) acc = fmaf(W[(o * cin + i) * tcn.k + j], src[i * Hs + src_t], acc);
+                    }
+                dst[o * Hs + t] = gelu_tanh(acc + bias[o]);
+            }
+            __syncthreads();
+        }
+        for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) {
+            const uint32_t o = q / Hs, t = q % Hs;
+            float res;
+            if (bk.wr) {
+                float r = 0.0f;
+                for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(bk.wr[o * bk.in + i], cur[i * Hs + t], r);
+                res = r + bk.br[o];
+            } else {
+                res = cur[o * Hs + t];
+            }
+            h1[o * Hs + t] = gelu_tanh(h2[o * Hs + t] + res);
+        }
+        __syncthreads();
+        for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) cur[q] = h1[q];
+        __syncthreads();
+    }
+    for (uint32_t u = tid; u < a.H; u += blockDim.x) {
+        float acc = 0.0f;
+        for (uint32_t c = 0; c < tcn.out_dim; ++c) acc = fmaf(a.proj_w[u * tcn.out_dim + c], cur[c * Hs + Hs - 1], acc);
+        h0[static_cast<size_t>(b) * a.H + u] = acc + a.proj_b[u];
+    }
+}
+
+// ------------------------------------------------------------ main kernel
+
+namespace {
+
+struct TcArgs {
+    SkyjepaArgs a;
+    const uint8_t* wc;  // packed chunks
+    const uint8_t* p1;  // packed prober layer 1
+    const float* h0;    // [B, 256]
+    uint32_t tiles_per_vehicle, tiles;
+    int* err;
+};
+
+// Action-TCN input of step t for one candidate (TemporalConvEncoder over the
+// window [history ++ candidate](t : t + 10), last position), written as bf16
+// into the X tile.  One thread per candidate, everything in registers: the
+// tensor-core path takes the 4-channel encoder with kernel 3 over a 10-step
+// window (compile-time sizes keep the window in registers).
+constexpr int kTcnHs = 10, kTcnK = 3, kTcnC = 4;
+
+template <int DIL>
+__device__ __forceinline__ void tcn_conv(const float (&in)[kTcnC][kTcnHs], const float* W, const float* B,
+                                         float (&out)[kTcnC][kTcnHs]) {
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o)
+#pragma unroll
+        for (int w = 0; w < kTcnHs; ++w) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kTcnC; ++i)
+#pragma unroll
+                for (int j = 0; j < kTcnK; ++j) {
+                    const int src = w - (kTcnK - 1 - j) * DIL;
+                    if (src >= 0) acc = fmaf(W[(o * kTcnC + i) * kTcnK + j], in[i][src], acc);
+                }
+            out[o][w] = gelu_tanh(acc + B[o]);
+        }
+}
+
+template <int DIL>
+__device__ __forceinline__ void tcn_block(float (&cur)[kTcnC][kTcnHs], const float* w1, const float* b1,
+                                          const float* w2, const float* b2) {
+    float h1[kTcnC][kTcnHs], h2[kTcnC][kTcnHs];
+    tcn_conv<DIL>(cur, w1, b1, h1);
+    tcn_conv<DIL>(h1, w2, b2, h2);
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o)
+#pragma unroll
+        for (int w = 0; w < kTcnHs; ++w) cur[o][w] = gelu_tanh(h2[o][w] + cur[o][w]);
+}
+
+__device__ void action_tcn_step(const TcArgs& p, const TcSmem& s, const float* cand_row, uint32_t b, uint32_t t,
+                                uint32_t row, uint8_t* xtile) {
+    const SkyjepaArgs& a = p.a;
+    const TcnView& tcn = a.action_tcn;
+    const float* wbase = tcn.blocks[0].w1;
+    float cur[kTcnC][kTcnHs];
+#pragma unroll
+    for (int w = 0; w < kTcnHs; ++w) {
+        const uint32_t pos = t + w;
+        const float* src = pos < kTcnHs - 1 ? a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4
+                                            : cand_row + (pos - (kTcnHs - 1)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        cur[0][w] = (v.x - a.action_mean[0]) / a.action_std[0];
+        cur[1][w] = (v.y - a.action_mean[1]) / a.action_std[1];
+        cur[2][w] = (v.z - a.action_mean[2]) / a.action_std[2];
+        cur[3][w] = (v.w - a.action_mean[3]) / a.action_std[3];
+    }
+    for (uint32_t l = 0; l < tcn.levels; ++l) {
+        const TcnBlockView& bk = tcn.blocks[l];
+        const float* w1 = s.tcn + (bk.w1 - wbase);
+        const float* b1 = s.tcn + (bk.b1 - wbase);
+        const float* w2 = s.tcn + (bk.w2 - wbase);
+        const float* b2 = s.tcn + (bk.b2 - wbase);
+        switch (bk.dil) {
+            case 1: tcn_block<1>(cur, w1, b1, w2, b2); break;
+            case 2: tcn_block<2>(cur, w1, b1, w2, b2); break;
+            case 4: tcn_block<4>(cur, w1, b1, w2, b2); break;
+            default: tcn_block<8>(cur, w1, b1, w2, b2); break;
+        }
+    }
+    *reinterpret_cast<uint4*>(xtile + tc::sw32_offset(row, 0)) =
+        make_uint4(bf2(cur[0][kTcnHs - 1], cur[1][kTcnHs - 1]), bf2(cur[2][kTcnHs - 1], cur[3][kTcnHs - 1]), 0u, 0u);
+    *reinterpret_cast<uint4*>(xtile + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const SkyjepaArgs& a = p.a;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t T = a.T, hid = a.hid;
+    volatile int* err = p.err;
+
+    // ---- setup: barriers, TMEM, resident weights
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&s.w_full[i], 1);
+            tc::mbar_init(&s.w_empty[i], 1);
+            tc::mbar_init(&s.full[0][i], 1);
+            tc::mbar_init(&s.full[1][i], 1);
+            tc::mbar_init(&s.empty[0][i], 8);
+            tc::mbar_init(&s.empty[1][i], 4);
+            tc::mbar_init(&s.x_full[i], 4);
+            tc::mbar_init(&s.x_empty[i], 1);
+        }
+        tc::mbar_init(&s.h_full, 8);
+        tc::mbar_init(&s.a_read, 1);
+        tc::mbar_init(&s.done, 1);
+        tc::mbar_fence_init();
+    }
+    if (warp == 1) tc::tmem_alloc(&s.tmem, 512);
+    for (uint32_t q = tid; q < kP1Bytes / 16; q += kThreadsTc)
+        reinterpret_cast<uint4*>(s.P1)[q] =
+            q < hid * 4 * 128 / 16 ? reinterpret_cast<const uint4*>(p.p1)[q] : make_uint4(0, 0, 0, 0);
+    for (uint32_t u = tid; u < kH; u += kThreadsTc) {
+        s.gbias[0][u] = a.b_ih[u] + a.b_hh[u];
+        s.gbias[1][u] = a.b_ih[kH + u] + a.b_hh[kH + u];
+        s.gbias[2][u] = a.b_ih[2 * kH + u];
+        s.gbias[3][u] = a.b_hh[2 * kH + u];
+    }
+    {
+        // prober: b1 [hid], hidden l: W [hid*hid], b [hid], output W [15*hid], b [15]
+        float* pw = s.pw;
+        for (uint32_t q = tid; q < hid; q += kThreadsTc) pw[q] = a.p_in_b[q];
+        uint32_t off = hid;
+        for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
+            for (uint32_t q = tid; q < hid * hid; q += kThreadsTc) pw[off + q] = a.p_hid_w[l][q];
+            for (uint32_t q = tid; q < hid; q += kThreadsTc) pw[off + hid * hid + q] = a.p_hid_b[l][q];
+            off += hid * hid + hid;
+        }
+        for (uint32_t q = tid; q < 15 * hid; q += kThreadsTc) pw[off + q] = a.p_out_w[q];
+        for (uint32_t q = tid; q < 15; q += kThreadsTc) pw[off + 15 * hid + q] = a.p_out_b[q];
+        const uint32_t n = tcn_weight_floats(a.action_tcn);
+        for (uint32_t q = tid; q < n; q += kThreadsTc) s.tcn[q] = a.action_tcn.blocks[0].w1[q];
+    }
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = s.tmem;
+    const uint32_t entries = 9 * T + 1;  // acc-ring entries per tile
+
+    if (warp == 0) {
+        // ================= producer: weight chunks, 2 slots
+        if (lane == 0) {
+            uint32_t j = 0;
+            for (uint32_t tile = blockIdx.x; tile < p.tiles && !err[0]; tile += gridDim.x)
+                for (uint32_t t = 0; t < T && !err[0]; ++t)
+                    for (uint32_t c = 0; c < kChunks; ++c, ++j) {
+                        const uint32_t slot = j & 1u, n = j >> 1;
+                        if (!tc::mbar_wait(&s.w_empty[slot], (n & 1u) ^ 1u, err, 1, j)) break;
+                        tc::mbar_expect_tx(&s.w_full[slot], kChunkBytes);
+                        tc::bulk_g2s(s.W[slot], p.wc + static_cast<size_t>(c) * kChunkBytes, kChunkBytes,
+                                     &s.w_full[slot]);
+                    }
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer
+        if (lane == 0) {
+            const uint32_t id_gru_x = tc::idesc_bf16_f32(128, 128), id_gru_h = tc::idesc_bf16_f32(128, 96);
+            const uint32_t id_prob = tc::idesc_bf16_f32(128, hid);
+            const uint32_t a_base = tc::smem_u32(s.A), p_base = tc::smem_u32(s.P1);
+            uint32_t j = 0, K = 0, xs = 0, hq = 0;
+            uint32_t uses[2][2] = {{0, 0}, {0, 0}};
+            int last[2] = {-1, -1};
+            // entry K goes to slot K & 1: wait until the slot's previous consumer group released it
+            auto acc_slot = [&](uint32_t k, uint32_t& col) -> bool {
+                const uint32_t slot = k & 1u;
+                col = slot * 128u;
+                if (last[slot] < 0) return true;
+                const int g = last[slot];
+                return tc::mbar_wait(&s.empty[g][slot], (uses[g][slot] - 1u) & 1u, err, 5, k);
+            };
+            auto publish = [&](uint32_t k, int g) {
+                const uint32_t slot = k & 1u;
+                tc::commit(&s.full[g][slot]);
+                ++uses[g][slot];
+                last[slot] = g;
+            };
+            auto prober = [&](bool real) -> bool {
+                uint32_t col;
+                if (!acc_slot(K, col)) return false;
+                tc::fence_after();
+                if (real)
+                    for (uint32_t ks = 0; ks < 16; ++ks) {
+                        const uint32_t kb = ks >> 2, jj = ks & 3u;
+                        tc::mma_bf16(tmem + col, tc::smem_desc(a_base + kb * 128 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
+                                     tc::smem_desc(p_base + kb * hid * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
+                                     id_prob, ks > 0);
+                    }
+                publish(K, 1);
+                ++K;
+                return true;
+            };
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+                for (uint32_t t = 0; ok && t < T; ++t) {
+                    ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq);  // A holds h_t
+                    ++hq;
+                    const uint32_t xslot = xs & 1u;
+                    if (ok) ok = tc::mbar_wait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs);
+                    for (uint32_t c = 0; ok && c < kChunks; ++c, ++j) {
+                        if (c == 1 && !(ok = prober(t > 0))) break;  // prober of step t-1 (A = h_t)
+                        const uint32_t wslot = j & 1u;
+                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j >> 1) & 1u, err, 4, j))) break;
+                        uint32_t col;
+                        if (!(ok = acc_slot(K, col))) break;
+                        tc::fence_after();
+                        const uint32_t w_base = tc::smem_u32(s.W[wslot]);
+                        tc::mma_bf16(tmem + col, tc::smem_desc(tc::smem_u32(s.X[xslot]), 16, 256, tc::kSwizzle32),
+                                     tc::smem_desc(w_base + kChunkHBytes, 16, 256, tc::kSwizzle32), id_gru_x, 0);
+                        for (uint32_t ks = 0; ks < 16; ++ks) {
+                            const uint32_t kb = ks >> 2, jj = ks & 3u;
+                            tc::mma_bf16(tmem + col,
+                                         tc::smem_desc(a_base + kb * 128 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
+                                         tc::smem_desc(w_base + kb * 96 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
+                                         id_gru_h, 1);
+                        }
+                        publish(K, 0);
+                        tc::commit(&s.w_empty[wslot]);
+                        if (c == kChunks - 1) tc::commit(&s.x_empty[xslot]);
+                        ++K;
+                    }
+                    ++xs;
+                }
+                if (ok) ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq);  // A holds h_T
+                ++hq;
+                if (ok) ok = prober(true);                           // prober of step T-1
+                if (ok) tc::commit(&s.a_read);                       // A is no longer read in this tile
+            }
+            // every MMA issued has completed before TMEM is released
+            tc::commit(&s.done);
+            tc::mbar_wait(&s.done, 0, err, 10, 0);
+        }
+    } else if (warp < kAuxWarp0) {
+        // ================= GRU epilogue: quadrant q, units [16 half, 16 half + 16) of each chunk
+        const uint32_t q = warp & 3u, half = (warp - kEpiWarp0) >> 2;
+        const uint32_t row = q * 32 + lane;
+        const uint32_t lane_base = tmem + ((q * 32) << 16);
+        uint32_t K0 = 0;  // acc-ring entry index of the tile's first entry
+        uint32_t eu[2] = {0, 0}, tiles_done = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+            const uint32_t b = tile / p.tiles_per_vehicle;
+            if (tiles_done > 0) {
+                // the previous tile's last prober MMA read A: wait for it before overwriting
+                if (!(ok = tc::mbar_wait(&s.a_read, (tiles_done - 1) & 1u, err, 7, tiles_done))) break;
+                tc::fence_after();
+            }
+            // h0 of the vehicle -> H (TMEM f32) and A (bf16), this warp's units
+            for (uint32_t c = 0; c < kChunks; ++c) {
+                const uint32_t u0 = c * 32 + half * 16;
+                float hv[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) hv[i] = __ldg(p.h0 + static_cast<size_t>(b) * kH + u0 + i);
+                tc::tmem_st16(lane_base + 256 + u0, hv);
+                uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
+                store_bf16x16(blk + tc::sw128_offset(row, u0 & 63u), blk + tc::sw128_offset(row, (u0 & 63u) + 8), hv);
+            }
+            tc::tmem_st_wait();
+            tc::fence_async_smem();
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s.h_full);
+            for (uint32_t t = 0; ok && t < T; ++t) {
+                for (uint32_t c = 0; c < kChunks; ++c) {
+                    const uint32_t k = K0 + 9 * t + (c == 0 ? 0u : c + 1u);
+                    const uint32_t slot = k & 1u;
+                    if (!(ok = tc::mbar_wait(&s.full[0][slot], eu[slot] & 1u, err, 6, k))) break;
+                    ++eu[slot];
+                    tc::fence_after();
+                    const uint32_t u0 = c * 32 + half * 16;
+                    const uint32_t acol = lane_base + slot * 128 + half * 16;
+                    float r[16], z[16], nh[16], nx[16], hv[16];
+                    tc::tmem_ld16(acol, r);
+                    tc::tmem_ld16(acol + 32, z);
+                    tc::tmem_ld16(acol + 64, nh);
+                    tc::tmem_ld16(acol + 96, nx);
+                    tc::tmem_ld16(lane_base + 256 + u0, hv);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const uint32_t u = u0 + i;
+                        const float rg = sigmoid_f(r[i] + s.gbias[0][u]);
+                        const float zg = sigmoid_f(z[i] + s.gbias[1][u]);
+                        const float ng = tanhf((nx[i] + s.gbias[2][u]) + rg * (nh[i] + s.gbias[3][u]));
+                        hv[i] = zg * hv[i] - (zg - 1.0f) * ng;  // GRU::step, h' = z h - (z - 1) n
+                    }
+                    tc::tmem_st16(lane_base + 256 + u0, hv);
+                    tc::tmem_st_wait();
+                    tc::fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.empty[0][slot]);
+                }
+                if (!ok) break;
+                // all MMAs of step t are done (the last chunk's completed): h_{t+1} -> A
+                for (uint32_t c = 0; c < kChunks; ++c) {
+                    const uint32_t u0 = c * 32 + half * 16;
+                    float hv[16];
+                    tc::tmem_ld16(lane_base + 256 + u0, hv);
+                    tc::tmem_ld_wait();
+                    uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
+                    store_bf16x16(blk + tc::sw128_offset(row, u0 & 63u), blk + tc::sw128_offset(row, (u0 & 63u) + 8),
+                                  hv);
+                }
+                tc::fence_async_smem();
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s.h_full);
+            }
+            K0 += entries;
+            ++tiles_done;
+        }
+    } else {
+        // ================= aux: one thread per candidate row
+        const uint32_t q = warp & 3u, row = q * 32 + lane, atid = tid - kAuxWarp0 * 32;
+        const uint32_t lane_base = tmem + ((q * 32) << 16);
+        const uint32_t TA = T * 4u;
+        uint32_t K0 = 0, xs = 0, au[2] = {0, 0};
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+            const uint32_t b = tile / p.tiles_per_vehicle, tv = tile % p.tiles_per_vehicle;
+            const uint32_t srow = tv * kRows + row;  // sample index within the shard
+            const size_t grow = static_cast<size_t>(b) * a.S + srow;
+            float* cand_row = a.cand_out + grow * TA;
+            // sampling (as sample_kernel / the fused kernels)
+            for (uint32_t e = 0; e < TA; ++e) {
+                const uint32_t act = e & 3u;
+                const size_t mi = static_cast<size_t>(b) * TA + e;
+                float v;
+                if (a.sample_base + srow == 0) {
+                    v = a.mean[mi];
+                } else {
+                    const uint64_t gi = global_row(b, srow, a.sample_base, a.sample_total, a.S) * TA + e;
+                    const float eps = a.noise ? a.noise[grow * TA + e] : normal_at(a.seed, a.offset + gi);
+                    v = a.mean[mi] + eps * a.std[mi];
+                }
+                cand_row[e] = cmin(cmax(v, a.low[act]), a.high[act]);
+            }
+            float x[18];
+#pragma unroll
+            for (int i = 0; i < 18; ++i) x[i] = a.state_hist[(static_cast<size_t>(b) * a.Hs + a.Hs - 1) * 18 + i];
+            const float mass = a.masses ? __ldg(a.masses + b) : a.mass;
+            float cost = 0.0f;
+            for (uint32_t t = 0; ok && t <= T; ++t) {
+                // (1) the action-TCN input of step t -> X ring
+                if (t < T) {
+                    const uint32_t xslot = xs & 1u;
+                    if (!(ok = tc::mbar_wait(&s.x_empty[xslot], ((xs >> 1) & 1u) ^ 1u, err, 8, xs))) break;
+                    action_tcn_step(p, s, cand_row, b, t, row, s.X[xslot]);
+                    tc::fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.x_full[xslot]);
+                    ++xs;
+                }
+                // (2) prober of step t-1 (entry 9t + 1; at t = 0 an empty entry; the last at 9T)
+                const uint32_t k = K0 + (t < T ? 9 * t + 1 : 9 * T);
+                const uint32_t slot = k & 1u;
+                if (!(ok = tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k))) break;
+                ++au[slot];
+                tc::fence_after();
+                if (t > 0) {
+                    constexpr uint32_t hid = kMaxHid;  // the tensor-core path takes prober hidden_dim 32
+                    float h1[kMaxHid];
+                    const float* pw = s.pw;
+#pragma unroll
+                    for (uint32_t c0 = 0; c0 < kMaxHid; c0 += 16) {
+                        float v[16];
+                        tc::tmem_ld16(lane_base + slot * 128 + c0, v);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) h1[c0 + i] = gelu_tanh(v[i] + pw[c0 + i]);
+                    }
+                    tc::fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.empty[1][slot]);
+                    uint32_t off = hid;
+                    float h2[kMaxHid];
+                    for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
+                        const float* W = pw + off;
+                        const float* bb = pw + off + hid * hid;
+#pragma unroll
+                        for (uint32_t o = 0; o < hid; ++o) {
+                            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                            for (uint32_t i = 0; i < hid; i += 2) {
+                                s0 = fmaf(h1[i], W[o * hid + i], s0);
+                                s1 = fmaf(h1[i + 1], W[o * hid + i + 1], s1);
+                            }
+                            h2[o] = gelu_tanh((s0 + s1) + bb[o]);
+                        }
+#pragma unroll
+                        for (uint32_t o = 0; o < hid; ++o) h1[o] = h2[o];
+                        off += hid * hid + hid;
+                    }
+                    float po[15];
+#pragma unroll
+                    for (uint32_t o = 0; o < 15; ++o) {
+                        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                        for (uint32_t i = 0; i < hid; i += 2) {
+                            s0 = fmaf(h1[i], pw[off + o * hid + i], s0);
+                            s1 = fmaf(h1[i + 1], pw[off + o * hid + i + 1], s1);
+                        }
+                        po[o] = (s0 + s1) + pw[off + 15 * hid + o];
+                    }
+                    // integrator step t-1 (lewm_skyjepa_integrate_f32, kinematics.rs:377-484) + cost
+                    const uint32_t ts = t - 1;
+                    const float* act = cand_row + ts * 4;
+                    const float sdt = a.dt;
+                    float ta;
+                    if (a.rotor_forces) {
+                        ta = (act[0] + act[1] + act[2] + act[3]) / mass;
+                    } else {
+                        const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
+                        ta = th * a.gravity / a.hover_throttle;
+                    }
+                    const float acc3[3] = {x[8] * ta + po[0], x[11] * ta + po[1], x[14] * ta - a.gravity + po[2]};
+                    float ang[3];
+#pragma unroll
+                    for (int r3 = 0; r3 < 3; ++r3)
+                        ang[r3] = po[3 + r3 * 4] * act[0] + po[4 + r3 * 4] * act[1] + po[5 + r3 * 4] * act[2] +
+                                  po[6 + r3 * 4] * act[3];
+#pragma unroll
+                    for (int ax = 0; ax < 3; ++ax) {
+                        x[ax] += x[3 + ax] * sdt;
+                        x[3 + ax] += acc3[ax] * sdt;
+                    }
+                    const float wx = x[15] * sdt, wy = x[16] * sdt, wz = x[17] * sdt;
+                    const float th2 = wx * wx + wy * wy + wz * wz;
+                    float ca, cb;
+                    if (th2 < 1.0e-6f) {
+                        const float th4 = th2 * th2;
+                        ca = 1.0f - th2 / 6.0f + th4 / 120.0f;
+                        cb = 0.5f - th2 / 24.0f + th4 / 720.0f;
+                    } else {
+                        const float th = sqrtf(th2);
+                        float sn, cs;
+                        sincosf(th, &sn, &cs);
+                        ca = sn / th;
+                        cb = (1.0f - cs) / th2;
+                    }
+                    const float dl[9] = {1.0f - cb * (wy * wy + wz * wz), cb * wx * wy - ca * wz,
+                                         cb * wx * wz + ca * wy, cb * wy * wx + ca * wz,
+                                         1.0f - cb * (wx * wx + wz * wz), cb * wy * wz - ca * wx,
+                                         cb * wz * wx - ca * wy, cb * wz * wy + ca * wx,
+                                         1.0f - cb * (wx * wx + wy * wy)};
+                    float nr[9];
+#pragma unroll
+                    for (int r3 = 0; r3 < 3; ++r3)
+#pragma unroll
+                        for (int c3 = 0; c3 < 3; ++c3)
+                            nr[r3 * 3 + c3] =
+                                x[6 + r3 * 3] * dl[c3] + x[7 + r3 * 3] * dl[3 + c3] + x[8 + r3 * 3] * dl[6 + c3];
+#pragma unroll
+                    for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
+#pragma unroll
+                    for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
+                    const float* ref = a.ref_states + (static_cast<size_t>(b) * T + ts) * 18;
+                    float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) { const float dd = x[i] - ref[i]; g0 += dd * dd; }
+#pragma unroll
+                    for (int i = 3; i < 6; ++i) { const float dd = x[i] - ref[i]; g1 += dd * dd; }
+#pragma unroll
+                    for (int i = 6; i < 15; ++i) { const float dd = x[i] - ref[i]; g2 += dd * dd; }
+#pragma unroll
+                    for (int i = 15; i < 18; ++i) { const float dd = x[i] - ref[i]; g3 += dd * dd; }
+                    const float* ra = a.ref_actions + (static_cast<size_t>(b) * T + ts) * 4;
+                    float ac = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) { const float dd = act[i] - ra[i]; ac += (dd * dd) * a.cost.action[i]; }
+                    float st = g0 * a.cost.position + g1 * a.cost.velocity;
+                    st = st + g2 * a.cost.attitude;
+                    st = st + g3 * a.cost.angular_velocity;
+                    cost += st + ac;
+                } else {
+                    tc::fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.empty[1][slot]);
+                }
+            }
+            if (!ok) break;
+            // score (mean over T) and the tile's MPPI tuple
+            const float score = cost * static_cast<float>(1.0 / static_cast<double>(T));
+            a.scores[grow] = score;
+            uint64_t key = score_key(score, a.sample_base + srow);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other < key ? other : key;
+            }
+            if (lane == 0) s.red_key[q] = key;
+            aux_sync();
+            uint64_t best = s.red_key[0];
+            for (int w = 1; w < 4; ++w) best = s.red_key[w] < best ? s.red_key[w] : best;
+            const float m = key_score(best);
+            const float wgt = expf((score - m) * a.m.mul);
+            s.red_w[row] = wgt;
+            float wsum = wgt;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+            if (lane == 0) s.red_f[q] = wsum;
+            aux_sync();
+            wsum = s.red_f[0] + s.red_f[1] + s.red_f[2] + s.red_f[3];
+            const MppiArgs& mm = a.m;
+            float* part = mm.partials + (static_cast<size_t>(b) * mm.P + tv) * mm.pw;
+            const float* cand_tile = a.cand_out + (static_cast<size_t>(b) * a.S + tv * kRows) * TA;
+            for (uint32_t e = atid; e < TA; e += kAuxThreads) {
+                float acc = 0.0f;
+                for (uint32_t rr = 0; rr < kRows; ++rr) acc += s.red_w[rr] * cand_tile[rr * TA + e];
+                part[4 + e] = acc;
+            }
+            if (atid == 0) {
+                part[0] = m;
+                part[1] = wsum;
+                reinterpret_cast<uint64_t*>(part)[1] = best;
+            }
+            __threadfence();
+            aux_sync();
+            if (atid == 0) s.last = atomicAdd(&mm.counters[b], 1u) == mm.P - 1;
+            aux_sync();
+            if (s.last) {
+                __threadfence();
+                // combine the vehicle's tile tuples (mppi_finish with the aux group)
+                const float* base = mm.partials + static_cast<size_t>(b) * mm.P * mm.pw;
+                uint64_t gk = ~0ull;
+                for (uint32_t i = atid; i < mm.P; i += kAuxThreads) {
+                    const uint64_t kk = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(i) * mm.pw)[1];
+                    gk = kk < gk ? kk : gk;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const uint64_t other = __shfl_xor_sync(0xffffffffu, gk, o);
+                    gk = other < gk ? other : gk;
+                }
+                aux_sync();
+                if (lane == 0) s.red_key[q] = gk;
+                aux_sync();
+                gk = s.red_key[0];
+                for (int w = 1; w < 4; ++w) gk = s.red_key[w] < gk ? s.red_key[w] : gk;
+                const float M = key_score(gk);
+                float* tuple = mm.shard_tuple ? mm.shard_tuple + static_cast<size_t>(b) * mm.pw : nullptr;
+                for (uint32_t e = atid; e < TA; e += kAuxThreads) {
+                    float W = 0.0f, V = 0.0f;
+                    for (uint32_t i = 0; i < mm.P; ++i) {
+                        const volatile float* pq = base + static_cast<size_t>(i) * mm.pw;
+                        if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;
+                        const float f = expf((pq[0] - M) * mm.mul);
+                        W += pq[1] * f;
+                        V += pq[4 + e] * f;
+                    }
+                    if (tuple) {
+                        tuple[4 + e] = V;
+                        if (e == 0) { tuple[0] = M; tuple[1] = W; reinterpret_cast<uint64_t*>(tuple)[1] = gk; }
+                        continue;
+                    }
+                    const float value = V / W;
+                    const uint32_t t = e / 4u, act = e & 3u;
+                    const size_t seq = static_cast<size_t>(b) * TA;
+                    mm.sequence[seq + e] = value;
+                    if (t == 0) mm.first_action[static_cast<size_t>(b) * 4 + act] = value;
+                    if (t >= 1) mm.warm_start[seq + e - 4] = value;
+                    if (t == T - 1) mm.warm_start[seq + e] = value;
+                }
+                if (atid == 0) {
+                    if (!tuple) {
+                        mm.best_index[b] = static_cast<uint32_t>(gk & 0xffffffffu);
+                        mm.best_score[b] = M;
+                    }
+                    mm.counters[b] = 0u;
+                }
+            }
+            aux_sync();
+            K0 += entries;
+        }
+    }
+
+    // ---- teardown
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 1) tc::tmem_free(tmem, 512);
+}
+
+// ------------------------------------------------------------ host side
+
+bool skyjepa_tc_supported(const SkyjepaArgs& a, const char** why) {
+    if (a.H != 256) { *why = "the tensor-core path needs latent_dim 256"; return false; }
+    if (a.A != 4 || a.E != 4 || a.action_tcn.max_ch != 4 || a.action_tcn.input_dim != 4) {
+        *why = "the tensor-core path needs 4 actions and a 4-channel action encoder";
+        return false;
+    }
+    if (a.hid != kMaxHid) { *why = "the tensor-core path needs prober hidden_dim 32"; return false; }
+    if (a.Hs != static_cast<uint32_t>(kTcnHs) || a.action_tcn.k != static_cast<uint32_t>(kTcnK)) {
+        *why = "the tensor-core path needs a 10-step history and action-encoder kernel 3";
+        return false;
+    }
+    if (a.prober_layers < 1 || a.prober_layers > kMaxLayers) { *why = "prober hidden_layers must be 1..3"; return false; }
+    if (a.S % kRows != 0) { *why = "the tensor-core path needs samples divisible by 128"; return false; }
+    if (a.Hs < 2 || a.Hs > kMaxHistTc || a.T == 0 || a.T > kMaxHorizon) { *why = "history/horizon out of range"; return false; }
+    if (tcn_weight_floats(a.action_tcn) > kTcnFloats) { *why = "action encoder too large"; return false; }
+    if (a.state_tcn.max_ch * a.Hs * 3 * sizeof(float) > 48 * 1024) { *why = "state encoder too wide"; return false; }
+    if (a.states) { *why = "predicted states are produced by the f32 path"; return false; }
+    if (!a.sample || !a.mppi) { *why = "the tensor-core path runs fused MPPI iterations"; return false; }
+    return true;
+}
+
+size_t skyjepa_tc_packed_bytes() { return static_cast<size_t>(kChunks) * kChunkBytes + kP1Bytes; }
+
+cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream) {
+    cudaError_t e = cudaMemsetAsync(packed, 0, skyjepa_tc_packed_bytes(), stream);
+    if (e != cudaSuccess) return e;
+    const size_t n = static_cast<size_t>(kChunks) * 96 * kH + static_cast<size_t>(kChunks) * 128 * 16 +
+                     static_cast<size_t>(a.hid) * kH;
+    pack_tc_weights_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, stream>>>(
+        a, packed, packed + static_cast<size_t>(kChunks) * kChunkBytes);
+    return cudaGetLastError();
+}
+
+uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S) { return S / kRows; }
+
+cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, int* err, cudaStream_t stream,
+                              int* launches) {
+    const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
+    skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    TcArgs p;
+    p.a = a;
+    p.wc = packed;
+    p.p1 = packed + static_cast<size_t>(kChunks) * kChunkBytes;
+    p.h0 = h0;
+    p.tiles_per_vehicle = a.S / kRows;
+    p.tiles = a.B * p.tiles_per_vehicle;
+    p.err = err;
+    const size_t smem = sizeof(TcSmem) + 1024;
+    static bool attr = false;
+    if (!attr) {
+        e = cudaFuncSetAttribute(skyjepa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t grid = static_cast<uint32_t>(sms) < p.tiles ? static_cast<uint32_t>(sms) : p.tiles;
+    skyjepa_tc_kernel<<<grid, kThreadsTc, smem, stream>>>(p);
+    if (launches) *launches = 2;
+    return cudaGetLastError();
+}
+
+}  // namespace lwm

@@ -114,6 +114,17 @@ struct TcnView {
     TcnBlockView blocks[8];
 };
 
+// Floats of an encoder's weights (contiguous in the blob).
+__host__ __device__ inline uint32_t tcn_weight_floats(const TcnView& t) {
+    uint32_t n = 0;
+    for (uint32_t l = 0; l < t.levels; ++l) {
+        const TcnBlockView& b = t.blocks[l];
+        n += b.out * b.in * t.k + b.out + b.out * b.out * t.k + b.out;
+        if (b.in != b.out) n += b.out * b.in + b.out;
+    }
+    return n;
+}
+
 struct SkyjepaArgs {
     uint32_t B, S, T, A, Hs, H, E, hid, prober_layers;
     TcnView state_tcn, action_tcn;
@@ -147,6 +158,14 @@ struct SkyjepaArgs {
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
+// Tensor-core (tcgen05, bf16) learned-MPPI path for large candidate counts.
+bool skyjepa_tc_supported(const SkyjepaArgs& a, const char** why);
+size_t skyjepa_tc_packed_bytes();
+cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
+uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S);
+cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, int* err, cudaStream_t stream,
+                              int* launches);
+
 cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
                                uint32_t S, cudaStream_t stream);
 // Combine `shards` per-vehicle tuples [shards][B][pw] into the final outputs.

@@ -261,6 +261,7 @@ _sig("lwm_scorer_skyjepa_create", C.c_int, VP, C.POINTER(SkyJepaConfig), FP, C.c
      C.POINTER(TrackingCost), F, C.POINTER(VP))
 _sig("lwm_scorer_skyjepa_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP)
 _sig("lwm_scorer_skyjepa_set_context_ex", C.c_int, VP, U32, U32, FP, FP, FP, FP, FP)
+_sig("lwm_scorer_skyjepa_set_precision", C.c_int, VP, I32)
 _sig("lwm_scorer_callback_create", C.c_int, VP, U32, SCORE_FN, VP, C.POINTER(VP))
 _sig("lwm_scorer_score_device", C.c_int, VP, VP, U32, U32, U32, U32, VP)
 _sig("lwm_scorer_predict_device", C.c_int, VP, VP, U32, U32, U32, VP)
@@ -623,6 +624,10 @@ class SkyJepaScorer(Scorer):
                                              _fp(_f32(action_std)), C.byref(cost), F(dt), C.byref(h)))
         self.handle = h
         _LIVE["scorer"].add(self)
+
+    def set_precision(self, precision: str) -> None:
+        """"f32" (CUDA cores) or "bf16" (tcgen05 tensor cores where the shape allows)."""
+        _check(lib.lwm_scorer_skyjepa_set_precision(self.handle, {"f32": 0, "bf16": 1}[precision]))
 
     def set_context(self, state_history, action_history, reference_states, reference_actions,
                     vehicle_mass=None) -> None:
