@@ -150,7 +150,7 @@ struct lwm_scorer {
     std::unique_ptr<lwm::LewmModel> lewm;
     // learned scorer on tensor cores (bf16): packed weights, per-vehicle h0, wait-timeout flag
     int32_t precision = LWM_PRECISION_F32;
-    DevBuf tc_packed, tc_h0, tc_err;
+    DevBuf tc_packed, tc_h0, tc_err, tc_x;
     bool tc_ready = false;
 };
 
@@ -438,7 +438,7 @@ lwm::NominalArgs nominal_args(lwm_scorer* sc, uint32_t S) {
 }
 
 // Packed bf16 weights (once per scorer), per-vehicle h0 and the error flag.
-lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B) {
+lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
     if (!sc->tc_ready) {
         LWM_TRY(sc->tc_packed.ensure(lwm::skyjepa_tc_packed_bytes()));
         LWM_CUDA(lwm::skyjepa_tc_pack(a, sc->tc_packed.as<uint8_t>(), sc->ctx->stream));
@@ -446,6 +446,7 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B) {
         sc->tc_ready = true;
     }
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    LWM_TRY(sc->tc_x.ensure(lwm::skyjepa_tc_xtile_bytes(B, S, T)));
     return LWM_OK;
 }
 
@@ -674,11 +675,14 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 int launched = 0;
                 const char* why = nullptr;
                 if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
-                    LWM_TRY(ensure_tc(sc, a, B));
+                    LWM_TRY(ensure_tc(sc, a, B, p->S, p->T));
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
+                    a.low_dev = low;
+                    a.high_dev = high;
                     LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
                     LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
-                                                    sc->tc_err.as<int>(), stream, &launched));
+                                                    sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
+                                                    &launched));
                 } else {
                     LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
                 }
@@ -1353,6 +1357,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->tc_packed.release();
     s->tc_h0.release();
     s->tc_err.release();
+    s->tc_x.release();
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;

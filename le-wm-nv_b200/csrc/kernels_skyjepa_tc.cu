@@ -16,18 +16,23 @@
 //   TMEM (f32) and in shared memory (bf16, the next step's A operand).
 //   The prober's first layer is one more MMA per step (A = h_{t+1}).
 //
-// Roles (448 threads): warp 0 streams the weight chunks (bulk copies, two
-// slots); warp 1 issues the MMAs and owns TMEM; warps 2-9 run the GRU
+// Before it, sample_kernel draws the candidates and skyjepa_tc_inputs_kernel
+// computes every candidate's action-TCN input x_t for every step (all
+// threads of the GPU), written as bf16 K-major tiles with a constant 1 at
+// k = E that carries the GRU biases through the x-block MMA.
+//
+// Roles (448 threads): warp 0 streams the weight chunks and the x tiles
+// (bulk copies); warp 1 issues the MMAs and owns TMEM; warps 2-9 run the GRU
 // epilogue (two warps per TMEM lane quadrant, 16 units each); warps 10-13
-// (one thread per candidate) sample the candidates, compute the action-TCN
-// input of the next step, finish the prober, integrate, accumulate the cost
-// and reduce the tile to an MPPI tuple.  All hand-offs are mbarriers with
-// bounded waits; a wait that gives up raises *err and the kernel unwinds.
+// (one thread per candidate) finish the prober, integrate, accumulate the
+// cost and reduce the tile to an MPPI tuple.  All hand-offs are mbarriers
+// with bounded waits; a wait that gives up records where and the kernel
+// unwinds.
 //
 // TMEM (512 columns): accumulator slots 0 and 1 = columns [0,128) and
 // [128,256); h_t (f32) = columns [256,512).  Weights are bf16 (packed once
-// per scorer by pack_tc_weights_kernel); biases, the prober's later layers,
-// the TCN and the integrator stay f32.
+// per scorer by pack_tc_weights_kernel; the GRU biases ride in the x block);
+// the prober's later layers, the TCN and the integrator stay f32.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -61,9 +66,7 @@ struct __align__(1024) TcSmem {
     uint8_t W[2][kChunkBytes];
     uint8_t X[2][kXBytes];
     uint8_t P1[kP1Bytes];
-    float gbias[4][kH];   // r (b_ir + b_hr), z (b_iz + b_hz), n_x (b_in), n_h (b_hn)
     float pw[kPwFloats];  // prober: b1, hidden layers (W, b), output (W, b)
-    float tcn[kTcnFloats];
     float red_w[kRows];
     uint64_t red_key[4];
     float red_f[4];
@@ -79,7 +82,20 @@ __device__ __forceinline__ void aux_sync() {
     asm volatile("bar.sync %0, %1;" ::"n"(kAuxBarrier), "n"(kAuxThreads) : "memory");
 }
 
-__device__ __forceinline__ float sigmoid_f(float v) { return __frcp_rn(1.0f + __expf(-v)); }
+// Hardware tanh (MUFU.TANH); the gates use it for sigmoid as well:
+// sigmoid(v) = 0.5 + 0.5 tanh(v / 2).  Relative error ~2^-11, far inside the
+// bf16 path's tolerance.
+__device__ __forceinline__ float tanh_fast(float v) {
+    float r;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+__device__ __forceinline__ float sigmoid_f(float v) { return fmaf(0.5f, tanh_fast(0.5f * v), 0.5f); }
+// Candle's tanh-approximation GELU with the hardware tanh (bf16 path).
+__device__ __forceinline__ float gelu_fast(float v) {
+    const float u = 0.7978845608028654f * v * fmaf(0.044715f * v, v, 1.0f);
+    return 0.5f * v * (1.0f + tanh_fast(u));
+}
 
 // Two f32 -> packed bf16x2 (the first value at the lower address).
 __device__ __forceinline__ uint32_t bf2(float lo, float hi) {
@@ -104,8 +120,9 @@ __host__ __device__ inline uint32_t packed_h_offset(uint32_t j, uint32_t k, uint
 // ------------------------------------------------------- weight packing
 //
 // Wc[chunk]: H part (rows r_u, z_u, n_u of the chunk's 32 units, K = 256 of
-// weight_hh) in SW128 K-blocks, then the X part (rows r, z, 0, n of
-// weight_ih, K = E <= 16) in SW32.  P1: prober input layer [hid x 256].
+// weight_hh) in SW128 K-blocks, then the X part (rows r, z, n_h, n_x; k < E
+// weight_ih (zero for n_h), k = E the biases) in SW32.  P1: prober input
+// layer [hid x 256].
 __global__ void pack_tc_weights_kernel(SkyjepaArgs a, uint8_t* wc, uint8_t* p1) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t n_h = static_cast<size_t>(kChunks) * 96 * kH;
@@ -125,6 +142,13 @@ __global__ void pack_tc_weights_kernel(SkyjepaArgs a, uint8_t* wc, uint8_t* p1) 
         if (k < a.E && g != 2) {
             const uint32_t gate = g == 3 ? 2u : g;  // n_x uses weight_ih's n rows
             v = a.w_ih[static_cast<size_t>(gate * kH + u) * a.E + k];
+        } else if (k == a.E) {
+            // biases, multiplied by the constant 1 of the x tiles:
+            // r: b_ir + b_hr, z: b_iz + b_hz, n_h: b_hn, n_x: b_in
+            if (g == 0) v = a.b_ih[u] + a.b_hh[u];
+            else if (g == 1) v = a.b_ih[kH + u] + a.b_hh[kH + u];
+            else if (g == 2) v = a.b_hh[2 * kH + u];
+            else v = a.b_ih[2 * kH + u];
         }
         *reinterpret_cast<__nv_bfloat16*>(wc + static_cast<size_t>(c) * kChunkBytes + kChunkHBytes +
                                           tc::sw32_offset(j, k)) = __float2bfloat16_rn(v);
@@ -197,6 +221,142 @@ __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h
     }
 }
 
+namespace {
+
+// Action-TCN input of step t for one candidate (TemporalConvEncoder over the
+// window [history ++ candidate](t : t + 10), last position), written as bf16
+// into the X tile.  One thread per candidate, in registers.
+//
+// Only the last output position of the window is used, so each block is
+// evaluated where that output depends on it (kernel 3, dilations 1, 2, 4,
+// causal zero padding inside the window):
+//   block 1: conv1 at all 10 positions, output at odd positions 1..9
+//   block 2: conv1 at odd positions, output at 1, 5, 9
+//   block 3: conv1 at 1, 5, 9, output at 9
+// (27 position-convolutions instead of 60; the values computed are the
+// reference's, tcn.rs:88-96 / 138-160).
+constexpr int kTcnHs = 10, kTcnK = 3, kTcnC = 4;
+
+// The 4 channels at window position P of conv(in) with dilation DIL (+ bias, GELU).
+template <int P, int DIL>
+__device__ __forceinline__ void conv_at(const float (&in)[kTcnC][kTcnHs], const float* W, const float* B,
+                                        float (&out)[kTcnC][kTcnHs]) {
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kTcnC; ++i)
+#pragma unroll
+            for (int j = 0; j < kTcnK; ++j) {
+                const int src = P - (kTcnK - 1 - j) * DIL;
+                if (src >= 0) acc = fmaf(W[(o * kTcnC + i) * kTcnK + j], in[i][src], acc);
+            }
+        out[o][P] = gelu_fast(acc + B[o]);
+    }
+}
+
+// out[P] = gelu(gelu(conv2(h)[P]) + res[P])
+template <int P, int DIL>
+__device__ __forceinline__ void block_out_at(const float (&h)[kTcnC][kTcnHs], const float (&res)[kTcnC][kTcnHs],
+                                             const float* W2, const float* B2, float (&out)[kTcnC][kTcnHs]) {
+    float c2[kTcnC][kTcnHs];
+    conv_at<P, DIL>(h, W2, B2, c2);
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o) out[o][P] = gelu_fast(c2[o][P] + res[o][P]);
+}
+
+struct TcnBlockW {
+    const float *w1, *b1, *w2, *b2;
+};
+
+// x_t of one candidate: `win` holds the normalised window (4 channels x 10).
+__device__ __forceinline__ void tcn_last(const TcnBlockW (&w)[3], const float (&x0)[kTcnC][kTcnHs], float (&x)[kTcnC]) {
+    // block 1 (dilation 1)
+    float h[kTcnC][kTcnHs], y1[kTcnC][kTcnHs];
+    conv_at<0, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<1, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<2, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<3, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<4, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<5, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<6, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<7, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<8, 1>(x0, w[0].w1, w[0].b1, h);
+    conv_at<9, 1>(x0, w[0].w1, w[0].b1, h);
+    block_out_at<1, 1>(h, x0, w[0].w2, w[0].b2, y1);
+    block_out_at<3, 1>(h, x0, w[0].w2, w[0].b2, y1);
+    block_out_at<5, 1>(h, x0, w[0].w2, w[0].b2, y1);
+    block_out_at<7, 1>(h, x0, w[0].w2, w[0].b2, y1);
+    block_out_at<9, 1>(h, x0, w[0].w2, w[0].b2, y1);
+    // block 2 (dilation 2): reads y1 at odd positions only
+    float y2[kTcnC][kTcnHs];
+    conv_at<1, 2>(y1, w[1].w1, w[1].b1, h);
+    conv_at<3, 2>(y1, w[1].w1, w[1].b1, h);
+    conv_at<5, 2>(y1, w[1].w1, w[1].b1, h);
+    conv_at<7, 2>(y1, w[1].w1, w[1].b1, h);
+    conv_at<9, 2>(y1, w[1].w1, w[1].b1, h);
+    block_out_at<1, 2>(h, y1, w[1].w2, w[1].b2, y2);
+    block_out_at<5, 2>(h, y1, w[1].w2, w[1].b2, y2);
+    block_out_at<9, 2>(h, y1, w[1].w2, w[1].b2, y2);
+    // block 3 (dilation 4): reads y2 at 1, 5, 9
+    float y3[kTcnC][kTcnHs];
+    conv_at<1, 4>(y2, w[2].w1, w[2].b1, h);
+    conv_at<5, 4>(y2, w[2].w1, w[2].b1, h);
+    conv_at<9, 4>(y2, w[2].w1, w[2].b1, h);
+    block_out_at<9, 4>(h, y2, w[2].w2, w[2].b2, y3);
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o) x[o] = y3[o][kTcnHs - 1];
+}
+
+}  // namespace
+
+// ------------------------------------------------------ per-step inputs
+//
+// x_t of every candidate and step (the action TCN over the window
+// [history ++ candidate](t : t + 10), last position), one thread per
+// (candidate, step), written as the bf16 x tile of (tile, step): rows = the
+// tile's 128 candidates, k < 4 the encoder output, k = 4 the constant 1.
+__global__ void __launch_bounds__(256) skyjepa_tc_inputs_kernel(SkyjepaArgs a, uint8_t* xtiles) {
+    __shared__ float sw[kTcnFloats];
+    const TcnView& tcn = a.action_tcn;
+    const float* wbase = tcn.blocks[0].w1;
+    const uint32_t nw = tcn_weight_floats(tcn);
+    for (uint32_t q = threadIdx.x; q < nw; q += blockDim.x) sw[q] = wbase[q];
+    __syncthreads();
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint64_t total = static_cast<uint64_t>(a.B) * a.S * a.T;
+    if (i >= total) return;
+    const uint32_t t = static_cast<uint32_t>(i % a.T);
+    const uint64_t grow = i / a.T;  // b * S + s
+    const uint32_t b = static_cast<uint32_t>(grow / a.S);
+    TcnBlockW w[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+        w[l] = {sw + (tcn.blocks[l].w1 - wbase), sw + (tcn.blocks[l].b1 - wbase), sw + (tcn.blocks[l].w2 - wbase),
+                sw + (tcn.blocks[l].b2 - wbase)};
+    const float* cand_row = a.cand_out + grow * a.T * 4;
+    float x0[kTcnC][kTcnHs];
+#pragma unroll
+    for (int q = 0; q < kTcnHs; ++q) {
+        const uint32_t pos = t + q;
+        const float* src = pos < kTcnHs - 1 ? a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4
+                                            : cand_row + (pos - (kTcnHs - 1)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        x0[0][q] = (v.x - a.action_mean[0]) / a.action_std[0];
+        x0[1][q] = (v.y - a.action_mean[1]) / a.action_std[1];
+        x0[2][q] = (v.z - a.action_mean[2]) / a.action_std[2];
+        x0[3][q] = (v.w - a.action_mean[3]) / a.action_std[3];
+    }
+    float x[kTcnC];
+    tcn_last(w, x0, x);
+    const uint64_t tile = grow / kRows;
+    const uint32_t row = static_cast<uint32_t>(grow % kRows);
+    uint8_t* xt = xtiles + (tile * a.T + t) * kXBytes;
+    *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 0)) =
+        make_uint4(bf2(x[0], x[1]), bf2(x[2], x[3]), bf2(1.0f, 0.0f), 0u);
+    *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // ------------------------------------------------------------ main kernel
 
 namespace {
@@ -206,82 +366,10 @@ struct TcArgs {
     const uint8_t* wc;  // packed chunks
     const uint8_t* p1;  // packed prober layer 1
     const float* h0;    // [B, 256]
+    const uint8_t* xt;  // x tiles [tiles][T][kXBytes]
     uint32_t tiles_per_vehicle, tiles;
     int* err;
 };
-
-// Action-TCN input of step t for one candidate (TemporalConvEncoder over the
-// window [history ++ candidate](t : t + 10), last position), written as bf16
-// into the X tile.  One thread per candidate, everything in registers: the
-// tensor-core path takes the 4-channel encoder with kernel 3 over a 10-step
-// window (compile-time sizes keep the window in registers).
-constexpr int kTcnHs = 10, kTcnK = 3, kTcnC = 4;
-
-template <int DIL>
-__device__ __forceinline__ void tcn_conv(const float (&in)[kTcnC][kTcnHs], const float* W, const float* B,
-                                         float (&out)[kTcnC][kTcnHs]) {
-#pragma unroll
-    for (int o = 0; o < kTcnC; ++o)
-#pragma unroll
-        for (int w = 0; w < kTcnHs; ++w) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kTcnC; ++i)
-#pragma unroll
-                for (int j = 0; j < kTcnK; ++j) {
-                    const int src = w - (kTcnK - 1 - j) * DIL;
-                    if (src >= 0) acc = fmaf(W[(o * kTcnC + i) * kTcnK + j], in[i][src], acc);
-                }
-            out[o][w] = gelu_tanh(acc + B[o]);
-        }
-}
-
-template <int DIL>
-__device__ __forceinline__ void tcn_block(float (&cur)[kTcnC][kTcnHs], const float* w1, const float* b1,
-                                          const float* w2, const float* b2) {
-    float h1[kTcnC][kTcnHs], h2[kTcnC][kTcnHs];
-    tcn_conv<DIL>(cur, w1, b1, h1);
-    tcn_conv<DIL>(h1, w2, b2, h2);
-#pragma unroll
-    for (int o = 0; o < kTcnC; ++o)
-#pragma unroll
-        for (int w = 0; w < kTcnHs; ++w) cur[o][w] = gelu_tanh(h2[o][w] + cur[o][w]);
-}
-
-__device__ void action_tcn_step(const TcArgs& p, const TcSmem& s, const float* cand_row, uint32_t b, uint32_t t,
-                                uint32_t row, uint8_t* xtile) {
-    const SkyjepaArgs& a = p.a;
-    const TcnView& tcn = a.action_tcn;
-    const float* wbase = tcn.blocks[0].w1;
-    float cur[kTcnC][kTcnHs];
-#pragma unroll
-    for (int w = 0; w < kTcnHs; ++w) {
-        const uint32_t pos = t + w;
-        const float* src = pos < kTcnHs - 1 ? a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4
-                                            : cand_row + (pos - (kTcnHs - 1)) * 4;
-        const float4 v = *reinterpret_cast<const float4*>(src);
-        cur[0][w] = (v.x - a.action_mean[0]) / a.action_std[0];
-        cur[1][w] = (v.y - a.action_mean[1]) / a.action_std[1];
-        cur[2][w] = (v.z - a.action_mean[2]) / a.action_std[2];
-        cur[3][w] = (v.w - a.action_mean[3]) / a.action_std[3];
-    }
-    for (uint32_t l = 0; l < tcn.levels; ++l) {
-        const TcnBlockView& bk = tcn.blocks[l];
-        const float* w1 = s.tcn + (bk.w1 - wbase);
-        const float* b1 = s.tcn + (bk.b1 - wbase);
-        const float* w2 = s.tcn + (bk.w2 - wbase);
-        const float* b2 = s.tcn + (bk.b2 - wbase);
-        switch (bk.dil) {
-            case 1: tcn_block<1>(cur, w1, b1, w2, b2); break;
-            case 2: tcn_block<2>(cur, w1, b1, w2, b2); break;
-            case 4: tcn_block<4>(cur, w1, b1, w2, b2); break;
-            default: tcn_block<8>(cur, w1, b1, w2, b2); break;
-        }
-    }
-    *reinterpret_cast<uint4*>(xtile + tc::sw32_offset(row, 0)) =
-        make_uint4(bf2(cur[0][kTcnHs - 1], cur[1][kTcnHs - 1]), bf2(cur[2][kTcnHs - 1], cur[3][kTcnHs - 1]), 0u, 0u);
-    *reinterpret_cast<uint4*>(xtile + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
-}
 
 }  // namespace
 
@@ -302,7 +390,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             tc::mbar_init(&s.full[1][i], 1);
             tc::mbar_init(&s.empty[0][i], 8);
             tc::mbar_init(&s.empty[1][i], 4);
-            tc::mbar_init(&s.x_full[i], 4);
+            tc::mbar_init(&s.x_full[i], 1);
             tc::mbar_init(&s.x_empty[i], 1);
         }
         tc::mbar_init(&s.h_full, 8);
@@ -314,12 +402,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     for (uint32_t q = tid; q < kP1Bytes / 16; q += kThreadsTc)
         reinterpret_cast<uint4*>(s.P1)[q] =
             q < hid * 4 * 128 / 16 ? reinterpret_cast<const uint4*>(p.p1)[q] : make_uint4(0, 0, 0, 0);
-    for (uint32_t u = tid; u < kH; u += kThreadsTc) {
-        s.gbias[0][u] = a.b_ih[u] + a.b_hh[u];
-        s.gbias[1][u] = a.b_ih[kH + u] + a.b_hh[kH + u];
-        s.gbias[2][u] = a.b_ih[2 * kH + u];
-        s.gbias[3][u] = a.b_hh[2 * kH + u];
-    }
     {
         // prober: b1 [hid], hidden l: W [hid*hid], b [hid], output W [15*hid], b [15]
         float* pw = s.pw;
@@ -332,8 +414,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
         }
         for (uint32_t q = tid; q < 15 * hid; q += kThreadsTc) pw[off + q] = a.p_out_w[q];
         for (uint32_t q = tid; q < 15; q += kThreadsTc) pw[off + 15 * hid + q] = a.p_out_b[q];
-        const uint32_t n = tcn_weight_floats(a.action_tcn);
-        for (uint32_t q = tid; q < n; q += kThreadsTc) s.tcn[q] = a.action_tcn.blocks[0].w1[q];
     }
     tc::fence_async_smem();
     tc::fence_before();
@@ -345,9 +425,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     if (warp == 0) {
         // ================= producer: weight chunks, 2 slots
         if (lane == 0) {
-            uint32_t j = 0;
+            uint32_t j = 0, xs = 0;
             for (uint32_t tile = blockIdx.x; tile < p.tiles && !err[0]; tile += gridDim.x)
-                for (uint32_t t = 0; t < T && !err[0]; ++t)
+                for (uint32_t t = 0; t < T && !err[0]; ++t, ++xs) {
+                    const uint32_t xslot = xs & 1u;
+                    if (!tc::mbar_wait(&s.x_empty[xslot], ((xs >> 1) & 1u) ^ 1u, err, 8, xs)) break;
+                    tc::mbar_expect_tx(&s.x_full[xslot], kXBytes);
+                    tc::bulk_g2s(s.X[xslot], p.xt + (static_cast<size_t>(tile) * T + t) * kXBytes, kXBytes,
+                                 &s.x_full[xslot]);
                     for (uint32_t c = 0; c < kChunks; ++c, ++j) {
                         const uint32_t slot = j & 1u, n = j >> 1;
                         if (!tc::mbar_wait(&s.w_empty[slot], (n & 1u) ^ 1u, err, 1, j)) break;
@@ -355,6 +440,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                         tc::bulk_g2s(s.W[slot], p.wc + static_cast<size_t>(c) * kChunkBytes, kChunkBytes,
                                      &s.w_full[slot]);
                     }
+                }
         }
     } else if (warp == 1) {
         // ================= MMA issuer
@@ -482,10 +568,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     tc::tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const uint32_t u = u0 + i;
-                        const float rg = sigmoid_f(r[i] + s.gbias[0][u]);
-                        const float zg = sigmoid_f(z[i] + s.gbias[1][u]);
-                        const float ng = tanhf((nx[i] + s.gbias[2][u]) + rg * (nh[i] + s.gbias[3][u]));
+                        const float rg = sigmoid_f(r[i]);
+                        const float zg = sigmoid_f(z[i]);
+                        const float ng = tanh_fast(fmaf(rg, nh[i], nx[i]));
                         hv[i] = zg * hv[i] - (zg - 1.0f) * ng;  // GRU::step, h' = z h - (z - 1) n
                     }
                     tc::tmem_st16(lane_base + 256 + u0, hv);
@@ -518,44 +603,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
         const uint32_t q = warp & 3u, row = q * 32 + lane, atid = tid - kAuxWarp0 * 32;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         const uint32_t TA = T * 4u;
-        uint32_t K0 = 0, xs = 0, au[2] = {0, 0};
+        uint32_t K0 = 0, au[2] = {0, 0};
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
             const uint32_t b = tile / p.tiles_per_vehicle, tv = tile % p.tiles_per_vehicle;
             const uint32_t srow = tv * kRows + row;  // sample index within the shard
             const size_t grow = static_cast<size_t>(b) * a.S + srow;
-            float* cand_row = a.cand_out + grow * TA;
-            // sampling (as sample_kernel / the fused kernels)
-            for (uint32_t e = 0; e < TA; ++e) {
-                const uint32_t act = e & 3u;
-                const size_t mi = static_cast<size_t>(b) * TA + e;
-                float v;
-                if (a.sample_base + srow == 0) {
-                    v = a.mean[mi];
-                } else {
-                    const uint64_t gi = global_row(b, srow, a.sample_base, a.sample_total, a.S) * TA + e;
-                    const float eps = a.noise ? a.noise[grow * TA + e] : normal_at(a.seed, a.offset + gi);
-                    v = a.mean[mi] + eps * a.std[mi];
-                }
-                cand_row[e] = cmin(cmax(v, a.low[act]), a.high[act]);
-            }
+            const float* cand_row = a.cand_out + grow * TA;  // drawn by sample_kernel
             float x[18];
 #pragma unroll
             for (int i = 0; i < 18; ++i) x[i] = a.state_hist[(static_cast<size_t>(b) * a.Hs + a.Hs - 1) * 18 + i];
             const float mass = a.masses ? __ldg(a.masses + b) : a.mass;
             float cost = 0.0f;
             for (uint32_t t = 0; ok && t <= T; ++t) {
-                // (1) the action-TCN input of step t -> X ring
-                if (t < T) {
-                    const uint32_t xslot = xs & 1u;
-                    if (!(ok = tc::mbar_wait(&s.x_empty[xslot], ((xs >> 1) & 1u) ^ 1u, err, 8, xs))) break;
-                    action_tcn_step(p, s, cand_row, b, t, row, s.X[xslot]);
-                    tc::fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&s.x_full[xslot]);
-                    ++xs;
-                }
-                // (2) prober of step t-1 (entry 9t + 1; at t = 0 an empty entry; the last at 9T)
+                // prober of step t-1 (entry 9t + 1; at t = 0 an empty entry; the last at 9T)
                 const uint32_t k = K0 + (t < T ? 9 * t + 1 : 9 * T);
                 const uint32_t slot = k & 1u;
                 if (!(ok = tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k))) break;
@@ -571,7 +632,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                         tc::tmem_ld16(lane_base + slot * 128 + c0, v);
                         tc::tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) h1[c0 + i] = gelu_tanh(v[i] + pw[c0 + i]);
+                        for (int i = 0; i < 16; ++i) h1[c0 + i] = gelu_fast(v[i] + pw[c0 + i]);
                     }
                     tc::fence_before();
                     __syncwarp();
@@ -589,7 +650,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                                 s0 = fmaf(h1[i], W[o * hid + i], s0);
                                 s1 = fmaf(h1[i + 1], W[o * hid + i + 1], s1);
                             }
-                            h2[o] = gelu_tanh((s0 + s1) + bb[o]);
+                            h2[o] = gelu_fast((s0 + s1) + bb[o]);
                         }
 #pragma unroll
                         for (uint32_t o = 0; o < hid; ++o) h1[o] = h2[o];
@@ -794,8 +855,10 @@ bool skyjepa_tc_supported(const SkyjepaArgs& a, const char** why) {
         return false;
     }
     if (a.hid != kMaxHid) { *why = "the tensor-core path needs prober hidden_dim 32"; return false; }
-    if (a.Hs != static_cast<uint32_t>(kTcnHs) || a.action_tcn.k != static_cast<uint32_t>(kTcnK)) {
-        *why = "the tensor-core path needs a 10-step history and action-encoder kernel 3";
+    if (a.Hs != static_cast<uint32_t>(kTcnHs) || a.action_tcn.k != static_cast<uint32_t>(kTcnK) ||
+        a.action_tcn.levels != 3 || a.action_tcn.blocks[0].dil != 1 || a.action_tcn.blocks[1].dil != 2 ||
+        a.action_tcn.blocks[2].dil != 4) {
+        *why = "the tensor-core path needs a 10-step history and a 3-level action encoder with kernel 3";
         return false;
     }
     if (a.prober_layers < 1 || a.prober_layers > kMaxLayers) { *why = "prober hidden_layers must be 1..3"; return false; }
@@ -822,17 +885,37 @@ cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t 
 
 uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S) { return S / kRows; }
 
-cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, int* err, cudaStream_t stream,
-                              int* launches) {
+cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
+                              cudaStream_t stream, int* launches) {
+    // 1. candidates (sample_kernel: Philox or injected noise, mean slot, clamp)
+    SampleArgs sa{};
+    sa.B = a.B; sa.S = a.S; sa.T = a.T; sa.A = 4;
+    sa.mean = a.mean;
+    sa.std = a.std;
+    sa.low = a.low_dev;
+    sa.high = a.high_dev;
+    sa.noise = a.noise;
+    sa.seed = a.seed;
+    sa.offset = a.offset;
+    sa.sample_base = a.sample_base;
+    sa.sample_total = a.sample_total;
+    sa.out = a.cand_out;
+    cudaError_t e = launch_sample(sa, stream);
+    if (e != cudaSuccess) return e;
+    // 2. per-step inputs of every candidate, 3. initial latent per vehicle
+    const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
+    skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, xtiles);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
     skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // 4. the rollout
     TcArgs p;
     p.a = a;
     p.wc = packed;
     p.p1 = packed + static_cast<size_t>(kChunks) * kChunkBytes;
     p.h0 = h0;
+    p.xt = xtiles;
     p.tiles_per_vehicle = a.S / kRows;
     p.tiles = a.B * p.tiles_per_vehicle;
     p.err = err;
@@ -848,8 +931,12 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t grid = static_cast<uint32_t>(sms) < p.tiles ? static_cast<uint32_t>(sms) : p.tiles;
     skyjepa_tc_kernel<<<grid, kThreadsTc, smem, stream>>>(p);
-    if (launches) *launches = 2;
+    if (launches) *launches = 4;
     return cudaGetLastError();
+}
+
+size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T) {
+    return static_cast<size_t>(B) * (S / kRows) * T * kXBytes;
 }
 
 }  // namespace lwm

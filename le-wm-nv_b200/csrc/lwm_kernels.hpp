@@ -147,6 +147,8 @@ struct SkyjepaArgs {
     const float* mean;            // [B,T,4]
     const float* std;             // [B,T,4]
     float low[4], high[4];
+    const float* low_dev;         // the same bounds in device memory ([16] each)
+    const float* high_dev;
     const float* noise;
     uint64_t seed, offset;
     const float* cand_in;
@@ -163,8 +165,9 @@ bool skyjepa_tc_supported(const SkyjepaArgs& a, const char** why);
 size_t skyjepa_tc_packed_bytes();
 cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
 uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S);
-cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, int* err, cudaStream_t stream,
-                              int* launches);
+cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
+                              cudaStream_t stream, int* launches);
+size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
 
 cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
                                uint32_t S, cudaStream_t stream);

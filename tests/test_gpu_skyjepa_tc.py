@@ -2,7 +2,7 @@
 recurrent state, f32 accumulation) against the f32 oracle: per-candidate
 costs within 2e-2 relative (the bf16 predictor tolerance), the MPPI sequence
 close to the oracle's, and the tensor-core path actually taken (it launches
-two kernels per iteration: h0 + the persistent rollout)."""
+four kernels per iteration: sampling, per-step inputs, h0 and the persistent rollout)."""
 import numpy as np
 import pytest
 
@@ -55,7 +55,7 @@ def test_tc_mppi_matches_oracle(ctx, batch, samples, horizon):
     sc = _scorer(ctx, w)
     n0 = ctx.launch_count()
     r = p.plan(sc, injected_noise=noise)
-    assert ctx.launch_count() - n0 == 2, "the tensor-core path was not taken"
+    assert ctx.launch_count() - n0 == 4, "the tensor-core path was not taken"
     _check(r, _oracle_plan(w, noise))
 
 
