@@ -29,8 +29,9 @@
 // with bounded waits; a wait that gives up records where and the kernel
 // unwinds.
 //
-// TMEM (512 columns): accumulator slots 0 and 1 = columns [0,128) and
-// [128,256); h_t (f32) = columns [256,512).  Weights are bf16 (packed once
+// TMEM (512 columns): two accumulator slots of 128 columns = [0,256); h_t
+// (f32) = [256,512).  (A tcgen05.mma of M = 128, K = 16 costs the issuing
+// thread about the same below N ~ 128, so chunks are as wide as TMEM allows.)  Weights are bf16 (packed once
 // per scorer by pack_tc_weights_kernel; the GRU biases ride in the x block);
 // the prober's later layers, the TCN and the integrator stay f32.
 #include <cuda_bf16.h>
@@ -46,10 +47,19 @@ namespace lwm {
 
 namespace {
 
-constexpr uint32_t kRows = 128, kH = 256, kChunks = 8;
-constexpr uint32_t kChunkHBytes = 4 * 96 * 128;  // 4 K-blocks x 96 rows (r, z, n_h) x 128 B
-constexpr uint32_t kChunkXBytes = 128 * 32;      // 128 rows (r, z, n_h, n_x) x 16 k (SW32)
-constexpr uint32_t kChunkBytes = kChunkHBytes + kChunkXBytes;
+constexpr uint32_t kRows = 128, kH = 256;
+constexpr uint32_t kUnits = 32;                   // hidden units per chunk
+constexpr uint32_t kChunks = kH / kUnits;         // 8 chunks per step
+constexpr uint32_t kHRows = 3 * kUnits;           // B rows of the h part: r, z, n_h
+constexpr uint32_t kXRows = 4 * kUnits;           // B rows of the x part: r, z, n_h, n_x
+constexpr uint32_t kChunkHBytes = 4 * kHRows * 128;  // 4 K-blocks x 96 rows x 128 B (SW128)
+constexpr uint32_t kChunkXBytes = kXRows * 32;       // 128 rows x 16 k (SW32)
+constexpr uint32_t kChunkBytes = kChunkHBytes + kChunkXBytes;  // 52 KB, 1024-aligned
+constexpr uint32_t kWStages = 2;                  // weight-chunk ring
+constexpr uint32_t kSlots = 2, kSlotCols = kXRows; // accumulator ring: 2 x 128 TMEM columns
+constexpr uint32_t kUPW = kUnits / 2;             // units per epilogue warp and chunk
+constexpr uint32_t kHCol = kSlots * kSlotCols;    // h (f32) lives in TMEM columns [256, 512)
+constexpr uint32_t kEntries = kChunks + 1;        // accumulator-ring entries per step (chunks + prober)
 constexpr uint32_t kABytes = 4 * 128 * 128;
 constexpr uint32_t kXBytes = 128 * 32;
 constexpr uint32_t kMaxHid = 32, kMaxLayers = 3;
@@ -63,7 +73,7 @@ constexpr uint32_t kMaxHistTc = 16;
 
 struct __align__(1024) TcSmem {
     uint8_t A[kABytes];
-    uint8_t W[2][kChunkBytes];
+    uint8_t W[kWStages][kChunkBytes];
     uint8_t X[2][kXBytes];
     uint8_t P1[kP1Bytes];
     float pw[kPwFloats];  // prober: b1, hidden layers (W, b), output (W, b)
@@ -73,7 +83,8 @@ struct __align__(1024) TcSmem {
     // accumulator slots are shared by two consumer groups (0: GRU epilogue,
     // 1: prober/aux); each group has its own full/empty barrier per slot so
     // every waiter sees every phase of the barriers it waits on
-    uint64_t w_full[2], w_empty[2], full[2][2], empty[2][2], x_full[2], x_empty[2], h_full, a_read, done;
+    uint64_t w_full[kWStages], w_empty[kWStages], full[2][kSlots], empty[2][kSlots], x_full[2], x_empty[2], h_full,
+        a_read, done;
     uint32_t tmem;
     int last;
 };
@@ -103,11 +114,9 @@ __device__ __forceinline__ uint32_t bf2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 16 f32 values as bf16 into two 16-byte chunks of a K-major tile row.
-__device__ __forceinline__ void store_bf16x16(uint8_t* dst0, uint8_t* dst1, const float (&v)[16]) {
-    *reinterpret_cast<uint4*>(dst0) = make_uint4(bf2(v[0], v[1]), bf2(v[2], v[3]), bf2(v[4], v[5]), bf2(v[6], v[7]));
-    *reinterpret_cast<uint4*>(dst1) =
-        make_uint4(bf2(v[8], v[9]), bf2(v[10], v[11]), bf2(v[12], v[13]), bf2(v[14], v[15]));
+// 8 f32 values as bf16 into one 16-byte chunk of a K-major tile row.
+__device__ __forceinline__ void store_bf16x8(uint8_t* dst, const float (&v)[8]) {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(bf2(v[0], v[1]), bf2(v[2], v[3]), bf2(v[4], v[5]), bf2(v[6], v[7]));
 }
 
 // The element (row, k) of the prober / recurrent weights in the packed layouts.
@@ -119,25 +128,25 @@ __host__ __device__ inline uint32_t packed_h_offset(uint32_t j, uint32_t k, uint
 
 // ------------------------------------------------------- weight packing
 //
-// Wc[chunk]: H part (rows r_u, z_u, n_u of the chunk's 32 units, K = 256 of
+// Wc[chunk]: H part (rows r_u, z_u, n_u of the chunk's 16 units, K = 256 of
 // weight_hh) in SW128 K-blocks, then the X part (rows r, z, n_h, n_x; k < E
 // weight_ih (zero for n_h), k = E the biases) in SW32.  P1: prober input
 // layer [hid x 256].
 __global__ void pack_tc_weights_kernel(SkyjepaArgs a, uint8_t* wc, uint8_t* p1) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const size_t n_h = static_cast<size_t>(kChunks) * 96 * kH;
-    const size_t n_x = static_cast<size_t>(kChunks) * 128 * 16;
+    const size_t n_h = static_cast<size_t>(kChunks) * kHRows * kH;
+    const size_t n_x = static_cast<size_t>(kChunks) * kXRows * 16;
     const size_t n_p = static_cast<size_t>(a.hid) * kH;
     if (i < n_h) {
-        const uint32_t c = static_cast<uint32_t>(i / (96 * kH)), rem = static_cast<uint32_t>(i % (96 * kH));
-        const uint32_t j = rem / kH, k = rem % kH, g = j / 32, u = c * 32 + j % 32;
+        const uint32_t c = static_cast<uint32_t>(i / (kHRows * kH)), rem = static_cast<uint32_t>(i % (kHRows * kH));
+        const uint32_t j = rem / kH, k = rem % kH, g = j / kUnits, u = c * kUnits + j % kUnits;
         const float v = a.w_hh[static_cast<size_t>(g * kH + u) * kH + k];
-        *reinterpret_cast<__nv_bfloat16*>(wc + static_cast<size_t>(c) * kChunkBytes + packed_h_offset(j, k, 96)) =
+        *reinterpret_cast<__nv_bfloat16*>(wc + static_cast<size_t>(c) * kChunkBytes + packed_h_offset(j, k, kHRows)) =
             __float2bfloat16_rn(v);
     } else if (i < n_h + n_x) {
         const size_t q = i - n_h;
-        const uint32_t c = static_cast<uint32_t>(q / (128 * 16)), rem = static_cast<uint32_t>(q % (128 * 16));
-        const uint32_t j = rem / 16, k = rem % 16, g = j / 32, u = c * 32 + j % 32;
+        const uint32_t c = static_cast<uint32_t>(q / (kXRows * 16)), rem = static_cast<uint32_t>(q % (kXRows * 16));
+        const uint32_t j = rem / 16, k = rem % 16, g = j / kUnits, u = c * kUnits + j % kUnits;
         float v = 0.0f;
         if (k < a.E && g != 2) {
             const uint32_t gate = g == 3 ? 2u : g;  // n_x uses weight_ih's n rows
@@ -383,13 +392,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
 
     // ---- setup: barriers, TMEM, resident weights
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (uint32_t i = 0; i < kWStages; ++i) {
             tc::mbar_init(&s.w_full[i], 1);
             tc::mbar_init(&s.w_empty[i], 1);
+        }
+        for (uint32_t i = 0; i < kSlots; ++i) {
             tc::mbar_init(&s.full[0][i], 1);
             tc::mbar_init(&s.full[1][i], 1);
             tc::mbar_init(&s.empty[0][i], 8);
             tc::mbar_init(&s.empty[1][i], 4);
+        }
+        for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&s.x_full[i], 1);
             tc::mbar_init(&s.x_empty[i], 1);
         }
@@ -420,7 +433,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = s.tmem;
-    const uint32_t entries = 9 * T + 1;  // acc-ring entries per tile
+    const uint32_t entries = kEntries * T + 1;  // acc-ring entries per tile
 
     if (warp == 0) {
         // ================= producer: weight chunks, 2 slots
@@ -434,7 +447,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     tc::bulk_g2s(s.X[xslot], p.xt + (static_cast<size_t>(tile) * T + t) * kXBytes, kXBytes,
                                  &s.x_full[xslot]);
                     for (uint32_t c = 0; c < kChunks; ++c, ++j) {
-                        const uint32_t slot = j & 1u, n = j >> 1;
+                        const uint32_t slot = j % kWStages, n = j / kWStages;
                         if (!tc::mbar_wait(&s.w_empty[slot], (n & 1u) ^ 1u, err, 1, j)) break;
                         tc::mbar_expect_tx(&s.w_full[slot], kChunkBytes);
                         tc::bulk_g2s(s.W[slot], p.wc + static_cast<size_t>(c) * kChunkBytes, kChunkBytes,
@@ -445,22 +458,23 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     } else if (warp == 1) {
         // ================= MMA issuer
         if (lane == 0) {
-            const uint32_t id_gru_x = tc::idesc_bf16_f32(128, 128), id_gru_h = tc::idesc_bf16_f32(128, 96);
+            const uint32_t id_gru_x = tc::idesc_bf16_f32(128, kXRows), id_gru_h = tc::idesc_bf16_f32(128, kHRows);
             const uint32_t id_prob = tc::idesc_bf16_f32(128, hid);
             const uint32_t a_base = tc::smem_u32(s.A), p_base = tc::smem_u32(s.P1);
             uint32_t j = 0, K = 0, xs = 0, hq = 0;
-            uint32_t uses[2][2] = {{0, 0}, {0, 0}};
-            int last[2] = {-1, -1};
-            // entry K goes to slot K & 1: wait until the slot's previous consumer group released it
+            uint32_t uses[2][kSlots] = {};
+            int last[kSlots];
+            for (uint32_t i = 0; i < kSlots; ++i) last[i] = -1;
+            // entry K goes to slot K % kSlots: wait until the slot's previous consumer group released it
             auto acc_slot = [&](uint32_t k, uint32_t& col) -> bool {
-                const uint32_t slot = k & 1u;
-                col = slot * 128u;
+                const uint32_t slot = k % kSlots;
+                col = slot * kSlotCols;
                 if (last[slot] < 0) return true;
                 const int g = last[slot];
                 return tc::mbar_wait(&s.empty[g][slot], (uses[g][slot] - 1u) & 1u, err, 5, k);
             };
             auto publish = [&](uint32_t k, int g) {
-                const uint32_t slot = k & 1u;
+                const uint32_t slot = k % kSlots;
                 tc::commit(&s.full[g][slot]);
                 ++uses[g][slot];
                 last[slot] = g;
@@ -489,8 +503,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     if (ok) ok = tc::mbar_wait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs);
                     for (uint32_t c = 0; ok && c < kChunks; ++c, ++j) {
                         if (c == 1 && !(ok = prober(t > 0))) break;  // prober of step t-1 (A = h_t)
-                        const uint32_t wslot = j & 1u;
-                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j >> 1) & 1u, err, 4, j))) break;
+                        const uint32_t wslot = j % kWStages;
+                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j / kWStages) & 1u, err, 4, j))) break;
                         uint32_t col;
                         if (!(ok = acc_slot(K, col))) break;
                         tc::fence_after();
@@ -501,7 +515,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                             const uint32_t kb = ks >> 2, jj = ks & 3u;
                             tc::mma_bf16(tmem + col,
                                          tc::smem_desc(a_base + kb * 128 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
-                                         tc::smem_desc(w_base + kb * 96 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
+                                         tc::smem_desc(w_base + kb * kHRows * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
                                          id_gru_h, 1);
                         }
                         publish(K, 0);
@@ -521,12 +535,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             tc::mbar_wait(&s.done, 0, err, 10, 0);
         }
     } else if (warp < kAuxWarp0) {
-        // ================= GRU epilogue: quadrant q, units [16 half, 16 half + 16) of each chunk
+        // ================= GRU epilogue: quadrant q, units [kUPW half, kUPW (half + 1)) of each chunk
         const uint32_t q = warp & 3u, half = (warp - kEpiWarp0) >> 2;
         const uint32_t row = q * 32 + lane;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         uint32_t K0 = 0;  // acc-ring entry index of the tile's first entry
-        uint32_t eu[2] = {0, 0}, tiles_done = 0;
+        uint32_t eu[kSlots] = {}, tiles_done = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
             const uint32_t b = tile / p.tiles_per_vehicle;
@@ -536,15 +550,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 tc::fence_after();
             }
             // h0 of the vehicle -> H (TMEM f32) and A (bf16), this warp's units
-            for (uint32_t c = 0; c < kChunks; ++c) {
-                const uint32_t u0 = c * 32 + half * 16;
-                float hv[16];
+            // this warp's units: kUPW of every chunk, u = kUnits c + kUPW half + i
+            for (uint32_t c = 0; c < kChunks; ++c)
+                for (uint32_t g8 = 0; g8 < kUPW; g8 += 8) {
+                    const uint32_t u0 = c * kUnits + half * kUPW + g8;
+                    float hv[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) hv[i] = __ldg(p.h0 + static_cast<size_t>(b) * kH + u0 + i);
-                tc::tmem_st16(lane_base + 256 + u0, hv);
-                uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
-                store_bf16x16(blk + tc::sw128_offset(row, u0 & 63u), blk + tc::sw128_offset(row, (u0 & 63u) + 8), hv);
-            }
+                    for (int i = 0; i < 8; ++i) hv[i] = __ldg(p.h0 + static_cast<size_t>(b) * kH + u0 + i);
+                    tc::tmem_st8(lane_base + kHCol + u0, hv);
+                    uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
+                    store_bf16x8(blk + tc::sw128_offset(row, u0 & 63u), hv);
+                }
             tc::tmem_st_wait();
             tc::fence_async_smem();
             tc::fence_before();
@@ -552,19 +568,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             if (lane == 0) tc::mbar_arrive(&s.h_full);
             for (uint32_t t = 0; ok && t < T; ++t) {
                 for (uint32_t c = 0; c < kChunks; ++c) {
-                    const uint32_t k = K0 + 9 * t + (c == 0 ? 0u : c + 1u);
-                    const uint32_t slot = k & 1u;
+                    const uint32_t k = K0 + kEntries * t + (c == 0 ? 0u : c + 1u);
+                    const uint32_t slot = k % kSlots;
                     if (!(ok = tc::mbar_wait(&s.full[0][slot], eu[slot] & 1u, err, 6, k))) break;
                     ++eu[slot];
                     tc::fence_after();
-                    const uint32_t u0 = c * 32 + half * 16;
-                    const uint32_t acol = lane_base + slot * 128 + half * 16;
+                    static_assert(kUPW == 16, "the gate loop loads 16 units per warp");
+                    {
+                    const uint32_t u0 = c * kUnits + half * kUPW;
+                    const uint32_t acol = lane_base + slot * kSlotCols + half * kUPW;
                     float r[16], z[16], nh[16], nx[16], hv[16];
                     tc::tmem_ld16(acol, r);
-                    tc::tmem_ld16(acol + 32, z);
-                    tc::tmem_ld16(acol + 64, nh);
-                    tc::tmem_ld16(acol + 96, nx);
-                    tc::tmem_ld16(lane_base + 256 + u0, hv);
+                    tc::tmem_ld16(acol + kUnits, z);
+                    tc::tmem_ld16(acol + 2 * kUnits, nh);
+                    tc::tmem_ld16(acol + 3 * kUnits, nx);
+                    tc::tmem_ld16(lane_base + kHCol + u0, hv);
                     tc::tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
@@ -573,7 +591,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                         const float ng = tanh_fast(fmaf(rg, nh[i], nx[i]));
                         hv[i] = zg * hv[i] - (zg - 1.0f) * ng;  // GRU::step, h' = z h - (z - 1) n
                     }
-                    tc::tmem_st16(lane_base + 256 + u0, hv);
+                    tc::tmem_st16(lane_base + kHCol + u0, hv);
+                    }
                     tc::tmem_st_wait();
                     tc::fence_before();
                     __syncwarp();
@@ -581,15 +600,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 }
                 if (!ok) break;
                 // all MMAs of step t are done (the last chunk's completed): h_{t+1} -> A
-                for (uint32_t c = 0; c < kChunks; ++c) {
-                    const uint32_t u0 = c * 32 + half * 16;
-                    float hv[16];
-                    tc::tmem_ld16(lane_base + 256 + u0, hv);
-                    tc::tmem_ld_wait();
-                    uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
-                    store_bf16x16(blk + tc::sw128_offset(row, u0 & 63u), blk + tc::sw128_offset(row, (u0 & 63u) + 8),
-                                  hv);
-                }
+                for (uint32_t c = 0; c < kChunks; ++c)
+                    for (uint32_t g8 = 0; g8 < kUPW; g8 += 8) {
+                        const uint32_t u0 = c * kUnits + half * kUPW + g8;
+                        float hv[8];
+                        tc::tmem_ld8(lane_base + kHCol + u0, hv);
+                        tc::tmem_ld_wait();
+                        uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
+                        store_bf16x8(blk + tc::sw128_offset(row, u0 & 63u), hv);
+                    }
                 tc::fence_async_smem();
                 tc::fence_before();
                 __syncwarp();
@@ -603,7 +622,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
         const uint32_t q = warp & 3u, row = q * 32 + lane, atid = tid - kAuxWarp0 * 32;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         const uint32_t TA = T * 4u;
-        uint32_t K0 = 0, au[2] = {0, 0};
+        uint32_t K0 = 0, au[kSlots] = {};
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
             const uint32_t b = tile / p.tiles_per_vehicle, tv = tile % p.tiles_per_vehicle;
@@ -616,9 +635,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             const float mass = a.masses ? __ldg(a.masses + b) : a.mass;
             float cost = 0.0f;
             for (uint32_t t = 0; ok && t <= T; ++t) {
-                // prober of step t-1 (entry 9t + 1; at t = 0 an empty entry; the last at 9T)
-                const uint32_t k = K0 + (t < T ? 9 * t + 1 : 9 * T);
-                const uint32_t slot = k & 1u;
+                // prober of step t-1 (entry kEntries t + 1; at t = 0 an empty entry; the last at kEntries T)
+                const uint32_t k = K0 + (t < T ? kEntries * t + 1 : kEntries * T);
+                const uint32_t slot = k % kSlots;
                 if (!(ok = tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k))) break;
                 ++au[slot];
                 tc::fence_after();
@@ -629,7 +648,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
 #pragma unroll
                     for (uint32_t c0 = 0; c0 < kMaxHid; c0 += 16) {
                         float v[16];
-                        tc::tmem_ld16(lane_base + slot * 128 + c0, v);
+                        tc::tmem_ld16(lane_base + slot * kSlotCols + c0, v);
                         tc::tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) h1[c0 + i] = gelu_fast(v[i] + pw[c0 + i]);
@@ -876,7 +895,7 @@ size_t skyjepa_tc_packed_bytes() { return static_cast<size_t>(kChunks) * kChunkB
 cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream) {
     cudaError_t e = cudaMemsetAsync(packed, 0, skyjepa_tc_packed_bytes(), stream);
     if (e != cudaSuccess) return e;
-    const size_t n = static_cast<size_t>(kChunks) * 96 * kH + static_cast<size_t>(kChunks) * 128 * 16 +
+    const size_t n = static_cast<size_t>(kChunks) * kHRows * kH + static_cast<size_t>(kChunks) * kXRows * 16 +
                      static_cast<size_t>(a.hid) * kH;
     pack_tc_weights_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, stream>>>(
         a, packed, packed + static_cast<size_t>(kChunks) * kChunkBytes);
