@@ -172,12 +172,23 @@ __global__ void pack_tc_weights_kernel(SkyjepaArgs a, uint8_t* wc, uint8_t* p1) 
 // --------------------------------------------------- initial latent h0
 //
 // encode_state_history (model.rs:57-61): the state TCN over the normalised
-// history, last step, state_projection.  One block per vehicle.
+// history, last step, state_projection.  One block per vehicle; one warp per
+// output channel, its lanes striding the (input channel, tap) weights of that
+// channel (contiguous in the blob) and a warp reduction per window position.
+constexpr int kH0MaxHist = 16;
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h0) {
     extern __shared__ float sh[];
-    const uint32_t b = blockIdx.x, tid = threadIdx.x, Hs = a.Hs;
+    const uint32_t b = blockIdx.x, tid = threadIdx.x, Hs = a.Hs, warp = tid >> 5, lane = tid & 31;
+    const uint32_t nwarps = blockDim.x >> 5;
     const TcnView& tcn = a.state_tcn;
-    const uint32_t C = tcn.max_ch;
+    const uint32_t C = tcn.max_ch, K = tcn.k;
     float* cur = sh;                 // [C][Hs]
     float* h1 = cur + C * Hs;        // [C][Hs]
     float* h2 = h1 + C * Hs;         // [C][Hs]
@@ -195,38 +206,60 @@ __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h
             const uint32_t cin = conv == 0 ? bk.in : bk.out;
             const float* W = conv == 0 ? bk.w1 : bk.w2;
             const float* bias = conv == 0 ? bk.b1 : bk.b2;
-            for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) {
-                const uint32_t o = q / Hs, t = q % Hs;
-                float acc = 0.0f;
-                for (uint32_t i = 0; i < cin; ++i)
-                    for (uint32_t j = 0; j < tcn.k; ++j) {
-                        const int src_t = static_cast<int>(t) - static_cast<int>((tcn.k - 1 - j) * bk.dil);
-                        if (src_t >= 0) acc = fmaf(W[(o * cin + i) * tcn.k + j], src[i * Hs + src_t], acc);
-                    }
-                dst[o * Hs + t] = gelu_tanh(acc + bias[o]);
+            for (uint32_t o = warp; o < bk.out; o += nwarps) {
+                float acc[kH0MaxHist];
+#pragma unroll
+                for (int t = 0; t < kH0MaxHist; ++t) acc[t] = 0.0f;
+                const float* wo = W + static_cast<size_t>(o) * cin * K;
+                for (uint32_t idx = lane; idx < cin * K; idx += 32) {
+                    const uint32_t i = idx / K, jj = idx % K;
+                    const float wv = __ldg(wo + idx);
+                    const int shift = static_cast<int>((K - 1 - jj) * bk.dil);
+                    const float* xi = src + i * Hs;
+#pragma unroll
+                    for (int t = 0; t < kH0MaxHist; ++t)
+                        if (t < static_cast<int>(Hs) && t >= shift) acc[t] = fmaf(wv, xi[t - shift], acc[t]);
+                }
+#pragma unroll
+                for (int t = 0; t < kH0MaxHist; ++t) {
+                    const float v = warp_sum_f(acc[t]);
+                    if (lane == 0 && t < static_cast<int>(Hs)) dst[o * Hs + t] = gelu_tanh(v + bias[o]);
+                }
             }
             __syncthreads();
         }
-        for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) {
-            const uint32_t o = q / Hs, t = q % Hs;
-            float res;
+        // residual (1x1 conv when the width changes) and the block output, into h1
+        for (uint32_t o = warp; o < bk.out; o += nwarps) {
+            float res[kH0MaxHist];
+#pragma unroll
+            for (int t = 0; t < kH0MaxHist; ++t) res[t] = 0.0f;
             if (bk.wr) {
-                float r = 0.0f;
-                for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(bk.wr[o * bk.in + i], cur[i * Hs + t], r);
-                res = r + bk.br[o];
+                for (uint32_t i = lane; i < bk.in; i += 32) {
+                    const float wv = __ldg(bk.wr + static_cast<size_t>(o) * bk.in + i);
+#pragma unroll
+                    for (int t = 0; t < kH0MaxHist; ++t)
+                        if (t < static_cast<int>(Hs)) res[t] = fmaf(wv, cur[i * Hs + t], res[t]);
+                }
+#pragma unroll
+                for (int t = 0; t < kH0MaxHist; ++t) res[t] = warp_sum_f(res[t]) + bk.br[o];
             } else {
-                res = cur[o * Hs + t];
+#pragma unroll
+                for (int t = 0; t < kH0MaxHist; ++t)
+                    if (t < static_cast<int>(Hs)) res[t] = cur[o * Hs + t];
             }
-            h1[o * Hs + t] = gelu_tanh(h2[o * Hs + t] + res);
+            if (lane == 0)
+                for (uint32_t t = 0; t < Hs; ++t) h1[o * Hs + t] = gelu_tanh(h2[o * Hs + t] + res[t]);
         }
         __syncthreads();
         for (uint32_t q = tid; q < bk.out * Hs; q += blockDim.x) cur[q] = h1[q];
         __syncthreads();
     }
-    for (uint32_t u = tid; u < a.H; u += blockDim.x) {
+    for (uint32_t u = warp; u < a.H; u += nwarps) {
         float acc = 0.0f;
-        for (uint32_t c = 0; c < tcn.out_dim; ++c) acc = fmaf(a.proj_w[u * tcn.out_dim + c], cur[c * Hs + Hs - 1], acc);
-        h0[static_cast<size_t>(b) * a.H + u] = acc + a.proj_b[u];
+        for (uint32_t c = lane; c < tcn.out_dim; c += 32)
+            acc = fmaf(__ldg(a.proj_w + static_cast<size_t>(u) * tcn.out_dim + c), cur[c * Hs + Hs - 1], acc);
+        acc = warp_sum_f(acc);
+        if (lane == 0) h0[static_cast<size_t>(b) * a.H + u] = acc + a.proj_b[u];
     }
 }
 
