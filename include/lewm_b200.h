@@ -528,6 +528,15 @@ lwm_status lwm_lewm_encode_vector_device(lwm_scorer* scorer, const float* obs, u
  * pixels [n, C, image, image] -> device embeddings [n, D]. */
 lwm_status lwm_lewm_encode_pixels_device(lwm_scorer* scorer, const float* pixels, uint32_t n, float* out);
 
+/* IcemPlanner::trace_device (src/planner.rs:900-1010): plan without
+ * deadlines and record, per iteration, the scores of the mean before
+ * sampling, the best candidate, the elite mean and the updated mean:
+ * *trace -> device [iterations][4][B] f32 (IcemTraceDeviceStep's
+ * mean_score, best_candidate_score, elite_mean_score, updated_mean_score),
+ * valid until the planner's next call. */
+lwm_status lwm_icem_trace_device(lwm_planner* planner, lwm_scorer* scorer, const float* injected_noise,
+                                 lwm_plan_device_result* out, const float** trace);
+
 /* ---------------------------------------------------------------- candidate-range sharding */
 
 /* Multi-GPU MPPI over one vehicle batch: each GPU's planner owns samples

@@ -171,6 +171,8 @@ struct lwm_planner {
         best, best_score, carried, noise_tmp;
     HostBuf staging;
     uint32_t last_batch = 0, last_cols = 0;
+    // iCEM trace: [iterations][4][B] scores and the elite mean of an iteration
+    DevBuf trace, trace_elite;
     // candidate-range shard (shard_total 0: unsharded) and its combined tuples
     uint32_t shard_base = 0, shard_total = 0;
     DevBuf shard_tuples;
@@ -571,7 +573,11 @@ lwm_status deadline_result(lwm_planner* p, uint32_t B, bool use_warm, const char
     return LWM_OK;
 }
 
-lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
+// `trace` (iCEM only): IcemPlanner::trace_device (src/planner.rs:900-1010) —
+// no deadlines; per iteration the scores of the mean, the best candidate, the
+// elite mean and the updated mean go to p->trace ([iterations][4][B]).
+lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out,
+                              bool trace = false) {
     const auto start = std::chrono::steady_clock::now();
     (void)cudaGetLastError();  // drop a stale non-sticky error of an earlier failed call
     LWM_TRY(validate_planner(p));
@@ -626,7 +632,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
     }
     const uint32_t carried_keep = p->kind == PlannerKind::Icem ? p->icem.keep_elites : 0;
     for (uint32_t it = 0; it < p->iterations; ++it) {
-        if (deadline_ns >= 0) {
+        if (deadline_ns >= 0 && !trace) {
             const auto el = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count();
             if (el >= deadline_ns) {
                 deadline_hit = true;
@@ -713,6 +719,8 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 s.inject = std::min(carried_keep, p->S - 1);
             }
             s.out = p->cand.as<float>();
+            float* tr = trace ? p->trace.as<float>() + static_cast<size_t>(it) * 4 * B : nullptr;
+            if (tr) LWM_TRY(score_device(sc, p->mean.as<float>(), B, 1, p->T, p->A, tr, nullptr));  // mean_score
             LWM_CUDA(lwm::launch_sample(s, stream));
             p->ctx->launches += 1;
             LWM_TRY(score_device(sc, p->cand.as<float>(), B, p->S, p->T, p->A, p->scores.as<float>(), nullptr));
@@ -745,8 +753,16 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 r.warm_start = p->kind == PlannerKind::Icem ? p->warm.as<float>() : nullptr;
                 r.best_index = p->best.as<uint32_t>();
                 r.best_score = p->best_score.as<float>();
+                r.elite_mean_out = tr ? p->trace_elite.as<float>() : nullptr;
                 LWM_CUDA(lwm::launch_topk_refit(r, B, stream));
                 p->ctx->launches += 1;
+                if (tr) {
+                    // best_candidate_score, elite_mean_score, updated_mean_score
+                    LWM_CUDA(cudaMemcpyAsync(tr + B, p->best_score.ptr, static_cast<size_t>(B) * 4,
+                                             cudaMemcpyDeviceToDevice, stream));
+                    LWM_TRY(score_device(sc, p->trace_elite.as<float>(), B, 1, p->T, p->A, tr + 2 * B, nullptr));
+                    LWM_TRY(score_device(sc, p->mean.as<float>(), B, 1, p->T, p->A, tr + 3 * B, nullptr));
+                }
             }
         }
         ++completed;
@@ -977,7 +993,8 @@ lwm_status lwm_planner_destroy(lwm_planner* p) {
     cudaSetDevice(p->ctx->device);
     cudaStreamSynchronize(p->ctx->stream);
     for (DevBuf* b : {&p->bounds, &p->zeros, &p->std_init, &p->mean, &p->stdv, &p->cand, &p->scores, &p->partials, &p->counters,
-                      &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp})
+                      &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp,
+                      &p->shard_tuples, &p->trace, &p->trace_elite})
         b->release();
     p->staging.release();
     delete p;
@@ -1374,6 +1391,22 @@ lwm_status lwm_plan_device(lwm_planner* p, lwm_scorer* sc, const float* injected
     std::lock_guard<std::mutex> lock2(sc->mu);
     LWM_CUDA(cudaSetDevice(p->ctx->device));
     return plan_device_locked(p, sc, injected, out);
+}
+
+lwm_status lwm_icem_trace_device(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out,
+                                 const float** trace) {
+    if (!p || !sc || !out || !trace) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (p->kind != PlannerKind::Icem) return fail(LWM_INVALID_ARGUMENT, "trace_device is an iCEM planner call");
+    if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    std::lock_guard<std::mutex> lock(p->mu);
+    std::lock_guard<std::mutex> lock2(sc->mu);
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    const uint32_t B = sc->batch;
+    LWM_TRY(p->trace.ensure(static_cast<size_t>(p->iterations) * 4 * std::max<uint32_t>(B, 1) * 4));
+    LWM_TRY(p->trace_elite.ensure(static_cast<size_t>(std::max<uint32_t>(B, 1)) * p->T * p->A * 4));
+    LWM_TRY(plan_device_locked(p, sc, injected, out, true));
+    *trace = p->trace.as<float>();
+    return LWM_OK;
 }
 
 lwm_status lwm_planner_set_shard(lwm_planner* p, uint32_t sample_base, uint32_t sample_total) {

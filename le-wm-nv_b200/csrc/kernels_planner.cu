@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
         }
         float sd = sqrtf(sq * inv_km1);
         if (a.min_std != 0.0f) sd = cmax(sd, a.min_std);
+        if (a.elite_mean_out) a.elite_mean_out[seq + e] = m;
         float new_mean = m, new_std = sd;
         if (a.icem) {
             const float pm = a.mean[seq + e], ps = a.std[seq + e];

@@ -67,6 +67,7 @@ struct RefitArgs {
     float* warm_start;     // [B,T,A] or nullptr
     uint32_t* best_index;  // [B]
     float* best_score;     // [B]
+    float* elite_mean_out; // [B,T,A] elite mean before the momentum update, or nullptr
 };
 
 // SkyJepaDomain (src/skyjepa_sim.rs:28-40) as laid out on the device.

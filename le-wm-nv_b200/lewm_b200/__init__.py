@@ -283,6 +283,7 @@ _sig("lwm_scorer_lewm_set_context", C.c_int, VP, U32, U32, U32, FP, FP)
 _sig("lwm_scorer_lewm_set_context_device", C.c_int, VP, U32, U32, U32, VP, VP)
 _sig("lwm_lewm_encode_vector_device", C.c_int, VP, VP, U32, VP)
 _sig("lwm_lewm_encode_pixels_device", C.c_int, VP, VP, U32, VP)
+_sig("lwm_icem_trace_device", C.c_int, VP, VP, VP, C.POINTER(_PlanDeviceResult), C.POINTER(VP))
 _sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
 _sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
@@ -847,6 +848,23 @@ class IcemPlanner(_Planner):
     """IcemPlanner (src/planner.rs:731-1053)."""
     kind = "iCEM"
     _create = staticmethod(lib.lwm_icem_create)
+
+    def trace_device(self, scorer: Scorer, injected_noise_ptr: Optional[int] = None):
+        """IcemPlanner::trace_device (src/planner.rs:900-1010): the plan plus, per
+        iteration, [mean_score, best_candidate_score, elite_mean_score,
+        updated_mean_score] per vehicle, as a host array [iterations, 4, B]."""
+        r = _PlanDeviceResult()
+        t = VP()
+        _check(lib.lwm_icem_trace_device(self.handle, scorer.handle,
+                                         VP(injected_noise_ptr) if injected_noise_ptr else None, C.byref(r),
+                                         C.byref(t)))
+        self.ctx.synchronize()  # the trace is written on the library's stream
+        steps = device_tensor(int(t.value), (r.iterations_completed, 4, r.batch)).cpu().numpy() \
+            if r.iterations_completed else np.zeros((0, 4, r.batch), np.float32)
+        res = PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
+                               r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9,
+                               bool(r.deadline_reached), _OUTCOME[r.deadline_outcome])
+        return res, steps
 
 
 # ------------------------------------------------------- device building blocks

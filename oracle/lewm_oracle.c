@@ -1143,10 +1143,13 @@ int orc_cem_plan(const lwm_cem_config* cfg, uint32_t B, const float* noise, uint
 }
 
 /* IcemPlanner::plan_device (src/planner.rs:778-898). */
-int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t B,
-                  const float* noise, uint64_t seed, uint64_t offset, orc_score_fn fn,
-                  void* user, float* sequence, float* scores, uint32_t* best, float* warm_out,
-                  float* last_cand) {
+/* IcemPlanner::plan_device (src/planner.rs:778-898); with `trace`, also
+ * IcemPlanner::trace_device (:900-1010): per iteration the scores of the
+ * mean, the best candidate, the elite mean and the updated mean
+ * ([iterations][4][B]). */
+static int icem_core(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise,
+                     uint64_t seed, uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores,
+                     uint32_t* best, float* warm_out, float* last_cand, float* trace) {
     uint32_t S = cfg->samples, T = cfg->horizon, A = cfg->action_dim, K = cfg->elites, keep = cfg->keep_elites;
     size_t seq_n = (size_t)B * T * A, n = (size_t)B * S * T * A;
     size_t per_iter = round_even(n);
@@ -1164,6 +1167,8 @@ int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t 
     if (warm_start) memcpy(mean, warm_start, seq_n * sizeof(float));
     for (size_t i = 0; i < seq_n; ++i) std[i] = cfg->init_std;
     for (uint32_t it = 0; it < cfg->iterations; ++it) {
+        float* tr = trace ? trace + (size_t)it * 4 * B : NULL;
+        if (tr) fn(user, mean, B, 1, T, A, tr);
         draw(noise, seed, offset, it, per_iter, n, eps);
         orc_color_noise(eps, eps, B, S, T, A, cfg->noise_beta);
         orc_sample(mean, std, eps, cfg->bounds_low, cfg->bounds_high, B, S, T, A, cand);
@@ -1172,9 +1177,14 @@ int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t 
         orc_lowest_k(sc, B, S, K, idx);
         orc_gather(cand, idx, B, S, K, T, A, el);
         orc_refit(el, B, K, T, A, cfg->min_std, em, es);
+        if (tr) {
+            for (uint32_t b = 0; b < B; ++b) tr[B + b] = sc[(size_t)b * S + idx[(size_t)b * K]];
+            fn(user, em, B, 1, T, A, tr + 2 * B);
+        }
         orc_momentum(mean, em, seq_n, cfg->alpha, mean);
         orc_momentum(std, es, seq_n, cfg->alpha, std);
         orc_min_std(std, seq_n, cfg->min_std);
+        if (tr) fn(user, mean, B, 1, T, A, tr + 3 * B);
         if (keep > 0) {
             for (uint32_t b = 0; b < B; ++b)
                 memcpy(carried + (size_t)b * keep * T * A, el + (size_t)b * K * T * A, sizeof(float) * keep * T * A);
@@ -1192,6 +1202,20 @@ int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t 
     if (last_cand) memcpy(last_cand, cand, n * sizeof(float));
     free(b1); free(mean); free(std); free(em); free(es); free(eps); free(cand); free(sc); free(idx); free(el); free(carried);
     return 0;
+}
+
+int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise, uint64_t seed,
+                  uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores, uint32_t* best,
+                  float* warm_out, float* last_cand) {
+    return icem_core(cfg, warm_start, B, noise, seed, offset, fn, user, sequence, scores, best, warm_out, last_cand,
+                     NULL);
+}
+
+int orc_icem_trace(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise, uint64_t seed,
+                   uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores, uint32_t* best,
+                   float* warm_out, float* trace) {
+    return icem_core(cfg, warm_start, B, noise, seed, offset, fn, user, sequence, scores, best, warm_out, NULL,
+                     trace);
 }
 
 /* ---------------------------------------------------------------- task */

@@ -122,6 +122,12 @@ int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t 
                   const float* noise, uint64_t seed, uint64_t offset, orc_score_fn fn,
                   void* user, float* sequence, float* scores, uint32_t* best, float* warm_out,
                   float* last_cand);
+/* IcemPlanner::trace_device (src/planner.rs:900-1010): as orc_icem_plan plus
+ * trace [iterations][4][B] = mean, best-candidate, elite-mean and
+ * updated-mean scores of every iteration. */
+int orc_icem_trace(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise,
+                   uint64_t seed, uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores,
+                   uint32_t* best, float* warm_out, float* trace);
 
 /* Scorer adapters usable as orc_score_fn (user = the matching struct). */
 typedef struct orc_nominal_ctx {

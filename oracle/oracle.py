@@ -89,6 +89,7 @@ _sig("orc_skyjepa_scores", None, VP, FP, FP, FP, FP, FP, FP, FP, FP, C.POINTER(T
 _sig("orc_mppi_plan", C.c_int, C.POINTER(_MppiConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, FP, FP, UP, FP)
 _sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
+_sig("orc_icem_trace", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_reference_state", None, C.c_int, F, F, F, FP)
 _sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
 _sig("orc_lewm_weight_count", C.c_size_t, C.c_void_p)
@@ -391,6 +392,21 @@ def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
                       fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq), fp(scores),
                       up(best), fp(warm), fp(cand))
     return dict(sequence=seq, scores=scores, best=best, warm=warm, candidates=cand)
+
+
+def icem_trace(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
+    c = cfg._c()
+    S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
+    fnp, user, keep = _plan_common(scorer, B, S, T, A)
+    seq = np.empty((B, T, A), np.float32)
+    scores = np.empty((B, S), np.float32)
+    best = np.empty(B, np.uint32)
+    warm = np.empty((B, T, A), np.float32)
+    trace = np.empty((cfg.iterations, 4, B), np.float32)
+    lib.orc_icem_trace(C.byref(c), fp(f32(warm_start)) if warm_start is not None else None, B,
+                       fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq), fp(scores),
+                       up(best), fp(warm), fp(trace))
+    return dict(sequence=seq, scores=scores, best=best, warm=warm, trace=trace)
 
 
 def reference_state(kind: int, time: float, radius: float, period: float):

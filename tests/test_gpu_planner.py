@@ -190,3 +190,47 @@ def test_warm_start_shape_mismatch_is_an_error(ctx):
     p.set_warm_start_sequence(np.zeros((2, 3, 2), np.float32))
     with pytest.raises(L.LwmError, match=r"MPPI warm-start shape \[2, 3, 2\] does not match expected \[1, 3, 2\]"):
         p.plan(L.CallbackScorer(ctx, 1, _sum_scorer))
+
+
+def test_icem_trace_matches_oracle(ctx):
+    # IcemPlanner::trace_device (src/planner.rs:900-1010) with the fused nominal
+    # scorer (the mean / elite-mean / updated-mean scores run it with one sample)
+    from lewm_b200 import workloads as W
+    w = W.nominal(seed=31, batch=2, samples=128, horizon=8)
+    cfg = L.IcemConfig(horizon=8, samples=128, elites=12, action_dim=4, keep_elites=2, iterations=3,
+                       noise_beta=1.5, alpha=0.1, init_std=0.5, action_bounds=w.mppi.action_bounds)
+    noise = normals(33, (3, 2, 128, 8, 4))
+    sc = L.NominalScorer(ctx, w.dt, w.trim, w.cost, w.substeps)
+    sc.set_context(w.initial, w.motors, w.reference_states, w.reference_actions)
+    p = L.IcemPlanner(ctx, cfg)
+    p.set_warm_start_sequence(w.warm_start)
+    d_noise = torch.as_tensor(noise).cuda()
+    torch.cuda.synchronize()
+    res, steps = p.trace_device(sc, d_noise.data_ptr())
+    ctx.synchronize()
+    seq = L.device_tensor(res.sequence, (2, 8, 4)).cpu().numpy()
+    ref = O.icem_trace(cfg, 2, (O.NOMINAL_FN, O.nominal_ctx(w.initial, w.motors, w.reference_states,
+                                                             w.reference_actions, w.cost, w.dt, w.trim)),
+                       noise=noise, warm_start=w.warm_start)
+    assert steps.shape == (3, 4, 2)
+    assert_actions_close(seq, ref["sequence"])
+    np.testing.assert_allclose(steps, ref["trace"], rtol=1e-4, atol=1e-5)
+
+
+def test_icem_trace_with_callback_scorer(ctx):
+    cfg = L.IcemConfig(horizon=6, samples=64, elites=8, action_dim=3, keep_elites=3, iterations=3, noise_beta=2.0,
+                       alpha=0.1, seed=5)
+    noise = normals(10, (3, 1, 64, 6, 3))
+    warm = normals(11, (1, 6, 3)) * 0.1
+    target = [0.2, -0.1, 0.5]
+    p = L.IcemPlanner(ctx, cfg)
+    p.set_warm_start_sequence(warm)
+    d_noise = torch.as_tensor(noise).cuda()
+    torch.cuda.synchronize()
+    res, steps = p.trace_device(L.CallbackScorer(ctx, 1, _quad(target)), d_noise.data_ptr())
+    ctx.synchronize()
+    ref = O.icem_trace(cfg, 1, lambda c: ((c - np.array(target, np.float32)) ** 2).sum(axis=(2, 3)), noise=noise,
+                       warm_start=warm)
+    assert_actions_close(L.device_tensor(res.sequence, (1, 6, 3)).cpu().numpy(), ref["sequence"], 1e-5)
+    np.testing.assert_allclose(steps, ref["trace"], rtol=1e-4, atol=1e-5)
+    assert_actions_close(p.warm_start_sequence(), ref["warm"], 1e-5)

@@ -336,3 +336,26 @@ def test_reference_trajectories():
     circle = O.reference_state(1, 0.0, 2.0, 8.0)
     assert circle[0:3].tolist() == [0.0, 0.0, 1.0]
     assert circle[8] < 0.0 and circle[14] < 1.0
+
+
+def test_icem_trace_records_the_reference_scores():
+    # IcemPlanner::trace_device (src/planner.rs:900-1010): the plan itself is
+    # the plain iCEM plan; per iteration it records the mean's score, the best
+    # candidate score, the elite mean's score and the updated mean's score.
+    cfg = IcemConfig(horizon=5, samples=48, elites=6, action_dim=2, keep_elites=2, iterations=3, noise_beta=1.0,
+                     alpha=0.2, seed=9)
+    target = np.array([0.3, -0.4], np.float32)
+
+    def quad(c):
+        return ((c - target) ** 2).sum(axis=(2, 3))
+
+    warm = np.full((2, 5, 2), 0.05, np.float32)
+    plan = O.icem_plan(cfg, 2, quad, seed=9, warm_start=warm)
+    tr = O.icem_trace(cfg, 2, quad, seed=9, warm_start=warm)
+    assert np.array_equal(tr["sequence"], plan["sequence"])
+    assert np.array_equal(tr["scores"], plan["scores"])
+    assert tr["trace"].shape == (3, 4, 2)
+    assert np.allclose(tr["trace"][0, 0], quad(warm[:, None])[:, 0], rtol=1e-6)
+    assert np.array_equal(tr["trace"][-1, 1], tr["scores"].min(axis=1))
+    # the final mean (return_mean) is the last updated mean
+    assert np.allclose(tr["trace"][-1, 3], quad(tr["sequence"][:, None])[:, 0], rtol=1e-6)
