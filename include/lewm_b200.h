@@ -664,6 +664,48 @@ lwm_status lwm_skyjepa_geometric_prior(const float* current_state, const float* 
 lwm_status lwm_rotor_plant_step(const lwm_domain* domain, float* state, float* motors,
                                 const float* commanded_forces, float dt);
 
+/* ---------------------------------------------------------------- checkpoints */
+
+/* Trained weights from safetensors files (the format candle's
+ * VarBuilder::from_mmaped_safetensors reads, src/checkpoint.rs:6-17), looked
+ * up by their VarBuilder names and written into the weight blob order above.
+ * F32, F64, F16 and BF16 tensors are converted to f32 (the sessions build
+ * their VarBuilders in F32).  Errors: LWM_INVALID_ARGUMENT with
+ * "cannot find tensor <name>" for a missing tensor, "shape mismatch for
+ * <name>, expected [..], got [..]", or the file/header problem. */
+typedef struct lwm_tensor_info {
+    char name[160];      /* VarBuilder path, e.g. "predictor.weight_hh_l0" */
+    uint32_t rank;
+    uint32_t shape[4];
+    size_t offset;       /* first element in the weight blob */
+    size_t numel;
+    int32_t file;        /* SkyJEPA: 0 latent model file, 1 prober file; LeWM: 0 */
+} lwm_tensor_info;
+
+/* Naming of a LeWM-family checkpoint: LeWm (src/models/lewm/model.rs:20-31:
+ * encoder.*, projector.*, predictor.*, action_encoder.*, pred_proj.*; ViT
+ * encoders only) or WorldModel (src/models/world_model/model.rs:19-33,
+ * 166-180: observation_encoder.{encoder,projector,vector_mlp}.*). */
+typedef enum lwm_lewm_names {
+    LWM_LEWM_NAMES_LEWM = 0,
+    LWM_LEWM_NAMES_WORLD_MODEL = 1,
+} lwm_lewm_names;
+
+/* The tensors of the blob in order: returns their count (0 for an invalid
+ * configuration) and fills *out for index < count. */
+size_t lwm_skyjepa_tensor_info(const lwm_skyjepa_config* cfg, size_t index, lwm_tensor_info* out);
+size_t lwm_lewm_tensor_info(const lwm_lewm_config* cfg, int32_t names, size_t index, lwm_tensor_info* out);
+
+/* SkyJEPA: the latent model (SkyJepaModel::new, src/models/skyjepa/model.rs:
+ * 22-39) from latent_path, the prober (SkyJepaProber::new, prober.rs:54-80)
+ * from prober_path, as SkyJepaSession::open loads them
+ * (src/models/skyjepa/session.rs:183-199). */
+lwm_status lwm_skyjepa_weights_from_safetensors(const lwm_skyjepa_config* cfg, const char* latent_path,
+                                                const char* prober_path, float* out, size_t count);
+/* LeWm / WorldModel weights from one safetensors file. */
+lwm_status lwm_lewm_weights_from_safetensors(const lwm_lewm_config* cfg, int32_t names, const char* path,
+                                             float* out, size_t count);
+
 #ifdef __cplusplus
 }
 #endif

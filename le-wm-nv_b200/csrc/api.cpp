@@ -21,6 +21,7 @@
 
 #include "../../include/lewm_b200.h"
 #include "lwm_kernels.hpp"
+#include "lwm_host.hpp"
 #include "lwm_lewm.hpp"
 
 using lwm::MppiArgs;

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <string>
 
+#include "lwm_host.hpp"
 #include "lwm_lewm.hpp"
 
 namespace lwm {
@@ -25,99 +26,121 @@ struct Walker {
     const float* base;
     size_t off = 0;
     std::vector<Spec>* specs;
-    const float* take(size_t n, int kind, uint32_t fan) {
+    std::vector<NamedTensor>* named = nullptr;  // VarBuilder path and shape of each tensor
+    const float* take(size_t n, int kind, uint32_t fan, const std::string& name, std::vector<uint32_t> shape) {
         if (specs) specs->push_back({off, n, kind, fan});
+        if (named) named->push_back({name, std::move(shape), off, n, 0});
         const float* p = base ? base + off : nullptr;
         off += n;
         return p;
     }
-    Lin lin(uint32_t out, uint32_t in, bool bias) {
+    // Linear (or convolution, with its weight shape given) at VarBuilder path `name`.
+    Lin lin(uint32_t out, uint32_t in, bool bias, const std::string& name, std::vector<uint32_t> wshape = {}) {
         Lin l;
         l.out = out;
         l.in = in;
-        l.w = take(static_cast<size_t>(out) * in, 0, in);
-        l.b = bias ? take(out, 1, in) : nullptr;
+        if (wshape.empty()) wshape = {out, in};
+        l.w = take(static_cast<size_t>(out) * in, 0, in, name + ".weight", std::move(wshape));
+        l.b = bias ? take(out, 1, in, name + ".bias", {out}) : nullptr;
         return l;
     }
-    Norm norm(int kind, uint32_t d) {
+    Norm norm(int kind, uint32_t d, const std::string& name) {
         Norm n;
         n.kind = kind;
         if (kind == kNormBatch) {
-            n.w = take(d, 2, 0);
-            n.b = take(d, 3, 0);
-            n.rm = take(d, 3, 0);
-            n.rv = take(d, 2, 0);
+            n.w = take(d, 2, 0, name + ".weight", {d});
+            n.b = take(d, 3, 0, name + ".bias", {d});
+            n.rm = take(d, 3, 0, name + ".running_mean", {d});
+            n.rv = take(d, 2, 0, name + ".running_var", {d});
         } else if (kind == kNormLayer) {
-            n.w = take(d, 2, 0);
-            n.b = take(d, 3, 0);
+            n.w = take(d, 2, 0, name + ".weight", {d});
+            n.b = take(d, 3, 0, name + ".bias", {d});
         }
         return n;
     }
-    MlpW mlp(uint32_t in, uint32_t hid, uint32_t out, int norm_kind) {
+    // Mlp (modules.rs:90-101): net.0 Linear, net.1 norm, net.3 Linear.
+    MlpW mlp(uint32_t in, uint32_t hid, uint32_t out, int norm_kind, const std::string& name) {
         MlpW m;
-        m.fc1 = lin(hid, in, true);
-        m.norm = norm(norm_kind, hid);
-        m.fc2 = lin(out, hid, true);
+        m.fc1 = lin(hid, in, true, name + ".net.0");
+        m.norm = norm(norm_kind, hid, name + ".net.1");
+        m.fc2 = lin(out, hid, true, name + ".net.3");
         return m;
     }
 };
 
-size_t walk(const lwm_lewm_config& c, const float* base, LewmWeights* out, std::vector<Spec>* specs) {
+// Walks the blob in its documented order.  `names` picks the checkpoint
+// naming of the observation encoder (LeWm: encoder / projector; WorldModel:
+// observation_encoder.{encoder, projector, vector_mlp}).
+size_t walk(const lwm_lewm_config& c, const float* base, LewmWeights* out, std::vector<Spec>* specs,
+            std::vector<NamedTensor>* named = nullptr, int names = LWM_LEWM_NAMES_WORLD_MODEL) {
     LewmWeights w;
-    Walker k{base, 0, specs};
+    Walker k{base, 0, specs, named};
     const uint32_t D = c.embed_dim, hid = c.pred_hidden_dim, inner = c.heads * c.dim_head;
-    w.act_conv = k.lin(c.smoothed_dim, c.action_dim, true);
-    w.act_fc1 = k.lin(c.action_mlp_scale * D, c.smoothed_dim, true);
-    w.act_fc2 = k.lin(D, c.action_mlp_scale * D, true);
-    w.pos = k.take(static_cast<size_t>(c.num_frames) * D, 4, 0);
+    // ActionEmbedder (modules.rs:120-145): Conv1d(A -> smoothed, k=1), embed.0, embed.2
+    w.act_conv = k.lin(c.smoothed_dim, c.action_dim, true, "action_encoder.patch_embed", {c.smoothed_dim, c.action_dim, 1});
+    w.act_fc1 = k.lin(c.action_mlp_scale * D, c.smoothed_dim, true, "action_encoder.embed.0");
+    w.act_fc2 = k.lin(D, c.action_mlp_scale * D, true, "action_encoder.embed.2");
+    // Predictor (modules.rs:360-372) and its Transformer (modules.rs:305-330)
+    w.pos = k.take(static_cast<size_t>(c.num_frames) * D, 4, 0, "predictor.pos_embedding", {1, c.num_frames, D});
+    const std::string tr = "predictor.transformer";
     w.has_proj = hid != D;
     if (w.has_proj) {
-        w.input_proj = k.lin(hid, D, true);
-        w.cond_proj = k.lin(hid, D, true);
+        w.input_proj = k.lin(hid, D, true, tr + ".input_proj");
+        w.cond_proj = k.lin(hid, D, true, tr + ".cond_proj");
     }
     w.blocks.resize(c.depth);
     for (uint32_t l = 0; l < c.depth; ++l) {
+        // ConditionalBlock (modules.rs:275-290): attn, mlp, adaLN_modulation.1
+        const std::string p = tr + ".layers." + std::to_string(l);
         BlockW& b = w.blocks[l];
-        b.attn_norm = k.norm(kNormLayer, hid);
-        b.qkv = k.lin(3 * inner, hid, false);
-        b.to_out = k.lin(hid, inner, true);
-        b.mlp_norm = k.norm(kNormLayer, hid);
-        b.fc1 = k.lin(c.mlp_dim, hid, true);
-        b.fc2 = k.lin(hid, c.mlp_dim, true);
-        b.ada = k.lin(6 * hid, hid, true);
+        b.attn_norm = k.norm(kNormLayer, hid, p + ".attn.norm");
+        b.qkv = k.lin(3 * inner, hid, false, p + ".attn.to_qkv");
+        b.to_out = k.lin(hid, inner, true, p + ".attn.to_out.0");
+        b.mlp_norm = k.norm(kNormLayer, hid, p + ".mlp.net.0");
+        b.fc1 = k.lin(c.mlp_dim, hid, true, p + ".mlp.net.1");
+        b.fc2 = k.lin(hid, c.mlp_dim, true, p + ".mlp.net.4");
+        b.ada = k.lin(6 * hid, hid, true, p + ".adaLN_modulation.1");
     }
-    w.final_norm = k.norm(kNormLayer, hid);
-    if (w.has_proj) w.output_proj = k.lin(D, hid, true);
-    w.pred_proj = k.mlp(D, c.pred_proj_hidden, D, c.pred_proj_norm);
+    w.final_norm = k.norm(kNormLayer, hid, tr + ".norm");
+    if (w.has_proj) w.output_proj = k.lin(D, hid, true, tr + ".output_proj");
+    w.pred_proj = k.mlp(D, c.pred_proj_hidden, D, c.pred_proj_norm, "pred_proj");
+    const bool lewm = names == LWM_LEWM_NAMES_LEWM;
     if (c.encoder == LWM_ENCODER_VECTOR_MLP) {
+        // VectorMlpEncoder (world_model/model.rs:215-250): layers.{j}, norms.{j}
+        const std::string p = "observation_encoder.vector_mlp";
         const int nk = c.obs_norm == LWM_NORM_NONE ? kNormNone : kNormLayer;
         w.enc_lin.resize(c.obs_depth);
         w.enc_norm.resize(c.obs_depth);
         for (uint32_t j = 0; j < c.obs_depth; ++j) {
             const uint32_t in = j == 0 ? c.obs_dim : c.obs_hidden_dim;
             const uint32_t o = j + 1 == c.obs_depth ? D : c.obs_hidden_dim;
-            w.enc_lin[j] = k.lin(o, in, true);
-            if (j + 1 < c.obs_depth) w.enc_norm[j] = k.norm(nk, c.obs_hidden_dim);
+            w.enc_lin[j] = k.lin(o, in, true, p + ".layers." + std::to_string(j));
+            if (j + 1 < c.obs_depth) w.enc_norm[j] = k.norm(nk, c.obs_hidden_dim, p + ".norms." + std::to_string(j));
         }
     } else {
+        // HfVitEncoder (vit.rs:30-45) with the Hugging Face ViT paths
+        const std::string e = lewm ? "encoder" : "observation_encoder.encoder";
         const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p;
-        w.cls = k.take(vh, 4, 0);
-        w.vpos = k.take(static_cast<size_t>(side * side + 1) * vh, 4, 0);
-        w.patch = k.lin(vh, c.channels * p * p, true);
+        w.cls = k.take(vh, 4, 0, e + ".embeddings.cls_token", {1, 1, vh});
+        w.vpos = k.take(static_cast<size_t>(side * side + 1) * vh, 4, 0, e + ".embeddings.position_embeddings",
+                        {1, side * side + 1, vh});
+        w.patch = k.lin(vh, c.channels * p * p, true, e + ".embeddings.patch_embeddings.projection",
+                        {vh, c.channels, p, p});
         w.vit.resize(c.vit_layers);
         for (uint32_t l = 0; l < c.vit_layers; ++l) {
+            const std::string q = e + ".encoder.layer." + std::to_string(l);
             VitBlockW& b = w.vit[l];
-            b.ln1 = k.norm(kNormLayer, vh);
-            b.q = k.lin(vh, vh, c.qkv_bias != 0);
-            b.k = k.lin(vh, vh, c.qkv_bias != 0);
-            b.v = k.lin(vh, vh, c.qkv_bias != 0);
-            b.o = k.lin(vh, vh, true);
-            b.ln2 = k.norm(kNormLayer, vh);
-            b.fc1 = k.lin(c.vit_mlp, vh, true);
-            b.fc2 = k.lin(vh, c.vit_mlp, true);
+            b.ln1 = k.norm(kNormLayer, vh, q + ".layernorm_before");
+            b.q = k.lin(vh, vh, c.qkv_bias != 0, q + ".attention.attention.query");
+            b.k = k.lin(vh, vh, c.qkv_bias != 0, q + ".attention.attention.key");
+            b.v = k.lin(vh, vh, c.qkv_bias != 0, q + ".attention.attention.value");
+            b.o = k.lin(vh, vh, true, q + ".attention.output.dense");
+            b.ln2 = k.norm(kNormLayer, vh, q + ".layernorm_after");
+            b.fc1 = k.lin(c.vit_mlp, vh, true, q + ".intermediate.dense");
+            b.fc2 = k.lin(vh, c.vit_mlp, true, q + ".output.dense");
         }
-        w.vit_norm = k.norm(kNormLayer, vh);
-        w.projector = k.mlp(vh, c.projector_hidden, D, c.projector_norm);
+        w.vit_norm = k.norm(kNormLayer, vh, e + ".layernorm");
+        w.projector = k.mlp(vh, c.projector_hidden, D, c.projector_norm, lewm ? "projector" : "observation_encoder.projector");
     }
     w.count = k.off;
     if (out) *out = w;
@@ -141,6 +164,12 @@ struct Mix {
 }  // namespace
 
 size_t lewm_walk(const lwm_lewm_config& c, const float* base, LewmWeights* out) { return walk(c, base, out, nullptr); }
+
+size_t lewm_named_tensors(const lwm_lewm_config& c, int names, std::vector<NamedTensor>* out) {
+    const char* why = nullptr;
+    if (!lewm_config_valid(c, &why)) return 0;
+    return walk(c, nullptr, nullptr, nullptr, out, names);
+}
 
 bool lewm_config_valid(const lwm_lewm_config& c, const char** why) {
     auto bad = [&](const char* m) { *why = m; return false; };

@@ -16,7 +16,7 @@ import ctypes as C
 import os
 import weakref
 from dataclasses import dataclass
-from typing import Callable, List, Optional, Sequence
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -165,6 +165,25 @@ class SkyJepaConfig(C.Structure):
         _check(lib.lwm_skyjepa_random_weights(C.byref(self), U64(seed), _fp(out), C.c_size_t(n)))
         return out
 
+    def tensors(self) -> List["TensorInfo"]:
+        """The weight blob's tensors in order, with their VarBuilder names."""
+        n = int(lib.lwm_skyjepa_tensor_info(C.byref(self), 0, None))
+        out = []
+        for i in range(n):
+            t = _TensorInfo()
+            lib.lwm_skyjepa_tensor_info(C.byref(self), i, C.byref(t))
+            out.append(t.info())
+        return out
+
+    def weights_from_safetensors(self, latent_path: str, prober_path: str) -> np.ndarray:
+        """The latent model and the prober from their safetensors files
+        (SkyJepaSession::open, src/models/skyjepa/session.rs:183-199)."""
+        n = self.weight_count()
+        out = np.empty(n, dtype=np.float32)
+        _check(lib.lwm_skyjepa_weights_from_safetensors(C.byref(self), os.fsencode(latent_path),
+                                                        os.fsencode(prober_path), _fp(out), C.c_size_t(n)))
+        return out
+
 
 class LewmConfig(C.Structure):
     """LeWmConfig / WorldModelConfig (src/models/lewm/config.rs, src/models/world_model/config.rs)."""
@@ -198,6 +217,46 @@ class LewmConfig(C.Structure):
         out = np.empty(n, dtype=np.float32)
         _check(lib.lwm_lewm_random_weights(C.byref(self), U64(seed), _fp(out), C.c_size_t(n)))
         return out
+
+    def tensors(self, names: str = "world_model") -> List["TensorInfo"]:
+        """The weight blob's tensors in order, named as a LeWm ("lewm") or
+        WorldModel ("world_model") checkpoint names them."""
+        k = LEWM_NAMES[names]
+        n = int(lib.lwm_lewm_tensor_info(C.byref(self), k, 0, None))
+        out = []
+        for i in range(n):
+            t = _TensorInfo()
+            lib.lwm_lewm_tensor_info(C.byref(self), k, i, C.byref(t))
+            out.append(t.info())
+        return out
+
+    def weights_from_safetensors(self, path: str, names: str = "world_model") -> np.ndarray:
+        n = self.weight_count()
+        out = np.empty(n, dtype=np.float32)
+        _check(lib.lwm_lewm_weights_from_safetensors(C.byref(self), LEWM_NAMES[names], os.fsencode(path), _fp(out),
+                                                     C.c_size_t(n)))
+        return out
+
+
+LEWM_NAMES = {"lewm": 0, "world_model": 1}
+
+
+@dataclass(frozen=True)
+class TensorInfo:
+    name: str
+    shape: Tuple[int, ...]
+    offset: int
+    numel: int
+    file: int
+
+
+class _TensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char * 160), ("rank", U32), ("shape", U32 * 4), ("offset", C.c_size_t),
+                ("numel", C.c_size_t), ("file", I32)]
+
+    def info(self) -> TensorInfo:
+        return TensorInfo(self.name.decode(), tuple(int(self.shape[i]) for i in range(self.rank)), int(self.offset),
+                          int(self.numel), int(self.file))
 
 
 NORM_KINDS = {"batch": 0, "layer": 1, "none": 2}
@@ -287,6 +346,11 @@ _sig("lwm_icem_trace_device", C.c_int, VP, VP, VP, C.POINTER(_PlanDeviceResult),
 _sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
 _sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
+_sig("lwm_skyjepa_tensor_info", C.c_size_t, C.POINTER(SkyJepaConfig), C.c_size_t, C.POINTER(_TensorInfo))
+_sig("lwm_lewm_tensor_info", C.c_size_t, C.POINTER(LewmConfig), I32, C.c_size_t, C.POINTER(_TensorInfo))
+_sig("lwm_skyjepa_weights_from_safetensors", C.c_int, C.POINTER(SkyJepaConfig), C.c_char_p, C.c_char_p, FP,
+     C.c_size_t)
+_sig("lwm_lewm_weights_from_safetensors", C.c_int, C.POINTER(LewmConfig), I32, C.c_char_p, FP, C.c_size_t)
 _sig("lwm_image_preprocess_imagenet_224", None, C.POINTER(ImagePreprocess))
 _sig("lwm_preprocess_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32, I32,
      VP)
