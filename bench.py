@@ -469,6 +469,7 @@ def run_lewm(args, rank, world, local_rank):
     ctx = L.Context(local_rank)
     stream = ctx.torch_stream()
     sc = L.LewmScorer(ctx, w.config, w.weights)
+    sc.set_precision(args.precision)
     planner = (L.MppiPlanner if image else L.CemPlanner)(ctx, w.planner)
     D = w.config.embed_dim
     if image:
@@ -546,9 +547,14 @@ def run_lewm(args, rank, world, local_rank):
         cand_steps = w.samples * w.horizon * iters
         ms = total_ms / args.steps
         plans_per_s = world * 1e3 / ms
-        sgemm = sgemm_peak_tflops(torch)
         flop = lewm_flop_per_candidate_step(w.config) * cand_steps
         achieved = flop / (percentile(times, 0.5) * 1e-3) / 1e12
+        if args.precision == "bf16":
+            peak = float(measured_peaks().get("bf16_tflops", 1590.0))
+            roof = {"bound": "tensor", "peak_source": "MEASURED_PEAKS bf16_tflops burst (of measured)"}
+        else:
+            peak = sgemm_peak_tflops(torch)
+            roof = {"bound": "fp32", "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run"}
         name = ("LeWM image MPPI: NV12 224x224 obs + goal -> preprocess -> ViT-Tiny (patch 16, 12 x 192) -> "
                 "projector; predictor depth 6, 16 x 64 heads, MLP 2048; 1024 candidates x 10 steps, lambda 0.5"
                 if image else
@@ -559,18 +565,20 @@ def run_lewm(args, rank, world, local_rank):
                       "and p50/p95 plan latency alongside",
             "value": round(plans_per_s, 3), "unit": "plans/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32",
+            "vs_baseline": None, "dtype": args.precision,
             "data": "synthetic (seeded random-init weights, seeded observations / NV12 noise frames)",
             "config": {"workload": name, "parallelism": f"replicas x{world}",
+                       "gemms": ("bf16 weights and inputs on tcgen05 tensor cores, f32 accumulation and activations"
+                                 if args.precision == "bf16" else "f32 CUDA cores"),
                        "l2": "flushed between steps (256 MiB write outside the timed region)"},
             "candidate_steps_per_s": round(plans_per_s * cand_steps, 1),
             "latency_ms": {"p50": round(percentile(times, 0.5), 4), "p95": round(percentile(times, 0.95), 4)},
             "e2e": {"value": round(world * 1e3 / e2e_mean, 3), "unit": "plans/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(seq.numel() * 4)},
             "gpu_launches": int(launches * args.steps),
-            "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2), "unit": "TFLOP/s",
-                         "frac": round(achieved / sgemm, 4), "traffic": None,
-                         "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
+            "roofline": {"bound": roof["bound"], "achieved": round(achieved, 3), "peak": round(peak, 2),
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": roof["peak_source"],
                          "note": "achieved = predictor FLOP per plan (encoders excluded) / p50 plan time"},
             "clocks": clocks.summary(),
         }
@@ -728,12 +736,15 @@ def main():
     ap.add_argument("--vehicles", type=int, default=256)
     ap.add_argument("--samples", type=int, default=4096)
     ap.add_argument("--horizon", type=int, default=30)
-    ap.add_argument("--precision", choices=["f32", "bf16"], default="bf16",
-                    help="fleet workload: bf16 weights on the tensor cores (default) or the f32 rollout")
+    ap.add_argument("--precision", choices=["f32", "bf16"], default=None,
+                    help="fleet and lewm-image: bf16 weights on the tensor cores (their default) or f32; "
+                         "lewm-vector: f32 (default) or bf16")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.precision is None:  # the precision each workload's configuration names
+        args.precision = "bf16" if args.workload in ("fleet", "lewm-image") else "f32"
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -315,6 +315,13 @@ typedef enum lwm_precision {
     LWM_PRECISION_BF16 = 1,
 } lwm_precision;
 lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* scorer, int32_t precision);
+/* Precision of the LeWM scorer's GEMMs (predictor, action embedder, pred_proj,
+ * encoders).  LWM_PRECISION_F32 (default): f32 CUDA-core GEMMs.
+ * LWM_PRECISION_BF16: bf16 weights (converted once) and bf16-rounded GEMM
+ * inputs on the tcgen05 tensor cores with f32 accumulation; the residual
+ * stream, norms, attention and the goal cost stay f32.  GEMMs whose K is not
+ * a multiple of 16 (the action embedder's input) stay f32. */
+lwm_status lwm_scorer_lewm_set_precision(lwm_scorer* scorer, int32_t precision);
 
 /* A scorer supplied by the caller: the CandidateScorer trait
  * (src/planner.rs:25-32).  The callback receives device pointers on the

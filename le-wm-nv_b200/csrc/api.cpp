@@ -1333,6 +1333,17 @@ lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* s, int32_t precision) {
     return LWM_OK;
 }
 
+lwm_status lwm_scorer_lewm_set_precision(lwm_scorer* s, int32_t precision) {
+    if (!s || s->kind != ScorerKind::Lewm) return fail(LWM_INVALID_ARGUMENT, "not a LeWM scorer");
+    if (precision != LWM_PRECISION_F32 && precision != LWM_PRECISION_BF16)
+        return fail(LWM_INVALID_ARGUMENT, "unknown precision " + std::to_string(precision));
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    LWM_CUDA(s->lewm->set_precision(precision, s->ctx->stream));
+    s->precision = precision;
+    return LWM_OK;
+}
+
 lwm_status lwm_scorer_callback_create(lwm_ctx* ctx, uint32_t batch, lwm_score_fn fn, void* user, lwm_scorer** out) {
     if (!ctx || !fn || !out || batch == 0) return fail(LWM_INVALID_ARGUMENT, "invalid callback scorer arguments");
     lwm_scorer* s = new_scorer(ctx, ScorerKind::Callback);
@@ -1505,8 +1516,11 @@ lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_p
     }
     if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
     int tc_err[4] = {0, 0, 0, 0};
-    if (sc->tc_err.ptr) LWM_CUDA(cudaMemcpyAsync(tc_err, sc->tc_err.ptr, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
+    int* err_dev = sc->tc_err.ptr ? sc->tc_err.as<int>()
+                   : (sc->kind == ScorerKind::Lewm ? sc->lewm->split.tc_err : nullptr);
+    if (err_dev) LWM_CUDA(cudaMemcpyAsync(tc_err, err_dev, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
     LWM_CUDA(cudaStreamSynchronize(stream));
+    if (tc_err[0] && sc->kind == ScorerKind::Lewm) LWM_CUDA(cudaMemset(err_dev, 0, sizeof tc_err));
     if (tc_err[0])
         return fail(LWM_TIMEOUT, "a tensor-core pipeline wait timed out on the device (site " + std::to_string(tc_err[0]) +
                                      ", block " + std::to_string(tc_err[1]) + ", index " + std::to_string(tc_err[2]) +

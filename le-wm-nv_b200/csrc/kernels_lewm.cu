@@ -21,6 +21,7 @@
 
 #include "lwm_device.cuh"
 #include "lwm_lewm.hpp"
+#include "lwm_lewm_epi.cuh"
 
 namespace lwm {
 
@@ -33,25 +34,6 @@ namespace lwm {
 // so its global-load latency overlaps the FMAs.  Each output's dot product
 // runs in k order (as the reference's matmul).
 constexpr int kBM = 64, kBN = 64, kBK = 32;
-
-__device__ __forceinline__ float apply_act(int act, float v) {
-    switch (act) {
-        case kActGeluTanh: return gelu_tanh(v);
-        case kActGeluErf: return (0.5f * v) * (1.0f + erff(v * 0.7071067811865476f));
-        case kActSilu: return v / (1.0f + expf(-v));
-        default: return v;
-    }
-}
-
-__device__ __forceinline__ float epilogue_value(const GemmArgs& g, uint32_t m, uint32_t n, float v, float* c) {
-    if (g.bias) v = v + g.bias[n];
-    if (g.residual) {
-        // x = x + gate * y (ConditionalBlock) or x = y + x (ViT layer)
-        if (g.gate) v = g.gate[g.map.row(m) * g.ldg + n] * v;
-        return *c + v;
-    }
-    return apply_act(g.act, v);
-}
 
 __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
     __shared__ __align__(16) float As[2][kBK][kBM + 4];
@@ -159,6 +141,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
 // waves of CTAs, at least 64 K per split, at most 16 splits.
 cudaError_t gemm_f32(const GemmArgs& in, cudaStream_t stream, const SplitScratch* sp) {
     if (in.M == 0 || in.N == 0) return cudaSuccess;
+    if (sp && sp->tc_err && gemm_tc_eligible(in)) return gemm_tc(in, stream, sp, sp->tc_err);
     GemmArgs g = in;
     const uint32_t tx = (g.N + kBN - 1) / kBN, ty = (g.M + kBM - 1) / kBM;
     const size_t tiles = static_cast<size_t>(tx) * ty;

@@ -1,0 +1,259 @@
+// kernels_lewm_tc.cu — bf16 tensor-core GEMM of the LeWM scorer (tcgen05).
+//
+// C[M,N] = A[M,K] . W[N,K]^T with the scorer's fused epilogue (bias, GELU /
+// SiLU, gated residual), for the bf16 predictor / encoder of the LeWM image
+// workload.  One 128 x 128 output tile per CTA (N tiles narrower at the
+// edge), K in 64-element blocks through two shared-memory stages:
+//   A  f32 activations from HBM/L2, rounded to bf16 by the loading threads
+//      and stored in the SW128 K-major layout (the residual stream and every
+//      other activation stay f32);
+//   W  bf16 weights [N, K] (converted once per scorer), 16-byte cp.async
+//      copies into the same layout;
+//   one thread issues tcgen05.mma (M 128, N <= 128, K 16) into a TMEM
+//   accumulator and commits each stage to an mbarrier that releases it; the
+//   next block's loads run while the tensor core works on this one.
+// The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
+// 32 (w % 4) .. +31 = rows, w / 4 picks the column half).  Split-K parks f32
+// partial tiles and the last CTA of a tile adds them in split order, as the
+// f32 GEMM does.  Every mbarrier wait is bounded and reports through err.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "lwm_lewm.hpp"
+#include "lwm_lewm_epi.cuh"
+#include "lwm_tc.cuh"
+
+namespace lwm {
+namespace {
+
+constexpr uint32_t kTM = 128, kTN = 128, kTK = 64;
+constexpr uint32_t kStageA = kTM * kTK * 2, kStageB = kTN * kTK * 2;  // 16 KB each
+constexpr uint32_t kTcSmem = 2 * (kStageA + kStageB) + 1024 + 64;
+constexpr int kSiteStage = 21, kSiteFinal = 22;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;                    // [2][128 rows x 128 B]
+    uint8_t* sB = smem + 2 * kStageA;      // [2][128 rows x 128 B]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * (kStageA + kStageB));  // stage[2], final
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+    const uint32_t n_tile = min(kTN, g.N - n0), n_mma = (n_tile + 15u) & ~15u;
+    const uint32_t kb = blockIdx.z * g.k_chunk, ke = min(g.K, kb + g.k_chunk);
+    const uint32_t nblk = (ke - kb + kTK - 1) / kTK;
+    if (tid == 0) {
+        tc::mbar_init(&bars[0], 1);
+        tc::mbar_init(&bars[1], 1);
+        tc::mbar_init(&bars[2], 1);
+        tc::mbar_fence_init();
+    }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 128);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // A: 128 rows x 64 k f32 = 2048 float4, 8 per thread; lanes of a warp read
+    // two rows' 256 contiguous bytes each.
+    float4 ra[8];
+    auto load_a = [&](uint32_t k0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t e = static_cast<uint32_t>(i) * 256u + tid;
+            const uint32_t row = e >> 4, kq = (e & 15u) * 4u;
+            const uint32_t m = m0 + row, k = k0 + kq;
+            ra[i] = (m < g.M && k < ke) ? __ldg(reinterpret_cast<const float4*>(g.A + static_cast<size_t>(m) * g.lda + k))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_a = [&](uint32_t s) {
+        uint8_t* base = sA + s * kStageA;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t e = static_cast<uint32_t>(i) * 256u + tid;
+            const uint32_t row = e >> 4, kq = (e & 15u) * 4u;
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(ra[i].x, ra[i].y);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(ra[i].z, ra[i].w);
+            uint2 v;
+            v.x = *reinterpret_cast<const uint32_t*>(&lo);
+            v.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(base + tc::sw128_offset(row, kq)) = v;
+        }
+    };
+    // W: 128 rows x 8 chunks of 16 B, 4 per thread; rows past N read nothing
+    // (zero-filled).
+    auto load_b = [&](uint32_t s, uint32_t k0) {
+        const uint32_t base = tc::smem_u32(sB + s * kStageB);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t c = static_cast<uint32_t>(i) * 256u + tid;
+            const uint32_t row = c >> 3, j = c & 7u;
+            const uint32_t n = n0 + row, k = k0 + j * 8u;
+            const bool ok = n < g.N && k < ke;
+            const uint16_t* src = ok ? g.Wb + static_cast<size_t>(n) * g.ldw + k : g.Wb;
+            cp_async16(base + tc::sw128_offset(row, j * 8u), src, ok ? 16u : 0u);
+        }
+    };
+
+    load_a(kb);
+    load_b(0, kb);
+    store_a(0);
+    cp_async_wait_all();
+    tc::fence_async_smem();
+    __syncthreads();
+    const uint32_t idesc = tc::idesc_bf16_f32(kTM, n_mma);
+    for (uint32_t i = 0; i < nblk; ++i) {
+        const uint32_t s = i & 1u, k0 = kb + i * kTK;
+        if (tid == 0) {
+            tc::fence_after();
+            const uint32_t a0 = tc::smem_u32(sA + s * kStageA), b0 = tc::smem_u32(sB + s * kStageB);
+            const uint32_t steps = min(4u, (ke - k0) / 16u);
+            for (uint32_t j = 0; j < steps; ++j)
+                tc::mma_bf16(tmem, tc::smem_desc(a0 + j * 32u, 16, 1024, tc::kSwizzle128),
+                             tc::smem_desc(b0 + j * 32u, 16, 1024, tc::kSwizzle128), idesc, (i | j) != 0u);
+            tc::commit(&bars[s]);
+        }
+        if (i + 1 < nblk) {
+            const uint32_t s2 = s ^ 1u, k1 = k0 + kTK;
+            load_a(k1);  // global loads in flight while the MMAs run
+            if (i >= 1) tc::mbar_wait(&bars[s2], ((i - 1) >> 1) & 1u, err, kSiteStage, static_cast<int>(i));
+            load_b(s2, k1);
+            store_a(s2);
+            cp_async_wait_all();
+            tc::fence_async_smem();
+            __syncthreads();
+        }
+    }
+    if (tid == 0) tc::commit(&bars[2]);
+    tc::mbar_wait(&bars[2], 0, err, kSiteFinal, static_cast<int>(nblk));
+    tc::fence_after();
+
+    const uint32_t q = warp & 3u, half = warp >> 2;
+    const uint32_t row = q * 32u + lane, m = m0 + row;
+    const uint32_t lane_addr = tmem + ((q * 32u) << 16);
+    if (g.splits <= 1) {
+#pragma unroll 1
+        for (uint32_t c = 0; c < 4; ++c) {
+            const uint32_t col0 = half * 64u + c * 16u;
+            if (col0 >= n_tile) break;
+            float v[16];
+            tc::tmem_ld16(lane_addr + col0, v);
+            tc::tmem_ld_wait();
+            if (m < g.M) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const uint32_t n = n0 + col0 + static_cast<uint32_t>(e);
+                    if (n < g.N) {
+                        float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
+                        *cp = epilogue_value(g, m, n, v[e], cp);
+                    }
+                }
+            }
+        }
+    } else {
+        const size_t tile = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+        float* mine = g.partial + (tile * g.splits + blockIdx.z) * (kTM * kTN);
+#pragma unroll 1
+        for (uint32_t c = 0; c < 4; ++c) {
+            const uint32_t col0 = half * 64u + c * 16u;
+            if (col0 >= n_tile) break;
+            float v[16];
+            tc::tmem_ld16(lane_addr + col0, v);
+            tc::tmem_ld_wait();
+            float4* dst = reinterpret_cast<float4*>(mine + row * kTN + col0);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_free(tmem, 128);
+    if (g.splits <= 1) return;
+
+    // split-K: the last split of the tile to arrive adds the partial tiles in
+    // split order (deterministic) and runs the epilogue
+    __threadfence();
+    __shared__ int s_last;
+    const size_t tile = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+    if (tid == 0) s_last = atomicAdd(&g.counters[tile], 1u) == g.splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* parts = g.partial + tile * g.splits * (kTM * kTN);
+    for (uint32_t idx = tid; idx < kTM * kTN; idx += 256u) {
+        const uint32_t r = idx / kTN, col = idx % kTN;
+        const uint32_t mm = m0 + r, n = n0 + col;
+        if (mm >= g.M || col >= n_tile) continue;
+        float v = 0.0f;
+        for (uint32_t z = 0; z < g.splits; ++z) v += __ldcg(parts + z * (kTM * kTN) + idx);
+        float* cp = g.C + static_cast<size_t>(mm) * g.ldc + n;
+        *cp = epilogue_value(g, mm, n, v, cp);
+    }
+    if (tid == 0) g.counters[tile] = 0u;
+}
+
+}  // namespace
+
+bool gemm_tc_eligible(const GemmArgs& g) {
+    return g.Wb && g.K >= 16 && g.K % 16 == 0 && g.lda % 4 == 0 && g.ldw % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(g.A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(g.Wb) & 15u) == 0;
+}
+
+// Splits K when the output tiles alone leave SMs idle: about one wave of
+// CTAs, at least two 64-wide K blocks per split, at most 16 splits.
+cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch* sp, int* err) {
+    static bool configured[64] = {};  // the attribute is per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem));
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    GemmArgs g = in;
+    const uint32_t tx = (g.N + kTN - 1) / kTN, ty = (g.M + kTM - 1) / kTM;
+    const size_t tiles = static_cast<size_t>(tx) * ty;
+    uint32_t splits = 1;
+    if (sp && sp->partial && tiles < 148 && g.K >= 2 * 2 * kTK) {
+        splits = static_cast<uint32_t>((148 + tiles - 1) / tiles);
+        splits = min(splits, min(16u, g.K / (2 * kTK)));
+        while (splits > 1 && tiles * splits * kTM * kTN > sp->floats) --splits;
+        if (tiles > sp->n_counters) splits = 1;
+    }
+    g.splits = splits;
+    g.k_chunk = splits > 1 ? ((g.K + splits - 1) / splits + kTK - 1) / kTK * kTK : g.K;
+    if (splits > 1) {
+        g.splits = (g.K + g.k_chunk - 1) / g.k_chunk;  // no empty split
+        g.partial = sp->partial;
+        g.counters = sp->counters;
+    }
+    dim3 grid(tx, ty, g.splits);
+    gemm_tc_kernel<<<grid, 256, kTcSmem, stream>>>(g, err);
+    return cudaGetLastError();
+}
+
+__global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, size_t n) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 148 * 8));
+    f32_to_bf16_kernel<<<blocks, 256, 0, s>>>(src, reinterpret_cast<__nv_bfloat16*>(dst), n);
+    return cudaGetLastError();
+}
+
+}  // namespace lwm

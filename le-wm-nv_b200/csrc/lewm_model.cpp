@@ -5,6 +5,7 @@
 // Reference: LeWm / WorldModel (src/models/lewm/model.rs:20-165,
 // src/models/world_model/model.rs:19-160), LeWmSession::score_candidates
 // (src/session.rs:46-66), modules.rs:9-399, vit.rs:7-57.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -213,6 +214,8 @@ void Arena::release() {
 LewmModel::~LewmModel() {
     g_score.reset();
     g_enc.reset();
+    if (blob_bf16) cudaFree(blob_bf16);
+    if (split.tc_err) cudaFree(split.tc_err);
     if (split.partial) cudaFree(split.partial);
     if (split.counters) cudaFree(split.counters);
     ws.release();
@@ -243,6 +246,7 @@ GemmArgs gemm(const float* A, uint32_t lda, const Lin& l, float* C, uint32_t ldc
     g.K = l.in;
     g.lda = lda;
     g.ldw = l.in;
+    g.Wb = l.wb;
     g.ldc = ldc;
     g.act = act;
     return g;
@@ -474,6 +478,63 @@ cudaError_t LewmModel::ensure_split() {
     LWM_CU(cudaMemset(split.counters, 0, kCounters * sizeof(unsigned int)));
     split.floats = kPartial;
     split.n_counters = kCounters;
+    return cudaSuccess;
+}
+
+namespace {
+
+// Every Linear of the model (the GEMM weights).
+template <class F>
+void for_each_lin(LewmWeights& w, F f) {
+    for (Lin* l : {&w.act_conv, &w.act_fc1, &w.act_fc2, &w.input_proj, &w.cond_proj, &w.output_proj,
+                   &w.pred_proj.fc1, &w.pred_proj.fc2, &w.patch, &w.projector.fc1, &w.projector.fc2})
+        f(*l);
+    for (BlockW& b : w.blocks)
+        for (Lin* l : {&b.qkv, &b.to_out, &b.fc1, &b.fc2, &b.ada}) f(*l);
+    for (Lin& l : w.enc_lin) f(l);
+    for (VitBlockW& b : w.vit)
+        for (Lin* l : {&b.q, &b.k, &b.v, &b.o, &b.fc1, &b.fc2}) f(*l);
+}
+
+}  // namespace
+
+cudaError_t LewmModel::set_precision(int p, cudaStream_t s) {
+    if (p == precision) return cudaSuccess;
+    LWM_CU(cudaStreamSynchronize(s));
+    g_score.reset();  // captured launches hold the old weight pointers
+    g_enc.reset();
+    if (p == LWM_PRECISION_F32) {
+        for_each_lin(w, [](Lin& l) { l.wb = nullptr; });
+        if (blob_bf16) cudaFree(blob_bf16);
+        blob_bf16 = nullptr;
+        if (split.tc_err) cudaFree(split.tc_err);
+        split.tc_err = nullptr;
+        precision = p;
+        return cudaSuccess;
+    }
+    // one bf16 slot per weight matrix, each 256-byte aligned
+    size_t total = 0;
+    for_each_lin(w, [&](Lin& l) {
+        if (l.w) total += (static_cast<size_t>(l.out) * l.in + 127) & ~static_cast<size_t>(127);
+    });
+    LWM_CU(ensure_split());
+    if (!split.tc_err) {
+        LWM_CU(cudaMalloc(&split.tc_err, 4 * sizeof(int)));
+        LWM_CU(cudaMemset(split.tc_err, 0, 4 * sizeof(int)));
+    }
+    LWM_CU(cudaMalloc(&blob_bf16, std::max<size_t>(total, 1) * sizeof(uint16_t)));
+    size_t off = 0;
+    cudaError_t err = cudaSuccess;
+    for_each_lin(w, [&](Lin& l) {
+        if (!l.w || err != cudaSuccess) return;
+        const size_t n = static_cast<size_t>(l.out) * l.in;
+        err = launch_f32_to_bf16(l.w, blob_bf16 + off, n, s);
+        l.wb = blob_bf16 + off;
+        off += (n + 127) & ~static_cast<size_t>(127);
+    });
+    LWM_CU(err);
+    LWM_CU(cudaStreamSynchronize(s));
+    precision = p;
     return cudaSuccess;
 }
 

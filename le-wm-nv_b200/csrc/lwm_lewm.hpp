@@ -35,6 +35,7 @@ struct GemmArgs {
     const float* gate;    // gate table, row map.row(m), stride ldg, or nullptr
     uint32_t ldg;
     RowMap map;
+    const uint16_t* Wb;   // bf16 copy of W (same [N, K] layout, row stride ldw): tensor-core path, or nullptr
     // split-K (set by gemm_f32): partial tiles and per-tile arrival counters
     uint32_t splits, k_chunk;
     float* partial;
@@ -47,11 +48,17 @@ struct SplitScratch {
     size_t floats = 0;
     unsigned int* counters = nullptr;  // zero between GEMMs (the last CTA of a tile resets its counter)
     size_t n_counters = 0;
+    int* tc_err = nullptr;             // error word of the tensor-core GEMM's bounded waits (4 ints)
 };
 
 // Launches C = A W^T (+ epilogue); splits K over CTAs (deterministically) when
-// `split` is given and the output tiles alone would leave most SMs idle.
+// `split` is given and the output tiles alone would leave most SMs idle.  With
+// g.Wb set (and K a multiple of 16, A and Wb 16-byte aligned) the product runs
+// on the tensor cores in bf16 with f32 accumulation (gemm_tc); otherwise f32.
 cudaError_t gemm_f32(const GemmArgs& g, cudaStream_t s, const SplitScratch* split);
+bool gemm_tc_eligible(const GemmArgs& g);
+cudaError_t gemm_tc(const GemmArgs& g, cudaStream_t s, const SplitScratch* split, int* err);
+cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, size_t n, cudaStream_t s);
 cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
                           uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b,
                           cudaStream_t s);
@@ -81,6 +88,7 @@ struct Lin {
     const float* w = nullptr;
     const float* b = nullptr;
     uint32_t out = 0, in = 0;
+    const uint16_t* wb = nullptr;  // bf16 copy of w (bf16 precision only)
 };
 struct Norm {
     int kind = kNormNone;
@@ -145,6 +153,8 @@ struct LewmModel {
     lwm_lewm_config c{};
     LewmWeights w;
     float* blob = nullptr;  // device weights
+    uint16_t* blob_bf16 = nullptr;  // bf16 copies of the GEMM weights, each 256-byte aligned
+    int precision = LWM_PRECISION_F32;
     // per-plan context
     uint32_t B = 0, h = 0, history = 0;
     float* emb = nullptr;   // [B, h, D]
@@ -159,6 +169,9 @@ struct LewmModel {
     cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_pixels_body(const float* pixels, uint32_t n, float* out, cudaStream_t s);
     cudaError_t ensure_split();
+    // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
+    // GEMM inputs on the tensor cores, f32 accumulation and activations.
+    cudaError_t set_precision(int p, cudaStream_t s);
     // scores [B,S] of candidates [B,S,T,A] (all device)
     cudaError_t score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s);

@@ -239,6 +239,7 @@ class LewmConfig(C.Structure):
 
 
 LEWM_NAMES = {"lewm": 0, "world_model": 1}
+PRECISIONS = {"f32": 0, "bf16": 1}
 
 
 @dataclass(frozen=True)
@@ -321,6 +322,7 @@ _sig("lwm_scorer_skyjepa_create", C.c_int, VP, C.POINTER(SkyJepaConfig), FP, C.c
 _sig("lwm_scorer_skyjepa_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP)
 _sig("lwm_scorer_skyjepa_set_context_ex", C.c_int, VP, U32, U32, FP, FP, FP, FP, FP)
 _sig("lwm_scorer_skyjepa_set_precision", C.c_int, VP, I32)
+_sig("lwm_scorer_lewm_set_precision", C.c_int, VP, I32)
 _sig("lwm_scorer_callback_create", C.c_int, VP, U32, SCORE_FN, VP, C.POINTER(VP))
 _sig("lwm_scorer_score_device", C.c_int, VP, VP, U32, U32, U32, U32, VP)
 _sig("lwm_scorer_predict_device", C.c_int, VP, VP, U32, U32, U32, VP)
@@ -692,7 +694,7 @@ class SkyJepaScorer(Scorer):
 
     def set_precision(self, precision: str) -> None:
         """"f32" (CUDA cores) or "bf16" (tcgen05 tensor cores where the shape allows)."""
-        _check(lib.lwm_scorer_skyjepa_set_precision(self.handle, {"f32": 0, "bf16": 1}[precision]))
+        _check(lib.lwm_scorer_skyjepa_set_precision(self.handle, PRECISIONS[precision]))
 
     def set_context(self, state_history, action_history, reference_states, reference_actions,
                     vehicle_mass=None) -> None:
@@ -718,6 +720,11 @@ class LewmScorer(Scorer):
         _check(lib.lwm_scorer_lewm_create(ctx.handle, C.byref(config), _fp(w), C.c_size_t(w.size), C.byref(h)))
         self.handle = h
         _LIVE["scorer"].add(self)
+
+    def set_precision(self, precision: str) -> None:
+        """"f32" (default) or "bf16": the GEMMs on the tcgen05 tensor cores
+        with bf16 weights and inputs, f32 accumulation and activations."""
+        _check(lib.lwm_scorer_lewm_set_precision(self.handle, PRECISIONS[precision]))
 
     def set_context(self, emb_history, goal, history: int = 0) -> None:
         """emb_history [B, h, D] and goal [B, D] host arrays; history 0 = h (the session's window)."""
