@@ -671,6 +671,90 @@ lwm_status lwm_skyjepa_geometric_prior(const float* current_state, const float* 
 lwm_status lwm_rotor_plant_step(const lwm_domain* domain, float* state, float* motors,
                                 const float* commanded_forces, float dt);
 
+/* ---------------------------------------------------------------- control session */
+
+/* SkyJepaControllerSession (src/models/skyjepa/session.rs:110-470): the
+ * closed-loop controller around one vehicle's MPPI planner.  It keeps the
+ * state/action histories, calibrates the trim from the holding action, builds
+ * the geometric prior and the warm start (fresh prior or prior + the shifted,
+ * clamped residual of the previous plan), and plans with the learned or the
+ * nominal-physics scorer.  Per plan: one upload of the context, one upload of
+ * the warm start, one synchronising read of the results. */
+typedef struct lwm_skyjepa_session lwm_skyjepa_session;
+
+typedef enum lwm_warm_start {
+    LWM_WARM_START_FRESH_PRIOR = 0,
+    LWM_WARM_START_SHIFTED_RESIDUAL = 1,
+} lwm_warm_start;
+
+typedef enum lwm_dynamics {
+    LWM_DYNAMICS_LEARNED = 0,         /* SkyJepaDynamics::Trained / Untrained: the given weights */
+    LWM_DYNAMICS_NOMINAL_PHYSICS = 1, /* SkyJepaDynamics::NominalPhysics */
+} lwm_dynamics;
+
+/* SkyJepaSessionConfig (session.rs:40-87) + the control settings the session
+ * derives (SkyJepaControlConfig::paper_derived, control.rs:83-94, with dt =
+ * 1 / model rate). */
+typedef struct lwm_skyjepa_session_config {
+    uint32_t samples;
+    uint32_t horizon;
+    uint64_t planner_seed;
+    int32_t warm_start;       /* lwm_warm_start */
+    float residual_limit_n;
+    int32_t dynamics;         /* lwm_dynamics */
+    float trim_multiplier;
+    float dt;
+    uint32_t iterations;
+    float temperature;
+    float action_noise[LWM_ROTOR_COUNT];
+    lwm_tracking_cost cost;
+} lwm_skyjepa_session_config;
+void lwm_skyjepa_session_config_paper(lwm_skyjepa_session_config* out);
+
+/* SkyJepaControllerPlan (session.rs:89-100).  action_sequence [horizon*4]
+ * and predicted_states [horizon*18] are caller buffers (predicted_states may
+ * be NULL when no prediction is asked for). */
+typedef struct lwm_skyjepa_controller_plan {
+    float action[LWM_ROTOR_COUNT];
+    float prior_action[LWM_ROTOR_COUNT];
+    float action_correction[LWM_ROTOR_COUNT];
+    float* action_sequence;
+    float* predicted_states;
+    float best_candidate_score;
+    double plan_ms;
+    int32_t deadline_reached;
+} lwm_skyjepa_controller_plan;
+
+/* Creates the session and resets it to `initial_state` [18] with the hover
+ * action.  The learned dynamics need the model, its weight blob and the
+ * normalisation; NULLs are accepted for the nominal physics. */
+lwm_status lwm_skyjepa_session_create(lwm_ctx* ctx, const lwm_skyjepa_session_config* cfg,
+                                      const lwm_skyjepa_config* model, const float* weights,
+                                      size_t weight_count, const float* state_mean,
+                                      const float* state_std, const float* action_mean,
+                                      const float* action_std, const float* initial_state,
+                                      lwm_skyjepa_session** out);
+void lwm_skyjepa_session_destroy(lwm_skyjepa_session* session);
+/* reset / reset_with_action (session.rs:241-299). */
+lwm_status lwm_skyjepa_session_reset(lwm_skyjepa_session* session, const float* state);
+lwm_status lwm_skyjepa_session_reset_with_action(lwm_skyjepa_session* session, const float* state,
+                                                 const float* action);
+/* commit_observation (session.rs:301-320): the state reached after `action`. */
+lwm_status lwm_skyjepa_session_commit_observation(lwm_skyjepa_session* session, const float* state,
+                                                  const float* action);
+/* plan / plan_with_prediction (session.rs:322-445): reference_states
+ * [horizon*18]. */
+lwm_status lwm_skyjepa_session_plan(lwm_skyjepa_session* session, const float* reference_states,
+                                    int32_t include_prediction, lwm_skyjepa_controller_plan* out);
+/* The session's scorer (for lwm_scorer_skyjepa_set_precision) and its
+ * calibrated trim scale. */
+lwm_scorer* lwm_skyjepa_session_scorer(lwm_skyjepa_session* session);
+float lwm_skyjepa_session_trim_scale(const lwm_skyjepa_session* session);
+/* shifted_residual (session.rs:534-543): clamp(sequence - prior, +-limit)
+ * shifted one step earlier with a zero last step; [horizon*action_dim]. */
+lwm_status lwm_skyjepa_shifted_residual(const float* sequence, const float* prior, uint32_t horizon,
+                                        uint32_t action_dim, float limit, float* out);
+
 /* ---------------------------------------------------------------- checkpoints */
 
 /* Trained weights from safetensors files (the format candle's

@@ -353,6 +353,16 @@ _sig("lwm_lewm_tensor_info", C.c_size_t, C.POINTER(LewmConfig), I32, C.c_size_t,
 _sig("lwm_skyjepa_weights_from_safetensors", C.c_int, C.POINTER(SkyJepaConfig), C.c_char_p, C.c_char_p, FP,
      C.c_size_t)
 _sig("lwm_lewm_weights_from_safetensors", C.c_int, C.POINTER(LewmConfig), I32, C.c_char_p, FP, C.c_size_t)
+_sig("lwm_skyjepa_session_config_paper", None, VP)
+_sig("lwm_skyjepa_session_create", C.c_int, VP, VP, VP, FP, C.c_size_t, FP, FP, FP, FP, FP, C.POINTER(VP))
+_sig("lwm_skyjepa_session_destroy", None, VP)
+_sig("lwm_skyjepa_session_reset", C.c_int, VP, FP)
+_sig("lwm_skyjepa_session_reset_with_action", C.c_int, VP, FP, FP)
+_sig("lwm_skyjepa_session_commit_observation", C.c_int, VP, FP, FP)
+_sig("lwm_skyjepa_session_plan", C.c_int, VP, FP, I32, VP)
+_sig("lwm_skyjepa_session_scorer", VP, VP)
+_sig("lwm_skyjepa_session_trim_scale", F, VP)
+_sig("lwm_skyjepa_shifted_residual", C.c_int, FP, FP, U32, U32, F, FP)
 _sig("lwm_image_preprocess_imagenet_224", None, C.POINTER(ImagePreprocess))
 _sig("lwm_preprocess_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32, I32,
      VP)
@@ -981,6 +991,113 @@ def preprocess_nv12_device(ctx: Context, y_plane, uv_plane, batch: int, height: 
     cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
     _check(lib.lwm_preprocess_nv12_device(ctx.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), batch, height, width,
                                           cs, C.byref(cfg), history_len, history_slot, int(bf16), VP(_ptr(out))))
+
+
+# ------------------------------------------------------------ control session
+
+WARM_STARTS = {"fresh_prior": 0, "shifted_residual": 1}
+DYNAMICS = {"learned": 0, "nominal_physics": 1}
+
+
+class SessionConfig(C.Structure):
+    """SkyJepaSessionConfig + SkyJepaControlConfig (session.rs:40-87, control.rs:72-94)."""
+    _fields_ = [("samples", U32), ("horizon", U32), ("planner_seed", U64), ("warm_start", I32),
+                ("residual_limit_n", F), ("dynamics", I32), ("trim_multiplier", F), ("dt", F), ("iterations", U32),
+                ("temperature", F), ("action_noise", F * 4), ("cost", TrackingCost)]
+
+    @staticmethod
+    def paper() -> "SessionConfig":
+        c = SessionConfig()
+        lib.lwm_skyjepa_session_config_paper(C.byref(c))
+        return c
+
+
+class _ControllerPlan(C.Structure):
+    _fields_ = [("action", F * 4), ("prior_action", F * 4), ("action_correction", F * 4), ("action_sequence", FP),
+                ("predicted_states", FP), ("best_candidate_score", F), ("plan_ms", C.c_double),
+                ("deadline_reached", I32)]
+
+
+@dataclass
+class ControllerPlan:
+    """SkyJepaControllerPlan (session.rs:89-100)."""
+    action: np.ndarray
+    prior_action: np.ndarray
+    action_correction: np.ndarray
+    action_sequence: np.ndarray
+    predicted_states: np.ndarray
+    best_candidate_score: float
+    plan_ms: float
+    deadline_reached: bool
+
+
+class SkyJepaSession:
+    """SkyJepaControllerSession (src/models/skyjepa/session.rs:110-470)."""
+
+    def __init__(self, ctx: Context, config: SessionConfig, initial_state, model: Optional[SkyJepaConfig] = None,
+                 weights=None, state_mean=None, state_std=None, action_mean=None, action_std=None):
+        self.ctx = ctx
+        self.config = config
+        w = None if weights is None else _f32(weights)
+        h = VP()
+        _check(lib.lwm_skyjepa_session_create(
+            ctx.handle, C.byref(config), C.byref(model) if model is not None else None, _fp(w),
+            C.c_size_t(0 if w is None else w.size), _fp(None if state_mean is None else _f32(state_mean)),
+            _fp(None if state_std is None else _f32(state_std)), _fp(None if action_mean is None else _f32(action_mean)),
+            _fp(None if action_std is None else _f32(action_std)), _fp(_f32(initial_state)), C.byref(h)))
+        self.handle = h
+        _LIVE["scorer"].add(self)
+
+    def reset(self, state) -> None:
+        _check(lib.lwm_skyjepa_session_reset(self.handle, _fp(_f32(state))))
+
+    def reset_with_action(self, state, action) -> None:
+        _check(lib.lwm_skyjepa_session_reset_with_action(self.handle, _fp(_f32(state)), _fp(_f32(action))))
+
+    def commit_observation(self, state, action) -> None:
+        _check(lib.lwm_skyjepa_session_commit_observation(self.handle, _fp(_f32(state)), _fp(_f32(action))))
+
+    def plan(self, reference_states, include_prediction: bool = False) -> ControllerPlan:
+        T = self.config.horizon
+        refs = _f32(reference_states, (T, 18))
+        seq = np.empty((T, 4), np.float32)
+        pred = np.empty((T, 18), np.float32) if include_prediction else np.empty((0, 18), np.float32)
+        r = _ControllerPlan()
+        r.action_sequence = _fp(seq)
+        r.predicted_states = _fp(pred) if include_prediction else None
+        _check(lib.lwm_skyjepa_session_plan(self.handle, _fp(refs), int(include_prediction), C.byref(r)))
+        return ControllerPlan(np.array(r.action[:], np.float32), np.array(r.prior_action[:], np.float32),
+                              np.array(r.action_correction[:], np.float32), seq, pred, float(r.best_candidate_score),
+                              float(r.plan_ms), bool(r.deadline_reached))
+
+    def set_precision(self, precision: str) -> None:
+        """Precision of the learned scorer (lwm_scorer_skyjepa_set_precision)."""
+        _check(lib.lwm_scorer_skyjepa_set_precision(lib.lwm_skyjepa_session_scorer(self.handle), PRECISIONS[precision]))
+
+    @property
+    def trim_scale(self) -> float:
+        return float(lib.lwm_skyjepa_session_trim_scale(self.handle))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            if getattr(self.ctx, "handle", None):
+                lib.lwm_skyjepa_session_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def shifted_residual(sequence, prior, limit: float) -> np.ndarray:
+    """shifted_residual (src/models/skyjepa/session.rs:534-543) for one [T, A] sequence."""
+    seq = _f32(sequence)
+    T, A = seq.shape
+    out = np.empty((T, A), np.float32)
+    _check(lib.lwm_skyjepa_shifted_residual(_fp(seq), _fp(_f32(prior, (T, A))), T, A, F(limit), _fp(out)))
+    return out
 
 
 # ----------------------------------------------------------------- task inputs
