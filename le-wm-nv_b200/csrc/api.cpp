@@ -152,6 +152,8 @@ struct lwm_scorer {
     // learned scorer on tensor cores (bf16): packed weights, per-vehicle h0, wait-timeout flag
     int32_t precision = LWM_PRECISION_F32;
     DevBuf tc_packed, tc_h0, tc_err, tc_x;
+    bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
+    DevBuf small_x;
     bool tc_ready = false;
 };
 
@@ -351,6 +353,7 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     uint32_t P = std::max<uint32_t>(lwm::nominal_blocks_per_vehicle(p->S),
                                     lwm::skyjepa_partials_per_vehicle(p->S, 32));
     P = std::max<uint32_t>(P, (p->S + 255) / 256);
+    P = std::max<uint32_t>(P, lwm::skyjepa_small_partials_per_vehicle(p->S));
     const size_t pw = (4 + static_cast<size_t>(p->T) * p->A + 3) & ~static_cast<size_t>(3);
     LWM_TRY(p->zeros.ensure(seq * 4));
     LWM_TRY(p->std_init.ensure(seq * 4));
@@ -453,6 +456,12 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint
     return LWM_OK;
 }
 
+lwm_status ensure_small(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
+    LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    LWM_TRY(sc->small_x.ensure(std::max<size_t>(lwm::skyjepa_small_x_bytes(a, B, S, T), 4)));
+    return LWM_OK;
+}
+
 lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
     lwm::SkyjepaArgs a = sc->sky_args;
     a.B = sc->batch;
@@ -514,7 +523,12 @@ lwm_status score_device(lwm_scorer* sc, const float* cand, uint32_t B, uint32_t 
         a.states = states;
         a.mppi = 0;
         int n = 0;
-        LWM_CUDA(lwm::launch_skyjepa(a, stream, &n));
+        if (sc->sky_small) {
+            LWM_TRY(ensure_small(sc, a, B, S, a.T));
+            LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream, &n));
+        } else {
+            LWM_CUDA(lwm::launch_skyjepa(a, stream, &n));
+        }
         sc->ctx->launches += static_cast<uint64_t>(n);
     } else if (sc->kind == ScorerKind::Lewm) {
         LWM_CUDA(sc->lewm->score(cand, S, T, scores, states, stream));
@@ -681,7 +695,14 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 a.m.P = lwm::skyjepa_partials_per_vehicle(p->S, a.rows);
                 int launched = 0;
                 const char* why = nullptr;
-                if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
+                if (sc->sky_small) {
+                    LWM_TRY(ensure_small(sc, a, B, p->S, p->T));
+                    a.m.P = lwm::skyjepa_small_partials_per_vehicle(p->S);
+                    a.low_dev = low;
+                    a.high_dev = high;
+                    LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream,
+                                                       &launched));
+                } else if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
                     LWM_TRY(ensure_tc(sc, a, B, p->S, p->T));
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
                     a.low_dev = low;
@@ -1183,10 +1204,14 @@ lwm_status lwm_scorer_skyjepa_create(lwm_ctx* ctx, const lwm_skyjepa_config* cfg
     a.cost = cost_params(*cost);
     a.T = 1;
     const char* why = nullptr;
+    const char* why_small = nullptr;
     if (!lwm::skyjepa_supported(a, &why)) {
-        s->weights.release();
-        delete s;
-        return fail(LWM_UNSUPPORTED, std::string("SkyJEPA configuration not supported by the fused kernel: ") + why);
+        if (!lwm::skyjepa_small_supported(a, &why_small)) {
+            s->weights.release();
+            delete s;
+            return fail(LWM_UNSUPPORTED, std::string("SkyJEPA configuration not supported: ") + why + "; " + why_small);
+        }
+        s->sky_small = true;
     }
     *out = s;
     return LWM_OK;
@@ -1210,7 +1235,8 @@ lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* s, uint32_t B, uint32_t
     lwm::SkyjepaArgs probe = s->sky_args;
     probe.T = T;
     const char* why = nullptr;
-    if (!lwm::skyjepa_supported(probe, &why)) return fail(LWM_UNSUPPORTED, why);
+    if (!(s->sky_small ? lwm::skyjepa_small_supported(probe, &why) : lwm::skyjepa_supported(probe, &why)))
+        return fail(LWM_UNSUPPORTED, why);
     std::lock_guard<std::mutex> lock(s->mu);
     LWM_CUDA(cudaSetDevice(s->ctx->device));
     const uint32_t Hs = s->sky.history_steps;
@@ -1387,6 +1413,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->tc_h0.release();
     s->tc_err.release();
     s->tc_x.release();
+    s->small_x.release();
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;

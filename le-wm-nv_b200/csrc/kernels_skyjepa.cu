@@ -349,16 +349,81 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
 }
 
 // SkyJepaModel::rollout_candidates window encoding (model.rs:192-215) with
-// TemporalBlock::forward (tcn.rs:88-96): window (row rr, step t0) is
-// [history(Hs-1) ++ candidates][t0 .. t0+Hs), each window zero-padded on its
-// own.  `ca` lanes of one warp own a window, one output channel each, all
-// time steps in registers; warp-level syncs between convolutions.
+// TemporalConvEncoder::forward (tcn.rs:88-96, 138-160) over one window held
+// in `cur` [Cm][Hs] (input channels normalised, zero elsewhere): `ca` lanes of
+// one warp, lane o computing output channel o of every convolution at every
+// position in registers, with warp-level syncs between the convolutions (every
+// lane of the warp calls this, `active` or not).  On return cur holds the
+// last block's output.  `aw` is where the encoder's weights (contiguous from
+// tcn.blocks[0].w1) are read: a shared-memory copy or the blob itself.
+template <int HS, int KT>
+__device__ void action_tcn_window(const TcnView& tcn, const float* aw, float* cur, float* hb, uint32_t Hs, uint32_t o,
+                                  bool active) {
+    const float* wbase = tcn.blocks[0].w1;
+    auto sm = [&](const float* p) { return aw + (p - wbase); };
+    for (uint32_t l = 0; l < tcn.levels; ++l) {
+        const TcnBlockView& bk = tcn.blocks[l];
+        const bool mine = active && o < bk.out;
+        float h2[kMaxHist];
+        for (int conv = 0; conv < 2; ++conv) {
+            const float* src = conv == 0 ? cur : hb;
+            const uint32_t cin = conv == 0 ? bk.in : bk.out;
+            const float* W = sm(conv == 0 ? bk.w1 : bk.w2);
+            float acc[kMaxHist];
+#pragma unroll
+            for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
+            if (mine)
+                for (uint32_t i = 0; i < cin; ++i)
+                    conv_channel<HS, KT>(acc, src + i * Hs, W + (o * cin + i) * tcn.k, Hs, tcn.k, bk.dil);
+            const float bias = mine ? sm(conv == 0 ? bk.b1 : bk.b2)[o] : 0.0f;
+            if (conv == 0) {
+                if (mine)
+#pragma unroll
+                    for (int t = 0; t < kMaxHist; ++t)
+                        if (t < static_cast<int>(Hs)) hb[o * Hs + t] = gelu_tanh(acc[t] + bias);
+            } else {
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t) h2[t] = gelu_tanh(acc[t] + bias);
+            }
+            __syncwarp();
+        }
+        float res[kMaxHist];
+#pragma unroll
+        for (int t = 0; t < kMaxHist; ++t) res[t] = 0.0f;
+        if (mine) {
+            if (bk.wr) {
+                const float br = sm(bk.br)[o];
+                const float* wr = sm(bk.wr) + o * bk.in;
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t) {
+                    if (t >= static_cast<int>(Hs)) break;
+                    float r = 0.0f;
+                    for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(wr[i], cur[i * Hs + t], r);
+                    res[t] = r + br;
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < kMaxHist; ++t)
+                    if (t < static_cast<int>(Hs)) res[t] = cur[o * Hs + t];
+            }
+        }
+        __syncwarp();
+        if (mine)
+#pragma unroll
+            for (int t = 0; t < kMaxHist; ++t)
+                if (t < static_cast<int>(Hs)) cur[o * Hs + t] = gelu_tanh(h2[t] + res[t]);
+        __syncwarp();
+    }
+}
+
+// The window of (row rr, step t0) is [history(Hs-1) ++ candidates][t0 .. t0+Hs),
+// each window zero-padded on its own (TemporalBlock::forward, tcn.rs:88-96).
+// The last position of every window of the CTA's own rows goes to every CTA
+// of the cluster.
 template <int HS, int KT>
 __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& cluster, uint32_t c, uint32_t b,
                                    uint32_t rpc, const float* s_cand, float* scratch, float* s_emb, const float* aw) {
     const TcnView& tcn = a.action_tcn;
-    const float* wbase = tcn.blocks[0].w1;  // the encoder's weights are contiguous from here
-    auto sm = [&](const float* p) { return aw + (p - wbase); };
     const uint32_t Hs = a.Hs, T = a.T, A = a.A, E = a.E, TA = T * A;
     const uint32_t ca = pow2_at_least(tcn.max_ch);
     const uint32_t wpp = kThreads / ca;
@@ -380,59 +445,7 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
             }
         }
         __syncwarp();
-        for (uint32_t l = 0; l < tcn.levels; ++l) {
-            const TcnBlockView& bk = tcn.blocks[l];
-            const bool mine = active && o < bk.out;
-            float h2[kMaxHist];
-            for (int conv = 0; conv < 2; ++conv) {
-                const float* src = conv == 0 ? cur : hb;
-                const uint32_t cin = conv == 0 ? bk.in : bk.out;
-                const float* W = sm(conv == 0 ? bk.w1 : bk.w2);
-                float acc[kMaxHist];
-#pragma unroll
-                for (int t = 0; t < kMaxHist; ++t) acc[t] = 0.0f;
-                if (mine)
-                    for (uint32_t i = 0; i < cin; ++i)
-                        conv_channel<HS, KT>(acc, src + i * Hs, W + (o * cin + i) * tcn.k, Hs, tcn.k, bk.dil);
-                const float bias = mine ? sm(conv == 0 ? bk.b1 : bk.b2)[o] : 0.0f;
-                if (conv == 0) {
-                    if (mine)
-#pragma unroll
-                        for (int t = 0; t < kMaxHist; ++t)
-                            if (t < static_cast<int>(Hs)) hb[o * Hs + t] = gelu_tanh(acc[t] + bias);
-                } else {
-#pragma unroll
-                    for (int t = 0; t < kMaxHist; ++t) h2[t] = gelu_tanh(acc[t] + bias);
-                }
-                __syncwarp();
-            }
-            float res[kMaxHist];
-#pragma unroll
-            for (int t = 0; t < kMaxHist; ++t) res[t] = 0.0f;
-            if (mine) {
-                if (bk.wr) {
-                    const float br = sm(bk.br)[o];
-                    const float* wr = sm(bk.wr) + o * bk.in;
-#pragma unroll
-                    for (int t = 0; t < kMaxHist; ++t) {
-                        if (t >= static_cast<int>(Hs)) break;
-                        float r = 0.0f;
-                        for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(wr[i], cur[i * Hs + t], r);
-                        res[t] = r + br;
-                    }
-                } else {
-#pragma unroll
-                    for (int t = 0; t < kMaxHist; ++t)
-                        if (t < static_cast<int>(Hs)) res[t] = cur[o * Hs + t];
-                }
-            }
-            __syncwarp();
-            if (mine)
-#pragma unroll
-                for (int t = 0; t < kMaxHist; ++t)
-                    if (t < static_cast<int>(Hs)) cur[o * Hs + t] = gelu_tanh(h2[t] + res[t]);
-            __syncwarp();
-        }
+        action_tcn_window<HS, KT>(tcn, aw, cur, hb, Hs, o, active);
         if (active && o < E) {
             const float v = cur[o * Hs + Hs - 1];
             const uint32_t m = c * rpc + rr;
@@ -440,6 +453,83 @@ __device__ void action_tcn_windows(const SkyjepaArgs& a, cg::cluster_group& clus
         }
         __syncwarp();
     }
+}
+
+// One step of lewm_skyjepa_integrate_f32 (kinematics.rs:377-484) from the
+// prober outputs po[15] and the candidate's action, and the tracking cost
+// (control.rs:430-452) of that step, returned.  x[18] is updated in place;
+// the state is written to a.states (row s of vehicle b, step t) when asked
+// and `store` is set.
+__device__ __forceinline__ float integrate_and_cost(const SkyjepaArgs& a, uint32_t b, uint32_t s, uint32_t t,
+                                                    float (&x)[18], const float* act, const float* po,
+                                                    bool store = true) {
+    const uint32_t T = a.T;
+    const float sdt = a.dt;
+    float ta;
+    if (a.rotor_forces) {
+        ta = (act[0] + act[1] + act[2] + act[3]) / (a.masses ? __ldg(a.masses + b) : a.mass);
+    } else {
+        const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
+        ta = th * a.gravity / a.hover_throttle;
+    }
+    const float acc[3] = {x[8] * ta + po[0], x[11] * ta + po[1], x[14] * ta - a.gravity + po[2]};
+    float ang[3];
+#pragma unroll
+    for (int row = 0; row < 3; ++row)
+        ang[row] = po[3 + row * 4] * act[0] + po[4 + row * 4] * act[1] + po[5 + row * 4] * act[2] +
+                   po[6 + row * 4] * act[3];
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) { x[ax] += x[3 + ax] * sdt; x[3 + ax] += acc[ax] * sdt; }
+    const float wx = x[15] * sdt, wy = x[16] * sdt, wz = x[17] * sdt;
+    const float th2 = wx * wx + wy * wy + wz * wz;
+    float ca, cb;
+    if (th2 < 1.0e-6f) {
+        const float th4 = th2 * th2;
+        ca = 1.0f - th2 / 6.0f + th4 / 120.0f;
+        cb = 0.5f - th2 / 24.0f + th4 / 720.0f;
+    } else {
+        const float th = sqrtf(th2);
+        float sn, cs;
+        sincosf(th, &sn, &cs);
+        ca = sn / th;
+        cb = (1.0f - cs) / th2;
+    }
+    const float dl[9] = {1.0f - cb * (wy * wy + wz * wz), cb * wx * wy - ca * wz, cb * wx * wz + ca * wy,
+                         cb * wy * wx + ca * wz, 1.0f - cb * (wx * wx + wz * wz), cb * wy * wz - ca * wx,
+                         cb * wz * wx - ca * wy, cb * wz * wy + ca * wx, 1.0f - cb * (wx * wx + wy * wy)};
+    float nr[9];
+#pragma unroll
+    for (int row = 0; row < 3; ++row)
+#pragma unroll
+        for (int col = 0; col < 3; ++col)
+            nr[row * 3 + col] = x[6 + row * 3] * dl[col] + x[7 + row * 3] * dl[3 + col] + x[8 + row * 3] * dl[6 + col];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
+    if (store && a.states && s < a.S) {
+        float* o = a.states + ((static_cast<size_t>(b) * a.S + s) * T + t) * 18;
+#pragma unroll
+        for (int i = 0; i < 18; ++i) o[i] = x[i];
+    }
+    const float* ref = a.ref_states + (static_cast<size_t>(b) * T + t) * 18;
+    float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) { const float dd = x[i] - ref[i]; g0 += dd * dd; }
+#pragma unroll
+    for (int i = 3; i < 6; ++i) { const float dd = x[i] - ref[i]; g1 += dd * dd; }
+#pragma unroll
+    for (int i = 6; i < 15; ++i) { const float dd = x[i] - ref[i]; g2 += dd * dd; }
+#pragma unroll
+    for (int i = 15; i < 18; ++i) { const float dd = x[i] - ref[i]; g3 += dd * dd; }
+    const float* ra = a.ref_actions + (static_cast<size_t>(b) * T + t) * 4;
+    float ac = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float dd = act[i] - ra[i]; ac += (dd * dd) * a.cost.action[i]; }
+    float st = g0 * a.cost.position + g1 * a.cost.velocity;
+    st = st + g2 * a.cost.attitude;
+    st = st + g3 * a.cost.angular_velocity;
+    return st + ac;
 }
 
 // ------------------------------------------------------- the prober warps
@@ -541,76 +631,9 @@ __device__ void prober_step(const SkyjepaArgs& a, const SkySmem& L, float* smem,
 #pragma unroll
         for (int i = 0; i < 18; ++i) x[i] = xs[i];
         const float* act = smem + L.cand + ptid * TA + t * A;
-        const float* po = s_pout + ptid * 16;
-        const float sdt = a.dt;
-        float ta;
-        if (a.rotor_forces) {
-            ta = (act[0] + act[1] + act[2] + act[3]) / (a.masses ? __ldg(a.masses + b) : a.mass);
-        } else {
-            const float th = fminf(1.0f, fmaxf(0.0f, act[2]));
-            ta = th * a.gravity / a.hover_throttle;
-        }
-        const float acc[3] = {x[8] * ta + po[0], x[11] * ta + po[1], x[14] * ta - a.gravity + po[2]};
-        float ang[3];
-#pragma unroll
-        for (int row = 0; row < 3; ++row)
-            ang[row] = po[3 + row * 4] * act[0] + po[4 + row * 4] * act[1] + po[5 + row * 4] * act[2] +
-                       po[6 + row * 4] * act[3];
-#pragma unroll
-        for (int ax = 0; ax < 3; ++ax) { x[ax] += x[3 + ax] * sdt; x[3 + ax] += acc[ax] * sdt; }
-        const float wx = x[15] * sdt, wy = x[16] * sdt, wz = x[17] * sdt;
-        const float th2 = wx * wx + wy * wy + wz * wz;
-        float ca, cb;
-        if (th2 < 1.0e-6f) {
-            const float th4 = th2 * th2;
-            ca = 1.0f - th2 / 6.0f + th4 / 120.0f;
-            cb = 0.5f - th2 / 24.0f + th4 / 720.0f;
-        } else {
-            const float th = sqrtf(th2);
-            float sn, cs;
-            sincosf(th, &sn, &cs);
-            ca = sn / th;
-            cb = (1.0f - cs) / th2;
-        }
-        const float dl[9] = {1.0f - cb * (wy * wy + wz * wz), cb * wx * wy - ca * wz, cb * wx * wz + ca * wy,
-                             cb * wy * wx + ca * wz, 1.0f - cb * (wx * wx + wz * wz), cb * wy * wz - ca * wx,
-                             cb * wz * wx - ca * wy, cb * wz * wy + ca * wx, 1.0f - cb * (wx * wx + wy * wy)};
-        float nr[9];
-#pragma unroll
-        for (int row = 0; row < 3; ++row)
-#pragma unroll
-            for (int col = 0; col < 3; ++col)
-                nr[row * 3 + col] = x[6 + row * 3] * dl[col] + x[7 + row * 3] * dl[3 + col] + x[8 + row * 3] * dl[6 + col];
-#pragma unroll
-        for (int i = 0; i < 9; ++i) x[6 + i] = nr[i];
-#pragma unroll
-        for (int ax = 0; ax < 3; ++ax) x[15 + ax] += ang[ax] * sdt;
-        const uint32_t s = own0 + ptid;
-        if (a.states && s < a.S) {
-            float* o = a.states + ((static_cast<size_t>(b) * a.S + s) * T + t) * 18;
-#pragma unroll
-            for (int i = 0; i < 18; ++i) o[i] = x[i];
-        }
-        const float* ref = a.ref_states + (static_cast<size_t>(b) * T + t) * 18;
-        float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 3; ++i) { const float dd = x[i] - ref[i]; g0 += dd * dd; }
-#pragma unroll
-        for (int i = 3; i < 6; ++i) { const float dd = x[i] - ref[i]; g1 += dd * dd; }
-#pragma unroll
-        for (int i = 6; i < 15; ++i) { const float dd = x[i] - ref[i]; g2 += dd * dd; }
-#pragma unroll
-        for (int i = 15; i < 18; ++i) { const float dd = x[i] - ref[i]; g3 += dd * dd; }
-        const float* ra = a.ref_actions + (static_cast<size_t>(b) * T + t) * 4;
-        float ac = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) { const float dd = act[i] - ra[i]; ac += (dd * dd) * a.cost.action[i]; }
-        float st = g0 * a.cost.position + g1 * a.cost.velocity;
-        st = st + g2 * a.cost.attitude;
-        st = st + g3 * a.cost.angular_velocity;
+        xs[18] += integrate_and_cost(a, b, own0 + ptid, t, x, act, s_pout + ptid * 16);
 #pragma unroll
         for (int i = 0; i < 18; ++i) xs[i] = x[i];
-        xs[18] += st + ac;
     }
 }
 
@@ -843,6 +866,217 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
     }
 }
 
+// ------------------------------------------------------ small-latent path
+//
+// Models whose latent fits one or two registers per lane (latent <= 64, the
+// paper-derived SkyJEPA: latent 24, TCN [8, 8, 16] / [4, 4, 8], prober 32 x 2)
+// run a warp per candidate:
+//   skyjepa_small_inputs_kernel  x_t of every (candidate, step): the action
+//       encoder over its window (action_tcn_window), `ca` lanes per window;
+//   skyjepa_small_kernel  the GRU rollout (lane j owns units j and j + 32;
+//       h is broadcast by shuffles), the prober (lane o owns outputs o and
+//       o + 32), then the integrator and the cost, computed by every lane
+//       of the warp alike; the scores and the fused MPPI partial of the block.
+// The initial latent per vehicle comes from skyjepa_h0_kernel.
+constexpr uint32_t kSmallMaxH = 64, kSmallWarps = 8, kSmallThreads = kSmallWarps * 32;
+
+struct SmallSmem {
+    uint32_t whh, wih, bih, bhh, w1, b1, wh, bh, wo, bo, score, w, total;
+    uint32_t hs, ps;  // row strides of W_hh and of the prober's hidden / output layers
+};
+
+__host__ __device__ inline SmallSmem small_layout(const SkyjepaArgs& a) {
+    SmallSmem L{};
+    const uint32_t H = a.H, E = a.E, hid = a.hid;
+    L.hs = H + 1;
+    L.ps = hid + 1;
+    uint32_t o = 0;
+    L.whh = o; o += 3 * H * L.hs;
+    L.wih = o; o += 3 * H * E;
+    L.bih = o; o += 3 * H;
+    L.bhh = o; o += 3 * H;
+    L.w1 = o; o += hid * L.hs;
+    L.b1 = o; o += hid;
+    L.wh = o; o += (a.prober_layers - 1) * hid * L.ps;
+    L.bh = o; o += (a.prober_layers - 1) * hid;
+    L.wo = o; o += 15 * L.ps;
+    L.bo = o; o += 16;
+    L.score = o; o += kSmallWarps;
+    L.w = o; o += kSmallWarps;
+    L.total = o;
+    return L;
+}
+
+template <int HS, int KT>
+__global__ void __launch_bounds__(256) skyjepa_small_inputs_kernel(SkyjepaArgs a, const float* cand, float* xout) {
+    extern __shared__ float scratch[];
+    const TcnView& tcn = a.action_tcn;
+    const uint32_t Hs = a.Hs, T = a.T, A = a.A, E = a.E, TA = T * A;
+    const uint32_t ca = pow2_at_least(tcn.max_ch), Cm = ca;
+    const uint32_t wpb = blockDim.x / ca;
+    const uint32_t slot = threadIdx.x / ca, o = threadIdx.x % ca;
+    const uint64_t windows = static_cast<uint64_t>(a.B) * a.S * T;
+    const uint64_t win = static_cast<uint64_t>(blockIdx.x) * wpb + slot;
+    const bool active = win < windows;
+    const uint64_t grow = active ? win / T : 0;  // b * S + s
+    const uint32_t t0 = active ? static_cast<uint32_t>(win % T) : 0;
+    const uint32_t b = static_cast<uint32_t>(grow / a.S);
+    float* cur = scratch + slot * 3 * Cm * Hs;
+    float* hb = cur + Cm * Hs;
+    for (uint32_t q = o; q < Cm * Hs; q += ca) cur[q] = 0.0f;
+    __syncwarp();
+    if (active && o < tcn.input_dim) {
+        for (uint32_t w = 0; w < Hs; ++w) {
+            const uint32_t pos = t0 + w;
+            const float v = pos < Hs - 1 ? a.action_hist[(static_cast<size_t>(b) * (Hs - 1) + pos) * A + o]
+                                         : cand[grow * TA + (pos - (Hs - 1)) * A + o];
+            cur[o * Hs + w] = (v - a.action_mean[o]) / a.action_std[o];
+        }
+    }
+    __syncwarp();
+    action_tcn_window<HS, KT>(tcn, tcn.blocks[0].w1, cur, hb, Hs, o, active);
+    if (active && o < E) xout[win * E + o] = cur[o * Hs + Hs - 1];
+}
+
+__global__ void __launch_bounds__(kSmallThreads) skyjepa_small_kernel(SkyjepaArgs a, const float* h0, const float* xin,
+                                                                    const float* cand) {
+    extern __shared__ __align__(16) float smem[];
+    const SmallSmem L = small_layout(a);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t H = a.H, E = a.E, hid = a.hid, T = a.T, A = a.A, TA = T * A;
+    const uint32_t b = blockIdx.y, s0 = blockIdx.x * kSmallWarps, s = s0 + warp;
+    // ---- weights into shared memory (padded rows: lane j reads row j conflict-free)
+    for (uint32_t q = tid; q < 3 * H * H; q += kSmallThreads) smem[L.whh + (q / H) * L.hs + q % H] = __ldg(a.w_hh + q);
+    for (uint32_t q = tid; q < 3 * H * E; q += kSmallThreads) smem[L.wih + q] = __ldg(a.w_ih + q);
+    for (uint32_t q = tid; q < 3 * H; q += kSmallThreads) {
+        smem[L.bih + q] = __ldg(a.b_ih + q);
+        smem[L.bhh + q] = __ldg(a.b_hh + q);
+    }
+    for (uint32_t q = tid; q < hid * H; q += kSmallThreads) smem[L.w1 + (q / H) * L.hs + q % H] = __ldg(a.p_in_w + q);
+    for (uint32_t q = tid; q < hid; q += kSmallThreads) smem[L.b1 + q] = __ldg(a.p_in_b + q);
+    for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
+        for (uint32_t q = tid; q < hid * hid; q += kSmallThreads)
+            smem[L.wh + l * hid * L.ps + (q / hid) * L.ps + q % hid] = __ldg(a.p_hid_w[l] + q);
+        for (uint32_t q = tid; q < hid; q += kSmallThreads) smem[L.bh + l * hid + q] = __ldg(a.p_hid_b[l] + q);
+    }
+    for (uint32_t q = tid; q < 15 * hid; q += kSmallThreads) smem[L.wo + (q / hid) * L.ps + q % hid] = __ldg(a.p_out_w + q);
+    for (uint32_t q = tid; q < 15; q += kSmallThreads) smem[L.bo + q] = __ldg(a.p_out_b + q);
+    __syncthreads();
+
+    const bool active = s < a.S;
+    if (active) {
+        const size_t grow = static_cast<size_t>(b) * a.S + s;
+        const uint32_t u0 = lane, u1 = lane + 32;
+        const bool has0 = u0 < H, has1 = u1 < H;
+        float hA = has0 ? h0[static_cast<size_t>(b) * H + u0] : 0.0f;
+        float hB = has1 ? h0[static_cast<size_t>(b) * H + u1] : 0.0f;
+        float x[18];
+#pragma unroll
+        for (int i = 0; i < 18; ++i) x[i] = a.state_hist[(static_cast<size_t>(b) * a.Hs + a.Hs - 1) * 18 + i];
+        float cost = 0.0f;
+        for (uint32_t t = 0; t < T; ++t) {
+            float xe[kMaxTcnCh];
+#pragma unroll
+            for (int e = 0; e < kMaxTcnCh; ++e) xe[e] = static_cast<uint32_t>(e) < E ? xin[(grow * T + t) * E + e] : 0.0f;
+            // candle GRU step (gates r, z, n; h' = z h + (1 - z) n) for units u0, u1
+            float gh[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+            const float* r0 = smem + L.whh + u0 * L.hs;
+            const float* r1 = smem + L.whh + (has1 ? u1 : 0) * L.hs;
+            for (uint32_t k = 0; k < H; ++k) {
+                const float hk = __shfl_sync(0xffffffffu, k < 32 ? hA : hB, k & 31);
+                if (has0) {
+#pragma unroll
+                    for (int g = 0; g < 3; ++g) gh[0][g] = fmaf(r0[g * H * L.hs + k], hk, gh[0][g]);
+                }
+                if (has1) {
+#pragma unroll
+                    for (int g = 0; g < 3; ++g) gh[1][g] = fmaf(r1[g * H * L.hs + k], hk, gh[1][g]);
+                }
+            }
+            float hn[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t u = q == 0 ? u0 : u1;
+                if (u >= H) continue;
+                float gi[3];
+#pragma unroll
+                for (int g = 0; g < 3; ++g) {
+                    const float* wi = smem + L.wih + (g * H + u) * E;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < kMaxTcnCh; ++e)
+                        if (static_cast<uint32_t>(e) < E) acc = fmaf(xe[e], wi[e], acc);
+                    gi[g] = acc + smem[L.bih + g * H + u];
+                }
+                const float rg = sigmoid(gi[0] + (gh[q][0] + smem[L.bhh + u]));
+                const float zg = sigmoid(gi[1] + (gh[q][1] + smem[L.bhh + H + u]));
+                const float ng = tanhf(gi[2] + rg * (gh[q][2] + smem[L.bhh + 2 * H + u]));
+                const float hp = q == 0 ? hA : hB;
+                hn[q] = zg * hp - (zg - 1.0f) * ng;
+            }
+            hA = hn[0];
+            hB = hn[1];
+            // SkyJepaProber::forward (prober.rs:84-102): lane o owns outputs o, o + 32
+            float p0 = 0.0f, p1 = 0.0f;
+            {
+                const bool o0 = lane < hid, o1 = lane + 32 < hid;
+                const float* w0 = smem + L.w1 + lane * L.hs;
+                const float* w1 = smem + L.w1 + (o1 ? lane + 32 : 0) * L.hs;
+                float s0 = 0.0f, s1 = 0.0f;
+                for (uint32_t k = 0; k < H; ++k) {
+                    const float hk = __shfl_sync(0xffffffffu, k < 32 ? hA : hB, k & 31);
+                    if (o0) s0 = fmaf(w0[k], hk, s0);
+                    if (o1) s1 = fmaf(w1[k], hk, s1);
+                }
+                p0 = o0 ? gelu_tanh(s0 + smem[L.b1 + lane]) : 0.0f;
+                p1 = o1 ? gelu_tanh(s1 + smem[L.b1 + lane + 32]) : 0.0f;
+            }
+            for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
+                const bool o0 = lane < hid, o1 = lane + 32 < hid;
+                const float* w0 = smem + L.wh + l * hid * L.ps + lane * L.ps;
+                const float* w1 = smem + L.wh + l * hid * L.ps + (o1 ? lane + 32 : 0) * L.ps;
+                float s0 = 0.0f, s1 = 0.0f;
+                for (uint32_t k = 0; k < hid; ++k) {
+                    const float ak = __shfl_sync(0xffffffffu, k < 32 ? p0 : p1, k & 31);
+                    if (o0) s0 = fmaf(w0[k], ak, s0);
+                    if (o1) s1 = fmaf(w1[k], ak, s1);
+                }
+                p0 = o0 ? gelu_tanh(s0 + smem[L.bh + l * hid + lane]) : 0.0f;
+                p1 = o1 ? gelu_tanh(s1 + smem[L.bh + l * hid + lane + 32]) : 0.0f;
+            }
+            float out = 0.0f;
+            {
+                const float* w0 = smem + L.wo + (lane < 15 ? lane : 0) * L.ps;
+                float s0 = 0.0f;
+                for (uint32_t k = 0; k < hid; ++k) {
+                    const float ak = __shfl_sync(0xffffffffu, k < 32 ? p0 : p1, k & 31);
+                    s0 = fmaf(w0[k], ak, s0);
+                }
+                out = s0 + smem[L.bo + (lane < 15 ? lane : 0)];
+            }
+            float po[16];
+#pragma unroll
+            for (int i = 0; i < 15; ++i) po[i] = __shfl_sync(0xffffffffu, out, i);
+            float act[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) act[i] = cand[(grow * T + t) * A + i];
+            // every lane integrates alike; lane 0 alone writes predicted states
+            cost += integrate_and_cost(a, b, s, t, x, act, po, lane == 0);
+        }
+        const float score = cost * static_cast<float>(1.0 / static_cast<double>(T));
+        if (lane == 0) {
+            smem[L.score + warp] = score;
+            a.scores[static_cast<size_t>(b) * a.S + s] = score;
+        }
+    }
+    __syncthreads();
+    if (a.mppi) {
+        const uint32_t nvalid = s0 >= a.S ? 0u : min(kSmallWarps, a.S - s0);
+        mppi_reduce_rows<kSmallThreads>(a.m, b, blockIdx.x, nvalid, smem + L.score, s0,
+                                        cand + (static_cast<size_t>(b) * a.S + s0) * TA, TA, smem + L.w);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 
@@ -932,6 +1166,76 @@ static cudaError_t launch_rollout(const SkyjepaArgs& a, cudaStream_t stream) {
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, skyjepa_rollout_kernel<H>, a);
+}
+
+bool skyjepa_small_supported(const SkyjepaArgs& a, const char** why) {
+    if (a.H == 0 || a.H > kSmallMaxH) { *why = "latent_dim must be <= 64 on the small-latent path"; return false; }
+    if (a.A != 4) { *why = "action_dim must be 4"; return false; }
+    if (a.E > kMaxTcnCh || a.action_tcn.max_ch > kMaxTcnCh) { *why = "action encoder channels must be <= 8"; return false; }
+    if (a.Hs > kMaxHist || a.Hs < 2) { *why = "history_steps must be in [2, 16]"; return false; }
+    if (a.hid == 0 || a.hid > 64) { *why = "prober hidden_dim must be in [1, 64]"; return false; }
+    if (a.prober_layers < 1 || a.prober_layers > 5) { *why = "prober hidden_layers must be in [1, 5]"; return false; }
+    if (a.T == 0 || a.T > kMaxHorizon) { *why = "horizon must be in [1, 64]"; return false; }
+    if (static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float) > 48 * 1024) {
+        *why = "state encoder too wide for the history kernel";
+        return false;
+    }
+    if (small_layout(a).total * sizeof(float) > 200 * 1024) { *why = "shared memory budget exceeded"; return false; }
+    return true;
+}
+
+uint32_t skyjepa_small_partials_per_vehicle(uint32_t S) { return (S + kSmallWarps - 1) / kSmallWarps; }
+
+size_t skyjepa_small_x_bytes(const SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
+    return static_cast<size_t>(B) * S * T * a.E * sizeof(float);
+}
+
+cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches) {
+    int n = 0;
+    cudaError_t e;
+    if (a.sample) {
+        // candidates (sample_kernel: Philox or injected noise, mean slot, clamp)
+        SampleArgs sa{};
+        sa.B = a.B; sa.S = a.S; sa.T = a.T; sa.A = a.A;
+        sa.mean = a.mean;
+        sa.std = a.std;
+        sa.low = a.low_dev;
+        sa.high = a.high_dev;
+        sa.noise = a.noise;
+        sa.seed = a.seed;
+        sa.offset = a.offset;
+        sa.sample_base = a.sample_base;
+        sa.sample_total = a.sample_total;
+        sa.out = a.cand_out;
+        if ((e = launch_sample(sa, stream)) != cudaSuccess) return e;
+        ++n;
+    }
+    const float* cand = a.sample ? a.cand_out : a.cand_in;
+    // per-step inputs of every candidate
+    const uint32_t ca = pow2_at_least(a.action_tcn.max_ch), wpb = 256 / ca;
+    const uint64_t windows = static_cast<uint64_t>(a.B) * a.S * a.T;
+    const uint32_t blocks = static_cast<uint32_t>((windows + wpb - 1) / wpb);
+    const size_t in_smem = static_cast<size_t>(wpb) * 3 * ca * a.Hs * sizeof(float);
+    if (a.Hs == 10 && a.action_tcn.k == 3)
+        skyjepa_small_inputs_kernel<10, 3><<<blocks, wpb * ca, in_smem, stream>>>(a, cand, x);
+    else
+        skyjepa_small_inputs_kernel<0, 0><<<blocks, wpb * ca, in_smem, stream>>>(a, cand, x);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    ++n;
+    // initial latent per vehicle
+    if ((e = launch_skyjepa_h0(a, h0, stream)) != cudaSuccess) return e;
+    ++n;
+    // rollout, cost, MPPI partials
+    const size_t smem = small_layout(a).total * sizeof(float);
+    if ((e = cudaFuncSetAttribute(skyjepa_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem))) != cudaSuccess)
+        return e;
+    skyjepa_small_kernel<<<dim3(skyjepa_small_partials_per_vehicle(a.S), a.B), kSmallThreads, smem, stream>>>(a, h0, x,
+                                                                                                          cand);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    ++n;
+    if (launches) *launches = n;
+    return cudaSuccess;
 }
 
 cudaError_t launch_skyjepa(const SkyjepaArgs& a, cudaStream_t stream, int* launches) {

@@ -263,6 +263,15 @@ __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h
     }
 }
 
+// h0 of every vehicle: state_projection(TemporalConvEncoder(normalised state
+// history))[last position] (SkyJepaModel::encode_history, model.rs:52-66).
+cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
+    if (a.Hs > kH0MaxHist) return cudaErrorInvalidValue;
+    const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
+    skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
+    return cudaGetLastError();
+}
+
 namespace {
 
 // Action-TCN input of step t for one candidate (TemporalConvEncoder over the
@@ -958,8 +967,8 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
     skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, xtiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
-    skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
+    e = launch_skyjepa_h0(a, h0, stream);
+    if (e != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // 4. the rollout
     TcArgs p;

@@ -339,6 +339,7 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
                 // softmax over a single key is exactly 1: the attention output is V
                 Lin v = b.qkv;
                 v.w = b.qkv.w + static_cast<size_t>(2) * inner * hid;
+                if (b.qkv.wb) v.wb = b.qkv.wb + static_cast<size_t>(2) * inner * hid;
                 v.out = inner;
                 LWM_CU(gemm_f32(sp, gemm(f_y, hid, v, f_att, inner, rows), s));
                 n += 2;

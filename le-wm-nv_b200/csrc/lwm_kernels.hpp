@@ -169,6 +169,14 @@ uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S);
 cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
                               cudaStream_t stream, int* launches);
 size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
+// Initial latent of every vehicle (state encoder + projection) into h0 [B, H].
+cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
+// Small-latent (<= 64) learned path: a warp per candidate (sampling, action
+// encoder inputs x [B,S,T,E], h0, rollout + cost + MPPI partials).
+bool skyjepa_small_supported(const SkyjepaArgs& a, const char** why);
+uint32_t skyjepa_small_partials_per_vehicle(uint32_t S);
+size_t skyjepa_small_x_bytes(const SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T);
+cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches);
 
 cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
                                uint32_t S, cudaStream_t stream);

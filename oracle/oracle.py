@@ -24,7 +24,7 @@ lib = C.CDLL(LIB_PATH)
 sys.path.insert(0, os.path.join(os.path.dirname(_HERE), "le-wm-nv_b200"))
 # Struct layouts only (ctypes mirrors of include/lewm_b200.h); no product call.
 from lewm_b200 import (  # noqa: E402
-    Domain, TrackingCost, SkyJepaConfig, KinematicConfig, _MppiConfig, _CemConfig, _IcemConfig,
+    Domain, TrackingCost, SkyJepaConfig, KinematicConfig, _MppiConfig, _CemConfig, _IcemConfig, SessionConfig,
 )
 
 F = C.c_float
@@ -516,3 +516,107 @@ class LewmModel:
         ctx = LewmCtx(self.handle, fp(emb), fp(goal), emb.shape[1], history or emb.shape[1])
         ctx._keep = (emb, goal)
         return ctx
+
+
+# ------------------------------------------------------------ control session
+
+def reference_horizon(kind: int, time: float, dt: float, horizon: int, radius: float, period: float):
+    """skyjepa_reference_horizon (src/skyjepa_task.rs:44-55): states at
+    time + k dt, k = 1..horizon, in f32."""
+    t0, d = np.float32(time), np.float32(dt)
+    return np.stack([reference_state(kind, float(t0 + np.float32(k) * d), radius, period)
+                     for k in range(1, horizon + 1)])
+
+
+def shifted_residual(sequence, prior, limit):
+    """shifted_residual (src/models/skyjepa/session.rs:534-543)."""
+    r = np.clip(f32(sequence) - f32(prior), np.float32(-limit), np.float32(limit)).astype(np.float32)
+    out = np.zeros_like(r)
+    out[:-1] = r[1:]
+    return out
+
+
+class _SessionPlanner:
+    """The session's MppiConfig (SkyJepaControlConfig::mppi_config,
+    src/models/skyjepa/control.rs:124-132) as the oracle planner takes it."""
+
+    def __init__(self, cfg, high, hover):
+        c = _MppiConfig()
+        c.horizon, c.samples, c.iterations, c.action_dim = cfg.horizon, cfg.samples, cfg.iterations, 4
+        for i in range(4):
+            c.bounds_low[i], c.bounds_high[i] = 0.0, float(high)
+            c.noise_std_per_action[i] = cfg.action_noise[i]
+            c.deadline_action[i] = float(hover[i])
+        c.noise_std = 1.0
+        c.has_noise_std_per_action = 1
+        c.temperature = cfg.temperature
+        c.deadline_ns = -1
+        c.has_deadline_action = 1
+        c.has_seed, c.seed = 1, cfg.planner_seed
+        self.c = c
+        self.horizon, self.samples, self.action_dim, self.iterations = cfg.horizon, cfg.samples, 4, cfg.iterations
+
+    def _c(self):
+        return self.c
+
+
+class SkyJepaSession:
+    """SkyJepaControllerSession (src/models/skyjepa/session.rs:241-445)
+    restated over the oracle's planner, scorers and geometric prior.
+    `sky` = (SkyJepaConfig, weights, (state_mean, state_std, action_mean,
+    action_std)) for the learned dynamics, None for the nominal physics."""
+
+    def __init__(self, cfg: SessionConfig, initial, sky=None):
+        dom = Domain.default()
+        self.cfg, self.dom = cfg, dom
+        self.hover = np.full(4, np.float32(dom.mass) * np.float32(dom.gravity) / np.float32(4.0), np.float32)
+        self.high = np.float32(dom.mass) * np.float32(dom.gravity) * np.float32(dom.max_thrust_weight) / np.float32(4.0)
+        self.model = None if sky is None else SkyJepaModel(sky[0], sky[1])
+        self.norm = None if sky is None else sky[2]
+        self.H = sky[0].history_steps if sky is not None else 10
+        self.mppi = _SessionPlanner(cfg, self.high, self.hover)
+        self.reset_with_action(initial, self.hover)
+
+    def reset_with_action(self, state, action):
+        a = f32(action)
+        collective = ((a[0] + a[1]) + a[2]) + a[3]
+        nominal = ((self.hover[0] + self.hover[1]) + self.hover[2]) + self.hover[3]
+        self.trim = collective / nominal * np.float32(self.cfg.trim_multiplier)
+        self.motors = (a / self.trim).astype(np.float32)
+        self.states = [f32(state).copy() for _ in range(self.H)]
+        self.actions = [a.copy() for _ in range(self.H - 1)]
+        self.active = self.pending = None
+        self.offset = 0  # MppiPlanner::new: a fresh sampler
+
+    def commit_observation(self, state, action):
+        self.active, self.pending = self.pending, None
+        response = np.float32(1.0) - np.exp(np.float32(-self.cfg.dt) / np.float32(self.dom.motor_time_constant),
+                                            dtype=np.float32)
+        for i in range(4):
+            target = np.clip(np.float32(action[i]) / self.trim, np.float32(0.0), self.high)
+            self.motors[i] += (target - self.motors[i]) * response
+        self.states = self.states[1:] + [f32(state).copy()]
+        self.actions = self.actions[1:] + [f32(action).copy()]
+
+    def plan(self, refs):
+        """-> (action sequence [T,4], prior [T,4], best candidate score)."""
+        self.pending = None
+        refs = f32(refs)
+        last = self.states[-1]
+        prior = np.clip(geometric_prior(last, refs, self.cfg.dt) * self.trim, 0.0, self.high).astype(np.float32)
+        warm = prior + self.active if (self.cfg.warm_start == 1 and self.active is not None) else prior
+        warm = np.clip(warm, 0.0, self.high).astype(np.float32)
+        if self.model is None:
+            c = nominal_ctx(last[None], self.motors[None], refs[None], prior[None], self.cfg.cost, self.cfg.dt,
+                            float(self.trim))
+            fn = NOMINAL_FN
+        else:
+            c = self.model.score_ctx(self.norm, np.stack(self.states)[None], np.stack(self.actions)[None],
+                                     refs[None], prior[None], self.cfg.cost, self.cfg.dt)
+            fn = SKYJEPA_FN
+        r = mppi_plan(self.mppi, 1, (fn, c), seed=self.cfg.planner_seed, offset=self.offset, warm_start=warm[None])
+        per = self.cfg.samples * self.cfg.horizon * 4
+        self.offset += (per + per % 2) * self.cfg.iterations
+        if self.cfg.warm_start == 1:
+            self.pending = shifted_residual(r["sequence"][0], prior, self.cfg.residual_limit_n)
+        return r["sequence"][0], prior, float(r["scores"].min())

@@ -69,7 +69,7 @@ def test_image_bf16_pipeline(ctx):
     assert_bf16_costs(_score(ctx, sc, cand), m.scores(e, g, cand))
 
 
-@pytest.mark.parametrize("S,T", [(37, 3), (1, 1), (130, 2)])
+@pytest.mark.parametrize("S,T", [(37, 3), (1, 4), (130, 5)])
 def test_ragged_tiles_and_history(ctx, S, T):
     # M not a multiple of 128 (and tiny); a 3-frame window with attention
     from test_lewm_oracle import small_config

@@ -17,72 +17,8 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _f(x):
-    return np.float32(x)
-
-
-class OracleSession:
-    """The session's host logic (session.rs:241-445) over the oracle."""
-
-    def __init__(self, cfg, initial, sky=None):
-        dom = L.Domain.default()
-        self.cfg, self.sky, self.dom = cfg, sky, dom
-        self.hover = np.full(4, _f(dom.mass) * _f(dom.gravity) / _f(4.0), np.float32)
-        self.high = _f(dom.mass) * _f(dom.gravity) * _f(dom.max_thrust_weight) / _f(4.0)
-        self.H = sky.model.history_steps if sky is not None else 10
-        self.mppi = L.MppiConfig(horizon=cfg.horizon, samples=cfg.samples, action_dim=4, iterations=cfg.iterations,
-                                 action_bounds=L.ActionBounds.scalar(4, 0.0, float(self.high)),
-                                 noise_std_per_action=list(cfg.action_noise), temperature=cfg.temperature,
-                                 seed=cfg.planner_seed)
-        self.reset_with_action(initial, self.hover)
-
-    def reset_with_action(self, state, action):
-        a = np.asarray(action, np.float32)
-        collective = ((a[0] + a[1]) + a[2]) + a[3]
-        nominal = ((self.hover[0] + self.hover[1]) + self.hover[2]) + self.hover[3]
-        self.trim = collective / nominal * _f(self.cfg.trim_multiplier)
-        self.motors = (a / self.trim).astype(np.float32)
-        self.states = [np.asarray(state, np.float32).copy() for _ in range(self.H)]
-        self.actions = [a.copy() for _ in range(self.H - 1)]
-        self.active = self.pending = None
-        self.offset = 0  # a fresh planner
-
-    def commit_observation(self, state, action):
-        self.active, self.pending = self.pending, None
-        response = _f(1.0) - np.exp(_f(-self.cfg.dt) / _f(self.dom.motor_time_constant), dtype=np.float32)
-        for i in range(4):
-            target = np.clip(_f(action[i]) / self.trim, _f(0.0), self.high)
-            self.motors[i] += (target - self.motors[i]) * response
-        self.states = self.states[1:] + [np.asarray(state, np.float32).copy()]
-        self.actions = self.actions[1:] + [np.asarray(action, np.float32).copy()]
-
-    def plan(self, refs):
-        self.pending = None
-        last = self.states[-1]
-        prior = np.clip(O.geometric_prior(last, refs, self.cfg.dt) * self.trim, 0.0, self.high).astype(np.float32)
-        warm = prior + self.active if (self.cfg.warm_start == 1 and self.active is not None) else prior
-        warm = np.clip(warm, 0.0, self.high).astype(np.float32)
-        if self.sky is None:
-            c = O.nominal_ctx(last[None], self.motors[None], refs[None], prior[None], self.cfg.cost, self.cfg.dt,
-                              float(self.trim))
-            fn = O.NOMINAL_FN
-        else:
-            m = O.SkyJepaModel(self.sky.model, self.sky.weights)
-            self._m = m
-            c = m.score_ctx((self.sky.state_mean, self.sky.state_std, self.sky.action_mean, self.sky.action_std),
-                            np.stack(self.states)[None], np.stack(self.actions)[None], refs[None], prior[None],
-                            self.cfg.cost, self.cfg.dt)
-            fn = O.SKYJEPA_FN
-        r = O.mppi_plan(self.mppi, 1, (fn, c), seed=self.cfg.planner_seed, offset=self.offset, warm_start=warm[None])
-        per = self.cfg.samples * self.cfg.horizon * 4
-        self.offset += (per + per % 2) * self.cfg.iterations
-        if self.cfg.warm_start == 1:
-            self.pending = L.shifted_residual(r["sequence"][0], prior, self.cfg.residual_limit_n)
-        return r["sequence"][0], prior, float(r["scores"].min())
-
-
 def _refs(t0, cfg):
-    return L.reference_horizon("figure-eight", t0, cfg.dt, cfg.horizon, 2.0, 8.0)
+    return O.reference_horizon(2, t0, cfg.dt, cfg.horizon, 2.0, 8.0)
 
 
 def _closed_loop(ctx, cfg, steps, sky=None):
@@ -95,7 +31,8 @@ def _closed_loop(ctx, cfg, steps, sky=None):
     else:
         sess = L.SkyJepaSession(ctx, cfg, x, sky.model, sky.weights, sky.state_mean, sky.state_std,
                                 sky.action_mean, sky.action_std)
-    ref = OracleSession(cfg, x, sky)
+    ref = O.SkyJepaSession(cfg, x, None if sky is None else
+                           (sky.model, sky.weights, (sky.state_mean, sky.state_std, sky.action_mean, sky.action_std)))
     motors = np.full(4, dom.mass * dom.gravity / 4, np.float32)
     for k in range(steps):
         refs = _refs(0.05 * k, cfg)
