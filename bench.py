@@ -10,6 +10,8 @@ reference).  A "step" is one plan call.
     python bench.py --impl reference ...   # the CPU restatement on the host cores
     python bench.py --workload fleet [--shard auto|vehicles|candidates] [--vehicles V --samples S --horizon T]
     python bench.py --workload lewm-vector|lewm-image    # LeWM CEM (vector obs) / MPPI (NV12 frames + ViT)
+    python bench.py --workload closed-loop [--dynamics learned|nominal] [--random-domains N]
+                                          # closed-loop session scenarios; --steps = control steps per scenario
 
 `value` is timed with CUDA events around each plan on the device with the
 context resident (L2 flushed between steps); `e2e` times the public C-ABI
@@ -630,6 +632,148 @@ def cpu_baseline_lewm(w, image: bool, budget_s: float):
             "sample": f"{len(times)} full plans (encoding included), oracle C restatement, {threads} OpenMP threads"}
 
 
+# -------------------------------------------------------- closed-loop scenarios
+
+REFERENCE_KINDS = {"hover": 0, "circle": 1, "figure-eight": 2}
+
+
+def closed_loop_setup(args):
+    """The session configuration, the model and the scenario list of the
+    closed-loop bench (lewm-bench-skyjepa.rs:215-262): hover / circle /
+    figure-eight references x (the nominal domain + `random_domains` sampled
+    domains), each flown for `steps` control steps of 50 ms."""
+    import lewm_b200 as L
+    from lewm_b200 import workloads as W
+    cfg = L.SessionConfig.paper()
+    cfg.dynamics = L.DYNAMICS["nominal_physics" if args.dynamics == "nominal" else "learned"]
+    sky = None
+    if args.dynamics == "learned":
+        sky = W.skyjepa(seed=37, config=L.SkyJepaConfig.paper())
+    domains = [("nominal", L.Domain.default())]
+    domains += [(f"sampled-{i}", L.Domain.sample(9001 + 7919 * i)) for i in range(args.random_domains)]
+    scenarios = [(kind, name, dom) for kind in REFERENCE_KINDS for name, dom in domains]
+    return cfg, sky, scenarios
+
+
+def run_closed_loop(args, rank, world, local_rank):
+    """SkyJEPA closed-loop control through the controller session: every
+    control step plans (one synchronised call: context upload, MPPI, result
+    download, as SkyJepaControllerSession::plan), the rotor plant advances
+    10 substeps of 5 ms on the host with the planned action, and the session
+    commits the observation.  Latency = wall time of the plan call."""
+    import torch
+    import lewm_b200 as L
+    torch.cuda.set_device(local_rank)
+    cfg, sky, scenarios = closed_loop_setup(args)
+    ctx = L.Context(local_rank)
+    hover = L.hover_state()
+    if sky is None:
+        sess = L.SkyJepaSession(ctx, cfg, hover)
+    else:
+        sess = L.SkyJepaSession(ctx, cfg, hover, sky.model, sky.weights, sky.state_mean, sky.state_std,
+                                sky.action_mean, sky.action_std)
+    dt = cfg.dt
+    refs0 = L.reference_horizon("hover", 0.0, dt, cfg.horizon, 2.0, 8.0)
+    for _ in range(args.warmup):  # SkyJepaControllerSession::warm_up: plan, then reset
+        sess.plan(refs0)
+    times, rmses, launches = [], [], 0
+    n0 = ctx.launch_count()
+    kinds = {v: k for k, v in REFERENCE_KINDS.items()}
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        for kind, _name, dom in scenarios:
+            x = L.hover_state()
+            motors = np.full(4, dom.mass * dom.gravity / 4, np.float32)
+            sess.reset_with_action(x, motors)  # the plant's nominal hover action
+            err2 = 0.0
+            for step in range(args.steps):
+                t = step * dt
+                refs = L.reference_horizon(kind, t, dt, cfg.horizon, 2.0, 8.0)
+                t0 = time.perf_counter()
+                plan = sess.plan(refs)
+                times.append((time.perf_counter() - t0) * 1e3)
+                for _ in range(10):
+                    L.plant_step(dom, x, motors, plan.action, dt / 10)
+                sess.commit_observation(x, plan.action)
+                ref = L.reference_horizon(kind, t, dt, 1, 2.0, 8.0)[0]
+                err2 += float(np.sum((x[:3] - ref[:3]) ** 2))
+            rmses.append((err2 / args.steps) ** 0.5)
+    launches = ctx.launch_count() - n0
+    sess.close()
+    ctx.close()
+    if rank != 0:
+        return None
+    mean = float(np.mean(times))
+    T, S = cfg.horizon, cfg.samples
+    model = ("nominal rotor physics (10 substeps)" if sky is None else
+             "SkyJEPA paper-derived model (latent 24, TCN [8,8,16]/[4,4,8], prober 32x2), random-init weights")
+    result = {
+        "metric": "closed-loop plan latency p95 (ms) and plans/s; 512 candidates x 15 steps, 1 MPPI iteration, "
+                  "one synchronised session plan per 50 ms control step",
+        "value": round(world * 1e3 / mean, 3), "unit": "plans/s", "n_gpus": world, "steps": len(times),
+        "warmup": args.warmup, "ms_per_step": round(mean, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init weights, generated references, sampled domains)",
+        "config": {"workload": f"closed-loop SkyJEPA MPPI session, {model}; {len(scenarios)} scenarios "
+                               f"(hover / circle / figure-eight x nominal + {args.random_domains} sampled domains) "
+                               f"x {args.steps} control steps",
+                   "parallelism": f"replicas x{world}", "l2": "not flushed: the session's working set is "
+                   "far below L2; the plant and the host bookkeeping run between plans"},
+        "latency_ms": {"p50": round(percentile(times, 0.5), 4), "p95": round(percentile(times, 0.95), 4),
+                       "p99": round(percentile(times, 0.99), 4), "max": round(max(times), 4)},
+        "candidate_steps_per_s": round(world * 1e3 / mean * S * T, 1),
+        "tracking": {"position_rmse_m_median": round(float(np.median(rmses)), 4),
+                     "position_rmse_m_max": round(float(np.max(rmses)), 4),
+                     "scenarios_within_0.75m": int(sum(r <= 0.75 for r in rmses))},
+        "reference_published_p95_ms": {"random-weight SkyJEPA MPPI": 8.931, "nominal-physics MPPI": 3.215,
+                                       "hardware": "RTX 4090 (shared)"},
+        "e2e": {"value": round(world * 1e3 / mean, 3), "unit": "plans/s",
+                "h2d_bytes_per_step": int(4 * (T * 18 + T * 4 + T * 4 + 10 * 18 + 9 * 4)),
+                "d2h_bytes_per_step": int(4 * (4 + T * 4 + S + 1))},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    if args.cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_closed_loop(args, args.cpu_seconds)
+    return result
+
+
+def cpu_baseline_closed_loop(args, budget_s: float):
+    """The oracle's session (the same closed loop) on the host cores, for a
+    bounded number of control steps of the first scenarios."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import lewm_b200 as L
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    cfg, sky, scenarios = closed_loop_setup(args)
+    sess = O.SkyJepaSession(cfg, L.hover_state(), None if sky is None else
+                            (sky.model, sky.weights, (sky.state_mean, sky.state_std, sky.action_mean, sky.action_std)))
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for kind, _name, dom in scenarios:
+        x = L.hover_state()
+        motors = np.full(4, dom.mass * dom.gravity / 4, np.float32)
+        sess.reset_with_action(x, motors)
+        for step in range(args.steps):
+            refs = O.reference_horizon(REFERENCE_KINDS[kind], step * cfg.dt, cfg.dt, cfg.horizon, 2.0, 8.0)
+            t0 = time.perf_counter()
+            seq, _, _ = sess.plan(refs)
+            times.append((time.perf_counter() - t0) * 1e3)
+            for _ in range(10):
+                O.plant_step(dom, x, motors, seq[0], cfg.dt / 10)
+            sess.commit_observation(x, seq[0])
+            if time.perf_counter() > t_end:
+                break
+        if time.perf_counter() > t_end:
+            break
+    mean = float(np.mean(times))
+    return {"value": round(1e3 / mean, 4), "unit": "plans/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} closed-loop session plans (oracle session, C planner and scorer, "
+                      f"{threads} OpenMP threads)",
+            "latency_ms": {"p50": round(percentile(times, 0.5), 3), "p95": round(percentile(times, 0.95), 3)}}
+
+
 # ----------------------------------------------------------------- CPU arm
 
 def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
@@ -683,6 +827,18 @@ def run_reference(args, rank, world):
                 "candidate_steps_per_s": base["candidate_steps_per_s"], "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "fleet plans/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload == "closed-loop":
+        base = cpu_baseline_closed_loop(args, args.cpu_seconds)
+        return {"impl": "reference", "metric": "closed-loop plan latency p95 (ms) and plans/s; 512 candidates x 15 "
+                "steps, 1 MPPI iteration, one synchronised session plan per 50 ms control step",
+                "value": base["value"], "unit": "plans/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init weights, generated references, sampled domains)",
+                "config": {"workload": f"closed-loop SkyJEPA MPPI session ({args.dynamics})",
+                           "parallelism": "host CPU"},
+                "latency_ms": base["latency_ms"], "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload.startswith("lewm"):
         from lewm_b200 import workloads as W
         image = args.workload == "lewm-image"
@@ -730,7 +886,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet", "lewm-vector", "lewm-image"],
+    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet", "lewm-vector", "lewm-image", "closed-loop"],
                     default="skyjepa")
     ap.add_argument("--shard", choices=["auto", "vehicles", "candidates"], default="auto")
     ap.add_argument("--vehicles", type=int, default=256)
@@ -739,6 +895,10 @@ def main():
     ap.add_argument("--precision", choices=["f32", "bf16"], default=None,
                     help="fleet and lewm-image: bf16 weights on the tensor cores (their default) or f32; "
                          "lewm-vector: f32 (default) or bf16")
+    ap.add_argument("--dynamics", choices=["learned", "nominal"], default="learned",
+                    help="closed-loop: the paper-derived SkyJEPA model (random init) or the nominal rotor physics")
+    ap.add_argument("--random-domains", type=int, default=2,
+                    help="closed-loop: sampled domains beside the nominal one (the reference bench uses 20)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
@@ -754,6 +914,8 @@ def main():
         out = run_fleet(args, rank, world, local_rank)
     elif args.workload.startswith("lewm"):
         out = run_lewm(args, rank, world, local_rank)
+    elif args.workload == "closed-loop":
+        out = run_closed_loop(args, rank, world, local_rank)
     else:
         out = run_ours(args, rank, world, local_rank)
     if rank == 0 and out is not None:
