@@ -564,6 +564,23 @@ lwm_status lwm_plan_device_shard(lwm_planner* planner, lwm_scorer* scorer, const
                                  const float** tuples, uint32_t* tuple_width);
 lwm_status lwm_mppi_combine_device(lwm_planner* planner, const float* tuples, uint32_t shards,
                                    lwm_plan_device_result* out);
+/* Candidate shards of a CEM / iCEM plan (any iteration count; set the range
+ * with lwm_planner_set_shard).  Every iteration each shard reduces its
+ * candidates to its lowest `elites` as tuples (score, global candidate index
+ * as uint32 bits, the T*A actions), `exchange` all-gathers the tuples of
+ * every shard in sample-range order, and every shard refits from the merged
+ * set: its lowest `elites` by (score, global index) are exactly the
+ * unsharded plan's elites, so all shards continue from the same mean, std
+ * and carried elites.  lwm_plan / lwm_plan_device then return the whole
+ * plan's sequence, first action, best (global) index and warm start; the
+ * scores are this shard's [B, samples].  `exchange(user, local, count,
+ * gathered, stream)` runs on the planning thread with device buffers (count
+ * floats of this shard; shards * count floats to fill) and the context's
+ * stream, and returns 0 on success.  Shards ignore the deadline (every
+ * shard must take the same iterations). */
+typedef int (*lwm_exchange_fn)(void* user, const float* local, size_t count, float* gathered, void* stream);
+lwm_status lwm_planner_set_shard_exchange(lwm_planner* planner, uint32_t shards, lwm_exchange_fn exchange,
+                                          void* user);
 
 /* ---------------------------------------------------------------- image preprocessing */
 

@@ -179,6 +179,11 @@ struct lwm_planner {
     // candidate-range shard (shard_total 0: unsharded) and its combined tuples
     uint32_t shard_base = 0, shard_total = 0;
     DevBuf shard_tuples;
+    // CEM / iCEM shards: the elite exchange and its buffers
+    lwm_exchange_fn exchange = nullptr;
+    void* exchange_user = nullptr;
+    uint32_t exchange_shards = 0;
+    DevBuf elite_local, elite_gathered, merged_scores, merged_cand, merged_index;
     bool has_result = false;
 };
 
@@ -647,7 +652,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
     }
     const uint32_t carried_keep = p->kind == PlannerKind::Icem ? p->icem.keep_elites : 0;
     for (uint32_t it = 0; it < p->iterations; ++it) {
-        if (deadline_ns >= 0 && !trace) {
+        if (deadline_ns >= 0 && !trace && !sharded) {  // every shard takes the same iterations
             const auto el = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - start).count();
             if (el >= deadline_ns) {
                 deadline_hit = true;
@@ -738,7 +743,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
             if (p->kind == PlannerKind::Icem && it > 0 && carried_keep > 0) {
                 s.carried = p->carried.as<float>();
                 s.carried_count = carried_keep;
-                s.inject = std::min(carried_keep, p->S - 1);
+                s.inject = std::min(carried_keep, (sharded ? p->shard_total : p->S) - 1);
             }
             s.out = p->cand.as<float>();
             float* tr = trace ? p->trace.as<float>() + static_cast<size_t>(it) * 4 * B : nullptr;
@@ -776,6 +781,30 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 r.best_index = p->best.as<uint32_t>();
                 r.best_score = p->best_score.as<float>();
                 r.elite_mean_out = tr ? p->trace_elite.as<float>() : nullptr;
+                if (sharded) {
+                    // this shard's elites -> every shard's (exchange) -> the merged set, refit as one
+                    const uint32_t K = r.K, TA = p->T * p->A, G = p->exchange_shards, W = 2 + TA;
+                    const size_t local = static_cast<size_t>(B) * K * W;
+                    LWM_TRY(p->elite_local.ensure(local * 4));
+                    LWM_TRY(p->elite_gathered.ensure(local * G * 4));
+                    LWM_TRY(p->merged_scores.ensure(static_cast<size_t>(B) * G * K * 4));
+                    LWM_TRY(p->merged_cand.ensure(static_cast<size_t>(B) * G * K * TA * 4));
+                    LWM_TRY(p->merged_index.ensure(static_cast<size_t>(B) * G * K * 4));
+                    LWM_CUDA(lwm::launch_elite_tuples(p->scores.as<float>(), p->cand.as<float>(), B, p->S, K, TA,
+                                                      p->shard_base, p->elite_local.as<float>(), stream));
+                    const int rc = p->exchange(p->exchange_user, p->elite_local.as<float>(), local,
+                                               p->elite_gathered.as<float>(), stream);
+                    if (rc != 0) return fail(LWM_NCCL_ERROR, "elite exchange callback failed with code " + std::to_string(rc));
+                    LWM_CUDA(lwm::launch_elite_merge(p->elite_gathered.as<float>(), G, B, K, TA,
+                                                     p->merged_scores.as<float>(), p->merged_cand.as<float>(),
+                                                     p->merged_index.as<uint32_t>(), stream));
+                    r.S = G * K;
+                    r.sort_len = lwm::sort_length(r.S);
+                    r.scores = p->merged_scores.as<float>();
+                    r.cand = p->merged_cand.as<float>();
+                    r.index_map = p->merged_index.as<uint32_t>();
+                    p->ctx->launches += 2;
+                }
                 LWM_CUDA(lwm::launch_topk_refit(r, B, stream));
                 p->ctx->launches += 1;
                 if (tr) {
@@ -789,7 +818,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
         }
         ++completed;
     }
-    if (sharded) {
+    if (sharded && p->kind == PlannerKind::Mppi) {
         // the outputs (and the warm start) come from lwm_mppi_combine_device
         out->first_action = nullptr;
         out->sequence = nullptr;
@@ -1016,7 +1045,8 @@ lwm_status lwm_planner_destroy(lwm_planner* p) {
     cudaStreamSynchronize(p->ctx->stream);
     for (DevBuf* b : {&p->bounds, &p->zeros, &p->std_init, &p->mean, &p->stdv, &p->cand, &p->scores, &p->partials, &p->counters,
                       &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp,
-                      &p->shard_tuples, &p->trace, &p->trace_elite})
+                      &p->shard_tuples, &p->trace, &p->trace_elite, &p->elite_local, &p->elite_gathered,
+                      &p->merged_scores, &p->merged_cand, &p->merged_index})
         b->release();
     p->staging.release();
     delete p;
@@ -1425,7 +1455,10 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
 lwm_status lwm_plan_device(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_device_result* out) {
     if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
-    if (p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
+    if (p->shard_total && p->kind == PlannerKind::Mppi)
+        return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
+    if (p->shard_total && !p->exchange)
+        return fail(LWM_INVALID_ARGUMENT, "CEM / iCEM candidate shards need an elite exchange (lwm_planner_set_shard_exchange)");
     std::lock_guard<std::mutex> lock(p->mu);
     std::lock_guard<std::mutex> lock2(sc->mu);
     LWM_CUDA(cudaSetDevice(p->ctx->device));
@@ -1456,14 +1489,35 @@ lwm_status lwm_planner_set_shard(lwm_planner* p, uint32_t sample_base, uint32_t 
         p->shard_total = 0;
         return LWM_OK;
     }
-    if (p->kind != PlannerKind::Mppi || p->iterations != 1)
+    if (p->kind == PlannerKind::Mppi && p->iterations != 1)
         return fail(LWM_UNSUPPORTED, "candidate sharding supports MPPI planners with one iteration");
+    if (p->kind != PlannerKind::Mppi) {
+        const uint32_t K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
+        if (K > p->S)
+            return fail(LWM_INVALID_ARGUMENT, "every shard needs at least `elites` (" + std::to_string(K) +
+                                                  ") candidates, this one has " + std::to_string(p->S));
+    }
     if (static_cast<uint64_t>(sample_base) + p->S > sample_total)
         return fail(LWM_INVALID_ARGUMENT, "shard samples [" + std::to_string(sample_base) + ", " +
                                               std::to_string(static_cast<uint64_t>(sample_base) + p->S) +
                                               ") exceed sample_total " + std::to_string(sample_total));
     p->shard_base = sample_base;
     p->shard_total = sample_total;
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_set_shard_exchange(lwm_planner* p, uint32_t shards, lwm_exchange_fn fn, void* user) {
+    if (!p) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (p->kind == PlannerKind::Mppi)
+        return fail(LWM_INVALID_ARGUMENT, "MPPI shards exchange tuples through lwm_mppi_combine_device");
+    if ((fn == nullptr) != (shards == 0)) return fail(LWM_INVALID_ARGUMENT, "exchange and shard count go together");
+    const uint32_t K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
+    if (fn && static_cast<uint64_t>(shards) * K > 16384)
+        return fail(LWM_UNSUPPORTED, "shards x elites must be at most 16384");
+    std::lock_guard<std::mutex> lock(p->mu);
+    p->exchange = fn;
+    p->exchange_user = user;
+    p->exchange_shards = shards;
     return LWM_OK;
 }
 
@@ -1511,7 +1565,10 @@ lwm_status lwm_mppi_combine_device(lwm_planner* p, const float* tuples, uint32_t
 lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_plan_result* out) {
     if (!p || !sc || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (sc->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
-    if (p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
+    if (p->shard_total && p->kind == PlannerKind::Mppi)
+        return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: use lwm_plan_device_shard");
+    if (p->shard_total && !p->exchange)
+        return fail(LWM_INVALID_ARGUMENT, "CEM / iCEM candidate shards need an elite exchange (lwm_planner_set_shard_exchange)");
     const auto start = std::chrono::steady_clock::now();
     std::lock_guard<std::mutex> lock(p->mu);
     std::lock_guard<std::mutex> lock2(sc->mu);

@@ -3,6 +3,7 @@
 // MPPI with a caller-supplied scorer.  The built-in scorers fuse sampling and
 // the MPPI reduction into their rollout kernels instead (kernels_nominal.cu,
 // kernels_skyjepa.cu).
+#include <algorithm>
 #include <cstdint>
 
 #include "lwm_device.cuh"
@@ -53,13 +54,14 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
         const float inv_std = 1.0f / sqrtf(var / static_cast<float>(a.T) + 1.0e-6f);
         for (uint32_t t = 0; t < a.T; ++t) eps[t] *= inv_std;
     }
-    const bool carried = a.carried && s >= 1 && s <= a.inject;
+    const uint32_t g = a.sample_base + s;  // the candidate's row in the (unsharded) plan
+    const bool carried = a.carried && g >= 1 && g <= a.inject;
     const float lo = a.low[act], hi = a.high[act];
     for (uint32_t t = 0; t < a.T; ++t) {
         const size_t mi = (static_cast<size_t>(b) * a.T + t) * a.A + act;
         float v;
         if (carried) {
-            v = a.carried[((static_cast<size_t>(b) * a.carried_count + (s - 1)) * a.T + t) * a.A + act];
+            v = a.carried[((static_cast<size_t>(b) * a.carried_count + (g - 1)) * a.T + t) * a.A + act];
         } else {
             v = (a.sample_base + s == 0) ? a.mean[mi] : __fadd_rn(a.mean[mi], __fmul_rn(eps[t], a.std[mi]));
             v = cmin(cmax(v, lo), hi);
@@ -135,9 +137,12 @@ __global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
     const uint32_t TA = a.T * a.A;
     const size_t seq = static_cast<size_t>(b) * TA;
     const float* cb = a.cand + static_cast<size_t>(b) * a.S * TA;
+    const uint32_t* imap = a.index_map ? a.index_map + static_cast<size_t>(b) * a.S : nullptr;
     if (a.elite_index)
-        for (uint32_t j = threadIdx.x; j < a.K; j += blockDim.x)
-            a.elite_index[static_cast<size_t>(b) * a.K + j] = static_cast<uint32_t>(s_keys[j]);
+        for (uint32_t j = threadIdx.x; j < a.K; j += blockDim.x) {
+            const uint32_t i = static_cast<uint32_t>(s_keys[j]);
+            a.elite_index[static_cast<size_t>(b) * a.K + j] = imap ? imap[i] : i;
+        }
     const float inv_k = a.inv_k, inv_km1 = a.inv_km1;
     const uint32_t best = static_cast<uint32_t>(s_keys[0]);
     for (uint32_t e = threadIdx.x; e < TA; e += blockDim.x) {
@@ -181,8 +186,53 @@ __global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
         }
     }
     if (threadIdx.x == 0) {
-        a.best_index[b] = best;
+        a.best_index[b] = imap ? imap[best] : best;
         a.best_score[b] = key_score(s_keys[0]);
+    }
+}
+
+// ------------------------------------------ candidate shards of CEM / iCEM
+//
+// A shard's lowest `K` candidates (the order of lowest_score_indices) as
+// tuples [B][K][2 + T*A]: score, global candidate index (bits), actions.
+// The union of every shard's tuples holds the plan's global elites, and
+// sorting the union by (score, position) with positions in shard order gives
+// the (score, global index) order of the unsharded selection.
+__global__ void __launch_bounds__(1024) elite_tuples_kernel(const float* scores, const float* cand, uint32_t S,
+                                                            uint32_t sort_len, uint32_t K, uint32_t TA,
+                                                            uint32_t base, float* out) {
+    extern __shared__ uint64_t s_keys[];
+    const uint32_t b = blockIdx.x, W = 2 + TA;
+    for (uint32_t i = threadIdx.x; i < sort_len; i += blockDim.x)
+        s_keys[i] = i < S ? score_key(scores[static_cast<size_t>(b) * S + i], i) : ~0ull;
+    __syncthreads();
+    bitonic_sort_keys(s_keys, sort_len);
+    for (uint32_t q = threadIdx.x; q < K * W; q += blockDim.x) {
+        const uint32_t j = q / W, f = q % W, idx = static_cast<uint32_t>(s_keys[j]);
+        const size_t row = static_cast<size_t>(b) * S + idx;
+        const float v = f == 0 ? scores[row] : (f == 1 ? __uint_as_float(base + idx) : cand[row * TA + f - 2]);
+        out[(static_cast<size_t>(b) * K + j) * W + f] = v;
+    }
+}
+
+// gathered [G][B][K][W] (shard-major) -> merged scores [B][G*K], candidates
+// [B][G*K][T*A] and global indices [B][G*K].
+__global__ void __launch_bounds__(256) elite_merge_kernel(const float* gathered, uint32_t G, uint32_t B, uint32_t K,
+                                                          uint32_t TA, float* scores, float* cand, uint32_t* index) {
+    const uint32_t W = 2 + TA;
+    const uint64_t total = static_cast<uint64_t>(G) * B * K * W;
+    for (uint64_t e = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t f = static_cast<uint32_t>(e % W);
+        uint64_t r = e / W;
+        const uint32_t k = static_cast<uint32_t>(r % K);
+        r /= K;
+        const uint32_t b = static_cast<uint32_t>(r % B), sh = static_cast<uint32_t>(r / B);
+        const size_t m = static_cast<size_t>(b) * G * K + static_cast<size_t>(sh) * K + k;
+        const float v = gathered[e];
+        if (f == 0) scores[m] = v;
+        else if (f == 1) index[m] = __float_as_uint(v);
+        else cand[m * TA + f - 2] = v;
     }
 }
 
@@ -272,6 +322,26 @@ cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t strea
     }
     const uint32_t threads = a.sort_len < 1024 ? (a.sort_len < 64 ? 64 : a.sort_len) : 1024;
     topk_refit_kernel<<<B, threads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_elite_tuples(const float* scores, const float* cand, uint32_t B, uint32_t S, uint32_t K,
+                                uint32_t TA, uint32_t base, float* out, cudaStream_t stream) {
+    const uint32_t len = sort_length(S);
+    const size_t smem = static_cast<size_t>(len) * sizeof(uint64_t);
+    if (smem > 200 * 1024 || K > S) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(elite_tuples_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    elite_tuples_kernel<<<B, 1024, smem, stream>>>(scores, cand, S, len, K, TA, base, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_elite_merge(const float* gathered, uint32_t G, uint32_t B, uint32_t K, uint32_t TA, float* scores,
+                               float* cand, uint32_t* index, cudaStream_t stream) {
+    const uint64_t total = static_cast<uint64_t>(G) * B * K * (2 + TA);
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 16));
+    elite_merge_kernel<<<blocks, 256, 0, stream>>>(gathered, G, B, K, TA, scores, cand, index);
     return cudaGetLastError();
 }
 

@@ -68,6 +68,7 @@ struct RefitArgs {
     uint32_t* best_index;  // [B]
     float* best_score;     // [B]
     float* elite_mean_out; // [B,T,A] elite mean before the momentum update, or nullptr
+    const uint32_t* index_map;  // [B,S] candidate -> reported index (merged shard elites), or nullptr
 };
 
 // SkyJepaDomain (src/skyjepa_sim.rs:28-40) as laid out on the device.
@@ -185,6 +186,12 @@ cudaError_t launch_mppi_combine(const MppiArgs& m, const float* tuples, uint32_t
                                 cudaStream_t stream);
 uint32_t sort_length(uint32_t S);
 cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream);
+// A CEM / iCEM shard's lowest K candidates as tuples [B][K][2 + TA] (score,
+// global index bits, actions), and the merge of every shard's tuples.
+cudaError_t launch_elite_tuples(const float* scores, const float* cand, uint32_t B, uint32_t S, uint32_t K,
+                                uint32_t TA, uint32_t base, float* out, cudaStream_t stream);
+cudaError_t launch_elite_merge(const float* gathered, uint32_t G, uint32_t B, uint32_t K, uint32_t TA, float* scores,
+                               float* cand, uint32_t* index, cudaStream_t stream);
 cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint32_t S, uint32_t K,
                             cudaStream_t stream);
 cudaError_t launch_color_noise(const float* in, float* out, uint32_t B, uint32_t S, uint32_t T, uint32_t A,

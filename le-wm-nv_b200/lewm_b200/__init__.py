@@ -277,6 +277,7 @@ class _PlanDeviceResult(C.Structure):
 
 
 SCORE_FN = C.CFUNCTYPE(C.c_int, VP, VP, U32, U32, U32, U32, VP, VP)
+EXCHANGE_FN = C.CFUNCTYPE(C.c_int, VP, VP, C.c_size_t, VP, VP)
 
 # ------------------------------------------------------------- signatures
 
@@ -348,6 +349,7 @@ _sig("lwm_icem_trace_device", C.c_int, VP, VP, VP, C.POINTER(_PlanDeviceResult),
 _sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
 _sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
+_sig("lwm_planner_set_shard_exchange", C.c_int, VP, U32, EXCHANGE_FN, VP)
 _sig("lwm_skyjepa_tensor_info", C.c_size_t, C.POINTER(SkyJepaConfig), C.c_size_t, C.POINTER(_TensorInfo))
 _sig("lwm_lewm_tensor_info", C.c_size_t, C.POINTER(LewmConfig), I32, C.c_size_t, C.POINTER(_TensorInfo))
 _sig("lwm_skyjepa_weights_from_safetensors", C.c_int, C.POINTER(SkyJepaConfig), C.c_char_p, C.c_char_p, FP,
@@ -866,6 +868,26 @@ class _Planner:
         return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
                                 r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
                                 _OUTCOME[r.deadline_outcome])
+
+    def set_shard_exchange(self, shards: int, exchange: Optional[Callable[[int, int, int, int], None]]) -> None:
+        """CEM / iCEM shards: `exchange(local_ptr, count, gathered_ptr, stream)`
+        all-gathers `count` floats of device memory from every shard (in
+        sample-range order) into `gathered_ptr`, on `stream`.  None clears it."""
+        if exchange is None:
+            self._exchange_cb = None
+            _check(lib.lwm_planner_set_shard_exchange(self.handle, 0, None, None))
+            return
+
+        def call(_user, local, count, gathered, stream):
+            try:
+                exchange(int(local or 0), int(count), int(gathered or 0), int(stream or 0))
+                return 0
+            except Exception:  # reported to the planner as a failed exchange
+                import traceback
+                traceback.print_exc()
+                return 1
+        self._exchange_cb = EXCHANGE_FN(call)
+        _check(lib.lwm_planner_set_shard_exchange(self.handle, shards, self._exchange_cb, None))
 
     def last_candidates_ptr(self) -> int:
         p = VP()

@@ -152,3 +152,18 @@ class FleetPlanner:
     def close(self) -> None:
         self.planner.close()
 
+
+
+def nccl_elite_exchange(ctx, group, shards: int):
+    """The exchange of CEM / iCEM candidate shards (IcemPlanner.set_shard_exchange)
+    as one NCCL all-gather over `group` on the context's stream."""
+    import torch
+    import torch.distributed as dist
+    from . import device_tensor
+
+    def exchange(local_ptr, count, gathered_ptr, _stream):
+        src = device_tensor(local_ptr, (count,))
+        dst = device_tensor(gathered_ptr, (shards * count,))
+        with torch.cuda.stream(ctx.torch_stream()):
+            dist.all_gather_into_tensor(dst, src, group=group)
+    return exchange
