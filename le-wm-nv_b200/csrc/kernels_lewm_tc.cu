@@ -13,9 +13,12 @@
 //   accumulator and commits each stage to an mbarrier that releases it; the
 //   next block's loads run while the tensor core works on this one.
 // The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32 (w % 4) .. +31 = rows, w / 4 picks the column half).  Split-K parks f32
-// partial tiles and the last CTA of a tile adds them in split order, as the
-// f32 GEMM does.  Every mbarrier wait is bounded and reports through err.
+// 32 (w % 4) .. +31 = rows, w / 4 picks the column half) into a shared-memory
+// tile, then writes it a warp per row so that C, the gate table and the
+// output move in whole cache lines.  Split-K writes each split's tile to a
+// [splits][M][N] partial buffer and splitk_reduce_kernel adds them in split
+// order (deterministic) with the epilogue.  Every mbarrier wait is bounded
+// and reports through err.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -31,7 +34,9 @@ namespace {
 
 constexpr uint32_t kTM = 128, kTN = 128, kTK = 64;
 constexpr uint32_t kStageA = kTM * kTK * 2, kStageB = kTN * kTK * 2;  // 16 KB each
-constexpr uint32_t kTcSmem = 2 * (kStageA + kStageB) + 1024 + 64;
+constexpr uint32_t kTileLd = 132;  // f32 row stride of the staged output tile (float4-aligned, fewer bank conflicts)
+constexpr uint32_t kStageBytes = 2 * (kStageA + kStageB) > kTM * kTileLd * 4 ? 2 * (kStageA + kStageB) : kTM * kTileLd * 4;
+constexpr uint32_t kTcSmem = kStageBytes + 1024 + 64;
 constexpr int kSiteStage = 21, kSiteFinal = 22;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -44,7 +49,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                    // [2][128 rows x 128 B]
     uint8_t* sB = smem + 2 * kStageA;      // [2][128 rows x 128 B]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * (kStageA + kStageB));  // stage[2], final
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStageBytes);  // stage[2], final
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
@@ -138,68 +143,58 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
     tc::mbar_wait(&bars[2], 0, err, kSiteFinal, static_cast<int>(nblk));
     tc::fence_after();
 
+    // accumulator -> shared-memory tile (the stage buffers are free now)
     const uint32_t q = warp & 3u, half = warp >> 2;
-    const uint32_t row = q * 32u + lane, m = m0 + row;
+    const uint32_t row = q * 32u + lane;
     const uint32_t lane_addr = tmem + ((q * 32u) << 16);
-    if (g.splits <= 1) {
+    float* stile = reinterpret_cast<float*>(smem);  // [128][kTileLd]
 #pragma unroll 1
-        for (uint32_t c = 0; c < 4; ++c) {
-            const uint32_t col0 = half * 64u + c * 16u;
-            if (col0 >= n_tile) break;
-            float v[16];
-            tc::tmem_ld16(lane_addr + col0, v);
-            tc::tmem_ld_wait();
-            if (m < g.M) {
+    for (uint32_t c = 0; c < 4; ++c) {
+        const uint32_t col0 = half * 64u + c * 16u;
+        if (col0 >= n_mma) break;
+        float v[16];
+        tc::tmem_ld16(lane_addr + col0, v);
+        tc::tmem_ld_wait();
+        float4* dst = reinterpret_cast<float4*>(stile + row * kTileLd + col0);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const uint32_t n = n0 + col0 + static_cast<uint32_t>(e);
-                    if (n < g.N) {
-                        float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
-                        *cp = epilogue_value(g, m, n, v[e], cp);
-                    }
-                }
-            }
-        }
-    } else {
-        const size_t tile = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
-        float* mine = g.partial + (tile * g.splits + blockIdx.z) * (kTM * kTN);
-#pragma unroll 1
-        for (uint32_t c = 0; c < 4; ++c) {
-            const uint32_t col0 = half * 64u + c * 16u;
-            if (col0 >= n_tile) break;
-            float v[16];
-            tc::tmem_ld16(lane_addr + col0, v);
-            tc::tmem_ld_wait();
-            float4* dst = reinterpret_cast<float4*>(mine + row * kTN + col0);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
-        }
+        for (int e = 0; e < 4; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
     }
     tc::fence_before();
     __syncthreads();
     if (warp == 0) tc::tmem_free(tmem, 128);
-    if (g.splits <= 1) return;
-
-    // split-K: the last split of the tile to arrive adds the partial tiles in
-    // split order (deterministic) and runs the epilogue
-    __threadfence();
-    __shared__ int s_last;
-    const size_t tile = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
-    if (tid == 0) s_last = atomicAdd(&g.counters[tile], 1u) == g.splits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float* parts = g.partial + tile * g.splits * (kTM * kTN);
-    for (uint32_t idx = tid; idx < kTM * kTN; idx += 256u) {
-        const uint32_t r = idx / kTN, col = idx % kTN;
-        const uint32_t mm = m0 + r, n = n0 + col;
-        if (mm >= g.M || col >= n_tile) continue;
-        float v = 0.0f;
-        for (uint32_t z = 0; z < g.splits; ++z) v += __ldcg(parts + z * (kTM * kTN) + idx);
-        float* cp = g.C + static_cast<size_t>(mm) * g.ldc + n;
-        *cp = epilogue_value(g, mm, n, v, cp);
+    // tile -> global, a warp per row, consecutive columns per lane: the
+    // epilogue (or the split's partial) is written, and C / the gate read,
+    // in whole cache lines
+    const bool split = g.splits > 1;
+    float* part = split ? g.partial + static_cast<size_t>(blockIdx.z) * g.M * g.N : nullptr;
+    for (uint32_t r = warp; r < kTM; r += 8u) {
+        const uint32_t m = m0 + r;
+        if (m >= g.M) break;
+        for (uint32_t col = lane; col < n_tile; col += 32u) {
+            const uint32_t n = n0 + col;
+            const float v = stile[r * kTileLd + col];
+            if (split) {
+                part[static_cast<size_t>(m) * g.N + n] = v;
+            } else {
+                float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
+                *cp = epilogue_value(g, m, n, v, cp);
+            }
+        }
     }
-    if (tid == 0) g.counters[tile] = 0u;
+}
+
+// Split-K: C = epilogue(sum over the splits' partials [splits][M][N], in
+// split order), one thread per output (coalesced; every SM takes part).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(GemmArgs g) {
+    const uint64_t total = static_cast<uint64_t>(g.M) * g.N, plane = total;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t m = static_cast<uint32_t>(i / g.N), n = static_cast<uint32_t>(i % g.N);
+        float v = 0.0f;
+        for (uint32_t z = 0; z < g.splits; ++z) v += __ldcg(g.partial + z * plane + i);
+        float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
+        *cp = epilogue_value(g, m, n, v, cp);
+    }
 }
 
 }  // namespace
@@ -228,18 +223,20 @@ cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch*
     if (sp && sp->partial && tiles < 148 && g.K >= 2 * 2 * kTK) {
         splits = static_cast<uint32_t>((148 + tiles - 1) / tiles);
         splits = min(splits, min(16u, g.K / (2 * kTK)));
-        while (splits > 1 && tiles * splits * kTM * kTN > sp->floats) --splits;
-        if (tiles > sp->n_counters) splits = 1;
+        while (splits > 1 && static_cast<size_t>(splits) * g.M * g.N > sp->floats) --splits;
     }
     g.splits = splits;
     g.k_chunk = splits > 1 ? ((g.K + splits - 1) / splits + kTK - 1) / kTK * kTK : g.K;
     if (splits > 1) {
         g.splits = (g.K + g.k_chunk - 1) / g.k_chunk;  // no empty split
         g.partial = sp->partial;
-        g.counters = sp->counters;
     }
     dim3 grid(tx, ty, g.splits);
     gemm_tc_kernel<<<grid, 256, kTcSmem, stream>>>(g, err);
+    if ((e = cudaGetLastError()) != cudaSuccess || g.splits <= 1) return e;
+    const uint64_t total = static_cast<uint64_t>(g.M) * g.N;
+    splitk_reduce_kernel<<<static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 8)), 256, 0, stream>>>(g);
+    if (sp->extra_launches) ++*sp->extra_launches;
     return cudaGetLastError();
 }
 

@@ -288,6 +288,7 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
     float *f_y = base + o_y, *f_qkv = base + o_qkv, *f_att = base + o_att, *f_f = base + o_f;
     float *f_last = base + o_last, *f_po = base + o_po, *f_p1 = base + o_p1, *f_pred = base + o_pred;
     int n = 0;
+    split_launches = 0;
     const uint32_t rows_all = static_cast<uint32_t>(all);
     // ActionEmbedder over every (sample, time) token (modules.rs:150-158)
     LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
@@ -388,7 +389,7 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
     LWM_CU(launch_goal_cost(f_pred, goal, S, bs, D, scores, s));
     ++n;
     if (last_emb) LWM_CU(cudaMemcpyAsync(last_emb, f_pred, bs * D * sizeof(float), cudaMemcpyDeviceToDevice, s));
-    launches = n;
+    launches = n + split_launches;
     return cudaSuccess;
 }
 
@@ -399,6 +400,7 @@ cudaError_t LewmModel::encode_vector(const float* obs, uint32_t n, float* out, c
     LWM_CU(enc.ensure(static_cast<size_t>(2) * n * oh));
     float *a = enc.ptr, *b = enc.ptr + static_cast<size_t>(n) * oh;
     int k = 0;
+    split_launches = 0;
     LWM_CU(gemm_f32(sp, gemm(obs, c.obs_dim, w.enc_lin[0], a, oh, n), s));
     ++k;
     for (uint32_t j = 0; j + 1 < c.obs_depth; ++j) {
@@ -414,7 +416,7 @@ cudaError_t LewmModel::encode_vector(const float* obs, uint32_t n, float* out, c
         }
     }
     LWM_CU(gemm_f32(sp, gemm(a, oh, w.enc_lin[c.obs_depth - 1], out, c.embed_dim, n), s));
-    launches = k + 1;
+    launches = k + 1 + split_launches;
     return cudaSuccess;
 }
 
@@ -435,6 +437,7 @@ cudaError_t LewmModel::encode_pixels_body(const float* pix, uint32_t n, float* o
     float *f_att = e + o_att, *f_f = e + o_f, *f_cls = e + o_cls, *f_ph = e + o_ph;
     const uint32_t rows = n * t;
     int k = 0;
+    split_launches = 0;
     LWM_CU(launch_patchify(pix, f_patch, n, c.channels, c.image_size, p, s));
     LWM_CU(gemm_f32(sp, gemm(f_patch, kdim, w.patch, f_pe, vh, n * np), s));
     LWM_CU(launch_vit_assemble(f_pe, w.cls, w.vpos, f_x, n, np, vh, s));
@@ -460,7 +463,7 @@ cudaError_t LewmModel::encode_pixels_body(const float* pix, uint32_t n, float* o
     LWM_CU(launch_layernorm(f_x, f_cls, n, vh, t, 0, w.vit_norm.w, w.vit_norm.b, c.vit_eps, s));
     ++k;
     LWM_CU(mlp(sp, w.projector, f_cls, n, f_ph, out, s, k));
-    launches = k;
+    launches = k + split_launches;
     return cudaSuccess;
 }
 
@@ -479,6 +482,7 @@ cudaError_t LewmModel::ensure_split() {
     LWM_CU(cudaMemset(split.counters, 0, kCounters * sizeof(unsigned int)));
     split.floats = kPartial;
     split.n_counters = kCounters;
+    split.extra_launches = &split_launches;
     return cudaSuccess;
 }
 

@@ -49,6 +49,7 @@ struct SplitScratch {
     unsigned int* counters = nullptr;  // zero between GEMMs (the last CTA of a tile resets its counter)
     size_t n_counters = 0;
     int* tc_err = nullptr;             // error word of the tensor-core GEMM's bounded waits (4 ints)
+    int* extra_launches = nullptr;     // counts the split-K reduce launches of the tensor-core GEMM
 };
 
 // Launches C = A W^T (+ epilogue); splits K over CTAs (deterministically) when
@@ -165,6 +166,7 @@ struct LewmModel {
     SplitScratch split;     // split-K partial tiles
     GraphCache g_score, g_enc;
     int launches = 0;
+    int split_launches = 0;  // split-K reduce kernels of the current launch sequence
     ~LewmModel();
     cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_pixels_body(const float* pixels, uint32_t n, float* out, cudaStream_t s);
