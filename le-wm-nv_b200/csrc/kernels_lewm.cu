@@ -172,6 +172,12 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
 // Per-row LayerNorm statistics over d elements held by one warp (x in global
 // or shared memory): mean = sum / d, var = sum((x - mean)^2) / d.
 __device__ __forceinline__ void row_stats(const float* x, uint32_t d, float& mean, float& den, float eps) {
@@ -371,6 +377,90 @@ __global__ void attention_kernel(const float* qkv, float* out, uint32_t seqs, ui
     }
 }
 
+// The same attention for long sequences (the ViT's 197 tokens): a block per
+// (sequence, head, 32 queries) keeps the head's K (rows padded to dh + 1, so
+// the lanes' different rows hit different banks) and V in shared memory; a
+// warp takes one query at a time, its lanes score 32 keys in parallel, the
+// softmax is a warp max / sum, and each lane then accumulates its own output
+// dimensions over the keys.
+constexpr uint32_t kAttnQ = 32, kAttnMaxT = 256;
+
+__global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, float* out, uint32_t t, uint32_t H,
+                                                             uint32_t dh, float scale, int causal, int scale_q_first) {
+    extern __shared__ float sm[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t h = blockIdx.y, q0 = blockIdx.x * kAttnQ;
+    const size_t s = blockIdx.z;
+    const uint32_t inner = H * dh, kld = dh + 1;
+    float* Ks = sm;                  // [t][dh + 1]
+    float* Vs = Ks + t * kld;        // [t][dh]
+    float* Ps = Vs + t * dh;         // [8][t]
+    float* Qs = Ps + 8 * t;          // [8][dh]
+    const float* base = qkv + s * t * 3 * inner;
+    for (uint32_t idx = threadIdx.x; idx < t * dh; idx += blockDim.x) {
+        const uint32_t j = idx / dh, d = idx % dh;
+        const float* row = base + static_cast<size_t>(j) * 3 * inner + h * dh + d;
+        Ks[j * kld + d] = row[inner];
+        Vs[j * dh + d] = row[2 * inner];
+    }
+    __syncthreads();
+    float* p = Ps + warp * t;
+    float* qv = Qs + warp * dh;
+    for (uint32_t qi = warp; qi < kAttnQ; qi += 8) {
+        const uint32_t i = q0 + qi;
+        if (i >= t) break;
+        const float* q = base + static_cast<size_t>(i) * 3 * inner + h * dh;
+        for (uint32_t d = lane; d < dh; d += 32) qv[d] = scale_q_first ? q[d] * scale : q[d];
+        __syncwarp();
+        const uint32_t jmax = causal ? i + 1 : t;
+        float sc[kAttnMaxT / 32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (uint32_t r = 0; r < kAttnMaxT / 32; ++r) {
+            const uint32_t j = r * 32 + lane;
+            float acc = -INFINITY;
+            if (j < jmax) {
+                const float* kr = Ks + j * kld;
+                acc = 0.0f;
+                for (uint32_t d = 0; d < dh; ++d) acc = fmaf(qv[d], kr[d], acc);
+                if (!scale_q_first) acc *= scale;
+            }
+            sc[r] = acc;
+            mx = fmaxf(mx, acc);
+        }
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll
+        for (uint32_t r = 0; r < kAttnMaxT / 32; ++r) {
+            const uint32_t j = r * 32 + lane;
+            if (j < jmax) {
+                const float e = expf(sc[r] - mx);
+                p[j] = e;
+                sum += e;
+            }
+        }
+        sum = warp_sum(sum);
+        __syncwarp();
+        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (uint32_t j = 0; j < jmax; ++j) {
+            const float w = p[j];
+            const float* vr = Vs + j * dh;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t d = lane + 32 * u;
+                if (d < dh) o[u] = fmaf(w, vr[d], o[u]);
+            }
+        }
+        float* orow = out + (s * t + i) * inner + h * dh;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t d = lane + 32 * u;
+            if (d < dh) orow[d] = o[u] / sum;
+        }
+        __syncwarp();
+    }
+}
+
 // Goal cost (goal_cost, model.rs:149-165): sum_d (pred - goal[r / S])^2.
 __global__ void goal_cost_kernel(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
                                  float* scores) {
@@ -479,6 +569,15 @@ cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32
                              float scale, int causal, int scale_q_first, cudaStream_t s) {
     const size_t warps = static_cast<size_t>(seqs) * H * t;
     if (!warps) return cudaSuccess;
+    const size_t smem = (static_cast<size_t>(t) * (2 * dh + 1) + 8 * t + 8 * dh) * sizeof(float);
+    if (t > 32 && t <= kAttnMaxT && dh <= 128 && smem <= 200 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attention_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        attention_smem_kernel<<<dim3((t + kAttnQ - 1) / kAttnQ, H, seqs), 256, smem, s>>>(qkv, out, t, H, dh, scale,
+                                                                                          causal, scale_q_first);
+        return cudaGetLastError();
+    }
     attention_kernel<<<blocks_for(warps, 8), 256, 0, s>>>(qkv, out, seqs, t, H, dh, scale, causal, scale_q_first);
     return cudaGetLastError();
 }

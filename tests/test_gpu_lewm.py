@@ -91,6 +91,21 @@ def test_small_vit_encoder_matches_oracle(ctx):
     np.testing.assert_allclose(out.cpu().numpy(), O.LewmModel(cfg, wts).encode_pixels(pix), rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("image,patch", [(64, 8), (128, 8)])
+def test_long_sequence_vit_attention_matches_oracle(ctx, image, patch):
+    # 65 and 257 tokens: the shared-memory attention kernel (> 32 tokens; 257
+    # exceeds its 256-token bound and takes the warp-per-query kernel)
+    cfg = small_vit()
+    cfg.image_size, cfg.patch_size = image, patch
+    wts = cfg.random_weights(12)
+    sc = L.LewmScorer(ctx, cfg, wts)
+    pix = np.random.default_rng(6).standard_normal((2, 3, image, image)).astype(np.float32)
+    with torch.cuda.stream(ctx.torch_stream()):
+        out = sc.encode_pixels(torch.as_tensor(pix).cuda())
+    ctx.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), O.LewmModel(cfg, wts).encode_pixels(pix), rtol=1e-4, atol=1e-4)
+
+
 def test_image_pipeline_matches_oracle(ctx):
     # c4 model in f32: NV12 -> preprocess -> ViT-Tiny -> projector; then 64 candidates x 10 steps
     w = W.lewm_image(seed=4, samples=64)
