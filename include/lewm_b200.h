@@ -772,6 +772,57 @@ float lwm_skyjepa_session_trim_scale(const lwm_skyjepa_session* session);
 lwm_status lwm_skyjepa_shifted_residual(const float* sequence, const float* prior, uint32_t horizon,
                                         uint32_t action_dim, float limit, float* out);
 
+/* ---------------------------------------------------------------- fleet loop */
+
+/* The control loop of a fleet on the device, without host round trips per
+ * control step.  Per step: lwm_fleet_control_step_device writes the scorer
+ * context (commit_observation's history shift, the reference window, the
+ * geometric prior as reference actions) into the learned scorer's context
+ * buffers (lwm_scorer_skyjepa_context_device) and the prior into the
+ * planner's warm start (lwm_planner_set_warm_start_device, a fresh-prior
+ * warm start as SkyJepaControllerSession::plan_internal uses,
+ * src/models/skyjepa/session.rs:322-400), lwm_plan_device plans, and
+ * lwm_rotor_plant_step_device advances every vehicle's plant with the plan's
+ * first action.  All calls are asynchronous on the context's stream. */
+typedef struct lwm_fleet_step {
+    uint32_t batch;
+    uint32_t horizon;
+    uint32_t history;            /* state history steps (>= 2) */
+    float time;                  /* time of the current state */
+    float dt;
+    int32_t reference_kind;      /* 0 hover, 1 circle, 2 figure-eight */
+    float radius;
+    float period;
+    lwm_domain prior_domain;     /* the controller's nominal domain (SkyJepaDomain::default) */
+    const float* trim;           /* device [B] trim scale per vehicle, or NULL (1) */
+    const float* state;          /* device [B,18]: the state each plant reached */
+    const float* last_action;    /* device, the executed action per vehicle (row stride below),
+                                    or NULL on the first step (no history shift) */
+    uint32_t last_action_stride;
+    float* state_history;        /* device [B,history,18], in/out */
+    float* action_history;       /* device [B,history-1,4], in/out */
+    float* reference_states;     /* device [B,horizon,18], out */
+    float* reference_actions;    /* device [B,horizon,4], out: the prior (trim-scaled, clamped) */
+} lwm_fleet_step;
+lwm_status lwm_fleet_control_step_device(lwm_ctx* ctx, const lwm_fleet_step* step);
+/* SkyJepaRotorPlant::step (src/skyjepa_sim.rs:206-281) for every vehicle:
+ * `substeps` steps of dt with its own domain (device [B] lwm_domain), state
+ * [B,18] and motors [B,4] in place (device), commands read with the given
+ * row stride (device; e.g. a plan's first_action, stride 4). */
+lwm_status lwm_rotor_plant_step_device(lwm_ctx* ctx, const lwm_domain* domains, float* states, float* motors,
+                                       const float* commands, uint32_t command_stride, uint32_t batch,
+                                       float dt, uint32_t substeps);
+/* Device addresses of a learned scorer's context sections (after
+ * lwm_scorer_skyjepa_set_context sized them): state_history [B,H,18],
+ * action_history [B,H-1,4], reference_states [B,T,18], reference_actions
+ * [B,T,4]; valid until the next set_context. */
+lwm_status lwm_scorer_skyjepa_context_device(lwm_scorer* scorer, float** state_history, float** action_history,
+                                             float** reference_states, float** reference_actions);
+/* The warm start from device memory [batch, horizon, action_dim]
+ * (asynchronous on the context's stream). */
+lwm_status lwm_planner_set_warm_start_device(lwm_planner* planner, const float* sequence, uint32_t batch,
+                                             uint32_t horizon, uint32_t action_dim);
+
 /* ---------------------------------------------------------------- checkpoints */
 
 /* Trained weights from safetensors files (the format candle's

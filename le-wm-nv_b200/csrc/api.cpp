@@ -1072,6 +1072,64 @@ lwm_status lwm_planner_set_warm_start(lwm_planner* p, const float* sequence, uin
     return LWM_OK;
 }
 
+lwm_status lwm_planner_set_warm_start_device(lwm_planner* p, const float* sequence, uint32_t batch, uint32_t horizon,
+                                             uint32_t action_dim) {
+    if (!p || !sequence) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> lock(p->mu);
+    if (p->kind == PlannerKind::Cem) return fail(LWM_INVALID_ARGUMENT, "CEM planners have no warm start");
+    if (horizon != p->T || action_dim != p->A || batch == 0)
+        return fail(LWM_INVALID_ARGUMENT, std::string(planner_name(p->kind)) + " warm-start shape [" + std::to_string(batch) + ", " +
+                                              std::to_string(horizon) + ", " + std::to_string(action_dim) + "] does not match expected [B, " +
+                                              std::to_string(p->T) + ", " + std::to_string(p->A) + "]");
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    LWM_TRY(ensure_planner_buffers(p, batch));
+    const size_t bytes = static_cast<size_t>(batch) * horizon * action_dim * 4;
+    LWM_CUDA(cudaMemcpyAsync(p->warm.ptr, sequence, bytes, cudaMemcpyDeviceToDevice, p->ctx->stream));
+    p->has_warm = true;
+    p->warm_batch = batch;
+    return LWM_OK;
+}
+
+lwm_status lwm_fleet_control_step_device(lwm_ctx* ctx, const lwm_fleet_step* st) {
+    if (!ctx || !st) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (!st->state || !st->state_history || !st->action_history || !st->reference_states || !st->reference_actions)
+        return fail(LWM_INVALID_ARGUMENT, "fleet step buffers must be device pointers, not null");
+    if (st->history < 2 || st->horizon == 0 || st->horizon > lwm::kMaxHorizon)
+        return fail(LWM_INVALID_ARGUMENT, "fleet step needs history >= 2 and horizon in [1, 64]");
+    if (st->reference_kind < 0 || st->reference_kind > 2) return fail(LWM_INVALID_ARGUMENT, "unknown reference kind");
+    if (!std::isfinite(st->dt) || st->dt <= 0.0f || !(st->period > 0.0f))
+        return fail(LWM_INVALID_ARGUMENT, "fleet step dt and period must be positive");
+    if (st->last_action && st->last_action_stride < 4) return fail(LWM_INVALID_ARGUMENT, "last_action_stride must be >= 4");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(lwm::launch_fleet_control(*st, ctx->stream));
+    ctx->launches += st->batch ? 1 : 0;
+    return LWM_OK;
+}
+
+lwm_status lwm_rotor_plant_step_device(lwm_ctx* ctx, const lwm_domain* domains, float* states, float* motors,
+                                       const float* commands, uint32_t stride, uint32_t batch, float dt,
+                                       uint32_t substeps) {
+    if (!ctx || !domains || !states || !motors || !commands) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (stride < 4) return fail(LWM_INVALID_ARGUMENT, "command_stride must be >= 4");
+    if (!std::isfinite(dt) || dt <= 0.0f) return fail(LWM_INVALID_ARGUMENT, "plant dt must be finite and positive");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(lwm::launch_plant(domains, states, motors, commands, stride, batch, dt, substeps, ctx->stream));
+    ctx->launches += batch ? 1 : 0;
+    return LWM_OK;
+}
+
+lwm_status lwm_scorer_skyjepa_context_device(lwm_scorer* s, float** state_history, float** action_history,
+                                             float** reference_states, float** reference_actions) {
+    if (!s || s->kind != ScorerKind::Skyjepa) return fail(LWM_INVALID_ARGUMENT, "not a SkyJEPA scorer");
+    if (!s->batch || !s->ctx_dev.ptr) return fail(LWM_INVALID_ARGUMENT, "set the scorer's context first");
+    char* base = s->ctx_dev.as<char>();
+    if (state_history) *state_history = reinterpret_cast<float*>(base + s->off_state_hist);
+    if (action_history) *action_history = reinterpret_cast<float*>(base + s->off_action_hist);
+    if (reference_states) *reference_states = reinterpret_cast<float*>(base + s->off_ref_states);
+    if (reference_actions) *reference_actions = reinterpret_cast<float*>(base + s->off_ref_actions);
+    return LWM_OK;
+}
+
 lwm_status lwm_planner_clear_warm_start(lwm_planner* p) {
     if (!p) return fail(LWM_INVALID_ARGUMENT, "null planner");
     std::lock_guard<std::mutex> lock(p->mu);

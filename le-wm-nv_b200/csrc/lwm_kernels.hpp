@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "../../include/lewm_b200.h"
+
 
 namespace lwm {
 
@@ -197,6 +199,11 @@ cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint
 cudaError_t launch_color_noise(const float* in, float* out, uint32_t B, uint32_t S, uint32_t T, uint32_t A,
                                float smooth, cudaStream_t stream);
 cudaError_t launch_normal_fill(uint64_t seed, uint64_t offset, uint64_t count, float* out, cudaStream_t stream);
+
+// The fleet loop on the device (kernels_fleet_loop.cu).
+cudaError_t launch_fleet_control(const lwm_fleet_step& a, cudaStream_t stream);
+cudaError_t launch_plant(const lwm_domain* domains, float* states, float* motors, const float* commands,
+                         uint32_t stride, uint32_t B, float dt, uint32_t substeps, cudaStream_t stream);
 
 // Number of blocks (MPPI partials per vehicle) the nominal kernel uses.
 uint32_t nominal_blocks_per_vehicle(uint32_t S);

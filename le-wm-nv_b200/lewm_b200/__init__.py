@@ -276,6 +276,14 @@ class _PlanDeviceResult(C.Structure):
                 ("deadline_reached", I32), ("deadline_outcome", I32)]
 
 
+class FleetStep(C.Structure):
+    """lwm_fleet_step: one control step of a fleet on the device (all pointers device addresses)."""
+    _fields_ = [("batch", U32), ("horizon", U32), ("history", U32), ("time", F), ("dt", F), ("reference_kind", I32),
+                ("radius", F), ("period", F), ("prior_domain", Domain), ("trim", VP), ("state", VP),
+                ("last_action", VP), ("last_action_stride", U32), ("state_history", VP), ("action_history", VP),
+                ("reference_states", VP), ("reference_actions", VP)]
+
+
 SCORE_FN = C.CFUNCTYPE(C.c_int, VP, VP, U32, U32, U32, U32, VP, VP)
 EXCHANGE_FN = C.CFUNCTYPE(C.c_int, VP, VP, C.c_size_t, VP, VP)
 
@@ -350,6 +358,10 @@ _sig("lwm_planner_set_shard", C.c_int, VP, U32, U32)
 _sig("lwm_plan_device_shard", C.c_int, VP, VP, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_mppi_combine_device", C.c_int, VP, VP, U32, C.POINTER(_PlanDeviceResult))
 _sig("lwm_planner_set_shard_exchange", C.c_int, VP, U32, EXCHANGE_FN, VP)
+_sig("lwm_fleet_control_step_device", C.c_int, VP, C.POINTER(FleetStep))
+_sig("lwm_rotor_plant_step_device", C.c_int, VP, VP, VP, VP, VP, U32, U32, F, U32)
+_sig("lwm_scorer_skyjepa_context_device", C.c_int, VP, C.POINTER(VP), C.POINTER(VP), C.POINTER(VP), C.POINTER(VP))
+_sig("lwm_planner_set_warm_start_device", C.c_int, VP, VP, U32, U32, U32)
 _sig("lwm_skyjepa_tensor_info", C.c_size_t, C.POINTER(SkyJepaConfig), C.c_size_t, C.POINTER(_TensorInfo))
 _sig("lwm_lewm_tensor_info", C.c_size_t, C.POINTER(LewmConfig), I32, C.c_size_t, C.POINTER(_TensorInfo))
 _sig("lwm_skyjepa_weights_from_safetensors", C.c_int, C.POINTER(SkyJepaConfig), C.c_char_p, C.c_char_p, FP,
@@ -708,6 +720,12 @@ class SkyJepaScorer(Scorer):
         """"f32" (CUDA cores) or "bf16" (tcgen05 tensor cores where the shape allows)."""
         _check(lib.lwm_scorer_skyjepa_set_precision(self.handle, PRECISIONS[precision]))
 
+    def context_device(self):
+        """Device addresses (state_history, action_history, reference_states, reference_actions) of the context."""
+        ptrs = [VP() for _ in range(4)]
+        _check(lib.lwm_scorer_skyjepa_context_device(self.handle, *(C.byref(p) for p in ptrs)))
+        return tuple(int(p.value) for p in ptrs)
+
     def set_context(self, state_history, action_history, reference_states, reference_actions,
                     vehicle_mass=None) -> None:
         """Per-plan context; `vehicle_mass` [B] overrides kinematics.mass per vehicle."""
@@ -846,6 +864,11 @@ class _Planner:
         return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
                                 r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
                                 _OUTCOME[r.deadline_outcome])
+
+    def set_warm_start_device(self, ptr: int, batch: int) -> None:
+        """The warm start from device memory [batch, horizon, action_dim] (on the context stream)."""
+        _check(lib.lwm_planner_set_warm_start_device(self.handle, VP(ptr), batch, self.config.horizon,
+                                                     self.config.action_dim))
 
     # ------------------------------------------------ candidate-range shards
     def set_shard(self, sample_base: int, sample_total: int) -> None:
@@ -1013,6 +1036,20 @@ def preprocess_nv12_device(ctx: Context, y_plane, uv_plane, batch: int, height: 
     cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
     _check(lib.lwm_preprocess_nv12_device(ctx.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), batch, height, width,
                                           cs, C.byref(cfg), history_len, history_slot, int(bf16), VP(_ptr(out))))
+
+
+# --------------------------------------------------------------- fleet loop
+
+def fleet_control_step_device(ctx: Context, step: FleetStep) -> None:
+    """commit_observation + reference window + geometric prior of every vehicle, on the device."""
+    _check(lib.lwm_fleet_control_step_device(ctx.handle, C.byref(step)))
+
+
+def plant_step_device(ctx: Context, domains_ptr: int, states_ptr: int, motors_ptr: int, commands_ptr: int,
+                      command_stride: int, batch: int, dt: float, substeps: int) -> None:
+    """SkyJepaRotorPlant::step x substeps for every vehicle, on the device."""
+    _check(lib.lwm_rotor_plant_step_device(ctx.handle, VP(domains_ptr), VP(states_ptr), VP(motors_ptr),
+                                           VP(commands_ptr), command_stride, batch, F(dt), substeps))
 
 
 # ------------------------------------------------------------ control session
