@@ -314,6 +314,37 @@ def run_fleet(args, rank, world, local_rank):
     def one_plan():
         return fp.plan_device()
 
+    if args.loop:
+        # the whole control step on the device: history shift + references +
+        # prior into the scorer's context, the prior as warm start, the plan,
+        # every vehicle's plant (10 substeps of 5 ms) with its first action
+        nv = v1 - v0
+        p_sh, p_ah, p_rs, p_ra = sc.context_device()
+        raw = np.frombuffer(b"".join(bytes(d) for d in full.domains[sl]), dtype=np.float32).reshape(nv, -1)
+        d_dom = torch.as_tensor(raw.copy()).cuda()
+        d_x = torch.as_tensor(hist[:, -1].copy()).cuda()
+        d_m = torch.as_tensor(np.stack([np.full(4, d.hover_force(), np.float32) for d in full.domains[sl]])).cuda()
+        loop = {"k": 0, "last": None}
+        torch.cuda.synchronize()
+
+        def one_plan():  # noqa: F811 - one control step replaces one plan
+            st = L.FleetStep()
+            st.batch, st.horizon, st.history = nv, T, full.model.history_steps
+            st.time, st.dt = 0.05 * loop["k"], 0.05
+            st.reference_kind, st.radius, st.period = 2, 2.0, 8.0
+            st.prior_domain = L.Domain.default()
+            st.trim, st.state = None, d_x.data_ptr()
+            st.last_action, st.last_action_stride = loop["last"], 4
+            st.state_history, st.action_history, st.reference_states, st.reference_actions = p_sh, p_ah, p_rs, p_ra
+            L.fleet_control_step_device(ctx, st)
+            fp.planner.set_warm_start_device(p_ra, nv)
+            r = fp.plan_device()
+            L.plant_step_device(ctx, d_dom.data_ptr(), d_x.data_ptr(), d_m.data_ptr(), r.first_action, 4, nv,
+                                0.005, 10)
+            loop["k"] += 1
+            loop["last"] = r.first_action
+            return r
+
     for _ in range(args.warmup):
         one_plan()
     ctx.synchronize()
@@ -372,8 +403,10 @@ def run_fleet(args, rank, world, local_rank):
                     "unit": "TFLOP/s", "frac": round(achieved / (sgemm * world), 4), "traffic": None,
                     "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run, x n_gpus"}
         result = {
-            "metric": f"fleet plan steps/s ({V} vehicles x {S} candidates x {T} steps per step); "
-                      "candidate-steps/s alongside",
+            "metric": (f"fleet closed-loop control steps/s ({V} vehicles: context, warm start, plan of {S} "
+                       f"candidates x {T} steps, 10 plant substeps per step, all on the device)" if args.loop else
+                       f"fleet plan steps/s ({V} vehicles x {S} candidates x {T} steps per step); "
+                       "candidate-steps/s alongside"),
             "value": round(plans_per_s, 4),
             "unit": "fleet plans/s",
             "n_gpus": world,
@@ -892,6 +925,8 @@ def main():
     ap.add_argument("--vehicles", type=int, default=256)
     ap.add_argument("--samples", type=int, default=4096)
     ap.add_argument("--horizon", type=int, default=30)
+    ap.add_argument("--loop", action="store_true",
+                    help="fleet: time whole control steps on the device (context, warm start, plan, plant)")
     ap.add_argument("--precision", choices=["f32", "bf16"], default=None,
                     help="fleet and lewm-image: bf16 weights on the tensor cores (their default) or f32; "
                          "lewm-vector: f32 (default) or bf16")
