@@ -42,6 +42,10 @@ FLOP_PER_CANDIDATE_STEP = {
     "nominal": 10 * 262 + 60,
 }
 FLOP_PER_CANDIDATE_STEP["fleet"] = FLOP_PER_CANDIDATE_STEP["skyjepa"]
+# DRAM bytes of one rollout launch of the default workload (512 x 15, latent
+# 256), from the ncu capture summarised under profiles/: the weight blob read
+# once, nothing written back but the scores and the MPPI tuple
+ROLLOUT_DRAM_BYTES = {"skyjepa": 2178048 + 0}
 
 
 def percentile(values, q):
@@ -258,7 +262,11 @@ def run_ours(args, rank, world, local_rank):
                                    "p95": round(percentile(e2e_times, 0.95), 5)}},
             "gpu_launches": int(launches * args.steps),
             "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2),
-                         "unit": "TFLOP/s", "frac": round(achieved / sgemm, 4), "traffic": None,
+                         "unit": "TFLOP/s", "frac": round(achieved / sgemm, 4),
+                         "traffic": ROLLOUT_DRAM_BYTES.get(kind),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the "
+                                           "same workload (cold cache), profiles/skyjepa_rollout_f32_512x15.md"
+                                           if kind in ROLLOUT_DRAM_BYTES else None,
                          "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
                          "note": "achieved = algorithmic FLOP per plan / p50 plan time (both kernels)"},
             "clocks": clocks.summary(),
