@@ -183,7 +183,9 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
-__global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h0) {
+// Wide encoders (>= 64 channels): a warp per output channel, the lanes over
+// the (input channel, tap) weights of that channel (coalesced weight rows).
+__global__ void __launch_bounds__(256) skyjepa_h0_warp_kernel(SkyjepaArgs a, float* h0) {
     extern __shared__ float sh[];
     const uint32_t b = blockIdx.x, tid = threadIdx.x, Hs = a.Hs, warp = tid >> 5, lane = tid & 31;
     const uint32_t nwarps = blockDim.x >> 5;
@@ -263,12 +265,80 @@ __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h
     }
 }
 
+// Narrow encoders: one CTA per vehicle, every convolution a thread per (output channel,
+// position) over the vehicle's [C][Hs] activations in shared memory; the
+// threads of one channel read the same weights (L1 broadcast) and the
+// taps run in (input channel, tap) order.
+__global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h0) {
+    extern __shared__ float sh[];
+    const uint32_t b = blockIdx.x, tid = threadIdx.x, Hs = a.Hs, nt = blockDim.x;
+    const TcnView& tcn = a.state_tcn;
+    const uint32_t C = tcn.max_ch, K = tcn.k;
+    float* cur = sh;                 // [C][Hs]
+    float* h1 = cur + C * Hs;        // [C][Hs]
+    float* h2 = h1 + C * Hs;         // [C][Hs]
+    for (uint32_t q = tid; q < 18 * Hs; q += nt) {
+        const uint32_t i = q / Hs, t = q % Hs;
+        const float v = a.state_hist[(static_cast<size_t>(b) * Hs + t) * 18 + i];
+        cur[i * Hs + t] = (v - a.state_mean[i]) / a.state_std[i];
+    }
+    __syncthreads();
+    for (uint32_t l = 0; l < tcn.levels; ++l) {
+        const TcnBlockView& bk = tcn.blocks[l];
+        for (int conv = 0; conv < 2; ++conv) {
+            const float* src = conv == 0 ? cur : h1;
+            float* dst = conv == 0 ? h1 : h2;
+            const uint32_t cin = conv == 0 ? bk.in : bk.out;
+            const float* W = conv == 0 ? bk.w1 : bk.w2;
+            const float* bias = conv == 0 ? bk.b1 : bk.b2;
+            for (uint32_t q = tid; q < bk.out * Hs; q += nt) {
+                const uint32_t o = q / Hs, t = q % Hs;
+                const float* wo = W + static_cast<size_t>(o) * cin * K;
+                float acc = 0.0f;
+                for (uint32_t i = 0; i < cin; ++i)
+                    for (uint32_t j = 0; j < K; ++j) {
+                        const uint32_t shift = (K - 1 - j) * bk.dil;
+                        if (t >= shift) acc = fmaf(__ldg(wo + i * K + j), src[i * Hs + t - shift], acc);
+                    }
+                dst[o * Hs + t] = gelu_tanh(acc + __ldg(bias + o));
+            }
+            __syncthreads();
+        }
+        // residual (1x1 conv when the width changes) and the block output
+        for (uint32_t q = tid; q < bk.out * Hs; q += nt) {
+            const uint32_t o = q / Hs, t = q % Hs;
+            float res;
+            if (bk.wr) {
+                float r = 0.0f;
+                for (uint32_t i = 0; i < bk.in; ++i) r = fmaf(__ldg(bk.wr + static_cast<size_t>(o) * bk.in + i), cur[i * Hs + t], r);
+                res = r + __ldg(bk.br + o);
+            } else {
+                res = cur[o * Hs + t];
+            }
+            h1[o * Hs + t] = gelu_tanh(h2[o * Hs + t] + res);
+        }
+        __syncthreads();
+        for (uint32_t q = tid; q < bk.out * Hs; q += nt) cur[q] = h1[q];
+        __syncthreads();
+    }
+    // state_projection of the last position
+    for (uint32_t u = tid; u < a.H; u += nt) {
+        const float* wu = a.proj_w + static_cast<size_t>(u) * tcn.out_dim;
+        float acc = 0.0f;
+        for (uint32_t c = 0; c < tcn.out_dim; ++c) acc = fmaf(__ldg(wu + c), cur[c * Hs + Hs - 1], acc);
+        h0[static_cast<size_t>(b) * a.H + u] = acc + a.proj_b[u];
+    }
+}
+
 // h0 of every vehicle: state_projection(TemporalConvEncoder(normalised state
 // history))[last position] (SkyJepaModel::encode_history, model.rs:52-66).
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
     if (a.Hs > kH0MaxHist) return cudaErrorInvalidValue;
     const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
-    skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
+    if (a.state_tcn.max_ch >= 64)
+        skyjepa_h0_warp_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
+    else
+        skyjepa_h0_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);
     return cudaGetLastError();
 }
 
