@@ -154,6 +154,7 @@ struct lwm_scorer {
     DevBuf tc_packed, tc_h0, tc_err, tc_x;
     bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
     DevBuf small_x;
+    lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
     bool tc_ready = false;
 };
 
@@ -449,7 +450,10 @@ lwm::NominalArgs nominal_args(lwm_scorer* sc, uint32_t S) {
 }
 
 // Packed bf16 weights (once per scorer), per-vehicle h0 and the error flag.
+lwm_status ensure_side(lwm_scorer* sc);
+
 lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
+    LWM_TRY(ensure_side(sc));
     if (!sc->tc_ready) {
         LWM_TRY(sc->tc_packed.ensure(lwm::skyjepa_tc_packed_bytes()));
         LWM_CUDA(lwm::skyjepa_tc_pack(a, sc->tc_packed.as<uint8_t>(), sc->ctx->stream));
@@ -461,7 +465,16 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint
     return LWM_OK;
 }
 
+lwm_status ensure_side(lwm_scorer* sc) {
+    if (sc->side.stream) return LWM_OK;
+    LWM_CUDA(cudaStreamCreateWithFlags(&sc->side.stream, cudaStreamNonBlocking));
+    LWM_CUDA(cudaEventCreateWithFlags(&sc->side.fork, cudaEventDisableTiming));
+    LWM_CUDA(cudaEventCreateWithFlags(&sc->side.join, cudaEventDisableTiming));
+    return LWM_OK;
+}
+
 lwm_status ensure_small(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
+    LWM_TRY(ensure_side(sc));
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
     LWM_TRY(sc->small_x.ensure(std::max<size_t>(lwm::skyjepa_small_x_bytes(a, B, S, T), 4)));
     return LWM_OK;
@@ -530,7 +543,8 @@ lwm_status score_device(lwm_scorer* sc, const float* cand, uint32_t B, uint32_t 
         int n = 0;
         if (sc->sky_small) {
             LWM_TRY(ensure_small(sc, a, B, S, a.T));
-            LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream, &n));
+            LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream, &n,
+                                               &sc->side));
         } else {
             LWM_CUDA(lwm::launch_skyjepa(a, stream, &n));
         }
@@ -706,7 +720,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     a.low_dev = low;
                     a.high_dev = high;
                     LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream,
-                                                       &launched));
+                                                       &launched, &sc->side));
                 } else if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
                     LWM_TRY(ensure_tc(sc, a, B, p->S, p->T));
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
@@ -715,7 +729,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
                     LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
                                                     sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
-                                                    &launched));
+                                                    &launched, &sc->side));
                 } else {
                     LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
                 }
@@ -1502,6 +1516,9 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->tc_err.release();
     s->tc_x.release();
     s->small_x.release();
+    if (s->side.stream) cudaStreamDestroy(s->side.stream);
+    if (s->side.fork) cudaEventDestroy(s->side.fork);
+    if (s->side.join) cudaEventDestroy(s->side.join);
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;

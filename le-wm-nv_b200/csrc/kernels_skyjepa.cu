@@ -1190,9 +1190,13 @@ size_t skyjepa_small_x_bytes(const SkyjepaArgs& a, uint32_t B, uint32_t S, uint3
     return static_cast<size_t>(B) * S * T * a.E * sizeof(float);
 }
 
-cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches) {
+cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches,
+                                 const SideStream* side) {
     int n = 0;
     cudaError_t e;
+    // initial latent per vehicle, independent of the candidates (side stream when given)
+    if ((e = fork_h0(a, h0, stream, side)) != cudaSuccess) return e;
+    ++n;
     if (a.sample) {
         // candidates (sample_kernel: Philox or injected noise, mean slot, clamp)
         SampleArgs sa{};
@@ -1222,9 +1226,7 @@ cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cuda
         skyjepa_small_inputs_kernel<0, 0><<<blocks, wpb * ca, in_smem, stream>>>(a, cand, x);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     ++n;
-    // initial latent per vehicle
-    if ((e = launch_skyjepa_h0(a, h0, stream)) != cudaSuccess) return e;
-    ++n;
+    if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     // rollout, cost, MPPI partials
     const size_t smem = small_layout(a).total * sizeof(float);
     if ((e = cudaFuncSetAttribute(skyjepa_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

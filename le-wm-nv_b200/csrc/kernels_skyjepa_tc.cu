@@ -1016,8 +1016,25 @@ cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t 
 
 uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S) { return S / kRows; }
 
+cudaError_t fork_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream, const SideStream* side) {
+    if (!side || !side->stream) return launch_skyjepa_h0(a, h0, stream);
+    cudaError_t e = cudaEventRecord(side->fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->stream, side->fork, 0);
+    if (e == cudaSuccess) e = launch_skyjepa_h0(a, h0, side->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(side->join, side->stream);
+    return e;
+}
+
+cudaError_t join_h0(cudaStream_t stream, const SideStream* side) {
+    if (!side || !side->stream) return cudaSuccess;
+    return cudaStreamWaitEvent(stream, side->join, 0);
+}
+
 cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
-                              cudaStream_t stream, int* launches) {
+                              cudaStream_t stream, int* launches, const SideStream* side) {
+    // 0. initial latent per vehicle (independent of the candidates: on the side stream when given)
+    cudaError_t e = fork_h0(a, h0, stream, side);
+    if (e != cudaSuccess) return e;
     // 1. candidates (sample_kernel: Philox or injected noise, mean slot, clamp)
     SampleArgs sa{};
     sa.B = a.B; sa.S = a.S; sa.T = a.T; sa.A = 4;
@@ -1031,14 +1048,13 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     sa.sample_base = a.sample_base;
     sa.sample_total = a.sample_total;
     sa.out = a.cand_out;
-    cudaError_t e = launch_sample(sa, stream);
+    e = launch_sample(sa, stream);
     if (e != cudaSuccess) return e;
-    // 2. per-step inputs of every candidate, 3. initial latent per vehicle
+    // 2. per-step inputs of every candidate; then the join with the latent
     const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
     skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, xtiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    e = launch_skyjepa_h0(a, h0, stream);
-    if (e != cudaSuccess) return e;
+    if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // 4. the rollout
     TcArgs p;

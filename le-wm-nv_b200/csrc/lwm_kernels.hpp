@@ -169,8 +169,14 @@ bool skyjepa_tc_supported(const SkyjepaArgs& a, const char** why);
 size_t skyjepa_tc_packed_bytes();
 cudaError_t skyjepa_tc_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
 uint32_t skyjepa_tc_partials_per_vehicle(uint32_t S);
+// A second stream of a scorer: work that does not depend on the main chain
+// (the history encoding) runs there between a fork and a join event.
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
 cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
-                              cudaStream_t stream, int* launches);
+                              cudaStream_t stream, int* launches, const SideStream* side = nullptr);
 size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
 // Initial latent of every vehicle (state encoder + projection) into h0 [B, H].
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
@@ -179,7 +185,12 @@ cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stre
 bool skyjepa_small_supported(const SkyjepaArgs& a, const char** why);
 uint32_t skyjepa_small_partials_per_vehicle(uint32_t S);
 size_t skyjepa_small_x_bytes(const SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T);
-cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches);
+cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cudaStream_t stream, int* launches,
+                                 const SideStream* side = nullptr);
+// h0 on `side` (forked from `stream`) when given, else on `stream`; the
+// caller joins with join_h0 before the rollout.
+cudaError_t fork_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream, const SideStream* side);
+cudaError_t join_h0(cudaStream_t stream, const SideStream* side);
 
 cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float* scores, uint32_t B,
                                uint32_t S, cudaStream_t stream);
