@@ -155,6 +155,7 @@ struct lwm_scorer {
     bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
     DevBuf small_x;
     lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
+    std::vector<float> action_tcn_host;  // the action encoder's weights, for kernel-parameter packing
     bool tc_ready = false;
 };
 
@@ -482,6 +483,7 @@ lwm_status ensure_small(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, u
 
 lwm::SkyjepaArgs skyjepa_args(lwm_scorer* sc, uint32_t S) {
     lwm::SkyjepaArgs a = sc->sky_args;
+    a.action_tcn_host = sc->action_tcn_host.empty() ? nullptr : sc->action_tcn_host.data();
     a.B = sc->batch;
     a.S = S;
     a.T = sc->horizon;
@@ -1275,7 +1277,9 @@ lwm_status lwm_scorer_skyjepa_create(lwm_ctx* ctx, const lwm_skyjepa_config* cfg
     const uint32_t H = cfg->latent_dim;
     a.proj_w = base + off; off += static_cast<size_t>(H) * a.state_tcn.out_dim;
     a.proj_b = base + off; off += H;
+    const size_t tcn_off = off;
     build_tcn_view(cfg->action_encoder, base, off, a.action_tcn);
+    s->action_tcn_host.assign(weights + tcn_off, weights + off);
     const uint32_t E = a.action_tcn.out_dim;
     a.w_ih = base + off; off += static_cast<size_t>(3) * H * E;
     a.w_hh = base + off; off += static_cast<size_t>(3) * H * H;

@@ -66,6 +66,7 @@ constexpr uint32_t kMaxHid = 32, kMaxLayers = 3;
 constexpr uint32_t kP1Bytes = 4 * kMaxHid * 128;
 constexpr uint32_t kPwFloats = kMaxHid + (kMaxLayers - 1) * (kMaxHid * kMaxHid + kMaxHid) + 16 * kMaxHid + 16;
 constexpr uint32_t kTcnFloats = 1024;
+constexpr uint32_t kTcnBlockFloats = 104, kTcnParamFloats = 3 * kTcnBlockFloats;  // the 4-channel, 3-level encoder
 constexpr int kThreadsTc = 448;
 constexpr uint32_t kAuxWarp0 = 10, kEpiWarp0 = 2;
 constexpr uint32_t kAuxBarrier = 3, kAuxThreads = 128;
@@ -437,13 +438,16 @@ __device__ __forceinline__ void tcn_last(const TcnBlockW (&w)[3], const float (&
 // [history ++ candidate](t : t + 10), last position), one thread per
 // (candidate, step), written as the bf16 x tile of (tile, step): rows = the
 // tile's 128 candidates, k < 4 the encoder output, k = 4 the constant 1.
-__global__ void __launch_bounds__(256) skyjepa_tc_inputs_kernel(SkyjepaArgs a, uint8_t* xtiles) {
-    __shared__ float sw[kTcnFloats];
-    const TcnView& tcn = a.action_tcn;
-    const float* wbase = tcn.blocks[0].w1;
-    const uint32_t nw = tcn_weight_floats(tcn);
-    for (uint32_t q = threadIdx.x; q < nw; q += blockDim.x) sw[q] = wbase[q];
-    __syncthreads();
+//
+// The encoder's 312 weights come as a kernel parameter: with every index a
+// compile-time constant after unrolling, the FMAs read them from the constant
+// bank directly instead of through shared-memory loads.
+struct TcnConst {
+    float v[kTcnParamFloats];  // per level: conv1 weight [4][4][3], bias [4], conv2 weight, bias
+};
+
+__global__ void __launch_bounds__(256) skyjepa_tc_inputs_kernel(SkyjepaArgs a, const __grid_constant__ TcnConst tw,
+                                                                uint8_t* xtiles) {
     const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint64_t total = static_cast<uint64_t>(a.B) * a.S * a.T;
     if (i >= total) return;
@@ -452,9 +456,10 @@ __global__ void __launch_bounds__(256) skyjepa_tc_inputs_kernel(SkyjepaArgs a, u
     const uint32_t b = static_cast<uint32_t>(grow / a.S);
     TcnBlockW w[3];
 #pragma unroll
-    for (int l = 0; l < 3; ++l)
-        w[l] = {sw + (tcn.blocks[l].w1 - wbase), sw + (tcn.blocks[l].b1 - wbase), sw + (tcn.blocks[l].w2 - wbase),
-                sw + (tcn.blocks[l].b2 - wbase)};
+    for (int l = 0; l < 3; ++l) {
+        const float* blk = tw.v + l * kTcnBlockFloats;
+        w[l] = {blk, blk + 48, blk + 52, blk + 100};
+    }
     const float* cand_row = a.cand_out + grow * a.T * 4;
     float x0[kTcnC][kTcnHs];
 #pragma unroll
@@ -1052,7 +1057,10 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     if (e != cudaSuccess) return e;
     // 2. per-step inputs of every candidate; then the join with the latent
     const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
-    skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, xtiles);
+    if (!a.action_tcn_host || tcn_weight_floats(a.action_tcn) != kTcnParamFloats) return cudaErrorInvalidValue;
+    TcnConst tw;
+    for (uint32_t q = 0; q < kTcnParamFloats; ++q) tw.v[q] = a.action_tcn_host[q];
+    skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

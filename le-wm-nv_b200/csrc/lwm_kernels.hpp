@@ -161,6 +161,7 @@ struct SkyjepaArgs {
     float* states;
     int mppi;
     MppiArgs m;
+    const float* action_tcn_host;  // host copy of the action encoder's weights (kernel-parameter packing), or nullptr
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
