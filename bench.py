@@ -10,6 +10,7 @@ reference).  A "step" is one plan call.
     python bench.py --impl reference ...   # the CPU restatement on the host cores
     python bench.py --workload fleet [--shard auto|vehicles|candidates] [--vehicles V --samples S --horizon T]
     python bench.py --workload lewm-vector|lewm-image    # LeWM CEM (vector obs) / MPPI (NV12 frames + ViT)
+    python bench.py --workload media [--precision f32|bf16]  # NV12 -> NCHW preprocessing vs the HBM roofline
     python bench.py --workload closed-loop [--dynamics learned|nominal] [--random-domains N]
                                           # closed-loop session scenarios; --steps = control steps per scenario
 
@@ -673,6 +674,118 @@ def cpu_baseline_lewm(w, image: bool, budget_s: float):
             "sample": f"{len(times)} full plans (encoding included), oracle C restatement, {threads} OpenMP threads"}
 
 
+# ------------------------------------------------------------ media workload
+
+def run_media(args, rank, world, local_rank):
+    """NV12 -> normalised NCHW (Nv12Preprocessor, src/media/mod.rs:196-273) for
+    a batch of full-HD frames at their own size (ImageNet mean / std): one
+    read of the NV12 planes, one write of the planar output per pixel — the
+    preprocessing kernel against the HBM roofline.  Inputs and outputs
+    (~0.9 GB f32) exceed the L2, so no flush is needed between steps."""
+    import torch
+    import lewm_b200 as L
+    torch.cuda.set_device(local_rank)
+    B, H, W = args.frames, 1080, 1920
+    bf16 = args.precision == "bf16"
+    ctx = L.Context(local_rank)
+    stream = ctx.torch_stream()
+    g = torch.Generator().manual_seed(7 + rank)
+    host_y = torch.randint(0, 256, (B, H, W), dtype=torch.uint8, generator=g).pin_memory()
+    host_uv = torch.randint(0, 256, (B, H // 2, W // 2, 2), dtype=torch.uint8, generator=g).pin_memory()
+    dev_y, dev_uv = host_y.cuda(), host_uv.cuda()
+    out = torch.empty((B, 3, H, W), dtype=torch.bfloat16 if bf16 else torch.float32, device="cuda")
+    cfg = L.ImagePreprocess.make(H, W, (0.485, 0.456, 0.406), (0.229, 0.224, 0.225))
+    torch.cuda.synchronize()
+
+    def step():
+        L.preprocess_nv12_device(ctx, dev_y, dev_uv, B, H, W, "bt601-video", cfg, out, bf16=bf16)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.synchronize()
+    n0 = ctx.launch_count()
+    times = []
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        for _ in range(args.steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            step()
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = ctx.launch_count() - n0
+    e2e = []
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    for _ in range(max(3, args.steps // 10)):
+        ctx.synchronize()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            dev_y.copy_(host_y, non_blocking=True)
+            dev_uv.copy_(host_uv, non_blocking=True)
+        step()
+        with torch.cuda.stream(stream):
+            host_out.copy_(out, non_blocking=True)
+        ctx.synchronize()
+        e2e.append(time.perf_counter() - t0)
+    ms = float(np.median(times))
+    px = B * H * W
+    bytes_per_call = px * (1.5 + (6 if bf16 else 12))
+    achieved = bytes_per_call / (ms * 1e-3) / 1e9
+    peak = float(measured_peaks().get("hbm_gbs", 6650.0))
+    result = {
+        "metric": f"frames/s of NV12 -> normalised NCHW preprocessing (1920x1080, batch {B}, same-size output)",
+        "value": round(world * B * 1e3 / ms, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8->" + ("bf16" if bf16 else "f32"), "data": "synthetic (seeded uniform NV12)",
+        "config": {"workload": f"NV12 bt601-video {W}x{H} x {B} -> NCHW {'bf16' if bf16 else 'f32'}, ImageNet "
+                               "mean/std", "parallelism": f"replicas x{world}",
+                   "l2": "not flushed: inputs + outputs exceed the L2"},
+        "e2e": {"value": round(world * B / float(np.median(e2e)), 1), "unit": "frames/s",
+                "h2d_bytes_per_step": int(host_y.numel() + host_uv.numel()),
+                "d2h_bytes_per_step": int(out.numel() * out.element_size())},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": "MEASURED_PEAKS hbm_gbs (of measured)",
+                     "note": "achieved = (1.5 B NV12 read + output bytes written) per pixel / p50 time"},
+        "clocks": clocks.summary(),
+    }
+    if args.cpu_baseline and rank == 0:
+        result["cpu_baseline"] = cpu_baseline_media(host_y[:2].numpy(), host_uv[:2].numpy(), args.cpu_seconds)
+    del host_y, host_uv, host_out
+    ctx.close()
+    return result if rank == 0 else None
+
+
+def cpu_baseline_media(y, uv, budget_s: float):
+    """The oracle's C NV12 -> NCHW conversion on the host cores: one frame per
+    call, the calls spread over a thread per core (ctypes releases the GIL),
+    repeated for about `budget_s` seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = os.cpu_count() or 1
+    B, H, W = y.shape
+    mean, std = (0.485, 0.456, 0.406), (0.229, 0.224, 0.225)
+    outs = [np.empty((1, 3, H, W), np.float32) for _ in range(threads)]
+
+    def one(i):
+        O.preprocess_nv12(y[i % B][None], uv[i % B][None], 0, H, W, mean=mean, std=std, out=outs[i % threads])
+
+    frames, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as pool:
+        while True:
+            list(pool.map(one, range(threads)))
+            frames += threads
+            dt = time.perf_counter() - t0
+            if dt >= budget_s:
+                break
+    return {"value": round(frames / dt, 2), "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"{frames} full-HD NV12 frames through the oracle's C preprocessing, one frame per call "
+                      f"on {threads} threads"}
+
+
 # -------------------------------------------------------- closed-loop scenarios
 
 REFERENCE_KINDS = {"hover": 0, "circle": 1, "figure-eight": 2}
@@ -880,6 +993,20 @@ def run_reference(args, rank, world):
                            "parallelism": "host CPU"},
                 "latency_ms": base["latency_ms"], "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "media":
+        g = np.random.default_rng(7)
+        y = g.integers(0, 256, (2, 1080, 1920), dtype=np.uint8)
+        uv = g.integers(0, 256, (2, 540, 960, 2), dtype=np.uint8)
+        base = cpu_baseline_media(y, uv, args.cpu_seconds)
+        return {"impl": "reference",
+                "metric": "frames/s of NV12 -> normalised NCHW preprocessing (1920x1080, batch 32, same-size output)",
+                "value": base["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(32e3 / base["value"], 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u8->f32", "data": "synthetic (seeded uniform NV12)",
+                "config": {"workload": "NV12 bt601-video 1920x1080 x 32 -> NCHW f32, ImageNet mean/std",
+                           "parallelism": "host CPU"},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload.startswith("lewm"):
         from lewm_b200 import workloads as W
         image = args.workload == "lewm-image"
@@ -927,7 +1054,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet", "lewm-vector", "lewm-image", "closed-loop"],
+    ap.add_argument("--workload", choices=["skyjepa", "nominal", "fleet", "lewm-vector", "lewm-image", "closed-loop",
+                                           "media"],
                     default="skyjepa")
     ap.add_argument("--shard", choices=["auto", "vehicles", "candidates"], default="auto")
     ap.add_argument("--vehicles", type=int, default=256)
@@ -943,6 +1071,7 @@ def main():
     ap.add_argument("--random-domains", type=int, default=2,
                     help="closed-loop: sampled domains beside the nominal one (the reference bench uses 20)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--frames", type=int, default=32, help="media workload: full-HD frames per batch")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -959,6 +1088,8 @@ def main():
         out = run_lewm(args, rank, world, local_rank)
     elif args.workload == "closed-loop":
         out = run_closed_loop(args, rank, world, local_rank)
+    elif args.workload == "media":
+        out = run_media(args, rank, world, local_rank)
     else:
         out = run_ours(args, rank, world, local_rank)
     if rank == 0 and out is not None:

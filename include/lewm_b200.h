@@ -61,6 +61,9 @@ lwm_status lwm_ctx_create(int device, lwm_ctx** out);
 lwm_status lwm_ctx_destroy(lwm_ctx* ctx);
 /* The context's cudaStream_t, for callers that interleave their own work. */
 lwm_status lwm_ctx_stream(lwm_ctx* ctx, void** stream_out);
+/* Waits for the context's stream.  Also reports (LWM_CUDA_ERROR, once) an
+ * NV12 preprocessing launch whose source-row copies never completed since
+ * the previous call; that launch's output is then incomplete. */
 lwm_status lwm_ctx_synchronize(lwm_ctx* ctx);
 /* Number of kernels this library has launched on the context so far. */
 lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out);
@@ -621,7 +624,11 @@ lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint
 /* Nv12Preprocessor::preprocess_nv12 and Nv12HistoryPreprocessor::
  * preprocess_nv12_into_slot (src/media/mod.rs:196-273, 345-468; kernel
  * :1196-1333).  Device Y plane [B,H,W] and interleaved UV plane
- * [B,H/2,W/2,2]; H and W must be even. */
+ * [B,H/2,W/2,2]; H and W must be even.  With W a multiple of 16 up to 4096,
+ * the output width a multiple of 4 up to 2048, 16-byte aligned planes and
+ * output (8 bytes for bf16), std in [2^-40, 2^40] and mean 0 or of magnitude
+ * in [2^-40, 2^40], a row-staged kernel runs (source rows bulk-copied into
+ * shared memory); otherwise a per-pixel kernel.  Both write the same values. */
 lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane,
                                       uint32_t batch, uint32_t height, uint32_t width, int32_t color_space,
                                       const lwm_image_preprocess* cfg, uint32_t history_len,

@@ -118,6 +118,10 @@ struct lwm_ctx {
     std::atomic<uint64_t> launches{0};
     uint64_t unseeded_seed = 0;
     std::atomic<uint64_t> unseeded_offset{0};
+    // error word of the row-staged NV12 kernel: mapped pinned host memory,
+    // read after every stream synchronisation (allocated on first use)
+    int* media_err = nullptr;
+    int* media_err_dev = nullptr;
 };
 
 enum class PlannerKind { Mppi, Cem, Icem };
@@ -954,6 +958,7 @@ lwm_status lwm_ctx_destroy(lwm_ctx* ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     cudaStreamDestroy(ctx->stream);
+    if (ctx->media_err) cudaFreeHost(ctx->media_err);
     delete ctx;
     return LWM_OK;
 }
@@ -968,6 +973,13 @@ lwm_status lwm_ctx_synchronize(lwm_ctx* ctx) {
     if (!ctx) return fail(LWM_INVALID_ARGUMENT, "null context");
     LWM_CUDA(cudaSetDevice(ctx->device));
     LWM_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->media_err && ctx->media_err[0]) {
+        const std::string where = "block " + std::to_string(ctx->media_err[1]) + ", row step " +
+                                  std::to_string(ctx->media_err[2]);
+        for (int i = 0; i < 4; ++i) ctx->media_err[i] = 0;
+        return fail(LWM_CUDA_ERROR, "NV12 preprocessing: a source-row copy never completed (" + where +
+                                        "); that launch's output is incomplete");
+    }
     return LWM_OK;
 }
 
@@ -1803,7 +1815,18 @@ lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, cons
     a.uv = uv_plane;
     a.channels = 1;
     a.format = static_cast<uint32_t>(color_space);
-    LWM_CUDA(lwm::launch_media(a, true, ctx->stream));
+    if (lwm::nv12_staged_eligible(a)) {
+        if (!ctx->media_err) {
+            void* dev = nullptr;
+            LWM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ctx->media_err), 4 * sizeof(int), cudaHostAllocMapped));
+            for (int i = 0; i < 4; ++i) ctx->media_err[i] = 0;
+            LWM_CUDA(cudaHostGetDevicePointer(&dev, ctx->media_err, 0));
+            ctx->media_err_dev = static_cast<int*>(dev);
+        }
+        LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, ctx->stream));
+    } else {
+        LWM_CUDA(lwm::launch_media(a, true, ctx->stream));
+    }
     ctx->launches += 1;
     return LWM_OK;
 }

@@ -11,9 +11,12 @@
 // with -fmad=false: every product and sum is rounded on its own.
 #include <cuda_bf16.h>
 
+#include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "lwm_kernels.hpp"
+#include "lwm_tc.cuh"
 
 namespace lwm {
 
@@ -105,6 +108,408 @@ __global__ void __launch_bounds__(256) nv12_to_nchw_kernel(MediaArgs a) {
     const float v[3] = {clampf(r, 0.0f, 255.0f) * 0.00392156862745098f, clampf(g, 0.0f, 255.0f) * 0.00392156862745098f,
                         clampf(bl, 0.0f, 255.0f) * 0.00392156862745098f};
     store3(a, b, y, x, v);
+}
+
+// ------------------------------------------------------------------------
+// NV12, row-staged.  The generic kernel above spends most of its issue slots
+// on index and conversion arithmetic (64-bit div/mod per pixel, I2F/F2I at
+// the conversion rate, a library division per channel); at full HD it runs
+// at a sixth of the HBM roofline.  This one keeps the arithmetic of
+// swm_nv12_to_nchw_f32 exactly, and removes the rest:
+//   * a block per output row at a time (grid-stride over batch x rows): the
+//     two luma rows and two chroma rows it taps are copied into shared
+//     memory by the bulk-copy engine (cp.async.bulk, one instruction per
+//     row, completion on an mbarrier), kStages rows ahead;
+//   * a thread owns four adjacent output columns for the whole kernel: their
+//     source columns and bilinear weights are computed once, in registers;
+//   * taps are u8 loads from shared memory turned into floats with the 2^23
+//     bit trick (bits 0x4B0000bb are the float 2^23 + b, exact), and the
+//     difference of two taps is taken before the 2^23 is removed (exact);
+//   * all per-pixel float arithmetic runs as Blackwell packed f32x2
+//     instructions (two pixels per instruction, each lane rounded as its own
+//     f32 op, subnormals kept); products that feed an add are written so
+//     that ptxas cannot fuse them (see Prod), and the clamp to [0, 255]
+//     with the scale by 1/255 is one saturating multiply per value (see
+//     unit_clamp);
+//   * the division by std is a product with the correctly rounded
+//     reciprocal r = 1/std (computed on the host) followed by two
+//     remainder corrections q += (a - std q) r; the second starts from a
+//     quotient within an ulp, so by Markstein's theorem (Markstein 1990;
+//     Cornea, Harrison, Tang 2002) it returns the correctly rounded a / std.
+// Taps, weights, products and sums are the same f32 operations, in the same
+// order, as the generic kernel's, so its outputs are bit-identical.
+namespace staged {
+
+constexpr uint32_t kStages = 3;
+constexpr uint32_t kMagic = 0x4B000000u;  // the float 2^23
+constexpr uint32_t kMaxThreads = 512;     // 4 columns each: output rows up to 2048
+constexpr uint32_t kWaitLimit = 1u << 26;
+
+struct f2 {
+    unsigned long long v;
+};
+__device__ __forceinline__ f2 mk(float a, float b) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ f2 splat(float a) { return mk(a, a); }
+__device__ __forceinline__ float lo(f2 a) {
+    float x;
+    asm("{\n\t.reg .f32 t;\n\tmov.b64 {%0, t}, %1;\n\t}" : "=f"(x) : "l"(a.v));
+    return x;
+}
+__device__ __forceinline__ float hi(f2 a) {
+    float y;
+    asm("{\n\t.reg .f32 t;\n\tmov.b64 {t, %0}, %1;\n\t}" : "=f"(y) : "l"(a.v));
+    return y;
+}
+__device__ __forceinline__ f2 add(f2 a, f2 b) {
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+__device__ __forceinline__ f2 sub(f2 a, f2 b) {
+    f2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+__device__ __forceinline__ f2 mul(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+// A product that feeds an add or a subtract.  ptxas contracts a packed
+// f32x2 multiply whose only use is an add into one fused multiply-add (the
+// .rn qualifier and -fmad=false notwithstanding), which rounds once where
+// swm_nv12_to_nchw_f32 rounds twice.  So the product is written as an fma
+// whose addend is -0 read from the kernel parameters: RN(a b + -0) is
+// RN(a b) for every a, b (signed zeros included), and with the addend
+// unknown at compile time the fma is neither simplified to a multiply nor
+// fused with the add that follows.
+__device__ __forceinline__ f2 fma(f2 a, f2 b, f2 c);
+struct Prod {
+    f2 nz;  // (-0, -0), from the kernel parameters
+    __device__ __forceinline__ f2 operator()(f2 a, f2 b) const { return fma(a, b, nz); }
+    __device__ __forceinline__ f2 operator()(f2 a, float k) const { return fma(a, splat(k), nz); }
+};
+__device__ __forceinline__ f2 fma(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+    return r;
+}
+// clamp(v, 0, 255) / 255 as RN(v RN(1/255)) saturated to [0, 1]: the
+// product is monotonic in v and RN(255 RN(1/255)) = 1, so the saturated
+// product equals the product of the clamped value (mul.sat: saturation after
+// rounding; the clamp of a negative v gives +0, as does the saturation).
+// Packed f32x2 multiplies take no .sat, so this one is scalar.
+__device__ __forceinline__ float unit_clamp(float a) {
+    float r;
+    asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(0.00392156862745098f));
+    return r;
+}
+__device__ __forceinline__ f2 unit_clamp(f2 a) { return mk(unit_clamp(lo(a)), unit_clamp(hi(a))); }
+__device__ __forceinline__ f2 relu(f2 a) { return mk(fmaxf(lo(a), 0.0f), fmaxf(hi(a), 0.0f)); }
+
+// u8 tap -> float with 2^23 added (exact): byte b of `word` under the magic.
+__device__ __forceinline__ float magic_byte(uint32_t word, uint32_t sel) {
+    return __uint_as_float(__byte_perm(word, kMagic, sel));
+}
+__device__ __forceinline__ float magic_u8(uint32_t byte) { return __uint_as_float(byte | kMagic); }
+
+// floor of v in [0, 2^23) as an integer and as a float, without conversion
+// instructions: v + 2^23 rounded toward zero keeps floor(v) in its low bits.
+__device__ __forceinline__ uint32_t floor_u(float v, float& f) {
+    const float t = __fadd_rz(v, 8388608.0f);
+    f = t - 8388608.0f;
+    return __float_as_uint(t) - kMagic;
+}
+
+// Bilinear lerp of two pixels' taps held with 2^23 added; weights wx per
+// pixel, wy shared (the arithmetic of sample_plane above).
+__device__ __forceinline__ f2 bilerp(const Prod& mul, f2 t00, f2 t01, f2 t10, f2 t11, f2 wx, f2 wy) {
+    const f2 m = splat(8388608.0f);
+    const f2 top = add(sub(t00, m), mul(sub(t01, t00), wx));
+    const f2 bottom = add(sub(t10, m), mul(sub(t11, t10), wx));
+    return add(top, mul(sub(bottom, top), wy));
+}
+
+struct Row {
+    uint32_t y0, y1, c0, c1;  // luma and chroma source rows
+    float wy, cwy;
+};
+__device__ __forceinline__ Row row_taps(float sy, uint32_t in_h) {
+    Row r;
+    float f;
+    const float s = clampf(sy, 0.0f, static_cast<float>(in_h - 1u));
+    r.y0 = floor_u(s, f);
+    r.y1 = r.y0 + 1u < in_h ? r.y0 + 1u : r.y0;
+    r.wy = s - f;
+    const uint32_t ch = in_h / 2u;
+    const float cs = clampf(sy * 0.5f, 0.0f, static_cast<float>(ch - 1u));
+    r.c0 = floor_u(cs, f);
+    r.c1 = r.c0 + 1u < ch ? r.c0 + 1u : r.c0;
+    r.cwy = cs - f;
+    return r;
+}
+
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (tc::mbar_try(bar, parity)) return true;
+    return false;
+}
+
+template <uint32_t CS>
+__device__ __forceinline__ void to_rgb(const Prod& mul_sep, f2 Y, f2 U, f2 V, f2& r, f2& g, f2& b) {
+    // colour matrices of src/media/mod.rs:1298-1318
+    if constexpr (CS == 0u || CS == 1u) {
+        const f2 yy = mul_sep(relu(sub(Y, splat(16.0f))), 1.16438356f);
+        if constexpr (CS == 0u) {
+            r = add(yy, mul_sep(V, 1.59602678f));
+            g = sub(sub(yy, mul_sep(U, 0.39176229f)), mul_sep(V, 0.81296765f));
+            b = add(yy, mul_sep(U, 2.01723214f));
+        } else {
+            r = add(yy, mul_sep(V, 1.79274107f));
+            g = sub(sub(yy, mul_sep(U, 0.21324861f)), mul_sep(V, 0.53290933f));
+            b = add(yy, mul_sep(U, 2.11240179f));
+        }
+    } else if constexpr (CS == 2u) {
+        r = add(Y, mul_sep(V, 1.402f));
+        g = sub(sub(Y, mul_sep(U, 0.344136f)), mul_sep(V, 0.714136f));
+        b = add(Y, mul_sep(U, 1.772f));
+    } else {
+        r = add(Y, mul_sep(V, 1.5748f));
+        g = sub(sub(Y, mul_sep(U, 0.187324f)), mul_sep(V, 0.468124f));
+        b = add(Y, mul_sep(U, 1.8556f));
+    }
+}
+
+// (clamp(v) / 255 - mean) / std, the division as described above.
+__device__ __forceinline__ f2 normalize(f2 v, float mean, float sd, float rcp) {
+    const f2 a = sub(unit_clamp(v), splat(mean));
+    const f2 r = splat(rcp), nsd = splat(-sd);
+    f2 q = mul(a, r);
+    q = fma(fma(nsd, q, a), r, q);
+    return fma(fma(nsd, q, a), r, q);
+}
+
+template <uint32_t CS, bool BF16, uint32_t ROWCAP>
+__global__ void __launch_bounds__(kMaxThreads) nv12_staged_kernel(MediaArgs a, StagedMedia m) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t kStageBytes = 4u * ROWCAP;  // luma y0, luma y1, chroma c0, chroma c1
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    const uint32_t tid = threadIdx.x, in_w = a.in_w, rows = a.batch * a.out_h;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) tc::mbar_init(&full[s], 1);
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](uint32_t k, uint32_t s) {
+        const uint32_t r = blockIdx.x + k * gridDim.x;
+        if (r >= rows) return;
+        const uint32_t b = r / a.out_h, y = r - b * a.out_h;
+        const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
+        uint8_t* st = smem + s * kStageBytes;
+        const size_t frame = static_cast<size_t>(b) * a.in_h;
+        tc::mbar_expect_tx(&full[s], 4u * in_w);
+        tc::bulk_g2s(st, a.a + (frame + t.y0) * in_w, in_w, &full[s]);
+        tc::bulk_g2s(st + ROWCAP, a.a + (frame + t.y1) * in_w, in_w, &full[s]);
+        tc::bulk_g2s(st + 2u * ROWCAP, a.uv + (frame / 2u + t.c0) * in_w, in_w, &full[s]);
+        tc::bulk_g2s(st + 3u * ROWCAP, a.uv + (frame / 2u + t.c1) * in_w, in_w, &full[s]);
+    };
+    if (tid == 0)
+        for (uint32_t s = 0; s < kStages; ++s) issue(s, s);
+
+    // the four output columns of this thread: source columns, weights
+    const uint32_t x4 = tid * 4u;
+    const bool active = x4 < a.out_w;
+    uint32_t l0[4], l1[4], u0[4], u1[4];
+    float wx[4], cwx[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t x = active ? x4 + i : 0u;
+        const float sx = (static_cast<float>(x) + 0.5f) * m.ratio_w - 0.5f;
+        float f;
+        const float s = clampf(sx, 0.0f, static_cast<float>(in_w - 1u));
+        l0[i] = floor_u(s, f);
+        l1[i] = l0[i] + 1u < in_w ? l0[i] + 1u : l0[i];
+        wx[i] = s - f;
+        const uint32_t cw = in_w / 2u;
+        const float cs = clampf(sx * 0.5f, 0.0f, static_cast<float>(cw - 1u));
+        const uint32_t c0 = floor_u(cs, f);
+        u0[i] = 2u * c0;
+        u1[i] = 2u * (c0 + 1u < cw ? c0 + 1u : c0);
+        cwx[i] = cs - f;
+    }
+    const Prod prod{splat(m.neg_zero)};
+    const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
+    const f2 cwxa = mk(cwx[0], cwx[1]), cwxb = mk(cwx[2], cwx[3]);
+    const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
+    const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
+
+    // one output row from stage S (a compile-time shared-memory offset);
+    // returns false once the block's rows are done or a copy never landed
+    auto step = [&](uint32_t k, auto stage) -> bool {
+        constexpr uint32_t S = decltype(stage)::value;
+        const uint32_t r = blockIdx.x + k * gridDim.x;
+        if (r >= rows) return false;
+        const uint32_t b = r / a.out_h, y = r - b * a.out_h;
+        const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
+        const bool ok = wait_stage(&full[S], (k / kStages) & 1u);
+        if (ok && active) {
+            const uint8_t* ly0 = smem + S * kStageBytes;
+            const uint8_t* ly1 = ly0 + ROWCAP;
+            const uint8_t* cr0 = ly0 + 2u * ROWCAP;
+            const uint8_t* cr1 = ly0 + 3u * ROWCAP;
+            const f2 wy = splat(t.wy), cwy = splat(t.cwy);
+            f2 out[3][2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int i = 2 * p, j = 2 * p + 1;
+                const f2 wxp = p ? wxb : wxa, cwxp = p ? cwxb : cwxa;
+                const f2 Y = bilerp(prod, mk(magic_u8(ly0[l0[i]]), magic_u8(ly0[l0[j]])),
+                                    mk(magic_u8(ly0[l1[i]]), magic_u8(ly0[l1[j]])),
+                                    mk(magic_u8(ly1[l0[i]]), magic_u8(ly1[l0[j]])),
+                                    mk(magic_u8(ly1[l1[i]]), magic_u8(ly1[l1[j]])), wxp, wy);
+                const uint32_t a00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[i]);
+                const uint32_t b00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[j]);
+                const uint32_t a01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[i]);
+                const uint32_t b01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[j]);
+                const uint32_t a10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[i]);
+                const uint32_t b10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[j]);
+                const uint32_t a11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[i]);
+                const uint32_t b11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[j]);
+                constexpr uint32_t kU = 0x7540u, kV = 0x7541u;
+                const f2 c128 = splat(128.0f);
+                const f2 U = sub(bilerp(prod, mk(magic_byte(a00, kU), magic_byte(b00, kU)),
+                                        mk(magic_byte(a01, kU), magic_byte(b01, kU)),
+                                        mk(magic_byte(a10, kU), magic_byte(b10, kU)),
+                                        mk(magic_byte(a11, kU), magic_byte(b11, kU)), cwxp, cwy),
+                                 c128);
+                const f2 V = sub(bilerp(prod, mk(magic_byte(a00, kV), magic_byte(b00, kV)),
+                                        mk(magic_byte(a01, kV), magic_byte(b01, kV)),
+                                        mk(magic_byte(a10, kV), magic_byte(b10, kV)),
+                                        mk(magic_byte(a11, kV), magic_byte(b11, kV)), cwxp, cwy),
+                                 c128);
+                f2 R, G, B;
+                to_rgb<CS>(prod, Y, U, V, R, G, B);
+                out[0][p] = normalize(R, a.mean[0], a.std[0], m.rcp_std[0]);
+                out[1][p] = normalize(G, a.mean[1], a.std[1], m.rcp_std[1]);
+                out[2][p] = normalize(B, a.mean[2], a.std[2], m.rcp_std[2]);
+            }
+            const size_t base = ((static_cast<size_t>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w + x4;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                if constexpr (BF16) {
+                    const __nv_bfloat162 p0 = __floats2bfloat162_rn(lo(out[c][0]), hi(out[c][0]));
+                    const __nv_bfloat162 p1 = __floats2bfloat162_rn(lo(out[c][1]), hi(out[c][1]));
+                    uint2 w;
+                    w.x = *reinterpret_cast<const uint32_t*>(&p0);
+                    w.y = *reinterpret_cast<const uint32_t*>(&p1);
+                    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + base + c * plane) = w;
+                } else {
+                    *reinterpret_cast<float4*>(static_cast<float*>(a.out) + base + c * plane) =
+                        make_float4(lo(out[c][0]), hi(out[c][0]), lo(out[c][1]), hi(out[c][1]));
+                }
+            }
+        }
+        // every thread is done with stage S before it is refilled
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                m.err[1] = static_cast<int>(blockIdx.x);
+                m.err[2] = static_cast<int>(k);
+                m.err[0] = 1;
+                // rows still in flight land before the block's shared memory is released
+                for (uint32_t j = k; j < k + kStages; ++j)
+                    if (blockIdx.x + j * gridDim.x < rows) wait_stage(&full[j % kStages], (j / kStages) & 1u);
+            }
+            __syncthreads();
+            return false;
+        }
+        if (tid == 0) issue(k + kStages, S);
+        return true;
+    };
+    static_assert(kStages == 3, "the row loop below is unrolled over three stages");
+    for (uint32_t k = 0;; k += kStages) {
+        if (!step(k, std::integral_constant<uint32_t, 0>{})) break;
+        if (!step(k + 1, std::integral_constant<uint32_t, 1>{})) break;
+        if (!step(k + 2, std::integral_constant<uint32_t, 2>{})) break;
+    }
+}
+
+template <uint32_t CS, bool BF16, uint32_t ROWCAP>
+cudaError_t launch_one(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
+    auto kern = nv12_staged_kernel<CS, BF16, ROWCAP>;
+    const uint32_t smem = kStages * 4u * ROWCAP + kStages * sizeof(uint64_t);
+    const uint32_t threads = ((a.out_w / 4u + 31u) / 32u) * 32u;
+    static int configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    static int per_sm[64] = {}, sms[64] = {};
+    static uint32_t per_sm_threads[64] = {};
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
+    if (per_sm_threads[dev] != threads) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], kern, static_cast<int>(threads), smem);
+        if (e != cudaSuccess) return e;
+        per_sm_threads[dev] = threads;
+    }
+    const uint64_t rows = static_cast<uint64_t>(a.batch) * a.out_h;
+    const uint64_t resident = static_cast<uint64_t>(per_sm[dev] > 0 ? per_sm[dev] : 1) * sms[dev];
+    const uint32_t grid = static_cast<uint32_t>(rows < resident ? rows : resident);
+    kern<<<grid, threads, smem, stream>>>(a, m);
+    return cudaGetLastError();
+}
+
+template <uint32_t CS>
+cudaError_t launch_cs(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
+    const bool small = a.in_w <= 2048u;
+    if (a.bf16) return small ? launch_one<CS, true, 2048>(a, m, stream) : launch_one<CS, true, 4096>(a, m, stream);
+    return small ? launch_one<CS, false, 2048>(a, m, stream) : launch_one<CS, false, 4096>(a, m, stream);
+}
+
+}  // namespace staged
+
+bool nv12_staged_eligible(const MediaArgs& a) {
+    const auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+    if (a.in_w % 16u != 0 || a.in_w > 4096u || a.in_h < 2u) return false;
+    if (a.out_w % 4u != 0 || a.out_w > 4u * staged::kMaxThreads || a.out_h == 0) return false;
+    if (!aligned(a.a, 16) || !aligned(a.uv, 16) || !aligned(a.out, a.bf16 ? 8 : 16)) return false;
+    if (static_cast<uint64_t>(a.batch) * a.out_h >= (1ull << 31) ||
+        static_cast<uint64_t>(a.batch) * a.in_h >= (1ull << 31))
+        return false;
+    for (int c = 0; c < 3; ++c) {
+        // The corrected quotient is exact while the quotient and the
+        // remainder stay normal: with values in [0, 1], std in [2^-40, 2^40]
+        // and mean 0 or of magnitude in [2^-40, 2^40] they do.
+        const float s = a.std[c], mu = std::fabs(a.mean[c]);
+        if (!(s >= 0x1p-40f && s <= 0x1p40f)) return false;
+        if (!(mu == 0.0f || (mu >= 0x1p-40f && mu <= 0x1p40f))) return false;
+    }
+    return true;
+}
+
+cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream) {
+    StagedMedia m{};
+    m.ratio_h = static_cast<float>(a.in_h) / static_cast<float>(a.out_h);
+    m.ratio_w = static_cast<float>(a.in_w) / static_cast<float>(a.out_w);
+    for (int c = 0; c < 3; ++c) m.rcp_std[c] = 1.0f / a.std[c];
+    m.err = err;
+    m.neg_zero = -0.0f;
+    switch (a.format) {
+        case 0: return staged::launch_cs<0>(a, m, stream);
+        case 1: return staged::launch_cs<1>(a, m, stream);
+        case 2: return staged::launch_cs<2>(a, m, stream);
+        default: return staged::launch_cs<3>(a, m, stream);
+    }
 }
 
 cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream) {

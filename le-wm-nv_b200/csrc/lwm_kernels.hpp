@@ -232,6 +232,20 @@ struct MediaArgs {
     float mean[3], std[3];
 };
 cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream);
+// The row-staged NV12 kernel (bulk-copied source rows, packed f32x2 math):
+// bit-identical to launch_media's NV12 kernel where eligible (row bytes a
+// multiple of 16 up to 4096, output width a multiple of 4 up to 2048,
+// aligned planes and output, std in [2^-40, 2^40], mean 0 or
+// of magnitude in [2^-40, 2^40]).  `err` (4 ints, device-
+// visible) gets 1 in err[0] when a row copy never completed.
+struct StagedMedia {
+    float ratio_h, ratio_w;
+    float rcp_std[3];
+    float neg_zero;  // -0.0f
+    int* err;
+};
+bool nv12_staged_eligible(const MediaArgs& a);
+cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream);
 
 // Rows per cluster (one wave of co-resident clusters when possible) and MPPI
 // partials per vehicle of the fused SkyJEPA kernel.

@@ -113,3 +113,57 @@ def test_bf16_output_is_rounded_oracle(ctx):
     ref = O.preprocess_nv12(y, uv, 1, 224, 224, **IMAGENET)
     np.testing.assert_array_equal(got[:, 2], _bf16_of(ref))
     assert (got[:, :2] == 7.0).all()
+
+
+# Shapes the row-staged NV12 kernel takes (row bytes a multiple of 16, output
+# width a multiple of 4): full HD at its own size, up- and down-scaling, the
+# 4096-byte row buffers, and two-row frames (a single chroma row).
+STAGED = [(1, 1080, 1920, 1080, 1920), (2, 64, 96, 200, 300), (1, 8, 4096, 16, 2048), (2, 720, 1280, 360, 640),
+          (2, 2, 16, 1, 4), (1, 2, 16, 3, 8)]
+
+
+@pytest.mark.parametrize("cs", ["bt601-video", "bt709-video", "bt601-full", "bt709-full"])
+@pytest.mark.parametrize("size", STAGED)
+def test_nv12_row_staged_matches_oracle_bit_exact(ctx, cs, size):
+    B, H, W, oh, ow = size
+    rng = np.random.default_rng(zlib.crc32(repr(("staged", cs, size)).encode()))
+    y = rng.integers(0, 256, (B, H, W), dtype=np.uint8)
+    uv = rng.integers(0, 256, (B, H // 2, W // 2, 2), dtype=np.uint8)
+    got = _run_nv12(ctx, y, uv, cs, oh, ow, **IMAGENET)
+    ref = O.preprocess_nv12(y, uv, L.NV12_COLOR_SPACES[cs], oh, ow, **IMAGENET)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("norm", [dict(mean=(0.0, 0.0, 0.0), std=(1.0, 1.0, 1.0)),
+                                  dict(mean=(0.5, 0.01, 0.9), std=(0.01, 3.7, 1e-3)),
+                                  dict(mean=(2.0 ** -40, -1000.0, 0.25), std=(2.0 ** -40, 2.0 ** 40, 0.3))])
+def test_nv12_row_staged_division_is_exact(ctx, norm):
+    # the staged kernel divides by std through a host reciprocal and two
+    # remainder corrections; its quotients equal the oracle's IEEE division
+    rng = np.random.default_rng(17)
+    y = rng.integers(0, 256, (2, 360, 640), dtype=np.uint8)
+    uv = rng.integers(0, 256, (2, 180, 320, 2), dtype=np.uint8)
+    for cs in ("bt601-video", "bt709-full"):
+        got = _run_nv12(ctx, y, uv, cs, 360, 640, **norm)
+        ref = O.preprocess_nv12(y, uv, L.NV12_COLOR_SPACES[cs], 360, 640, **norm)
+        np.testing.assert_array_equal(got, ref)
+
+
+def test_nv12_staged_and_generic_kernels_agree(ctx):
+    # an output that starts 4 bytes past a 16-byte boundary takes the generic
+    # per-pixel kernel; both kernels write identical values
+    rng = np.random.default_rng(23)
+    B, H, W, oh, ow = 2, 480, 640, 240, 320
+    y = torch.from_numpy(rng.integers(0, 256, (B, H, W), dtype=np.uint8)).cuda()
+    uv = torch.from_numpy(rng.integers(0, 256, (B, H // 2, W // 2, 2), dtype=np.uint8)).cuda()
+    cfg = L.ImagePreprocess.make(oh, ow, **IMAGENET)
+    n = B * 3 * oh * ow
+    aligned = torch.full((n,), 7.0, device="cuda")
+    shifted = torch.full((n + 1,), 7.0, device="cuda")
+    torch.cuda.synchronize()
+    for out in (aligned, shifted[1:]):
+        L.preprocess_nv12_device(ctx, y, uv, B, H, W, "bt601-video", cfg, out)
+    ctx.synchronize()
+    assert shifted[1:].data_ptr() % 16 == 4
+    np.testing.assert_array_equal(aligned.cpu().numpy(), shifted[1:].cpu().numpy())
+    assert float(shifted[0]) == 7.0
