@@ -116,10 +116,13 @@ __global__ void __launch_bounds__(256) nv12_to_nchw_kernel(MediaArgs a) {
 // the conversion rate, a library division per channel); at full HD it runs
 // at a sixth of the HBM roofline.  This one keeps the arithmetic of
 // swm_nv12_to_nchw_f32 exactly, and removes the rest:
-//   * a block per output row at a time (grid-stride over batch x rows): the
-//     two luma rows and two chroma rows it taps are copied into shared
-//     memory by the bulk-copy engine (cp.async.bulk, one instruction per
-//     row, completion on an mbarrier), kStages rows ahead;
+//   * warp-specialised blocks, grid-stride over batch x output rows: one
+//     producer thread copies, kStages rows ahead, the two luma rows and two
+//     chroma rows each output row taps into shared memory with the
+//     bulk-copy engine (cp.async.bulk, one instruction per row, completion
+//     on an mbarrier) and writes the row's weights and output offset beside
+//     them; the consumer warps take one output row at a time and hand the
+//     stage back through a second mbarrier (no block-wide barrier);
 //   * a thread owns four adjacent output columns for the whole kernel: their
 //     source columns and bilinear weights are computed once, in registers;
 //   * taps are u8 loads from shared memory turned into floats with the 2^23
@@ -140,9 +143,10 @@ __global__ void __launch_bounds__(256) nv12_to_nchw_kernel(MediaArgs a) {
 // order, as the generic kernel's, so its outputs are bit-identical.
 namespace staged {
 
-constexpr uint32_t kStages = 3;
+constexpr uint32_t kStages = 4;
 constexpr uint32_t kMagic = 0x4B000000u;  // the float 2^23
-constexpr uint32_t kMaxThreads = 512;     // 4 columns each: output rows up to 2048
+constexpr uint32_t kMaxConsumers = 512;   // 4 columns each: output rows up to 2048
+constexpr uint32_t kMaxThreads = kMaxConsumers + 32;  // + the producer warp
 constexpr uint32_t kWaitLimit = 1u << 26;
 
 struct f2 {
@@ -293,36 +297,75 @@ __device__ __forceinline__ f2 normalize(f2 v, float mean, float sd, float rcp) {
     return fma(fma(nsd, q, a), r, q);
 }
 
+// Per staged row: the row weights and the output offset, written by the
+// producer next to the row's copies.
+struct RowSlot {
+    float wy, cwy;
+    unsigned long long base;  // element offset of (frame, channel 0, row y, column 0)
+};
+
+// Warp-specialised: the last warp's lane 0 is the producer (row weights and
+// the four bulk copies of each row, kStages rows ahead); the other warps are
+// consumers.  full[s] completes when stage s's bytes have landed, empty[s]
+// when every consumer warp is done with it; no block-wide barrier in the
+// row loop.
 template <uint32_t CS, bool BF16, uint32_t ROWCAP>
-__global__ void __launch_bounds__(kMaxThreads) nv12_staged_kernel(MediaArgs a, StagedMedia m) {
+__global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a, StagedMedia m) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t kStageBytes = 4u * ROWCAP;  // luma y0, luma y1, chroma c0, chroma c1
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    RowSlot* slots = reinterpret_cast<RowSlot*>(smem + kStages * kStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(slots + kStages);
+    uint64_t* empty = full + kStages;
     const uint32_t tid = threadIdx.x, in_w = a.in_w, rows = a.batch * a.out_h;
+    const uint32_t consumers = blockDim.x - 32u;
     if (tid == 0) {
-        for (uint32_t s = 0; s < kStages; ++s) tc::mbar_init(&full[s], 1);
+        for (uint32_t s = 0; s < kStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], consumers / 32u);
+        }
         tc::mbar_fence_init();
     }
     __syncthreads();
 
-    auto issue = [&](uint32_t k, uint32_t s) {
-        const uint32_t r = blockIdx.x + k * gridDim.x;
-        if (r >= rows) return;
-        const uint32_t b = r / a.out_h, y = r - b * a.out_h;
-        const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
-        uint8_t* st = smem + s * kStageBytes;
-        const size_t frame = static_cast<size_t>(b) * a.in_h;
-        tc::mbar_expect_tx(&full[s], 4u * in_w);
-        tc::bulk_g2s(st, a.a + (frame + t.y0) * in_w, in_w, &full[s]);
-        tc::bulk_g2s(st + ROWCAP, a.a + (frame + t.y1) * in_w, in_w, &full[s]);
-        tc::bulk_g2s(st + 2u * ROWCAP, a.uv + (frame / 2u + t.c0) * in_w, in_w, &full[s]);
-        tc::bulk_g2s(st + 3u * ROWCAP, a.uv + (frame / 2u + t.c1) * in_w, in_w, &full[s]);
-    };
-    if (tid == 0)
-        for (uint32_t s = 0; s < kStages; ++s) issue(s, s);
+    if (tid >= consumers) {
+        if (tid != consumers) return;
+        // producer
+        const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
+        uint32_t k = 0;
+        for (;; ++k) {
+            const uint32_t r = blockIdx.x + k * gridDim.x;
+            if (r >= rows) break;
+            const uint32_t s = k % kStages;
+            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u)) {
+                m.err[1] = static_cast<int>(blockIdx.x);
+                m.err[2] = static_cast<int>(k);
+                m.err[3] = 2;
+                m.err[0] = 1;
+                break;
+            }
+            const uint32_t b = r / a.out_h, y = r - b * a.out_h;
+            const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
+            slots[s].wy = t.wy;
+            slots[s].cwy = t.cwy;
+            slots[s].base = ((static_cast<unsigned long long>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w;
+            uint8_t* st = smem + s * kStageBytes;
+            const size_t frame = static_cast<size_t>(b) * a.in_h;
+            tc::mbar_expect_tx(&full[s], 4u * in_w);
+            tc::bulk_g2s(st, a.a + (frame + t.y0) * in_w, in_w, &full[s]);
+            tc::bulk_g2s(st + ROWCAP, a.a + (frame + t.y1) * in_w, in_w, &full[s]);
+            tc::bulk_g2s(st + 2u * ROWCAP, a.uv + (frame / 2u + t.c0) * in_w, in_w, &full[s]);
+            tc::bulk_g2s(st + 3u * ROWCAP, a.uv + (frame / 2u + t.c1) * in_w, in_w, &full[s]);
+        }
+        // the copies still in flight land before the block's shared memory
+        // can be released
+        for (uint32_t j = k > kStages ? k - kStages : 0u; j < k; ++j)
+            wait_stage(&full[j % kStages], (j / kStages) & 1u);
+        return;
+    }
 
-    // the four output columns of this thread: source columns, weights
-    const uint32_t x4 = tid * 4u;
+    // consumers: the four output columns of this thread, their source
+    // columns and weights
+    const uint32_t x4 = tid * 4u, lane = tid & 31u;
     const bool active = x4 < a.out_w;
     uint32_t l0[4], l1[4], u0[4], u1[4];
     float wx[4], cwx[4];
@@ -346,23 +389,28 @@ __global__ void __launch_bounds__(kMaxThreads) nv12_staged_kernel(MediaArgs a, S
     const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
     const f2 cwxa = mk(cwx[0], cwx[1]), cwxb = mk(cwx[2], cwx[3]);
     const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
-    const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
 
     // one output row from stage S (a compile-time shared-memory offset);
     // returns false once the block's rows are done or a copy never landed
     auto step = [&](uint32_t k, auto stage) -> bool {
         constexpr uint32_t S = decltype(stage)::value;
-        const uint32_t r = blockIdx.x + k * gridDim.x;
-        if (r >= rows) return false;
-        const uint32_t b = r / a.out_h, y = r - b * a.out_h;
-        const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
-        const bool ok = wait_stage(&full[S], (k / kStages) & 1u);
-        if (ok && active) {
+        if (blockIdx.x + k * gridDim.x >= rows) return false;
+        if (!wait_stage(&full[S], (k / kStages) & 1u)) {
+            if (lane == 0) {
+                m.err[1] = static_cast<int>(blockIdx.x);
+                m.err[2] = static_cast<int>(k);
+                m.err[3] = 1;
+                m.err[0] = 1;
+            }
+            return false;
+        }
+        if (active) {
+            const RowSlot rs = slots[S];
             const uint8_t* ly0 = smem + S * kStageBytes;
             const uint8_t* ly1 = ly0 + ROWCAP;
             const uint8_t* cr0 = ly0 + 2u * ROWCAP;
             const uint8_t* cr1 = ly0 + 3u * ROWCAP;
-            const f2 wy = splat(t.wy), cwy = splat(t.cwy);
+            const f2 wy = splat(rs.wy), cwy = splat(rs.cwy);
             f2 out[3][2];
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
@@ -398,7 +446,7 @@ __global__ void __launch_bounds__(kMaxThreads) nv12_staged_kernel(MediaArgs a, S
                 out[1][p] = normalize(G, a.mean[1], a.std[1], m.rcp_std[1]);
                 out[2][p] = normalize(B, a.mean[2], a.std[2], m.rcp_std[2]);
             }
-            const size_t base = ((static_cast<size_t>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w + x4;
+            const size_t base = rs.base + x4;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
                 if constexpr (BF16) {
@@ -414,35 +462,25 @@ __global__ void __launch_bounds__(kMaxThreads) nv12_staged_kernel(MediaArgs a, S
                 }
             }
         }
-        // every thread is done with stage S before it is refilled
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) {
-                m.err[1] = static_cast<int>(blockIdx.x);
-                m.err[2] = static_cast<int>(k);
-                m.err[0] = 1;
-                // rows still in flight land before the block's shared memory is released
-                for (uint32_t j = k; j < k + kStages; ++j)
-                    if (blockIdx.x + j * gridDim.x < rows) wait_stage(&full[j % kStages], (j / kStages) & 1u);
-            }
-            __syncthreads();
-            return false;
-        }
-        if (tid == 0) issue(k + kStages, S);
+        // the warp is done with stage S
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[S]);
         return true;
     };
-    static_assert(kStages == 3, "the row loop below is unrolled over three stages");
+    static_assert(kStages == 4, "the row loop below is unrolled over four stages");
     for (uint32_t k = 0;; k += kStages) {
         if (!step(k, std::integral_constant<uint32_t, 0>{})) break;
         if (!step(k + 1, std::integral_constant<uint32_t, 1>{})) break;
         if (!step(k + 2, std::integral_constant<uint32_t, 2>{})) break;
+        if (!step(k + 3, std::integral_constant<uint32_t, 3>{})) break;
     }
 }
 
 template <uint32_t CS, bool BF16, uint32_t ROWCAP>
 cudaError_t launch_one(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
     auto kern = nv12_staged_kernel<CS, BF16, ROWCAP>;
-    const uint32_t smem = kStages * 4u * ROWCAP + kStages * sizeof(uint64_t);
-    const uint32_t threads = ((a.out_w / 4u + 31u) / 32u) * 32u;
+    const uint32_t smem = kStages * (4u * ROWCAP + sizeof(RowSlot) + 2u * sizeof(uint64_t));
+    const uint32_t threads = ((a.out_w / 4u + 31u) / 32u) * 32u + 32u;
     static int configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -481,7 +519,7 @@ cudaError_t launch_cs(const MediaArgs& a, const StagedMedia& m, cudaStream_t str
 bool nv12_staged_eligible(const MediaArgs& a) {
     const auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
     if (a.in_w % 16u != 0 || a.in_w > 4096u || a.in_h < 2u) return false;
-    if (a.out_w % 4u != 0 || a.out_w > 4u * staged::kMaxThreads || a.out_h == 0) return false;
+    if (a.out_w % 4u != 0 || a.out_w > 4u * staged::kMaxConsumers || a.out_h == 0) return false;
     if (!aligned(a.a, 16) || !aligned(a.uv, 16) || !aligned(a.out, a.bf16 ? 8 : 16)) return false;
     if (static_cast<uint64_t>(a.batch) * a.out_h >= (1ull << 31) ||
         static_cast<uint64_t>(a.batch) * a.in_h >= (1ull << 31))
