@@ -10,7 +10,8 @@ reference).  A "step" is one plan call.
     python bench.py --impl reference ...   # the CPU restatement on the host cores
     python bench.py --workload fleet [--shard auto|vehicles|candidates] [--vehicles V --samples S --horizon T]
     python bench.py --workload lewm-vector|lewm-image    # LeWM CEM (vector obs) / MPPI (NV12 frames + ViT)
-    python bench.py --workload media [--precision f32|bf16]  # NV12 -> NCHW preprocessing vs the HBM roofline
+    python bench.py --workload media [--precision f32|bf16] [--media-format nv12|rgb|rgba]
+                                           # frame preprocessing -> NCHW vs the HBM roofline
     python bench.py --workload closed-loop [--dynamics learned|nominal] [--random-domains N]
                                           # closed-loop session scenarios; --steps = control steps per scenario
 
@@ -687,18 +688,27 @@ def run_media(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     B, H, W = args.frames, 1080, 1920
     bf16 = args.precision == "bf16"
+    fmt = args.media_format
+    channels = {"nv12": 1.5, "rgb": 3, "rgba": 4}[fmt]
     ctx = L.Context(local_rank)
     stream = ctx.torch_stream()
     g = torch.Generator().manual_seed(7 + rank)
-    host_y = torch.randint(0, 256, (B, H, W), dtype=torch.uint8, generator=g).pin_memory()
-    host_uv = torch.randint(0, 256, (B, H // 2, W // 2, 2), dtype=torch.uint8, generator=g).pin_memory()
+    if fmt == "nv12":
+        host_y = torch.randint(0, 256, (B, H, W), dtype=torch.uint8, generator=g).pin_memory()
+        host_uv = torch.randint(0, 256, (B, H // 2, W // 2, 2), dtype=torch.uint8, generator=g).pin_memory()
+    else:
+        host_y = torch.randint(0, 256, (B, H, W, int(channels)), dtype=torch.uint8, generator=g).pin_memory()
+        host_uv = torch.empty(0, dtype=torch.uint8).pin_memory()
     dev_y, dev_uv = host_y.cuda(), host_uv.cuda()
     out = torch.empty((B, 3, H, W), dtype=torch.bfloat16 if bf16 else torch.float32, device="cuda")
     cfg = L.ImagePreprocess.make(H, W, (0.485, 0.456, 0.406), (0.229, 0.224, 0.225))
     torch.cuda.synchronize()
 
     def step():
-        L.preprocess_nv12_device(ctx, dev_y, dev_uv, B, H, W, "bt601-video", cfg, out, bf16=bf16)
+        if fmt == "nv12":
+            L.preprocess_nv12_device(ctx, dev_y, dev_uv, B, H, W, "bt601-video", cfg, out, bf16=bf16)
+        else:
+            L.preprocess_packed_device(ctx, dev_y, B, H, W, fmt, cfg, out, 0, 0, bf16)
 
     for _ in range(args.warmup):
         step()
@@ -730,16 +740,17 @@ def run_media(args, rank, world, local_rank):
         e2e.append(time.perf_counter() - t0)
     ms = float(np.median(times))
     px = B * H * W
-    bytes_per_call = px * (1.5 + (6 if bf16 else 12))
+    bytes_per_call = px * (channels + (6 if bf16 else 12))
     achieved = bytes_per_call / (ms * 1e-3) / 1e9
     peak = float(measured_peaks().get("hbm_gbs", 6650.0))
     result = {
-        "metric": f"frames/s of NV12 -> normalised NCHW preprocessing (1920x1080, batch {B}, same-size output)",
+        "metric": f"frames/s of {fmt.upper()} -> normalised NCHW preprocessing (1920x1080, batch {B}, same-size output)",
         "value": round(world * B * 1e3 / ms, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u8->" + ("bf16" if bf16 else "f32"), "data": "synthetic (seeded uniform NV12)",
-        "config": {"workload": f"NV12 bt601-video {W}x{H} x {B} -> NCHW {'bf16' if bf16 else 'f32'}, ImageNet "
-                               "mean/std", "parallelism": f"replicas x{world}",
+        "vs_baseline": None, "dtype": "u8->" + ("bf16" if bf16 else "f32"),
+        "data": f"synthetic (seeded uniform {fmt.upper()})",
+        "config": {"workload": f"{'NV12 bt601-video' if fmt == 'nv12' else fmt.upper()} {W}x{H} x {B} -> NCHW "
+                               f"{'bf16' if bf16 else 'f32'}, ImageNet mean/std", "parallelism": f"replicas x{world}",
                    "l2": "not flushed: inputs + outputs exceed the L2"},
         "e2e": {"value": round(world * B / float(np.median(e2e)), 1), "unit": "frames/s",
                 "h2d_bytes_per_step": int(host_y.numel() + host_uv.numel()),
@@ -748,10 +759,11 @@ def run_media(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": "MEASURED_PEAKS hbm_gbs (of measured)",
-                     "note": "achieved = (1.5 B NV12 read + output bytes written) per pixel / p50 time"},
+                     "note": f"achieved = ({channels} B of {fmt.upper()} read + output bytes written) per pixel "
+                             "/ p50 time"},
         "clocks": clocks.summary(),
     }
-    if args.cpu_baseline and rank == 0:
+    if args.cpu_baseline and rank == 0 and fmt == "nv12":
         result["cpu_baseline"] = cpu_baseline_media(host_y[:2].numpy(), host_uv[:2].numpy(), args.cpu_seconds)
     del host_y, host_uv, host_out
     ctx.close()
@@ -1072,6 +1084,8 @@ def main():
                     help="closed-loop: sampled domains beside the nominal one (the reference bench uses 20)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--frames", type=int, default=32, help="media workload: full-HD frames per batch")
+    ap.add_argument("--media-format", choices=["nv12", "rgb", "rgba"], default="nv12",
+                    help="media workload: NV12 planes or packed RGB / RGBA frames")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -616,7 +616,11 @@ void lwm_image_preprocess_imagenet_224(lwm_image_preprocess* out);
  * (src/media/mod.rs:275-343, 470-543; kernel :1113-1194).  `input` is a
  * device [B,H,W,C] u8 frame batch (C = 3 or 4 by `format`); `output` is a
  * device [B,3,oh,ow] buffer (history_len == 0) or [B,history_len,3,oh,ow]
- * with slot `history_slot` written; out_bf16 selects bf16 instead of f32. */
+ * with slot `history_slot` written; out_bf16 selects bf16 instead of f32.
+ * With W x channels a multiple of 16 up to 8192 bytes and the output /
+ * normalisation conditions of lwm_preprocess_nv12_device below, a
+ * row-staged kernel runs; otherwise a per-pixel kernel.  Both write the same
+ * values. */
 lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint32_t batch, uint32_t height,
                                         uint32_t width, int32_t format, const lwm_image_preprocess* cfg,
                                         uint32_t history_len, uint32_t history_slot, int32_t out_bf16,

@@ -977,7 +977,7 @@ lwm_status lwm_ctx_synchronize(lwm_ctx* ctx) {
         const std::string where = "block " + std::to_string(ctx->media_err[1]) + ", row step " +
                                   std::to_string(ctx->media_err[2]);
         for (int i = 0; i < 4; ++i) ctx->media_err[i] = 0;
-        return fail(LWM_CUDA_ERROR, "NV12 preprocessing: a source-row copy never completed (" + where +
+        return fail(LWM_CUDA_ERROR, "image preprocessing: a source-row copy never completed (" + where +
                                         "); that launch's output is incomplete");
     }
     return LWM_OK;
@@ -1764,6 +1764,24 @@ static lwm_status validate_preprocess(const lwm_image_preprocess* cfg, uint32_t 
     return LWM_OK;
 }
 
+// The error word of the row-staged preprocessing kernels (mapped pinned
+// host memory, read by lwm_ctx_synchronize), allocated on first use.
+static lwm_status ensure_media_err(lwm_ctx* ctx) {
+    if (ctx->media_err) return LWM_OK;
+    void* dev = nullptr;
+    int* host = nullptr;
+    LWM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&host), 4 * sizeof(int), cudaHostAllocMapped));
+    for (int i = 0; i < 4; ++i) host[i] = 0;
+    const cudaError_t e = cudaHostGetDevicePointer(&dev, host, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(host);
+        return fail(LWM_CUDA_ERROR, std::string("cudaHostGetDevicePointer: ") + cudaGetErrorString(e));
+    }
+    ctx->media_err = host;
+    ctx->media_err_dev = static_cast<int*>(dev);
+    return LWM_OK;
+}
+
 static lwm::MediaArgs media_args(const lwm_image_preprocess* cfg, uint32_t B, uint32_t H, uint32_t W,
                                  uint32_t history_len, uint32_t slot, int32_t bf16, void* out) {
     lwm::MediaArgs a{};
@@ -1791,7 +1809,12 @@ lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint
     a.a = input;
     a.channels = format >= 2 ? 4 : 3;
     a.format = static_cast<uint32_t>(format);
-    LWM_CUDA(lwm::launch_media(a, false, ctx->stream));
+    if (lwm::packed_staged_eligible(a)) {
+        LWM_TRY(ensure_media_err(ctx));
+        LWM_CUDA(lwm::launch_packed_staged(a, ctx->media_err_dev, ctx->stream));
+    } else {
+        LWM_CUDA(lwm::launch_media(a, false, ctx->stream));
+    }
     ctx->launches += 1;
     return LWM_OK;
 }
@@ -1816,13 +1839,7 @@ lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, cons
     a.channels = 1;
     a.format = static_cast<uint32_t>(color_space);
     if (lwm::nv12_staged_eligible(a)) {
-        if (!ctx->media_err) {
-            void* dev = nullptr;
-            LWM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ctx->media_err), 4 * sizeof(int), cudaHostAllocMapped));
-            for (int i = 0; i < 4; ++i) ctx->media_err[i] = 0;
-            LWM_CUDA(cudaHostGetDevicePointer(&dev, ctx->media_err, 0));
-            ctx->media_err_dev = static_cast<int*>(dev);
-        }
+        LWM_TRY(ensure_media_err(ctx));
         LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, ctx->stream));
     } else {
         LWM_CUDA(lwm::launch_media(a, true, ctx->stream));

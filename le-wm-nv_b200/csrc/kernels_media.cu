@@ -288,13 +288,37 @@ __device__ __forceinline__ void to_rgb(const Prod& mul_sep, f2 Y, f2 U, f2 V, f2
     }
 }
 
-// (clamp(v) / 255 - mean) / std, the division as described above.
-__device__ __forceinline__ f2 normalize(f2 v, float mean, float sd, float rcp) {
-    const f2 a = sub(unit_clamp(v), splat(mean));
+// a / sd with rcp = RN(1 / sd), the division as described above.
+__device__ __forceinline__ f2 divide(f2 a, float sd, float rcp) {
     const f2 r = splat(rcp), nsd = splat(-sd);
     f2 q = mul(a, r);
     q = fma(fma(nsd, q, a), r, q);
     return fma(fma(nsd, q, a), r, q);
+}
+
+// (clamp(v) / 255 - mean) / std.
+__device__ __forceinline__ f2 normalize(f2 v, float mean, float sd, float rcp) {
+    return divide(sub(unit_clamp(v), splat(mean)), sd, rcp);
+}
+
+// The three channel planes of four adjacent output pixels: one 16-byte
+// (f32) or 8-byte (bf16) store per channel.
+template <bool BF16>
+__device__ __forceinline__ void store4(const MediaArgs& a, size_t base, size_t plane, const f2 (&out)[3][2]) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        if constexpr (BF16) {
+            const __nv_bfloat162 p0 = __floats2bfloat162_rn(lo(out[c][0]), hi(out[c][0]));
+            const __nv_bfloat162 p1 = __floats2bfloat162_rn(lo(out[c][1]), hi(out[c][1]));
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&p0);
+            w.y = *reinterpret_cast<const uint32_t*>(&p1);
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + base + c * plane) = w;
+        } else {
+            *reinterpret_cast<float4*>(static_cast<float*>(a.out) + base + c * plane) =
+                make_float4(lo(out[c][0]), hi(out[c][0]), lo(out[c][1]), hi(out[c][1]));
+        }
+    }
 }
 
 // Per staged row: the row weights and the output offset, written by the
@@ -446,21 +470,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a
                 out[1][p] = normalize(G, a.mean[1], a.std[1], m.rcp_std[1]);
                 out[2][p] = normalize(B, a.mean[2], a.std[2], m.rcp_std[2]);
             }
-            const size_t base = rs.base + x4;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                if constexpr (BF16) {
-                    const __nv_bfloat162 p0 = __floats2bfloat162_rn(lo(out[c][0]), hi(out[c][0]));
-                    const __nv_bfloat162 p1 = __floats2bfloat162_rn(lo(out[c][1]), hi(out[c][1]));
-                    uint2 w;
-                    w.x = *reinterpret_cast<const uint32_t*>(&p0);
-                    w.y = *reinterpret_cast<const uint32_t*>(&p1);
-                    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + base + c * plane) = w;
-                } else {
-                    *reinterpret_cast<float4*>(static_cast<float*>(a.out) + base + c * plane) =
-                        make_float4(lo(out[c][0]), hi(out[c][0]), lo(out[c][1]), hi(out[c][1]));
-                }
-            }
+            store4<BF16>(a, rs.base + x4, plane, out);
         }
         // the warp is done with stage S
         __syncwarp();
@@ -476,10 +486,11 @@ __global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a
     }
 }
 
-template <uint32_t CS, bool BF16, uint32_t ROWCAP>
-cudaError_t launch_one(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
-    auto kern = nv12_staged_kernel<CS, BF16, ROWCAP>;
-    const uint32_t smem = kStages * (4u * ROWCAP + sizeof(RowSlot) + 2u * sizeof(uint64_t));
+// Launches a staged kernel with one consumer thread per 4 output columns
+// plus the producer warp, as many blocks as fit on the device at once (or
+// one per output row when there are fewer rows).
+template <auto Kern>
+cudaError_t launch_grid(uint32_t smem, const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
     const uint32_t threads = ((a.out_w / 4u + 31u) / 32u) * 32u + 32u;
     static int configured[64] = {};
     int dev = 0;
@@ -489,22 +500,28 @@ cudaError_t launch_one(const MediaArgs& a, const StagedMedia& m, cudaStream_t st
     static int per_sm[64] = {}, sms[64] = {};
     static uint32_t per_sm_threads[64] = {};
     if (!configured[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
     if (per_sm_threads[dev] != threads) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], kern, static_cast<int>(threads), smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], Kern, static_cast<int>(threads), smem);
         if (e != cudaSuccess) return e;
         per_sm_threads[dev] = threads;
     }
     const uint64_t rows = static_cast<uint64_t>(a.batch) * a.out_h;
     const uint64_t resident = static_cast<uint64_t>(per_sm[dev] > 0 ? per_sm[dev] : 1) * sms[dev];
     const uint32_t grid = static_cast<uint32_t>(rows < resident ? rows : resident);
-    kern<<<grid, threads, smem, stream>>>(a, m);
+    Kern<<<grid, threads, smem, stream>>>(a, m);
     return cudaGetLastError();
+}
+
+template <uint32_t CS, bool BF16, uint32_t ROWCAP>
+cudaError_t launch_one(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
+    const uint32_t smem = kStages * (4u * ROWCAP + sizeof(RowSlot) + 2u * sizeof(uint64_t));
+    return launch_grid<nv12_staged_kernel<CS, BF16, ROWCAP>>(smem, a, m, stream);
 }
 
 template <uint32_t CS>
@@ -514,13 +531,184 @@ cudaError_t launch_cs(const MediaArgs& a, const StagedMedia& m, cudaStream_t str
     return small ? launch_one<CS, false, 2048>(a, m, stream) : launch_one<CS, false, 4096>(a, m, stream);
 }
 
+// ------------------------------------------------------------------------
+// Packed RGB / BGR / RGBA / BGRA frames, row-staged the same way
+// (swm_packed_u8_to_nchw_f32, src/media/mod.rs:1113-1194): the producer
+// bulk-copies the two source rows each output row taps; each consumer
+// thread keeps its four columns' byte offsets and weights in registers and
+// makes all three channels of its pixels.  The source coordinates are
+// clamped below at 0 only, as the reference does (the upper neighbour is
+// clamped to the last row / column, where the weight no longer matters:
+// both taps are the same byte).
+template <uint32_t C, bool SWAP, bool BF16, uint32_t ROWCAP>
+__global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs a, StagedMedia m) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t kStageBytes = 2u * ROWCAP;  // source rows y0, y1
+    RowSlot* slots = reinterpret_cast<RowSlot*>(smem + kStages * kStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(slots + kStages);
+    uint64_t* empty = full + kStages;
+    const uint32_t tid = threadIdx.x, in_w = a.in_w, rows = a.batch * a.out_h, row_bytes = a.in_w * C;
+    const uint32_t consumers = blockDim.x - 32u;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], consumers / 32u);
+        }
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (tid >= consumers) {
+        if (tid != consumers) return;
+        // producer
+        const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
+        uint32_t k = 0;
+        for (;; ++k) {
+            const uint32_t r = blockIdx.x + k * gridDim.x;
+            if (r >= rows) break;
+            const uint32_t s = k % kStages;
+            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u)) {
+                m.err[1] = static_cast<int>(blockIdx.x);
+                m.err[2] = static_cast<int>(k);
+                m.err[3] = 2;
+                m.err[0] = 1;
+                break;
+            }
+            const uint32_t b = r / a.out_h, y = r - b * a.out_h;
+            float f;
+            const float sy = fmaxf((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, 0.0f);
+            const uint32_t y0 = floor_u(sy, f), y1 = y0 + 1u < a.in_h ? y0 + 1u : y0;
+            slots[s].wy = sy - f;
+            slots[s].base = ((static_cast<unsigned long long>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w;
+            uint8_t* st = smem + s * kStageBytes;
+            const size_t frame = static_cast<size_t>(b) * a.in_h;
+            tc::mbar_expect_tx(&full[s], 2u * row_bytes);
+            tc::bulk_g2s(st, a.a + (frame + y0) * row_bytes, row_bytes, &full[s]);
+            tc::bulk_g2s(st + ROWCAP, a.a + (frame + y1) * row_bytes, row_bytes, &full[s]);
+        }
+        for (uint32_t j = k > kStages ? k - kStages : 0u; j < k; ++j)
+            wait_stage(&full[j % kStages], (j / kStages) & 1u);
+        return;
+    }
+
+    // consumers: byte offsets of the two source columns of each of this
+    // thread's four output columns, and their weights
+    const uint32_t x4 = tid * 4u, lane = tid & 31u;
+    const bool active = x4 < a.out_w;
+    uint32_t o0[4], o1[4];
+    float wx[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t x = active ? x4 + i : 0u;
+        float f;
+        const float sx = fmaxf((static_cast<float>(x) + 0.5f) * m.ratio_w - 0.5f, 0.0f);
+        const uint32_t x0 = floor_u(sx, f);
+        o0[i] = C * x0;
+        o1[i] = C * (x0 + 1u < in_w ? x0 + 1u : x0);
+        wx[i] = sx - f;
+    }
+    const Prod prod{splat(m.neg_zero)};
+    const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
+    const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
+
+    auto step = [&](uint32_t k, auto stage) -> bool {
+        constexpr uint32_t S = decltype(stage)::value;
+        if (blockIdx.x + k * gridDim.x >= rows) return false;
+        if (!wait_stage(&full[S], (k / kStages) & 1u)) {
+            if (lane == 0) {
+                m.err[1] = static_cast<int>(blockIdx.x);
+                m.err[2] = static_cast<int>(k);
+                m.err[3] = 1;
+                m.err[0] = 1;
+            }
+            return false;
+        }
+        if (active) {
+            const RowSlot rs = slots[S];
+            const uint8_t* r0 = smem + S * kStageBytes;
+            const uint8_t* r1 = r0 + ROWCAP;
+            const f2 wy = splat(rs.wy);
+            f2 out[3][2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int i = 2 * p, j = 2 * p + 1;
+                const f2 wxp = p ? wxb : wxa;
+                f2 t00[3], t01[3], t10[3], t11[3];
+                if constexpr (C == 4) {
+                    // one 32-bit load per tap, the channels picked by byte permutes
+                    const uint32_t w00i = *reinterpret_cast<const uint32_t*>(r0 + o0[i]);
+                    const uint32_t w00j = *reinterpret_cast<const uint32_t*>(r0 + o0[j]);
+                    const uint32_t w01i = *reinterpret_cast<const uint32_t*>(r0 + o1[i]);
+                    const uint32_t w01j = *reinterpret_cast<const uint32_t*>(r0 + o1[j]);
+                    const uint32_t w10i = *reinterpret_cast<const uint32_t*>(r1 + o0[i]);
+                    const uint32_t w10j = *reinterpret_cast<const uint32_t*>(r1 + o0[j]);
+                    const uint32_t w11i = *reinterpret_cast<const uint32_t*>(r1 + o1[i]);
+                    const uint32_t w11j = *reinterpret_cast<const uint32_t*>(r1 + o1[j]);
+#pragma unroll
+                    for (uint32_t c = 0; c < 3; ++c) {
+                        const uint32_t sel = 0x7540u | (SWAP ? 2u - c : c);
+                        t00[c] = mk(magic_byte(w00i, sel), magic_byte(w00j, sel));
+                        t01[c] = mk(magic_byte(w01i, sel), magic_byte(w01j, sel));
+                        t10[c] = mk(magic_byte(w10i, sel), magic_byte(w10j, sel));
+                        t11[c] = mk(magic_byte(w11i, sel), magic_byte(w11j, sel));
+                    }
+                } else {
+#pragma unroll
+                    for (uint32_t c = 0; c < 3; ++c) {
+                        const uint32_t sc = SWAP ? 2u - c : c;
+                        t00[c] = mk(magic_u8(r0[o0[i] + sc]), magic_u8(r0[o0[j] + sc]));
+                        t01[c] = mk(magic_u8(r0[o1[i] + sc]), magic_u8(r0[o1[j] + sc]));
+                        t10[c] = mk(magic_u8(r1[o0[i] + sc]), magic_u8(r1[o0[j] + sc]));
+                        t11[c] = mk(magic_u8(r1[o1[i] + sc]), magic_u8(r1[o1[j] + sc]));
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    const f2 v = prod(bilerp(prod, t00[c], t01[c], t10[c], t11[c], wxp, wy), 0.00392156862745098f);
+                    out[c][p] = divide(sub(v, splat(a.mean[c])), a.std[c], m.rcp_std[c]);
+                }
+            }
+            store4<BF16>(a, rs.base + x4, plane, out);
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[S]);
+        return true;
+    };
+    static_assert(kStages == 4, "the row loop below is unrolled over four stages");
+    for (uint32_t k = 0;; k += kStages) {
+        if (!step(k, std::integral_constant<uint32_t, 0>{})) break;
+        if (!step(k + 1, std::integral_constant<uint32_t, 1>{})) break;
+        if (!step(k + 2, std::integral_constant<uint32_t, 2>{})) break;
+        if (!step(k + 3, std::integral_constant<uint32_t, 3>{})) break;
+    }
+}
+
+template <uint32_t C, bool SWAP, bool BF16>
+cudaError_t launch_packed_rc(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
+    if (a.in_w * C <= 4096u) {
+        constexpr uint32_t R = 4096;
+        return launch_grid<packed_staged_kernel<C, SWAP, BF16, R>>(
+            kStages * (2u * R + sizeof(RowSlot) + 2u * sizeof(uint64_t)), a, m, stream);
+    }
+    constexpr uint32_t R = 8192;
+    return launch_grid<packed_staged_kernel<C, SWAP, BF16, R>>(
+        kStages * (2u * R + sizeof(RowSlot) + 2u * sizeof(uint64_t)), a, m, stream);
+}
+
+template <uint32_t C, bool SWAP>
+cudaError_t launch_packed(const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
+    return a.bf16 ? launch_packed_rc<C, SWAP, true>(a, m, stream) : launch_packed_rc<C, SWAP, false>(a, m, stream);
+}
+
 }  // namespace staged
 
-bool nv12_staged_eligible(const MediaArgs& a) {
-    const auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
-    if (a.in_w % 16u != 0 || a.in_w > 4096u || a.in_h < 2u) return false;
+namespace {
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+// What both staged kernels need of the output and the normalisation.
+bool staged_common_ok(const MediaArgs& a) {
     if (a.out_w % 4u != 0 || a.out_w > 4u * staged::kMaxConsumers || a.out_h == 0) return false;
-    if (!aligned(a.a, 16) || !aligned(a.uv, 16) || !aligned(a.out, a.bf16 ? 8 : 16)) return false;
+    if (!aligned(a.out, a.bf16 ? 8 : 16)) return false;
     if (static_cast<uint64_t>(a.batch) * a.out_h >= (1ull << 31) ||
         static_cast<uint64_t>(a.batch) * a.in_h >= (1ull << 31))
         return false;
@@ -535,13 +723,42 @@ bool nv12_staged_eligible(const MediaArgs& a) {
     return true;
 }
 
-cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream) {
+StagedMedia staged_params(const MediaArgs& a, int* err) {
     StagedMedia m{};
     m.ratio_h = static_cast<float>(a.in_h) / static_cast<float>(a.out_h);
     m.ratio_w = static_cast<float>(a.in_w) / static_cast<float>(a.out_w);
     for (int c = 0; c < 3; ++c) m.rcp_std[c] = 1.0f / a.std[c];
     m.err = err;
     m.neg_zero = -0.0f;
+    return m;
+}
+}  // namespace
+
+bool nv12_staged_eligible(const MediaArgs& a) {
+    if (a.in_w % 16u != 0 || a.in_w > 4096u || a.in_h < 2u) return false;
+    if (!aligned(a.a, 16) || !aligned(a.uv, 16)) return false;
+    return staged_common_ok(a);
+}
+
+bool packed_staged_eligible(const MediaArgs& a) {
+    const uint64_t row_bytes = static_cast<uint64_t>(a.in_w) * a.channels;
+    if (a.format > 3u || (a.channels != 3u && a.channels != 4u)) return false;
+    if (row_bytes % 16u != 0 || row_bytes > 8192u || a.in_h == 0 || !aligned(a.a, 16)) return false;
+    return staged_common_ok(a);
+}
+
+cudaError_t launch_packed_staged(const MediaArgs& a, int* err, cudaStream_t stream) {
+    const StagedMedia m = staged_params(a, err);
+    switch (a.format) {
+        case 0: return staged::launch_packed<3, false>(a, m, stream);
+        case 1: return staged::launch_packed<3, true>(a, m, stream);
+        case 2: return staged::launch_packed<4, false>(a, m, stream);
+        default: return staged::launch_packed<4, true>(a, m, stream);
+    }
+}
+
+cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream) {
+    const StagedMedia m = staged_params(a, err);
     switch (a.format) {
         case 0: return staged::launch_cs<0>(a, m, stream);
         case 1: return staged::launch_cs<1>(a, m, stream);

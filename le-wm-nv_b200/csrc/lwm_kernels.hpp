@@ -246,6 +246,12 @@ struct StagedMedia {
 };
 bool nv12_staged_eligible(const MediaArgs& a);
 cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream);
+// The row-staged packed RGB / BGR / RGBA / BGRA kernel, bit-identical with
+// launch_media's packed kernel where eligible (row bytes W x channels a
+// multiple of 16 up to 8192, the output and normalisation conditions as
+// above).
+bool packed_staged_eligible(const MediaArgs& a);
+cudaError_t launch_packed_staged(const MediaArgs& a, int* err, cudaStream_t stream);
 
 // Rows per cluster (one wave of co-resident clusters when possible) and MPPI
 // partials per vehicle of the fused SkyJEPA kernel.

@@ -167,3 +167,38 @@ def test_nv12_staged_and_generic_kernels_agree(ctx):
     assert shifted[1:].data_ptr() % 16 == 4
     np.testing.assert_array_equal(aligned.cpu().numpy(), shifted[1:].cpu().numpy())
     assert float(shifted[0]) == 7.0
+
+
+# Shapes the row-staged packed kernel takes (row bytes W x channels a multiple
+# of 16 up to 8192, output width a multiple of 4): full HD at its own size
+# (RGB 5760-byte and RGBA 7680-byte rows), up- and down-scaling, 2048-pixel
+# RGBA rows, two-row frames.
+PACKED_STAGED = [(1, 1080, 1920, 1080, 1920), (2, 32, 64, 100, 200), (2, 720, 1280, 360, 640),
+                 (1, 4, 2048, 8, 2048), (1, 2, 16, 3, 8)]
+
+
+@pytest.mark.parametrize("fmt", ["rgb", "bgr", "rgba", "bgra"])
+@pytest.mark.parametrize("size", PACKED_STAGED)
+def test_packed_row_staged_matches_oracle_bit_exact(ctx, fmt, size):
+    B, H, W, oh, ow = size
+    C = 4 if fmt in ("rgba", "bgra") else 3
+    rng = np.random.default_rng(zlib.crc32(repr(("packed-staged", fmt, size)).encode()))
+    frames = rng.integers(0, 256, (B, H, W, C), dtype=np.uint8)
+    got = _run_packed(ctx, frames, fmt, oh, ow, **IMAGENET)
+    ref = O.preprocess_packed(frames, L.PACKED_FORMATS[fmt], oh, ow, **IMAGENET)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_packed_staged_and_generic_kernels_agree(ctx):
+    rng = np.random.default_rng(29)
+    B, H, W, oh, ow = 2, 240, 320, 120, 160
+    frames = torch.from_numpy(rng.integers(0, 256, (B, H, W, 3), dtype=np.uint8)).cuda()
+    cfg = L.ImagePreprocess.make(oh, ow, mean=(0.5, 0.01, 0.9), std=(0.01, 3.7, 1e-3))
+    n = B * 3 * oh * ow
+    aligned = torch.full((n,), 7.0, device="cuda")
+    shifted = torch.full((n + 1,), 7.0, device="cuda")
+    torch.cuda.synchronize()
+    for out in (aligned, shifted[1:]):
+        L.preprocess_packed_device(ctx, frames, B, H, W, "rgb", cfg, out)
+    ctx.synchronize()
+    np.testing.assert_array_equal(aligned.cpu().numpy(), shifted[1:].cpu().numpy())
