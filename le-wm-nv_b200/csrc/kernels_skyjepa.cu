@@ -815,14 +815,29 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
                 const uint32_t mrow = grp * G::R + my_r;
                 const float* xe = s_emb + (mrow * T + t) * E;
                 float gi[3];
+                if (E == 4) {
+                    // the common width: one 16-byte load per operand (the
+                    // same fmas in the same order as the loop below)
+                    const float4 x = *reinterpret_cast<const float4*>(xe);
 #pragma unroll
-                for (int g = 0; g < 3; ++g) {
-                    const float* wi = s_wih + (g * G::U + my_local) * E;
-                    float s = 0.0f;
+                    for (int g = 0; g < 3; ++g) {
+                        const float4 w = *reinterpret_cast<const float4*>(s_wih + (g * G::U + my_local) * 4);
+                        float s = fmaf(x.x, w.x, 0.0f);
+                        s = fmaf(x.y, w.y, s);
+                        s = fmaf(x.z, w.z, s);
+                        s = fmaf(x.w, w.w, s);
+                        gi[g] = s + s_bih[g * G::U];
+                    }
+                } else {
 #pragma unroll
-                    for (int e = 0; e < kMaxTcnCh; ++e)
-                        if (static_cast<uint32_t>(e) < E) s = fmaf(xe[e], wi[e], s);
-                    gi[g] = s + s_bih[g * G::U];
+                    for (int g = 0; g < 3; ++g) {
+                        const float* wi = s_wih + (g * G::U + my_local) * E;
+                        float s = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < kMaxTcnCh; ++e)
+                            if (static_cast<uint32_t>(e) < E) s = fmaf(xe[e], wi[e], s);
+                        gi[g] = s + s_bih[g * G::U];
+                    }
                 }
                 const float ghr = acc[0][0] + s_bhh[0], ghz = acc[0][1] + s_bhh[G::U], ghn = acc[0][2] + s_bhh[2 * G::U];
                 const float rg = sigmoid(gi[0] + ghr);
