@@ -254,7 +254,8 @@ class SkyJepaModel:
         self.handle = lib.orc_skyjepa_new(C.byref(cfg), fp(self.weights), self.weights.size)
 
     def __del__(self):
-        if getattr(self, "handle", None):
+        # at interpreter exit the module's `lib` may already be gone
+        if getattr(self, "handle", None) and globals().get("lib") is not None:
             lib.orc_skyjepa_free(self.handle)
             self.handle = None
 
@@ -472,7 +473,7 @@ class LewmModel:
             raise ValueError("LeWM weight count mismatch")
 
     def __del__(self):
-        if getattr(self, "handle", None):
+        if getattr(self, "handle", None) and globals().get("lib") is not None:
             lib.orc_lewm_free(self.handle)
             self.handle = None
 
