@@ -677,6 +677,13 @@ def cpu_baseline_lewm(w, image: bool, budget_s: float):
 
 # ------------------------------------------------------------ media workload
 
+# DRAM bytes (read + write) of one staged-kernel launch at 32 full-HD frames,
+# f32 output, from a one-pass ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum); profiles/media_nv12_staged_fullhd.md.  The writes
+# fall short of the output size by what is still in the L2 when the kernel ends.
+MEDIA_DRAM_BYTES = {("nv12", False, 32): 101.31e6 + 736.08e6, ("rgb", False, 32): 202.08e6 + 736.31e6}
+
+
 def run_media(args, rank, world, local_rank):
     """NV12 -> normalised NCHW (Nv12Preprocessor, src/media/mod.rs:196-273) for
     a batch of full-HD frames at their own size (ImageNet mean / std): one
@@ -757,7 +764,9 @@ def run_media(args, rank, world, local_rank):
                 "d2h_bytes_per_step": int(out.numel() * out.element_size())},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4), "traffic": MEDIA_DRAM_BYTES.get((fmt, bf16, B)),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the same "
+                                       "workload, profiles/media_nv12_staged_fullhd.md",
                      "peak_source": "MEASURED_PEAKS hbm_gbs (of measured)",
                      "note": f"achieved = ({channels} B of {fmt.upper()} read + output bytes written) per pixel "
                              "/ p50 time"},
