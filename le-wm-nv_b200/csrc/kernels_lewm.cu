@@ -199,6 +199,10 @@ __device__ __forceinline__ void row_stats(const float* x, uint32_t d, float& mea
 // The row (d <= 1024) is held in registers, 32 values per lane at most;
 // shift/scale are fetched together with it.
 constexpr int kRowRegs = 32;
+// NQ = values a lane holds: the row width over 32 rounded up (kRowRegs for
+// any width up to 1024; the exact count for the common widths, so that no
+// predicated-off loads or math are issued).
+template <int NQ>
 __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t d, const float* ada, uint32_t ld_ada,
                               uint32_t shift_off, uint32_t scale_off, RowMap map, const float* w, const float* b) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,10 +210,10 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     if (r >= rows) return;
     const float* xr = x + static_cast<size_t>(r) * d;
     const float* a = ada + map.row(r) * ld_ada;
-    float v[kRowRegs], sh[kRowRegs], sc[kRowRegs];
+    float v[NQ], sh[NQ], sc[NQ];
     float s = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kRowRegs; ++q) {
+    for (int q = 0; q < NQ; ++q) {
         const uint32_t i = lane + 32 * q;
         const bool in = i < d;
         v[q] = in ? xr[i] : 0.0f;
@@ -220,7 +224,7 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     float mean = warp_sum(s) / static_cast<float>(d);
     float var = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kRowRegs; ++q)
+    for (int q = 0; q < NQ; ++q)
         if (lane + 32 * q < d) {
             const float c = v[q] - mean;
             var += c * c;
@@ -228,7 +232,7 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     float den = sqrtf(warp_sum(var) / static_cast<float>(d) + 1e-6f);
     s = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kRowRegs; ++q)
+    for (int q = 0; q < NQ; ++q)
         if (lane + 32 * q < d) {
             v[q] = (v[q] - mean) / den * (sc[q] + 1.0f) + sh[q];
             s += v[q];
@@ -236,7 +240,7 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     mean = warp_sum(s) / static_cast<float>(d);
     var = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kRowRegs; ++q)
+    for (int q = 0; q < NQ; ++q)
         if (lane + 32 * q < d) {
             const float c = v[q] - mean;
             var += c * c;
@@ -244,7 +248,7 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     den = sqrtf(warp_sum(var) / static_cast<float>(d) + 1e-5f);
     float* yr = y + static_cast<size_t>(r) * d;
 #pragma unroll
-    for (int q = 0; q < kRowRegs; ++q) {
+    for (int q = 0; q < NQ; ++q) {
         const uint32_t i = lane + 32 * q;
         if (i < d) yr[i] = (v[q] - mean) / den * w[i] + b[i];
     }
@@ -279,6 +283,57 @@ __global__ void norm_act_kernel(float* x, uint32_t rows, uint32_t d, int kind, c
         if (kind == kNormLayer) v = (v - mean) / den * w[i] + b[i];
         else if (kind == kNormBatch) v = (v - rm[i]) / sqrtf(rv[i] + 1e-5f) * w[i] + b[i];
         xr[i] = gelu_tanh(v);
+    }
+}
+
+// The same for wide hidden layers (d up to 2048, e.g. the image model's
+// pred_proj): a block per row, the row held in registers (kNaPer values a
+// thread), one read and one write of it; the mean and the variance are
+// block reductions (two passes over the registers, as row_stats does).
+constexpr uint32_t kNaThreads = 256, kNaPer = 8;
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    __syncthreads();  // red is reused by consecutive reductions
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < (kNaThreads >> 5) ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+__global__ void __launch_bounds__(kNaThreads) norm_act_row_kernel(float* x, uint32_t d, int kind, const float* w,
+                                                                  const float* b, const float* rm, const float* rv) {
+    __shared__ float red[kNaThreads >> 5];
+    float* xr = x + static_cast<size_t>(blockIdx.x) * d;
+    float v[kNaPer];
+#pragma unroll
+    for (uint32_t j = 0; j < kNaPer; ++j) {
+        const uint32_t i = threadIdx.x + j * kNaThreads;
+        v[j] = i < d ? xr[i] : 0.0f;
+    }
+    float mean = 0.0f, den = 1.0f;
+    if (kind == kNormLayer) {
+        float s = 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < kNaPer; ++j) s += v[j];
+        mean = block_sum(s, red) / static_cast<float>(d);
+        float q = 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < kNaPer; ++j) {
+            const uint32_t i = threadIdx.x + j * kNaThreads;
+            const float c = v[j] - mean;
+            if (i < d) q += c * c;
+        }
+        den = sqrtf(block_sum(q, red) / static_cast<float>(d) + 1e-5f);
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kNaPer; ++j) {
+        const uint32_t i = threadIdx.x + j * kNaThreads;
+        if (i >= d) break;
+        float u = v[j];
+        if (kind == kNormLayer) u = (u - mean) / den * w[i] + b[i];
+        else if (kind == kNormBatch) u = (u - rm[i]) / sqrtf(rv[i] + 1e-5f) * w[i] + b[i];
+        xr[i] = gelu_tanh(u);
     }
 }
 
@@ -461,6 +516,134 @@ __global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, f
     }
 }
 
+// The same attention for 64-wide heads, register-tiled: a block per
+// (sequence, head, 32 queries), K (rows padded to 68 floats: 16-byte rows
+// that eight lanes read from eight different bank quads), V and the block's
+// queries in shared memory.  Warp w scores its 4 queries against keys
+// lane + 32 u (u < 8), 4 x 8 accumulators a thread, 16-byte operand loads;
+// the softmax weights go to a per-warp [key][4] table, and the lanes then
+// accumulate output dimensions lane and lane + 32 of the 4 queries over the
+// keys.  Every dot product, the softmax and the weighted sums run in the
+// same order as attention_smem_kernel's, so the outputs are identical.
+constexpr uint32_t kAtQ = 32, kAtDh = 64, kAtKld = 68;
+__host__ __device__ inline uint32_t at_tpad(uint32_t t) { return (t + 31u) & ~31u; }
+__host__ __device__ inline size_t at_smem_floats(uint32_t t) {
+    const uint32_t tp = at_tpad(t);
+    return static_cast<size_t>(tp) * kAtKld + static_cast<size_t>(tp) * kAtDh + kAtQ * kAtKld + 8u * tp * 4u;
+}
+
+__global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, float* out, uint32_t t, uint32_t H,
+                                                              float scale, int causal, int scale_q_first) {
+    extern __shared__ __align__(16) float sm[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t h = blockIdx.y, q0 = blockIdx.x * kAtQ, tp = at_tpad(t);
+    const size_t s = blockIdx.z;
+    const uint32_t inner = H * kAtDh;
+    float* Ks = sm;                    // [tp][68]
+    float* Vs = Ks + tp * kAtKld;      // [tp][64]
+    float* Qs = Vs + tp * kAtDh;       // [32][68]
+    float* Pt = Qs + kAtQ * kAtKld + warp * tp * 4u;  // this warp's [tp][4]
+    const float* base = qkv + s * t * 3 * inner;
+    for (uint32_t idx = threadIdx.x; idx < tp * 16u; idx += blockDim.x) {
+        const uint32_t j = idx >> 4, c = (idx & 15u) * 4u;
+        float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+        if (j < t) {
+            const float* row = base + static_cast<size_t>(j) * 3 * inner + h * kAtDh + c;
+            k = *reinterpret_cast<const float4*>(row + inner);
+            v = *reinterpret_cast<const float4*>(row + 2 * inner);
+        }
+        *reinterpret_cast<float4*>(Ks + j * kAtKld + c) = k;
+        *reinterpret_cast<float4*>(Vs + j * kAtDh + c) = v;
+    }
+    for (uint32_t idx = threadIdx.x; idx < kAtQ * 16u; idx += blockDim.x) {
+        const uint32_t qi = idx >> 4, c = (idx & 15u) * 4u, i = q0 + qi;
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < t) {
+            q = *reinterpret_cast<const float4*>(base + static_cast<size_t>(i) * 3 * inner + h * kAtDh + c);
+            if (scale_q_first) { q.x *= scale; q.y *= scale; q.z *= scale; q.w *= scale; }
+        }
+        *reinterpret_cast<float4*>(Qs + qi * kAtKld + c) = q;
+    }
+    __syncthreads();
+    const uint32_t ql = warp * 4u;  // the warp's first query, block-local
+    if (q0 + ql >= t) return;
+    float acc[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[a][u] = 0.0f;
+    const uint32_t nu = tp / 32u;  // key rounds that hold real keys (the rest of the 8 stay unused)
+#pragma unroll 1
+    for (uint32_t d = 0; d < kAtDh; d += 4) {
+        float4 q[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) q[a] = *reinterpret_cast<const float4*>(Qs + (ql + a) * kAtKld + d);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (static_cast<uint32_t>(u) >= nu) break;
+            const float4 k = *reinterpret_cast<const float4*>(Ks + (u * 32u + lane) * kAtKld + d);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                acc[a][u] = fmaf(q[a].x, k.x, acc[a][u]);
+                acc[a][u] = fmaf(q[a].y, k.y, acc[a][u]);
+                acc[a][u] = fmaf(q[a].z, k.z, acc[a][u]);
+                acc[a][u] = fmaf(q[a].w, k.w, acc[a][u]);
+            }
+        }
+    }
+    float inv[4];
+    uint32_t jend = 0;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const uint32_t i = q0 + ql + a;
+        const uint32_t jmax = i >= t ? 0u : (causal ? i + 1 : t);
+        jend = jmax > jend ? jmax : jend;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t j = u * 32u + lane;
+            float v = -INFINITY;
+            if (static_cast<uint32_t>(u) < nu && j < jmax) v = scale_q_first ? acc[a][u] : acc[a][u] * scale;
+            acc[a][u] = v;
+            mx = fmaxf(mx, v);
+        }
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t j = u * 32u + lane;
+            if (static_cast<uint32_t>(u) >= nu) break;
+            float e = 0.0f;
+            if (j < jmax) {
+                e = expf(acc[a][u] - mx);
+                sum += e;
+            }
+            Pt[j * 4u + a] = e;  // zero past the query's last key: adds nothing below
+        }
+        inv[a] = warp_sum(sum);
+    }
+    __syncwarp();
+    float o[4][2];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
+    for (uint32_t j = 0; j < jend; ++j) {
+        const float4 p = *reinterpret_cast<const float4*>(Pt + j * 4u);
+        const float v0 = Vs[j * kAtDh + lane], v1 = Vs[j * kAtDh + lane + 32u];
+        o[0][0] = fmaf(p.x, v0, o[0][0]); o[0][1] = fmaf(p.x, v1, o[0][1]);
+        o[1][0] = fmaf(p.y, v0, o[1][0]); o[1][1] = fmaf(p.y, v1, o[1][1]);
+        o[2][0] = fmaf(p.z, v0, o[2][0]); o[2][1] = fmaf(p.z, v1, o[2][1]);
+        o[3][0] = fmaf(p.w, v0, o[3][0]); o[3][1] = fmaf(p.w, v1, o[3][1]);
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const uint32_t i = q0 + ql + a;
+        if (i >= t) break;
+        float* orow = out + (s * t + i) * inner + h * kAtDh;
+        orow[lane] = o[a][0] / inv[a];
+        orow[lane + 32u] = o[a][1] / inv[a];
+    }
+}
+
 // Goal cost (goal_cost, model.rs:149-165): sum_d (pred - goal[r / S])^2.
 __global__ void goal_cost_kernel(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
                                  float* scores) {
@@ -516,8 +699,15 @@ cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, c
                           cudaStream_t s) {
     if (!rows) return cudaSuccess;
     constexpr int kWarps = 8;
-    ada_ln_kernel<<<blocks_for(rows, kWarps), kWarps * 32, 0, s>>>(
-        x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b);
+    const dim3 grid(blocks_for(rows, kWarps)), block(kWarps * 32);
+    switch (d) {
+        case 192: ada_ln_kernel<6><<<grid, block, 0, s>>>(x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b); break;
+        case 256: ada_ln_kernel<8><<<grid, block, 0, s>>>(x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b); break;
+        case 384: ada_ln_kernel<12><<<grid, block, 0, s>>>(x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b); break;
+        case 512: ada_ln_kernel<16><<<grid, block, 0, s>>>(x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b); break;
+        default:
+            ada_ln_kernel<kRowRegs><<<grid, block, 0, s>>>(x, y, rows, d, ada, ld_ada, shift_off, scale_off, map, w, b);
+    }
     return cudaGetLastError();
 }
 
@@ -531,7 +721,10 @@ cudaError_t launch_layernorm(const float* x, float* y, uint32_t rows, uint32_t d
 cudaError_t launch_norm_act(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
                             const float* rm, const float* rv, cudaStream_t s) {
     if (!rows) return cudaSuccess;
-    norm_act_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, rows, d, kind, w, b, rm, rv);
+    if (d >= 512 && d <= kNaThreads * kNaPer)
+        norm_act_row_kernel<<<rows, kNaThreads, 0, s>>>(x, d, kind, w, b, rm, rv);
+    else
+        norm_act_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, rows, d, kind, w, b, rm, rv);
     return cudaGetLastError();
 }
 
@@ -569,6 +762,16 @@ cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32
                              float scale, int causal, int scale_q_first, cudaStream_t s) {
     const size_t warps = static_cast<size_t>(seqs) * H * t;
     if (!warps) return cudaSuccess;
+    const size_t tsmem = at_smem_floats(t) * sizeof(float);
+    const bool aligned = (reinterpret_cast<uintptr_t>(qkv) & 15u) == 0 && (H * kAtDh * 3u) % 4u == 0;
+    if (t > 32 && t <= kAttnMaxT && dh == kAtDh && aligned && tsmem <= 200 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(tsmem));
+        if (e != cudaSuccess) return e;
+        attention_tiled_kernel<<<dim3((t + kAtQ - 1) / kAtQ, H, seqs), 256, tsmem, s>>>(qkv, out, t, H, scale, causal,
+                                                                                      scale_q_first);
+        return cudaGetLastError();
+    }
     const size_t smem = (static_cast<size_t>(t) * (2 * dh + 1) + 8 * t + 8 * dh) * sizeof(float);
     if (t > 32 && t <= kAttnMaxT && dh <= 128 && smem <= 200 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

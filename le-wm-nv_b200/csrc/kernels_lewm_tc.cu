@@ -2,8 +2,9 @@
 //
 // C[M,N] = A[M,K] . W[N,K]^T with the scorer's fused epilogue (bias, GELU /
 // SiLU, gated residual), for the bf16 predictor / encoder of the LeWM image
-// workload.  One 128 x 128 output tile per CTA (N tiles narrower at the
-// edge), K in 64-element blocks through two shared-memory stages:
+// workload.  One 128 x 128 (or 128 x 64) output tile per CTA (N tiles
+// narrower at the edge), K in 64-element blocks through two shared-memory
+// stages:
 //   A  f32 activations from HBM/L2, rounded to bf16 by the loading threads
 //      and stored in the SW128 K-major layout (the residual stream and every
 //      other activation stay f32);
@@ -44,7 +45,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-__global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
+__global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err, uint32_t tn) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                    // [2][128 rows x 128 B]
@@ -52,8 +53,8 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStageBytes);  // stage[2], final
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
-    const uint32_t n_tile = min(kTN, g.N - n0), n_mma = (n_tile + 15u) & ~15u;
+    const uint32_t m0 = blockIdx.y * kTM, n0 = blockIdx.x * tn;
+    const uint32_t n_tile = min(tn, g.N - n0), n_mma = (n_tile + 15u) & ~15u;
     const uint32_t kb = blockIdx.z * g.k_chunk, ke = min(g.K, kb + g.k_chunk);
     const uint32_t nblk = (ke - kb + kTK - 1) / kTK;
     if (tid == 0) {
@@ -95,14 +96,15 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
             *reinterpret_cast<uint2*>(base + tc::sw128_offset(row, kq)) = v;
         }
     };
-    // W: 128 rows x 8 chunks of 16 B, 4 per thread; rows past N read nothing
-    // (zero-filled).
+    // W: the tile's rows x 8 chunks of 16 B, up to 4 per thread; rows past N
+    // read nothing (zero-filled); rows past the MMA's N are not copied.
     auto load_b = [&](uint32_t s, uint32_t k0) {
         const uint32_t base = tc::smem_u32(sB + s * kStageB);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint32_t c = static_cast<uint32_t>(i) * 256u + tid;
             const uint32_t row = c >> 3, j = c & 7u;
+            if (row >= n_mma) break;
             const uint32_t n = n0 + row, k = k0 + j * 8u;
             const bool ok = n < g.N && k < ke;
             const uint16_t* src = ok ? g.Wb + static_cast<size_t>(n) * g.ldw + k : g.Wb;
@@ -164,20 +166,45 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
     if (warp == 0) tc::tmem_free(tmem, 128);
     // tile -> global, a warp per row, consecutive columns per lane: the
     // epilogue (or the split's partial) is written, and C / the gate read,
-    // in whole cache lines
+    // in whole cache lines; each lane takes 4 rows (8 apart) at a time and
+    // issues their loads before it uses them
     const bool split = g.splits > 1;
     float* part = split ? g.partial + static_cast<size_t>(blockIdx.z) * g.M * g.N : nullptr;
-    for (uint32_t r = warp; r < kTM; r += 8u) {
-        const uint32_t m = m0 + r;
-        if (m >= g.M) break;
+    for (uint32_t r0 = warp; r0 < kTM; r0 += 32u) {
+        if (m0 + r0 >= g.M) break;
         for (uint32_t col = lane; col < n_tile; col += 32u) {
             const uint32_t n = n0 + col;
-            const float v = stile[r * kTileLd + col];
-            if (split) {
-                part[static_cast<size_t>(m) * g.N + n] = v;
-            } else {
-                float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
-                *cp = epilogue_value(g, m, n, v, cp);
+            float v[4], cv[4], gv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t r = r0 + 8u * q, m = m0 + r;
+                v[q] = stile[r * kTileLd + col];
+                cv[q] = 0.0f;
+                gv[q] = 0.0f;
+                if (!split && g.residual && m < g.M) {
+                    cv[q] = g.C[static_cast<size_t>(m) * g.ldc + n];
+                    if (g.gate) gv[q] = g.gate[g.map.row(m) * g.ldg + n];
+                }
+            }
+            const float bias = (!split && g.bias) ? g.bias[n] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t m = m0 + r0 + 8u * q;
+                if (m >= g.M) break;
+                if (split) {
+                    part[static_cast<size_t>(m) * g.N + n] = v[q];
+                    continue;
+                }
+                // epilogue_value's arithmetic: bias, then the gated residual or the activation
+                float x = v[q];
+                if (g.bias) x = x + bias;
+                if (g.residual) {
+                    if (g.gate) x = gv[q] * x;
+                    x = cv[q] + x;
+                } else {
+                    x = apply_act(g.act, x);
+                }
+                g.C[static_cast<size_t>(m) * g.ldc + n] = x;
             }
         }
     }
@@ -185,13 +212,21 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err) {
 
 // Split-K: C = epilogue(sum over the splits' partials [splits][M][N], in
 // split order), one thread per output (coalesced; every SM takes part).
+// The partials of an output are all loaded before they are added (in split
+// order); indices are 32-bit (the partial buffer holds under 2^32 floats).
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(GemmArgs g) {
-    const uint64_t total = static_cast<uint64_t>(g.M) * g.N, plane = total;
-    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        const uint32_t m = static_cast<uint32_t>(i / g.N), n = static_cast<uint32_t>(i % g.N);
+    constexpr uint32_t kMaxSplits = 16;
+    const uint32_t total = g.M * g.N, plane = total;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t m = i / g.N, n = i - m * g.N;
+        float p[kMaxSplits];
+#pragma unroll
+        for (uint32_t z = 0; z < kMaxSplits; ++z)
+            p[z] = z < g.splits ? __ldcg(g.partial + static_cast<size_t>(z) * plane + i) : 0.0f;
         float v = 0.0f;
-        for (uint32_t z = 0; z < g.splits; ++z) v += __ldcg(g.partial + z * plane + i);
+#pragma unroll
+        for (uint32_t z = 0; z < kMaxSplits; ++z)
+            if (z < g.splits) v += p[z];
         float* cp = g.C + static_cast<size_t>(m) * g.ldc + n;
         *cp = epilogue_value(g, m, n, v, cp);
     }
@@ -204,8 +239,11 @@ bool gemm_tc_eligible(const GemmArgs& g) {
            (reinterpret_cast<uintptr_t>(g.A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(g.Wb) & 15u) == 0;
 }
 
-// Splits K when the output tiles alone leave SMs idle: about one wave of
-// CTAs, at least two 64-wide K blocks per split, at most 16 splits.
+// Output tiles are 128 x 128, or 128 x 64 when the 128-wide tiles would not
+// give every SM a CTA (two CTAs fit an SM, so one's epilogue overlaps the
+// other's loads); then K is split when the tiles alone still leave SMs idle:
+// about one wave of CTAs, at least two 64-wide K blocks per split, at most 16
+// splits.
 cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch* sp, int* err) {
     static bool configured[64] = {};  // the attribute is per device
     int dev = 0;
@@ -217,10 +255,12 @@ cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch*
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     GemmArgs g = in;
-    const uint32_t tx = (g.N + kTN - 1) / kTN, ty = (g.M + kTM - 1) / kTM;
+    const uint32_t ty = (g.M + kTM - 1) / kTM;
+    const uint32_t tn = (static_cast<size_t>((g.N + kTN - 1) / kTN) * ty < 148 && g.N > 64) ? 64u : kTN;
+    const uint32_t tx = (g.N + tn - 1) / tn;
     const size_t tiles = static_cast<size_t>(tx) * ty;
     uint32_t splits = 1;
-    if (sp && sp->partial && tiles < 148 && g.K >= 2 * 2 * kTK) {
+    if (sp && sp->partial && tiles < 148 && g.K >= 2 * 2 * kTK && static_cast<uint64_t>(g.M) * g.N < (1ull << 31)) {
         splits = static_cast<uint32_t>((148 + tiles - 1) / tiles);
         splits = min(splits, min(16u, g.K / (2 * kTK)));
         while (splits > 1 && static_cast<size_t>(splits) * g.M * g.N > sp->floats) --splits;
@@ -232,7 +272,7 @@ cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch*
         g.partial = sp->partial;
     }
     dim3 grid(tx, ty, g.splits);
-    gemm_tc_kernel<<<grid, 256, kTcSmem, stream>>>(g, err);
+    gemm_tc_kernel<<<grid, 256, kTcSmem, stream>>>(g, err, tn);
     if ((e = cudaGetLastError()) != cudaSuccess || g.splits <= 1) return e;
     const uint64_t total = static_cast<uint64_t>(g.M) * g.N;
     splitk_reduce_kernel<<<static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 8)), 256, 0, stream>>>(g);
