@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "lwm_lewm.hpp"
@@ -245,7 +246,7 @@ bool gemm_tc_eligible(const GemmArgs& g) {
 // about one wave of CTAs, at least two 64-wide K blocks per split, at most 16
 // splits.
 cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch* sp, int* err) {
-    static bool configured[64] = {};  // the attribute is per device
+    static std::atomic<bool> configured[64] = {};  // the attribute is per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;

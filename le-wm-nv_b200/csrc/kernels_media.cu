@@ -13,6 +13,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 #include <type_traits>
 
 #include "lwm_kernels.hpp"
@@ -492,27 +493,36 @@ __global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a
 template <auto Kern>
 cudaError_t launch_grid(uint32_t smem, const MediaArgs& a, const StagedMedia& m, cudaStream_t stream) {
     const uint32_t threads = ((a.out_w / 4u + 31u) / 32u) * 32u + 32u;
-    static int configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    static int per_sm[64] = {}, sms[64] = {};
+    // per device: the shared-memory opt-in, the SM count and the resident
+    // blocks per SM of the last block size; guarded, since contexts on other
+    // threads may launch at the same time
+    static std::mutex mu;
+    static int configured[64] = {}, per_sm[64] = {}, sms[64] = {};
     static uint32_t per_sm_threads[64] = {};
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
-    if (per_sm_threads[dev] != threads) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], Kern, static_cast<int>(threads), smem);
-        if (e != cudaSuccess) return e;
-        per_sm_threads[dev] = threads;
+    int blocks_per_sm = 1, sm_count = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+            configured[dev] = 1;
+        }
+        if (per_sm_threads[dev] != threads) {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], Kern, static_cast<int>(threads), smem);
+            if (e != cudaSuccess) return e;
+            per_sm_threads[dev] = threads;
+        }
+        blocks_per_sm = per_sm[dev] > 0 ? per_sm[dev] : 1;
+        sm_count = sms[dev];
     }
     const uint64_t rows = static_cast<uint64_t>(a.batch) * a.out_h;
-    const uint64_t resident = static_cast<uint64_t>(per_sm[dev] > 0 ? per_sm[dev] : 1) * sms[dev];
+    const uint64_t resident = static_cast<uint64_t>(blocks_per_sm) * sm_count;
     const uint32_t grid = static_cast<uint32_t>(rows < resident ? rows : resident);
     Kern<<<grid, threads, smem, stream>>>(a, m);
     return cudaGetLastError();
