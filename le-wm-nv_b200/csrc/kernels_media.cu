@@ -335,7 +335,7 @@ struct RowSlot {
 // when every consumer warp is done with it; no block-wide barrier in the
 // row loop.
 template <uint32_t CS, bool BF16, uint32_t ROWCAP>
-__global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a, StagedMedia m) {
+__global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a, StagedMedia m) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t kStageBytes = 4u * ROWCAP;  // luma y0, luma y1, chroma c0, chroma c1
     RowSlot* slots = reinterpret_cast<RowSlot*>(smem + kStages * kStageBytes);
@@ -413,6 +413,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a
     const Prod prod{splat(m.neg_zero)};
     const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
     const f2 cwxa = mk(cwx[0], cwx[1]), cwxb = mk(cwx[2], cwx[3]);
+    const bool csh[2] = {u0[0] == u0[1] && u1[0] == u1[1], u0[2] == u0[3] && u1[2] == u1[3]};
     const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
 
     // one output row from stage S (a compile-time shared-memory offset);
@@ -445,26 +446,42 @@ __global__ void __launch_bounds__(kMaxThreads, 2) nv12_staged_kernel(MediaArgs a
                                     mk(magic_u8(ly0[l1[i]]), magic_u8(ly0[l1[j]])),
                                     mk(magic_u8(ly1[l0[i]]), magic_u8(ly1[l0[j]])),
                                     mk(magic_u8(ly1[l1[i]]), magic_u8(ly1[l1[j]])), wxp, wy);
-                const uint32_t a00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[i]);
-                const uint32_t b00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[j]);
-                const uint32_t a01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[i]);
-                const uint32_t b01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[j]);
-                const uint32_t a10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[i]);
-                const uint32_t b10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[j]);
-                const uint32_t a11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[i]);
-                const uint32_t b11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[j]);
                 constexpr uint32_t kU = 0x7540u, kV = 0x7541u;
                 const f2 c128 = splat(128.0f);
-                const f2 U = sub(bilerp(prod, mk(magic_byte(a00, kU), magic_byte(b00, kU)),
-                                        mk(magic_byte(a01, kU), magic_byte(b01, kU)),
-                                        mk(magic_byte(a10, kU), magic_byte(b10, kU)),
-                                        mk(magic_byte(a11, kU), magic_byte(b11, kU)), cwxp, cwy),
-                                 c128);
-                const f2 V = sub(bilerp(prod, mk(magic_byte(a00, kV), magic_byte(b00, kV)),
-                                        mk(magic_byte(a01, kV), magic_byte(b01, kV)),
-                                        mk(magic_byte(a10, kV), magic_byte(b10, kV)),
-                                        mk(magic_byte(a11, kV), magic_byte(b11, kV)), cwxp, cwy),
-                                 c128);
+                f2 U, V;
+                if (csh[p]) {
+                    // both pixels tap the same chroma columns (native size,
+                    // upscaling, downscaling under 2x): one load per tap
+                    const uint32_t a00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[i]);
+                    const uint32_t a01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[i]);
+                    const uint32_t a10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[i]);
+                    const uint32_t a11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[i]);
+                    U = sub(bilerp(prod, splat(magic_byte(a00, kU)), splat(magic_byte(a01, kU)),
+                                   splat(magic_byte(a10, kU)), splat(magic_byte(a11, kU)), cwxp, cwy),
+                            c128);
+                    V = sub(bilerp(prod, splat(magic_byte(a00, kV)), splat(magic_byte(a01, kV)),
+                                   splat(magic_byte(a10, kV)), splat(magic_byte(a11, kV)), cwxp, cwy),
+                            c128);
+                } else {
+                    const uint32_t a00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[i]);
+                    const uint32_t b00 = *reinterpret_cast<const uint16_t*>(cr0 + u0[j]);
+                    const uint32_t a01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[i]);
+                    const uint32_t b01 = *reinterpret_cast<const uint16_t*>(cr0 + u1[j]);
+                    const uint32_t a10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[i]);
+                    const uint32_t b10 = *reinterpret_cast<const uint16_t*>(cr1 + u0[j]);
+                    const uint32_t a11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[i]);
+                    const uint32_t b11 = *reinterpret_cast<const uint16_t*>(cr1 + u1[j]);
+                    U = sub(bilerp(prod, mk(magic_byte(a00, kU), magic_byte(b00, kU)),
+                                   mk(magic_byte(a01, kU), magic_byte(b01, kU)),
+                                   mk(magic_byte(a10, kU), magic_byte(b10, kU)),
+                                   mk(magic_byte(a11, kU), magic_byte(b11, kU)), cwxp, cwy),
+                            c128);
+                    V = sub(bilerp(prod, mk(magic_byte(a00, kV), magic_byte(b00, kV)),
+                                   mk(magic_byte(a01, kV), magic_byte(b01, kV)),
+                                   mk(magic_byte(a10, kV), magic_byte(b10, kV)),
+                                   mk(magic_byte(a11, kV), magic_byte(b11, kV)), cwxp, cwy),
+                            c128);
+                }
                 f2 R, G, B;
                 to_rgb<CS>(prod, Y, U, V, R, G, B);
                 out[0][p] = normalize(R, a.mean[0], a.std[0], m.rcp_std[0]);
