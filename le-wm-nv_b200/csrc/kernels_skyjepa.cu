@@ -745,10 +745,17 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
         // ---- GEMM warps: registers hold this thread's W_hh slice
         const uint32_t pl = lane / G::KG, kg = lane % G::KG;
         const uint32_t pair = warp * G::PPW + pl;
+        // Accumulator slot s of this lane holds (unit-in-pair, row) combo
+        // s ^ (kg % COMBOS): the lane's weights and h rows are taken in that
+        // permuted order, so that every level of the reduce-scatter below
+        // keeps slots [0, m) and sends slots [m, 2m) on every lane (the
+        // partner's slot cc + m holds the combo of this lane's slot cc) and
+        // needs no per-lane selects; the sums are the same, in the same order.
+        const uint32_t xq = (kg % G::COMBOS) / G::R, xr = kg % G::R;
         float wr[2][3][G::KPT];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-            const uint32_t j = c * G::U + pair * 2 + q;
+            const uint32_t j = c * G::U + pair * 2 + (q ^ xq);
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
                 const float* row = a.w_hh + (static_cast<size_t>(g) * H + j) * H;
@@ -780,7 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
                     float4 hv[G::R];
 #pragma unroll
                     for (int r = 0; r < G::R; ++r)
-                        hv[r] = *reinterpret_cast<const float4*>(hc + (grp * G::R + r) * H + kg * 4 + 4 * G::KG * i);
+                        hv[r] = *reinterpret_cast<const float4*>(hc + (grp * G::R + (r ^ xr)) * H + kg * 4 +
+                                                                 4 * G::KG * i);
 #pragma unroll
                     for (int comp = 0; comp < 4; ++comp)
 #pragma unroll
@@ -794,19 +802,15 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_rollout_kernel(SkyjepaArg
                         }
                 }
                 // reduce-scatter over the low 3 lane bits (lane kg ends with
-                // combo kg & 7), then all-reduce over the remaining k-group bits
+                // combo kg & 7 in slot 0), then all-reduce over the remaining
+                // k-group bits
 #pragma unroll
-                for (int m = G::COMBOS / 2; m >= 1; m >>= 1) {
-                    const bool upper = (kg & m) != 0;
+                for (int m = G::COMBOS / 2; m >= 1; m >>= 1)
 #pragma unroll
                     for (int cc = 0; cc < m; ++cc)
 #pragma unroll
-                        for (int g = 0; g < 3; ++g) {
-                            const float send = upper ? acc[cc][g] : acc[cc + m][g];
-                            const float keep = upper ? acc[cc + m][g] : acc[cc][g];
-                            acc[cc][g] = keep + __shfl_xor_sync(0xffffffffu, send, m);
-                        }
-                }
+                        for (int g = 0; g < 3; ++g)
+                            acc[cc][g] = acc[cc][g] + __shfl_xor_sync(0xffffffffu, acc[cc + m][g], m);
 #pragma unroll
                 for (int m = G::COMBOS; m < G::KG; m <<= 1)
 #pragma unroll
