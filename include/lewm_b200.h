@@ -160,6 +160,16 @@ lwm_status lwm_planner_warm_start(lwm_planner* planner, float* sequence_out, siz
 /* reset_rng_sequence / rng_offset (src/planner.rs:442-448, 583-589). */
 lwm_status lwm_planner_reset_rng(lwm_planner* planner);
 lwm_status lwm_planner_rng_offset(lwm_planner* planner, uint64_t* out);
+/* The elite indices each iteration of the last CEM / iCEM plan selected,
+ * as select_elites / lowest_score_indices return them (src/planner.rs:
+ * 1647-1659, 1730-1754; ascending score, ties to the lower index), copied to
+ * `out` as [iterations][batch][elites]; a sharded plan reports the global
+ * candidate indices.  The reference keeps them inside plan_device; they are
+ * exposed here so callers (and parity tests) can check the selection.  Sets
+ * *iterations_out to the iterations the plan completed (0 before the first
+ * plan or after a deadline fallback).  MPPI planners: LWM_INVALID_ARGUMENT. */
+lwm_status lwm_planner_elite_indices(lwm_planner* planner, uint32_t* out, size_t capacity,
+                                     uint32_t* iterations_out, uint32_t* batch_out, uint32_t* elites_out);
 
 /* ---------------------------------------------------------------- scorers */
 
@@ -671,13 +681,20 @@ typedef struct lwm_nominal_mppi_io {
  * until the process exits.  Limits: batch <= 1024 vehicles and
  * batch * ceil(samples / 64) * (4 + 4 * horizon, rounded up to 4) * 4 bytes
  * <= 1,040,384 bytes; larger requests fail with LWM_INVALID_ARGUMENT and do
- * no GPU work.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream
- * capture.  All calls share the one array and each call clears its counters
+ * no GPU work.  The first call on a device loads this library's device code
+ * on that device (CUDA loads modules lazily; loading them takes device
+ * memory for the code and for the array) and looks up the array's device
+ * address (cudaGetSymbolAddress), so make one call at start-up, before the
+ * loop that may not allocate and before any stream capture.  The address is
+ * kept for the life of the process: a cudaDeviceReset (or any teardown of
+ * the device's primary context) invalidates it, and this entry point must
+ * not be called on that device afterwards.  The call makes `device` current
+ * while it runs and gives the caller's current device back before it
+ * returns.  All calls share the one array and each call clears its counters
  * first, so two calls whose work overlaps on the GPU (different streams, or
  * different threads) race on it: serialise them.  Results equal
  * lwm_plan_device's for an MPPI planner with the nominal scorer given the
- * same mean, std, noise and context. */
+ * same mean, std, noise (or seed and offset) and context. */
 lwm_status lwm_nominal_mppi_noalloc(int device, void* stream, const lwm_nominal_scorer_config* cfg,
                                     uint32_t batch, uint32_t samples, uint32_t horizon,
                                     const float* bounds_low, const float* bounds_high, float temperature,

@@ -190,6 +190,9 @@ struct lwm_planner {
     void* exchange_user = nullptr;
     uint32_t exchange_shards = 0;
     DevBuf elite_local, elite_gathered, merged_scores, merged_cand, merged_index;
+    // CEM / iCEM: the elite indices every iteration of the last plan selected [iterations][B][K]
+    DevBuf elite_idx;
+    uint32_t elite_iterations = 0;
     bool has_result = false;
 };
 
@@ -390,6 +393,10 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     LWM_TRY(p->shard_tuples.ensure(static_cast<size_t>(B) * pw * 4));
     const uint32_t keep = p->kind == PlannerKind::Icem ? std::max<uint32_t>(p->icem.keep_elites, 1) : 1;
     LWM_TRY(p->carried.ensure(static_cast<size_t>(B) * keep * p->T * p->A * 4));
+    if (p->kind != PlannerKind::Mppi) {
+        const uint32_t K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
+        LWM_TRY(p->elite_idx.ensure(static_cast<size_t>(p->iterations) * B * K * 4));
+    }
     LWM_TRY(p->bounds.ensure(2 * LWM_MAX_ACTION_DIM * 4));
     // staging carries the bounds (2 x 16 floats), the initial std, deadline
     // sequences and the result burst of lwm_plan
@@ -572,6 +579,7 @@ lwm_status deadline_result(lwm_planner* p, uint32_t B, bool use_warm, const char
                            std::chrono::steady_clock::time_point start) {
     const size_t seq = static_cast<size_t>(B) * p->T * p->A;
     cudaStream_t stream = p->ctx->stream;
+    p->elite_iterations = 0;
     int outcome;
     if (use_warm) {
         LWM_CUDA(cudaMemcpyAsync(p->sequence.ptr, p->warm.ptr, seq * 4, cudaMemcpyDeviceToDevice, stream));
@@ -781,9 +789,10 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 r.S = p->S; r.T = p->T; r.A = p->A;
                 r.K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
                 r.keep = carried_keep;
-                r.sort_len = lwm::sort_length(p->S);
-                if (static_cast<size_t>(r.sort_len) * 8 > 200 * 1024)
-                    return fail(LWM_UNSUPPORTED, "elite selection supports at most 16384 samples");
+                if (!lwm::topk_layout(p->S, r.K, &r.sort_len, &r.select))
+                    return fail(LWM_UNSUPPORTED, "elite selection supports at most " + std::to_string(lwm::kMaxElites) +
+                                                     " elites");
+                r.elite_index = p->elite_idx.as<uint32_t>() + static_cast<size_t>(it) * B * r.K;
                 r.scores = p->scores.as<float>();
                 r.cand = p->cand.as<float>();
                 r.mean = p->mean.as<float>();
@@ -819,7 +828,9 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                                                      p->merged_scores.as<float>(), p->merged_cand.as<float>(),
                                                      p->merged_index.as<uint32_t>(), stream));
                     r.S = G * K;
-                    r.sort_len = lwm::sort_length(r.S);
+                    if (!lwm::topk_layout(r.S, K, &r.sort_len, &r.select))
+                        return fail(LWM_UNSUPPORTED, "elite selection supports at most " +
+                                                         std::to_string(lwm::kMaxElites) + " elites");
                     r.scores = p->merged_scores.as<float>();
                     r.cand = p->merged_cand.as<float>();
                     r.index_map = p->merged_index.as<uint32_t>();
@@ -838,6 +849,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
         }
         ++completed;
     }
+    p->elite_iterations = p->kind == PlannerKind::Mppi ? 0u : completed;
     if (sharded && p->kind == PlannerKind::Mppi) {
         // the outputs (and the warm start) come from lwm_mppi_combine_device
         out->first_action = nullptr;
@@ -1074,7 +1086,7 @@ lwm_status lwm_planner_destroy(lwm_planner* p) {
     for (DevBuf* b : {&p->bounds, &p->zeros, &p->std_init, &p->mean, &p->stdv, &p->cand, &p->scores, &p->partials, &p->counters,
                       &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp,
                       &p->shard_tuples, &p->trace, &p->trace_elite, &p->elite_local, &p->elite_gathered,
-                      &p->merged_scores, &p->merged_cand, &p->merged_index})
+                      &p->merged_scores, &p->merged_cand, &p->merged_index, &p->elite_idx})
         b->release();
     p->staging.release();
     delete p;
@@ -1189,6 +1201,25 @@ lwm_status lwm_planner_reset_rng(lwm_planner* p) {
 lwm_status lwm_planner_rng_offset(lwm_planner* p, uint64_t* out) {
     if (!p || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     *out = p->rng_offset.load();
+    return LWM_OK;
+}
+
+lwm_status lwm_planner_elite_indices(lwm_planner* p, uint32_t* out, size_t capacity, uint32_t* iterations_out,
+                                     uint32_t* batch_out, uint32_t* elites_out) {
+    if (!p || !iterations_out || !batch_out || !elites_out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (p->kind == PlannerKind::Mppi) return fail(LWM_INVALID_ARGUMENT, "MPPI selects no elites");
+    std::lock_guard<std::mutex> lock(p->mu);
+    const uint32_t K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
+    const uint32_t its = p->has_result ? p->elite_iterations : 0u, B = p->has_result ? p->last_batch : 0u;
+    *iterations_out = its;
+    *batch_out = B;
+    *elites_out = K;
+    const size_t n = static_cast<size_t>(its) * B * K;
+    if (n == 0) return LWM_OK;
+    if (!out || capacity < n) return fail(LWM_INVALID_ARGUMENT, "elite index output buffer too small");
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    LWM_CUDA(cudaMemcpyAsync(out, p->elite_idx.ptr, n * 4, cudaMemcpyDeviceToHost, p->ctx->stream));
+    LWM_CUDA(cudaStreamSynchronize(p->ctx->stream));
     return LWM_OK;
 }
 
@@ -1602,9 +1633,6 @@ lwm_status lwm_planner_set_shard_exchange(lwm_planner* p, uint32_t shards, lwm_e
     if (p->kind == PlannerKind::Mppi)
         return fail(LWM_INVALID_ARGUMENT, "MPPI shards exchange tuples through lwm_mppi_combine_device");
     if ((fn == nullptr) != (shards == 0)) return fail(LWM_INVALID_ARGUMENT, "exchange and shard count go together");
-    const uint32_t K = p->kind == PlannerKind::Cem ? p->cem.elites : p->icem.elites;
-    if (fn && static_cast<uint64_t>(shards) * K > 16384)
-        return fail(LWM_UNSUPPORTED, "shards x elites must be at most 16384");
     std::lock_guard<std::mutex> lock(p->mu);
     p->exchange = fn;
     p->exchange_user = user;
@@ -1721,7 +1749,8 @@ lwm_status lwm_lowest_k_device(lwm_ctx* ctx, const float* scores, uint32_t B, ui
     if (K == 0) return fail(LWM_INVALID_ARGUMENT, "top-k count must be greater than zero");
     if (S == 0) return fail(LWM_INVALID_ARGUMENT, "score tensor must contain at least one sample");
     if (K > S) return fail(LWM_INVALID_ARGUMENT, "top-k count " + std::to_string(K) + " cannot exceed samples " + std::to_string(S));
-    if (S > 16384) return fail(LWM_UNSUPPORTED, "lowest-k supports at most 16384 samples");
+    if (K > lwm::kMaxElites)
+        return fail(LWM_UNSUPPORTED, "lowest-k supports at most " + std::to_string(lwm::kMaxElites) + " selected indices");
     LWM_CUDA(cudaSetDevice(ctx->device));
     LWM_CUDA(lwm::launch_lowest_k(scores, out, B, S, K, ctx->stream));
     ctx->launches += 1;

@@ -12,6 +12,7 @@
 // This file is compiled with -fmad=false so that every product and sum is
 // rounded separately, as in the reference's f32 CPU plant.
 #include <cstdint>
+#include <mutex>
 
 #include "lwm_device.cuh"
 #include "lwm_kernels.hpp"
@@ -195,11 +196,25 @@ __global__ void __launch_bounds__(kNominalThreads) nominal_mppi_kernel(NominalAr
 uint32_t nominal_blocks_per_vehicle(uint32_t S) { return (S + kNominalThreads - 1) / kNominalThreads; }
 
 cudaError_t launch_nominal(const NominalArgs& a, cudaStream_t stream) {
+    if (a.T == 0 || a.T > kMaxHorizon) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kNominalThreads) * (a.T * 4 + 1) * sizeof(float);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(nominal_mppi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+        // the opt-in for the longest horizon, once per device (not a driver
+        // call on every plan of a real-time loop)
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        static std::mutex mu;
+        static bool configured[64] = {};
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            const size_t max_smem = static_cast<size_t>(kNominalThreads) * (kMaxHorizon * 4 + 1) * sizeof(float);
+            e = cudaFuncSetAttribute(nominal_mppi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(max_smem));
+            if (e != cudaSuccess) return e;
+            configured[dev] = true;
+        }
     }
     dim3 grid(nominal_blocks_per_vehicle(a.S), a.B);
     nominal_mppi_kernel<<<grid, kNominalThreads, smem, stream>>>(a);

@@ -5,12 +5,35 @@
 // kernels_skyjepa.cu).
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "lwm_device.cuh"
 #include "lwm_kernels.hpp"
 #include "lwm_mppi.cuh"
 
 namespace lwm {
+
+// color_temporal_noise of one (sample, action) lane held in registers
+// (swm_temporal_color_noise_f32, src/planner.rs:1852-1896): EMA with factor
+// `smooth`, then centre and scale by 1 / sqrt(var + 1e-6) over the horizon.
+__device__ __forceinline__ void color_lane(float (&eps)[kMaxHorizon], uint32_t T, float smooth) {
+    const float keep = 1.0f - smooth;
+    float prev = eps[0], mean = 0.0f;
+    for (uint32_t t = 0; t < T; ++t) {
+        prev = (t == 0) ? eps[t] : fmaf(smooth, prev, keep * eps[t]);
+        eps[t] = prev;
+        mean += prev;
+    }
+    mean /= static_cast<float>(T);
+    float var = 0.0f;
+    for (uint32_t t = 0; t < T; ++t) {
+        const float c = eps[t] - mean;
+        eps[t] = c;
+        var += c * c;
+    }
+    const float inv_std = 1.0f / sqrtf(var / static_cast<float>(T) + 1.0e-6f);
+    for (uint32_t t = 0; t < T; ++t) eps[t] *= inv_std;
+}
 
 // ----------------------------------------------------------------- sampling
 //
@@ -35,25 +58,7 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
         const uint64_t idx = base + static_cast<uint64_t>(t) * a.A;
         eps[t] = a.noise ? a.noise[idx] : normal_at(a.seed, a.offset + gbase + static_cast<uint64_t>(t) * a.A);
     }
-    if (a.smooth > 0.0f && a.T > 1) {
-        // swm_temporal_color_noise_f32 (src/planner.rs:1852-1896)
-        const float keep = 1.0f - a.smooth;
-        float prev = eps[0], mean = 0.0f;
-        for (uint32_t t = 0; t < a.T; ++t) {
-            prev = (t == 0) ? eps[t] : fmaf(a.smooth, prev, keep * eps[t]);
-            eps[t] = prev;
-            mean += prev;
-        }
-        mean /= static_cast<float>(a.T);
-        float var = 0.0f;
-        for (uint32_t t = 0; t < a.T; ++t) {
-            const float c = eps[t] - mean;
-            eps[t] = c;
-            var += c * c;
-        }
-        const float inv_std = 1.0f / sqrtf(var / static_cast<float>(a.T) + 1.0e-6f);
-        for (uint32_t t = 0; t < a.T; ++t) eps[t] *= inv_std;
-    }
+    if (a.smooth > 0.0f && a.T > 1) color_lane(eps, a.T, a.smooth);
     const uint32_t g = a.sample_base + s;  // the candidate's row in the (unsharded) plan
     const bool carried = a.carried && g >= 1 && g <= a.inject;
     const float lo = a.low[act], hi = a.high[act];
@@ -100,10 +105,15 @@ __global__ void __launch_bounds__(256) mppi_combine_kernel(MppiArgs m, const flo
 
 // ------------------------------------------------ top-k + elite refit
 //
-// One block per vehicle.  Keys (score, index) are sorted ascending with a
-// shared-memory bitonic network, which gives lowest_score_indices
-// (src/planner.rs:1647-1659) for any count; then select_elites +
-// gather_candidate_sequences (:1730-1754) and the refit of
+// One block per vehicle.  lowest_score_indices (src/planner.rs:1647-1659:
+// ascending scores, NaN as +inf, ties to the lower index) is the ascending
+// order of the unique 64-bit keys (score, index).  Short rows are sorted
+// whole in shared memory (bitonic).  Longer rows are radix-selected first:
+// four 8-bit digit passes over the scores find the K-th smallest score, an
+// ordered compaction keeps the keys below it and the lowest-index keys equal
+// to it (exactly K keys), and only those K are sorted — the same K keys in
+// the same order as the full sort, with no limit on the row length.  Then
+// select_elites + gather_candidate_sequences (:1730-1754) and the refit of
 //   CEM  (:516-517):  mean = elites.mean(1), std = max(sqrt(var_unbiased), min_std)
 //   iCEM (:859-868):  mean = momentum(mean, elite_mean, alpha),
 //                     std = max(momentum(std, max(sqrt(var), min_std), alpha), min_std)
@@ -127,13 +137,135 @@ __device__ __forceinline__ void bitonic_sort_keys(uint64_t* keys, uint32_t n) {
     }
 }
 
+// The orderable score word of score_key (its high 32 bits).
+__device__ __forceinline__ uint32_t score_ord(float v) { return static_cast<uint32_t>(score_key(v, 0u) >> 32); }
+
+struct SelectShared {
+    uint32_t hist[256];
+    uint32_t warp_lt[32], warp_eq[32];
+    uint32_t bin, need;
+};
+
+// keys[0..K) = the K lowest keys of scores[0..S) in ascending order; keys has
+// room for `len` entries (sort_length(S) for a whole-row sort, else
+// sort_length(K)).  Needs blockDim.x a multiple of 32, at most 1024, and
+// 1 <= K <= S.
+__device__ void lowest_keys(const float* scores, uint32_t S, uint32_t K, uint32_t len, bool select,
+                            uint64_t* keys) {
+    const uint32_t tid = threadIdx.x, nt = blockDim.x, lane = tid & 31u, warp = tid >> 5, nwarps = nt >> 5;
+    if (!select) {
+        for (uint32_t i = tid; i < len; i += nt) keys[i] = i < S ? score_key(scores[i], i) : ~0ull;
+        __syncthreads();
+        bitonic_sort_keys(keys, len);
+        return;
+    }
+    __shared__ SelectShared sh;
+    // 1. the K-th smallest score word, one 8-bit digit per pass (most significant first)
+    uint32_t prefix = 0u, mask = 0u, need = K;  // need: rank of the K-th key inside the current bucket
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (uint32_t i = tid; i < 256; i += nt) sh.hist[i] = 0u;
+        __syncthreads();
+        for (uint32_t base = 0; base < S; base += nt) {  // block-uniform trip count: whole warps below
+            const uint32_t i = base + tid;
+            bool take = false;
+            uint32_t bin = 256u + lane;  // lanes that do not count get a bin of their own
+            if (i < S) {
+                const uint32_t o = score_ord(scores[i]);
+                take = (o & mask) == prefix;
+                if (take) bin = (o >> shift) & 255u;
+            }
+            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+            if (take && lane == static_cast<uint32_t>(__ffs(peers) - 1)) atomicAdd(&sh.hist[bin], __popc(peers));
+        }
+        if (tid == 0) {  // overwritten below; keeps the state defined whatever the counts
+            sh.bin = 0u;
+            sh.need = need;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t c[8], sum = 0u;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = sh.hist[lane * 8u + j];
+                sum += c[j];
+            }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += v;
+            }
+            uint32_t run = incl - sum;
+            if (run < need && need <= incl) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run < need && need <= run + c[j]) {
+                        sh.bin = lane * 8u + j;
+                        sh.need = need - run;
+                    }
+                    run += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= sh.bin << shift;
+        mask |= 255u << shift;
+        need = sh.need;
+        __syncthreads();
+    }
+    // 2. ordered compaction: every key below the K-th score word, then the
+    //    `need` lowest-index keys equal to it
+    const uint32_t n_less = K - need;
+    const uint32_t below = (1u << lane) - 1u;
+    uint32_t lt_base = 0u, eq_base = 0u;
+    for (uint32_t base = 0; base < S; base += nt) {
+        const uint32_t i = base + tid;
+        uint32_t o = 0u;
+        bool lt = false, eq = false;
+        if (i < S) {
+            o = score_ord(scores[i]);
+            lt = o < prefix;
+            eq = o == prefix;
+        }
+        const uint32_t blt = __ballot_sync(0xffffffffu, lt), beq = __ballot_sync(0xffffffffu, eq);
+        if (lane == 0) {
+            sh.warp_lt[warp] = __popc(blt);
+            sh.warp_eq[warp] = __popc(beq);
+        }
+        __syncthreads();
+        uint32_t off_lt = 0u, off_eq = 0u, tot_lt = 0u, tot_eq = 0u;
+        for (uint32_t w = 0; w < nwarps; ++w) {
+            const uint32_t nl = sh.warp_lt[w], ne = sh.warp_eq[w];
+            if (w < warp) {
+                off_lt += nl;
+                off_eq += ne;
+            }
+            tot_lt += nl;
+            tot_eq += ne;
+        }
+        const uint64_t key = (static_cast<uint64_t>(o) << 32) | i;
+        if (lt) {
+            const uint32_t r = lt_base + off_lt + __popc(blt & below);
+            if (r < n_less) keys[r] = key;  // always true: exactly n_less keys are below
+        }
+        if (eq) {
+            const uint32_t r = eq_base + off_eq + __popc(beq & below);
+            if (r < need) keys[n_less + r] = key;
+        }
+        lt_base += tot_lt;
+        eq_base += tot_eq;
+        __syncthreads();
+        if (lt_base == n_less && eq_base >= need) break;  // block-uniform: every key is placed
+    }
+    for (uint32_t i = K + tid; i < len; i += nt) keys[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort_keys(keys, len);
+}
+
 __global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
     extern __shared__ uint64_t s_keys[];
     const uint32_t b = blockIdx.x;
-    for (uint32_t i = threadIdx.x; i < a.sort_len; i += blockDim.x)
-        s_keys[i] = i < a.S ? score_key(a.scores[static_cast<size_t>(b) * a.S + i], i) : ~0ull;
-    __syncthreads();
-    bitonic_sort_keys(s_keys, a.sort_len);
+    lowest_keys(a.scores + static_cast<size_t>(b) * a.S, a.S, a.K, a.sort_len, a.select != 0, s_keys);
     const uint32_t TA = a.T * a.A;
     const size_t seq = static_cast<size_t>(b) * TA;
     const float* cb = a.cand + static_cast<size_t>(b) * a.S * TA;
@@ -199,14 +331,11 @@ __global__ void __launch_bounds__(1024) topk_refit_kernel(RefitArgs a) {
 // sorting the union by (score, position) with positions in shard order gives
 // the (score, global index) order of the unsharded selection.
 __global__ void __launch_bounds__(1024) elite_tuples_kernel(const float* scores, const float* cand, uint32_t S,
-                                                            uint32_t sort_len, uint32_t K, uint32_t TA,
-                                                            uint32_t base, float* out) {
+                                                            uint32_t sort_len, uint32_t select, uint32_t K,
+                                                            uint32_t TA, uint32_t base, float* out) {
     extern __shared__ uint64_t s_keys[];
     const uint32_t b = blockIdx.x, W = 2 + TA;
-    for (uint32_t i = threadIdx.x; i < sort_len; i += blockDim.x)
-        s_keys[i] = i < S ? score_key(scores[static_cast<size_t>(b) * S + i], i) : ~0ull;
-    __syncthreads();
-    bitonic_sort_keys(s_keys, sort_len);
+    lowest_keys(scores + static_cast<size_t>(b) * S, S, K, sort_len, select != 0, s_keys);
     for (uint32_t q = threadIdx.x; q < K * W; q += blockDim.x) {
         const uint32_t j = q / W, f = q % W, idx = static_cast<uint32_t>(s_keys[j]);
         const size_t row = static_cast<size_t>(b) * S + idx;
@@ -237,43 +366,29 @@ __global__ void __launch_bounds__(256) elite_merge_kernel(const float* gathered,
 }
 
 // lowest_score_indices alone (the swm_lowest_k_indices_f32 replacement).
-__global__ void __launch_bounds__(1024) lowest_k_kernel(const float* scores, uint32_t* out,
-                                                        uint32_t S, uint32_t sort_len, uint32_t K) {
+__global__ void __launch_bounds__(1024) lowest_k_kernel(const float* scores, uint32_t* out, uint32_t S,
+                                                        uint32_t sort_len, uint32_t select, uint32_t K) {
     extern __shared__ uint64_t s_keys[];
     const uint32_t b = blockIdx.x;
-    for (uint32_t i = threadIdx.x; i < sort_len; i += blockDim.x)
-        s_keys[i] = i < S ? score_key(scores[static_cast<size_t>(b) * S + i], i) : ~0ull;
-    __syncthreads();
-    bitonic_sort_keys(s_keys, sort_len);
+    lowest_keys(scores + static_cast<size_t>(b) * S, S, K, sort_len, select != 0, s_keys);
     for (uint32_t j = threadIdx.x; j < K; j += blockDim.x)
         out[static_cast<size_t>(b) * K + j] = static_cast<uint32_t>(s_keys[j]);
 }
 
-// color_temporal_noise alone (src/planner.rs:1852-1896), one thread per lane.
-__global__ void __launch_bounds__(256) color_noise_kernel(const float* in, float* out, uint64_t sequences,
-                                                          uint32_t T, uint32_t A, float smooth) {
-    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= sequences) return;
-    const uint64_t action = idx % A, sample = idx / A;
-    const uint64_t base = sample * T * A + action;
-    const float keep = 1.0f - smooth;
-    float prev = in[base], mean = 0.0f;
-    for (uint32_t t = 0; t < T; ++t) {
-        const uint64_t o = base + static_cast<uint64_t>(t) * A;
-        prev = (t == 0) ? in[o] : fmaf(smooth, prev, keep * in[o]);
-        out[o] = prev;
-        mean += prev;
-    }
-    mean /= static_cast<float>(T);
-    float var = 0.0f;
-    for (uint32_t t = 0; t < T; ++t) {
-        const uint64_t o = base + static_cast<uint64_t>(t) * A;
-        const float c = out[o] - mean;
-        out[o] = c;
-        var += c * c;
-    }
-    const float inv_std = 1.0f / sqrtf(var / static_cast<float>(T) + 1.0e-6f);
-    for (uint32_t t = 0; t < T; ++t) out[base + static_cast<uint64_t>(t) * A] *= inv_std;
+// color_temporal_noise alone: each thread loads one (sample, action) lane
+// into registers, colors it with the sampler's lane code and stores it.
+__global__ void __launch_bounds__(256) color_noise_kernel(const float* in, float* out, uint64_t lanes, uint32_t T,
+                                                          uint32_t A, float smooth) {
+    const uint64_t lane_id = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (lane_id >= lanes) return;
+    const uint64_t row = lane_id / A;
+    const uint32_t act = static_cast<uint32_t>(lane_id - row * A);
+    const float* src = in + row * T * A + act;
+    float eps[kMaxHorizon];
+    for (uint32_t t = 0; t < T; ++t) eps[t] = src[static_cast<size_t>(t) * A];
+    color_lane(eps, T, smooth);
+    float* dst = out + row * T * A + act;
+    for (uint32_t t = 0; t < T; ++t) dst[static_cast<size_t>(t) * A] = eps[t];
 }
 
 __global__ void __launch_bounds__(256) normal_fill_kernel(uint64_t seed, uint64_t offset, uint64_t count,
@@ -313,27 +428,65 @@ uint32_t sort_length(uint32_t S) {
     return n;
 }
 
-cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(a.sort_len) * sizeof(uint64_t);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(topk_refit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+bool topk_layout(uint32_t S, uint32_t K, uint32_t* len, uint32_t* select) {
+    if (K == 0 || K > S || K > kMaxElites) return false;
+    const bool sel = S > kSortWholeRow;
+    *select = sel ? 1u : 0u;
+    *len = sort_length(sel ? K : S);
+    return true;
+}
+
+namespace {
+
+// Dynamic shared memory for `len` keys, with the opt-in above 48 KB made
+// once per (kernel, device) for the largest layout.
+template <typename Kern>
+cudaError_t keys_smem(Kern kernel, uint32_t len, size_t* smem) {
+    *smem = static_cast<size_t>(len) * sizeof(uint64_t);
+    if (*smem <= 48 * 1024) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    static std::mutex mu;
+    static bool done[3][64] = {};
+    const int which = reinterpret_cast<const void*>(kernel) == reinterpret_cast<const void*>(topk_refit_kernel) ? 0
+                      : reinterpret_cast<const void*>(kernel) == reinterpret_cast<const void*>(elite_tuples_kernel) ? 1
+                                                                                                                  : 2;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[which][dev]) {
+        const size_t max_smem = static_cast<size_t>(sort_length(kMaxElites > kSortWholeRow ? kMaxElites : kSortWholeRow)) *
+                                sizeof(uint64_t);
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(max_smem));
         if (e != cudaSuccess) return e;
+        done[which][dev] = true;
     }
-    const uint32_t threads = a.sort_len < 1024 ? (a.sort_len < 64 ? 64 : a.sort_len) : 1024;
-    topk_refit_kernel<<<B, threads, smem, stream>>>(a);
+    return cudaSuccess;
+}
+
+uint32_t keys_threads(uint32_t len, uint32_t select) {
+    if (select) return 1024;  // the selection passes stride the whole row
+    return len < 1024 ? (len < 64 ? 64 : len) : 1024;
+}
+
+}  // namespace
+
+cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream) {
+    size_t smem = 0;
+    cudaError_t e = keys_smem(topk_refit_kernel, a.sort_len, &smem);
+    if (e != cudaSuccess) return e;
+    topk_refit_kernel<<<B, keys_threads(a.sort_len, a.select), smem, stream>>>(a);
     return cudaGetLastError();
 }
 
 cudaError_t launch_elite_tuples(const float* scores, const float* cand, uint32_t B, uint32_t S, uint32_t K,
                                 uint32_t TA, uint32_t base, float* out, cudaStream_t stream) {
-    const uint32_t len = sort_length(S);
-    const size_t smem = static_cast<size_t>(len) * sizeof(uint64_t);
-    if (smem > 200 * 1024 || K > S) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(elite_tuples_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    uint32_t len = 0, select = 0;
+    if (!topk_layout(S, K, &len, &select)) return cudaErrorInvalidValue;
+    size_t smem = 0;
+    cudaError_t e = keys_smem(elite_tuples_kernel, len, &smem);
     if (e != cudaSuccess) return e;
-    elite_tuples_kernel<<<B, 1024, smem, stream>>>(scores, cand, S, len, K, TA, base, out);
+    elite_tuples_kernel<<<B, 1024, smem, stream>>>(scores, cand, S, len, select, K, TA, base, out);
     return cudaGetLastError();
 }
 
@@ -347,15 +500,12 @@ cudaError_t launch_elite_merge(const float* gathered, uint32_t G, uint32_t B, ui
 
 cudaError_t launch_lowest_k(const float* scores, uint32_t* out, uint32_t B, uint32_t S, uint32_t K,
                             cudaStream_t stream) {
-    const uint32_t n = sort_length(S);
-    const size_t smem = static_cast<size_t>(n) * sizeof(uint64_t);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(lowest_k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-    }
-    const uint32_t threads = n < 1024 ? (n < 64 ? 64 : n) : 1024;
-    lowest_k_kernel<<<B, threads, smem, stream>>>(scores, out, S, n, K);
+    uint32_t len = 0, select = 0;
+    if (!topk_layout(S, K, &len, &select)) return cudaErrorInvalidValue;
+    size_t smem = 0;
+    cudaError_t e = keys_smem(lowest_k_kernel, len, &smem);
+    if (e != cudaSuccess) return e;
+    lowest_k_kernel<<<B, keys_threads(len, select), smem, stream>>>(scores, out, S, len, select, K);
     return cudaGetLastError();
 }
 

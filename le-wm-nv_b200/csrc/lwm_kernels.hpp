@@ -55,7 +55,7 @@ struct SampleArgs {
 };
 
 struct RefitArgs {
-    uint32_t S, T, A, K, keep, sort_len;
+    uint32_t S, T, A, K, keep, sort_len, select;  // sort_len, select: from topk_layout
     const float* scores;   // [B,S]
     const float* cand;     // [B,S,T,A]
     float* mean;           // [B,T,A] in/out
@@ -199,6 +199,13 @@ cudaError_t launch_mppi_reduce(const MppiArgs& m, const float* cand, const float
 cudaError_t launch_mppi_combine(const MppiArgs& m, const float* tuples, uint32_t B, uint32_t shards,
                                 cudaStream_t stream);
 uint32_t sort_length(uint32_t S);
+// Lowest-K selection limits: rows of up to kSortWholeRow scores are sorted
+// whole; longer rows (any length) are radix-selected down to their K lowest
+// keys first.  K is at most kMaxElites (its keys are sorted in shared memory).
+constexpr uint32_t kSortWholeRow = 4096, kMaxElites = 16384;
+// The shared-memory key count (`len`) and mode of a lowest-K selection over
+// S scores; false when K is 0, above S or above kMaxElites.
+bool topk_layout(uint32_t S, uint32_t K, uint32_t* len, uint32_t* select);
 cudaError_t launch_topk_refit(const RefitArgs& a, uint32_t B, cudaStream_t stream);
 // A CEM / iCEM shard's lowest K candidates as tuples [B][K][2 + TA] (score,
 // global index bits, actions), and the merge of every shard's tuples.

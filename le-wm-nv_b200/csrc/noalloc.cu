@@ -58,6 +58,15 @@ lwm_status scratch_address(int device, unsigned char** out) {
 
 bool finite(float v) { return v == v && v - v == 0.0f; }
 
+// Puts the caller's current device back when the entry point returns.
+struct CurrentDevice {
+    int device;
+    explicit CurrentDevice(int d) : device(d) {}
+    ~CurrentDevice() { cudaSetDevice(device); }
+    CurrentDevice(const CurrentDevice&) = delete;
+    CurrentDevice& operator=(const CurrentDevice&) = delete;
+};
+
 }  // namespace
 
 extern "C" lwm_status lwm_nominal_mppi_noalloc(int device, void* stream, const lwm_nominal_scorer_config* cfg,
@@ -94,7 +103,11 @@ extern "C" lwm_status lwm_nominal_mppi_noalloc(int device, void* stream, const l
     int count = 0;
     if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count || device >= kMaxDevices)
         return fail(LWM_INVALID_ARGUMENT, "CUDA device " + std::to_string(device) + " does not exist");
-    cudaError_t e = cudaSetDevice(device);
+    int caller_device = 0;
+    cudaError_t e = cudaGetDevice(&caller_device);
+    if (e != cudaSuccess) return fail(LWM_CUDA_ERROR, std::string("cudaGetDevice failed: ") + cudaGetErrorString(e));
+    const CurrentDevice keep(caller_device);  // the caller's current device is back on every return
+    e = cudaSetDevice(device);
     if (e != cudaSuccess) return fail(LWM_CUDA_ERROR, std::string("cudaSetDevice failed: ") + cudaGetErrorString(e));
     unsigned char* base = nullptr;
     const lwm_status st = scratch_address(device, &base);

@@ -316,6 +316,8 @@ _sig("lwm_planner_clear_warm_start", C.c_int, VP)
 _sig("lwm_planner_warm_start", C.c_int, VP, FP, C.c_size_t, C.POINTER(U32))
 _sig("lwm_planner_reset_rng", C.c_int, VP)
 _sig("lwm_planner_rng_offset", C.c_int, VP, C.POINTER(U64))
+_sig("lwm_planner_elite_indices", C.c_int, VP, C.POINTER(U32), C.c_size_t, C.POINTER(U32), C.POINTER(U32),
+     C.POINTER(U32))
 _sig("lwm_planner_last_candidates", C.c_int, VP, C.POINTER(VP), C.POINTER(U32))
 _sig("lwm_domain_default", None, C.POINTER(Domain))
 _sig("lwm_domain_sample", None, U64, C.POINTER(Domain))
@@ -961,7 +963,22 @@ class MppiPlanner(_Planner):
     _create = staticmethod(lib.lwm_mppi_create)
 
 
-class CemPlanner(_Planner):
+class _ElitePlanner(_Planner):
+    def elite_indices(self) -> np.ndarray:
+        """The elite indices every iteration of the last plan selected, in
+        selection order (ascending score, ties to the lower index), as
+        [iterations, batch, elites] uint32."""
+        its, b, k = U32(), U32(), U32()
+        cfg = self.config
+        cap = cfg.iterations * 4096 * cfg.elites
+        buf = np.empty(cap, np.uint32)
+        _check(lib.lwm_planner_elite_indices(self.handle, buf.ctypes.data_as(C.POINTER(U32)), C.c_size_t(cap),
+                                             C.byref(its), C.byref(b), C.byref(k)))
+        n = its.value * b.value * k.value
+        return buf[:n].reshape(its.value, b.value, k.value).copy()
+
+
+class CemPlanner(_ElitePlanner):
     """CemPlanner (src/planner.rs:418-541)."""
     kind = "CEM"
     _create = staticmethod(lib.lwm_cem_create)
@@ -970,7 +987,7 @@ class CemPlanner(_Planner):
         raise LwmError(1, "CEM planners have no warm start")
 
 
-class IcemPlanner(_Planner):
+class IcemPlanner(_ElitePlanner):
     """IcemPlanner (src/planner.rs:731-1053)."""
     kind = "iCEM"
     _create = staticmethod(lib.lwm_icem_create)

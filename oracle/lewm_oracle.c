@@ -562,6 +562,9 @@ struct orc_skyjepa {
     const float *p_hid_w[16], *p_hid_b[16];
     const float *p_out_w, *p_out_b;
     float* storage;
+    /* 1: round where the bf16 tensor-core rollout rounds (see
+     * orc_skyjepa_set_tensor_core_rounding) */
+    int tc_rounding;
 };
 
 static size_t tcn_layout(const lwm_tcn_config* c, orc_tcn* t, const float* base, size_t off) {
@@ -636,6 +639,48 @@ orc_skyjepa* orc_skyjepa_new(const lwm_skyjepa_config* cfg, const float* weights
     memcpy(m->storage, weights, sizeof(float) * count);
     model_layout(cfg, m, m->storage);
     return m;
+}
+
+/* f32 -> bf16 -> f32, round to nearest even (the rounding of
+ * __float2bfloat16_rn; NaN stays NaN). */
+static float round_bf16(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return v;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    memcpy(&v, &u, 4);
+    return v;
+}
+
+/* The tensor-core rollout's numerics (bf16 operands, f32 accumulation and
+ * state), not a reference behaviour: the recurrent and input weights and the
+ * prober's first-layer weights are bf16; the GRU biases enter the GEMM as one
+ * bf16 value per gate row (r: b_ir + b_hr, z: b_iz + b_hz, n: b_in and b_hn
+ * apart); the action-encoder output and the copy of h that the GEMMs read are
+ * rounded to bf16 every step while h itself stays f32.  It lets the bf16
+ * path be checked against a model of its own rounding instead of only the
+ * f32 tolerance.  The weights of `m` are re-rounded in place: make a fresh
+ * model to go back to f32. */
+void orc_skyjepa_set_tensor_core_rounding(orc_skyjepa* m) {
+    uint32_t H = m->cfg.latent_dim, E = m->tcn[1].out_dim, hid = m->cfg.prober_hidden_dim;
+    float* w_ih = (float*)m->w_ih;
+    float* w_hh = (float*)m->w_hh;
+    float* b_ih = (float*)m->b_ih;
+    float* b_hh = (float*)m->b_hh;
+    float* p_in = (float*)m->p_in_w;
+    for (size_t i = 0; i < (size_t)3 * H * E; ++i) w_ih[i] = round_bf16(w_ih[i]);
+    for (size_t i = 0; i < (size_t)3 * H * H; ++i) w_hh[i] = round_bf16(w_hh[i]);
+    for (size_t i = 0; i < (size_t)hid * H; ++i) p_in[i] = round_bf16(p_in[i]);
+    for (uint32_t u = 0; u < 2 * H; ++u) {  /* r and z rows: one combined bias */
+        b_ih[u] = round_bf16(b_ih[u] + b_hh[u]);
+        b_hh[u] = 0.0f;
+    }
+    for (uint32_t u = 2 * H; u < 3 * H; ++u) {
+        b_ih[u] = round_bf16(b_ih[u]);
+        b_hh[u] = round_bf16(b_hh[u]);
+    }
+    m->tc_rounding = 1;
 }
 
 void orc_skyjepa_free(orc_skyjepa* m) {
@@ -750,8 +795,18 @@ void orc_initial_latent(const orc_skyjepa* m, const float* norm_state_hist, uint
 static void gru_row(const orc_skyjepa* m, const float* x, const float* h, float* gi, float* gh, float* out) {
     uint32_t H = m->cfg.latent_dim;
     uint32_t E = m->tcn[1].out_dim;
-    linear(x, E, m->w_ih, m->b_ih, 3 * H, gi);
-    linear(h, H, m->w_hh, m->b_hh, 3 * H, gh);
+    if (m->tc_rounding) {  /* the GEMMs read bf16 copies of x and h */
+        float* xq = (float*)malloc(sizeof(float) * (E + H));
+        float* hq = xq + E;
+        for (uint32_t i = 0; i < E; ++i) xq[i] = round_bf16(x[i]);
+        for (uint32_t i = 0; i < H; ++i) hq[i] = round_bf16(h[i]);
+        linear(xq, E, m->w_ih, m->b_ih, 3 * H, gi);
+        linear(hq, H, m->w_hh, m->b_hh, 3 * H, gh);
+        free(xq);
+    } else {
+        linear(x, E, m->w_ih, m->b_ih, 3 * H, gi);
+        linear(h, H, m->w_hh, m->b_hh, 3 * H, gh);
+    }
     for (uint32_t j = 0; j < H; ++j) {
         float r = sigmoidf(gi[j] + gh[j]);
         float z = sigmoidf(gi[H + j] + gh[H + j]);
@@ -775,7 +830,8 @@ void orc_gru_step(const orc_skyjepa* m, const float* x, const float* h, uint32_t
  * layout lets the compiler vectorise across rows. */
 #define ORC_LANES 8
 static void gru_rows8(const orc_skyjepa* m, const float* x8 /*[E][8]*/, const float* hT /*[H][8]*/,
-                      float* gi /*[3H][8]*/, float* gh /*[3H][8]*/, float* outT /*[H][8]*/) {
+                      const float* hqT /*[H][8]: the h the GEMM reads*/, float* gi /*[3H][8]*/,
+                      float* gh /*[3H][8]*/, float* outT /*[H][8]*/) {
     uint32_t H = m->cfg.latent_dim;
     uint32_t E = m->tcn[1].out_dim;
     for (uint32_t g = 0; g < 3 * H; ++g) {
@@ -790,7 +846,7 @@ static void gru_rows8(const orc_skyjepa* m, const float* x8 /*[E][8]*/, const fl
         const float* w = m->w_hh + (size_t)g * H;
         for (uint32_t k = 0; k < H; ++k) {
             float wk = w[k];
-            const float* hk = hT + (size_t)k * ORC_LANES;
+            const float* hk = hqT + (size_t)k * ORC_LANES;
             for (int l = 0; l < ORC_LANES; ++l) acc[l] += hk[l] * wk;
         }
         for (int l = 0; l < ORC_LANES; ++l) gh[g * ORC_LANES + l] = acc[l] + m->b_hh[g];
@@ -827,6 +883,7 @@ void orc_rollout_latents(const orc_skyjepa* m, const float* norm_state_hist,
         float* emb = (float*)malloc(sizeof(float) * (size_t)T * E * ORC_LANES);
         float* hT = (float*)malloc(sizeof(float) * (size_t)H * ORC_LANES);
         float* nT = (float*)malloc(sizeof(float) * (size_t)H * ORC_LANES);
+        float* qT = m->tc_rounding ? (float*)malloc(sizeof(float) * (size_t)H * ORC_LANES) : NULL;
         float* gi = (float*)malloc(sizeof(float) * (size_t)3 * H * ORC_LANES);
         float* gh = (float*)malloc(sizeof(float) * (size_t)3 * H * ORC_LANES);
         float* last = (float*)malloc(sizeof(float) * E);
@@ -846,12 +903,15 @@ void orc_rollout_latents(const orc_skyjepa* m, const float* norm_state_hist,
                         memcpy(window + (size_t)w * A, src, A * sizeof(float));
                     }
                     tcn_sequence(tcn, window, Hs, work, last);
-                    for (uint32_t e = 0; e < E; ++e) emb[((size_t)t * E + e) * ORC_LANES + l] = last[e];
+                    for (uint32_t e = 0; e < E; ++e)
+                        emb[((size_t)t * E + e) * ORC_LANES + l] = m->tc_rounding ? round_bf16(last[e]) : last[e];
                 }
                 for (uint32_t j = 0; j < H; ++j) hT[(size_t)j * ORC_LANES + l] = h0[(size_t)b * H + j];
             }
             for (uint32_t t = 0; t < T; ++t) {
-                gru_rows8(m, emb + (size_t)t * E * ORC_LANES, hT, gi, gh, nT);
+                if (qT)
+                    for (size_t q = 0; q < (size_t)H * ORC_LANES; ++q) qT[q] = round_bf16(hT[q]);
+                gru_rows8(m, emb + (size_t)t * E * ORC_LANES, hT, qT ? qT : hT, gi, gh, nT);
                 float* tmp = hT; hT = nT; nT = tmp;
                 for (int l = 0; l < ORC_LANES; ++l) {
                     uint32_t s = s0 + (uint32_t)l;
@@ -861,7 +921,7 @@ void orc_rollout_latents(const orc_skyjepa* m, const float* norm_state_hist,
                 }
             }
         }
-        free(work); free(window); free(emb); free(hT); free(nT); free(gi); free(gh); free(last);
+        free(work); free(window); free(emb); free(hT); free(nT); free(qT); free(gi); free(gh); free(last);
     }
     free(h0);
 }
@@ -874,9 +934,15 @@ void orc_prober(const orc_skyjepa* m, const float* latents, uint32_t N, float* o
     {
         float* a = (float*)malloc(sizeof(float) * hid);
         float* b = (float*)malloc(sizeof(float) * hid);
+        float* q = m->tc_rounding ? (float*)malloc(sizeof(float) * H) : NULL;
 #pragma omp for schedule(static)
         for (long long n = 0; n < (long long)N; ++n) {
-            linear(latents + (size_t)n * H, H, m->p_in_w, m->p_in_b, hid, a);
+            const float* in = latents + (size_t)n * H;
+            if (q) {  /* the prober's first GEMM reads the bf16 copy of h */
+                for (uint32_t i = 0; i < H; ++i) q[i] = round_bf16(in[i]);
+                in = q;
+            }
+            linear(in, H, m->p_in_w, m->p_in_b, hid, a);
             for (uint32_t i = 0; i < hid; ++i) a[i] = gelu_tanh(a[i]);
             for (uint32_t l = 0; l + 1 < m->cfg.prober_hidden_layers; ++l) {
                 linear(a, hid, m->p_hid_w[l], m->p_hid_b[l], hid, b);
@@ -886,6 +952,7 @@ void orc_prober(const orc_skyjepa* m, const float* latents, uint32_t N, float* o
         }
         free(a);
         free(b);
+        free(q);
     }
 }
 
@@ -1114,7 +1181,7 @@ int orc_mppi_plan(const lwm_mppi_config* cfg, const float* warm_start, uint32_t 
 /* CemPlanner::plan_device (src/planner.rs:450-541). */
 int orc_cem_plan(const lwm_cem_config* cfg, uint32_t B, const float* noise, uint64_t seed,
                  uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores,
-                 uint32_t* best, float* last_cand) {
+                 uint32_t* best, float* last_cand, uint32_t* elites_out, float* iter_scores_out) {
     uint32_t S = cfg->samples, T = cfg->horizon, A = cfg->action_dim, K = cfg->elites;
     size_t seq_n = (size_t)B * T * A, n = (size_t)B * S * T * A;
     size_t per_iter = round_even(n);
@@ -1131,6 +1198,8 @@ int orc_cem_plan(const lwm_cem_config* cfg, uint32_t B, const float* noise, uint
         orc_sample(mean, std, eps, cfg->bounds_low, cfg->bounds_high, B, S, T, A, cand);
         fn(user, cand, B, S, T, A, sc);
         orc_lowest_k(sc, B, S, K, idx);
+        if (elites_out) memcpy(elites_out + (size_t)it * B * K, idx, sizeof(uint32_t) * B * K);
+        if (iter_scores_out) memcpy(iter_scores_out + (size_t)it * B * S, sc, sizeof(float) * B * S);
         orc_gather(cand, idx, B, S, K, T, A, el);
         orc_refit(el, B, K, T, A, cfg->min_std, mean, std);
     }
@@ -1149,7 +1218,8 @@ int orc_cem_plan(const lwm_cem_config* cfg, uint32_t B, const float* noise, uint
  * ([iterations][4][B]). */
 static int icem_core(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise,
                      uint64_t seed, uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores,
-                     uint32_t* best, float* warm_out, float* last_cand, float* trace) {
+                     uint32_t* best, float* warm_out, float* last_cand, float* trace, uint32_t* elites_out,
+                     float* iter_scores_out) {
     uint32_t S = cfg->samples, T = cfg->horizon, A = cfg->action_dim, K = cfg->elites, keep = cfg->keep_elites;
     size_t seq_n = (size_t)B * T * A, n = (size_t)B * S * T * A;
     size_t per_iter = round_even(n);
@@ -1175,6 +1245,8 @@ static int icem_core(const lwm_icem_config* cfg, const float* warm_start, uint32
         if (have_carried) orc_inject_carried(cand, carried, keep, keep, B, S, T, A);
         fn(user, cand, B, S, T, A, sc);
         orc_lowest_k(sc, B, S, K, idx);
+        if (elites_out) memcpy(elites_out + (size_t)it * B * K, idx, sizeof(uint32_t) * B * K);
+        if (iter_scores_out) memcpy(iter_scores_out + (size_t)it * B * S, sc, sizeof(float) * B * S);
         orc_gather(cand, idx, B, S, K, T, A, el);
         orc_refit(el, B, K, T, A, cfg->min_std, em, es);
         if (tr) {
@@ -1206,16 +1278,16 @@ static int icem_core(const lwm_icem_config* cfg, const float* warm_start, uint32
 
 int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise, uint64_t seed,
                   uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores, uint32_t* best,
-                  float* warm_out, float* last_cand) {
+                  float* warm_out, float* last_cand, uint32_t* elites_out, float* iter_scores_out) {
     return icem_core(cfg, warm_start, B, noise, seed, offset, fn, user, sequence, scores, best, warm_out, last_cand,
-                     NULL);
+                     NULL, elites_out, iter_scores_out);
 }
 
 int orc_icem_trace(const lwm_icem_config* cfg, const float* warm_start, uint32_t B, const float* noise, uint64_t seed,
                    uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores, uint32_t* best,
                    float* warm_out, float* trace) {
     return icem_core(cfg, warm_start, B, noise, seed, offset, fn, user, sequence, scores, best, warm_out, NULL,
-                     trace);
+                     trace, NULL, NULL);
 }
 
 /* ---------------------------------------------------------------- task */

@@ -77,6 +77,9 @@ void orc_nominal_scores(const float* initial, const float* motors, const float* 
 /* ---- SkyJEPA learned model ---- */
 typedef struct orc_skyjepa orc_skyjepa;
 orc_skyjepa* orc_skyjepa_new(const lwm_skyjepa_config* cfg, const float* weights, size_t count);
+/* Switch a model to the bf16 tensor-core rollout's rounding (weights
+ * re-rounded in place; not reversible). */
+void orc_skyjepa_set_tensor_core_rounding(orc_skyjepa* m);
 void orc_skyjepa_free(orc_skyjepa* m);
 size_t orc_skyjepa_weight_count(const lwm_skyjepa_config* cfg);
 /* which = 0 state encoder, 1 action encoder; x [N, time, in] -> out [N, C_last] */
@@ -115,13 +118,16 @@ int orc_mppi_plan(const lwm_mppi_config* cfg, const float* warm_start, uint32_t 
                   const float* noise, uint64_t seed, uint64_t offset, orc_score_fn fn,
                   void* user, float* sequence, float* scores, uint32_t* best, float* warm_out,
                   float* last_cand);
+/* elites_out (nullable): every iteration's lowest_score_indices
+ * [iterations][B][elites]; iter_scores_out (nullable): every iteration's
+ * candidate scores [iterations][B][S]. */
 int orc_cem_plan(const lwm_cem_config* cfg, uint32_t B, const float* noise, uint64_t seed,
                  uint64_t offset, orc_score_fn fn, void* user, float* sequence, float* scores,
-                 uint32_t* best, float* last_cand);
+                 uint32_t* best, float* last_cand, uint32_t* elites_out, float* iter_scores_out);
 int orc_icem_plan(const lwm_icem_config* cfg, const float* warm_start, uint32_t B,
                   const float* noise, uint64_t seed, uint64_t offset, orc_score_fn fn,
                   void* user, float* sequence, float* scores, uint32_t* best, float* warm_out,
-                  float* last_cand);
+                  float* last_cand, uint32_t* elites_out, float* iter_scores_out);
 /* IcemPlanner::trace_device (src/planner.rs:900-1010): as orc_icem_plan plus
  * trace [iterations][4][B] = mean, best-candidate, elite-mean and
  * updated-mean scores of every iteration. */

@@ -74,6 +74,7 @@ _sig("orc_tracking_scores", None, FP, FP, FP, FP, C.POINTER(TrackingCost), U32, 
 _sig("orc_nominal_scores", None, FP, FP, FP, FP, C.POINTER(TrackingCost), F, F, U32, C.POINTER(Domain),
      C.POINTER(Domain), FP, U32, U32, U32, FP, FP)
 _sig("orc_skyjepa_new", VP, C.POINTER(SkyJepaConfig), FP, C.c_size_t)
+_sig("orc_skyjepa_set_tensor_core_rounding", None, VP)
 _sig("orc_skyjepa_free", None, VP)
 _sig("orc_skyjepa_weight_count", C.c_size_t, C.POINTER(SkyJepaConfig))
 _sig("orc_tcn_forward_last", None, VP, C.c_int, FP, U32, U32, FP)
@@ -87,8 +88,8 @@ _sig("orc_so3_exp", None, FP, FP)
 _sig("orc_skyjepa_scores", None, VP, FP, FP, FP, FP, FP, FP, FP, FP, C.POINTER(TrackingCost), F, FP, U32, U32,
      U32, FP, FP, FP)
 _sig("orc_mppi_plan", C.c_int, C.POINTER(_MppiConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
-_sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, FP, FP, UP, FP)
-_sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
+_sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, UP, FP)
+_sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP, UP, FP)
 _sig("orc_icem_trace", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_reference_state", None, C.c_int, F, F, F, FP)
 _sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
@@ -245,13 +246,18 @@ def nominal_scores(initial, motors, ref_states, ref_actions, cost, dt, trim, can
 class SkyJepaModel:
     """Oracle SkyJEPA model over a weight blob (the layout of include/lewm_b200.h)."""
 
-    def __init__(self, cfg: SkyJepaConfig, weights: np.ndarray):
+    def __init__(self, cfg: SkyJepaConfig, weights: np.ndarray, tensor_core_rounding: bool = False):
+        """`tensor_core_rounding`: round where the bf16 tensor-core rollout
+        rounds (bf16 GRU / first prober-layer weights, combined GRU biases,
+        bf16 encoder outputs and GEMM copy of h; f32 state and accumulation)."""
         self.cfg = cfg
         self.weights = f32(weights)
         n = lib.orc_skyjepa_weight_count(C.byref(cfg))
         if n != self.weights.size:
             raise ValueError(f"weight blob has {self.weights.size} values, oracle layout needs {n}")
         self.handle = lib.orc_skyjepa_new(C.byref(cfg), fp(self.weights), self.weights.size)
+        if tensor_core_rounding:
+            lib.orc_skyjepa_set_tensor_core_rounding(self.handle)
 
     def __del__(self):
         # at interpreter exit the module's `lib` may already be gone
@@ -375,9 +381,11 @@ def cem_plan(cfg, B, scorer, noise=None, seed=0, offset=0):
     scores = np.empty((B, S), np.float32)
     best = np.empty(B, np.uint32)
     cand = np.empty((B, S, T, A), np.float32)
+    elites = np.empty((cfg.iterations, B, cfg.elites), np.uint32)
+    iter_scores = np.empty((cfg.iterations, B, S), np.float32)
     lib.orc_cem_plan(C.byref(c), B, fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq),
-                     fp(scores), up(best), fp(cand))
-    return dict(sequence=seq, scores=scores, best=best, candidates=cand)
+                     fp(scores), up(best), fp(cand), up(elites), fp(iter_scores))
+    return dict(sequence=seq, scores=scores, best=best, candidates=cand, elites=elites, iteration_scores=iter_scores)
 
 
 def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
@@ -389,10 +397,13 @@ def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
     best = np.empty(B, np.uint32)
     warm = np.empty((B, T, A), np.float32)
     cand = np.empty((B, S, T, A), np.float32)
+    elites = np.empty((cfg.iterations, B, cfg.elites), np.uint32)
+    iter_scores = np.empty((cfg.iterations, B, S), np.float32)
     lib.orc_icem_plan(C.byref(c), fp(f32(warm_start)) if warm_start is not None else None, B,
                       fp(f32(noise)) if noise is not None else None, seed, offset, fnp, user, fp(seq), fp(scores),
-                      up(best), fp(warm), fp(cand))
-    return dict(sequence=seq, scores=scores, best=best, warm=warm, candidates=cand)
+                      up(best), fp(warm), fp(cand), up(elites), fp(iter_scores))
+    return dict(sequence=seq, scores=scores, best=best, warm=warm, candidates=cand, elites=elites,
+                iteration_scores=iter_scores)
 
 
 def icem_trace(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):

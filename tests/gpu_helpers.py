@@ -34,6 +34,34 @@ def assert_same_argmin(best_ours, best_ref, scores_ref, rel=COST_REL, floor=1e-6
             assert abs(si - sj) <= rel * abs(sj) + floor, (b, i, j, si, sj)
 
 
+def assert_same_elites(ours, ref_elites, ref_iteration_scores, rel=COST_REL, floor=1e-6):
+    """Every iteration's elite indices, in selection order (ascending score,
+    ties to the lower index), equal the oracle's except where the two
+    candidates at a position have scores tied within the cost tolerance (the
+    contract's "bit-exact except for ties").  After an iteration whose
+    selection differs by such a tie, the next iteration refits from a
+    different elite set and is no longer comparable: the check stops there.
+    Returns the number of iterations compared exactly."""
+    ours = np.asarray(ours)
+    ref_elites = np.asarray(ref_elites)
+    assert ours.shape == ref_elites.shape, (ours.shape, ref_elites.shape)
+    for it in range(ours.shape[0]):
+        differs = False
+        for b in range(ours.shape[1]):
+            o, r = ours[it, b], ref_elites[it, b]
+            if np.array_equal(o, r):
+                continue
+            differs = True
+            sc = np.asarray(ref_iteration_scores[it, b], np.float64)
+            for j in np.nonzero(o != r)[0]:
+                si, sj = sc[o[j]], sc[r[j]]
+                assert abs(si - sj) <= rel * abs(sj) + floor, \
+                    f"iteration {it}, vehicle {b}, elite {j}: candidate {o[j]} ({si}) vs oracle {r[j]} ({sj})"
+        if differs:
+            return it
+    return ours.shape[0]
+
+
 def normals(seed, shape, offset=0):
     return O.normals(seed, offset, int(np.prod(shape))).reshape(shape)
 

@@ -6,7 +6,7 @@ import pytest
 
 import lewm_b200 as L
 import oracle as O
-from gpu_helpers import assert_actions_close, assert_costs_close, normals
+from gpu_helpers import assert_actions_close, assert_costs_close, assert_same_elites, normals
 from lewm_b200 import workloads as W
 from test_lewm_oracle import small_config, small_vit
 
@@ -73,11 +73,14 @@ def test_vector_cem_matches_oracle(ctx):
     e, g = emb.cpu().numpy()[:, None, :], goal.cpu().numpy()
     sc.set_context(e, g)
     noise = normals(53, (3, 1, 300, 5, 2))
-    r = L.CemPlanner(ctx, w.planner).plan(sc, injected_noise=noise)
+    planner = L.CemPlanner(ctx, w.planner)
+    r = planner.plan(sc, injected_noise=noise)
     m = O.LewmModel(w.config, w.weights)
     ref = O.cem_plan(w.planner, 1, (O.LEWM_FN, m.score_ctx(e, g)), noise=noise)
     assert_costs_close(r.scores, ref["scores"])
     assert_actions_close(r.sequence, ref["sequence"])
+    # the 30 elites of each of the 3 iterations equal the oracle's, up to ties within tolerance
+    assert assert_same_elites(planner.elite_indices(), ref["elites"], ref["iteration_scores"]) >= 1
 
 
 def test_small_vit_encoder_matches_oracle(ctx):

@@ -5,7 +5,7 @@ import pytest
 
 import lewm_b200 as L
 import oracle as O
-from gpu_helpers import assert_actions_close, normals
+from gpu_helpers import assert_actions_close, assert_same_elites, normals
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -45,12 +45,48 @@ def test_lowest_k_reference_known_answers(ctx):
     assert _lowest_k(ctx, weird, 7).tolist() == O.lowest_k(weird, 7).tolist()
 
 
-@pytest.mark.parametrize("S,k", [(1, 1), (7, 3), (300, 30), (4096, 64), (5000, 17), (16384, 100)])
+# Rows up to 4096 scores are sorted whole; longer ones go through the radix
+# selection (no limit on the row length), including K = S and K at its limit.
+@pytest.mark.parametrize("S,k", [(1, 1), (7, 3), (300, 30), (4096, 64), (4097, 4097), (5000, 17), (16384, 100),
+                                 (20000, 16384), (65536, 30), (100003, 4096)])
 def test_lowest_k_bit_exact_with_ties(ctx, S, k):
     rng = np.random.default_rng(S)
     scores = rng.integers(0, max(2, S // 8), (3, S)).astype(np.float32)  # many ties
     scores[0, rng.integers(0, S, max(1, S // 50))] = np.nan
+    scores[2] = rng.standard_normal(S).astype(np.float32)                # distinct values
     assert np.array_equal(_lowest_k(ctx, scores, k), O.lowest_k(scores, k))
+
+
+def test_lowest_k_selection_degenerate_rows(ctx):
+    # every score tied, all NaN, +-inf only, NaN with three finite values at
+    # the end, signed zeros: the selection path orders them as the full sort
+    S = 9000
+    idx = np.arange(S)
+    rows = np.stack([np.full(S, np.nan), np.full(S, 1.5), np.where(idx % 2 == 1, np.inf, -np.inf),
+                     np.concatenate([np.full(S - 3, np.nan), [3.0, 2.0, 1.0]]),
+                     np.where(idx % 3 == 0, -0.0, 0.0)]).astype(np.float32)
+    for k in (1, 5, 4500, S):
+        assert np.array_equal(_lowest_k(ctx, rows, min(k, 16384)), O.lowest_k(rows, min(k, 16384))), k
+
+
+def test_lowest_k_rejects_more_than_its_elite_limit(ctx):
+    s = torch.zeros((1, 20000), device="cuda")
+    out = torch.empty((1, 16385), dtype=torch.int32, device="cuda")
+    with pytest.raises(L.LwmError, match="at most 16384"):
+        L.lowest_k_device(ctx, s.data_ptr(), 1, 20000, 16385, out.data_ptr())
+
+
+def test_cem_beyond_sixteen_thousand_samples_matches_oracle(ctx):
+    # the reference has no sample limit (arg-sort fallback, src/planner.rs:1655-1658)
+    cfg = L.CemConfig(horizon=4, samples=40000, elites=64, action_dim=2, iterations=2, init_std=0.8, seed=8)
+    noise = normals(14, (2, 1, 40000, 4, 2))
+    target = [0.3, -0.2]
+    planner = L.CemPlanner(ctx, cfg)
+    r = planner.plan(L.CallbackScorer(ctx, 1, _quad(target)), injected_noise=noise)
+    ref = O.cem_plan(cfg, 1, lambda c: ((c - np.array(target, np.float32)) ** 2).sum(axis=(2, 3)), noise=noise)
+    assert_actions_close(r.sequence, ref["sequence"], 1e-5)
+    assert r.best_indices == ref["best"].tolist()
+    assert assert_same_elites(planner.elite_indices(), ref["elites"], ref["iteration_scores"], rel=1e-6) == 2
 
 
 def test_lowest_k_rejects_count_above_samples(ctx):
@@ -138,6 +174,7 @@ def test_icem_matches_oracle_with_colored_noise_and_carried_elites(ctx):
     assert_actions_close(r.sequence, ref["sequence"], 1e-5)
     assert r.best_indices == ref["best"].tolist()
     assert_actions_close(p.warm_start_sequence(), ref["warm"], 1e-5)
+    assert assert_same_elites(p.elite_indices(), ref["elites"], ref["iteration_scores"]) == 3
 
 
 def test_mppi_generic_matches_oracle(ctx):

@@ -6,7 +6,7 @@ import pytest
 
 import lewm_b200 as L
 import oracle as O
-from gpu_helpers import assert_actions_close, assert_costs_close, assert_same_argmin, normals
+from gpu_helpers import assert_actions_close, assert_costs_close, assert_same_argmin, assert_same_elites, normals
 from lewm_b200 import workloads as W
 
 torch = pytest.importorskip("torch")
@@ -83,8 +83,11 @@ def test_skyjepa_cem_elites_match_oracle(ctx):
     cfg = L.CemConfig(horizon=15, samples=128, elites=16, action_dim=4, iterations=2,
                       action_bounds=L.ActionBounds.scalar(4, 0.0, 2 * w.hover), init_std=0.5, seed=3)
     noise = normals(400, (2, 1, 128, 15, 4))
-    r = L.CemPlanner(ctx, cfg).plan(_scorer(ctx, w), injected_noise=noise)
+    planner = L.CemPlanner(ctx, cfg)
+    r = planner.plan(_scorer(ctx, w), injected_noise=noise)
     m, c = _oracle(w)
     ref = O.cem_plan(cfg, 1, (O.SKYJEPA_FN, c), noise=noise)
     assert_costs_close(r.scores, ref["scores"])
     assert_actions_close(r.sequence, ref["sequence"], 1e-4)
+    # the elite index set of every iteration (select_elites, src/planner.rs:1730-1754)
+    assert assert_same_elites(planner.elite_indices(), ref["elites"], ref["iteration_scores"]) == 2

@@ -1,20 +1,39 @@
 """Learned SkyJEPA MPPI on the tcgen05 tensor cores (bf16 weights and
-recurrent state, f32 accumulation) against the f32 oracle: per-candidate
-costs within 2e-2 relative (the bf16 predictor tolerance), the MPPI sequence
-close to the oracle's, and the tensor-core path actually taken (it launches
-four kernels per iteration: sampling, per-step inputs, h0 and the persistent rollout)."""
+recurrent-state copy, f32 accumulation and state) against the oracle.
+
+Three checks per plan:
+- per-candidate costs within 2e-2 relative of the f32 oracle (the contract's
+  bf16 predictor tolerance), and within TC_REL of the oracle run with the
+  kernel's own rounding (bf16 weights, combined GRU biases, bf16 encoder
+  outputs and GEMM copy of h: oracle `tensor_core_rounding`), which leaves
+  only the kernel's hardware tanh/sigmoid and summation order as differences;
+- the MPPI sequence equals the oracle's weighting of the same candidates by
+  the kernel's own scores within 1e-4 (the selection stage itself is exact:
+  only the cost tolerance reaches the action);
+- the best index is the argmin of the kernel's scores, and the oracle's up to
+  ties within the cost tolerance.
+
+The persistent kernel runs one CTA per SM over 128-candidate tiles, so the
+multi-tile tests use more tiles than three times the SM count: every CTA
+runs three or more tiles and crosses its barrier phases between tiles.  The
+path taken is shown by its launch count (sampling, per-step inputs, h0 and
+the persistent rollout)."""
 import numpy as np
 import pytest
 
 import lewm_b200 as L
 import oracle as O
-from gpu_helpers import normals
+from gpu_helpers import ACTION_ABS, normals
 from lewm_b200 import workloads as W
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 BF16_REL = 2e-2
+# against the oracle with the kernel's rounding: what is left is the hardware
+# tanh (MUFU.TANH, about 2^-11 relative) in the gates, the action encoder and
+# the prober, and the MMA's summation order
+TC_REL = 5e-3
 
 
 def _norm(w):
@@ -29,21 +48,38 @@ def _scorer(ctx, w, masses=None, precision="bf16"):
     return sc
 
 
-def _oracle_plan(w, noise, masses=None):
-    m = O.SkyJepaModel(w.model, w.weights)
+def _oracle_plan(w, noise, masses=None, rounding=False):
+    m = O.SkyJepaModel(w.model, w.weights, tensor_core_rounding=rounding)
     c = m.score_ctx(_norm(w), w.state_history, w.action_history, w.reference_states, w.reference_actions, w.cost,
                     w.dt, masses=masses)
     return O.mppi_plan(w.mppi, w.batch, (O.SKYJEPA_FN, c), noise=noise, warm_start=w.warm_start)
 
 
-def _check(r, ref):
-    s, rs = np.asarray(r.scores, np.float64), np.asarray(ref["scores"], np.float64)
-    rel = np.abs(s - rs) / np.maximum(np.abs(rs), 1e-6)
-    assert rel.max() <= BF16_REL, f"worst relative cost error {rel.max():.3e}"
-    # the weighted sequence: a convex combination of candidates whose weights
-    # carry the cost error; compare against the spread of the candidates
-    scale = np.abs(ref["sequence"]).max()
-    assert np.abs(np.asarray(r.sequence) - ref["sequence"]).max() <= 5e-2 * scale
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return np.abs(a - b) / np.maximum(np.abs(b), 1e-6)
+
+
+def _check(r, w, noise, masses=None, f32_oracle=True):
+    ref_q = _oracle_plan(w, noise, masses, rounding=True)
+    s = np.asarray(r.scores, np.float64)
+    rel_q = _rel(s, ref_q["scores"])
+    print(f"tensor-core vs rounding oracle: worst {rel_q.max():.3e}, p99 {np.quantile(rel_q, 0.99):.3e}")
+    assert rel_q.max() <= TC_REL, f"worst relative cost error vs the rounding oracle {rel_q.max():.3e}"
+    if f32_oracle:
+        ref = _oracle_plan(w, noise, masses)
+        rel = _rel(s, ref["scores"])
+        print(f"tensor-core vs f32 oracle: worst {rel.max():.3e}")
+        assert rel.max() <= BF16_REL, f"worst relative cost error vs the f32 oracle {rel.max():.3e}"
+    # the weighting of the (identical) candidates by the kernel's scores
+    seq = O.mppi_weighted(ref_q["candidates"], np.asarray(r.scores, np.float32), w.mppi.temperature)
+    assert np.abs(np.asarray(r.sequence) - seq).max() <= ACTION_ABS
+    best = np.asarray(r.best_indices)
+    assert best.tolist() == np.argmin(np.asarray(r.scores), axis=1).tolist()
+    for b, (i, j) in enumerate(zip(best, ref_q["best"])):
+        if i != j:
+            si, sj = ref_q["scores"][b][i], ref_q["scores"][b][j]
+            assert abs(si - sj) <= TC_REL * abs(sj), (b, i, j, si, sj)
 
 
 @pytest.mark.parametrize("batch, samples, horizon", [(1, 512, 15), (2, 256, 10)])
@@ -56,7 +92,7 @@ def test_tc_mppi_matches_oracle(ctx, batch, samples, horizon):
     n0 = ctx.launch_count()
     r = p.plan(sc, injected_noise=noise)
     assert ctx.launch_count() - n0 == 4, "the tensor-core path was not taken"
-    _check(r, _oracle_plan(w, noise))
+    _check(r, w, noise)
 
 
 def test_tc_fleet_with_masses_matches_oracle(ctx):
@@ -65,7 +101,33 @@ def test_tc_fleet_with_masses_matches_oracle(ctx):
     p = L.MppiPlanner(ctx, w.mppi)
     p.set_warm_start_sequence(w.warm_start)
     r = p.plan(_scorer(ctx, w, w.masses), injected_noise=noise)
-    _check(r, _oracle_plan(w, noise, w.masses))
+    _check(r, w, noise, w.masses)
+
+
+# more tiles than 3 x 148 SMs: every CTA runs 3 or 4 tiles (16 vehicles x 32
+# tiles, the fleet's shape: 4096 x 30 with per-vehicle masses), and an odd
+# horizon with 4 tiles per vehicle (the accumulator ring's phase parity flips
+# between tiles when 9 T + 1 is odd)
+@pytest.mark.parametrize("vehicles, samples, horizon", [(16, 4096, 30), (128, 512, 7)])
+def test_tc_persistent_multi_tile_matches_oracle(ctx, vehicles, samples, horizon):
+    w = W.fleet(seed=25, vehicles=vehicles, samples=samples, horizon=horizon)
+    tiles = vehicles * samples // 128
+    assert tiles >= 3 * 148
+    noise = normals(63, (1, vehicles, samples, horizon, 4))
+    p = L.MppiPlanner(ctx, w.mppi)
+    p.set_warm_start_sequence(w.warm_start)
+    sc = _scorer(ctx, w, w.masses)
+    n0 = ctx.launch_count()
+    r = p.plan(sc, injected_noise=noise)
+    assert ctx.launch_count() - n0 == 4, "the tensor-core path was not taken"
+    _check(r, w, noise, w.masses, f32_oracle=horizon < 30)
+    # a second plan on the same scorer and planner (warm-started): the
+    # persistent kernel's second launch starts from fresh barriers
+    noise2 = normals(64, (1, vehicles, samples, horizon, 4))
+    w.warm_start = p.warm_start_sequence()
+    r2 = p.plan(sc, injected_noise=noise2)
+    if horizon < 30:
+        _check(r2, w, noise2, w.masses, f32_oracle=False)
 
 
 def test_tc_seeded_plan_matches_f32_path(ctx):

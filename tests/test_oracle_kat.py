@@ -321,6 +321,25 @@ def test_gru_step_matches_pytorch_gate_convention():
         ref = gru(torch.from_numpy(x), torch.from_numpy(h)).numpy()
     assert np.abs(ours - ref).max() < 1e-5
 
+    # the tensor-core rounding model: the same cell fed bf16 weights, bf16
+    # x and a bf16 copy of h (f32 h in the update), one bf16 bias per r / z row
+    def bf(a):
+        return torch.from_numpy(np.asarray(a, np.float32)).to(torch.bfloat16).to(torch.float32)
+
+    mq = O.SkyJepaModel(cfg, w, tensor_core_rounding=True)
+    ours_q = mq.gru_step(x, h)
+    wi, wh = bf(w_ih), bf(w_hh)
+    xq, hq, hf = bf(x), bf(h), torch.from_numpy(h)
+    b_rz = bf(b_ih[:2 * H] + b_hh[:2 * H])
+    gi = xq @ wi.T
+    gh = hq @ wh.T
+    r = torch.sigmoid(gi[:, :H] + gh[:, :H] + b_rz[:H])
+    z = torch.sigmoid(gi[:, H:2 * H] + gh[:, H:2 * H] + b_rz[H:])
+    n = torch.tanh(gi[:, 2 * H:] + bf(b_ih[2 * H:]) + r * (gh[:, 2 * H:] + bf(b_hh[2 * H:])))
+    ref_q = (z * hf - (z - 1.0) * n).numpy()
+    assert np.abs(ours_q - ref_q).max() < 1e-5
+    assert np.abs(ours_q - ours).max() > 1e-4   # the rounding is actually applied
+
 
 # ---------------------------------------------------------------- task
 
