@@ -50,6 +50,9 @@ FLOP_PER_CANDIDATE_STEP["fleet"] = FLOP_PER_CANDIDATE_STEP["skyjepa"]
 ROLLOUT_DRAM_BYTES = {"skyjepa": 2178048 + 0}
 
 
+NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)
+
+
 def percentile(values, q):
     """values[round((n-1) q)] of the sorted list (lewm-bench-skyjepa.rs:547-553)."""
     v = sorted(values)
@@ -152,6 +155,8 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     if world > 1:
+        global NCCL_LOG
+        NCCL_LOG = nccl_log_setup()
         dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     ctx = L.Context(local_rank)
@@ -273,14 +278,165 @@ def run_ours(args, rank, world, local_rank):
                          "note": "achieved = algorithmic FLOP per plan / p50 plan time (both kernels)"},
             "clocks": clocks.summary(),
         }
-        if args.cpu_baseline:
+        if args.cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
+            result["cpu_baseline_1thread"] = cpu_baseline(kind, min(args.cpu_seconds, 10.0), threads=1)
     planner.close()
     sc.close()
+    if args.fleet_record and kind == "skyjepa":
+        fleet = fleet_collective_record(args, rank, world, local_rank, ctx)
+        if rank == 0:
+            result["fleet"] = fleet
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
     return result
+
+
+def nccl_log_setup():
+    """Route NCCL's communicator log (INIT lines: ranks, devices, NVLS) to a
+    per-process file, so stdout keeps the one JSON line; returns the path."""
+    import tempfile
+    if "NCCL_DEBUG" in os.environ:
+        return None
+    path = os.path.join(tempfile.gettempdir(), f"lewm_nccl_{os.getpid()}.log")
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ["NCCL_DEBUG_FILE"] = path
+    return path
+
+
+def nccl_log_lines(path, limit=6):
+    """The communicator lines of this rank's NCCL log (rank count, NVLS)."""
+    if not path or not os.path.exists(path):
+        return []
+    keep = []
+    with open(path, errors="replace") as f:
+        for line in f:
+            if "Init COMPLETE" in line or "nRanks" in line or "NVLS" in line:
+                keep.append(line.strip()[-200:])
+    return keep[:limit]
+
+
+def fleet_collective_record(args, rank, world, local_rank, ctx):
+    """The fleet across every rank by candidate shards: 256 vehicles x 4096
+    candidates x 30 steps, bf16 rollout on the tensor cores, each rank scoring
+    4096 / N candidates of every vehicle and reducing them to per-vehicle
+    MPPI tuples, one NCCL all-gather of the tuples per plan, then the combine
+    kernel.  Times are device times (CUDA events), max over ranks; `t1_ms` is
+    the whole fleet planned by one GPU in the same run (rank 0), the
+    reference for the per-N overhead; `exchange_ms` is the all-gather alone."""
+    import dataclasses
+    import torch
+    import torch.distributed as dist
+    import lewm_b200 as L
+    from lewm_b200 import fleet as F
+    from lewm_b200 import workloads as W
+
+    V, S, T = 256, 4096, 30
+    steps, warmup = max(5, min(args.steps, 20)), 3
+    parts = F.partition(V, S, world, "candidates")
+    group = F.new_groups(parts) if world > 1 else None
+    part = parts[rank]
+    full = W.fleet(seed=23, vehicles=V, samples=S, horizon=T)
+    stream = ctx.torch_stream()
+    sc = L.SkyJepaScorer(ctx, full.model, full.weights, full.state_mean, full.state_std, full.action_mean,
+                         full.action_std, full.cost, full.dt)
+    sc.set_precision("bf16")
+    sc.set_context(full.state_history, full.action_history, full.reference_states, full.reference_actions,
+                   vehicle_mass=full.masses)
+    fp = F.FleetPlanner(ctx, part, sc, full.mppi, group, time_exchange=True)
+    fp.planner.set_warm_start_sequence(full.warm_start)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def timed(fn, n):
+        out = []
+        for _ in range(n):
+            with torch.cuda.stream(stream):
+                flush.add_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            e.synchronize()
+            out.append(s.elapsed_time(e))
+        return out
+
+    for _ in range(warmup):
+        fp.plan_device()
+    ctx.synchronize()
+    fp.exchange_ms()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        times = timed(fp.plan_device, steps)
+    exch = fp.exchange_ms()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    # the whole fleet on one GPU (rank 0 only; the others wait at the barrier)
+    t1 = None
+    if rank == 0:
+        if world == 1:
+            t1 = times
+        else:
+            one = L.MppiPlanner(ctx, dataclasses.replace(full.mppi))
+            one.set_warm_start_sequence(full.warm_start)
+            for _ in range(warmup):
+                one.plan_device(sc)
+            ctx.synchronize()
+            t1 = timed(lambda: one.plan_device(sc), steps)
+            one.close()
+    if world > 1:
+        dist.barrier()
+    stats = torch.tensor([float(np.mean(times)), percentile(times, 0.5), percentile(times, 0.95),
+                          float(np.mean(exch)) if exch else 0.0], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    mean_ms, p50, p95, exch_ms = stats.tolist()
+    fp.close()
+    sc.close()
+    del flush
+    if rank != 0:
+        return None
+    t1_ms = float(np.mean(t1))
+    cand_steps = V * S * T
+    peaks = measured_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0)) * world
+    achieved = FLOP_PER_CANDIDATE_STEP["fleet"] * cand_steps / (mean_ms * 1e-3) / 1e12
+    overhead = mean_ms - t1_ms / world
+    limiter = ("none: the plan time is within 5 % of the one-GPU time / N" if overhead <= 0.05 * mean_ms else
+               "the all-gather of the per-vehicle tuples" if exch_ms >= 0.5 * overhead else
+               "per-plan work that does not shrink with N (the per-vehicle history encoder, the combine and "
+               "launch latency)")
+    return {
+        "workload": f"fleet SkyJEPA learned MPPI, {V} vehicles x {S} candidates x {T} steps, bf16 tcgen05 rollout, "
+                    "per-vehicle masses",
+        "parallelism": f"1 vehicle group x {world} candidate shards ({S // world} candidates of every vehicle "
+                       "per rank)",
+        "collective": "NCCL all_gather_into_tensor of per-vehicle MPPI tuples (min score, sum of weights, best key, "
+                      f"weighted action sums): {V} x {4 + T * 4} floats per rank per plan" if world > 1 else "none",
+        "n_gpus": world,
+        "steps": steps,
+        "ms_per_plan": round(mean_ms, 4),
+        "latency_ms": {"p50": round(p50, 4), "p95": round(p95, 4)},
+        "fleet_plans_per_s": round(1e3 / mean_ms, 3),
+        "candidate_steps_per_s": round(cand_steps * 1e3 / mean_ms, 1),
+        "t1_ms": round(t1_ms, 4),
+        "exchange_ms": round(exch_ms, 4),
+        "exchange_share": round(exch_ms / mean_ms, 4),
+        "overhead_ms_vs_t1_over_n": round(overhead, 4),
+        "limiter": limiter,
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_source": "MEASURED_PEAKS bf16_tflops_sustained (of measured) x n_gpus"},
+        "timing": "CUDA events on the planner's stream, L2 flushed between plans, max over ranks",
+        "nccl": {"version": ".".join(str(v) for v in torch.cuda.nccl.version()) if world > 1 else None,
+                 "log": nccl_log_lines(NCCL_LOG)},
+        "clocks": clocks.summary(),
+    }
 
 
 # ------------------------------------------------------------ fleet workload
@@ -1096,6 +1252,9 @@ def main():
     ap.add_argument("--media-format", choices=["nv12", "rgb", "rgba"], default="nv12",
                     help="media workload: NV12 planes or packed RGB / RGBA frames")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-fleet-record", dest="fleet_record", action="store_false",
+                    help="default workload: skip the fleet record (256 x 4096 x 30 by candidate shards over all "
+                         "ranks, one NCCL all-gather per plan) added to the JSON line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.precision is None:  # the precision each workload's configuration names

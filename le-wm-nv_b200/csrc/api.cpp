@@ -155,7 +155,7 @@ struct lwm_scorer {
     std::unique_ptr<lwm::LewmModel> lewm;
     // learned scorer on tensor cores (bf16): packed weights, per-vehicle h0, wait-timeout flag
     int32_t precision = LWM_PRECISION_F32;
-    DevBuf tc_packed, tc_h0, tc_err, tc_x;
+    DevBuf tc_packed, tc_h0, tc_err, tc_x, h0_work;
     bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
     DevBuf small_x;
     lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
@@ -473,6 +473,7 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint
         sc->tc_ready = true;
     }
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    LWM_TRY(sc->h0_work.ensure(lwm::skyjepa_h0_work_bytes(a, B)));
     LWM_TRY(sc->tc_x.ensure(lwm::skyjepa_tc_xtile_bytes(B, S, T)));
     return LWM_OK;
 }
@@ -488,6 +489,7 @@ lwm_status ensure_side(lwm_scorer* sc) {
 lwm_status ensure_small(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
     LWM_TRY(ensure_side(sc));
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    LWM_TRY(sc->h0_work.ensure(lwm::skyjepa_h0_work_bytes(a, B)));
     LWM_TRY(sc->small_x.ensure(std::max<size_t>(lwm::skyjepa_small_x_bytes(a, B, S, T), 4)));
     return LWM_OK;
 }
@@ -556,6 +558,7 @@ lwm_status score_device(lwm_scorer* sc, const float* cand, uint32_t B, uint32_t 
         int n = 0;
         if (sc->sky_small) {
             LWM_TRY(ensure_small(sc, a, B, S, a.T));
+            a.h0_work = sc->h0_work.as<float>();
             LWM_CUDA(lwm::launch_skyjepa_small(a, sc->tc_h0.as<float>(), sc->small_x.as<float>(), stream, &n,
                                                &sc->side));
         } else {
@@ -730,6 +733,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 const char* why = nullptr;
                 if (sc->sky_small) {
                     LWM_TRY(ensure_small(sc, a, B, p->S, p->T));
+                    a.h0_work = sc->h0_work.as<float>();
                     a.m.P = lwm::skyjepa_small_partials_per_vehicle(p->S);
                     a.low_dev = low;
                     a.high_dev = high;
@@ -737,6 +741,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                                                        &launched, &sc->side));
                 } else if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
                     LWM_TRY(ensure_tc(sc, a, B, p->S, p->T));
+                    a.h0_work = sc->h0_work.as<float>();
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
                     a.low_dev = low;
                     a.high_dev = high;
@@ -1560,6 +1565,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->weights.release();
     s->tc_packed.release();
     s->tc_h0.release();
+    s->h0_work.release();
     s->tc_err.release();
     s->tc_x.release();
     s->small_x.release();

@@ -331,10 +331,139 @@ __global__ void __launch_bounds__(256) skyjepa_h0_kernel(SkyjepaArgs a, float* h
     }
 }
 
+// Many vehicles: the encoder runs layer by layer over the whole fleet, a
+// thread per (vehicle, output channel) over all HS positions, activations in
+// global scratch laid out [channel][vehicle][position] so that a warp's 32
+// vehicles read one contiguous run per input channel (and share each weight:
+// a broadcast load).  Same (input channel, tap) summation order as
+// skyjepa_h0_kernel.  Launches: normalise, then per level conv1 and
+// conv2 + residual + block output, then the projection.
+template <int HS>
+__global__ void __launch_bounds__(256) h0_normalise_kernel(SkyjepaArgs a, float* x /*[18][B][HS]*/) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;  // (b, t, i) in the history's order
+    if (q >= a.B * HS * 18u) return;
+    const uint32_t i = q % 18u, bt = q / 18u;
+    x[static_cast<size_t>(i) * a.B * HS + bt] = (a.state_hist[q] - a.state_mean[i]) / a.state_std[i];
+}
+
+// conv == 1: out = gelu(conv1(in) + b1).  conv == 2: out = gelu(gelu(conv2(in)
+// + b2) + res), res = wr . res_in + br (1x1, width change) or res_in itself.
+template <int HS>
+__global__ void __launch_bounds__(256) h0_conv_kernel(const float* __restrict__ in, const float* __restrict__ W,
+                                                      const float* __restrict__ bias, uint32_t cin, uint32_t cout,
+                                                      uint32_t B, uint32_t dil, int conv,
+                                                      const float* __restrict__ res_in,
+                                                      const float* __restrict__ wr, const float* __restrict__ br,
+                                                      uint32_t cres, float* __restrict__ out) {
+    constexpr int K = 3;
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= cout * B) return;
+    const uint32_t o = q / B, b = q % B;
+    const size_t plane = static_cast<size_t>(B) * HS;
+    float acc[HS];
+#pragma unroll
+    for (int t = 0; t < HS; ++t) acc[t] = 0.0f;
+    const float* wo = W + static_cast<size_t>(o) * cin * K;
+    for (uint32_t i = 0; i < cin; ++i) {
+        const float* xi = in + i * plane + static_cast<size_t>(b) * HS;
+        float xv[HS];
+#pragma unroll
+        for (int t = 0; t < HS; ++t) xv[t] = xi[t];
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            const float wv = __ldg(wo + i * K + j);
+            const uint32_t shift = static_cast<uint32_t>(K - 1 - j) * dil;
+#pragma unroll
+            for (int t = 0; t < HS; ++t)
+                if (static_cast<uint32_t>(t) >= shift) acc[t] = fmaf(wv, xv[t - shift], acc[t]);
+        }
+    }
+    const float bo = __ldg(bias + o);
+    float* dst = out + o * plane + static_cast<size_t>(b) * HS;
+    if (conv == 1) {
+#pragma unroll
+        for (int t = 0; t < HS; ++t) dst[t] = gelu_tanh(acc[t] + bo);
+        return;
+    }
+    float res[HS];
+    if (wr) {
+#pragma unroll
+        for (int t = 0; t < HS; ++t) res[t] = 0.0f;
+        const float* wro = wr + static_cast<size_t>(o) * cres;
+        for (uint32_t i = 0; i < cres; ++i) {
+            const float wv = __ldg(wro + i);
+            const float* xi = res_in + i * plane + static_cast<size_t>(b) * HS;
+#pragma unroll
+            for (int t = 0; t < HS; ++t) res[t] = fmaf(wv, xi[t], res[t]);
+        }
+        const float bro = __ldg(br + o);
+#pragma unroll
+        for (int t = 0; t < HS; ++t) res[t] = res[t] + bro;
+    } else {
+        const float* xo = res_in + o * plane + static_cast<size_t>(b) * HS;
+#pragma unroll
+        for (int t = 0; t < HS; ++t) res[t] = xo[t];
+    }
+#pragma unroll
+    for (int t = 0; t < HS; ++t) dst[t] = gelu_tanh(gelu_tanh(acc[t] + bo) + res[t]);
+}
+
+// state_projection of the last position: a thread per (vehicle, latent unit).
+template <int HS>
+__global__ void __launch_bounds__(256) h0_project_kernel(SkyjepaArgs a, const float* __restrict__ cur, float* h0) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= a.H * a.B) return;
+    const uint32_t u = q / a.B, b = q % a.B;
+    const size_t plane = static_cast<size_t>(a.B) * HS;
+    const float* wu = a.proj_w + static_cast<size_t>(u) * a.state_tcn.out_dim;
+    float acc = 0.0f;
+    for (uint32_t c = 0; c < a.state_tcn.out_dim; ++c)
+        acc = fmaf(__ldg(wu + c), cur[c * plane + static_cast<size_t>(b) * HS + HS - 1], acc);
+    h0[static_cast<size_t>(b) * a.H + u] = acc + a.proj_b[u];
+}
+
+constexpr uint32_t kH0BatchedMinVehicles = 32, kH0BatchedHist = 10;
+
+size_t skyjepa_h0_work_bytes(const SkyjepaArgs& a, uint32_t B) {
+    const uint32_t C = a.state_tcn.max_ch > 18u ? a.state_tcn.max_ch : 18u;
+    return 3 * static_cast<size_t>(C) * B * kH0BatchedHist * sizeof(float);
+}
+
+namespace {
+
+cudaError_t launch_h0_batched(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
+    constexpr int HS = static_cast<int>(kH0BatchedHist);
+    const uint32_t B = a.B, C = a.state_tcn.max_ch > 18u ? a.state_tcn.max_ch : 18u;
+    const size_t buf = static_cast<size_t>(C) * B * HS;
+    float* cur = a.h0_work;
+    float* h1 = cur + buf;
+    float* nxt = h1 + buf;
+    const uint32_t n_in = B * HS * 18u;
+    h0_normalise_kernel<HS><<<(n_in + 255) / 256, 256, 0, stream>>>(a, cur);
+    for (uint32_t l = 0; l < a.state_tcn.levels; ++l) {
+        const TcnBlockView& bk = a.state_tcn.blocks[l];
+        const uint32_t n = bk.out * B;
+        h0_conv_kernel<HS><<<(n + 255) / 256, 256, 0, stream>>>(cur, bk.w1, bk.b1, bk.in, bk.out, B, bk.dil, 1,
+                                                                 nullptr, nullptr, nullptr, 0, h1);
+        h0_conv_kernel<HS><<<(n + 255) / 256, 256, 0, stream>>>(h1, bk.w2, bk.b2, bk.out, bk.out, B, bk.dil, 2, cur,
+                                                                 bk.wr, bk.br, bk.in, nxt);
+        float* t = cur;
+        cur = nxt;
+        nxt = t;
+    }
+    const uint32_t n = a.H * B;
+    h0_project_kernel<HS><<<(n + 255) / 256, 256, 0, stream>>>(a, cur, h0);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 // h0 of every vehicle: state_projection(TemporalConvEncoder(normalised state
 // history))[last position] (SkyJepaModel::encode_history, model.rs:52-66).
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
     if (a.Hs > kH0MaxHist) return cudaErrorInvalidValue;
+    if (a.h0_work && a.B >= kH0BatchedMinVehicles && a.Hs == kH0BatchedHist && a.state_tcn.k == 3)
+        return launch_h0_batched(a, h0, stream);
     const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
     if (a.state_tcn.max_ch >= 64)
         skyjepa_h0_warp_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);

@@ -162,6 +162,7 @@ struct SkyjepaArgs {
     int mppi;
     MppiArgs m;
     const float* action_tcn_host;  // host copy of the action encoder's weights (kernel-parameter packing), or nullptr
+    float* h0_work;                // scratch of the batched history encoder (skyjepa_h0_work_bytes), or nullptr
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
@@ -181,6 +182,9 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
 size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
 // Initial latent of every vehicle (state encoder + projection) into h0 [B, H].
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
+// Scratch for the history encoder run over many vehicles at once (used when
+// SkyjepaArgs::h0_work is set, B >= 32 and the history has 10 steps).
+size_t skyjepa_h0_work_bytes(const SkyjepaArgs& a, uint32_t B);
 // Small-latent (<= 64) learned path: a warp per candidate (sampling, action
 // encoder inputs x [B,S,T,E], h0, rollout + cost + MPPI partials).
 bool skyjepa_small_supported(const SkyjepaArgs& a, const char** why);

@@ -117,13 +117,17 @@ class FleetPlanner:
     """One rank's share of a fleet: a learned (SkyJEPA) or nominal scorer over
     its vehicle range and an MPPI planner over its candidate range."""
 
-    def __init__(self, ctx, part: FleetPart, scorer, mppi_config, group=None):
+    def __init__(self, ctx, part: FleetPart, scorer, mppi_config, group=None, time_exchange: bool = False):
+        """`time_exchange`: record CUDA events around every tuple exchange on
+        the context's stream (exchange_ms() reads them back)."""
         import torch
         from . import MppiPlanner
         self.ctx = ctx
         self.part = part
         self.scorer = scorer
         self.group = group
+        self.time_exchange = time_exchange
+        self._events = []
         s0, s1 = part.samples
         self.planner = MppiPlanner(ctx, dataclasses.replace(mppi_config, samples=s1 - s0))
         self.sharded = part.candidate_shards > 1
@@ -145,9 +149,26 @@ class FleetPlanner:
         if self._gathered is None or self._gathered.shape != (self.part.candidate_shards, B, width):
             self._gathered = torch.empty((self.part.candidate_shards, B, width), dtype=torch.float32,
                                          device=local.device)
-        with torch.cuda.stream(self.ctx.torch_stream()):
+        stream = self.ctx.torch_stream()
+        with torch.cuda.stream(stream):
+            if self.time_exchange:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record(stream)
             exchange_tuples(local, self.group, self.part.candidate_shards, out=self._gathered)
+            if self.time_exchange:
+                ev[1].record(stream)
+                self._events.append(ev)
         return self.planner.combine_device(self._gathered.data_ptr(), self.part.candidate_shards)
+
+    def exchange_ms(self, clear: bool = True):
+        """Device time of every timed tuple exchange since the last call (ms)."""
+        out = []
+        for s, e in self._events:
+            e.synchronize()
+            out.append(s.elapsed_time(e))
+        if clear:
+            self._events = []
+        return out
 
     def close(self) -> None:
         self.planner.close()

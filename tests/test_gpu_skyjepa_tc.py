@@ -32,8 +32,9 @@ pytestmark = pytest.mark.gpu
 BF16_REL = 2e-2
 # against the oracle with the kernel's rounding: what is left is the hardware
 # tanh (MUFU.TANH, about 2^-11 relative) in the gates, the action encoder and
-# the prober, and the MMA's summation order
-TC_REL = 5e-3
+# the prober, and the MMA's summation order (measured on a B200: worst
+# 1.2e-5 over these tests; the bound keeps a 10x margin)
+TC_REL = 1e-4
 
 
 def _norm(w):
