@@ -680,7 +680,6 @@ def run_lewm(args, rank, world, local_rank):
         host_uv = torch.from_numpy(np.concatenate([w.uv_plane, w.goal_uv])).pin_memory()
         dev_y = torch.empty(host_y.shape, dtype=torch.uint8, device="cuda")
         dev_uv = torch.empty(host_uv.shape, dtype=torch.uint8, device="cuda")
-        pix = torch.empty((2, 3, s_img, s_img), device="cuda")
         h2d = host_y.numel() + host_uv.numel()
     else:
         host_obs = torch.from_numpy(np.concatenate([w.obs, w.goal_obs])).pin_memory()
@@ -700,8 +699,8 @@ def run_lewm(args, rank, world, local_rank):
                 if upload:
                     dev_y.copy_(host_y, non_blocking=True)
                     dev_uv.copy_(host_uv, non_blocking=True)
-                L.preprocess_nv12_device(ctx, dev_y, dev_uv, 2, s_img, s_img, "bt601-video", prep, pix)
-                emb = sc.encode_pixels(pix)
+                # NV12 preprocessing written straight into the ViT's patch matrix
+                emb = sc.encode_nv12(dev_y, dev_uv, 2, s_img, s_img, "bt601-video", prep)
             else:
                 if upload:
                     dev_obs.copy_(host_obs, non_blocking=True)
@@ -789,7 +788,7 @@ def run_lewm(args, rank, world, local_rank):
     # that stream still exists (the host allocator records events on it)
     ctx.synchronize()
     if image:
-        del host_y, host_uv, dev_y, dev_uv, pix
+        del host_y, host_uv, dev_y, dev_uv
     else:
         del host_obs, dev_obs
     del seq, r

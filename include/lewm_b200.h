@@ -647,6 +647,33 @@ lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, cons
                                       uint32_t batch, uint32_t height, uint32_t width, int32_t color_space,
                                       const lwm_image_preprocess* cfg, uint32_t history_len,
                                       uint32_t history_slot, int32_t out_bf16, void* output);
+/* The same preprocessing written as the ViT patch-embedding input instead of
+ * an NCHW image: output [B, (oh/p)(ow/p), 3 p p] where element (b, c, y, x)
+ * of the normalised image sits at patch (y/p) (ow/p) + x/p, column
+ * c p p + (y%p) p + x%p — the layout Embeddings' stride-p convolution reads
+ * (src/models/lewm/vit.rs:32-52, fed by src/media/mod.rs:1113-1333).  The
+ * values equal the NCHW call's, permuted; `patch` must divide oh and ow (the
+ * row-staged kernels take patch sizes that are multiples of 4). */
+lwm_status lwm_preprocess_packed_patches_device(lwm_ctx* ctx, const uint8_t* input, uint32_t batch,
+                                                uint32_t height, uint32_t width, int32_t format,
+                                                const lwm_image_preprocess* cfg, uint32_t patch,
+                                                int32_t out_bf16, void* output);
+lwm_status lwm_preprocess_nv12_patches_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane,
+                                              uint32_t batch, uint32_t height, uint32_t width,
+                                              int32_t color_space, const lwm_image_preprocess* cfg,
+                                              uint32_t patch, int32_t out_bf16, void* output);
+/* LeWm::encode_pixels (src/models/lewm/model.rs:41-55) of device NV12 /
+ * packed frames with the preprocessing fused into the encoder's input: the
+ * frames are preprocessed (as above, f32) straight into the encoder's patch
+ * matrix, then the ViT and projector run from it — no NCHW image and no
+ * patchify pass.  cfg's output size must be the encoder's image size; out
+ * [n, D] device embeddings. */
+lwm_status lwm_lewm_encode_nv12_device(lwm_scorer* scorer, const uint8_t* y_plane, const uint8_t* uv_plane,
+                                       uint32_t n, uint32_t height, uint32_t width, int32_t color_space,
+                                       const lwm_image_preprocess* cfg, float* out);
+lwm_status lwm_lewm_encode_packed_device(lwm_scorer* scorer, const uint8_t* input, uint32_t n, uint32_t height,
+                                         uint32_t width, int32_t format, const lwm_image_preprocess* cfg,
+                                         float* out);
 
 /* ---------------------------------------------------------------- allocation-free iteration */
 

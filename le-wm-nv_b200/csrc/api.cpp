@@ -1829,9 +1829,15 @@ static lwm::MediaArgs media_args(const lwm_image_preprocess* cfg, uint32_t B, ui
     return a;
 }
 
-lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uint32_t H, uint32_t W,
-                                        int32_t format, const lwm_image_preprocess* cfg, uint32_t history_len,
-                                        uint32_t slot, int32_t out_bf16, void* output) {
+}  // extern "C"
+
+namespace {
+
+// Argument checks and the launch of packed / NV12 preprocessing into any
+// output layout (`patch` > 0: the ViT patch matrix).
+lwm_status preprocess_packed(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uint32_t H, uint32_t W, int32_t format,
+                             const lwm_image_preprocess* cfg, uint32_t history_len, uint32_t slot, uint32_t patch,
+                             int32_t out_bf16, void* output) {
     if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (format < 0 || format > 3)
         return fail(LWM_INVALID_ARGUMENT, "unknown packed image format " + std::to_string(format) +
@@ -1844,6 +1850,7 @@ lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint
     a.a = input;
     a.channels = format >= 2 ? 4 : 3;
     a.format = static_cast<uint32_t>(format);
+    a.patch = patch;
     if (lwm::packed_staged_eligible(a)) {
         LWM_TRY(ensure_media_err(ctx));
         LWM_CUDA(lwm::launch_packed_staged(a, ctx->media_err_dev, ctx->stream));
@@ -1854,9 +1861,9 @@ lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint
     return LWM_OK;
 }
 
-lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B,
-                                      uint32_t H, uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg,
-                                      uint32_t history_len, uint32_t slot, int32_t out_bf16, void* output) {
+lwm_status preprocess_nv12(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B, uint32_t H,
+                           uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg, uint32_t history_len,
+                           uint32_t slot, uint32_t patch, int32_t out_bf16, void* output) {
     if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (color_space < 0 || color_space > 3)
         return fail(LWM_INVALID_ARGUMENT, "unknown NV12 color space " + std::to_string(color_space) +
@@ -1873,6 +1880,7 @@ lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, cons
     a.uv = uv_plane;
     a.channels = 1;
     a.format = static_cast<uint32_t>(color_space);
+    a.patch = patch;
     if (lwm::nv12_staged_eligible(a)) {
         LWM_TRY(ensure_media_err(ctx));
         LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, ctx->stream));
@@ -1880,6 +1888,88 @@ lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, cons
         LWM_CUDA(lwm::launch_media(a, true, ctx->stream));
     }
     ctx->launches += 1;
+    return LWM_OK;
+}
+
+lwm_status check_patch(const lwm_image_preprocess* cfg, uint32_t patch) {
+    if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (patch == 0 || cfg->output_height % patch != 0 || cfg->output_width % patch != 0)
+        return fail(LWM_INVALID_ARGUMENT, "patch size " + std::to_string(patch) + " must divide the output size " +
+                                              std::to_string(cfg->output_height) + "x" +
+                                              std::to_string(cfg->output_width));
+    return LWM_OK;
+}
+
+// The image encoder's patch size and frame size must be the output's.
+lwm_status check_vit_frames(lwm_scorer* s, const lwm_image_preprocess* cfg, uint32_t n, float* out) {
+    if (!s || s->kind != ScorerKind::Lewm || !cfg || !out || n == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid encode arguments");
+    const lwm_lewm_config& c = s->lewm->c;
+    if (c.encoder != LWM_ENCODER_VIT) return fail(LWM_INVALID_ARGUMENT, "encode_pixels called on non-image observation encoder");
+    if (c.channels != 3) return fail(LWM_INVALID_ARGUMENT, "frame encoding needs a 3-channel image encoder");
+    if (cfg->output_height != c.image_size || cfg->output_width != c.image_size)
+        return fail(LWM_INVALID_ARGUMENT, "preprocess output " + std::to_string(cfg->output_height) + "x" +
+                                              std::to_string(cfg->output_width) + " does not match the encoder's image size " +
+                                              std::to_string(c.image_size));
+    return LWM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+lwm_status lwm_preprocess_packed_device(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uint32_t H, uint32_t W,
+                                        int32_t format, const lwm_image_preprocess* cfg, uint32_t history_len,
+                                        uint32_t slot, int32_t out_bf16, void* output) {
+    return preprocess_packed(ctx, input, B, H, W, format, cfg, history_len, slot, 0, out_bf16, output);
+}
+
+lwm_status lwm_preprocess_nv12_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B,
+                                      uint32_t H, uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg,
+                                      uint32_t history_len, uint32_t slot, int32_t out_bf16, void* output) {
+    return preprocess_nv12(ctx, y_plane, uv_plane, B, H, W, color_space, cfg, history_len, slot, 0, out_bf16, output);
+}
+
+lwm_status lwm_preprocess_packed_patches_device(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uint32_t H, uint32_t W,
+                                                int32_t format, const lwm_image_preprocess* cfg, uint32_t patch,
+                                                int32_t out_bf16, void* output) {
+    LWM_TRY(check_patch(cfg, patch));
+    return preprocess_packed(ctx, input, B, H, W, format, cfg, 0, 0, patch, out_bf16, output);
+}
+
+lwm_status lwm_preprocess_nv12_patches_device(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane,
+                                              uint32_t B, uint32_t H, uint32_t W, int32_t color_space,
+                                              const lwm_image_preprocess* cfg, uint32_t patch, int32_t out_bf16,
+                                              void* output) {
+    LWM_TRY(check_patch(cfg, patch));
+    return preprocess_nv12(ctx, y_plane, uv_plane, B, H, W, color_space, cfg, 0, 0, patch, out_bf16, output);
+}
+
+lwm_status lwm_lewm_encode_nv12_device(lwm_scorer* s, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t n,
+                                       uint32_t H, uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg,
+                                       float* out) {
+    LWM_TRY(check_vit_frames(s, cfg, n, out));
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    float* patches = nullptr;
+    LWM_CUDA(s->lewm->patch_buffer(n, &patches));
+    LWM_TRY(preprocess_nv12(s->ctx, y_plane, uv_plane, n, H, W, color_space, cfg, 0, 0, s->lewm->c.patch_size, 0,
+                            patches));
+    LWM_CUDA(s->lewm->encode_patches(n, out, s->ctx->stream));
+    s->ctx->launches += static_cast<uint64_t>(s->lewm->launches);
+    return LWM_OK;
+}
+
+lwm_status lwm_lewm_encode_packed_device(lwm_scorer* s, const uint8_t* input, uint32_t n, uint32_t H, uint32_t W,
+                                         int32_t format, const lwm_image_preprocess* cfg, float* out) {
+    LWM_TRY(check_vit_frames(s, cfg, n, out));
+    std::lock_guard<std::mutex> lock(s->mu);
+    LWM_CUDA(cudaSetDevice(s->ctx->device));
+    float* patches = nullptr;
+    LWM_CUDA(s->lewm->patch_buffer(n, &patches));
+    LWM_TRY(preprocess_packed(s->ctx, input, n, H, W, format, cfg, 0, 0, s->lewm->c.patch_size, 0, patches));
+    LWM_CUDA(s->lewm->encode_patches(n, out, s->ctx->stream));
+    s->ctx->launches += static_cast<uint64_t>(s->lewm->launches);
     return LWM_OK;
 }
 

@@ -7,8 +7,11 @@
 // (src/media/mod.rs:1113-1194, 1196-1333).  Here one thread produces all
 // three channels of an output pixel (the reference's packed kernel runs one
 // thread per output element and repeats the coordinate math and the four
-// taps per channel), so every source byte is read once per pixel.  Compiled
-// with -fmad=false: every product and sum is rounded on its own.
+// taps per channel), so every source byte is read once per pixel; the
+// row-staged kernels go further (below).  The output can also be the ViT's
+// patch matrix, so the patch-embedding GEMM reads the preprocessed frames
+// directly.  Compiled with -fmad=false: every product and sum is rounded on
+// its own.
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -24,91 +27,146 @@ namespace lwm {
 
 __device__ __forceinline__ float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
 
-// Bilinear tap of channel `ch` of an interleaved plane; coordinates clamped
-// to the plane (swm_sample_plane, src/media/mod.rs:1201-1230).
-__device__ __forceinline__ float sample_plane(const uint8_t* plane, uint32_t b, uint32_t h, uint32_t w, uint32_t channels,
-                                              uint32_t ch, float sy, float sx) {
-    sy = clampf(sy, 0.0f, static_cast<float>(h - 1u));
-    sx = clampf(sx, 0.0f, static_cast<float>(w - 1u));
-    const uint32_t y0 = static_cast<uint32_t>(floorf(sy)), x0 = static_cast<uint32_t>(floorf(sx));
-    const uint32_t y1 = y0 + 1u < h ? y0 + 1u : y0, x1 = x0 + 1u < w ? x0 + 1u : x0;
-    const float wy = sy - static_cast<float>(y0), wx = sx - static_cast<float>(x0);
-    const size_t row0 = (static_cast<size_t>(b) * h + y0) * w, row1 = (static_cast<size_t>(b) * h + y1) * w;
-    const float v00 = __ldg(plane + (row0 + x0) * channels + ch), v01 = __ldg(plane + (row0 + x1) * channels + ch);
-    const float v10 = __ldg(plane + (row1 + x0) * channels + ch), v11 = __ldg(plane + (row1 + x1) * channels + ch);
+// ------------------------------------------------------------ output maps
+//
+// Where element (frame b, channel c, row y, column x) of the normalised
+// image goes: NCHW (or one slot of an [B, history, 3, H, W] buffer), or —
+// with a.patch = p > 0 — the ViT's patch matrix [B, (H/p)(W/p), 3 p p]
+// (the patch-embedding convolution's input, vit.rs:32-52), at patch
+// (y / p, x / p), column c p p + (y % p) p + x % p.  An offset is
+// row_base(b, y) + col(x) + c * plane; four columns 4j .. 4j+3 are
+// contiguous in both layouts (p a multiple of 4).
+__device__ __forceinline__ size_t out_row_base(const MediaArgs& a, uint32_t b, uint32_t y) {
+    if (a.patch) {
+        const uint32_t p = a.patch, side = a.out_w / p;
+        return (static_cast<size_t>(b) * (a.out_h / p) * side + static_cast<size_t>(y / p) * side) * (3u * p * p) +
+               static_cast<size_t>(y % p) * p;
+    }
+    const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
+    return ((static_cast<size_t>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w;
+}
+__device__ __forceinline__ size_t out_col(const MediaArgs& a, uint32_t x) {
+    return a.patch ? static_cast<size_t>(x / a.patch) * (3u * a.patch * a.patch) + x % a.patch : x;
+}
+__device__ __forceinline__ size_t out_plane(const MediaArgs& a) {
+    return a.patch ? static_cast<size_t>(a.patch) * a.patch : static_cast<size_t>(a.out_h) * a.out_w;
+}
+
+// ------------------------------------------------------ per-pixel kernels
+//
+// For the shapes the row-staged kernels below do not take.  One thread per
+// output pixel makes all three channels: the source coordinates and the
+// bilinear neighbours are found once per axis, the taps of every channel
+// come from the same neighbours, the result is normalised and stored.
+
+// One resampling axis: the neighbours of a source coordinate clamped to
+// [0, n - 1] and the weight of the upper one.
+struct Axis {
+    uint32_t i0, i1;
+    float w;
+};
+__device__ __forceinline__ Axis axis_of(float s, uint32_t n) {
+    s = clampf(s, 0.0f, static_cast<float>(n - 1u));
+    const float f = floorf(s);
+    const uint32_t i0 = static_cast<uint32_t>(f);
+    return {i0, i0 + 1u < n ? i0 + 1u : i0, s - f};
+}
+
+// Four taps blended along x within each row, then along y (the order the
+// reference rounds in: swm_sample_plane, src/media/mod.rs:1201-1230).
+__device__ __forceinline__ float blend(float v00, float v01, float v10, float v11, float wx, float wy) {
     const float top = v00 + (v01 - v00) * wx;
     const float bottom = v10 + (v11 - v10) * wx;
     return top + (bottom - top) * wy;
 }
 
-__device__ __forceinline__ void store3(const MediaArgs& a, uint32_t b, uint32_t y, uint32_t x, const float (&v)[3]) {
+__device__ __forceinline__ void store_pixel(const MediaArgs& a, uint32_t b, uint32_t y, uint32_t x,
+                                            const float (&v)[3]) {
+    const size_t base = out_row_base(a, b, y) + out_col(a, x), plane = out_plane(a);
+#pragma unroll
     for (uint32_t c = 0; c < 3; ++c) {
         const float normalized = (v[c] - a.mean[c]) / a.std[c];
-        size_t idx;
-        if (a.history_len == 0)
-            idx = ((static_cast<size_t>(b) * 3 + c) * a.out_h + y) * a.out_w + x;
-        else
-            idx = (((static_cast<size_t>(b) * a.history_len + a.history_slot) * 3 + c) * a.out_h + y) * a.out_w + x;
-        if (a.bf16) static_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(normalized);
-        else static_cast<float*>(a.out)[idx] = normalized;
+        if (a.bf16) static_cast<__nv_bfloat16*>(a.out)[base + c * plane] = __float2bfloat16_rn(normalized);
+        else static_cast<float*>(a.out)[base + c * plane] = normalized;
     }
 }
 
-__global__ void __launch_bounds__(256) packed_to_nchw_kernel(MediaArgs a) {
-    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const uint64_t pixels = static_cast<uint64_t>(a.batch) * a.out_h * a.out_w;
-    if (idx >= pixels) return;
-    const uint32_t x = static_cast<uint32_t>(idx % a.out_w);
-    const uint64_t tmp = idx / a.out_w;
-    const uint32_t y = static_cast<uint32_t>(tmp % a.out_h), b = static_cast<uint32_t>(tmp / a.out_h);
-    // swm_packed_u8_to_nchw_f32: half-pixel source coordinate, clamped below at 0
-    float sy = (static_cast<float>(y) + 0.5f) * (static_cast<float>(a.in_h) / static_cast<float>(a.out_h)) - 0.5f;
-    float sx = (static_cast<float>(x) + 0.5f) * (static_cast<float>(a.in_w) / static_cast<float>(a.out_w)) - 0.5f;
-    if (sy < 0.0f) sy = 0.0f;
-    if (sx < 0.0f) sx = 0.0f;
-    const bool swap = a.format == 1u || a.format == 3u;
-    float v[3];
-    for (uint32_t c = 0; c < 3; ++c)
-        v[c] = sample_plane(a.a, b, a.in_h, a.in_w, a.channels, swap ? 2u - c : c, sy, sx) * 0.00392156862745098f;
-    store3(a, b, y, x, v);
+// (b, y, x) of output pixel `idx`.
+__device__ __forceinline__ void pixel_of(const MediaArgs& a, uint64_t idx, uint32_t& b, uint32_t& y, uint32_t& x) {
+    x = static_cast<uint32_t>(idx % a.out_w);
+    const uint64_t q = idx / a.out_w;
+    y = static_cast<uint32_t>(q % a.out_h);
+    b = static_cast<uint32_t>(q / a.out_h);
 }
 
-__global__ void __launch_bounds__(256) nv12_to_nchw_kernel(MediaArgs a) {
+// Packed RGB / BGR / RGBA / BGRA (swm_packed_u8_to_nchw_f32, src/media/
+// mod.rs:1113-1194): half-pixel source coordinates clamped below at 0.
+__global__ void __launch_bounds__(256) packed_pixel_kernel(MediaArgs a) {
     const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const uint64_t pixels = static_cast<uint64_t>(a.batch) * a.out_h * a.out_w;
-    if (idx >= pixels) return;
-    const uint32_t x = static_cast<uint32_t>(idx % a.out_w);
-    const uint64_t tmp = idx / a.out_w;
-    const uint32_t y = static_cast<uint32_t>(tmp % a.out_h), b = static_cast<uint32_t>(tmp / a.out_h);
+    if (idx >= static_cast<uint64_t>(a.batch) * a.out_h * a.out_w) return;
+    uint32_t b, y, x;
+    pixel_of(a, idx, b, y, x);
+    const Axis ay = axis_of(fmaxf((static_cast<float>(y) + 0.5f) * (static_cast<float>(a.in_h) / static_cast<float>(a.out_h)) - 0.5f, 0.0f), a.in_h);
+    const Axis ax = axis_of(fmaxf((static_cast<float>(x) + 0.5f) * (static_cast<float>(a.in_w) / static_cast<float>(a.out_w)) - 0.5f, 0.0f), a.in_w);
+    const uint32_t C = a.channels;
+    const uint8_t* r0 = a.a + (static_cast<size_t>(b) * a.in_h + ay.i0) * a.in_w * C;
+    const uint8_t* r1 = a.a + (static_cast<size_t>(b) * a.in_h + ay.i1) * a.in_w * C;
+    const bool swap = a.format == 1u || a.format == 3u;  // BGR, BGRA
+    float v[3];
+#pragma unroll
+    for (uint32_t c = 0; c < 3; ++c) {
+        const uint32_t k = swap ? 2u - c : c;
+        v[c] = blend(__ldg(r0 + ax.i0 * C + k), __ldg(r0 + ax.i1 * C + k), __ldg(r1 + ax.i0 * C + k),
+                     __ldg(r1 + ax.i1 * C + k), ax.w, ay.w) * 0.00392156862745098f;
+    }
+    store_pixel(a, b, y, x, v);
+}
+
+// YUV -> RGB of the four NV12 colour spaces (src/media/mod.rs:1298-1318):
+// limited range scales (Y - 16)+ by 255/219 first; then R = Y + rv V,
+// G = Y - gu U - gv V, B = Y + bu U.
+struct ColourSpace {
+    int limited;
+    float rv, gu, gv, bu;
+};
+__constant__ ColourSpace kColourSpaces[4] = {
+    {1, 1.59602678f, 0.39176229f, 0.81296765f, 2.01723214f},  // BT.601, video range
+    {1, 1.79274107f, 0.21324861f, 0.53290933f, 2.11240179f},  // BT.709, video range
+    {0, 1.402f, 0.344136f, 0.714136f, 1.772f},                 // BT.601, full range
+    {0, 1.5748f, 0.187324f, 0.468124f, 1.8556f},               // BT.709, full range
+};
+
+// NV12 (swm_nv12_to_nchw_f32, src/media/mod.rs:1232-1333): luma at the
+// half-pixel source coordinate, chroma at half of it on the half-size
+// interleaved UV plane, both clamped to their planes.
+__global__ void __launch_bounds__(256) nv12_pixel_kernel(MediaArgs a) {
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(a.batch) * a.out_h * a.out_w) return;
+    uint32_t b, y, x;
+    pixel_of(a, idx, b, y, x);
     const float sy = (static_cast<float>(y) + 0.5f) * (static_cast<float>(a.in_h) / static_cast<float>(a.out_h)) - 0.5f;
     const float sx = (static_cast<float>(x) + 0.5f) * (static_cast<float>(a.in_w) / static_cast<float>(a.out_w)) - 0.5f;
-    const float yv = sample_plane(a.a, b, a.in_h, a.in_w, 1u, 0u, sy, sx);
-    const float u = sample_plane(a.uv, b, a.in_h / 2u, a.in_w / 2u, 2u, 0u, sy * 0.5f, sx * 0.5f) - 128.0f;
-    const float vv = sample_plane(a.uv, b, a.in_h / 2u, a.in_w / 2u, 2u, 1u, sy * 0.5f, sx * 0.5f) - 128.0f;
-    float r, g, bl;
-    // colour matrices of src/media/mod.rs:1298-1318
-    if (a.format == 0u) {
-        const float yy = fmaxf(yv - 16.0f, 0.0f) * 1.16438356f;
-        r = yy + 1.59602678f * vv;
-        g = yy - 0.39176229f * u - 0.81296765f * vv;
-        bl = yy + 2.01723214f * u;
-    } else if (a.format == 1u) {
-        const float yy = fmaxf(yv - 16.0f, 0.0f) * 1.16438356f;
-        r = yy + 1.79274107f * vv;
-        g = yy - 0.21324861f * u - 0.53290933f * vv;
-        bl = yy + 2.11240179f * u;
-    } else if (a.format == 2u) {
-        r = yv + 1.402f * vv;
-        g = yv - 0.344136f * u - 0.714136f * vv;
-        bl = yv + 1.772f * u;
-    } else {
-        r = yv + 1.5748f * vv;
-        g = yv - 0.187324f * u - 0.468124f * vv;
-        bl = yv + 1.8556f * u;
-    }
+    const Axis ly = axis_of(sy, a.in_h), lx = axis_of(sx, a.in_w);
+    const uint32_t ch = a.in_h / 2u, cw = a.in_w / 2u;
+    const Axis cy = axis_of(sy * 0.5f, ch), cx = axis_of(sx * 0.5f, cw);
+    const uint8_t* l0 = a.a + (static_cast<size_t>(b) * a.in_h + ly.i0) * a.in_w;
+    const uint8_t* l1 = a.a + (static_cast<size_t>(b) * a.in_h + ly.i1) * a.in_w;
+    const float Y = blend(__ldg(l0 + lx.i0), __ldg(l0 + lx.i1), __ldg(l1 + lx.i0), __ldg(l1 + lx.i1), lx.w, ly.w);
+    const uint8_t* c0 = a.uv + (static_cast<size_t>(b) * ch + cy.i0) * cw * 2u;
+    const uint8_t* c1 = a.uv + (static_cast<size_t>(b) * ch + cy.i1) * cw * 2u;
+    float uvv[2];
+#pragma unroll
+    for (uint32_t k = 0; k < 2; ++k)  // U at even bytes, V at odd bytes
+        uvv[k] = blend(__ldg(c0 + 2u * cx.i0 + k), __ldg(c0 + 2u * cx.i1 + k), __ldg(c1 + 2u * cx.i0 + k),
+                       __ldg(c1 + 2u * cx.i1 + k), cx.w, cy.w) - 128.0f;
+    const ColourSpace cs = kColourSpaces[a.format & 3u];
+    const float yy = cs.limited ? fmaxf(Y - 16.0f, 0.0f) * 1.16438356f : Y;
+    const float r = yy + cs.rv * uvv[1];
+    const float g = yy - cs.gu * uvv[0] - cs.gv * uvv[1];
+    const float bl = yy + cs.bu * uvv[0];
     const float v[3] = {clampf(r, 0.0f, 255.0f) * 0.00392156862745098f, clampf(g, 0.0f, 255.0f) * 0.00392156862745098f,
                         clampf(bl, 0.0f, 255.0f) * 0.00392156862745098f};
-    store3(a, b, y, x, v);
+    store_pixel(a, b, y, x, v);
 }
 
 // ------------------------------------------------------------------------
@@ -231,7 +289,7 @@ __device__ __forceinline__ uint32_t floor_u(float v, float& f) {
 }
 
 // Bilinear lerp of two pixels' taps held with 2^23 added; weights wx per
-// pixel, wy shared (the arithmetic of sample_plane above).
+// pixel, wy shared (the arithmetic of blend above).
 __device__ __forceinline__ f2 bilerp(const Prod& mul, f2 t00, f2 t01, f2 t10, f2 t11, f2 wx, f2 wy) {
     const f2 m = splat(8388608.0f);
     const f2 top = add(sub(t00, m), mul(sub(t01, t00), wx));
@@ -326,7 +384,7 @@ __device__ __forceinline__ void store4(const MediaArgs& a, size_t base, size_t p
 // producer next to the row's copies.
 struct RowSlot {
     float wy, cwy;
-    unsigned long long base;  // element offset of (frame, channel 0, row y, column 0)
+    unsigned long long base;  // element offset of (frame, channel 0, row y, column 0): out_row_base
 };
 
 // Warp-specialised: the last warp's lane 0 is the producer (row weights and
@@ -355,7 +413,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
     if (tid >= consumers) {
         if (tid != consumers) return;
         // producer
-        const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
         uint32_t k = 0;
         for (;; ++k) {
             const uint32_t r = blockIdx.x + k * gridDim.x;
@@ -372,7 +429,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
             const Row t = row_taps((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, a.in_h);
             slots[s].wy = t.wy;
             slots[s].cwy = t.cwy;
-            slots[s].base = ((static_cast<unsigned long long>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w;
+            slots[s].base = out_row_base(a, b, y);
             uint8_t* st = smem + s * kStageBytes;
             const size_t frame = static_cast<size_t>(b) * a.in_h;
             tc::mbar_expect_tx(&full[s], 4u * in_w);
@@ -414,7 +471,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
     const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
     const f2 cwxa = mk(cwx[0], cwx[1]), cwxb = mk(cwx[2], cwx[3]);
     const bool csh[2] = {u0[0] == u0[1] && u1[0] == u1[1], u0[2] == u0[3] && u1[2] == u1[3]};
-    const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
+    const size_t plane = out_plane(a), col = out_col(a, active ? x4 : 0u);
 
     // one output row from stage S (a compile-time shared-memory offset);
     // returns false once the block's rows are done or a copy never landed
@@ -488,7 +545,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
                 out[1][p] = normalize(G, a.mean[1], a.std[1], m.rcp_std[1]);
                 out[2][p] = normalize(B, a.mean[2], a.std[2], m.rcp_std[2]);
             }
-            store4<BF16>(a, rs.base + x4, plane, out);
+            store4<BF16>(a, rs.base + col, plane, out);
         }
         // the warp is done with stage S
         __syncwarp();
@@ -588,7 +645,6 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
     if (tid >= consumers) {
         if (tid != consumers) return;
         // producer
-        const uint32_t frames = a.history_len ? a.history_len : 1u, slot = a.history_len ? a.history_slot : 0u;
         uint32_t k = 0;
         for (;; ++k) {
             const uint32_t r = blockIdx.x + k * gridDim.x;
@@ -606,7 +662,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
             const float sy = fmaxf((static_cast<float>(y) + 0.5f) * m.ratio_h - 0.5f, 0.0f);
             const uint32_t y0 = floor_u(sy, f), y1 = y0 + 1u < a.in_h ? y0 + 1u : y0;
             slots[s].wy = sy - f;
-            slots[s].base = ((static_cast<unsigned long long>(b) * frames + slot) * 3u * a.out_h + y) * a.out_w;
+            slots[s].base = out_row_base(a, b, y);
             uint8_t* st = smem + s * kStageBytes;
             const size_t frame = static_cast<size_t>(b) * a.in_h;
             tc::mbar_expect_tx(&full[s], 2u * row_bytes);
@@ -636,7 +692,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
     }
     const Prod prod{splat(m.neg_zero)};
     const f2 wxa = mk(wx[0], wx[1]), wxb = mk(wx[2], wx[3]);
-    const size_t plane = static_cast<size_t>(a.out_h) * a.out_w;
+    const size_t plane = out_plane(a), col = out_col(a, active ? x4 : 0u);
 
     auto step = [&](uint32_t k, auto stage) -> bool {
         constexpr uint32_t S = decltype(stage)::value;
@@ -695,7 +751,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
                     out[c][p] = divide(sub(v, splat(a.mean[c])), a.std[c], m.rcp_std[c]);
                 }
             }
-            store4<BF16>(a, rs.base + x4, plane, out);
+            store4<BF16>(a, rs.base + col, plane, out);
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[S]);
@@ -735,6 +791,7 @@ bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p
 // What both staged kernels need of the output and the normalisation.
 bool staged_common_ok(const MediaArgs& a) {
     if (a.out_w % 4u != 0 || a.out_w > 4u * staged::kMaxConsumers || a.out_h == 0) return false;
+    if (a.patch % 4u != 0) return false;  // four-column stores stay inside one patch row
     if (!aligned(a.out, a.bf16 ? 8 : 16)) return false;
     if (static_cast<uint64_t>(a.batch) * a.out_h >= (1ull << 31) ||
         static_cast<uint64_t>(a.batch) * a.in_h >= (1ull << 31))
@@ -797,8 +854,8 @@ cudaError_t launch_nv12_staged(const MediaArgs& a, int* err, cudaStream_t stream
 cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream) {
     const uint64_t pixels = static_cast<uint64_t>(a.batch) * a.out_h * a.out_w;
     const uint32_t blocks = static_cast<uint32_t>((pixels + 255) / 256);
-    if (nv12) nv12_to_nchw_kernel<<<blocks, 256, 0, stream>>>(a);
-    else packed_to_nchw_kernel<<<blocks, 256, 0, stream>>>(a);
+    if (nv12) nv12_pixel_kernel<<<blocks, 256, 0, stream>>>(a);
+    else packed_pixel_kernel<<<blocks, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -420,28 +420,59 @@ cudaError_t LewmModel::encode_vector(const float* obs, uint32_t n, float* out, c
     return cudaSuccess;
 }
 
+// The encoder workspace of n frames: the patch matrix first (offset 0), so
+// that preprocessing can write it directly (patch_buffer).
+size_t LewmModel::encoder_layout(uint32_t n, EncoderOffsets* o) const {
+    const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p, np = side * side, t = np + 1;
+    const uint32_t kdim = c.channels * p * p;
+    size_t off = 0;
+    auto take = [&](size_t k) { const size_t q = off; off += (k + 63) & ~static_cast<size_t>(63); return q; };
+    EncoderOffsets e;
+    e.patch = take(static_cast<size_t>(n) * np * kdim);
+    e.pe = take(static_cast<size_t>(n) * np * vh);
+    e.x = take(static_cast<size_t>(n) * t * vh);
+    e.y = take(static_cast<size_t>(n) * t * vh);
+    e.qkv = take(static_cast<size_t>(n) * t * 3 * vh);
+    e.att = take(static_cast<size_t>(n) * t * vh);
+    e.f = take(static_cast<size_t>(n) * t * c.vit_mlp);
+    e.cls = take(static_cast<size_t>(n) * vh);
+    e.ph = take(static_cast<size_t>(n) * c.projector_hidden);
+    if (o) *o = e;
+    return off;
+}
+
+cudaError_t LewmModel::patch_buffer(uint32_t n, float** patches) {
+    LWM_CU(enc.ensure(encoder_layout(n, nullptr)));
+    *patches = enc.ptr;  // EncoderOffsets::patch == 0
+    return cudaSuccess;
+}
+
 cudaError_t LewmModel::encode_pixels_body(const float* pix, uint32_t n, float* out, cudaStream_t s) {
+    LWM_CU(enc.ensure(encoder_layout(n, nullptr)));
+    LWM_CU(launch_patchify(pix, enc.ptr, n, c.channels, c.image_size, c.patch_size, s));
+    LWM_CU(encode_patches_body(n, out, s));
+    launches += 1;
+    return cudaSuccess;
+}
+
+// HfVitEncoder::forward from the patch matrix in the workspace: patch
+// embedding GEMM, [CLS] + position embeddings, the encoder layers, the final
+// norm of the CLS token, then the projector.
+cudaError_t LewmModel::encode_patches_body(uint32_t n, float* out, cudaStream_t s) {
     const SplitScratch* sp = &split;
     const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p, np = side * side, t = np + 1;
     const uint32_t kdim = c.channels * p * p, H = c.vit_heads, dh = vh / H;
-    size_t off = 0;
-    auto take = [&](size_t k) { const size_t o = off; off += (k + 63) & ~static_cast<size_t>(63); return o; };
-    const size_t o_patch = take(static_cast<size_t>(n) * np * kdim), o_pe = take(static_cast<size_t>(n) * np * vh);
-    const size_t o_x = take(static_cast<size_t>(n) * t * vh), o_y = take(static_cast<size_t>(n) * t * vh);
-    const size_t o_qkv = take(static_cast<size_t>(n) * t * 3 * vh), o_att = take(static_cast<size_t>(n) * t * vh);
-    const size_t o_f = take(static_cast<size_t>(n) * t * c.vit_mlp), o_cls = take(static_cast<size_t>(n) * vh);
-    const size_t o_ph = take(static_cast<size_t>(n) * c.projector_hidden);
-    LWM_CU(enc.ensure(off));
+    EncoderOffsets o;
+    LWM_CU(enc.ensure(encoder_layout(n, &o)));
     float* e = enc.ptr;
-    float *f_patch = e + o_patch, *f_pe = e + o_pe, *f_x = e + o_x, *f_y = e + o_y, *f_qkv = e + o_qkv;
-    float *f_att = e + o_att, *f_f = e + o_f, *f_cls = e + o_cls, *f_ph = e + o_ph;
+    float *f_patch = e + o.patch, *f_pe = e + o.pe, *f_x = e + o.x, *f_y = e + o.y, *f_qkv = e + o.qkv;
+    float *f_att = e + o.att, *f_f = e + o.f, *f_cls = e + o.cls, *f_ph = e + o.ph;
     const uint32_t rows = n * t;
     int k = 0;
     split_launches = 0;
-    LWM_CU(launch_patchify(pix, f_patch, n, c.channels, c.image_size, p, s));
     LWM_CU(gemm_f32(sp, gemm(f_patch, kdim, w.patch, f_pe, vh, n * np), s));
     LWM_CU(launch_vit_assemble(f_pe, w.cls, w.vpos, f_x, n, np, vh, s));
-    k += 3;
+    k += 2;
     const float scale = 1.0f / std::sqrt(static_cast<float>(dh));
     for (uint32_t l = 0; l < c.vit_layers; ++l) {
         const VitBlockW& b = w.vit[l];
@@ -594,6 +625,12 @@ cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, c
     LWM_CU(ensure_split());
     const uint64_t key[GraphCache::kKey] = {u(pix), n, u(out), u(enc.ptr), enc.floats, u(s), 2};
     return run_graphed(g_enc, key, s, launches, [&] { return encode_pixels_body(pix, n, out, s); });
+}
+
+cudaError_t LewmModel::encode_patches(uint32_t n, float* out, cudaStream_t s) {
+    LWM_CU(ensure_split());
+    const uint64_t key[GraphCache::kKey] = {n, u(out), u(enc.ptr), enc.floats, u(s), 3};
+    return run_graphed(g_enc, key, s, launches, [&] { return encode_patches_body(n, out, s); });
 }
 
 }  // namespace lwm

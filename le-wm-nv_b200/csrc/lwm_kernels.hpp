@@ -241,6 +241,7 @@ struct MediaArgs {
     uint32_t history_len, history_slot;
     int bf16;
     float mean[3], std[3];
+    uint32_t patch;     // 0: NCHW / history slot; p > 0: ViT patch matrix [B, (H/p)(W/p), 3 p p]
 };
 cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream);
 // The row-staged NV12 kernel (bulk-copied source rows, packed f32x2 math):

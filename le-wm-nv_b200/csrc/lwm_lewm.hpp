@@ -150,6 +150,11 @@ struct GraphCache {
     void reset();
 };
 
+// Float offsets of the encoder workspace's regions (the patch matrix at 0).
+struct EncoderOffsets {
+    size_t patch, pe, x, y, qkv, att, f, cls, ph;
+};
+
 struct LewmModel {
     lwm_lewm_config c{};
     LewmWeights w;
@@ -170,6 +175,8 @@ struct LewmModel {
     ~LewmModel();
     cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_pixels_body(const float* pixels, uint32_t n, float* out, cudaStream_t s);
+    cudaError_t encode_patches_body(uint32_t n, float* out, cudaStream_t s);
+    size_t encoder_layout(uint32_t n, EncoderOffsets* o) const;
     cudaError_t ensure_split();
     // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
     // GEMM inputs on the tensor cores, f32 accumulation and activations.
@@ -178,6 +185,11 @@ struct LewmModel {
     cudaError_t score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s);
     cudaError_t encode_pixels(const float* pixels, uint32_t n, float* out, cudaStream_t s);
+    // The ViT patch matrix [n, (image/p)^2, C p p] of the encoder workspace,
+    // for preprocessing to write directly; then encode_patches runs the
+    // encoder from it (no NCHW image, no patchify pass).
+    cudaError_t patch_buffer(uint32_t n, float** patches);
+    cudaError_t encode_patches(uint32_t n, float* out, cudaStream_t s);
 };
 
 }  // namespace lwm

@@ -384,6 +384,12 @@ _sig("lwm_preprocess_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POIN
      VP)
 _sig("lwm_preprocess_nv12_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32, U32,
      I32, VP)
+_sig("lwm_preprocess_packed_patches_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32,
+     I32, VP)
+_sig("lwm_preprocess_nv12_patches_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32,
+     I32, VP)
+_sig("lwm_lewm_encode_nv12_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), VP)
+_sig("lwm_lewm_encode_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), VP)
 
 
 def _check(status: int) -> None:
@@ -787,6 +793,24 @@ class LewmScorer(Scorer):
                                                  VP(out.data_ptr())))
         return out
 
+    def encode_nv12(self, y_plane, uv_plane, n: int, height: int, width: int, color_space, cfg: "ImagePreprocess"):
+        """NV12 device frames -> [n, D] embeddings, preprocessed straight into the ViT's patch matrix."""
+        import torch
+        cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
+        out = torch.empty((n, self.config.embed_dim), device="cuda", dtype=torch.float32)
+        _check(lib.lwm_lewm_encode_nv12_device(self.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), n, height, width,
+                                               cs, C.byref(cfg), VP(out.data_ptr())))
+        return out
+
+    def encode_packed(self, frames, n: int, height: int, width: int, fmt, cfg: "ImagePreprocess"):
+        """Packed RGB/BGR(A) device frames -> [n, D] embeddings, preprocessed straight into the patch matrix."""
+        import torch
+        f = PACKED_FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+        out = torch.empty((n, self.config.embed_dim), device="cuda", dtype=torch.float32)
+        _check(lib.lwm_lewm_encode_packed_device(self.handle, VP(_ptr(frames)), n, height, width, f, C.byref(cfg),
+                                                 VP(out.data_ptr())))
+        return out
+
 
 class _CudaArray:
     def __init__(self, ptr: int, shape, typestr: str = "<f4"):
@@ -1043,6 +1067,22 @@ def preprocess_packed_device(ctx: Context, frames, batch: int, height: int, widt
     f = PACKED_FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
     _check(lib.lwm_preprocess_packed_device(ctx.handle, VP(_ptr(frames)), batch, height, width, f, C.byref(cfg),
                                             history_len, history_slot, int(bf16), VP(_ptr(out))))
+
+
+def preprocess_packed_patches_device(ctx: Context, frames, batch: int, height: int, width: int, fmt,
+                                     cfg: ImagePreprocess, patch: int, out, bf16: bool = False) -> None:
+    """Packed frames -> the ViT patch matrix [B, (oh/p)(ow/p), 3 p p] (the NCHW values, permuted)."""
+    f = PACKED_FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    _check(lib.lwm_preprocess_packed_patches_device(ctx.handle, VP(_ptr(frames)), batch, height, width, f,
+                                                    C.byref(cfg), patch, int(bf16), VP(_ptr(out))))
+
+
+def preprocess_nv12_patches_device(ctx: Context, y_plane, uv_plane, batch: int, height: int, width: int, color_space,
+                                   cfg: ImagePreprocess, patch: int, out, bf16: bool = False) -> None:
+    """NV12 planes -> the ViT patch matrix [B, (oh/p)(ow/p), 3 p p] (the NCHW values, permuted)."""
+    cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
+    _check(lib.lwm_preprocess_nv12_patches_device(ctx.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), batch, height,
+                                                  width, cs, C.byref(cfg), patch, int(bf16), VP(_ptr(out))))
 
 
 def preprocess_nv12_device(ctx: Context, y_plane, uv_plane, batch: int, height: int, width: int, color_space,

@@ -134,6 +134,43 @@ def test_image_pipeline_matches_oracle(ctx):
     assert_costs_close(got, ref)
 
 
+@pytest.mark.parametrize("precision", ["f32", "bf16"])
+def test_fused_frame_encoding_equals_preprocess_then_encode(ctx, precision):
+    # the fused path (preprocess straight into the ViT patch matrix) feeds the
+    # encoder the same values as preprocess -> NCHW -> patchify: identical
+    # embeddings, with one launch fewer and no NCHW image
+    w = W.lewm_image(seed=4, samples=64)
+    sc = L.LewmScorer(ctx, w.config, w.weights)
+    sc.set_precision(precision)
+    cfg = L.ImagePreprocess.imagenet_224()
+    y = torch.as_tensor(np.concatenate([w.y_plane, w.goal_y])).cuda()
+    uv = torch.as_tensor(np.concatenate([w.uv_plane, w.goal_uv])).cuda()
+    pix = torch.empty((2, 3, 224, 224), device="cuda")
+    torch.cuda.synchronize()
+    n0 = ctx.launch_count()
+    L.preprocess_nv12_device(ctx, y, uv, 2, 224, 224, "bt601-video", cfg, pix)
+    with torch.cuda.stream(ctx.torch_stream()):
+        two_step = sc.encode_pixels(pix)
+    ctx.synchronize()
+    n1 = ctx.launch_count()
+    with torch.cuda.stream(ctx.torch_stream()):
+        fused = sc.encode_nv12(y, uv, 2, 224, 224, "bt601-video", cfg)
+    ctx.synchronize()
+    n2 = ctx.launch_count()
+    assert torch.equal(fused, two_step)
+    assert (n2 - n1) == (n1 - n0) - 1, "the fused path should save the patchify launch"
+    # packed RGB frames through the same fused path
+    rgb = np.random.default_rng(9).integers(0, 256, (2, 240, 320, 3), dtype=np.uint8)
+    rgb_dev = torch.as_tensor(rgb).cuda()
+    torch.cuda.synchronize()
+    L.preprocess_packed_device(ctx, rgb_dev, 2, 240, 320, "rgb", cfg, pix)
+    with torch.cuda.stream(ctx.torch_stream()):
+        ref = sc.encode_pixels(pix)
+        got = sc.encode_packed(rgb_dev, 2, 240, 320, "rgb", cfg)
+    ctx.synchronize()
+    assert torch.equal(got, ref)
+
+
 def test_lewm_validation(ctx):
     cfg = L.LewmConfig.vector()
     with pytest.raises(L.LwmError, match="weight blob"):

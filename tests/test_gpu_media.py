@@ -202,3 +202,59 @@ def test_packed_staged_and_generic_kernels_agree(ctx):
         L.preprocess_packed_device(ctx, frames, B, H, W, "rgb", cfg, out)
     ctx.synchronize()
     np.testing.assert_array_equal(aligned.cpu().numpy(), shifted[1:].cpu().numpy())
+
+
+# ------------------------------------------------- ViT patch-matrix output
+
+def _patchify(nchw: np.ndarray, p: int) -> np.ndarray:
+    """[B, 3, H, W] -> [B, (H/p)(W/p), 3 p p]: the stride-p patch-embedding
+    input (Embeddings, src/models/lewm/vit.rs:32-52)."""
+    B, C, H, W = nchw.shape
+    x = nchw.reshape(B, C, H // p, p, W // p, p).transpose(0, 2, 4, 1, 3, 5)
+    return x.reshape(B, (H // p) * (W // p), C * p * p)
+
+
+# (B, H, W, oh, ow, p): row-staged shapes (widths multiple of 16, p multiple
+# of 4) and per-pixel ones (odd source width, p = 2 is not a multiple of 4)
+@pytest.mark.parametrize("shape", [(2, 480, 640, 224, 224, 16), (3, 224, 224, 224, 224, 16),
+                                   (2, 90, 122, 32, 48, 8), (1, 64, 80, 12, 10, 2)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_nv12_patch_layout_equals_oracle_patchified(ctx, shape, bf16):
+    B, H, W, oh, ow, p = shape
+    rng = np.random.default_rng(zlib.crc32(repr(("nv12p", shape)).encode()))
+    y = rng.integers(0, 256, (B, H, W), dtype=np.uint8)
+    uv = rng.integers(0, 256, (B, H // 2, W // 2, 2), dtype=np.uint8)
+    cfg = L.ImagePreprocess.make(oh, ow, **IMAGENET)
+    out = torch.full((B, (oh // p) * (ow // p), 3 * p * p), 7.0, device="cuda",
+                     dtype=torch.bfloat16 if bf16 else torch.float32)
+    torch.cuda.synchronize()
+    L.preprocess_nv12_patches_device(ctx, torch.from_numpy(y).cuda(), torch.from_numpy(uv).cuda(), B, H, W,
+                                     "bt709-video", cfg, p, out, bf16)
+    ctx.synchronize()
+    ref = _patchify(O.preprocess_nv12(y, uv, 1, oh, ow, **IMAGENET), p)
+    got = out.float().cpu().numpy()
+    assert np.array_equal(got, _bf16_of(ref) if bf16 else ref)
+
+
+@pytest.mark.parametrize("fmt", ["rgb", "bgra"])
+@pytest.mark.parametrize("shape", [(2, 480, 640, 224, 224, 16), (2, 33, 47, 16, 16, 4)])
+def test_packed_patch_layout_equals_oracle_patchified(ctx, fmt, shape):
+    B, H, W, oh, ow, p = shape
+    C = 4 if fmt.endswith("a") else 3
+    rng = np.random.default_rng(zlib.crc32(repr(("packedp", fmt, shape)).encode()))
+    frames = rng.integers(0, 256, (B, H, W, C), dtype=np.uint8)
+    cfg = L.ImagePreprocess.make(oh, ow, **IMAGENET)
+    out = torch.full((B, (oh // p) * (ow // p), 3 * p * p), 7.0, device="cuda")
+    torch.cuda.synchronize()
+    L.preprocess_packed_patches_device(ctx, torch.from_numpy(frames).cuda(), B, H, W, fmt, cfg, p, out)
+    ctx.synchronize()
+    ref = _patchify(O.preprocess_packed(frames, L.PACKED_FORMATS[fmt], oh, ow, **IMAGENET), p)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_patch_layout_rejects_sizes_it_does_not_divide(ctx):
+    y = torch.zeros((1, 32, 32), dtype=torch.uint8, device="cuda")
+    uv = torch.zeros((1, 16, 16, 2), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((1, 64, 48), device="cuda")
+    with pytest.raises(L.LwmError, match="must divide the output size"):
+        L.preprocess_nv12_patches_device(ctx, y, uv, 1, 32, 32, 0, L.ImagePreprocess.make(30, 30), 4, out)
