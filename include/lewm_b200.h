@@ -68,6 +68,31 @@ lwm_status lwm_ctx_synchronize(lwm_ctx* ctx);
 /* Number of kernels this library has launched on the context so far. */
 lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out);
 
+/* Fault injection for tests of the failure paths (no counterpart in the
+ * reference, whose only failure path is the planning deadline,
+ * src/planner.rs:1055-1150).  Every pipeline wait in this library's kernels
+ * is bounded: a wait that gives up records where in an error word and the
+ * kernel unwinds and returns (nothing traps or hangs).  These knobs make
+ * such a wait run out on purpose, from the host, on a context's later
+ * launches; all zero = off (the default).
+ *   wait_polls            pipeline waits give up after this many polls
+ *                         (0: the built-in limit);
+ *   tc_skip_h_arrive      1: in the bf16 tensor-core rollout, the first GRU
+ *                         epilogue warp of block 0 skips its first hand-off
+ *                         of h to the MMA issuer, whose wait then runs out:
+ *                         the plan returns LWM_TIMEOUT naming the site;
+ *   media_skip_row_plus1  r + 1: the row-staged preprocessing producer
+ *                         skips the source-row copies of output row r;
+ *                         the consumers' wait runs out and
+ *                         lwm_ctx_synchronize reports LWM_CUDA_ERROR.
+ * NULL clears every knob. */
+typedef struct lwm_test_faults {
+    uint32_t wait_polls;
+    uint32_t tc_skip_h_arrive;
+    uint32_t media_skip_row_plus1;
+} lwm_test_faults;
+lwm_status lwm_ctx_set_test_faults(lwm_ctx* ctx, const lwm_test_faults* faults);
+
 /* ---------------------------------------------------------------- planners */
 
 /* ActionBounds + MppiConfig (src/planner.rs:67-103, 178-254).

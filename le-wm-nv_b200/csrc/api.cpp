@@ -122,6 +122,7 @@ struct lwm_ctx {
     // read after every stream synchronisation (allocated on first use)
     int* media_err = nullptr;
     int* media_err_dev = nullptr;
+    lwm_test_faults faults{};  // fault injection for tests (lwm_ctx_set_test_faults)
 };
 
 enum class PlannerKind { Mppi, Cem, Icem };
@@ -742,6 +743,8 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                 } else if (sc->precision == LWM_PRECISION_BF16 && lwm::skyjepa_tc_supported(a, &why)) {
                     LWM_TRY(ensure_tc(sc, a, B, p->S, p->T));
                     a.h0_work = sc->h0_work.as<float>();
+                    a.test_wait_polls = p->ctx->faults.wait_polls;
+                    a.test_skip_h_arrive = p->ctx->faults.tc_skip_h_arrive;
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
                     a.low_dev = low;
                     a.high_dev = high;
@@ -997,6 +1000,13 @@ lwm_status lwm_ctx_synchronize(lwm_ctx* ctx) {
         return fail(LWM_CUDA_ERROR, "image preprocessing: a source-row copy never completed (" + where +
                                         "); that launch's output is incomplete");
     }
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_set_test_faults(lwm_ctx* ctx, const lwm_test_faults* faults) {
+    if (!ctx) return fail(LWM_INVALID_ARGUMENT, "null context");
+    if (faults) ctx->faults = *faults;
+    else ctx->faults = lwm_test_faults{};
     return LWM_OK;
 }
 
@@ -1730,6 +1740,12 @@ lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_p
     if (err_dev) LWM_CUDA(cudaMemcpyAsync(tc_err, err_dev, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
     LWM_CUDA(cudaStreamSynchronize(stream));
     if (tc_err[0] && sc->kind == ScorerKind::Lewm) LWM_CUDA(cudaMemset(err_dev, 0, sizeof tc_err));
+    if (tc_err[0] && p->counters.ptr) {
+        // the blocks that gave up never arrived: clear the per-vehicle
+        // arrival counters so the planner's next plan starts clean
+        LWM_CUDA(cudaMemsetAsync(p->counters.ptr, 0, p->counters.bytes, stream));
+        LWM_CUDA(cudaStreamSynchronize(stream));
+    }
     if (tc_err[0])
         return fail(LWM_TIMEOUT, "a tensor-core pipeline wait timed out on the device (site " + std::to_string(tc_err[0]) +
                                      ", block " + std::to_string(tc_err[1]) + ", index " + std::to_string(tc_err[2]) +
@@ -1851,6 +1867,8 @@ lwm_status preprocess_packed(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uin
     a.channels = format >= 2 ? 4 : 3;
     a.format = static_cast<uint32_t>(format);
     a.patch = patch;
+    a.test_skip_row_plus1 = ctx->faults.media_skip_row_plus1;
+    a.test_wait_polls = ctx->faults.wait_polls;
     if (lwm::packed_staged_eligible(a)) {
         LWM_TRY(ensure_media_err(ctx));
         LWM_CUDA(lwm::launch_packed_staged(a, ctx->media_err_dev, ctx->stream));
@@ -1881,6 +1899,8 @@ lwm_status preprocess_nv12(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* 
     a.channels = 1;
     a.format = static_cast<uint32_t>(color_space);
     a.patch = patch;
+    a.test_skip_row_plus1 = ctx->faults.media_skip_row_plus1;
+    a.test_wait_polls = ctx->faults.wait_polls;
     if (lwm::nv12_staged_eligible(a)) {
         LWM_TRY(ensure_media_err(ctx));
         LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, ctx->stream));

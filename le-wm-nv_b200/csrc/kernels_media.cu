@@ -316,8 +316,8 @@ __device__ __forceinline__ Row row_taps(float sy, uint32_t in_h) {
     return r;
 }
 
-__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (tc::mbar_try(bar, parity)) return true;
     return false;
 }
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
             const uint32_t r = blockIdx.x + k * gridDim.x;
             if (r >= rows) break;
             const uint32_t s = k % kStages;
-            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u)) {
+            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u, m.wait_polls)) {
                 m.err[1] = static_cast<int>(blockIdx.x);
                 m.err[2] = static_cast<int>(k);
                 m.err[3] = 2;
@@ -432,6 +432,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
             slots[s].base = out_row_base(a, b, y);
             uint8_t* st = smem + s * kStageBytes;
             const size_t frame = static_cast<size_t>(b) * a.in_h;
+            if (r == m.skip_row) continue;  // fault injection: this stage never fills
             tc::mbar_expect_tx(&full[s], 4u * in_w);
             tc::bulk_g2s(st, a.a + (frame + t.y0) * in_w, in_w, &full[s]);
             tc::bulk_g2s(st + ROWCAP, a.a + (frame + t.y1) * in_w, in_w, &full[s]);
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
         // the copies still in flight land before the block's shared memory
         // can be released
         for (uint32_t j = k > kStages ? k - kStages : 0u; j < k; ++j)
-            wait_stage(&full[j % kStages], (j / kStages) & 1u);
+            wait_stage(&full[j % kStages], (j / kStages) & 1u, m.wait_polls);
         return;
     }
 
@@ -478,7 +479,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) nv12_staged_kernel(MediaArgs a
     auto step = [&](uint32_t k, auto stage) -> bool {
         constexpr uint32_t S = decltype(stage)::value;
         if (blockIdx.x + k * gridDim.x >= rows) return false;
-        if (!wait_stage(&full[S], (k / kStages) & 1u)) {
+        if (!wait_stage(&full[S], (k / kStages) & 1u, m.wait_polls)) {
             if (lane == 0) {
                 m.err[1] = static_cast<int>(blockIdx.x);
                 m.err[2] = static_cast<int>(k);
@@ -650,7 +651,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
             const uint32_t r = blockIdx.x + k * gridDim.x;
             if (r >= rows) break;
             const uint32_t s = k % kStages;
-            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u)) {
+            if (k >= kStages && !wait_stage(&empty[s], (k / kStages - 1u) & 1u, m.wait_polls)) {
                 m.err[1] = static_cast<int>(blockIdx.x);
                 m.err[2] = static_cast<int>(k);
                 m.err[3] = 2;
@@ -665,12 +666,13 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
             slots[s].base = out_row_base(a, b, y);
             uint8_t* st = smem + s * kStageBytes;
             const size_t frame = static_cast<size_t>(b) * a.in_h;
+            if (r == m.skip_row) continue;  // fault injection: this stage never fills
             tc::mbar_expect_tx(&full[s], 2u * row_bytes);
             tc::bulk_g2s(st, a.a + (frame + y0) * row_bytes, row_bytes, &full[s]);
             tc::bulk_g2s(st + ROWCAP, a.a + (frame + y1) * row_bytes, row_bytes, &full[s]);
         }
         for (uint32_t j = k > kStages ? k - kStages : 0u; j < k; ++j)
-            wait_stage(&full[j % kStages], (j / kStages) & 1u);
+            wait_stage(&full[j % kStages], (j / kStages) & 1u, m.wait_polls);
         return;
     }
 
@@ -697,7 +699,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2) packed_staged_kernel(MediaArgs
     auto step = [&](uint32_t k, auto stage) -> bool {
         constexpr uint32_t S = decltype(stage)::value;
         if (blockIdx.x + k * gridDim.x >= rows) return false;
-        if (!wait_stage(&full[S], (k / kStages) & 1u)) {
+        if (!wait_stage(&full[S], (k / kStages) & 1u, m.wait_polls)) {
             if (lane == 0) {
                 m.err[1] = static_cast<int>(blockIdx.x);
                 m.err[2] = static_cast<int>(k);
@@ -814,6 +816,8 @@ StagedMedia staged_params(const MediaArgs& a, int* err) {
     for (int c = 0; c < 3; ++c) m.rcp_std[c] = 1.0f / a.std[c];
     m.err = err;
     m.neg_zero = -0.0f;
+    m.skip_row = a.test_skip_row_plus1 ? a.test_skip_row_plus1 - 1u : ~0u;
+    m.wait_polls = a.test_wait_polls ? a.test_wait_polls : staged::kWaitLimit;
     return m;
 }
 }  // namespace

@@ -94,6 +94,21 @@ __device__ __forceinline__ void aux_sync() {
     asm volatile("bar.sync %0, %1;" ::"n"(kAuxBarrier), "n"(kAuxThreads) : "memory");
 }
 
+// True on every aux thread iff `v` is true on all of them (a barrier with an
+// AND reduction).  The aux warps take every wait's outcome through it, so
+// they leave their loop together and never meet aux_sync() short of a warp
+// (a named barrier that a departed warp never reaches would not end).
+__device__ __forceinline__ bool aux_all(bool v) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(out)
+        : "r"(static_cast<uint32_t>(v)), "n"(kAuxBarrier), "n"(kAuxThreads)
+        : "memory");
+    return out != 0;
+}
+
 // Hardware tanh (MUFU.TANH); the gates use it for sigmoid as well:
 // sigmoid(v) = 0.5 + 0.5 tanh(v / 2).  Relative error ~2^-11, far inside the
 // bf16 path's tolerance.
@@ -624,6 +639,8 @@ struct TcArgs {
     const uint8_t* xt;  // x tiles [tiles][T][kXBytes]
     uint32_t tiles_per_vehicle, tiles;
     int* err;
+    uint32_t wait_polls;     // polls before a pipeline wait gives up
+    uint32_t skip_h_arrive;  // fault injection: CTA 0's first GRU-epilogue warp skips its first h_full arrival
 };
 
 }  // namespace
@@ -635,6 +652,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t T = a.T, hid = a.hid;
     volatile int* err = p.err;
+    const uint32_t lim = p.wait_polls;
 
     // ---- setup: barriers, TMEM, resident weights
     if (tid == 0) {
@@ -688,17 +706,30 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             for (uint32_t tile = blockIdx.x; tile < p.tiles && !err[0]; tile += gridDim.x)
                 for (uint32_t t = 0; t < T && !err[0]; ++t, ++xs) {
                     const uint32_t xslot = xs & 1u;
-                    if (!tc::mbar_wait(&s.x_empty[xslot], ((xs >> 1) & 1u) ^ 1u, err, 8, xs)) break;
+                    if (!tc::mbar_wait(&s.x_empty[xslot], ((xs >> 1) & 1u) ^ 1u, err, 8, xs, lim)) break;
                     tc::mbar_expect_tx(&s.x_full[xslot], kXBytes);
                     tc::bulk_g2s(s.X[xslot], p.xt + (static_cast<size_t>(tile) * T + t) * kXBytes, kXBytes,
                                  &s.x_full[xslot]);
                     for (uint32_t c = 0; c < kChunks; ++c, ++j) {
                         const uint32_t slot = j % kWStages, n = j / kWStages;
-                        if (!tc::mbar_wait(&s.w_empty[slot], (n & 1u) ^ 1u, err, 1, j)) break;
+                        if (!tc::mbar_wait(&s.w_empty[slot], (n & 1u) ^ 1u, err, 1, j, lim)) break;
                         tc::mbar_expect_tx(&s.w_full[slot], kChunkBytes);
                         tc::bulk_g2s(s.W[slot], p.wc + static_cast<size_t>(c) * kChunkBytes, kChunkBytes,
                                      &s.w_full[slot]);
                     }
+                }
+            // j weight chunks and xs x tiles were issued; when a wait gave up,
+            // the last ones may not have been consumed: they land before the
+            // CTA exits (each slot's last phase completes once its copy has)
+            for (uint32_t sl = 0; sl < kWStages; ++sl)
+                if (j > sl) {
+                    const uint32_t last = sl + ((j - 1u - sl) / kWStages) * kWStages;
+                    tc::mbar_wait_landing(&s.w_full[sl], (last / kWStages) & 1u, lim);
+                }
+            for (uint32_t sl = 0; sl < 2u; ++sl)
+                if (xs > sl) {
+                    const uint32_t last = sl + ((xs - 1u - sl) / 2u) * 2u;
+                    tc::mbar_wait_landing(&s.x_full[sl], (last >> 1) & 1u, lim);
                 }
         }
     } else if (warp == 1) {
@@ -717,7 +748,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 col = slot * kSlotCols;
                 if (last[slot] < 0) return true;
                 const int g = last[slot];
-                return tc::mbar_wait(&s.empty[g][slot], (uses[g][slot] - 1u) & 1u, err, 5, k);
+                return tc::mbar_wait(&s.empty[g][slot], (uses[g][slot] - 1u) & 1u, err, 5, k, lim);
             };
             auto publish = [&](uint32_t k, int g) {
                 const uint32_t slot = k % kSlots;
@@ -743,14 +774,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
                 for (uint32_t t = 0; ok && t < T; ++t) {
-                    ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq);  // A holds h_t
+                    ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_t
                     ++hq;
                     const uint32_t xslot = xs & 1u;
-                    if (ok) ok = tc::mbar_wait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs);
+                    if (ok) ok = tc::mbar_wait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs, lim);
                     for (uint32_t c = 0; ok && c < kChunks; ++c, ++j) {
                         if (c == 1 && !(ok = prober(t > 0))) break;  // prober of step t-1 (A = h_t)
                         const uint32_t wslot = j % kWStages;
-                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j / kWStages) & 1u, err, 4, j))) break;
+                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j / kWStages) & 1u, err, 4, j, lim))) break;
                         uint32_t col;
                         if (!(ok = acc_slot(K, col))) break;
                         tc::fence_after();
@@ -771,14 +802,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     }
                     ++xs;
                 }
-                if (ok) ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq);  // A holds h_T
+                if (ok) ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_T
                 ++hq;
                 if (ok) ok = prober(true);                           // prober of step T-1
                 if (ok) tc::commit(&s.a_read);                       // A is no longer read in this tile
             }
             // every MMA issued has completed before TMEM is released
             tc::commit(&s.done);
-            tc::mbar_wait(&s.done, 0, err, 10, 0);
+            tc::mbar_wait_landing(&s.done, 0, lim);
         }
     } else if (warp < kAuxWarp0) {
         // ================= GRU epilogue: quadrant q, units [kUPW half, kUPW (half + 1)) of each chunk
@@ -792,7 +823,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             const uint32_t b = tile / p.tiles_per_vehicle;
             if (tiles_done > 0) {
                 // the previous tile's last prober MMA read A: wait for it before overwriting
-                if (!(ok = tc::mbar_wait(&s.a_read, (tiles_done - 1) & 1u, err, 7, tiles_done))) break;
+                if (!(ok = tc::mbar_wait(&s.a_read, (tiles_done - 1) & 1u, err, 7, tiles_done, lim))) break;
                 tc::fence_after();
             }
             // h0 of the vehicle -> H (TMEM f32) and A (bf16), this warp's units
@@ -811,12 +842,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
             tc::fence_async_smem();
             tc::fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s.h_full);
+            const bool skip = p.skip_h_arrive && blockIdx.x == 0 && warp == kEpiWarp0 && tiles_done == 0;
+            if (lane == 0 && !skip) tc::mbar_arrive(&s.h_full);
             for (uint32_t t = 0; ok && t < T; ++t) {
                 for (uint32_t c = 0; c < kChunks; ++c) {
                     const uint32_t k = K0 + kEntries * t + (c == 0 ? 0u : c + 1u);
                     const uint32_t slot = k % kSlots;
-                    if (!(ok = tc::mbar_wait(&s.full[0][slot], eu[slot] & 1u, err, 6, k))) break;
+                    if (!(ok = tc::mbar_wait(&s.full[0][slot], eu[slot] & 1u, err, 6, k, lim))) break;
                     ++eu[slot];
                     tc::fence_after();
                     static_assert(kUPW == 16, "the gate loop loads 16 units per warp");
@@ -884,7 +916,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 // prober of step t-1 (entry kEntries t + 1; at t = 0 an empty entry; the last at kEntries T)
                 const uint32_t k = K0 + (t < T ? kEntries * t + 1 : kEntries * T);
                 const uint32_t slot = k % kSlots;
-                if (!(ok = tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k))) break;
+                ok = aux_all(tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k, lim));
+                if (!ok) break;
                 ++au[slot];
                 tc::fence_after();
                 if (t > 0) {
@@ -1203,6 +1236,8 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     p.tiles_per_vehicle = a.S / kRows;
     p.tiles = a.B * p.tiles_per_vehicle;
     p.err = err;
+    p.wait_polls = a.test_wait_polls ? a.test_wait_polls : tc::kWaitLimit;
+    p.skip_h_arrive = a.test_skip_h_arrive;
     const size_t smem = sizeof(TcSmem) + 1024;
     static bool attr = false;
     if (!attr) {

@@ -163,6 +163,9 @@ struct SkyjepaArgs {
     MppiArgs m;
     const float* action_tcn_host;  // host copy of the action encoder's weights (kernel-parameter packing), or nullptr
     float* h0_work;                // scratch of the batched history encoder (skyjepa_h0_work_bytes), or nullptr
+    // fault injection for tests (lwm_ctx_set_test_faults): 0 = off
+    uint32_t test_wait_polls;      // tensor-core pipeline waits give up after this many polls
+    uint32_t test_skip_h_arrive;   // the tensor-core rollout's first h hand-off of CTA 0 misses one arrival
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
@@ -242,6 +245,10 @@ struct MediaArgs {
     int bf16;
     float mean[3], std[3];
     uint32_t patch;     // 0: NCHW / history slot; p > 0: ViT patch matrix [B, (H/p)(W/p), 3 p p]
+    // fault injection for tests (lwm_ctx_set_test_faults), 0 = off: the
+    // row-staged producer skips output row test_skip_row_plus1 - 1; waits
+    // give up after test_wait_polls polls
+    uint32_t test_skip_row_plus1, test_wait_polls;
 };
 cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream);
 // The row-staged NV12 kernel (bulk-copied source rows, packed f32x2 math):
@@ -251,6 +258,10 @@ cudaError_t launch_media(const MediaArgs& a, bool nv12, cudaStream_t stream);
 // of magnitude in [2^-40, 2^40]).  `err` (4 ints, device-
 // visible) gets 1 in err[0] when a row copy never completed.
 struct StagedMedia {
+    // fault injection for tests (lwm_ctx_set_test_faults): the producer skips
+    // the copies of output row `skip_row` (~0u: none); waits give up after
+    // `wait_polls` polls
+    uint32_t skip_row, wait_polls;
     float ratio_h, ratio_w;
     float rcp_std[3];
     float neg_zero;  // -0.0f

@@ -160,8 +160,8 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 // parity in err[1..3]; every other wait returns false soon after.
 constexpr uint32_t kWaitLimit = 1u << 26;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* err, int site = 1,
-                                          int detail = 0) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+                                          int detail = 0, uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try(bar, parity)) return true;
         if ((i & 1023u) == 1023u && err[0]) return false;
     }
@@ -170,6 +170,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         err[2] = detail;
         err[3] = static_cast<int>(parity);
     }
+    return false;
+}
+
+// Waits for work this thread started itself (bulk copies it issued, MMAs it
+// committed) to land before the CTA frees what that work touches: unlike
+// mbar_wait it does not give up early when another wait failed, only after
+// `limit` polls.
+__device__ __forceinline__ bool mbar_wait_landing(uint64_t* bar, uint32_t parity, uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try(bar, parity)) return true;
     return false;
 }
 

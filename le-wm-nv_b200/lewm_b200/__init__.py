@@ -38,6 +38,11 @@ FP = C.POINTER(C.c_float)
 VP = C.c_void_p
 
 
+class FaultKnobs(C.Structure):
+    """lwm_test_faults (include/lewm_b200.h)."""
+    _fields_ = [("wait_polls", C.c_uint32), ("tc_skip_h_arrive", C.c_uint32), ("media_skip_row_plus1", C.c_uint32)]
+
+
 class LwmError(RuntimeError):
     """A failing lwm_* call: .status is the lwm_status name."""
 
@@ -316,6 +321,7 @@ _sig("lwm_planner_clear_warm_start", C.c_int, VP)
 _sig("lwm_planner_warm_start", C.c_int, VP, FP, C.c_size_t, C.POINTER(U32))
 _sig("lwm_planner_reset_rng", C.c_int, VP)
 _sig("lwm_planner_rng_offset", C.c_int, VP, C.POINTER(U64))
+_sig("lwm_ctx_set_test_faults", C.c_int, VP, C.POINTER(FaultKnobs))
 _sig("lwm_planner_elite_indices", C.c_int, VP, C.POINTER(U32), C.c_size_t, C.POINTER(U32), C.POINTER(U32),
      C.POINTER(U32))
 _sig("lwm_planner_last_candidates", C.c_int, VP, C.POINTER(VP), C.POINTER(U32))
@@ -451,6 +457,13 @@ class Context:
 
     def synchronize(self) -> None:
         _check(lib.lwm_ctx_synchronize(self.handle))
+
+    def set_test_faults(self, wait_polls: int = 0, tc_skip_h_arrive: bool = False,
+                        media_skip_row: Optional[int] = None) -> None:
+        """Fault injection for failure-path tests (lwm_ctx_set_test_faults);
+        no arguments clears every knob."""
+        f = FaultKnobs(wait_polls, int(tc_skip_h_arrive), 0 if media_skip_row is None else media_skip_row + 1)
+        _check(lib.lwm_ctx_set_test_faults(self.handle, C.byref(f)))
 
     def launch_count(self) -> int:
         n = U64()

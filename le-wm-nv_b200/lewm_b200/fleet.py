@@ -113,6 +113,19 @@ def exchange_tuples(local, group, shards: int, out=None):
     return out
 
 
+def exchange_tuples_checked(local, group, shards: int, out=None):
+    """exchange_tuples whose failure — a rank of the vehicle group that left,
+    or a collective that ran out the process group's timeout (the bounded
+    wait of the exchange) — surfaces as LwmError with status NCCL_ERROR, so a
+    caller can drop the group and re-plan on the ranks that remain."""
+    from . import LwmError
+    try:
+        return exchange_tuples(local, group, shards, out=out)
+    except Exception as e:  # gloo / NCCL raise RuntimeError subclasses (or DistBackendError)
+        raise LwmError(4, f"candidate-shard tuple exchange over {shards} ranks failed "
+                          f"({type(e).__name__}: {str(e).splitlines()[0] if str(e) else ''})") from e
+
+
 class FleetPlanner:
     """One rank's share of a fleet: a learned (SkyJEPA) or nominal scorer over
     its vehicle range and an MPPI planner over its candidate range."""
@@ -154,7 +167,7 @@ class FleetPlanner:
             if self.time_exchange:
                 ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 ev[0].record(stream)
-            exchange_tuples(local, self.group, self.part.candidate_shards, out=self._gathered)
+            exchange_tuples_checked(local, self.group, self.part.candidate_shards, out=self._gathered)
             if self.time_exchange:
                 ev[1].record(stream)
                 self._events.append(ev)

@@ -150,3 +150,42 @@ def _free_port():
 def test_sharded_mppi_equals_unsharded_over_gloo(world, vehicles, samples, mode):
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(world, _free_port(), vehicles, samples, mode, 0.7), nprocs=world, join=True)
+
+
+def _leaving_worker(rank, world, port, result_path):
+    """Rank 1 leaves the job between two plan steps (its process exits); the
+    other rank's next exchange fails within the process group's timeout and
+    reports NCCL_ERROR instead of waiting for good."""
+    import datetime
+    import time as _time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from lewm_b200 import LwmError
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    parts = F.partition(2, 64, world, "candidates")
+    group = F.new_groups(parts)
+    me = parts[rank]
+    cand, scores = _problem(2, 64)
+    (s0, s1) = me.samples
+    local = torch.from_numpy(shard_tuples(scores[:, s0:s1], cand[:, s0:s1], s0, 0.7))
+    F.exchange_tuples_checked(local, group, world)  # plan step 1: every rank takes part
+    if rank == 1:
+        os._exit(0)  # leaves between plan steps, with no collective in flight
+    t0 = _time.monotonic()
+    try:
+        F.exchange_tuples_checked(local, group, world)  # plan step 2: the peer is gone
+        outcome = "no error"
+    except LwmError as e:
+        outcome = f"{e.status} after {_time.monotonic() - t0:.1f}s"
+    with open(result_path, "w") as f:
+        f.write(outcome)
+    os._exit(0)  # the group cannot be torn down collectively without the peer
+
+
+def test_rank_leaving_between_plan_steps_fails_the_next_exchange(tmp_path):
+    import torch.multiprocessing as mp
+    out = tmp_path / "outcome.txt"
+    mp.spawn(_leaving_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    outcome = out.read_text()
+    assert outcome.startswith("NCCL_ERROR"), outcome
+    assert float(outcome.split()[-1][:-1]) < 30.0, outcome
