@@ -51,7 +51,10 @@ def test_tensor_core_wait_timeout_reports_and_recovers(ctx):
             planner.plan(sc, injected_noise=noise)
     finally:
         ctx.set_test_faults()
-    assert e.value.status == "TIMEOUT" and "site 2" in e.value.message, str(e.value)
+    # the first wait to give up records its site: the MMA issuer's wait for h
+    # (site 2) or the weight producer's wait behind it (site 1), in block 0
+    assert e.value.status == "TIMEOUT" and "block 0" in e.value.message, str(e.value)
+    assert any(f"site {k}," in e.value.message for k in (1, 2)), str(e.value)
     # the context, the scorer and the planner keep working
     ref = _oracle_scores(w, noise)
     planner.set_warm_start_sequence(w.warm_start)
