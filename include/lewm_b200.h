@@ -341,16 +341,23 @@ lwm_status lwm_scorer_skyjepa_set_context_ex(lwm_scorer* scorer, uint32_t batch,
                                              const float* vehicle_mass);
 
 /* Arithmetic of the learned scorer's fused MPPI iterations.
- * LWM_PRECISION_F32 (default): the f32 CUDA-core rollout.
- * LWM_PRECISION_BF16: bf16 weights and recurrent state on the tcgen05 tensor
- * cores with f32 accumulation, f32 gates / prober tail / integrator, for
- * plans whose sample count is a multiple of 128 (latent 256, 4 actions,
- * 4-channel action encoder with kernel 3 over a 10-step history, prober
- * hidden 32); other shapes keep the f32 rollout.  Costs agree with f32
- * within about 2e-2 relative. */
+ * LWM_PRECISION_F32 (default): f32-class results.  For the model shape the
+ * tensor-core rollouts take (latent 256, 4 actions, 4-channel action encoder
+ * with kernel 3 over a 10-step history, prober hidden 32) and sample counts
+ * that are multiples of 128, the recurrent and prober-input GEMMs run on the
+ * tcgen05 tensor cores with every operand split into two fp16 halves and
+ * three partial products per product (about 22 significant bits, f32
+ * accumulation), gates / state / prober tail / integrator / cost in f32;
+ * other shapes run the f32 CUDA-core rollout.  Both match the f32 reference
+ * within 1e-4 relative.
+ * LWM_PRECISION_BF16: bf16 weights and recurrent state on the tensor cores
+ * with f32 accumulation, for the same shapes; costs agree with f32 within
+ * about 2e-2 relative (other shapes keep the f32 rollout).
+ * LWM_PRECISION_F32_CUDA_CORE: always the f32 CUDA-core rollout. */
 typedef enum lwm_precision {
     LWM_PRECISION_F32 = 0,
     LWM_PRECISION_BF16 = 1,
+    LWM_PRECISION_F32_CUDA_CORE = 2,
 } lwm_precision;
 lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* scorer, int32_t precision);
 /* Precision of the LeWM scorer's GEMMs (predictor, action embedder, pred_proj,

@@ -162,6 +162,8 @@ struct lwm_scorer {
     lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
     std::vector<float> action_tcn_host;  // the action encoder's weights, for kernel-parameter packing
     bool tc_ready = false;
+    DevBuf mma_packed;       // split-fp16 weights of the f32 tensor-core path (per CTA rank)
+    bool mma_ready = false;
 };
 
 struct lwm_planner {
@@ -479,6 +481,20 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint
     return LWM_OK;
 }
 
+lwm_status ensure_mma(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint32_t S, uint32_t T) {
+    LWM_TRY(ensure_side(sc));
+    if (!sc->mma_ready) {
+        LWM_TRY(sc->mma_packed.ensure(lwm::skyjepa_mma_packed_bytes()));
+        LWM_CUDA(lwm::skyjepa_mma_pack(a, sc->mma_packed.as<uint8_t>(), sc->ctx->stream));
+        sc->mma_ready = true;
+    }
+    LWM_TRY(sc->tc_err.ensure(256));
+    LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
+    LWM_TRY(sc->h0_work.ensure(lwm::skyjepa_h0_work_bytes(a, B)));
+    LWM_TRY(sc->tc_x.ensure(lwm::skyjepa_mma_xtile_bytes(B, S, T)));
+    return LWM_OK;
+}
+
 lwm_status ensure_side(lwm_scorer* sc) {
     if (sc->side.stream) return LWM_OK;
     LWM_CUDA(cudaStreamCreateWithFlags(&sc->side.stream, cudaStreamNonBlocking));
@@ -752,6 +768,19 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
                                                     sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
                                                     &launched, &sc->side));
+                } else if (sc->precision == LWM_PRECISION_F32 && lwm::skyjepa_mma_supported(a, &why) &&
+                           lwm::skyjepa_mma_fits_device()) {
+                    // f32-class accuracy on the tensor cores (split-fp16 operands)
+                    LWM_TRY(ensure_mma(sc, a, B, p->S, p->T));
+                    a.h0_work = sc->h0_work.as<float>();
+                    a.test_wait_polls = p->ctx->faults.wait_polls;
+                    a.m.P = lwm::skyjepa_mma_partials_per_vehicle(p->S);
+                    a.low_dev = low;
+                    a.high_dev = high;
+                    LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    LWM_CUDA(lwm::launch_skyjepa_mma(a, sc->mma_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
+                                                     sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
+                                                     &launched, &sc->side));
                 } else {
                     LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
                 }
@@ -1516,7 +1545,7 @@ lwm_status lwm_lewm_encode_pixels_device(lwm_scorer* s, const float* pixels, uin
 
 lwm_status lwm_scorer_skyjepa_set_precision(lwm_scorer* s, int32_t precision) {
     if (!s || s->kind != ScorerKind::Skyjepa) return fail(LWM_INVALID_ARGUMENT, "not a SkyJEPA scorer");
-    if (precision != LWM_PRECISION_F32 && precision != LWM_PRECISION_BF16)
+    if (precision != LWM_PRECISION_F32 && precision != LWM_PRECISION_BF16 && precision != LWM_PRECISION_F32_CUDA_CORE)
         return fail(LWM_INVALID_ARGUMENT, "unknown precision " + std::to_string(precision));
     std::lock_guard<std::mutex> lock(s->mu);
     s->precision = precision;
@@ -1574,6 +1603,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     if (s->staged) cudaEventDestroy(s->staged);
     s->weights.release();
     s->tc_packed.release();
+    s->mma_packed.release();
     s->tc_h0.release();
     s->h0_work.release();
     s->tc_err.release();

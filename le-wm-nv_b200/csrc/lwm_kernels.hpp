@@ -184,6 +184,17 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
                               cudaStream_t stream, int* launches, const SideStream* side = nullptr);
 size_t skyjepa_tc_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
 // Initial latent of every vehicle (state encoder + projection) into h0 [B, H].
+// Split-fp16 tensor-core path of the f32 learned scorer (kernels_skyjepa_mma.cu):
+// every GEMM operand as two fp16 halves and three partial products per
+// product, f32 gates / state / prober tail; one 16-CTA cluster per 128 rows.
+bool skyjepa_mma_supported(const SkyjepaArgs& a, const char** why);
+bool skyjepa_mma_fits_device();
+size_t skyjepa_mma_packed_bytes();
+cudaError_t skyjepa_mma_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
+uint32_t skyjepa_mma_partials_per_vehicle(uint32_t S);
+size_t skyjepa_mma_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
+cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
+                               cudaStream_t stream, int* launches, const SideStream* side);
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
 // Scratch for the history encoder run over many vehicles at once (used when
 // SkyjepaArgs::h0_work is set, B >= 32 and the history has 10 steps).

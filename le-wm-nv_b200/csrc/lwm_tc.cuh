@@ -58,6 +58,13 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// The same instruction with fp16 operands (the instruction descriptor names
+// the operand types).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    mma_bf16(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
 // The mbarrier gets one arrival once every tcgen05 op issued so far by this
 // thread has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {

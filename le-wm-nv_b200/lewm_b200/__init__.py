@@ -244,7 +244,7 @@ class LewmConfig(C.Structure):
 
 
 LEWM_NAMES = {"lewm": 0, "world_model": 1}
-PRECISIONS = {"f32": 0, "bf16": 1}
+PRECISIONS = {"f32": 0, "bf16": 1, "f32-cuda-core": 2}
 
 
 @dataclass(frozen=True)
@@ -738,7 +738,8 @@ class SkyJepaScorer(Scorer):
         _LIVE["scorer"].add(self)
 
     def set_precision(self, precision: str) -> None:
-        """"f32" (CUDA cores) or "bf16" (tcgen05 tensor cores where the shape allows)."""
+        """"f32" (split-fp16 tensor cores where the shape allows, else CUDA cores; f32-class results),
+        "bf16" (bf16 tensor cores where the shape allows) or "f32-cuda-core"."""
         _check(lib.lwm_scorer_skyjepa_set_precision(self.handle, PRECISIONS[precision]))
 
     def context_device(self):

@@ -17,9 +17,10 @@ def _norm(w):
     return (w.state_mean, w.state_std, w.action_mean, w.action_std)
 
 
-def _scorer(ctx, w):
+def _scorer(ctx, w, precision="f32"):
     sc = L.SkyJepaScorer(ctx, w.model, w.weights, w.state_mean, w.state_std, w.action_mean, w.action_std, w.cost,
                          w.dt)
+    sc.set_precision(precision)
     sc.set_context(w.state_history, w.action_history, w.reference_states, w.reference_actions)
     return sc
 
@@ -31,12 +32,18 @@ def _oracle(w):
     return m, c
 
 
-def test_skyjepa_mppi_matches_oracle_injected_noise(ctx):
+# "f32" takes the split-fp16 tensor-core rollout at this shape (4 launches:
+# sampling, inputs, h0, rollout); "f32-cuda-core" the fused CUDA-core kernel
+@pytest.mark.parametrize("precision, launches", [("f32", 4), ("f32-cuda-core", 1)])
+def test_skyjepa_mppi_matches_oracle_injected_noise(ctx, precision, launches):
     w = W.skyjepa(seed=1)
     noise = normals(300, (1, 1, 512, 15, 4))
     p = L.MppiPlanner(ctx, w.mppi)
     p.set_warm_start_sequence(w.warm_start)
-    r = p.plan(_scorer(ctx, w), injected_noise=noise)
+    sc = _scorer(ctx, w, precision)
+    n0 = ctx.launch_count()
+    r = p.plan(sc, injected_noise=noise)
+    assert ctx.launch_count() - n0 == launches
     m, c = _oracle(w)
     ref = O.mppi_plan(w.mppi, 1, (O.SKYJEPA_FN, c), noise=noise, warm_start=w.warm_start)
     assert_costs_close(r.scores, ref["scores"])
