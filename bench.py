@@ -53,6 +53,14 @@ ROLLOUT_DRAM_BYTES = {"skyjepa": 2178048 + 0}
 NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)
 
 
+def default_workload_config(kind: str, world: int) -> dict:
+    """The `config` both arms print for the default and nominal workloads
+    (the same seeded inputs, planner and model widths in both)."""
+    model = (", latent 256, TCN [128,128,128]/[4,4,4], prober 32x2" if kind == "skyjepa" else ", 10 rotor substeps")
+    return {"workload": f"{kind} MPPI, 1 vehicle per plan, 512 candidates x 15 steps, 1 iteration, seed 17" + model,
+            "parallelism": f"one vehicle per rank, replicas x{world}"}
+
+
 def percentile(values, q):
     """values[round((n-1) q)] of the sorted list (lewm-bench-skyjepa.rs:547-553)."""
     v = sorted(values)
@@ -255,11 +263,9 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded random-init weights, generated figure-eight references)",
-            "config": {"workload": f"{kind} MPPI, 1 vehicle per GPU, 512 candidates x 15 steps, 1 iteration"
-                                   + (", latent 256, TCN [128,128,128]/[4,4,4], prober 32x2" if kind == "skyjepa"
-                                      else ", 10 rotor substeps"),
-                       "parallelism": f"replicas x{world}",
-                       "l2": "flushed between steps (256 MiB write outside the timed region)"},
+            "config": default_workload_config(kind, world),
+            "timing": "CUDA events around each plan on the planner's stream; L2 flushed between steps "
+                      "(256 MiB write outside the timed region)",
             "candidate_steps_per_s": round(plans_per_s * cand_steps, 1),
             "latency_ms": {"p50": round(percentile(times, 0.5), 5), "p95": round(percentile(times, 0.95), 5),
                            "p99": round(percentile(times, 0.99), 5), "max": round(max(times), 5)},
@@ -1215,8 +1221,8 @@ def run_reference(args, rank, world):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded random-init weights, generated figure-eight references)",
-        "config": {"workload": f"{args.workload} MPPI, 1 vehicle, 512 candidates x 15 steps, 1 iteration",
-                   "parallelism": "host CPU"},
+        "config": default_workload_config(args.workload, world),
+        "timing": "wall clock around each full plan on the host cores",
         "candidate_steps_per_s": round(base["value"] * 512 * 15, 1),
         "latency_ms": base["latency_ms"],
         "cpu_baseline": base,

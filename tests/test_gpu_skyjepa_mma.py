@@ -46,14 +46,14 @@ def _plan(ctx, w, noise, masses=None):
     return r, p, sc
 
 
-@pytest.mark.parametrize("batch, samples, horizon", [(1, 512, 15), (2, 256, 7), (1, 128, 64)])
+@pytest.mark.parametrize("batch, samples, horizon", [(1, 512, 15), (2, 256, 7), (1, 128, 30)])
 def test_split_fp16_mppi_matches_oracle(ctx, batch, samples, horizon):
     w = W.skyjepa(seed=51, batch=batch, samples=samples, horizon=horizon)
     noise = normals(81, (1, batch, samples, horizon, 4))
     r, _, _ = _plan(ctx, w, noise)
     ref = _oracle_plan(w, noise)
     rel = np.abs(np.asarray(r.scores, np.float64) - ref["scores"]) / np.maximum(np.abs(ref["scores"]), 1e-6)
-    print(f"split-fp16 vs f32 oracle: worst {rel.max():.3e}")
+    print(f"split-fp16 vs f32 oracle: worst {rel.max():.3e}, mean {rel.mean():.3e}, cost range {ref['scores'].min():.4g}..{ref['scores'].max():.4g}")
     assert_costs_close(r.scores, ref["scores"])
     assert_actions_close(r.sequence, ref["sequence"])
     assert_same_argmin(r.best_indices, ref["best"], ref["scores"])
