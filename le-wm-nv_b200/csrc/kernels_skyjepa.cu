@@ -349,6 +349,60 @@ __device__ void state_tcn_cluster(const SkyjepaArgs& a, cg::cluster_group& clust
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// The history encoder alone: h0 of vehicle blockIdx.y by one 8-CTA cluster
+// (state_tcn_cluster, the rollout kernel's prologue, as a kernel of its own)
+// for the tensor-core rollouts of few vehicles with a wide state encoder.
+__global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_cluster_kernel(SkyjepaArgs a, float* h0,
+                                                                         uint32_t scratch_floats, uint32_t sw_half) {
+    extern __shared__ __align__(16) float smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t c = cluster.block_rank(), b = blockIdx.y;
+    float* scratch = smem;
+    float* sw = smem + scratch_floats;
+    float* h0v = sw + 2 * sw_half;
+    cluster.sync();  // every CTA of the cluster runs before any DSMEM access
+    if (a.Hs == 10 && a.state_tcn.k == 3) state_tcn_cluster<10, 3>(a, cluster, c, b, scratch, h0v, sw, sw_half);
+    else state_tcn_cluster<0, 0>(a, cluster, c, b, scratch, h0v, sw, sw_half);
+    cluster.sync();  // h0 complete in every CTA
+    if (c == 0)
+        for (uint32_t u = threadIdx.x; u < a.H; u += kThreads) h0[static_cast<size_t>(b) * a.H + u] = h0v[u];
+}
+
+cudaError_t launch_skyjepa_h0_cluster(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
+    const TcnView& tcn = a.state_tcn;
+    const uint32_t C = tcn.max_ch, Hs = a.Hs, K = tcn.k;
+    const uint32_t per = (C + kCluster - 1) / kCluster, ks = kThreads / per;
+    const uint32_t scratch = ((3 * C * Hs + ks * per * Hs + 8) + 3u) & ~3u;
+    uint32_t wmax = (a.H / kCluster) * (tcn.out_dim + 4);
+    uint32_t cin = tcn.input_dim;
+    for (uint32_t l = 0; l < tcn.levels; ++l) {
+        const uint32_t w1n = per * odd_stride(cin * K);
+        const uint32_t w2n = per * odd_stride(C * K) + (cin != C ? per * cin : 0);
+        wmax = w1n > wmax ? w1n : wmax;
+        wmax = w2n > wmax ? w2n : wmax;
+        cin = C;
+    }
+    const uint32_t sw_half = (wmax + 3u) & ~3u;
+    const size_t smem = (static_cast<size_t>(scratch) + 2 * sw_half + a.H) * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(skyjepa_h0_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kCluster, a.B, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, skyjepa_h0_cluster_kernel, a, h0, scratch, sw_half);
+}
+
 // SkyJepaModel::rollout_candidates window encoding (model.rs:192-215) with
 // TemporalConvEncoder::forward (tcn.rs:88-96, 138-160) over one window held
 // in `cur` [Cm][Hs] (input channels normalised, zero elsewhere): `ca` lanes of

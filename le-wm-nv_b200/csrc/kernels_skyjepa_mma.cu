@@ -21,8 +21,10 @@
 // W_hh plus rows 2c, 2c+1 of the prober's first layer; one step is
 //   D[128 x 80] = X_t . Bx^T                  (r | z | n_h | prober | n_x)
 //   D[:, 0:64] += H_t . Bh^T                   (K = 256, 16 K-slices)
-// then the GRU gates of the CTA's 16 units for the 128 rows, and the new h
-// slice (both fp16 halves) is stored into every CTA's A operand (DSMEM).
+// then the GRU gates of the CTA's 16 units for the 128 rows; the new h slice
+// (both fp16 halves) is written into the CTA's own A operand and bulk-copied
+// from there into every peer's (cp.async.bulk shared::cta -> shared::cluster,
+// completing on the peer's h_full barrier).
 // The A operand is 16 K-slices of [128 rows x 16] (SW32), so CTA c's units
 // are exactly one slice.  The prober's first layer for latent t comes out of
 // step t + 1's MMA (its A operand is h_{t+1}); each CTA sends its two hidden
@@ -88,7 +90,7 @@ struct __align__(1024) MmaSmem {
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
     float red_w[kOwnRows];
     uint64_t red_key[4];
-    uint64_t w_full, x_full[2], x_empty[2], h_full, a_free, mma_done[2], empty[2], pro_full[2], done;
+    uint64_t w_full, x_full[2], x_empty[2], h_full, a_free, mma_done[2], empty[2], pro_full[2], slice_ready, done;
     uint32_t tmem;
     int last;
 };
@@ -122,11 +124,6 @@ __device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
     return r;
-}
-__device__ __forceinline__ void st_peer_v4(uint32_t addr, uint4 v) {
-    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-                 "r"(v.w)
-                 : "memory");
 }
 __device__ __forceinline__ void st_peer_v2f(uint32_t addr, float a, float b) {
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
@@ -170,9 +167,16 @@ __device__ __forceinline__ void commit_multicast(uint64_t* bar, uint16_t mask) {
         "h"(mask)
         : "memory");
 }
-// Generic-proxy writes to cluster shared memory made visible to the tensor core.
-__device__ __forceinline__ void fence_async_cluster() {
-    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+// Bulk copy of `bytes` from this CTA's shared memory to a peer's (both
+// addresses 16-byte aligned, bytes a multiple of 16), completing as
+// transaction bytes on the peer's mbarrier `peer_bar`.
+__device__ __forceinline__ void bulk_to_peer(uint32_t peer_dst, uint32_t local_src, uint32_t bytes,
+                                             uint32_t peer_bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            peer_dst),
+        "r"(local_src), "r"(bytes), "r"(peer_bar)
+        : "memory");
 }
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -334,7 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             tc::mbar_init(&s.empty[i], 12);      // 8 gate warps + 4 prober warps release a slot
             tc::mbar_init(&s.pro_full[i], kRowsM);  // 8 own rows x 16 CTAs deliver per step
         }
-        tc::mbar_init(&s.h_full, 8 * kCl);  // 8 gate warps of every CTA deliver their slice
+        // h_t complete: the MMA issuer's arrival (with the 15 peer slices'
+        // bytes expected) and the 8 gate warps' own-slice arrivals
+        tc::mbar_init(&s.h_full, 9);
+        tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is written (sender may copy it)
         tc::mbar_init(&s.a_free, kCl);      // every CTA's MMAs of the step are done
         tc::mbar_init(&s.done, 1);
         tc::mbar_fence_init();
@@ -375,9 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             const uint32_t a_base = tc::smem_u32(s.A), w_base = tc::smem_u32(s.W);
             const uint32_t bx_base = w_base + kBhBytes;
             bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
+            tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
-                ok = wait_cluster(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
+                ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
+                // the next phase expects the 15 peer slices of h_{t+1} (both halves)
+                if (ok && t < T) tc::mbar_expect_tx(&s.h_full, (kCl - 1) * 2 * kSliceBytes);
                 if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
                 if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
@@ -443,10 +453,10 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         for (int i = 0; i < 8; ++i) hprev[i] = __ldg(h0 + c * kU + half * 8 + i);
         tc::fence_async_smem();
         __syncwarp();
-        // phase 0 of h_full: this CTA's own 8 warps stand in for the 16 CTAs
-        if (lane < kCl) tc::mbar_arrive(&s.h_full);
+        if (lane == 0) tc::mbar_arrive(&s.h_full);  // phase 0: h_0 written locally
         const uint32_t slice_off = c * kSliceBytes + tc::sw32_offset(row, half * 8);
         const uint32_t a_local = tc::smem_u32(s.A), hfull_local = tc::smem_u32(&s.h_full);
+        const bool sender = warp == kEpiWarp0 && lane == 0;
         bool ok = true;
         for (uint32_t t = 0; ok && t < T; ++t) {
             const uint32_t slot = t & 1u;
@@ -473,18 +483,32 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             uint32_t hi[4], lo[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) split2(hprev[2 * i], hprev[2 * i + 1], hi[i], lo[i]);
-            // every CTA's MMAs of step t have finished reading h_t
+            // every CTA's MMAs of step t are done reading h_t; so are the bulk
+            // copies of this CTA's slice of h_t to its peers (each peer's MMA
+            // waited for them), and the slice can be overwritten
             if (!(ok = wait_cluster(&s.a_free, t & 1u, err, 7, t, lim))) break;
-            const uint4 vh = make_uint4(hi[0], hi[1], hi[2], hi[3]), vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-#pragma unroll 4
-            for (uint32_t d = 0; d < kCl; ++d) {
-                const uint32_t base = peer_addr(a_local, d);
-                st_peer_v4(base + slice_off, vh);
-                st_peer_v4(base + kCl * kSliceBytes + slice_off, vl);
-            }
-            fence_async_cluster();
+            *reinterpret_cast<uint4*>(s.A + slice_off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(s.A + kCl * kSliceBytes + slice_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            tc::fence_async_smem();  // visible to the tensor core and the bulk-copy engine
             __syncwarp();
-            if (lane < kCl) arrive_peer(peer_addr(hfull_local, lane));
+            if (lane == 0) {
+                tc::mbar_arrive(&s.slice_ready);
+                tc::mbar_arrive(&s.h_full);
+            }
+            if (sender) {
+                // once the whole slice is written: the slice (both halves) to the 15 peers
+                ok = tc::mbar_wait(&s.slice_ready, t & 1u, err, 10, t, lim);
+                if (ok)
+                    for (uint32_t d = 1; d < kCl; ++d) {
+                        const uint32_t peer = (c + d) % kCl;
+                        const uint32_t dst = peer_addr(a_local, peer), bar = peer_addr(hfull_local, peer);
+                        for (uint32_t hh = 0; hh < 2; ++hh) {
+                            const uint32_t off = (hh * kCl + c) * kSliceBytes;
+                            bulk_to_peer(dst + off, a_local + off, kSliceBytes, bar);
+                        }
+                    }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
         failed = !ok;
     } else {

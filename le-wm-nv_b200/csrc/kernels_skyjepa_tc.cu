@@ -484,6 +484,9 @@ cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stre
     if (a.Hs > kH0MaxHist) return cudaErrorInvalidValue;
     if (a.h0_work && a.B >= kH0BatchedMinVehicles && a.Hs == kH0BatchedHist && a.state_tcn.k == 3)
         return launch_h0_batched(a, h0, stream);
+    // few vehicles, wide encoder: one 8-CTA cluster per vehicle (weights
+    // staged in shared memory, output channels split over the cluster)
+    if (a.state_tcn.max_ch >= 64) return launch_skyjepa_h0_cluster(a, h0, stream);
     const size_t h0_smem = static_cast<size_t>(a.state_tcn.max_ch) * a.Hs * 3 * sizeof(float);
     if (a.state_tcn.max_ch >= 64)
         skyjepa_h0_warp_kernel<<<a.B, 256, h0_smem, stream>>>(a, h0);

@@ -196,6 +196,8 @@ size_t skyjepa_mma_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
 cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
                                cudaStream_t stream, int* launches, const SideStream* side);
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
+// h0 of every vehicle by one 8-CTA cluster each (kernels_skyjepa.cu).
+cudaError_t launch_skyjepa_h0_cluster(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
 // Scratch for the history encoder run over many vehicles at once (used when
 // SkyjepaArgs::h0_work is set, B >= 32 and the history has 10 steps).
 size_t skyjepa_h0_work_bytes(const SkyjepaArgs& a, uint32_t B);
