@@ -64,18 +64,21 @@ constexpr uint32_t kH = 256;                 // latent
 constexpr uint32_t kU = kH / kCl;            // 16 hidden units per CTA
 constexpr uint32_t kOwnRows = kRowsM / kCl;  // 8 rows whose prober / cost a CTA finishes
 constexpr uint32_t kHid = 32;                // prober hidden width
-constexpr uint32_t kNh = 64;                 // h-part columns: r, z, n_h (16 each), prober (2 used)
-constexpr uint32_t kNx = 80;                 // x-part columns: + n_x
-constexpr uint32_t kColR = 0, kColZ = 16, kColNh = 32, kColP = 48, kColNx = 64;
-constexpr uint32_t kSlotCols = 128;          // TMEM columns per accumulator slot (80 used)
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kNh = 64;                 // gate columns: r, z, n_h (16 each), prober (2 used)
+// TMEM accumulator slot: columns [0, 64) the products with the weights' high
+// halves (and x1 w0, h1 w0), [64, 128) the products with their low halves
+// (x0 w1, h0 w1), [128, 144) / [144, 160) the same two for n_x; a gate's
+// pre-activation is the sum of its two columns
+constexpr uint32_t kColR = 0, kColZ = 16, kColNh = 32, kColP = 48, kColLo = 64, kColNx = 128, kColNxLo = 144;
+constexpr uint32_t kSlotCols = 256;
+constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSliceBytes = kRowsM * 32;        // one [128 x 16] fp16 K-slice, SW32: 4 KB
-constexpr uint32_t kABytes = 2 * kCl * kSliceBytes;  // two halves x 16 slices: 128 KB
-constexpr uint32_t kBhBlock = kNh * 128;             // one K-block of 64-element rows, SW128: 8 KB
-constexpr uint32_t kBhHalf = 4 * kBhBlock;           // K = 256: 32 KB
-constexpr uint32_t kBhBytes = 2 * kBhHalf;           // 64 KB
-constexpr uint32_t kBxHalf = kNx * 32;               // [80 x 16] SW32: 2.5 KB
-constexpr uint32_t kBxBytes = 2 * kBxHalf;
+constexpr uint32_t kSlicePair = 2 * kSliceBytes;     // a slice's two halves, adjacent: 8 KB
+constexpr uint32_t kABytes = kCl * kSlicePair;       // 16 slices x 2 halves: 128 KB
+constexpr uint32_t kBhBlock = 2 * kNh * 128;         // one K-block: [w0 rows; w1 rows] of 64 elements, SW128: 16 KB
+constexpr uint32_t kBhBytes = 4 * kBhBlock;          // K = 256: 64 KB
+constexpr uint32_t kBxRows = 2 * kNh + 2 * 16;       // [w0 main; w1 main; w0 n_x; w1 n_x]
+constexpr uint32_t kBxBytes = kBxRows * 32;          // SW32: 5 KB
 constexpr uint32_t kWBytes = kBhBytes + kBxBytes;    // the CTA's packed weights
 constexpr uint32_t kXTileBytes = 2 * kSliceBytes;    // one step's x tile, both halves: 8 KB
 constexpr int kThreads = 448;
@@ -83,8 +86,8 @@ constexpr uint32_t kEpiWarp0 = 2, kAuxWarp0 = 10, kAuxBarrier = 3, kAuxThreads =
 constexpr uint32_t kMaxLayers = 3;
 
 struct __align__(1024) MmaSmem {
-    uint8_t A[kABytes];            // h_t: [half][slice][128 x 16] fp16, SW32
-    uint8_t W[kWBytes];            // Bh [half][4 K-blocks][64 x 64] SW128, then Bx [half][80 x 16] SW32
+    uint8_t A[kABytes];            // h_t: [slice][half][128 x 16] fp16, SW32
+    uint8_t W[kWBytes];            // Bh [4 K-blocks][128 x 64] SW128, then Bx [160 x 16] SW32
     uint8_t X[2][kXTileBytes];     // x tiles of step t (double buffer), [half][128 x 16] SW32
     float pre[2][kOwnRows][kHid];  // prober first-layer sums of the own rows, by step parity
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
@@ -204,14 +207,17 @@ struct AccurateGelu {
 
 // ------------------------------------------------------- weight packing
 //
-// Per CTA rank c: Bh (two fp16 halves) — rows 0-15 W_hr, 16-31 W_hz, 32-47
-// W_hn of units 16c..16c+15, rows 48-49 the prober's first-layer rows 2c,
-// 2c+1, rows 50-63 zero — K-major SW128 in 4 K-blocks; then Bx (two halves):
-// rows 0-15 W_ir | b_ir + b_hr, 16-31 W_iz | b_iz + b_hz, 32-47 0 | b_hn,
-// 48-63 zero, 64-79 W_in | b_in (k < E the weight, k = E the bias), SW32.
+// Per CTA rank c: Bh — gate rows 0-15 W_hr, 16-31 W_hz, 32-47 W_hn of units
+// 16c..16c+15, rows 48-49 the prober's first-layer rows 2c, 2c+1, rows 50-63
+// zero; the high fp16 halves as operand rows 0-63 and the low halves as rows
+// 64-127, K-major SW128 in 4 K-blocks.  Then Bx — gate rows 0-15 W_ir |
+// b_ir + b_hr, 16-31 W_iz | b_iz + b_hz, 32-47 0 | b_hn, 48-63 zero, and the
+// n_x rows W_in | b_in (k < E the weight, k = E the bias): high halves of the
+// gate rows as operand rows 0-63, low halves 64-127, n_x high 128-143, low
+// 144-159, SW32.
 __global__ void pack_mma_weights_kernel(SkyjepaArgs a, uint8_t* packed) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t n_h = kCl * kNh * kH, n_x = kCl * kNx * 16;
+    const uint32_t n_h = kCl * kNh * kH, n_x = kCl * (kNh + 16) * 16;
     uint32_t hi, lo;
     if (i < n_h) {
         const uint32_t c = i / (kNh * kH), rem = i % (kNh * kH), j = rem / kH, k = rem % kH;
@@ -223,12 +229,12 @@ __global__ void pack_mma_weights_kernel(SkyjepaArgs a, uint8_t* packed) {
             v = a.p_in_w[static_cast<size_t>(2 * c + (j - 48)) * kH + k];
         }
         split2(v, 0.0f, hi, lo);
-        uint8_t* base = packed + static_cast<size_t>(c) * kWBytes;
-        const uint32_t off = (k >> 6) * kBhBlock + tc::sw128_offset(j, k & 63u);
-        *reinterpret_cast<uint16_t*>(base + off) = static_cast<uint16_t>(hi & 0xffffu);
-        *reinterpret_cast<uint16_t*>(base + kBhHalf + off) = static_cast<uint16_t>(lo & 0xffffu);
+        uint8_t* base = packed + static_cast<size_t>(c) * kWBytes + (k >> 6) * kBhBlock;
+        *reinterpret_cast<uint16_t*>(base + tc::sw128_offset(j, k & 63u)) = static_cast<uint16_t>(hi & 0xffffu);
+        *reinterpret_cast<uint16_t*>(base + tc::sw128_offset(kNh + j, k & 63u)) = static_cast<uint16_t>(lo & 0xffffu);
     } else if (i < n_h + n_x) {
-        const uint32_t q = i - n_h, c = q / (kNx * 16), rem = q % (kNx * 16), j = rem / 16, k = rem % 16;
+        const uint32_t q = i - n_h, c = q / ((kNh + 16) * 16), rem = q % ((kNh + 16) * 16), j = rem / 16,
+                       k = rem % 16;
         const uint32_t grp = j / kU, u = c * kU + j % kU;
         float v = 0.0f;
         if (k < a.E) {
@@ -242,9 +248,9 @@ __global__ void pack_mma_weights_kernel(SkyjepaArgs a, uint8_t* packed) {
         }
         split2(v, 0.0f, hi, lo);
         uint8_t* base = packed + static_cast<size_t>(c) * kWBytes + kBhBytes;
-        const uint32_t off = tc::sw32_offset(j, k);
-        *reinterpret_cast<uint16_t*>(base + off) = static_cast<uint16_t>(hi & 0xffffu);
-        *reinterpret_cast<uint16_t*>(base + kBxHalf + off) = static_cast<uint16_t>(lo & 0xffffu);
+        const uint32_t rhi = j < kNh ? j : 2 * kNh + (j - kNh), rlo = rhi + (j < kNh ? kNh : 16u);
+        *reinterpret_cast<uint16_t*>(base + tc::sw32_offset(rhi, k)) = static_cast<uint16_t>(hi & 0xffffu);
+        *reinterpret_cast<uint16_t*>(base + tc::sw32_offset(rlo, k)) = static_cast<uint16_t>(lo & 0xffffu);
     }
 }
 
@@ -378,45 +384,45 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
     } else if (warp == 1) {
         // ================= MMA issuer
         if (lane == 0) {
-            const uint32_t id_x = idesc_f16_f32(kRowsM, kNx), id_h = idesc_f16_f32(kRowsM, kNh);
-            const uint32_t a_base = tc::smem_u32(s.A), w_base = tc::smem_u32(s.W);
-            const uint32_t bx_base = w_base + kBhBytes;
+            const uint32_t id128 = idesc_f16_f32(kRowsM, 2 * kNh), id64 = idesc_f16_f32(kRowsM, kNh);
+            const uint32_t id32 = idesc_f16_f32(kRowsM, 32), id16 = idesc_f16_f32(kRowsM, 16);
+            const uint32_t w_base = tc::smem_u32(s.W);
+            // descriptors of the operand bases; an offset of n bytes adds n >> 4
+            // to the start-address field (all addresses below 256 KB)
+            const uint64_t da = tc::smem_desc(tc::smem_u32(s.A), 16, 256, tc::kSwizzle32);
+            const uint64_t dbh = tc::smem_desc(w_base, 16, 1024, tc::kSwizzle128);
+            const uint64_t dbx = tc::smem_desc(w_base + kBhBytes, 16, 256, tc::kSwizzle32);
             bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
             tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
                 ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
                 // the next phase expects the 15 peer slices of h_{t+1} (both halves)
-                if (ok && t < T) tc::mbar_expect_tx(&s.h_full, (kCl - 1) * 2 * kSliceBytes);
+                if (ok && t < T) tc::mbar_expect_tx(&s.h_full, (kCl - 1) * kSlicePair);
                 if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
                 if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
                 tc::fence_after();
                 const uint32_t d = tmem + slot * kSlotCols;
+                // split products: v0 [w0; w1] (both columns halves at once, N = 128)
+                // and v1 w0 (N = 64), for x and for every K-slice of h
                 uint32_t acc = 0;
                 if (t < T) {
-                    const uint32_t x_base = tc::smem_u32(s.X[slot]);
-                    // the three split products x0 w0, x0 w1, x1 w0
-#pragma unroll
-                    for (uint32_t q = 0; q < 3; ++q) {
-                        const uint32_t ha = q == 2 ? 1u : 0u, hb = q == 1 ? 1u : 0u;
-                        tc::mma_f16(d, tc::smem_desc(x_base + ha * kSliceBytes, 16, 256, tc::kSwizzle32),
-                                    tc::smem_desc(bx_base + hb * kBxHalf, 16, 256, tc::kSwizzle32), id_x, acc);
-                        acc = 1;
-                    }
+                    const uint64_t dx = tc::smem_desc(tc::smem_u32(s.X[slot]), 16, 256, tc::kSwizzle32);
+                    constexpr uint64_t x1 = kSliceBytes >> 4, nx = (2 * kNh * 32) >> 4;
+                    tc::mma_f16(d, dx, dbx, id128, 0);
+                    tc::mma_f16(d, dx + x1, dbx, id64, 1);
+                    tc::mma_f16(d + kColNx, dx, dbx + nx, id32, 0);
+                    tc::mma_f16(d + kColNx, dx + x1, dbx + nx, id16, 1);
+                    acc = 1;
                 }
-                for (uint32_t j = 0; j < kCl; ++j) {
-                    const uint32_t kb = j >> 2, jj = j & 3u;
 #pragma unroll
-                    for (uint32_t q = 0; q < 3; ++q) {
-                        const uint32_t ha = q == 2 ? 1u : 0u, hb = q == 1 ? 1u : 0u;
-                        tc::mma_f16(d,
-                                    tc::smem_desc(a_base + (ha * kCl + j) * kSliceBytes, 16, 256, tc::kSwizzle32),
-                                    tc::smem_desc(w_base + hb * kBhHalf + kb * kBhBlock + jj * 32, 16, 1024,
-                                                  tc::kSwizzle128),
-                                    id_h, acc);
-                        acc = 1;
-                    }
+                for (uint32_t j = 0; j < kCl; ++j) {
+                    const uint64_t a0 = da + ((j * kSlicePair) >> 4), a1 = a0 + (kSliceBytes >> 4);
+                    const uint64_t b = dbh + (((j >> 2) * kBhBlock + (j & 3u) * 32) >> 4);
+                    tc::mma_f16(d, a0, b, id128, acc);
+                    tc::mma_f16(d, a1, b, id64, 1);
+                    acc = 1;
                 }
                 tc::commit(&s.mma_done[slot]);
                 if (t < T) {
@@ -444,9 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) split2(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
-                const uint32_t off = j * kSliceBytes + tc::sw32_offset(row, k8);
+                const uint32_t off = j * kSlicePair + tc::sw32_offset(row, k8);
                 *reinterpret_cast<uint4*>(s.A + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(s.A + kCl * kSliceBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4*>(s.A + kSliceBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
         float hprev[8];
 #pragma unroll
@@ -454,21 +460,33 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         tc::fence_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&s.h_full);  // phase 0: h_0 written locally
-        const uint32_t slice_off = c * kSliceBytes + tc::sw32_offset(row, half * 8);
+        const uint32_t slice_off = c * kSlicePair + tc::sw32_offset(row, half * 8);
         const uint32_t a_local = tc::smem_u32(s.A), hfull_local = tc::smem_u32(&s.h_full);
-        const bool sender = warp == kEpiWarp0 && lane == 0;
+        // this warp bulk-copies the CTA's slice to peers c + 2w + 1 and c + 2w + 2
+        const uint32_t wi = warp - kEpiWarp0;
         bool ok = true;
         for (uint32_t t = 0; ok && t < T; ++t) {
             const uint32_t slot = t & 1u;
             if (!(ok = tc::mbar_wait(&s.mma_done[slot], (t >> 1) & 1u, err, 6, t, lim))) break;
             tc::fence_after();
             const uint32_t col = lane_base + slot * kSlotCols + half * 8;
-            float r[8], z[8], nh[8], nx[8];
+            float r[8], z[8], nh[8], nx[8], r1[8], z1[8], nh1[8], nx1[8];
             tc::tmem_ld8(col + kColR, r);
             tc::tmem_ld8(col + kColZ, z);
             tc::tmem_ld8(col + kColNh, nh);
             tc::tmem_ld8(col + kColNx, nx);
+            tc::tmem_ld8(col + kColLo + kColR, r1);
+            tc::tmem_ld8(col + kColLo + kColZ, z1);
+            tc::tmem_ld8(col + kColLo + kColNh, nh1);
+            tc::tmem_ld8(col + kColNxLo, nx1);
             tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                r[i] += r1[i];
+                z[i] += z1[i];
+                nh[i] += nh1[i];
+                nx[i] += nx1[i];
+            }
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s.empty[slot]);
@@ -488,24 +506,22 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             // waited for them), and the slice can be overwritten
             if (!(ok = wait_cluster(&s.a_free, t & 1u, err, 7, t, lim))) break;
             *reinterpret_cast<uint4*>(s.A + slice_off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(s.A + kCl * kSliceBytes + slice_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4*>(s.A + kSliceBytes + slice_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             tc::fence_async_smem();  // visible to the tensor core and the bulk-copy engine
             __syncwarp();
             if (lane == 0) {
                 tc::mbar_arrive(&s.slice_ready);
                 tc::mbar_arrive(&s.h_full);
             }
-            if (sender) {
-                // once the whole slice is written: the slice (both halves) to the 15 peers
+            if (lane == 0) {
+                // once the whole slice is written: both halves (8 KB, contiguous)
+                // to this warp's two peers
                 ok = tc::mbar_wait(&s.slice_ready, t & 1u, err, 10, t, lim);
                 if (ok)
-                    for (uint32_t d = 1; d < kCl; ++d) {
+                    for (uint32_t d = 2 * wi + 1; d <= 2 * wi + 2 && d < kCl; ++d) {
                         const uint32_t peer = (c + d) % kCl;
-                        const uint32_t dst = peer_addr(a_local, peer), bar = peer_addr(hfull_local, peer);
-                        for (uint32_t hh = 0; hh < 2; ++hh) {
-                            const uint32_t off = (hh * kCl + c) * kSliceBytes;
-                            bulk_to_peer(dst + off, a_local + off, kSliceBytes, bar);
-                        }
+                        bulk_to_peer(peer_addr(a_local, peer) + c * kSlicePair, a_local + c * kSlicePair, kSlicePair,
+                                     peer_addr(hfull_local, peer));
                     }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -533,9 +549,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             ok = aux_all(tc::mbar_wait(&s.mma_done[slot], (m >> 1) & 1u, err, 8, m, lim));
             if (!ok) break;
             tc::fence_after();
-            float v[8];
+            float v[8], v1[8];
             tc::tmem_ld8(lane_base + slot * kSlotCols + kColP, v);
+            tc::tmem_ld8(lane_base + slot * kSlotCols + kColLo + kColP, v1);
             tc::tmem_ld_wait();
+            v[0] += v1[0];
+            v[1] += v1[1];
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s.empty[slot]);
@@ -734,7 +753,7 @@ bool skyjepa_mma_supported(const SkyjepaArgs& a, const char** why) {
 size_t skyjepa_mma_packed_bytes() { return static_cast<size_t>(kCl) * kWBytes; }
 
 cudaError_t skyjepa_mma_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream) {
-    const uint32_t n = kCl * kNh * kH + kCl * kNx * 16;
+    const uint32_t n = kCl * kNh * kH + kCl * (kNh + 16) * 16;
     pack_mma_weights_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a, packed);
     return cudaGetLastError();
 }
