@@ -24,8 +24,7 @@
 // then the GRU gates of the CTA's 16 units for the 128 rows; the new h slice
 // (both fp16 halves) is written into the CTA's own A operand and bulk-copied
 // from there into every peer's (cp.async.bulk shared::cta -> shared::cluster,
-// completing on the peer's barrier of that slice); the next step's MMAs
-// start on each K-slice as soon as it is in place.
+// completing on the peer's h_full barrier).
 // The A operand is 16 K-slices of [128 rows x 16] (SW32), so CTA c's units
 // are exactly one slice.  The prober's first layer for latent t comes out of
 // step t + 1's MMA (its A operand is h_{t+1}); each CTA sends its two hidden
@@ -94,8 +93,7 @@ struct __align__(1024) MmaSmem {
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
     float red_w[kOwnRows];
     uint64_t red_key[4];
-    uint64_t w_full, x_full[2], x_empty[2], h0_ready, a_free, mma_done[2], empty[2], pro_full[2], slice_ready, done;
-    uint64_t slice_full[kCl];  // K-slice j of h_{t+1} is in A: phase t
+    uint64_t w_full, x_full[2], x_empty[2], h_full, a_free, mma_done[2], empty[2], pro_full[2], slice_ready, done;
     uint32_t tmem;
     int last;
 };
@@ -346,12 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             tc::mbar_init(&s.empty[i], 12);      // 8 gate warps + 4 prober warps release a slot
             tc::mbar_init(&s.pro_full[i], kRowsM);  // 8 own rows x 16 CTAs deliver per step
         }
-        tc::mbar_init(&s.h0_ready, 8);     // the 8 gate warps wrote h_0 into every slice
-        tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is written (the copies may go)
-        // slice j of h_{t+1}: the own slice by the 8 gate warps; a peer's by
-        // the MMA issuer's expect-tx arrival and the peer's 8 KB copy
-        const uint32_t me = cluster_rank();
-        for (uint32_t j = 0; j < kCl; ++j) tc::mbar_init(&s.slice_full[j], j == me ? 8 : 1);
+        // h_t complete: the MMA issuer's arrival (with the 15 peer slices'
+        // bytes expected) and the 8 gate warps' own-slice arrivals
+        tc::mbar_init(&s.h_full, 9);
+        tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is written (sender may copy it)
         tc::mbar_init(&s.a_free, kCl);      // every CTA's MMAs of the step are done
         tc::mbar_init(&s.done, 1);
         tc::mbar_fence_init();
@@ -397,14 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             const uint64_t dbh = tc::smem_desc(w_base, 16, 1024, tc::kSwizzle128);
             const uint64_t dbx = tc::smem_desc(w_base + kBhBytes, 16, 256, tc::kSwizzle32);
             bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
+            tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
-                if (t == 0) {
-                    ok = tc::mbar_wait(&s.h0_ready, 0, err, 3, 0, lim);  // A holds h_0
-                    // phase 0 of every peer slice: 8 KB of h_1 from that peer
-                    for (uint32_t j = 0; ok && j < kCl; ++j)
-                        if (j != c) tc::mbar_expect_tx(&s.slice_full[j], kSlicePair);
-                }
+                ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
+                // the next phase expects the 15 peer slices of h_{t+1} (both halves)
+                if (ok && t < T) tc::mbar_expect_tx(&s.h_full, (kCl - 1) * kSlicePair);
                 if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
                 if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
@@ -422,22 +416,14 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     tc::mma_f16(d + kColNx, dx + x1, dbx + nx, id16, 1);
                     acc = 1;
                 }
-                // K-slices in the order they tend to arrive (the own slice first),
-                // each as soon as it is in A
-                for (uint32_t jj = 0; ok && jj < kCl; ++jj) {
-                    const uint32_t j = (c + jj) & (kCl - 1u);
-                    if (t > 0) {
-                        if (!(ok = tc::mbar_wait(&s.slice_full[j], (t - 1u) & 1u, err, 3, t, lim))) break;
-                        if (j != c && t < T) tc::mbar_expect_tx(&s.slice_full[j], kSlicePair);  // for h_{t+1}
-                        tc::fence_after();
-                    }
+#pragma unroll
+                for (uint32_t j = 0; j < kCl; ++j) {
                     const uint64_t a0 = da + ((j * kSlicePair) >> 4), a1 = a0 + (kSliceBytes >> 4);
                     const uint64_t b = dbh + (((j >> 2) * kBhBlock + (j & 3u) * 32) >> 4);
                     tc::mma_f16(d, a0, b, id128, acc);
                     tc::mma_f16(d, a1, b, id64, 1);
                     acc = 1;
                 }
-                if (!ok) break;
                 tc::commit(&s.mma_done[slot]);
                 if (t < T) {
                     commit_multicast(&s.a_free, 0xFFFFu);  // every CTA learns this CTA is done reading h_t
@@ -473,9 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         for (int i = 0; i < 8; ++i) hprev[i] = __ldg(h0 + c * kU + half * 8 + i);
         tc::fence_async_smem();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&s.h0_ready);
+        if (lane == 0) tc::mbar_arrive(&s.h_full);  // phase 0: h_0 written locally
         const uint32_t slice_off = c * kSlicePair + tc::sw32_offset(row, half * 8);
-        const uint32_t a_local = tc::smem_u32(s.A), sfull_local = tc::smem_u32(&s.slice_full[c]);
+        const uint32_t a_local = tc::smem_u32(s.A), hfull_local = tc::smem_u32(&s.h_full);
         // this warp bulk-copies the CTA's slice to peers c + 2w + 1 and c + 2w + 2
         const uint32_t wi = warp - kEpiWarp0;
         bool ok = true;
@@ -525,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             __syncwarp();
             if (lane == 0) {
                 tc::mbar_arrive(&s.slice_ready);
-                tc::mbar_arrive(&s.slice_full[c]);
+                tc::mbar_arrive(&s.h_full);
             }
             if (lane == 0) {
                 // once the whole slice is written: both halves (8 KB, contiguous)
@@ -535,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     for (uint32_t d = 2 * wi + 1; d <= 2 * wi + 2 && d < kCl; ++d) {
                         const uint32_t peer = (c + d) % kCl;
                         bulk_to_peer(peer_addr(a_local, peer) + c * kSlicePair, a_local + c * kSlicePair, kSlicePair,
-                                     peer_addr(sfull_local, peer));
+                                     peer_addr(hfull_local, peer));
                     }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
