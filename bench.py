@@ -44,10 +44,13 @@ FLOP_PER_CANDIDATE_STEP = {
     "nominal": 10 * 262 + 60,
 }
 FLOP_PER_CANDIDATE_STEP["fleet"] = FLOP_PER_CANDIDATE_STEP["skyjepa"]
-# DRAM bytes of one rollout launch of the default workload (512 x 15, latent
-# 256), from the ncu capture summarised under profiles/: the weight blob read
-# once, nothing written back but the scores and the MPPI tuple
-ROLLOUT_DRAM_BYTES = {"skyjepa": 2178048 + 0}
+# The rollout kernel's share: everything above but the action TCN, which the
+# input kernel ahead of it evaluates.
+ROLLOUT_FLOP_PER_CANDIDATE_STEP = 2 * (4 * 768 + 256 * 768 + 256 * 32 + 32 * 32 + 32 * 15) + 200
+# DRAM bytes (read + write) of one rollout launch of the default workload
+# (512 x 15, latent 256, split-fp16 tensor-core kernel), from an ncu capture
+# of that launch: weights, x tiles and the per-step h exchange buffer.
+ROLLOUT_DRAM_BYTES = {"skyjepa": None}
 
 
 NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)
@@ -218,6 +221,17 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
 
+    # ---- the dominant kernel alone (for the roofline): CUDA events the
+    # library records on its stream around the rollout launch, same loop
+    kernel_ms = []
+    if kind == "skyjepa":
+        ctx.set_kernel_timing(True)
+        for _ in range(args.steps):
+            flush_l2()
+            planner.plan_device(sc)
+            kernel_ms.append(ctx.kernel_time_ms())
+        ctx.set_kernel_timing(False)
+
     # ---- end to end through the public ABI (host context in, host result out)
     e2e_times = []
     for _ in range(args.warmup):
@@ -232,9 +246,6 @@ def run_ours(args, rank, world, local_rank):
         e2e_times.append((time.perf_counter() - t0) * 1e3)
     d2h = 4 * (w.batch * 4 + w.batch * T * 4 + w.batch * S + w.batch)
 
-    # ---- dominant kernel alone (for the roofline): the rollout kernel is
-    # timed as the plan minus the context kernel by the ncu share; here the
-    # plan time bounds it from above.
     total_ms = sum(times)
     stats = torch.tensor([total_ms, float(np.mean(e2e_times))], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -246,9 +257,32 @@ def run_ours(args, rank, world, local_rank):
         plans_per_s = world * args.steps / (total_ms * 1e-3)
         e2e_plans_per_s = world * 1e3 / e2e_mean
         peaks = measured_peaks()
-        sgemm = sgemm_peak_tflops(torch)
-        flop = FLOP_PER_CANDIDATE_STEP[kind] * cand_steps
-        achieved = flop / (percentile(times, 0.5) * 1e-3) / 1e12
+        if kind == "skyjepa":
+            # the split-fp16 tensor-core rollout: FLOP of the model (not the
+            # three fp16 products each f32 MAC takes) over its mean device time
+            kmean = float(np.mean(kernel_ms))
+            flop = ROLLOUT_FLOP_PER_CANDIDATE_STEP * cand_steps
+            achieved = flop / (kmean * 1e-3) / 1e12
+            peak = float(peaks.get("bf16_tflops") or 1590.0)
+            roofline = {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1),
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 5),
+                        "traffic": ROLLOUT_DRAM_BYTES.get(kind),
+                        "kernel": "skyjepa_mma_kernel (split-fp16 tcgen05 GRU rollout, 4 clusters x 16 CTAs)",
+                        "kernel_ms": {"mean": round(kmean, 5), "p50": round(percentile(kernel_ms, 0.5), 5)},
+                        "kernel_share_of_plan": round(kmean / float(np.mean(times)), 3),
+                        "peak_source": ("MEASURED_PEAKS bf16_tflops burst (of measured)" if peaks.get("bf16_tflops")
+                                        else "1.59 PFLOP/s bf16 (of fallback)"),
+                        "note": "achieved = model FLOP of the rollout (GRU, prober, integrator, cost) per launch / "
+                                "mean CUDA-event launch time; the f32-class split executes 3 fp16 products per MAC "
+                                "and the 15-step recurrence on 128-row tiles is latency-bound, not throughput-bound"}
+        else:
+            sgemm = sgemm_peak_tflops(torch)
+            flop = FLOP_PER_CANDIDATE_STEP[kind] * cand_steps
+            achieved = flop / (percentile(times, 0.5) * 1e-3) / 1e12
+            roofline = {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2),
+                        "unit": "TFLOP/s", "frac": round(achieved / sgemm, 4), "traffic": None,
+                        "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
+                        "note": "achieved = algorithmic FLOP per plan / p50 plan time (one fused kernel)"}
         result = {
             "metric": "plan steps/s (one plan of 512 candidates x 15 steps per step); candidate-steps/s and "
                       "p50/p95 plan latency alongside",
@@ -274,14 +308,7 @@ def run_ours(args, rank, world, local_rank):
                     "latency_ms": {"p50": round(percentile(e2e_times, 0.5), 5),
                                    "p95": round(percentile(e2e_times, 0.95), 5)}},
             "gpu_launches": int(launches * args.steps),
-            "roofline": {"bound": "fp32", "achieved": round(achieved, 3), "peak": round(sgemm, 2),
-                         "unit": "TFLOP/s", "frac": round(achieved / sgemm, 4),
-                         "traffic": ROLLOUT_DRAM_BYTES.get(kind),
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the "
-                                           "same workload (cold cache), profiles/skyjepa_rollout_f32_512x15.md"
-                                           if kind in ROLLOUT_DRAM_BYTES else None,
-                         "peak_source": "cuBLAS SGEMM 8192^3 (TF32 off) measured in this run",
-                         "note": "achieved = algorithmic FLOP per plan / p50 plan time (both kernels)"},
+            "roofline": roofline,
             "clocks": clocks.summary(),
         }
         if args.cpu_baseline and world == 1:
@@ -840,7 +867,7 @@ def cpu_baseline_lewm(w, image: bool, budget_s: float):
 
 # DRAM bytes (read + write) of one staged-kernel launch at 32 full-HD frames,
 # f32 output, from a one-pass ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum); profiles/media_nv12_staged_fullhd.md.  The writes
+# dram__bytes_write.sum) of that launch.  The writes
 # fall short of the output size by what is still in the L2 when the kernel ends.
 MEDIA_DRAM_BYTES = {("nv12", False, 32): 101.31e6 + 736.08e6, ("rgb", False, 32): 202.08e6 + 736.31e6}
 
@@ -927,7 +954,7 @@ def run_media(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": MEDIA_DRAM_BYTES.get((fmt, bf16, B)),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the same "
-                                       "workload, profiles/media_nv12_staged_fullhd.md",
+                                       "workload",
                      "peak_source": "MEASURED_PEAKS hbm_gbs (of measured)",
                      "note": f"achieved = ({channels} B of {fmt.upper()} read + output bytes written) per pixel "
                              "/ p50 time"},

@@ -67,6 +67,14 @@ lwm_status lwm_ctx_stream(lwm_ctx* ctx, void** stream_out);
 lwm_status lwm_ctx_synchronize(lwm_ctx* ctx);
 /* Number of kernels this library has launched on the context so far. */
 lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out);
+/* Device time of the rollout kernel (the dominant kernel of a SkyJEPA plan),
+ * for measurement; no counterpart in the reference.  While on, every
+ * SkyJEPA plan on the context records two CUDA events on its stream around
+ * the rollout launch; lwm_ctx_kernel_time_ms waits for the later one and
+ * returns the milliseconds between them for the most recent plan
+ * (LWM_INVALID_ARGUMENT while off or before the first timed launch). */
+lwm_status lwm_ctx_set_kernel_timing(lwm_ctx* ctx, int on);
+lwm_status lwm_ctx_kernel_time_ms(lwm_ctx* ctx, float* ms_out);
 
 /* Fault injection for tests of the failure paths (no counterpart in the
  * reference, whose only failure path is the planning deadline,

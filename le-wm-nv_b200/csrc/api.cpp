@@ -123,6 +123,16 @@ struct lwm_ctx {
     int* media_err = nullptr;
     int* media_err_dev = nullptr;
     lwm_test_faults faults{};  // fault injection for tests (lwm_ctx_set_test_faults)
+    // kernel timing (lwm_ctx_set_kernel_timing): events around the last
+    // SkyJEPA rollout launch
+    cudaEvent_t kt_begin = nullptr, kt_end = nullptr;
+    bool kt_on = false, kt_valid = false;
+    void kernel_timing(lwm::SkyjepaArgs& a) {
+        if (!kt_on) return;
+        a.time_begin = kt_begin;
+        a.time_end = kt_end;
+        kt_valid = true;
+    }
 };
 
 enum class PlannerKind { Mppi, Cem, Icem };
@@ -163,6 +173,7 @@ struct lwm_scorer {
     std::vector<float> action_tcn_host;  // the action encoder's weights, for kernel-parameter packing
     bool tc_ready = false;
     DevBuf mma_packed;       // split-fp16 weights of the f32 tensor-core path (per CTA rank)
+    DevBuf mma_xchg;         // its per-step h exchange between the CTAs of a cluster
     bool mma_ready = false;
 };
 
@@ -492,6 +503,7 @@ lwm_status ensure_mma(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uin
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
     LWM_TRY(sc->h0_work.ensure(lwm::skyjepa_h0_work_bytes(a, B)));
     LWM_TRY(sc->tc_x.ensure(lwm::skyjepa_mma_xtile_bytes(B, S, T)));
+    LWM_TRY(sc->mma_xchg.ensure(lwm::skyjepa_mma_exchange_bytes(B, S)));
     return LWM_OK;
 }
 
@@ -765,6 +777,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     a.low_dev = low;
                     a.high_dev = high;
                     LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
                                                     sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
                                                     &launched, &sc->side));
@@ -778,10 +791,13 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     a.low_dev = low;
                     a.high_dev = high;
                     LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa_mma(a, sc->mma_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
-                                                     sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
+                                                     sc->tc_x.as<uint8_t>(), sc->mma_xchg.as<uint8_t>(),
+                                                     sc->tc_err.as<int>(), stream,
                                                      &launched, &sc->side));
                 } else {
+                    p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
                 }
                 p->ctx->launches += static_cast<uint64_t>(launched);
@@ -1008,6 +1024,8 @@ lwm_status lwm_ctx_destroy(lwm_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     cudaStreamDestroy(ctx->stream);
     if (ctx->media_err) cudaFreeHost(ctx->media_err);
+    if (ctx->kt_begin) cudaEventDestroy(ctx->kt_begin);
+    if (ctx->kt_end) cudaEventDestroy(ctx->kt_end);
     delete ctx;
     return LWM_OK;
 }
@@ -1042,6 +1060,27 @@ lwm_status lwm_ctx_set_test_faults(lwm_ctx* ctx, const lwm_test_faults* faults) 
 lwm_status lwm_ctx_launch_count(lwm_ctx* ctx, uint64_t* out) {
     if (!ctx || !out) return fail(LWM_INVALID_ARGUMENT, "null argument");
     *out = ctx->launches.load();
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_set_kernel_timing(lwm_ctx* ctx, int on) {
+    if (!ctx) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    if (on && !ctx->kt_begin) {
+        LWM_CUDA(cudaEventCreate(&ctx->kt_begin));
+        LWM_CUDA(cudaEventCreate(&ctx->kt_end));
+    }
+    ctx->kt_on = on != 0;
+    ctx->kt_valid = false;
+    return LWM_OK;
+}
+
+lwm_status lwm_ctx_kernel_time_ms(lwm_ctx* ctx, float* ms_out) {
+    if (!ctx || !ms_out) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (!ctx->kt_on || !ctx->kt_valid) return fail(LWM_INVALID_ARGUMENT, "no rollout launch timed");
+    LWM_CUDA(cudaSetDevice(ctx->device));
+    LWM_CUDA(cudaEventSynchronize(ctx->kt_end));
+    LWM_CUDA(cudaEventElapsedTime(ms_out, ctx->kt_begin, ctx->kt_end));
     return LWM_OK;
 }
 
@@ -1604,6 +1643,7 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->weights.release();
     s->tc_packed.release();
     s->mma_packed.release();
+    s->mma_xchg.release();
     s->tc_h0.release();
     s->h0_work.release();
     s->tc_err.release();

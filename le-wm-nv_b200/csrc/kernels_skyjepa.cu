@@ -1239,7 +1239,9 @@ cudaError_t launch_skyjepa_small(const SkyjepaArgs& a, float* h0, float* x, cuda
 
 cudaError_t launch_skyjepa(const SkyjepaArgs& a, cudaStream_t stream, int* launches) {
     if (a.rows % kCluster != 0 || a.rows < 32 || a.rows > kMaxRowsPerCta * kCluster) return cudaErrorInvalidValue;
+    if (a.time_begin) cudaEventRecord(a.time_begin, stream);
     const cudaError_t e = (a.H == 256) ? launch_rollout<256>(a, stream) : launch_rollout<128>(a, stream);
+    if (a.time_end) cudaEventRecord(a.time_end, stream);
     if (launches) *launches = 1;
     return e;
 }

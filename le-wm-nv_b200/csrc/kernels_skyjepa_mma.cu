@@ -22,9 +22,10 @@
 //   D[128 x 80] = X_t . Bx^T                  (r | z | n_h | prober | n_x)
 //   D[:, 0:64] += H_t . Bh^T                   (K = 256, 16 K-slices)
 // then the GRU gates of the CTA's 16 units for the 128 rows; the new h slice
-// (both fp16 halves) is written into the CTA's own A operand and bulk-copied
-// from there into every peer's (cp.async.bulk shared::cta -> shared::cluster,
-// completing on the peer's h_full barrier).
+// (both fp16 halves) goes into the CTA's own A operand and to a per-cluster
+// exchange buffer in global memory (L2), and every CTA bulk-loads the 15
+// slices of its peers from there (the all-to-all goes through L2, whose
+// bandwidth per SM is several times the SM-to-SM network's).
 // The A operand is 16 K-slices of [128 rows x 16] (SW32), so CTA c's units
 // are exactly one slice.  The prober's first layer for latent t comes out of
 // step t + 1's MMA (its A operand is h_{t+1}); each CTA sends its two hidden
@@ -93,7 +94,8 @@ struct __align__(1024) MmaSmem {
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
     float red_w[kOwnRows];
     uint64_t red_key[4];
-    uint64_t w_full, x_full[2], x_empty[2], h_full, a_free, mma_done[2], empty[2], pro_full[2], slice_ready, done;
+    uint64_t w_full, x_full[2], x_empty[2], h_full, mma_done[2], empty[2], pro_full[2], g_ready[2], slice_ready,
+        done;
     uint32_t tmem;
     int last;
 };
@@ -160,26 +162,6 @@ __device__ __forceinline__ bool wait_cluster(uint64_t* bar, uint32_t parity, vol
         err[3] = static_cast<int>(parity);
     }
     return false;
-}
-// tcgen05.commit arriving, once this thread's MMAs are complete, on the
-// mbarrier at the same offset in every CTA of `mask`.
-__device__ __forceinline__ void commit_multicast(uint64_t* bar, uint16_t mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            tc::smem_u32(bar)),
-        "h"(mask)
-        : "memory");
-}
-// Bulk copy of `bytes` from this CTA's shared memory to a peer's (both
-// addresses 16-byte aligned, bytes a multiple of 16), completing as
-// transaction bytes on the peer's mbarrier `peer_bar`.
-__device__ __forceinline__ void bulk_to_peer(uint32_t peer_dst, uint32_t local_src, uint32_t bytes,
-                                             uint32_t peer_bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            peer_dst),
-        "r"(local_src), "r"(bytes), "r"(peer_bar)
-        : "memory");
 }
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -315,6 +297,7 @@ struct MmaArgs {
     const uint8_t* w;    // packed weights [16][kWBytes]
     const float* h0;     // [B, 256]
     const uint8_t* xt;   // x tiles [tiles][T][kXTileBytes]
+    uint8_t* xchg;       // h exchange [tiles][2 step parities][16 slices][kSlicePair]
     uint32_t tiles_per_vehicle, tiles;
     int* err;
     uint32_t wait_polls;
@@ -347,8 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         // h_t complete: the MMA issuer's arrival (with the 15 peer slices'
         // bytes expected) and the 8 gate warps' own-slice arrivals
         tc::mbar_init(&s.h_full, 9);
-        tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is written (sender may copy it)
-        tc::mbar_init(&s.a_free, kCl);      // every CTA's MMAs of the step are done
+        tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is in the exchange buffer
+        for (int i = 0; i < 2; ++i) tc::mbar_init(&s.g_ready[i], kCl - 1);  // the 15 peers' slices are, by step parity
         tc::mbar_init(&s.done, 1);
         tc::mbar_fence_init();
     }
@@ -365,13 +348,35 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         if (lane == 0) {
             tc::mbar_expect_tx(&s.w_full, kWBytes);
             tc::bulk_g2s(s.W, p.w + static_cast<size_t>(c) * kWBytes, kWBytes, &s.w_full);
-            uint32_t t = 0;
-            for (; t < T && !err[0]; ++t) {
-                const uint32_t xs = t & 1u;
-                if (!tc::mbar_wait(&s.x_empty[xs], ((t >> 1) & 1u) ^ 1u, err, 1, t, lim)) break;
+            tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
+            const uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes;
+            uint32_t t = 0;  // x tiles issued
+            auto load_x = [&](uint32_t k) -> bool {
+                const uint32_t xs = k & 1u;
+                if (!tc::mbar_wait(&s.x_empty[xs], ((k >> 1) & 1u) ^ 1u, err, 1, k, lim)) return false;
                 tc::mbar_expect_tx(&s.x_full[xs], kXTileBytes);
-                tc::bulk_g2s(s.X[xs], p.xt + (static_cast<size_t>(tile) * T + t) * kXTileBytes, kXTileBytes,
+                tc::bulk_g2s(s.X[xs], p.xt + (static_cast<size_t>(tile) * T + k) * kXTileBytes, kXTileBytes,
                              &s.x_full[xs]);
+                return true;
+            };
+            bool ok = load_x(0);
+            t = ok ? 1u : 0u;
+            for (uint32_t k = 0; ok && k < T; ++k) {
+                // the next step's x tile ahead of the exchange
+                if (k + 1 < T) {
+                    if (!(ok = load_x(k + 1))) break;
+                    t = k + 2;
+                }
+                // h_{k+1}: the 15 peer slices, once they are in the exchange buffer
+                // and this CTA's MMAs of step k are done reading A
+                if (!(ok = wait_cluster(&s.g_ready[k & 1u], (k >> 1) & 1u, err, 11, k, lim))) break;
+                if (!(ok = tc::mbar_wait(&s.mma_done[k & 1u], (k >> 1) & 1u, err, 12, k, lim))) break;
+                tc::mbar_expect_tx(&s.h_full, (kCl - 1) * kSlicePair);
+                const uint8_t* src = xg + static_cast<size_t>((k + 1) & 1u) * kABytes;
+                for (uint32_t d = 1; d < kCl; ++d) {
+                    const uint32_t j = (c + d) & (kCl - 1u);
+                    tc::bulk_g2s(s.A + j * kSlicePair, src + j * kSlicePair, kSlicePair, &s.h_full);
+                }
             }
             // copies issued and maybe not consumed land before the CTA exits
             tc::mbar_wait_landing(&s.w_full, 0, lim);
@@ -393,12 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             const uint64_t dbh = tc::smem_desc(w_base, 16, 1024, tc::kSwizzle128);
             const uint64_t dbx = tc::smem_desc(w_base + kBhBytes, 16, 256, tc::kSwizzle32);
             bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
-            tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
                 ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
-                // the next phase expects the 15 peer slices of h_{t+1} (both halves)
-                if (ok && t < T) tc::mbar_expect_tx(&s.h_full, (kCl - 1) * kSlicePair);
                 if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
                 if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
@@ -425,10 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     acc = 1;
                 }
                 tc::commit(&s.mma_done[slot]);
-                if (t < T) {
-                    commit_multicast(&s.a_free, 0xFFFFu);  // every CTA learns this CTA is done reading h_t
-                    tc::commit(&s.x_empty[slot]);
-                }
+                if (t < T) tc::commit(&s.x_empty[slot]);
             }
             failed = !ok;
             // every MMA issued has completed before TMEM is released
@@ -461,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&s.h_full);  // phase 0: h_0 written locally
         const uint32_t slice_off = c * kSlicePair + tc::sw32_offset(row, half * 8);
-        const uint32_t a_local = tc::smem_u32(s.A), hfull_local = tc::smem_u32(&s.h_full);
-        // this warp bulk-copies the CTA's slice to peers c + 2w + 1 and c + 2w + 2
+        const uint32_t gready_local = tc::smem_u32(&s.g_ready[0]);
+        uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes + slice_off;
+        // this warp tells peers c + 2w + 1 and c + 2w + 2 that the CTA's slice is out
         const uint32_t wi = warp - kEpiWarp0;
         bool ok = true;
         for (uint32_t t = 0; ok && t < T; ++t) {
@@ -501,28 +501,29 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             uint32_t hi[4], lo[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) split2(hprev[2 * i], hprev[2 * i + 1], hi[i], lo[i]);
-            // every CTA's MMAs of step t are done reading h_t; so are the bulk
-            // copies of this CTA's slice of h_t to its peers (each peer's MMA
-            // waited for them), and the slice can be overwritten
-            if (!(ok = wait_cluster(&s.a_free, t & 1u, err, 7, t, lim))) break;
-            *reinterpret_cast<uint4*>(s.A + slice_off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(s.A + kSliceBytes + slice_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            tc::fence_async_smem();  // visible to the tensor core and the bulk-copy engine
+            const uint4 vh = make_uint4(hi[0], hi[1], hi[2], hi[3]), vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            // the own slice of h_{t+1}: into the exchange buffer of parity
+            // (t + 1) & 1 (its readers of h_{t-1} are done: they passed their
+            // MMA of step t - 1 before this CTA's MMA of step t could run) ...
+            uint8_t* gslot = xg + static_cast<size_t>((t + 1) & 1u) * kABytes;
+            *reinterpret_cast<uint4*>(gslot) = vh;
+            *reinterpret_cast<uint4*>(gslot + kSliceBytes) = vl;
+            // ... and into the local A operand (this CTA's MMA of step t is done
+            // reading it: mma_done above)
+            *reinterpret_cast<uint4*>(s.A + slice_off) = vh;
+            *reinterpret_cast<uint4*>(s.A + kSliceBytes + slice_off) = vl;
+            __threadfence();
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // the peers' bulk loads read it
+            tc::fence_async_smem();                                  // the tensor core reads A
             __syncwarp();
             if (lane == 0) {
                 tc::mbar_arrive(&s.slice_ready);
                 tc::mbar_arrive(&s.h_full);
-            }
-            if (lane == 0) {
-                // once the whole slice is written: both halves (8 KB, contiguous)
-                // to this warp's two peers
+                // the whole slice is out: tell this warp's two peers
                 ok = tc::mbar_wait(&s.slice_ready, t & 1u, err, 10, t, lim);
                 if (ok)
-                    for (uint32_t d = 2 * wi + 1; d <= 2 * wi + 2 && d < kCl; ++d) {
-                        const uint32_t peer = (c + d) % kCl;
-                        bulk_to_peer(peer_addr(a_local, peer) + c * kSlicePair, a_local + c * kSlicePair, kSlicePair,
-                                     peer_addr(hfull_local, peer));
-                    }
+                    for (uint32_t d = 2 * wi + 1; d <= 2 * wi + 2 && d < kCl; ++d)
+                        arrive_peer(peer_addr(gready_local + (t & 1u) * 8u, (c + d) & (kCl - 1u)));
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
@@ -808,8 +809,12 @@ bool skyjepa_mma_fits_device() {
     return mma_configure(dev);
 }
 
-cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
-                               cudaStream_t stream, int* launches, const SideStream* side) {
+size_t skyjepa_mma_exchange_bytes(uint32_t B, uint32_t S) {
+    return static_cast<size_t>(B) * (S / kRowsM) * 2 * kABytes;
+}
+
+cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles,
+                               uint8_t* xchg, int* err, cudaStream_t stream, int* launches, const SideStream* side) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -844,6 +849,7 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     p.w = packed;
     p.h0 = h0;
     p.xt = xtiles;
+    p.xchg = xchg;
     p.tiles_per_vehicle = a.S / kRowsM;
     p.tiles = a.B * p.tiles_per_vehicle;
     p.err = err;
@@ -860,7 +866,9 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (a.time_begin) cudaEventRecord(a.time_begin, stream);
     e = cudaLaunchKernelEx(&cfg, skyjepa_mma_kernel, p);
+    if (a.time_end) cudaEventRecord(a.time_end, stream);
     if (launches) *launches = 4;
     return e;
 }

@@ -1172,7 +1172,9 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t grid = static_cast<uint32_t>(sms) < p.tiles ? static_cast<uint32_t>(sms) : p.tiles;
+    if (a.time_begin) cudaEventRecord(a.time_begin, stream);
     skyjepa_tc_kernel<<<grid, kThreadsTc, smem, stream>>>(p);
+    if (a.time_end) cudaEventRecord(a.time_end, stream);
     if (launches) *launches = 4;
     return cudaGetLastError();
 }

@@ -166,6 +166,9 @@ struct SkyjepaArgs {
     // fault injection for tests (lwm_ctx_set_test_faults): 0 = off
     uint32_t test_wait_polls;      // tensor-core pipeline waits give up after this many polls
     uint32_t test_skip_h_arrive;   // the tensor-core rollout's first h hand-off of CTA 0 misses one arrival
+    // CUDA events recorded on the stream around the rollout kernel's launch
+    // (kernel timing, lwm_ctx_set_kernel_timing), or nullptr
+    cudaEvent_t time_begin, time_end;
 };
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
@@ -193,8 +196,10 @@ size_t skyjepa_mma_packed_bytes();
 cudaError_t skyjepa_mma_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
 uint32_t skyjepa_mma_partials_per_vehicle(uint32_t S);
 size_t skyjepa_mma_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
-cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles, int* err,
-                               cudaStream_t stream, int* launches, const SideStream* side);
+// Global buffer of the per-step h exchange between a cluster's CTAs.
+size_t skyjepa_mma_exchange_bytes(uint32_t B, uint32_t S);
+cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles,
+                               uint8_t* xchg, int* err, cudaStream_t stream, int* launches, const SideStream* side);
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
 // h0 of every vehicle by one 8-CTA cluster each (kernels_skyjepa.cu).
 cudaError_t launch_skyjepa_h0_cluster(const SkyjepaArgs& a, float* h0, cudaStream_t stream);

@@ -309,6 +309,8 @@ _sig("lwm_ctx_destroy", C.c_int, VP)
 _sig("lwm_ctx_stream", C.c_int, VP, C.POINTER(VP))
 _sig("lwm_ctx_synchronize", C.c_int, VP)
 _sig("lwm_ctx_launch_count", C.c_int, VP, C.POINTER(U64))
+_sig("lwm_ctx_set_kernel_timing", C.c_int, VP, C.c_int)
+_sig("lwm_ctx_kernel_time_ms", C.c_int, VP, C.POINTER(C.c_float))
 _sig("lwm_mppi_config_default", None, U32, U32, U32, C.POINTER(_MppiConfig))
 _sig("lwm_cem_config_default", None, U32, U32, U32, U32, C.POINTER(_CemConfig))
 _sig("lwm_icem_config_default", None, U32, U32, U32, U32, C.POINTER(_IcemConfig))
@@ -469,6 +471,17 @@ class Context:
         n = U64()
         _check(lib.lwm_ctx_launch_count(self.handle, C.byref(n)))
         return int(n.value)
+
+    def set_kernel_timing(self, on: bool = True) -> None:
+        """Records CUDA events around every SkyJEPA rollout launch
+        (lwm_ctx_set_kernel_timing)."""
+        _check(lib.lwm_ctx_set_kernel_timing(self.handle, int(on)))
+
+    def kernel_time_ms(self) -> float:
+        """Device time of the last timed rollout launch (lwm_ctx_kernel_time_ms)."""
+        ms = C.c_float()
+        _check(lib.lwm_ctx_kernel_time_ms(self.handle, C.byref(ms)))
+        return float(ms.value)
 
     def torch_stream(self):
         import torch
