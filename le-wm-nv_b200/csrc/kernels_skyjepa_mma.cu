@@ -70,6 +70,9 @@ constexpr uint32_t kNh = 64;                 // gate columns: r, z, n_h (16 each
 // halves (and x1 w0, h1 w0), [64, 128) the products with their low halves
 // (x0 w1, h0 w1), [128, 144) / [144, 160) the same two for n_x; a gate's
 // pre-activation is the sum of its two columns
+// K-slices of h in groups of 4: the MMAs of a group issue as soon as its
+// peer slices have landed, while the next group's are still in flight
+constexpr uint32_t kGroups = 4, kGroupSlices = kCl / kGroups;
 constexpr uint32_t kColR = 0, kColZ = 16, kColNh = 32, kColP = 48, kColLo = 64, kColNx = 128, kColNxLo = 144;
 constexpr uint32_t kSlotCols = 256;
 constexpr uint32_t kTmemCols = 512;
@@ -85,6 +88,10 @@ constexpr uint32_t kXTileBytes = 2 * kSliceBytes;    // one step's x tile, both 
 constexpr int kThreads = 448;
 constexpr uint32_t kEpiWarp0 = 2, kAuxWarp0 = 10, kAuxBarrier = 3, kAuxThreads = 128;
 constexpr uint32_t kMaxLayers = 3;
+// The prober's hidden and output layers transposed ([in][out], the output
+// layer padded to 16), after the CTAs' packed weights: a warp's lanes (one
+// output each) read 32 consecutive floats per input.
+constexpr uint32_t kProberTFloats = (kMaxLayers - 1) * kHid * kHid + kHid * 16;
 
 struct __align__(1024) MmaSmem {
     uint8_t A[kABytes];            // h_t: [slice][half][128 x 16] fp16, SW32
@@ -96,6 +103,7 @@ struct __align__(1024) MmaSmem {
     uint64_t red_key[4];
     uint64_t w_full, x_full[2], x_empty[2], h_full, mma_done[2], empty[2], pro_full[2], g_ready[2], slice_ready,
         done;
+    uint64_t h_grp[kGroups];  // the peer slices of K-slice group g of h_{t+1} have landed
     uint32_t tmem;
     int last;
 };
@@ -137,6 +145,23 @@ __device__ __forceinline__ void st_peer_v2f(uint32_t addr, float a, float b) {
 // this thread's earlier writes to the cluster.
 __device__ __forceinline__ void arrive_peer(uint32_t addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// One arrival on the mbarrier at cluster-shared address `addr` without
+// ordering of its own (a fence ahead of it releases what it publishes).
+__device__ __forceinline__ void arrive_peer_relaxed(uint32_t addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// Bulk copy of `bytes` from this CTA's shared memory to global memory,
+// waited for to completion (both addresses 16-byte aligned, bytes a
+// multiple of 16); the writes are then ordered for the async proxy.
+__device__ __forceinline__ void bulk_s2g_wait(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile(
+        "cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n\t"
+        "cp.async.bulk.commit_group;\n\t"
+        "cp.async.bulk.wait_group 0;\n\t"
+        "fence.proxy.async.global;" ::"l"(dst),
+        "r"(src), "r"(bytes)
+        : "memory");
 }
 // Bounded wait with acquire at cluster scope, for barriers that other CTAs
 // arrive on (the same give-up protocol as tc::mbar_wait).
@@ -201,6 +226,20 @@ __global__ void pack_mma_weights_kernel(SkyjepaArgs a, uint8_t* packed) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t n_h = kCl * kNh * kH, n_x = kCl * (kNh + 16) * 16;
     uint32_t hi, lo;
+    if (i >= n_h + n_x) {
+        const uint32_t q = i - n_h - n_x;
+        if (q >= kProberTFloats) return;
+        float* wt = reinterpret_cast<float*>(packed + static_cast<size_t>(kCl) * kWBytes);
+        const uint32_t n_hid = (kMaxLayers - 1) * kHid * kHid;
+        if (q < n_hid) {
+            const uint32_t l = q / (kHid * kHid), in = (q / kHid) % kHid, out = q % kHid;
+            wt[q] = l + 1 < a.prober_layers ? a.p_hid_w[l][out * kHid + in] : 0.0f;
+        } else {
+            const uint32_t in = (q - n_hid) / 16, out = (q - n_hid) % 16;
+            wt[q] = out < 15 ? a.p_out_w[out * kHid + in] : 0.0f;
+        }
+        return;
+    }
     if (i < n_h) {
         const uint32_t c = i / (kNh * kH), rem = i % (kNh * kH), j = rem / kH, k = rem % kH;
         float v = 0.0f;
@@ -329,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         }
         // h_t complete: the MMA issuer's arrival (with the 15 peer slices'
         // bytes expected) and the 8 gate warps' own-slice arrivals
-        tc::mbar_init(&s.h_full, 9);
+        tc::mbar_init(&s.h_full, 8);  // the own slice of h_t (all of h_0) is in A
+        for (uint32_t g = 0; g < kGroups; ++g) tc::mbar_init(&s.h_grp[g], 1);
         tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is in the exchange buffer
         for (int i = 0; i < 2; ++i) tc::mbar_init(&s.g_ready[i], kCl - 1);  // the 15 peers' slices are, by step parity
         tc::mbar_init(&s.done, 1);
@@ -348,7 +388,6 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         if (lane == 0) {
             tc::mbar_expect_tx(&s.w_full, kWBytes);
             tc::bulk_g2s(s.W, p.w + static_cast<size_t>(c) * kWBytes, kWBytes, &s.w_full);
-            tc::mbar_arrive(&s.h_full);  // phase 0 (h_0, written locally): no peer bytes
             const uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes;
             uint32_t t = 0;  // x tiles issued
             auto load_x = [&](uint32_t k) -> bool {
@@ -371,11 +410,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 // and this CTA's MMAs of step k are done reading A
                 if (!(ok = wait_cluster(&s.g_ready[k & 1u], (k >> 1) & 1u, err, 11, k, lim))) break;
                 if (!(ok = tc::mbar_wait(&s.mma_done[k & 1u], (k >> 1) & 1u, err, 12, k, lim))) break;
-                tc::mbar_expect_tx(&s.h_full, (kCl - 1) * kSlicePair);
                 const uint8_t* src = xg + static_cast<size_t>((k + 1) & 1u) * kABytes;
-                for (uint32_t d = 1; d < kCl; ++d) {
-                    const uint32_t j = (c + d) & (kCl - 1u);
-                    tc::bulk_g2s(s.A + j * kSlicePair, src + j * kSlicePair, kSlicePair, &s.h_full);
+                for (uint32_t g = 0; g < kGroups; ++g) {
+                    const uint32_t n = (g == c / kGroupSlices) ? kGroupSlices - 1u : kGroupSlices;
+                    tc::mbar_expect_tx(&s.h_grp[g], n * kSlicePair);
+                    for (uint32_t j = g * kGroupSlices; j < (g + 1) * kGroupSlices; ++j)
+                        if (j != c) tc::bulk_g2s(s.A + j * kSlicePair, src + j * kSlicePair, kSlicePair, &s.h_grp[g]);
                 }
             }
             // copies issued and maybe not consumed land before the CTA exits
@@ -400,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
-                ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds h_t
+                ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds the own slice of h_t
                 if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
                 if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
@@ -418,14 +458,27 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     tc::mma_f16(d + kColNx, dx + x1, dbx + nx, id16, 1);
                     acc = 1;
                 }
-#pragma unroll
-                for (uint32_t j = 0; j < kCl; ++j) {
+                auto slice = [&](uint32_t j) {
                     const uint64_t a0 = da + ((j * kSlicePair) >> 4), a1 = a0 + (kSliceBytes >> 4);
                     const uint64_t b = dbh + (((j >> 2) * kBhBlock + (j & 3u) * 32) >> 4);
                     tc::mma_f16(d, a0, b, id128, acc);
                     tc::mma_f16(d, a1, b, id64, 1);
                     acc = 1;
+                };
+                // the own slice first, then the peers' group by group as they land
+                slice(c);
+                for (uint32_t g = 0; ok && g < kGroups; ++g) {
+                    if (t > 0) {
+                        if (!(ok = tc::mbar_wait(&s.h_grp[g], (t - 1u) & 1u, err, 13, t, lim))) break;
+                        tc::fence_after();
+                    }
+#pragma unroll
+                    for (uint32_t i = 0; i < kGroupSlices; ++i) {
+                        const uint32_t j = g * kGroupSlices + i;
+                        if (j != c) slice(j);
+                    }
                 }
+                if (!ok) break;
                 tc::commit(&s.mma_done[slot]);
                 if (t < T) tc::commit(&s.x_empty[slot]);
             }
@@ -461,8 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         if (lane == 0) tc::mbar_arrive(&s.h_full);  // phase 0: h_0 written locally
         const uint32_t slice_off = c * kSlicePair + tc::sw32_offset(row, half * 8);
         const uint32_t gready_local = tc::smem_u32(&s.g_ready[0]);
-        uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes + slice_off;
-        // this warp tells peers c + 2w + 1 and c + 2w + 2 that the CTA's slice is out
+        const uint32_t a_slice = tc::smem_u32(s.A) + c * kSlicePair;
+        uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes + c * kSlicePair;
+        // the first gate warp publishes the CTA's slice and tells the peers
         const uint32_t wi = warp - kEpiWarp0;
         bool ok = true;
         for (uint32_t t = 0; ok && t < T; ++t) {
@@ -501,29 +555,29 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             uint32_t hi[4], lo[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) split2(hprev[2 * i], hprev[2 * i + 1], hi[i], lo[i]);
-            const uint4 vh = make_uint4(hi[0], hi[1], hi[2], hi[3]), vl = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            // the own slice of h_{t+1}: into the exchange buffer of parity
-            // (t + 1) & 1 (its readers of h_{t-1} are done: they passed their
-            // MMA of step t - 1 before this CTA's MMA of step t could run) ...
-            uint8_t* gslot = xg + static_cast<size_t>((t + 1) & 1u) * kABytes;
-            *reinterpret_cast<uint4*>(gslot) = vh;
-            *reinterpret_cast<uint4*>(gslot + kSliceBytes) = vl;
-            // ... and into the local A operand (this CTA's MMA of step t is done
-            // reading it: mma_done above)
-            *reinterpret_cast<uint4*>(s.A + slice_off) = vh;
-            *reinterpret_cast<uint4*>(s.A + kSliceBytes + slice_off) = vl;
-            __threadfence();
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // the peers' bulk loads read it
-            tc::fence_async_smem();                                  // the tensor core reads A
+            // the own slice of h_{t+1} into the local A operand (this CTA's MMA
+            // of step t is done reading it: mma_done above), for the tensor
+            // core and the bulk store below
+            *reinterpret_cast<uint4*>(s.A + slice_off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(s.A + kSliceBytes + slice_off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) {
                 tc::mbar_arrive(&s.slice_ready);
                 tc::mbar_arrive(&s.h_full);
-                // the whole slice is out: tell this warp's two peers
-                ok = tc::mbar_wait(&s.slice_ready, t & 1u, err, 10, t, lim);
-                if (ok)
-                    for (uint32_t d = 2 * wi + 1; d <= 2 * wi + 2 && d < kCl; ++d)
-                        arrive_peer(peer_addr(gready_local + (t & 1u) * 8u, (c + d) & (kCl - 1u)));
+                if (wi == 0) {
+                    // once the whole slice is in A: its 8 KB to the exchange buffer
+                    // of parity (t + 1) & 1 (whose readers of h_{t-1} are done: they
+                    // passed their MMA of step t - 1 before this CTA's MMA of step
+                    // t could run), then one release for the 15 peers' arrivals
+                    ok = tc::mbar_wait(&s.slice_ready, t & 1u, err, 10, t, lim);
+                    if (ok) {
+                        bulk_s2g_wait(xg + static_cast<size_t>((t + 1) & 1u) * kABytes, a_slice, kSlicePair);
+                        asm volatile("fence.release.cluster;" ::: "memory");
+                        for (uint32_t d = 1; d < kCl; ++d)
+                            arrive_peer_relaxed(peer_addr(gready_local + (t & 1u) * 8u, (c + d) & (kCl - 1u)));
+                    }
+                }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
@@ -532,7 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         // ================= prober, integrator, cost and MPPI partial of the own rows
         const uint32_t q = warp & 3u, row = q * 32 + lane, atid = tid - kAuxWarp0 * 32;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
-        const uint32_t TA = T * 4u, hid = kHid;
+        const uint32_t TA = T * 4u;
+        const float* wt = reinterpret_cast<const float*>(p.w + static_cast<size_t>(kCl) * kWBytes);
         const uint32_t own0 = tv * kRowsM + c * kOwnRows;  // first sample of this CTA's own rows
         const size_t grow0 = static_cast<size_t>(b) * a.S + own0;
         // the slot of MMA(0) has no prober columns to read
@@ -574,31 +629,44 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             aux_sync();
             float(*pin)[kHid] = s.a1;
             float(*pout)[kHid] = s.a2;
+            // lane = output unit, rows q and q + 4 (the weights' transposed copy:
+            // coalesced reads shared by both rows)
+            const uint32_t ra = q, rb = q + 4;
             for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
-                const float* W = a.p_hid_w[l];
-                const float* bb = a.p_hid_b[l];
-                for (uint32_t e = atid; e < kOwnRows * kHid; e += kAuxThreads) {
-                    const uint32_t rr = e / kHid, o = e % kHid;
-                    float s0 = 0.0f, s1 = 0.0f;
-                    for (uint32_t i = 0; i < hid; i += 2) {
-                        s0 = fmaf(pin[rr][i], __ldg(W + o * hid + i), s0);
-                        s1 = fmaf(pin[rr][i + 1], __ldg(W + o * hid + i + 1), s1);
-                    }
-                    pout[rr][o] = gelu_tanh((s0 + s1) + __ldg(bb + o));
+                const float* W = wt + l * kHid * kHid + lane;
+                float s0a = 0.0f, s1a = 0.0f, s0b = 0.0f, s1b = 0.0f;
+#pragma unroll
+                for (uint32_t i = 0; i < kHid; i += 2) {
+                    const float w0 = __ldg(W + i * kHid), w1 = __ldg(W + (i + 1) * kHid);
+                    s0a = fmaf(pin[ra][i], w0, s0a);
+                    s1a = fmaf(pin[ra][i + 1], w1, s1a);
+                    s0b = fmaf(pin[rb][i], w0, s0b);
+                    s1b = fmaf(pin[rb][i + 1], w1, s1b);
                 }
+                const float bias = __ldg(a.p_hid_b[l] + lane);
+                pout[ra][lane] = gelu_tanh((s0a + s1a) + bias);
+                pout[rb][lane] = gelu_tanh((s0b + s1b) + bias);
                 aux_sync();
                 float(*tmp)[kHid] = pin;
                 pin = pout;
                 pout = tmp;
             }
-            for (uint32_t e = atid; e < kOwnRows * 15; e += kAuxThreads) {
-                const uint32_t rr = e / 15, o = e % 15;
-                float s0 = 0.0f, s1 = 0.0f;
-                for (uint32_t i = 0; i < hid; i += 2) {
-                    s0 = fmaf(pin[rr][i], __ldg(a.p_out_w + o * hid + i), s0);
-                    s1 = fmaf(pin[rr][i + 1], __ldg(a.p_out_w + o * hid + i + 1), s1);
+            if (lane < 16) {
+                const float* W = wt + (kMaxLayers - 1) * kHid * kHid + lane;
+                float s0a = 0.0f, s1a = 0.0f, s0b = 0.0f, s1b = 0.0f;
+#pragma unroll
+                for (uint32_t i = 0; i < kHid; i += 2) {
+                    const float w0 = __ldg(W + i * 16), w1 = __ldg(W + (i + 1) * 16);
+                    s0a = fmaf(pin[ra][i], w0, s0a);
+                    s1a = fmaf(pin[ra][i + 1], w1, s1a);
+                    s0b = fmaf(pin[rb][i], w0, s0b);
+                    s1b = fmaf(pin[rb][i + 1], w1, s1b);
                 }
-                s.pout[rr][o] = (s0 + s1) + __ldg(a.p_out_b + o);
+                if (lane < 15) {
+                    const float bias = __ldg(a.p_out_b + lane);
+                    s.pout[ra][lane] = (s0a + s1a) + bias;
+                    s.pout[rb][lane] = (s0b + s1b) + bias;
+                }
             }
             aux_sync();
             if (atid < kOwnRows) {
@@ -751,10 +819,10 @@ bool skyjepa_mma_supported(const SkyjepaArgs& a, const char** why) {
     return true;
 }
 
-size_t skyjepa_mma_packed_bytes() { return static_cast<size_t>(kCl) * kWBytes; }
+size_t skyjepa_mma_packed_bytes() { return static_cast<size_t>(kCl) * kWBytes + kProberTFloats * sizeof(float); }
 
 cudaError_t skyjepa_mma_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream) {
-    const uint32_t n = kCl * kNh * kH + kCl * (kNh + 16) * 16;
+    const uint32_t n = kCl * kNh * kH + kCl * (kNh + 16) * 16 + kProberTFloats;
     pack_mma_weights_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a, packed);
     return cudaGetLastError();
 }
