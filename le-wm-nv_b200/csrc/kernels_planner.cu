@@ -75,6 +75,36 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs a) {
     }
 }
 
+// The same without the colored-noise pass (white noise): one thread per
+// (vehicle, sample, step, action) element, each of which is independent.
+__global__ void __launch_bounds__(256) sample_elem_kernel(SampleArgs a) {
+    const uint64_t e = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t TA = a.T * a.A;
+    if (e >= static_cast<uint64_t>(a.B) * a.S * TA) return;
+    const uint32_t act = static_cast<uint32_t>(e % a.A);
+    const uint32_t t = static_cast<uint32_t>((e / a.A) % a.T);
+    const uint64_t row = e / TA;  // b * S + s
+    const uint32_t s = static_cast<uint32_t>(row % a.S);
+    const uint32_t b = static_cast<uint32_t>(row / a.S);
+    const uint32_t g = a.sample_base + s;  // the candidate's row in the (unsharded) plan
+    const size_t mi = (static_cast<size_t>(b) * a.T + t) * a.A + act;
+    float v;
+    if (a.carried && g >= 1 && g <= a.inject) {
+        v = a.carried[((static_cast<size_t>(b) * a.carried_count + (g - 1)) * a.T + t) * a.A + act];
+    } else {
+        if (g == 0) {
+            v = a.mean[mi];
+        } else {
+            const uint64_t gi = global_row(b, s, a.sample_base, a.sample_total, a.S) * TA +
+                                static_cast<uint64_t>(t) * a.A + act;
+            const float eps = a.noise ? a.noise[e] : normal_at(a.seed, a.offset + gi);
+            v = __fadd_rn(a.mean[mi], __fmul_rn(eps, a.std[mi]));
+        }
+        v = cmin(cmax(v, a.low[act]), a.high[act]);
+    }
+    a.out[e] = v;
+}
+
 // --------------------------------------------------- MPPI reduce (generic)
 __global__ void __launch_bounds__(256) mppi_reduce_kernel(MppiArgs m, const float* cand,
                                                           const float* scores, uint32_t S) {
@@ -403,7 +433,10 @@ static inline uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uin
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream) {
     const uint64_t lanes = static_cast<uint64_t>(a.B) * a.S * a.A;
-    sample_kernel<<<ceil_div(lanes, 256), 256, 0, stream>>>(a);
+    if (a.smooth > 0.0f && a.T > 1)
+        sample_kernel<<<ceil_div(lanes, 256), 256, 0, stream>>>(a);
+    else
+        sample_elem_kernel<<<ceil_div(lanes * a.T, 256), 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -287,17 +287,26 @@ struct MmaTcnConst {
 
 __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, const __grid_constant__ MmaTcnConst tw,
                                                                  uint8_t* xtiles) {
-    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // four lanes per (candidate, step): lane o computes the encoder's channel o
+    const uint64_t gt = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t o = static_cast<uint32_t>(gt & 3u), base = threadIdx.x & 28u;
     const uint64_t total = static_cast<uint64_t>(a.B) * a.S * a.T;
-    if (i >= total) return;
+    const bool live = (gt >> 2) < total;
+    const uint64_t i = live ? (gt >> 2) : total - 1;  // dead lanes still take part in the shuffles
     const uint32_t t = static_cast<uint32_t>(i % a.T);
     const uint64_t grow = i / a.T;  // b * S + s
     const uint32_t b = static_cast<uint32_t>(grow / a.S);
-    TcnBlockW w[3];
+    TcnChannelW w;
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
         const float* blk = tw.v + l * 104;
-        w[l] = {blk, blk + 48, blk + 52, blk + 100};
+#pragma unroll
+        for (int q = 0; q < kTcnC * kTcnK; ++q) {
+            w.w[2 * l][q] = blk[o * kTcnC * kTcnK + q];
+            w.w[2 * l + 1][q] = blk[52 + o * kTcnC * kTcnK + q];
+        }
+        w.b[2 * l] = blk[48 + o];
+        w.b[2 * l + 1] = blk[100 + o];
     }
     const float* cand_row = a.cand_out + grow * a.T * 4;
     float x0[kTcnC][kTcnHs];
@@ -312,8 +321,11 @@ __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, 
         x0[2][q] = (v.z - a.action_mean[2]) / a.action_std[2];
         x0[3][q] = (v.w - a.action_mean[3]) / a.action_std[3];
     }
+    const float mine = tcn_last_channel<AccurateGelu>(w, x0, o, base);
     float x[kTcnC];
-    tcn_last<AccurateGelu>(w, x0, x);
+#pragma unroll
+    for (int q = 0; q < kTcnC; ++q) x[q] = __shfl_sync(0xffffffffu, mine, base + q);
+    if (!live || o != 0) return;
     const uint64_t tile = grow / kRowsM;
     const uint32_t row = static_cast<uint32_t>(grow % kRowsM);
     uint8_t* xt = xtiles + (tile * a.T + t) * kXTileBytes;
@@ -908,7 +920,7 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     MmaTcnConst tw;
     for (uint32_t q = 0; q < 3 * 104; ++q) tw.v[q] = a.action_tcn_host[q];
     const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
-    skyjepa_mma_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles);
+    skyjepa_mma_inputs_kernel<<<static_cast<uint32_t>((4 * n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     // 3. the rollout: one 16-CTA cluster per 128 rows

@@ -96,4 +96,65 @@ __device__ __forceinline__ void tcn_last(const TcnBlockW (&w)[3], const float (&
     for (int o = 0; o < kTcnC; ++o) x[o] = y3[o][kTcnHs - 1];
 }
 
+// The same encoder split over the 4 lanes of a window (lane `o` computes
+// output channel o of every convolution; the lanes of one window are
+// consecutive, starting at lane `base` of the warp).  Each convolution's
+// outputs are gathered back to all 4 lanes with shuffles.  Every sum is
+// formed in the order conv_at forms it, so the values are tcn_last's.
+struct TcnChannelW {
+    float w[6][kTcnC * kTcnK];  // convolution 2l + k (level l; k = 0 conv1, 1 conv2): row o
+    float b[6];
+};
+
+// Output channel o at position P of conv(in) with dilation `dil`, + bias, GELU.
+template <typename Gelu>
+__device__ __forceinline__ float conv_ch(const float (&in)[kTcnC][kTcnHs], const float (&W)[kTcnC * kTcnK],
+                                         float B, int P, int dil) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kTcnC; ++i)
+#pragma unroll
+        for (int j = 0; j < kTcnK; ++j) {
+            const int src = P - (kTcnK - 1 - j) * dil;
+            if (src >= 0) acc = fmaf(W[i * kTcnK + j], in[i][src], acc);
+        }
+    return Gelu()(acc + B);
+}
+
+__device__ __forceinline__ void gather_ch(float (&dst)[kTcnC][kTcnHs], int P, float mine, uint32_t base) {
+#pragma unroll
+    for (int i = 0; i < kTcnC; ++i) dst[i][P] = __shfl_sync(0xffffffffu, mine, base + i);
+}
+
+// Channel o of x_t; the return value is the lane's own channel.  (Arrays
+// are indexed with compile-time positions only, so they stay in registers;
+// the lane's own channel of a block output is kept beside it.)
+template <typename Gelu>
+__device__ __forceinline__ float tcn_last_channel(const TcnChannelW& w, const float (&x0)[kTcnC][kTcnHs], uint32_t o,
+                                                  uint32_t base) {
+    float h1[kTcnC][kTcnHs], y1[kTcnC][kTcnHs], h2[kTcnC][kTcnHs], y2[kTcnC][kTcnHs], h3[kTcnC][kTcnHs];
+    float y1o[kTcnHs], y2o[kTcnHs];
+    // block 1 (dilation 1): conv1 everywhere, output at odd positions
+#pragma unroll
+    for (int P = 0; P < kTcnHs; ++P) gather_ch(h1, P, conv_ch<Gelu>(x0, w.w[0], w.b[0], P, 1), base);
+#pragma unroll
+    for (int P = 1; P < kTcnHs; P += 2) {
+        const float res = o == 0 ? x0[0][P] : o == 1 ? x0[1][P] : o == 2 ? x0[2][P] : x0[3][P];
+        y1o[P] = Gelu()(conv_ch<Gelu>(h1, w.w[1], w.b[1], P, 1) + res);
+        gather_ch(y1, P, y1o[P], base);
+    }
+    // block 2 (dilation 2): conv1 at odd positions, output at 1, 5, 9
+#pragma unroll
+    for (int P = 1; P < kTcnHs; P += 2) gather_ch(h2, P, conv_ch<Gelu>(y1, w.w[2], w.b[2], P, 2), base);
+#pragma unroll
+    for (int P = 1; P < kTcnHs; P += 4) {
+        y2o[P] = Gelu()(conv_ch<Gelu>(h2, w.w[3], w.b[3], P, 2) + y1o[P]);
+        gather_ch(y2, P, y2o[P], base);
+    }
+    // block 3 (dilation 4): conv1 at 1, 5, 9, output at 9
+#pragma unroll
+    for (int P = 1; P < kTcnHs; P += 4) gather_ch(h3, P, conv_ch<Gelu>(y2, w.w[4], w.b[4], P, 4), base);
+    return Gelu()(conv_ch<Gelu>(h3, w.w[5], w.b[5], kTcnHs - 1, 4) + y2o[kTcnHs - 1]);
+}
+
 }  // namespace lwm
