@@ -196,6 +196,11 @@ size_t skyjepa_mma_packed_bytes();
 cudaError_t skyjepa_mma_pack(const SkyjepaArgs& a, uint8_t* packed, cudaStream_t stream);
 uint32_t skyjepa_mma_partials_per_vehicle(uint32_t S);
 size_t skyjepa_mma_xtile_bytes(uint32_t B, uint32_t S, uint32_t T);
+// The history encoder for the default shape (10 steps, kernel 3, three
+// 128-channel levels with dilations 1, 2, 4, latent 256): one 16-CTA cluster
+// per vehicle, only the positions the last output depends on.
+bool skyjepa_h0_pruned_supported(const SkyjepaArgs& a);
+cudaError_t launch_skyjepa_h0_pruned(const SkyjepaArgs& a, float* h0, cudaStream_t stream);
 // Global buffer of the per-step h exchange between a cluster's CTAs.
 size_t skyjepa_mma_exchange_bytes(uint32_t B, uint32_t S);
 cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, float* h0, uint8_t* xtiles,
