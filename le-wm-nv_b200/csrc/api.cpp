@@ -63,8 +63,10 @@ bool finite(float v) { return std::isfinite(v); }
 struct DevBuf {
     void* ptr = nullptr;
     size_t bytes = 0;
+    bool view = false;  // a part of another DevBuf's allocation (not freed here)
     lwm_status ensure(size_t need) {
         if (need <= bytes) return LWM_OK;
+        if (view) return fail(LWM_CUDA_ERROR, "internal: a buffer view cannot grow");
         if (ptr) cudaFree(ptr);
         ptr = nullptr;
         bytes = 0;
@@ -75,11 +77,34 @@ struct DevBuf {
     }
     template <class T> T* as() const { return static_cast<T*>(ptr); }
     void release() {
-        if (ptr) cudaFree(ptr);
+        if (ptr && !view) cudaFree(ptr);
         ptr = nullptr;
         bytes = 0;
+        view = false;
+    }
+    void set_view(void* base, size_t off, size_t n) {
+        ptr = static_cast<char*>(base) + off;
+        bytes = n;
+        view = true;
     }
 };
+
+// A plan's outputs (first action, sequence, scores, best indices) share one
+// device allocation laid out like the pinned staging they are copied to, so
+// that lwm_plan reads all of them back with one copy.
+struct ResultLayout {
+    size_t fa, seq, sc, best, total;
+};
+inline size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+inline ResultLayout result_layout(size_t B, size_t T, size_t A, size_t S) {
+    ResultLayout l;
+    l.fa = 0;
+    l.seq = round256(B * A * 4);
+    l.sc = round256(l.seq + B * T * A * 4);
+    l.best = round256(l.sc + B * S * 4);
+    l.total = l.best + B * 4;
+    return l;
+}
 
 // Pinned host staging that only grows.
 struct HostBuf {
@@ -192,6 +217,7 @@ struct lwm_planner {
     uint32_t cap_b = 0;
     DevBuf bounds, zeros, std_init, mean, stdv, cand, scores, partials, counters, sequence, first_action, warm,
         best, best_score, carried, noise_tmp;
+    DevBuf results;  // holds first_action, sequence, scores and best (views into it)
     HostBuf staging;
     uint32_t last_batch = 0, last_cols = 0;
     // iCEM trace: [iterations][4][B] scores and the elite mean of an iteration
@@ -388,11 +414,17 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     LWM_TRY(p->mean.ensure(seq * 4));
     LWM_TRY(p->stdv.ensure(seq * 4));
     LWM_TRY(p->cand.ensure(n * 4));
-    LWM_TRY(p->scores.ensure(static_cast<size_t>(B) * p->S * 4));
+    const ResultLayout rl = result_layout(B, p->T, p->A, p->S);
+    if (p->results.bytes < rl.total) {
+        LWM_TRY(p->results.ensure(rl.total));
+        p->first_action.set_view(p->results.ptr, rl.fa, static_cast<size_t>(B) * p->A * 4);
+        p->sequence.set_view(p->results.ptr, rl.seq, seq * 4);
+        p->scores.set_view(p->results.ptr, rl.sc, static_cast<size_t>(B) * p->S * 4);
+        p->best.set_view(p->results.ptr, rl.best, static_cast<size_t>(B) * 4);
+    }
     LWM_TRY(p->partials.ensure(static_cast<size_t>(B) * P * pw * 4));
     LWM_TRY(p->counters.ensure(static_cast<size_t>(B) * 4));
-    LWM_TRY(p->sequence.ensure(seq * 4));
-    LWM_TRY(p->first_action.ensure(static_cast<size_t>(B) * p->A * 4));
+
     // the warm start is kept across plans: preserve it when growing
     if (p->warm.bytes < seq * 4) {
         DevBuf grown;
@@ -402,7 +434,6 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
         p->warm.release();
         p->warm = grown;
     }
-    LWM_TRY(p->best.ensure(static_cast<size_t>(B) * 4));
     LWM_TRY(p->best_score.ensure(static_cast<size_t>(B) * 4));
     LWM_TRY(p->shard_tuples.ensure(static_cast<size_t>(B) * pw * 4));
     const uint32_t keep = p->kind == PlannerKind::Icem ? std::max<uint32_t>(p->icem.keep_elites, 1) : 1;
@@ -790,7 +821,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     a.m.P = lwm::skyjepa_mma_partials_per_vehicle(p->S);
                     a.low_dev = low;
                     a.high_dev = high;
-                    LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    // (the input kernel ahead of the rollout clears the error word)
                     p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa_mma(a, sc->mma_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
                                                      sc->tc_x.as<uint8_t>(), sc->mma_xchg.as<uint8_t>(),
@@ -1169,7 +1200,7 @@ lwm_status lwm_planner_destroy(lwm_planner* p) {
     for (DevBuf* b : {&p->bounds, &p->zeros, &p->std_init, &p->mean, &p->stdv, &p->cand, &p->scores, &p->partials, &p->counters,
                       &p->sequence, &p->first_action, &p->warm, &p->best, &p->best_score, &p->carried, &p->noise_tmp,
                       &p->shard_tuples, &p->trace, &p->trace_elite, &p->elite_local, &p->elite_gathered,
-                      &p->merged_scores, &p->merged_cand, &p->merged_index, &p->elite_idx})
+                      &p->merged_scores, &p->merged_cand, &p->merged_index, &p->elite_idx, &p->results})
         b->release();
     p->staging.release();
     delete p;
@@ -1790,20 +1821,29 @@ lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_p
     const size_t B = d.batch;
     const size_t seq = B * p->T * p->A;
     const size_t nsc = B * d.scores_cols;
-    // one D2H burst through the planner's pinned staging
+    // the results through the planner's pinned staging, laid out as the
+    // planner's device result block: one copy when every output is wanted
+    // and comes from that block
+    const ResultLayout rl = result_layout(B, p->T, p->A, p->S);
+    const size_t off_fa = rl.fa, off_seq = rl.seq, off_sc = rl.sc, off_best = rl.best;
+    if (out->scores && out->scores_capacity < nsc) return fail(LWM_INVALID_ARGUMENT, "scores buffer too small");
+    LWM_TRY(p->staging.ensure(rl.total));
     char* h = p->staging.as<char>();
-    const size_t off_fa = 0, off_seq = align256(B * p->A * 4), off_sc = align256(off_seq + seq * 4),
-                 off_best = align256(off_sc + nsc * 4), total = off_best + B * 4;
-    LWM_TRY(p->staging.ensure(total));
-    h = p->staging.as<char>();
     cudaStream_t stream = p->ctx->stream;
-    if (out->first_action) LWM_CUDA(cudaMemcpyAsync(h + off_fa, d.first_action, B * p->A * 4, cudaMemcpyDeviceToHost, stream));
-    if (out->sequence) LWM_CUDA(cudaMemcpyAsync(h + off_seq, d.sequence, seq * 4, cudaMemcpyDeviceToHost, stream));
-    if (out->scores) {
-        if (out->scores_capacity < nsc) return fail(LWM_INVALID_ARGUMENT, "scores buffer too small");
-        LWM_CUDA(cudaMemcpyAsync(h + off_sc, d.scores, nsc * 4, cudaMemcpyDeviceToHost, stream));
+    const char* blk = p->results.as<char>();
+    const bool one_copy = out->first_action && out->sequence && out->scores && out->best_indices &&
+                          d.first_action == reinterpret_cast<const float*>(blk + rl.fa) &&
+                          d.sequence == reinterpret_cast<const float*>(blk + rl.seq) &&
+                          d.scores == reinterpret_cast<const float*>(blk + rl.sc) &&
+                          d.best_indices == reinterpret_cast<const uint32_t*>(blk + rl.best);
+    if (one_copy) {
+        LWM_CUDA(cudaMemcpyAsync(h, blk, rl.total, cudaMemcpyDeviceToHost, stream));
+    } else {
+        if (out->first_action) LWM_CUDA(cudaMemcpyAsync(h + off_fa, d.first_action, B * p->A * 4, cudaMemcpyDeviceToHost, stream));
+        if (out->sequence) LWM_CUDA(cudaMemcpyAsync(h + off_seq, d.sequence, seq * 4, cudaMemcpyDeviceToHost, stream));
+        if (out->scores) LWM_CUDA(cudaMemcpyAsync(h + off_sc, d.scores, nsc * 4, cudaMemcpyDeviceToHost, stream));
+        if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
     }
-    if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
     int tc_err[4] = {0, 0, 0, 0};
     int* err_dev = sc->tc_err.ptr ? sc->tc_err.as<int>()
                    : (sc->kind == ScorerKind::Lewm ? sc->lewm->split.tc_err : nullptr);

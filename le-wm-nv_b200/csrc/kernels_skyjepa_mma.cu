@@ -286,7 +286,9 @@ struct MmaTcnConst {
 };
 
 __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, const __grid_constant__ MmaTcnConst tw,
-                                                                 uint8_t* xtiles) {
+                                                                 uint8_t* xtiles, int* err) {
+    // the rollout's error word starts clear (the rollout follows on this stream)
+    if (blockIdx.x == 0 && threadIdx.x < 4) err[threadIdx.x] = 0;
     // four lanes per (candidate, step): lane o computes the encoder's channel o
     const uint64_t gt = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint32_t o = static_cast<uint32_t>(gt & 3u), base = threadIdx.x & 28u;
@@ -920,7 +922,8 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     MmaTcnConst tw;
     for (uint32_t q = 0; q < 3 * 104; ++q) tw.v[q] = a.action_tcn_host[q];
     const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
-    skyjepa_mma_inputs_kernel<<<static_cast<uint32_t>((4 * n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles);
+    skyjepa_mma_inputs_kernel<<<static_cast<uint32_t>((4 * n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles,
+                                                                                                    err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     // 3. the rollout: one 16-CTA cluster per 128 rows
