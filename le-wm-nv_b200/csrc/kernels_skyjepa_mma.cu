@@ -88,6 +88,7 @@ constexpr uint32_t kXTileBytes = 2 * kSliceBytes;    // one step's x tile, both 
 constexpr int kThreads = 448;
 constexpr uint32_t kEpiWarp0 = 2, kAuxWarp0 = 10, kAuxBarrier = 3, kAuxThreads = 128;
 constexpr uint32_t kMaxLayers = 3;
+static_assert(kMaxHorizon * 4 <= 2 * kAuxThreads, "the last CTA's combine: two sequence elements per prober thread");
 // The prober's hidden and output layers transposed ([in][out], the output
 // layer padded to 16), after the CTAs' packed weights: a warp's lanes (one
 // output each) read 32 consecutive floats per input.
@@ -101,6 +102,8 @@ struct __align__(1024) MmaSmem {
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
     float red_w[kOwnRows];
     uint64_t red_key[4];
+    float fac[kAuxThreads], facw[kAuxThreads];  // the last CTA's combine: a chunk of partials' factors
+    uint32_t live[kAuxThreads];
     uint64_t w_full, x_full[2], x_empty[2], h_full, mma_done[2], empty[2], pro_full[2], g_ready[2], slice_ready,
         done;
     uint64_t h_grp[kGroups];  // the peer slices of K-slice group g of h_{t+1} have landed
@@ -752,25 +755,51 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 for (int w = 1; w < 4; ++w) gk = s.red_key[w] < gk ? s.red_key[w] : gk;
                 const float M = key_score(gk);
                 float* tuple = mm.shard_tuple ? mm.shard_tuple + static_cast<size_t>(b) * mm.pw : nullptr;
-                for (uint32_t e = atid; e < TA; e += kAuxThreads) {
-                    float W = 0.0f, V = 0.0f;
-                    for (uint32_t i = 0; i < mm.P; ++i) {
-                        const volatile float* pq = base + static_cast<size_t>(i) * mm.pw;
-                        if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;
-                        const float f = expf((pq[0] - M) * mm.mul);
-                        W += pq[1] * f;
-                        V += pq[4 + e] * f;
+                // W = sum_i w_i f_i and V[e] = sum_i v_i[e] f_i, f_i = exp((m_i - M) mul), over
+                // the non-empty partials in ascending order; the partials come in
+                // chunks of 128 whose factors are computed once (one thread each)
+                // and whose loads are independent of one another
+                constexpr uint32_t kMaxE = 2;  // TA <= 2 x 128
+                float W[kMaxE] = {0.0f, 0.0f}, V[kMaxE] = {0.0f, 0.0f};
+                for (uint32_t i0 = 0; i0 < mm.P; i0 += kAuxThreads) {
+                    const uint32_t n = mm.P - i0 < kAuxThreads ? mm.P - i0 : kAuxThreads;
+                    if (atid < n) {
+                        const float* pq = base + static_cast<size_t>(i0 + atid) * mm.pw;
+                        const bool lv = __ldcg(reinterpret_cast<const unsigned long long*>(pq) + 1) != ~0ull;
+                        s.live[atid] = lv;
+                        s.fac[atid] = lv ? expf((__ldcg(pq) - M) * mm.mul) : 0.0f;
+                        s.facw[atid] = lv ? __ldcg(pq + 1) : 0.0f;
                     }
+                    aux_sync();
+#pragma unroll
+                    for (uint32_t k = 0; k < kMaxE; ++k) {
+                        const uint32_t e = atid + k * kAuxThreads;
+                        if (e >= TA) continue;
+                        const float* col = base + static_cast<size_t>(i0) * mm.pw + 4 + e;
+#pragma unroll 8
+                        for (uint32_t j = 0; j < n; ++j) {
+                            const float v = __ldcg(col + static_cast<size_t>(j) * mm.pw);
+                            if (s.live[j]) {
+                                W[k] += s.facw[j] * s.fac[j];
+                                V[k] += v * s.fac[j];
+                            }
+                        }
+                    }
+                    aux_sync();
+                }
+                for (uint32_t k = 0; k < kMaxE; ++k) {
+                    const uint32_t e = atid + k * kAuxThreads;
+                    if (e >= TA) continue;
                     if (tuple) {
-                        tuple[4 + e] = V;
+                        tuple[4 + e] = V[k];
                         if (e == 0) {
                             tuple[0] = M;
-                            tuple[1] = W;
+                            tuple[1] = W[k];
                             reinterpret_cast<uint64_t*>(tuple)[1] = gk;
                         }
                         continue;
                     }
-                    const float value = V / W;
+                    const float value = V[k] / W[k];
                     const uint32_t tt = e / 4u, act = e & 3u;
                     const size_t seq = static_cast<size_t>(b) * TA;
                     mm.sequence[seq + e] = value;

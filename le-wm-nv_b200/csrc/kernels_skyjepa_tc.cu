@@ -1012,8 +1012,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 // combine the vehicle's tile tuples (mppi_finish with the aux group)
                 const float* base = mm.partials + static_cast<size_t>(b) * mm.P * mm.pw;
                 uint64_t gk = ~0ull;
+                // (read at L2 with loads independent of one another, as mppi_finish)
                 for (uint32_t i = atid; i < mm.P; i += kAuxThreads) {
-                    const uint64_t kk = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(i) * mm.pw)[1];
+                    const uint64_t kk =
+                        __ldcg(reinterpret_cast<const unsigned long long*>(base + static_cast<size_t>(i) * mm.pw) + 1);
                     gk = kk < gk ? kk : gk;
                 }
 #pragma unroll
@@ -1030,12 +1032,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 float* tuple = mm.shard_tuple ? mm.shard_tuple + static_cast<size_t>(b) * mm.pw : nullptr;
                 for (uint32_t e = atid; e < TA; e += kAuxThreads) {
                     float W = 0.0f, V = 0.0f;
+#pragma unroll 4
                     for (uint32_t i = 0; i < mm.P; ++i) {
-                        const volatile float* pq = base + static_cast<size_t>(i) * mm.pw;
-                        if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;
-                        const float f = expf((pq[0] - M) * mm.mul);
-                        W += pq[1] * f;
-                        V += pq[4 + e] * f;
+                        const float* pq = base + static_cast<size_t>(i) * mm.pw;
+                        const uint64_t kk = __ldcg(reinterpret_cast<const unsigned long long*>(pq) + 1);
+                        const float m = __ldcg(pq), w = __ldcg(pq + 1), v = __ldcg(pq + 4 + e);
+                        if (kk == ~0ull) continue;
+                        const float f = expf((m - M) * mm.mul);
+                        W += w * f;
+                        V += v * f;
                     }
                     if (tuple) {
                         tuple[4 + e] = V;

@@ -60,8 +60,11 @@ __device__ void mppi_finish(const MppiArgs& a, uint32_t b, const float* base, ui
                             uint64_t* s_key_scratch) {
     const uint32_t TA = a.T * a.A;
     uint64_t gkey = ~0ull;
+    // (the tuples were written by other blocks before their arrival on the
+    // vehicle's counter: read at L2, where they are, with loads independent of
+    // one another so that they overlap)
     for (uint32_t q = threadIdx.x; q < count; q += NT) {
-        const uint64_t k = reinterpret_cast<const volatile uint64_t*>(base + static_cast<size_t>(q) * stride)[1];
+        const uint64_t k = __ldcg(reinterpret_cast<const unsigned long long*>(base + static_cast<size_t>(q) * stride) + 1);
         gkey = k < gkey ? k : gkey;
     }
     gkey = block_min_u64<NT>(gkey, s_key_scratch);
@@ -70,12 +73,15 @@ __device__ void mppi_finish(const MppiArgs& a, uint32_t b, const float* base, ui
     float Wtot = 0.0f;
     for (uint32_t e = threadIdx.x; e < TA; e += NT) {
         float W = 0.0f, V = 0.0f;
+#pragma unroll 4
         for (uint32_t q = 0; q < count; ++q) {
-            const volatile float* pq = base + static_cast<size_t>(q) * stride;
-            if (reinterpret_cast<const volatile uint64_t*>(pq)[1] == ~0ull) continue;  // tuple without rows
-            const float f = expf((pq[0] - M) * a.mul);
-            W += pq[1] * f;
-            V += pq[4 + e] * f;
+            const float* pq = base + static_cast<size_t>(q) * stride;
+            const uint64_t k = __ldcg(reinterpret_cast<const unsigned long long*>(pq) + 1);
+            const float m = __ldcg(pq), w = __ldcg(pq + 1), v = __ldcg(pq + 4 + e);
+            if (k == ~0ull) continue;  // tuple without rows
+            const float f = expf((m - M) * a.mul);
+            W += w * f;
+            V += v * f;
         }
         Wtot = W;
         if (tuple) {
