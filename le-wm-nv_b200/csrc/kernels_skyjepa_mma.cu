@@ -102,11 +102,10 @@ struct __align__(1024) MmaSmem {
     float a1[kOwnRows][kHid], a2[kOwnRows][kHid], pout[kOwnRows][16];
     float red_w[kOwnRows];
     uint64_t red_key[4];
-    float fac[kAuxThreads], facw[kAuxThreads];  // the last CTA's combine: a chunk of partials' factors
-    uint32_t live[kAuxThreads];
     uint64_t w_full, x_full[2], x_empty[2], h_full, mma_done[2], empty[2], pro_full[2], g_ready[2], slice_ready,
         done;
     uint64_t h_grp[kGroups];  // the peer slices of K-slice group g of h_{t+1} have landed
+    uint64_t staged;          // the last CTA's combine: a round of partial tuples has landed
     uint32_t tmem;
     int last;
 };
@@ -390,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
         tc::mbar_init(&s.slice_ready, 8);  // the own slice of h is in the exchange buffer
         for (int i = 0; i < 2; ++i) tc::mbar_init(&s.g_ready[i], kCl - 1);  // the 15 peers' slices are, by step parity
         tc::mbar_init(&s.done, 1);
+        tc::mbar_init(&s.staged, 1);
         tc::mbar_fence_init();
     }
     if (warp == 1) tc::tmem_alloc(&s.tmem, kTmemCols);
@@ -755,34 +755,44 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 for (int w = 1; w < 4; ++w) gk = s.red_key[w] < gk ? s.red_key[w] : gk;
                 const float M = key_score(gk);
                 float* tuple = mm.shard_tuple ? mm.shard_tuple + static_cast<size_t>(b) * mm.pw : nullptr;
-                // W = sum_i w_i f_i and V[e] = sum_i v_i[e] f_i, f_i = exp((m_i - M) mul), over
-                // the non-empty partials in ascending order; the partials come in
-                // chunks of 128 whose factors are computed once (one thread each)
-                // and whose loads are independent of one another
+                // W = sum_i w_i f_i and V[e] = sum_i v_i[e] f_i, f_i = exp((m_i - M) mul),
+                // over the non-empty partials in ascending order.  The partials
+                // are staged into shared memory (the h operand, idle now) by one
+                // bulk copy per round, as many as fit; each f_i is computed once,
+                // by one thread.
+                tc::fence_async_smem();
+                float* stage = reinterpret_cast<float*>(s.A);
+                const uint32_t cap = kABytes / (mm.pw * 4u + 4u);
                 constexpr uint32_t kMaxE = 2;  // TA <= 2 x 128
                 float W[kMaxE] = {0.0f, 0.0f}, V[kMaxE] = {0.0f, 0.0f};
-                for (uint32_t i0 = 0; i0 < mm.P; i0 += kAuxThreads) {
-                    const uint32_t n = mm.P - i0 < kAuxThreads ? mm.P - i0 : kAuxThreads;
-                    if (atid < n) {
-                        const float* pq = base + static_cast<size_t>(i0 + atid) * mm.pw;
-                        const bool lv = __ldcg(reinterpret_cast<const unsigned long long*>(pq) + 1) != ~0ull;
-                        s.live[atid] = lv;
-                        s.fac[atid] = lv ? expf((__ldcg(pq) - M) * mm.mul) : 0.0f;
-                        s.facw[atid] = lv ? __ldcg(pq + 1) : 0.0f;
+                bool staged_ok = true;
+                for (uint32_t i0 = 0, round = 0; i0 < mm.P; i0 += cap, ++round) {
+                    const uint32_t n = mm.P - i0 < cap ? mm.P - i0 : cap;
+                    if (atid == 0) {
+                        // (tuples are 16-byte multiples: pw is a multiple of 4)
+                        const uint32_t bytes = n * mm.pw * 4u;
+                        tc::mbar_expect_tx(&s.staged, bytes);
+                        tc::bulk_g2s(stage, base + static_cast<size_t>(i0) * mm.pw, bytes, &s.staged);
+                        staged_ok = tc::mbar_wait(&s.staged, round & 1u, err, 14, static_cast<int>(round), lim);
+                    }
+                    if (!aux_all(staged_ok)) break;
+                    float* fac = stage + static_cast<size_t>(n) * mm.pw;
+                    for (uint32_t j = atid; j < n; j += kAuxThreads) {
+                        const float* pq = stage + static_cast<size_t>(j) * mm.pw;
+                        fac[j] = expf((pq[0] - M) * mm.mul);
                     }
                     aux_sync();
 #pragma unroll
                     for (uint32_t k = 0; k < kMaxE; ++k) {
                         const uint32_t e = atid + k * kAuxThreads;
                         if (e >= TA) continue;
-                        const float* col = base + static_cast<size_t>(i0) * mm.pw + 4 + e;
 #pragma unroll 8
                         for (uint32_t j = 0; j < n; ++j) {
-                            const float v = __ldcg(col + static_cast<size_t>(j) * mm.pw);
-                            if (s.live[j]) {
-                                W[k] += s.facw[j] * s.fac[j];
-                                V[k] += v * s.fac[j];
-                            }
+                            const float* pq = stage + static_cast<size_t>(j) * mm.pw;
+                            const bool rows = reinterpret_cast<const uint64_t*>(pq)[1] != ~0ull;  // else no rows
+                            const float w = pq[1] * fac[j], v = pq[4 + e] * fac[j];
+                            W[k] = rows ? W[k] + w : W[k];
+                            V[k] = rows ? V[k] + v : V[k];
                         }
                     }
                     aux_sync();
