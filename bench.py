@@ -49,8 +49,9 @@ FLOP_PER_CANDIDATE_STEP["fleet"] = FLOP_PER_CANDIDATE_STEP["skyjepa"]
 ROLLOUT_FLOP_PER_CANDIDATE_STEP = 2 * (4 * 768 + 256 * 768 + 256 * 32 + 32 * 32 + 32 * 15) + 200
 # DRAM bytes (read + write) of one rollout launch of the default workload
 # (512 x 15, latent 256, split-fp16 tensor-core kernel), from an ncu capture
-# of that launch: weights, x tiles and the per-step h exchange buffer.
-ROLLOUT_DRAM_BYTES = {"skyjepa": None}
+# of that launch: the packed weights and the x tiles (the per-step h exchange
+# through its global buffer stays in L2).
+ROLLOUT_DRAM_BYTES = {"skyjepa": 1847040}
 
 
 NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)

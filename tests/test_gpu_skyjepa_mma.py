@@ -46,7 +46,7 @@ def _plan(ctx, w, noise, masses=None):
     return r, p, sc
 
 
-@pytest.mark.parametrize("batch, samples, horizon", [(1, 512, 15), (2, 256, 7), (1, 128, 30)])
+@pytest.mark.parametrize("batch, samples, horizon", [(1, 512, 15), (2, 256, 7), (1, 128, 30), (1, 128, 1), (1, 256, 2)])
 def test_split_fp16_mppi_matches_oracle(ctx, batch, samples, horizon):
     w = W.skyjepa(seed=51, batch=batch, samples=samples, horizon=horizon)
     noise = normals(81, (1, batch, samples, horizon, 4))
