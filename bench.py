@@ -1141,10 +1141,12 @@ def cpu_baseline_closed_loop(args, budget_s: float):
 # ----------------------------------------------------------------- CPU arm
 
 def cpu_baseline(kind: str, budget_s: float, threads: int = 0):
-    """The oracle (C restatement of the reference's CPU path) on the host cores."""
+    """The oracle (C restatement of the reference's CPU path) on the host cores,
+    on the workload built from the oracle alone (oracle/workload.py: the same
+    arrays as the product's generator, without loading the product)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    from lewm_b200 import workloads as W
+    import workload as W
     threads = threads or os.cpu_count() or 1
     O.set_threads(threads)
     if kind == "skyjepa":
@@ -1177,9 +1179,10 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     if args.workload == "fleet":
-        from lewm_b200 import workloads as W
-        base = cpu_baseline_fleet(W.fleet(seed=23, vehicles=args.vehicles, samples=args.samples,
-                                          horizon=args.horizon), args.cpu_seconds)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import workload as OW  # the fleet built from the oracle alone
+        base = cpu_baseline_fleet(OW.fleet(seed=23, vehicles=args.vehicles, samples=args.samples,
+                                           horizon=args.horizon), args.cpu_seconds)
         return {"impl": "reference",
                 "metric": f"fleet plan steps/s ({args.vehicles} vehicles x {args.samples} candidates x "
                           f"{args.horizon} steps per step); candidate-steps/s alongside",

@@ -173,6 +173,14 @@ void orc_reference_state(int kind, float time, float radius, float period, float
 void orc_geometric_prior(const float* current, const float* refs, uint32_t T, float dt,
                          const lwm_domain* d, float* out);
 
+/* ---- synthetic workload inputs (lewm_workload.c) ---- */
+void orc_domain_default(lwm_domain* d);
+void orc_tracking_cost_paper(lwm_tracking_cost* c);
+void orc_skyjepa_config(int wide, lwm_skyjepa_config* c);
+void orc_reference_horizon(int kind, float time, float dt, uint32_t horizon, float radius, float period,
+                           float* out);
+int orc_skyjepa_random_weights(const lwm_skyjepa_config* c, uint64_t seed, float* out, size_t count);
+
 /* ---- LeWM / WorldModel scorer (lewm_world.c) ---- */
 typedef struct orc_lewm orc_lewm;
 size_t orc_lewm_weight_count(const lwm_lewm_config* cfg);

@@ -10,7 +10,6 @@ from __future__ import annotations
 
 import ctypes as C
 import os
-import sys
 from typing import Optional
 
 import numpy as np
@@ -21,19 +20,133 @@ if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing: build it with `make -C oracle`")
 lib = C.CDLL(LIB_PATH)
 
-sys.path.insert(0, os.path.join(os.path.dirname(_HERE), "le-wm-nv_b200"))
-# Struct layouts only (ctypes mirrors of include/lewm_b200.h); no product call.
-from lewm_b200 import (  # noqa: E402
-    Domain, TrackingCost, SkyJepaConfig, KinematicConfig, _MppiConfig, _CemConfig, _IcemConfig, SessionConfig,
-)
-
 F = C.c_float
 U32 = C.c_uint32
 U64 = C.c_uint64
+I32 = C.c_int32
 FP = C.POINTER(C.c_float)
 UP = C.POINTER(C.c_uint32)
 VP = C.c_void_p
 SCORE_FN = C.CFUNCTYPE(None, VP, FP, U32, U32, U32, U32, FP)
+
+# ---- ctypes mirrors of the structs of include/lewm_b200.h that the oracle's
+# C interface takes (the oracle includes that header for its types).  This
+# module defines its own and imports nothing from the product package; a
+# product struct instance handed in by a test is copied byte for byte into the
+# mirror (_own), the layouts being the same header's.
+MAX_ACTION_DIM = 16
+TCN_MAX_LEVELS = 8
+
+
+class _MppiConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("iterations", U32), ("action_dim", U32),
+                ("bounds_low", F * MAX_ACTION_DIM), ("bounds_high", F * MAX_ACTION_DIM), ("noise_std", F),
+                ("has_noise_std_per_action", I32), ("noise_std_per_action", F * MAX_ACTION_DIM), ("temperature", F),
+                ("deadline_ns", C.c_int64), ("has_deadline_action", I32), ("deadline_action", F * MAX_ACTION_DIM),
+                ("has_seed", I32), ("seed", U64)]
+
+
+class _CemConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("elites", U32), ("iterations", U32), ("action_dim", U32),
+                ("bounds_low", F * MAX_ACTION_DIM), ("bounds_high", F * MAX_ACTION_DIM), ("init_std", F),
+                ("min_std", F), ("deadline_ns", C.c_int64), ("has_deadline_action", I32),
+                ("deadline_action", F * MAX_ACTION_DIM), ("has_seed", I32), ("seed", U64)]
+
+
+class _IcemConfig(C.Structure):
+    _fields_ = [("horizon", U32), ("samples", U32), ("elites", U32), ("keep_elites", U32), ("iterations", U32),
+                ("noise_beta", F), ("alpha", F), ("action_dim", U32), ("bounds_low", F * MAX_ACTION_DIM),
+                ("bounds_high", F * MAX_ACTION_DIM), ("init_std", F), ("min_std", F), ("return_mean", I32),
+                ("deadline_ns", C.c_int64), ("has_deadline_action", I32), ("deadline_action", F * MAX_ACTION_DIM),
+                ("has_seed", I32), ("seed", U64)]
+
+
+class Domain(C.Structure):
+    """SkyJepaDomain (src/skyjepa_sim.rs:28-56)."""
+    _fields_ = [("mass", F), ("inertia", F * 3), ("motor_time_constant", F), ("drag", F * 3), ("thrust_scale", F),
+                ("torque_scale", F), ("arm_length", F), ("gravity", F), ("max_thrust_weight", F)]
+
+    @staticmethod
+    def default() -> "Domain":
+        d = Domain()
+        lib.orc_domain_default(C.byref(d))
+        return d
+
+    def hover_force(self) -> float:
+        return float(np.float32(self.mass) * np.float32(self.gravity) / (np.float32(4.0) * np.float32(self.thrust_scale)))
+
+
+class TrackingCost(C.Structure):
+    """SkyJepaTrackingCost (src/models/skyjepa/control.rs:19-37)."""
+    _fields_ = [("position", F), ("velocity", F), ("attitude", F), ("angular_velocity", F), ("action", F * 4)]
+
+    @staticmethod
+    def paper() -> "TrackingCost":
+        c = TrackingCost()
+        lib.orc_tracking_cost_paper(C.byref(c))
+        return c
+
+    @staticmethod
+    def make(position, velocity, attitude, angular_velocity, action) -> "TrackingCost":
+        return TrackingCost(position, velocity, attitude, angular_velocity, (F * 4)(*action))
+
+
+class TcnConfig(C.Structure):
+    _fields_ = [("input_dim", U32), ("levels", U32), ("channels", U32 * TCN_MAX_LEVELS), ("kernel_size", U32)]
+
+
+class KinematicConfig(C.Structure):
+    _fields_ = [("mass", C.c_double), ("gravity", C.c_double), ("hover_throttle", C.c_double), ("action_space", I32)]
+
+
+class SkyJepaConfig(C.Structure):
+    """SkyJepaConfig + SkyJepaProberConfig (config.rs:45-55, prober.rs:10-16)."""
+    _fields_ = [("state_dim", U32), ("action_dim", U32), ("history_steps", U32), ("rollout_steps", U32),
+                ("latent_dim", U32), ("state_encoder", TcnConfig), ("action_encoder", TcnConfig),
+                ("prober_hidden_dim", U32), ("prober_hidden_layers", U32), ("kinematics", KinematicConfig)]
+
+    @staticmethod
+    def paper() -> "SkyJepaConfig":
+        c = SkyJepaConfig()
+        lib.orc_skyjepa_config(0, C.byref(c))
+        return c
+
+    @staticmethod
+    def wide() -> "SkyJepaConfig":
+        c = SkyJepaConfig()
+        lib.orc_skyjepa_config(1, C.byref(c))
+        return c
+
+    def weight_count(self) -> int:
+        return int(lib.orc_skyjepa_weight_count(C.byref(self)))
+
+    def random_weights(self, seed: int) -> np.ndarray:
+        n = self.weight_count()
+        out = np.empty(n, dtype=np.float32)
+        if n == 0 or lib.orc_skyjepa_random_weights(C.byref(self), U64(seed), fp(out), C.c_size_t(n)) != 0:
+            raise ValueError("invalid SkyJEPA configuration")
+        return out
+
+
+class SessionConfig(C.Structure):
+    """SkyJepaSessionConfig + SkyJepaControlConfig (session.rs:40-87, control.rs:72-94)."""
+    _fields_ = [("samples", U32), ("horizon", U32), ("planner_seed", U64), ("warm_start", I32),
+                ("residual_limit_n", F), ("dynamics", I32), ("trim_multiplier", F), ("dt", F), ("iterations", U32),
+                ("temperature", F), ("action_noise", F * 4), ("cost", TrackingCost)]
+
+
+def skyjepa_weight_count(cfg) -> int:
+    return int(lib.orc_skyjepa_weight_count(C.byref(_own(SkyJepaConfig, cfg))))
+
+
+def _own(cls, obj):
+    """obj as this module's mirror `cls` (a product struct of the same header
+    layout is copied byte for byte)."""
+    if obj is None or isinstance(obj, cls):
+        return obj
+    if C.sizeof(obj) != C.sizeof(cls):
+        raise TypeError(f"{type(obj).__name__} does not have the layout of {cls.__name__}")
+    return cls.from_buffer_copy(obj)
 
 
 class NominalCtx(C.Structure):
@@ -92,6 +205,10 @@ _sig("orc_cem_plan", C.c_int, C.POINTER(_CemConfig), U32, FP, U64, U64, VP, VP, 
 _sig("orc_icem_plan", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP, UP, FP)
 _sig("orc_icem_trace", C.c_int, C.POINTER(_IcemConfig), FP, U32, FP, U64, U64, VP, VP, FP, FP, UP, FP, FP)
 _sig("orc_reference_state", None, C.c_int, F, F, F, FP)
+_sig("orc_domain_default", None, C.POINTER(Domain))
+_sig("orc_tracking_cost_paper", None, C.POINTER(TrackingCost))
+_sig("orc_skyjepa_config", None, C.c_int, C.POINTER(SkyJepaConfig))
+_sig("orc_skyjepa_random_weights", C.c_int, C.POINTER(SkyJepaConfig), U64, FP, C.c_size_t)
 _sig("orc_geometric_prior", None, FP, FP, U32, F, C.POINTER(Domain), FP)
 _sig("orc_lewm_weight_count", C.c_size_t, C.c_void_p)
 _sig("orc_lewm_new", VP, C.c_void_p, FP, C.c_size_t)
@@ -208,7 +325,7 @@ def shift(seq):
 
 
 def plant_step(domain, state, motors, cmd, dt):
-    lib.orc_plant_step(C.byref(domain), fp(state), fp(motors), fp(f32(cmd)), F(dt))
+    lib.orc_plant_step(C.byref(_own(Domain, domain)), fp(state), fp(motors), fp(f32(cmd)), F(dt))
 
 
 def nominal_rollout(initial, actions, motors, dt, substeps, domain, kernel_form=False):
@@ -216,7 +333,7 @@ def nominal_rollout(initial, actions, motors, dt, substeps, domain, kernel_form=
     N, T, _ = actions.shape
     out = np.empty((N, T, 18), np.float32)
     fn = lib.orc_nominal_rollout_k4 if kernel_form else lib.orc_nominal_rollout
-    fn(fp(f32(initial)), fp(actions), fp(f32(motors)), N, T, F(dt), substeps, C.byref(domain), fp(out))
+    fn(fp(f32(initial)), fp(actions), fp(f32(motors)), N, T, F(dt), substeps, C.byref(_own(Domain, domain)), fp(out))
     return out
 
 
@@ -224,7 +341,8 @@ def tracking_scores(pred, actions, ref_states, ref_actions, cost):
     pred = f32(pred)
     B, S, T, _ = pred.shape
     out = np.empty((B, S), np.float32)
-    lib.orc_tracking_scores(fp(pred), fp(f32(actions)), fp(f32(ref_states)), fp(f32(ref_actions)), C.byref(cost),
+    lib.orc_tracking_scores(fp(pred), fp(f32(actions)), fp(f32(ref_states)), fp(f32(ref_actions)),
+                            C.byref(_own(TrackingCost, cost)),
                             B, S, T, fp(out))
     return out
 
@@ -235,8 +353,9 @@ def nominal_scores(initial, motors, ref_states, ref_actions, cost, dt, trim, can
     B, S, T, _ = cand.shape
     scores = np.empty((B, S), np.float32)
     states = np.empty((B, S, T, 18), np.float32) if with_states else None
-    d = domain or Domain.default()
-    dd = (Domain * B)(*domains) if domains is not None else None
+    d = _own(Domain, domain) or Domain.default()
+    dd = (Domain * B)(*[_own(Domain, x) for x in domains]) if domains is not None else None
+    cost = _own(TrackingCost, cost)
     lib.orc_nominal_scores(fp(f32(initial)), fp(f32(motors)), fp(f32(ref_states)), fp(f32(ref_actions)),
                            C.byref(cost), F(dt), F(trim), substeps, C.byref(d), dd, fp(cand), B, S, T, fp(scores),
                            fp(states))
@@ -252,6 +371,7 @@ class SkyJepaModel:
         bf16 encoder outputs and GEMM copy of h; f32 state and accumulation)."""
         self.cfg = cfg
         self.weights = f32(weights)
+        cfg = _own(SkyJepaConfig, cfg)
         n = lib.orc_skyjepa_weight_count(C.byref(cfg))
         if n != self.weights.size:
             raise ValueError(f"weight blob has {self.weights.size} values, oracle layout needs {n}")
@@ -308,11 +428,13 @@ class SkyJepaModel:
         states = np.empty((B, S, T, 18), np.float32) if with_states else None
         sm, ss, am, as_ = (f32(v) for v in norm)
         lib.orc_skyjepa_scores(self.handle, fp(sm), fp(ss), fp(am), fp(as_), fp(f32(state_hist)),
-                               fp(f32(action_hist)), fp(f32(ref_states)), fp(f32(ref_actions)), C.byref(cost),
-                               F(dt), fp(cand), B, S, T, fp(masses), fp(scores), fp(states))
+                               fp(f32(action_hist)), fp(f32(ref_states)), fp(f32(ref_actions)),
+                               C.byref(_own(TrackingCost, cost)), F(dt), fp(cand), B, S, T, fp(masses), fp(scores),
+                               fp(states))
         return (scores, states) if with_states else scores
 
     def score_ctx(self, norm, state_hist, action_hist, ref_states, ref_actions, cost, dt, masses=None):
+        cost = _own(TrackingCost, cost)
         keep = [f32(v) for v in norm] + [f32(state_hist), f32(action_hist), f32(ref_states), f32(ref_actions)]
         m = None if masses is None else f32(masses)
         ctx = SkyCtx(self.handle, *(fp(v) for v in keep), cost, dt, fp(m))
@@ -326,7 +448,8 @@ def integrate(initial, actions, dt, residual, maps, kin, reference_form=False):
     N, T, _ = actions.shape
     out = np.empty((N, T, 18), np.float32)
     fn = lib.orc_integrate_reference if reference_form else lib.orc_integrate_k3
-    fn(fp(f32(initial)), fp(actions), fp(f32(dt)), fp(f32(residual)), fp(f32(maps)), N, T, C.byref(kin), fp(out))
+    fn(fp(f32(initial)), fp(actions), fp(f32(dt)), fp(f32(residual)), fp(f32(maps)), N, T,
+       C.byref(_own(KinematicConfig, kin)), fp(out))
     return out
 
 
@@ -338,8 +461,9 @@ def so3_exp(w):
 
 def nominal_ctx(initial, motors, ref_states, ref_actions, cost, dt, trim, substeps=10, domain=None, domains=None):
     keep = [f32(initial), f32(motors), f32(ref_states), f32(ref_actions)]
-    dd = (Domain * len(domains))(*domains) if domains is not None else None
-    ctx = NominalCtx(*(fp(v) for v in keep), cost, dt, trim, substeps, domain or Domain.default(), dd)
+    dd = (Domain * len(domains))(*[_own(Domain, x) for x in domains]) if domains is not None else None
+    ctx = NominalCtx(*(fp(v) for v in keep), _own(TrackingCost, cost), dt, trim, substeps,
+                     _own(Domain, domain) or Domain.default(), dd)
     ctx._keep = (keep, dd)
     return ctx
 
@@ -359,7 +483,7 @@ def _plan_common(fn_user, B, S, T, A):
 
 def mppi_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
     """scorer: python fn(cand)->scores, or (NOMINAL_FN, NominalCtx) / (SKYJEPA_FN, SkyCtx)."""
-    c = cfg._c()
+    c = _own(_MppiConfig, cfg._c())
     S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
     fnp, user, keep = _plan_common(scorer, B, S, T, A)
     seq = np.empty((B, T, A), np.float32)
@@ -374,7 +498,7 @@ def mppi_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
 
 
 def cem_plan(cfg, B, scorer, noise=None, seed=0, offset=0):
-    c = cfg._c()
+    c = _own(_CemConfig, cfg._c())
     S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
     fnp, user, keep = _plan_common(scorer, B, S, T, A)
     seq = np.empty((B, T, A), np.float32)
@@ -389,7 +513,7 @@ def cem_plan(cfg, B, scorer, noise=None, seed=0, offset=0):
 
 
 def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
-    c = cfg._c()
+    c = _own(_IcemConfig, cfg._c())
     S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
     fnp, user, keep = _plan_common(scorer, B, S, T, A)
     seq = np.empty((B, T, A), np.float32)
@@ -407,7 +531,7 @@ def icem_plan(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
 
 
 def icem_trace(cfg, B, scorer, noise=None, seed=0, offset=0, warm_start=None):
-    c = cfg._c()
+    c = _own(_IcemConfig, cfg._c())
     S, T, A = cfg.samples, cfg.horizon, cfg.action_dim
     fnp, user, keep = _plan_common(scorer, B, S, T, A)
     seq = np.empty((B, T, A), np.float32)
@@ -430,7 +554,7 @@ def reference_state(kind: int, time: float, radius: float, period: float):
 def geometric_prior(current, refs, dt, domain=None):
     refs = f32(refs)
     out = np.empty((refs.shape[0], 4), np.float32)
-    lib.orc_geometric_prior(fp(f32(current)), fp(refs), refs.shape[0], F(dt), C.byref(domain or Domain.default()),
+    lib.orc_geometric_prior(fp(f32(current)), fp(refs), refs.shape[0], F(dt), C.byref(_own(Domain, domain) or Domain.default()),
                             fp(out))
     return out
 
@@ -580,6 +704,7 @@ class SkyJepaSession:
 
     def __init__(self, cfg: SessionConfig, initial, sky=None):
         dom = Domain.default()
+        cfg = _own(SessionConfig, cfg)
         self.cfg, self.dom = cfg, dom
         self.hover = np.full(4, np.float32(dom.mass) * np.float32(dom.gravity) / np.float32(4.0), np.float32)
         self.high = np.float32(dom.mass) * np.float32(dom.gravity) * np.float32(dom.max_thrust_weight) / np.float32(4.0)

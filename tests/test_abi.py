@@ -141,7 +141,7 @@ def test_domain_sample_matches_reference_ranges_and_is_deterministic():
 @pytest.mark.parametrize("make", [L.SkyJepaConfig.paper, L.SkyJepaConfig.wide])
 def test_weight_layout_count_matches_oracle_layout(make):
     cfg = make()
-    assert cfg.weight_count() == O.lib.orc_skyjepa_weight_count(cfg)
+    assert cfg.weight_count() == O.skyjepa_weight_count(cfg)
     w = cfg.random_weights(7)
     assert w.size == cfg.weight_count() and np.isfinite(w).all()
     assert np.array_equal(w, cfg.random_weights(7))

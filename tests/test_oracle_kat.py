@@ -263,7 +263,7 @@ def test_candidate_rollout_batches_samples_and_windows():
     # tests/skyjepa.rs:79-108 (shapes, finiteness) on the tiny config
     cfg = _tiny_config()
     rng = np.random.default_rng(1)
-    w = rng.normal(0, 0.3, O.lib.orc_skyjepa_weight_count(cfg)).astype(np.float32)
+    w = rng.normal(0, 0.3, O.skyjepa_weight_count(cfg)).astype(np.float32)
     m = O.SkyJepaModel(cfg, w)
     states = rng.normal(size=(2, 4, 6)).astype(np.float32)
     ah = rng.normal(size=(2, 3, 2)).astype(np.float32)
@@ -277,7 +277,7 @@ def test_tcn_windows_are_padded_independently():
     # 10 steps (left zero padding per window), so a window equals a fresh call.
     cfg = SkyJepaConfig.paper()
     rng = np.random.default_rng(2)
-    m = O.SkyJepaModel(cfg, rng.normal(0, 0.2, O.lib.orc_skyjepa_weight_count(cfg)).astype(np.float32))
+    m = O.SkyJepaModel(cfg, rng.normal(0, 0.2, O.skyjepa_weight_count(cfg)).astype(np.float32))
     hist = rng.normal(size=(1, 9, 4)).astype(np.float32)
     cand = rng.normal(size=(1, 1, 3, 4)).astype(np.float32)
     seq = np.concatenate([hist[0], cand[0, 0]], axis=0)
@@ -292,7 +292,7 @@ def test_gru_step_matches_pytorch_gate_convention():
     import torch
     cfg = SkyJepaConfig.paper()
     rng = np.random.default_rng(3)
-    w = rng.normal(0, 0.3, O.lib.orc_skyjepa_weight_count(cfg)).astype(np.float32)
+    w = rng.normal(0, 0.3, O.skyjepa_weight_count(cfg)).astype(np.float32)
     m = O.SkyJepaModel(cfg, w)
     H, E = 24, 8
     # locate the GRU tensors in the blob (layout of include/lewm_b200.h)
