@@ -110,20 +110,9 @@ __device__ __forceinline__ bool aux_all(bool v) {
     return out != 0;
 }
 
-// Hardware tanh (MUFU.TANH); the gates use it for sigmoid as well:
-// sigmoid(v) = 0.5 + 0.5 tanh(v / 2).  Relative error ~2^-11, far inside the
-// bf16 path's tolerance.
-__device__ __forceinline__ float tanh_fast(float v) {
-    float r;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
-}
+// The gates use the hardware tanh for sigmoid as well:
+// sigmoid(v) = 0.5 + 0.5 tanh(v / 2).
 __device__ __forceinline__ float sigmoid_f(float v) { return fmaf(0.5f, tanh_fast(0.5f * v), 0.5f); }
-// Candle's tanh-approximation GELU with the hardware tanh (bf16 path).
-__device__ __forceinline__ float gelu_fast(float v) {
-    const float u = 0.7978845608028654f * v * fmaf(0.044715f * v, v, 1.0f);
-    return 0.5f * v * (1.0f + tanh_fast(u));
-}
 
 struct FastGelu {
     __device__ __forceinline__ float operator()(float v) const { return gelu_fast(v); }

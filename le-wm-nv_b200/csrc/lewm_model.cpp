@@ -215,6 +215,7 @@ LewmModel::~LewmModel() {
     g_score.reset();
     g_enc.reset();
     if (blob_bf16) cudaFree(blob_bf16);
+    if (pred_w) cudaFree(pred_w);
     if (split.tc_err) cudaFree(split.tc_err);
     if (split.partial) cudaFree(split.partial);
     if (split.counters) cudaFree(split.counters);
@@ -281,6 +282,10 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
     const size_t o_y = take(bs * W * hid), o_qkv = take(bs * W * 3 * inner), o_att = take(bs * W * inner);
     const size_t o_f = take(bs * W * c.mlp_dim), o_last = take(bs * hid), o_po = take(bs * D);
     const size_t o_p1 = take(bs * ph), o_pred = take(bs * D);
+    // the fused rollout (bf16, the image model's predictor shape) and its exchange buffers
+    const bool fused = pred_ready && precision == LWM_PRECISION_BF16 && history == 1 && T >= h && !w.has_proj;
+    const size_t xa_bytes = static_cast<size_t>((bs + 127) / 128) * 2 * 8 * 3 * 2048;
+    const size_t o_xch = fused ? take((lewm_pred_exchange_bytes(static_cast<uint32_t>(bs)) + 3) / 4) : 0;
     LWM_CU(ws.ensure(off));
     float* base = ws.ptr;
     float *f_sm = base + o_sm, *f_ah = base + o_ah, *f_act = base + o_act, *f_cond = base + o_cond;
@@ -310,6 +315,30 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
         LWM_CU(gemm_f32(sp, gemm(f_cond, hid, w.blocks[l].ada, f_ada + static_cast<size_t>(l) * all * 6 * hid, 6 * hid,
                              rows_all), s));
         ++n;
+    }
+    if (fused) {
+        // the whole rollout in one launch
+        PredArgs a = pred;
+        a.tokens = static_cast<uint32_t>(bs);
+        a.S = S;
+        a.T = T;
+        a.h = h;
+        a.steps = T - h + 1;
+        a.emb = emb;
+        a.pos = w.pos;
+        a.ada = base + o_ada;
+        a.pred = f_pred;
+        a.xa = reinterpret_cast<uint8_t*>(base + o_xch);
+        a.xp = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(base + o_xch) + xa_bytes);
+        a.err = split.tc_err;
+        a.wait_polls = 0;
+        LWM_CU(launch_lewm_pred(a, s));
+        ++n;
+        LWM_CU(launch_goal_cost(f_pred, goal, S, bs, D, scores, s));
+        ++n;
+        if (last_emb) LWM_CU(cudaMemcpyAsync(last_emb, f_pred, bs * D * sizeof(float), cudaMemcpyDeviceToDevice, s));
+        launches = n + split_launches;
+        return cudaSuccess;
     }
     LWM_CU(launch_frames_init(emb, h, S, f_frames, nframes, bs, D, s));
     ++n;
@@ -543,6 +572,9 @@ cudaError_t LewmModel::set_precision(int p, cudaStream_t s) {
         for_each_lin(w, [](Lin& l) { l.wb = nullptr; });
         if (blob_bf16) cudaFree(blob_bf16);
         blob_bf16 = nullptr;
+        if (pred_w) cudaFree(pred_w);
+        pred_w = nullptr;
+        pred_ready = false;
         if (split.tc_err) cudaFree(split.tc_err);
         split.tc_err = nullptr;
         precision = p;
@@ -569,8 +601,70 @@ cudaError_t LewmModel::set_precision(int p, cudaStream_t s) {
         off += (n + 127) & ~static_cast<size_t>(127);
     });
     LWM_CU(err);
+    LWM_CU(build_pred(s));
     LWM_CU(cudaStreamSynchronize(s));
     precision = p;
+    return cudaSuccess;
+}
+
+// The fused predictor's packed weights and its per-half-layer views, when the
+// model has the shape lewm_pred_kernel takes; otherwise the rollout keeps its
+// per-GEMM launch sequence.
+cudaError_t LewmModel::build_pred(cudaStream_t s) {
+    pred_ready = false;
+    const char* why = nullptr;
+    if (!lewm_pred_supported(c, c.history_size, &why)) return cudaSuccess;
+    const uint32_t inner = c.heads * c.dim_head, L = c.depth;
+    size_t total = 0;
+    for (uint32_t l = 0; l < L; ++l) total += 8 * (lewm_pred_half_bytes(inner) + lewm_pred_half_bytes(c.mlp_dim));
+    total += 8 * lewm_pred_half_bytes(c.pred_proj_hidden);
+    if (!pred_w) LWM_CU(cudaMalloc(&pred_w, total));
+    PredArgs a{};
+    size_t off = 0;
+    auto half = [&](uint32_t i, int kind, uint32_t layer, const float* w1, uint32_t row0, uint32_t ld1,
+                    const float* w2, uint32_t ld2, uint32_t n1_total) -> cudaError_t {
+        PredHalf& h = a.half[i];
+        h.w = pred_w + off;
+        h.bytes = static_cast<uint32_t>(lewm_pred_half_bytes(n1_total));
+        h.n1 = n1_total / 8;
+        h.kind = kind;
+        h.layer = layer;
+        const cudaError_t e = lewm_pred_pack(w1, row0, ld1, w2, ld2, n1_total, pred_w + off, s);
+        off += static_cast<size_t>(8) * h.bytes;
+        return e;
+    };
+    for (uint32_t l = 0; l < L; ++l) {
+        const BlockW& b = w.blocks[l];
+        // attention half: V = rows [2 inner, 3 inner) of the qkv projection, then the out-projection
+        LWM_CU(half(2 * l, 0, l, b.qkv.w, 2 * inner, b.qkv.in, b.to_out.w, b.to_out.in, inner));
+        PredHalf& ha = a.half[2 * l];
+        ha.b1 = b.qkv.b ? b.qkv.b + static_cast<size_t>(2) * inner : nullptr;
+        ha.b2 = b.to_out.b;
+        ha.ln_w = b.attn_norm.w;
+        ha.ln_b = b.attn_norm.b;
+        LWM_CU(half(2 * l + 1, 1, l, b.fc1.w, 0, b.fc1.in, b.fc2.w, b.fc2.in, c.mlp_dim));
+        PredHalf& hm = a.half[2 * l + 1];
+        hm.b1 = b.fc1.b;
+        hm.b2 = b.fc2.b;
+        hm.ln_w = b.mlp_norm.w;
+        hm.ln_b = b.mlp_norm.b;
+    }
+    const MlpW& pp = w.pred_proj;
+    LWM_CU(half(2 * L, 2, 0, pp.fc1.w, 0, pp.fc1.in, pp.fc2.w, pp.fc2.in, c.pred_proj_hidden));
+    PredHalf& hp = a.half[2 * L];
+    hp.b1 = pp.fc1.b;
+    hp.b2 = pp.fc2.b;
+    if (pp.norm.kind == kNormBatch) {
+        hp.bn_w = pp.norm.w;
+        hp.bn_b = pp.norm.b;
+        hp.bn_rm = pp.norm.rm;
+        hp.bn_rv = pp.norm.rv;
+    }
+    hp.ln_w = w.final_norm.w;
+    hp.ln_b = w.final_norm.b;
+    a.halves = 2 * L + 1;
+    pred = a;
+    pred_ready = true;
     return cudaSuccess;
 }
 

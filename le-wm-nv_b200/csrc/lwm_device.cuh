@@ -56,6 +56,19 @@ __device__ __forceinline__ float gelu_tanh(float v) {
                                             1.0f + __fmul_rn(__fmul_rn(0.044715f, v), v))));
 }
 
+// Hardware tanh (MUFU.TANH, tanh.approx.f32): relative error about 2^-11,
+// inside the bf16 paths' tolerance, where its result is rounded to bf16.
+__device__ __forceinline__ float tanh_fast(float v) {
+    float r;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+// Candle's tanh-approximation GELU with the hardware tanh (bf16 paths).
+__device__ __forceinline__ float gelu_fast(float v) {
+    const float u = 0.7978845608028654f * v * fmaf(0.044715f * v, v, 1.0f);
+    return 0.5f * v * (1.0f + tanh_fast(u));
+}
+
 // 1 / (1 + exp(-v)); the correctly rounded reciprocal equals IEEE 1/x exactly.
 __device__ __forceinline__ float sigmoid(float v) { return __frcp_rn(1.0f + expf(-v)); }
 

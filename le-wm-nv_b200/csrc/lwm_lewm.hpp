@@ -83,6 +83,53 @@ cudaError_t launch_patchify(const float* pix, float* patches, uint32_t n, uint32
 cudaError_t launch_vit_assemble(const float* patch_out, const float* cls, const float* pos, float* x, uint32_t n,
                                 uint32_t np, uint32_t vh, cudaStream_t s);
 
+// ------------------------------------------------- fused predictor rollout
+//
+// The predictor's whole rollout in one launch for the image model's shape
+// (width 192, one-frame windows), bf16 on the tensor cores:
+// kernels_lewm_pred.cu.  Half-layers in order: attention and MLP halves of
+// every layer, then pred_proj; each a pair of GEMMs split over the 8 CTAs of
+// a cluster.
+constexpr uint32_t kPredMaxHalves = 2 * 8 + 1;
+
+// One half-layer's device views (the caller's f32 blob and the packed bf16 weights).
+struct PredHalf {
+    const uint8_t* w;   // this half-layer's packed weights of CTA rank 0 (rank j at + j * bytes)
+    uint32_t bytes;     // per rank: W1 blocks, then W2 blocks
+    uint32_t n1;        // first GEMM's columns per rank (64..256)
+    const float* b1;    // first GEMM's bias (full width) or nullptr
+    const float* b2;    // second GEMM's bias [192] or nullptr
+    const float *bn_w, *bn_b, *bn_rm, *bn_rv;  // pred_proj BatchNorm (eval) or nullptr
+    const float *ln_w, *ln_b;  // the LayerNorm that produces this half-layer's A (AdaLN's affine / final)
+    int kind;
+    uint32_t layer;     // transformer layer (AdaLN table slice)
+};
+
+struct PredArgs {
+    PredHalf half[kPredMaxHalves];
+    uint32_t halves;          // 2 depth + 1
+    uint32_t tokens;          // B S
+    uint32_t S, T, h, steps;  // samples per vehicle, horizon, context frames, steps = T - h + 1
+    const float* emb;         // [B, h, 192] context embeddings
+    const float* pos;         // [192] position embedding 0
+    const float* ada;         // [depth][tokens * T][6 * 192]
+    float* pred;              // [tokens, 192] the last step's frame
+    uint8_t* xa;              // A exchange [tiles][2][8 owners][3][2 KB]
+    float* xp;                // partial exchange [tiles][2][8 src][8 owners][16][192]
+    int* err;
+    uint32_t wait_polls;
+};
+
+bool lewm_pred_supported(const lwm_lewm_config& c, uint32_t history, const char** why);
+// Bytes of one half-layer's packed weights per CTA rank (first GEMM width n1_total).
+size_t lewm_pred_half_bytes(uint32_t n1_total);
+// Packs rows [w1_row0, w1_row0 + n1_total) of w1 ([., 192], row stride w1_ld)
+// and the matching n1_total columns of w2 ([192, w2_ld]) for the 8 ranks.
+cudaError_t lewm_pred_pack(const float* w1, uint32_t w1_row0, uint32_t w1_ld, const float* w2, uint32_t w2_ld,
+                           uint32_t n1_total, uint8_t* out, cudaStream_t s);
+size_t lewm_pred_exchange_bytes(uint32_t tokens);
+cudaError_t launch_lewm_pred(const PredArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------------ host model
 
 struct Lin {
@@ -161,6 +208,11 @@ struct LewmModel {
     float* blob = nullptr;  // device weights
     uint16_t* blob_bf16 = nullptr;  // bf16 copies of the GEMM weights, each 256-byte aligned
     int precision = LWM_PRECISION_F32;
+    // bf16 with the image model's predictor shape: the whole rollout in one
+    // launch (lewm_pred_kernel) with its weights packed per CTA rank
+    uint8_t* pred_w = nullptr;
+    PredArgs pred{};
+    bool pred_ready = false;
     // per-plan context
     uint32_t B = 0, h = 0, history = 0;
     float* emb = nullptr;   // [B, h, D]
@@ -181,6 +233,7 @@ struct LewmModel {
     // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
     // GEMM inputs on the tensor cores, f32 accumulation and activations.
     cudaError_t set_precision(int p, cudaStream_t s);
+    cudaError_t build_pred(cudaStream_t s);
     // scores [B,S] of candidates [B,S,T,A] (all device)
     cudaError_t score(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
     cudaError_t encode_vector(const float* obs, uint32_t n, float* out, cudaStream_t s);
