@@ -61,8 +61,10 @@ constexpr uint32_t kStage = 32 * 1024;      // weight ring stage (a [256 x 64] b
 constexpr uint32_t kStages = 3;
 constexpr uint32_t kColD2 = 256;            // TMEM column of the second GEMM's accumulator
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kThreads = 320;
-constexpr uint32_t kCompWarp0 = 2, kCompWarps = 8, kCompThreads = kCompWarps * 32, kCompBarrier = 1;
+constexpr uint32_t kCompWarp0 = 2, kCompWarps = 16, kCompThreads = kCompWarps * 32, kCompBarrier = 1;
+constexpr uint32_t kThreads = (kCompWarp0 + kCompWarps) * 32;  // 576
+constexpr uint32_t kColSplit = kCompWarps / 4;  // compute warps per TMEM lane quadrant
+constexpr uint32_t kRowsPerWarp = kOwn / kCompWarps;
 constexpr uint32_t kOwnChunk = kOwn * 128;  // an owner's 16 rows of one A block: 2 KB
 constexpr uint32_t kPerLane = kD / 32;      // 6 residual columns a lane holds
 
@@ -317,13 +319,15 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
     } else {
         // ================= accumulator drains and the owner work
         const uint32_t cw = warp - kCompWarp0;          // 0..7
-        const uint32_t q = warp & 3u, half = cw >> 2;   // TMEM lane quadrant, column half
+        const uint32_t q = warp & 3u, part = cw >> 2;   // TMEM lane quadrant, column part
         const uint32_t row = q * 32 + lane;             // accumulator row = token of the tile
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         // the owned tokens of this warp: rows 2 cw, 2 cw + 1 of the CTA's 16
-        const uint32_t tok0 = tile * kM + c * kOwn + 2 * cw;
-        const bool live0 = tok0 < p.tokens, live1 = tok0 + 1 < p.tokens;
-        float x[2][kPerLane];
+        const uint32_t tok0 = tile * kM + c * kOwn + kRowsPerWarp * cw;
+        bool live[kRowsPerWarp];
+#pragma unroll
+        for (uint32_t r = 0; r < kRowsPerWarp; ++r) live[r] = tok0 + r < p.tokens;
+        float x[kRowsPerWarp][kPerLane];
         uint8_t* own_base = s.own[0];
         const uint32_t own_s = tc::smem_u32(own_base);
 
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
         // scale of this lane's columns, and the LayerNorm affine), fetched
         // ahead of the wait that precedes their use.
         struct Next {
-            float sh[2][kPerLane], sc[2][kPerLane], lw[kPerLane], lb[kPerLane];
+            float sh[kRowsPerWarp][kPerLane], sc[kRowsPerWarp][kPerLane], lw[kPerLane], lb[kPerLane];
             int kind;
         };
         auto fetch_next = [&](uint32_t g_next, Next& nx) {
@@ -346,8 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             if (hn.kind == kPred) return;
             const uint32_t sh_off = hn.kind == kAttn ? 0 : 3 * kD, sc_off = sh_off + kD;
 #pragma unroll
-            for (uint32_t r = 0; r < 2; ++r) {
-                const uint32_t tok = (r ? live1 : live0) ? tok0 + r : 0;
+            for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+                const uint32_t tok = live[r] ? tok0 + r : 0;
                 const size_t arow = static_cast<size_t>(tok) * p.T + (p.h - 1 + step);
                 const float* a = p.ada + (static_cast<size_t>(hn.layer) * p.tokens * p.T + arow) * 6 * kD;
 #pragma unroll
@@ -360,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
         // the A rows of the next half-layer from the owned residual rows
         auto publish_a = [&](uint32_t g_next, const Next& nx) {
 #pragma unroll
-            for (uint32_t r = 0; r < 2; ++r) {
-                const bool live = r ? live1 : live0;
+            for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
                 float v[kPerLane];
 #pragma unroll
                 for (uint32_t i = 0; i < kPerLane; ++i) v[i] = x[r][i];
@@ -381,12 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
                     for (uint32_t i = 0; i < kPerLane; ++i) v[i] = (v[i] - mean) / den * nx.lw[i] + nx.lb[i];
                 }
                 // bf16, SW128 K-major: row 2 cw + r of the owner's 16, column col
-                const uint32_t orow = 2 * cw + r;
+                const uint32_t orow = kRowsPerWarp * cw + r;
 #pragma unroll
                 for (uint32_t i = 0; i < kPerLane; ++i) {
                     const uint32_t col = lane + 32 * i, kb = col / kKB;
                     *reinterpret_cast<uint16_t*>(own_base + kb * kOwnChunk + tc::sw128_offset(orow, col % kKB)) =
-                        bf16_bits(live ? v[i] : 0.0f);
+                        bf16_bits(live[r] ? v[i] : 0.0f);
                 }
             }
             tc::fence_async_smem();
@@ -402,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
         };
 
         // the first step's input: x = frame + pos[0], the frame the last context embedding
-        for (uint32_t r = 0; r < 2; ++r) {
-            const uint32_t tok = (r ? live1 : live0) ? tok0 + r : 0;
+        for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+            const uint32_t tok = live[r] ? tok0 + r : 0;
             const float* e = p.emb + (static_cast<size_t>(tok / p.S) * p.h + (p.h - 1)) * kD;
 #pragma unroll
             for (uint32_t i = 0; i < kPerLane; ++i) {
@@ -443,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             if (!(ok = comp_all(ok))) break;
             tc::fence_after();
             {
-                const uint32_t cols = n1 / 2, c0 = half * cols;
+                const uint32_t cols = n1 / kColSplit, c0 = part * cols;
                 for (uint32_t cc = 0; cc < cols; cc += 32) {
                     float v[32];
                     tc::tmem_ld16(lane_base + c0 + cc, *reinterpret_cast<float(*)[16]>(v));
@@ -498,14 +501,15 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
                 // over the banks; the owners undo the permutation
                 const uint32_t o = row / kOwn, rr = row % kOwn;
                 uint8_t* chunk = (o < 4 ? s.X[0] : s.H[0]) + (o & 3u) * kPartChunk + rr * kPartRow;
-                const uint32_t c0 = half * (kD / 2);
-                for (uint32_t cc = 0; cc < kD / 2; cc += 32) {
-                    float v[32];
-                    tc::tmem_ld16(lane_base + kColD2 + c0 + cc, *reinterpret_cast<float(*)[16]>(v));
-                    tc::tmem_ld16(lane_base + kColD2 + c0 + cc + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+                constexpr uint32_t kCols2 = kD / kColSplit;  // 48
+                const uint32_t c0 = part * kCols2;
+#pragma unroll
+                for (uint32_t cc = 0; cc < kCols2; cc += 16) {
+                    float v[16];
+                    tc::tmem_ld16(lane_base + kColD2 + c0 + cc, v);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (uint32_t i = 0; i < 32; i += 4) {
+                    for (uint32_t i = 0; i < 16; i += 4) {
                         const uint32_t u = ((c0 + cc + i) >> 2) ^ (rr & 7u);
                         *reinterpret_cast<float4*>(chunk + u * 16) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
                     }
@@ -531,12 +535,12 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             }
             // ---- owner: this half-layer's gates and the next one's AdaLN inputs, fetched
             // while the partials arrive; then the 8 partials of the owned rows in CTA order
-            float gate[2][kPerLane], bias2[kPerLane];
+            float gate[kRowsPerWarp][kPerLane], bias2[kPerLane];
             if (kind != kPred) {
                 const uint32_t gate_off = kind == kAttn ? 2 * kD : 5 * kD;
 #pragma unroll
-                for (uint32_t r = 0; r < 2; ++r) {
-                    const uint32_t tok = (r ? live1 : live0) ? tok0 + r : 0;
+                for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+                    const uint32_t tok = live[r] ? tok0 + r : 0;
                     const size_t arow = static_cast<size_t>(tok) * p.T + (p.h - 1 + step);
                     const float* gt = p.ada + (static_cast<size_t>(layer) * p.tokens * p.T + arow) * 6 * kD + gate_off;
 #pragma unroll
@@ -549,16 +553,16 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             if (!(ok = comp_all(wait_cluster(&s.p_ready[ph], (g >> 1) & 1u, err, 13, g, lim)))) break;
             {
                 const float* src = xp_tile + static_cast<size_t>(ph) * kTP * kTP * kOwn * kD;
-                float sum[2][kPerLane];
+                float sum[kRowsPerWarp][kPerLane];
 #pragma unroll
-                for (uint32_t r = 0; r < 2; ++r)
+                for (uint32_t r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
                     for (uint32_t i = 0; i < kPerLane; ++i) sum[r][i] = 0.0f;
 #pragma unroll
                 for (uint32_t j = 0; j < kTP; ++j)
 #pragma unroll
-                    for (uint32_t r = 0; r < 2; ++r) {
-                        const uint32_t orow = 2 * cw + r;
+                    for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+                        const uint32_t orow = kRowsPerWarp * cw + r;
                         const float* pr = src + ((static_cast<size_t>(j) * kTP + c) * kOwn + orow) * kD;
 #pragma unroll
                         for (uint32_t i = 0; i < kPerLane; ++i) {
@@ -567,8 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
                         }
                     }
 #pragma unroll
-                for (uint32_t r = 0; r < 2; ++r) {
-                    const bool live = r ? live1 : live0;
+                for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
 #pragma unroll
                     for (uint32_t i = 0; i < kPerLane; ++i) {
                         const uint32_t col = lane + 32 * i;
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
                         if (kind == kPred) {
                             // the predicted frame; the next step's input adds pos[0]
                             if (g + 1 == G) {
-                                if (live) p.pred[static_cast<size_t>(tok0 + r) * kD + col] = t;
+                                if (live[r]) p.pred[static_cast<size_t>(tok0 + r) * kD + col] = t;
                             } else {
                                 x[r][i] = t + __ldg(p.pos + col);
                             }
