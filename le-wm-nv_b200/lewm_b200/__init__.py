@@ -269,8 +269,9 @@ NORM_KINDS = {"batch": 0, "layer": 1, "none": 2}
 
 
 class _PlanResult(C.Structure):
-    _fields_ = [("first_action", FP), ("sequence", FP), ("scores", FP), ("scores_capacity", C.c_size_t),
-                ("best_indices", C.POINTER(U32)), ("batch", U32), ("scores_cols", U32),
+    # the output pointers as plain addresses (filled by _addr, the cheap path)
+    _fields_ = [("first_action", VP), ("sequence", VP), ("scores", VP), ("scores_capacity", C.c_size_t),
+                ("best_indices", VP), ("batch", U32), ("scores_cols", U32),
                 ("iterations_completed", U32), ("elapsed_ns", U64), ("deadline_reached", I32),
                 ("deadline_outcome", I32)]
 
@@ -339,14 +340,14 @@ _sig("lwm_skyjepa_random_weights", C.c_int, C.POINTER(SkyJepaConfig), U64, FP, C
 _sig("lwm_scorer_skyjepa_create", C.c_int, VP, C.POINTER(SkyJepaConfig), FP, C.c_size_t, FP, FP, FP, FP,
      C.POINTER(TrackingCost), F, C.POINTER(VP))
 _sig("lwm_scorer_skyjepa_set_context", C.c_int, VP, U32, U32, FP, FP, FP, FP)
-_sig("lwm_scorer_skyjepa_set_context_ex", C.c_int, VP, U32, U32, FP, FP, FP, FP, FP)
+_sig("lwm_scorer_skyjepa_set_context_ex", C.c_int, VP, U32, U32, VP, VP, VP, VP, VP)
 _sig("lwm_scorer_skyjepa_set_precision", C.c_int, VP, I32)
 _sig("lwm_scorer_lewm_set_precision", C.c_int, VP, I32)
 _sig("lwm_scorer_callback_create", C.c_int, VP, U32, SCORE_FN, VP, C.POINTER(VP))
 _sig("lwm_scorer_score_device", C.c_int, VP, VP, U32, U32, U32, U32, VP)
 _sig("lwm_scorer_predict_device", C.c_int, VP, VP, U32, U32, U32, VP)
 _sig("lwm_scorer_destroy", C.c_int, VP)
-_sig("lwm_plan", C.c_int, VP, VP, FP, C.POINTER(_PlanResult))
+_sig("lwm_plan", C.c_int, VP, VP, VP, C.POINTER(_PlanResult))
 _sig("lwm_plan_device", C.c_int, VP, VP, VP, C.POINTER(_PlanDeviceResult))
 _sig("lwm_lowest_k_device", C.c_int, VP, VP, U32, U32, U32, VP)
 _sig("lwm_color_noise_device", C.c_int, VP, VP, VP, U32, U32, U32, U32, F)
@@ -410,6 +411,18 @@ def _fp(a: Optional[np.ndarray]):
         return None
     assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(FP)
+
+
+def _addr(a: Optional[np.ndarray]) -> Optional[int]:
+    """The address of a C-contiguous array's data for c_void_p arguments: a
+    view of its buffer for writable arrays (about a fifth of the cost of
+    ndarray.ctypes), ndarray.ctypes.data otherwise."""
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    if a.flags["WRITEABLE"] and a.nbytes:
+        return C.addressof(C.c_char.from_buffer(a))
+    return a.ctypes.data
 
 
 def _f32(x, shape=None) -> np.ndarray:
@@ -767,9 +780,9 @@ class SkyJepaScorer(Scorer):
         sh = _f32(state_history)
         ref = _f32(reference_states)
         m = None if vehicle_mass is None else _f32(vehicle_mass)
-        _check(lib.lwm_scorer_skyjepa_set_context_ex(self.handle, sh.shape[0], ref.shape[1], _fp(sh),
-                                                     _fp(_f32(action_history)), _fp(ref),
-                                                     _fp(_f32(reference_actions)), _fp(m)))
+        _check(lib.lwm_scorer_skyjepa_set_context_ex(self.handle, sh.shape[0], ref.shape[1], _addr(sh),
+                                                     _addr(_f32(action_history)), _addr(ref),
+                                                     _addr(_f32(reference_actions)), _addr(m)))
         self.batch = sh.shape[0]
 
 
@@ -902,13 +915,13 @@ class _Planner:
         seq = np.empty((B, T, A), np.float32)
         sc = np.empty((B, S), np.float32)
         best = np.empty((B,), np.uint32)
-        r = _PlanResult(_fp(fa), _fp(seq), _fp(sc), C.c_size_t(sc.size), best.ctypes.data_as(C.POINTER(U32)))
+        r = _PlanResult(_addr(fa), _addr(seq), _addr(sc), sc.size, _addr(best))
         noise = None if injected_noise is None else _f32(injected_noise)
-        _check(lib.lwm_plan(self.handle, scorer.handle, _fp(noise), C.byref(r)))
+        _check(lib.lwm_plan(self.handle, scorer.handle, _addr(noise), C.byref(r)))
         cols = r.scores_cols
-        return PlanResult(fa, seq, sc.reshape(-1)[: B * cols].reshape(B, cols).copy(), [int(x) for x in best],
-                          int(r.iterations_completed), r.elapsed_ns * 1e-9, bool(r.deadline_reached),
-                          _OUTCOME[r.deadline_outcome])
+        scores = sc if cols == S else sc.reshape(-1)[: B * cols].reshape(B, cols).copy()
+        return PlanResult(fa, seq, scores, best.tolist(), int(r.iterations_completed), r.elapsed_ns * 1e-9,
+                          bool(r.deadline_reached), _OUTCOME[r.deadline_outcome])
 
     def plan_device(self, scorer: Scorer, injected_noise_ptr: Optional[int] = None) -> PlanDeviceResult:
         r = _PlanDeviceResult()
