@@ -18,9 +18,9 @@
 // shared memory once, at the start, with 16-byte cp.async.  In a stage, warp
 // w computes channel 8c + w at the stage's positions: the lanes split the
 // input channels, a butterfly reduction gives every lane all sums, lane k
-// finishes position k (bias, GELU, residual) and writes it into the
-// activation of all 16 CTAs (distributed shared memory); one cluster barrier
-// closes the stage.
+// finishes position k (bias, GELU, residual) and writes it into this CTA's
+// activation; after one cluster barrier every CTA pulls the peers' channels
+// of that activation from their shared memory (distributed shared memory).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -65,13 +65,25 @@ __device__ __forceinline__ uint32_t cta_rank() {
 __device__ __forceinline__ void cluster_barrier() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// v into the float at `local` (a shared-memory address) in every CTA of the cluster
-__device__ __forceinline__ void broadcast(uint32_t local, float v) {
-#pragma unroll
-    for (uint32_t d = 0; d < kCl; ++d) {
+// Every peer d's channels [8 d, 8 d + 8) of the activation at float offset
+// `off` ([pos][128]), at positions P0 + k PSTEP (k < NP), into this CTA's
+// copy: 16-byte loads from the peers' shared memory (each CTA writes only
+// its own channels; after the cluster barrier every CTA pulls the rest).
+template <int NP, int P0, int PSTEP>
+__device__ __forceinline__ void pull(float* sm, uint32_t off, uint32_t c, uint32_t tid) {
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm));
+    for (uint32_t q = tid; q < kCl * NP * 2; q += kThreads) {
+        const uint32_t d = q / (NP * 2), k = (q / 2) % NP, h = q % 2;
+        if (d == c) continue;
+        const uint32_t e = off + (P0 + k * PSTEP) * kC + d * kPer + h * 4;
         uint32_t r;
-        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(d));
-        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(sbase + e * 4u), "r"(d));
+        float4 v;
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(r)
+                     : "memory");
+        *reinterpret_cast<float4*>(sm + e) = v;
     }
 }
 // n floats (a multiple of 4, both addresses 16-byte aligned) global -> shared
@@ -145,18 +157,18 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    cluster_barrier();  // every CTA runs (and holds its weights) before the first remote write
 
     const uint32_t o = o0 + warp;
-    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm));
-    auto out_addr = [&](uint32_t off, int p) { return sbase + (off + p * kC + o) * 4u; };
+    auto out = [&](uint32_t off, int p) -> float& { return sm[off + p * kC + o]; };
     // ---- level 1, conv1 at all positions
     {
         float acc[10];
         conv_sums<kIn, 10, 0, 1, 1>(sm + kOffW1a + warp * kIn * 3, X, kXLd, lane, acc);
-        if (lane < 10) broadcast(out_addr(kOffH1, lane), gelu_tanh(pick(acc, lane) + __ldg(L1.b1 + o)));
+        if (lane < 10) out(kOffH1, lane) = gelu_tanh(pick(acc, lane) + __ldg(L1.b1 + o));
     }
     cluster_barrier();
+    pull<10, 0, 1>(sm, kOffH1, c, tid);
+    __syncthreads();
     // ---- level 1, conv2 + residual projection at the odd positions
     {
         float acc[5];
@@ -171,17 +183,21 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
                 r1 = fmaf(wr[i + 1], X[p * kXLd + i + 1], r1);
             }
             const float res = (r0 + r1) + __ldg(L1.br + o);
-            broadcast(out_addr(kOffY1, p), gelu_tanh(h2 + res));
+            out(kOffY1, p) = gelu_tanh(h2 + res);
         }
     }
     cluster_barrier();
+    pull<5, 1, 2>(sm, kOffY1, c, tid);
+    __syncthreads();
     // ---- level 2, conv1 at the odd positions
     {
         float acc[5];
         conv_sums<kC, 5, 1, 2, 2>(sm + kOffW1b + warp * kC * 3, sm + kOffY1, kC, lane, acc);
-        if (lane < 5) broadcast(out_addr(kOffH2, 1 + 2 * lane), gelu_tanh(pick(acc, lane) + __ldg(L2.b1 + o)));
+        if (lane < 5) out(kOffH2, 1 + 2 * lane) = gelu_tanh(pick(acc, lane) + __ldg(L2.b1 + o));
     }
     cluster_barrier();
+    pull<5, 1, 2>(sm, kOffH2, c, tid);
+    __syncthreads();
     // ---- level 2, conv2 + identity residual at 1, 5, 9
     {
         float acc[3];
@@ -189,27 +205,33 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
         if (lane < 3) {
             const int p = 1 + 4 * static_cast<int>(lane);
             const float h2 = gelu_tanh(pick(acc, lane) + __ldg(L2.b2 + o));
-            broadcast(out_addr(kOffY2, p), gelu_tanh(h2 + sm[kOffY1 + p * kC + o]));
+            out(kOffY2, p) = gelu_tanh(h2 + sm[kOffY1 + p * kC + o]);
         }
     }
     cluster_barrier();
+    pull<3, 1, 4>(sm, kOffY2, c, tid);
+    __syncthreads();
     // ---- level 3, conv1 at 1, 5, 9
     {
         float acc[3];
         conv_sums<kC, 3, 1, 4, 4>(sm + kOffW1c + warp * kC * 3, sm + kOffY2, kC, lane, acc);
-        if (lane < 3) broadcast(out_addr(kOffH3, 1 + 4 * lane), gelu_tanh(pick(acc, lane) + __ldg(L3.b1 + o)));
+        if (lane < 3) out(kOffH3, 1 + 4 * lane) = gelu_tanh(pick(acc, lane) + __ldg(L3.b1 + o));
     }
     cluster_barrier();
+    pull<3, 1, 4>(sm, kOffH3, c, tid);
+    __syncthreads();
     // ---- level 3, conv2 + identity residual at 9
     {
         float acc[1];
         conv_sums<kC, 1, 9, 1, 4>(sm + kOffW2c + warp * kC * 3, sm + kOffH3, kC, lane, acc);
         if (lane == 0) {
             const float h2 = gelu_tanh(acc[0] + __ldg(L3.b2 + o));
-            broadcast(out_addr(kOffY3, 9), gelu_tanh(h2 + sm[kOffY2 + 9 * kC + o]));
+            out(kOffY3, 9) = gelu_tanh(h2 + sm[kOffY2 + 9 * kC + o]);
         }
     }
-    cluster_barrier();  // after it no CTA writes another's shared memory
+    cluster_barrier();
+    pull<1, 9, 1>(sm, kOffY3, c, tid);
+    __syncthreads();
     // ---- the projection of position 9: outputs 16c + 2w, 16c + 2w + 1
     const float* y = sm + kOffY3 + 9 * kC;
 #pragma unroll
@@ -226,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
             h0[static_cast<size_t>(b) * kLat + oo] = s + __ldg(a.proj_b + oo);
         }
     }
+    cluster_barrier();  // no CTA leaves while a peer may still read its shared memory
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
