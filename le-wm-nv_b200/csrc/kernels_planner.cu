@@ -87,21 +87,12 @@ __global__ void __launch_bounds__(256) sample_elem_kernel(SampleArgs a) {
     const uint32_t s = static_cast<uint32_t>(row % a.S);
     const uint32_t b = static_cast<uint32_t>(row / a.S);
     const uint32_t g = a.sample_base + s;  // the candidate's row in the (unsharded) plan
-    const size_t mi = (static_cast<size_t>(b) * a.T + t) * a.A + act;
     float v;
-    if (a.carried && g >= 1 && g <= a.inject) {
+    if (a.carried && g >= 1 && g <= a.inject)
         v = a.carried[((static_cast<size_t>(b) * a.carried_count + (g - 1)) * a.T + t) * a.A + act];
-    } else {
-        if (g == 0) {
-            v = a.mean[mi];
-        } else {
-            const uint64_t gi = global_row(b, s, a.sample_base, a.sample_total, a.S) * TA +
-                                static_cast<uint64_t>(t) * a.A + act;
-            const float eps = a.noise ? a.noise[e] : normal_at(a.seed, a.offset + gi);
-            v = __fadd_rn(a.mean[mi], __fmul_rn(eps, a.std[mi]));
-        }
-        v = cmin(cmax(v, a.low[act]), a.high[act]);
-    }
+    else
+        v = sample_white(a.mean, a.std, a.low, a.high, a.noise, a.seed, a.offset, a.sample_base, a.sample_total, b, s,
+                         t, act, a.S, a.T, a.A);
     a.out[e] = v;
 }
 

@@ -39,10 +39,10 @@
 // partial of the CTA's 8 rows.  Every hand-off is an mbarrier with a bounded
 // wait; a wait that gives up records its site and the kernel unwinds.
 //
-// Before it, per plan: sample_kernel (candidates), skyjepa_mma_inputs_kernel
-// (the action encoder of every (candidate, step) as split-fp16 x tiles with a
-// constant-1 column that carries the GRU biases) and the history encoder
-// (h0 per vehicle, on a side stream).
+// Before it, per plan: skyjepa_mma_inputs_kernel (the candidates, sampled as
+// sample_elem_kernel does, and the action encoder of every (candidate, step)
+// as split-fp16 x tiles with a constant-1 column that carries the GRU biases)
+// and the history encoder (h0 per vehicle, on a side stream).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -50,6 +50,7 @@
 #include <mutex>
 
 #include "lwm_device.cuh"
+#include "lwm_mppi.cuh"
 #include "lwm_kernels.hpp"
 #include "lwm_skyjepa_dev.cuh"
 #include "lwm_skyjepa_tcn.cuh"
@@ -289,17 +290,23 @@ struct MmaTcnConst {
 
 __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, const __grid_constant__ MmaTcnConst tw,
                                                                  uint8_t* xtiles, int* err) {
-    // the rollout's error word starts clear (the rollout follows on this stream)
-    if (blockIdx.x == 0 && threadIdx.x < 4) err[threadIdx.x] = 0;
-    // four lanes per (candidate, step): lane o computes the encoder's channel o
-    const uint64_t gt = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const uint32_t o = static_cast<uint32_t>(gt & 3u), base = threadIdx.x & 28u;
-    const uint64_t total = static_cast<uint64_t>(a.B) * a.S * a.T;
-    const bool live = (gt >> 2) < total;
-    const uint64_t i = live ? (gt >> 2) : total - 1;  // dead lanes still take part in the shuffles
-    const uint32_t t = static_cast<uint32_t>(i % a.T);
-    const uint64_t grow = i / a.T;  // b * S + s
-    const uint32_t b = static_cast<uint32_t>(grow / a.S);
+    // one block per candidate: thread 4 t + o samples the candidate's action o
+    // at step t (white noise, as sample_elem_kernel) and, with the other three
+    // lanes of its group, encodes the window of step t (lane o: channel o)
+    __shared__ float cand_s[kMaxHorizon][4];
+    if (blockIdx.x == 0 && threadIdx.x < 4) err[threadIdx.x] = 0;  // the rollout's error word starts clear
+    const uint64_t grow = blockIdx.x;  // b * S + s
+    const uint32_t b = static_cast<uint32_t>(grow / a.S), sidx = static_cast<uint32_t>(grow % a.S);
+    const uint32_t o = threadIdx.x & 3u, base = threadIdx.x & 28u;
+    const bool live = (threadIdx.x >> 2) < a.T;
+    const uint32_t t = live ? (threadIdx.x >> 2) : a.T - 1;  // dead lanes still take part in the shuffles
+    if (live) {
+        const float v = sample_white(a.mean, a.std, a.low_dev, a.high_dev, a.noise, a.seed, a.offset, a.sample_base,
+                                     a.sample_total, b, sidx, t, o, a.S, a.T, 4);
+        a.cand_out[grow * a.T * 4 + t * 4 + o] = v;
+        cand_s[t][o] = v;
+    }
+    __syncthreads();
     TcnChannelW w;
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
@@ -312,14 +319,17 @@ __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, 
         w.b[2 * l] = blk[48 + o];
         w.b[2 * l + 1] = blk[100 + o];
     }
-    const float* cand_row = a.cand_out + grow * a.T * 4;
     float x0[kTcnC][kTcnHs];
 #pragma unroll
     for (int q = 0; q < kTcnHs; ++q) {
         const uint32_t pos = t + q;
-        const float* src = pos < kTcnHs - 1 ? a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4
-                                            : cand_row + (pos - (kTcnHs - 1)) * 4;
-        const float4 v = *reinterpret_cast<const float4*>(src);
+        float4 v;
+        if (pos < kTcnHs - 1) {
+            v = *reinterpret_cast<const float4*>(a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4);
+        } else {
+            const uint32_t k = pos - (kTcnHs - 1);
+            v = make_float4(cand_s[k][0], cand_s[k][1], cand_s[k][2], cand_s[k][3]);
+        }
         x0[0][q] = (v.x - a.action_mean[0]) / a.action_std[0];
         x0[1][q] = (v.y - a.action_mean[1]) / a.action_std[1];
         x0[2][q] = (v.z - a.action_mean[2]) / a.action_std[2];
@@ -943,26 +953,12 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     if (!a.action_tcn_host) return cudaErrorInvalidValue;
     // 0. initial latent per vehicle (on the side stream when given)
     if ((e = fork_h0(a, h0, stream, side)) != cudaSuccess) return e;
-    // 1. candidates
-    SampleArgs sa{};
-    sa.B = a.B; sa.S = a.S; sa.T = a.T; sa.A = 4;
-    sa.mean = a.mean;
-    sa.std = a.std;
-    sa.low = a.low_dev;
-    sa.high = a.high_dev;
-    sa.noise = a.noise;
-    sa.seed = a.seed;
-    sa.offset = a.offset;
-    sa.sample_base = a.sample_base;
-    sa.sample_total = a.sample_total;
-    sa.out = a.cand_out;
-    if ((e = launch_sample(sa, stream)) != cudaSuccess) return e;
-    // 2. the action encoder of every (candidate, step) as split-fp16 x tiles
+    // 1. the candidates (white noise) and the action encoder of every
+    // (candidate, step) as split-fp16 x tiles, one block per candidate
     MmaTcnConst tw;
     for (uint32_t q = 0; q < 3 * 104; ++q) tw.v[q] = a.action_tcn_host[q];
-    const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
-    skyjepa_mma_inputs_kernel<<<static_cast<uint32_t>((4 * n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles,
-                                                                                                    err);
+    const uint32_t threads = (4 * a.T + 31) / 32 * 32;
+    skyjepa_mma_inputs_kernel<<<a.B * a.S, threads, 0, stream>>>(a, tw, xtiles, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     // 3. the rollout: one 16-CTA cluster per 128 rows
@@ -991,7 +987,7 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     if (a.time_begin) cudaEventRecord(a.time_begin, stream);
     e = cudaLaunchKernelEx(&cfg, skyjepa_mma_kernel, p);
     if (a.time_end) cudaEventRecord(a.time_end, stream);
-    if (launches) *launches = 4;
+    if (launches) *launches = 3;
     return e;
 }
 

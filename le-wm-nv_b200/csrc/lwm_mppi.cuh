@@ -21,6 +21,28 @@
 
 namespace lwm {
 
+// One element of the white-noise candidate sampler: candidate (b, s) of a
+// plan with S samples per vehicle, step t, action act (of A; horizon T):
+// slot 0 of the unsharded plan is the mean, the others mean + eps std with
+// eps the injected noise or the Philox normal of the global index, then the
+// action bounds (sample_candidates, src/planner.rs:1152-1208, 1614-1616).
+__device__ __forceinline__ float sample_white(const float* mean, const float* std, const float* low,
+                                             const float* high, const float* noise, uint64_t seed, uint64_t offset,
+                                             uint32_t sample_base, uint32_t sample_total, uint32_t b, uint32_t s,
+                                             uint32_t t, uint32_t act, uint32_t S, uint32_t T, uint32_t A) {
+    const size_t mi = (static_cast<size_t>(b) * T + t) * A + act;
+    float v;
+    if (sample_base + s == 0) {
+        v = mean[mi];
+    } else {
+        const uint64_t e = ((static_cast<uint64_t>(b) * S + s) * T + t) * A + act;
+        const uint64_t gi = global_row(b, s, sample_base, sample_total, S) * T * A + static_cast<uint64_t>(t) * A + act;
+        const float eps = noise ? noise[e] : normal_at(seed, offset + gi);
+        v = __fadd_rn(mean[mi], __fmul_rn(eps, std[mi]));
+    }
+    return cmin(cmax(v, low[act]), high[act]);
+}
+
 template <int NT>
 __device__ __forceinline__ uint64_t block_min_u64(uint64_t v, uint64_t* scratch) {
 #pragma unroll
