@@ -25,6 +25,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <type_traits>
 
 #include "lwm_device.cuh"
 #include "lwm_kernels.hpp"
@@ -138,16 +139,26 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     const TcnView& tcn = a.state_tcn;
     const TcnBlockView &L1 = tcn.blocks[0], &L2 = tcn.blocks[1], &L3 = tcn.blocks[2];
     const uint32_t o0 = c * kPer;
-    // the CTA's weight rows, once
+    // the CTA's weight rows, once, one copy group per stage: each stage waits
+    // only for its own rows, the later ones land under the earlier stages
+    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
     copy16(sm + kOffW1a, L1.w1 + o0 * kIn * 3, kW1a);
+    commit();
     copy16(sm + kOffW2a, L1.w2 + o0 * kC * 3, kW2);
     copy16(sm + kOffWr, L1.wr + o0 * kIn, kWr);
+    commit();
     copy16(sm + kOffW1b, L2.w1 + o0 * kC * 3, kW2);
+    commit();
     copy16(sm + kOffW2b, L2.w2 + o0 * kC * 3, kW2);
+    commit();
     copy16(sm + kOffW1c, L3.w1 + o0 * kC * 3, kW2);
+    commit();
     copy16(sm + kOffW2c, L3.w2 + o0 * kC * 3, kW2);
+    commit();
     copy16(sm + kOffWp, a.proj_w + c * kProjPer * kC, kWp);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    commit();
+    // groups still allowed in flight when a stage starts (its own and the earlier ones landed)
+    auto landed = [](auto n) { asm volatile("cp.async.wait_group %0;" ::"n"(decltype(n)::value) : "memory"); };
     // the normalised history (every CTA its own copy)
     float* X = sm + kOffX;
     for (uint32_t q = tid; q < kHs * kIn; q += kThreads) {
@@ -155,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
         const float v = a.state_hist[(static_cast<size_t>(b) * kHs + t) * kIn + i];
         X[t * kXLd + i] = (v - a.state_mean[i]) / a.state_std[i];
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    landed(std::integral_constant<int, 6>{});
     __syncthreads();
 
     const uint32_t o = o0 + warp;
@@ -168,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<10, 0, 1>(sm, kOffH1, c, tid);
+    landed(std::integral_constant<int, 5>{});
     __syncthreads();
     // ---- level 1, conv2 + residual projection at the odd positions
     {
@@ -188,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<5, 1, 2>(sm, kOffY1, c, tid);
+    landed(std::integral_constant<int, 4>{});
     __syncthreads();
     // ---- level 2, conv1 at the odd positions
     {
@@ -197,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<5, 1, 2>(sm, kOffH2, c, tid);
+    landed(std::integral_constant<int, 3>{});
     __syncthreads();
     // ---- level 2, conv2 + identity residual at 1, 5, 9
     {
@@ -210,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<3, 1, 4>(sm, kOffY2, c, tid);
+    landed(std::integral_constant<int, 2>{});
     __syncthreads();
     // ---- level 3, conv1 at 1, 5, 9
     {
@@ -219,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<3, 1, 4>(sm, kOffH3, c, tid);
+    landed(std::integral_constant<int, 1>{});
     __syncthreads();
     // ---- level 3, conv2 + identity residual at 9
     {
@@ -231,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaA
     }
     cluster_barrier();
     pull<1, 9, 1>(sm, kOffY3, c, tid);
+    landed(std::integral_constant<int, 0>{});
     __syncthreads();
     // ---- the projection of position 9: outputs 16c + 2w, 16c + 2w + 1
     const float* y = sm + kOffY3 + 9 * kC;
