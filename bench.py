@@ -57,6 +57,24 @@ ROLLOUT_DRAM_BYTES = {"skyjepa": 1847040}
 NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)
 
 
+def nccl_log_setup():
+    """Route NCCL's communicator log (INIT lines: ranks, devices, NVLS) to a
+    per-process file, so stdout keeps the one JSON line; returns the path.
+    Called before torch (and NCCL) are loaded, so NCCL reads the settings."""
+    import tempfile
+    if "NCCL_DEBUG" in os.environ:
+        return None
+    path = os.path.join(tempfile.gettempdir(), f"lewm_nccl_{os.getpid()}.log")
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ["NCCL_DEBUG_FILE"] = path
+    return path
+
+
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    NCCL_LOG = nccl_log_setup()
+
+
 def default_workload_config(kind: str, world: int) -> dict:
     """The `config` both arms print for the default and nominal workloads
     (the same seeded inputs, planner and model widths in both)."""
@@ -167,8 +185,6 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     if world > 1:
-        global NCCL_LOG
-        NCCL_LOG = nccl_log_setup()
         dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     ctx = L.Context(local_rank)
@@ -325,19 +341,6 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.destroy_process_group()
     return result
-
-
-def nccl_log_setup():
-    """Route NCCL's communicator log (INIT lines: ranks, devices, NVLS) to a
-    per-process file, so stdout keeps the one JSON line; returns the path."""
-    import tempfile
-    if "NCCL_DEBUG" in os.environ:
-        return None
-    path = os.path.join(tempfile.gettempdir(), f"lewm_nccl_{os.getpid()}.log")
-    os.environ["NCCL_DEBUG"] = "INFO"
-    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
-    os.environ["NCCL_DEBUG_FILE"] = path
-    return path
 
 
 def nccl_log_lines(path, limit=6):
