@@ -79,7 +79,8 @@ struct __align__(1024) PredSmem {
     float b1s[kN1Max];             // the first GEMM's bias of this CTA's columns
     float bns[4][kN1Max];          // and pred_proj's BatchNorm weight, bias, mean, variance
     uint64_t w_full[kStages], w_empty[kStages];
-    uint64_t a_full, x_free, d1_full, d2_full, h_ready, h_free, d1_drained, d2_drained, done;
+    uint64_t a_full, x_free, d1_full, d2_full, h_free, d1_drained, d2_drained, done;
+    uint64_t h_ready[kHBlks];      // K block kb of H is written (every compute warp arrives once)
     uint64_t a_ready[2], p_ready[2];  // remote: the 8 owners' A rows / the 8 CTAs' partials, by parity
     uint32_t tmem;
 };
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
         tc::mbar_init(&s.x_free, 1);
         tc::mbar_init(&s.d1_full, 1);
         tc::mbar_init(&s.d2_full, 1);
-        tc::mbar_init(&s.h_ready, kCompWarps);
+        for (uint32_t kb = 0; kb < kHBlks; ++kb) tc::mbar_init(&s.h_ready[kb], kCompWarps);
         tc::mbar_init(&s.h_free, 1);
         tc::mbar_init(&s.d1_drained, kCompWarps);
         tc::mbar_init(&s.d2_drained, kCompWarps);
@@ -293,10 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
                 tc::commit(&s.d1_full);
                 // second GEMM: D2 = H W2^T ([128 x n1] x [n1 x 192]), this CTA's K slice
                 if (g > 0 && !(ok = tc::mbar_wait(&s.d2_drained, (g - 1) & 1u, err, 7, g, lim))) break;
-                if (!(ok = tc::mbar_wait(&s.h_ready, ph, err, 8, g, lim))) break;
-                tc::fence_after();
                 const uint32_t id2 = tc::idesc_bf16_f32(kM, kD);
                 for (uint32_t kb = 0; ok && kb < nkb2; ++kb, ++n) {
+                    // each K block as soon as the drains have written it
+                    if (!(ok = tc::mbar_wait(&s.h_ready[kb], ph, err, 8, g, lim))) break;
+                    tc::fence_after();
                     const uint32_t slot = n % kStages;
                     if (!(ok = tc::mbar_wait(&s.w_full[slot], (n / kStages) & 1u, err, 9, n, lim))) break;
                     tc::fence_after();
@@ -446,50 +448,54 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             if (!(ok = comp_all(ok))) break;
             tc::fence_after();
             {
-                const uint32_t cols = n1 / kColSplit, c0 = part * cols;
-                for (uint32_t cc = 0; cc < cols; cc += 32) {
-                    float v[32];
-                    tc::tmem_ld16(lane_base + c0 + cc, *reinterpret_cast<float(*)[16]>(v));
-                    tc::tmem_ld16(lane_base + c0 + cc + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-                    tc::tmem_ld_wait();
-                    if (kind == kAttn) {
+                // K block by K block: warp part p takes columns [16 p, 16 p + 16)
+                // of every block, so all warps finish block 0 first and the
+                // second GEMM starts on it while the later blocks drain
+                const uint32_t nkb = n1 / kKB;
+                for (uint32_t kb = 0; kb < kHBlks; ++kb) {
+                    if (kb < nkb) {
+                        const uint32_t c0 = kb * kKB + part * 16;
+                        float v[16];
+                        tc::tmem_ld16(lane_base + c0, v);
+                        tc::tmem_ld_wait();
+                        if (kind == kAttn) {
 #pragma unroll
-                        for (uint32_t i = 0; i < 32; ++i) v[i] = v[i] + s.b1s[c0 + cc + i];
-                    } else if (kind == kMlp) {
+                            for (uint32_t i = 0; i < 16; ++i) v[i] = v[i] + s.b1s[c0 + i];
+                        } else if (kind == kMlp) {
 #pragma unroll
-                        for (uint32_t i = 0; i < 32; ++i) v[i] = gelu_fast(v[i] + s.b1s[c0 + cc + i]);
-                    } else {
-                        // BatchNorm (eval, with the reciprocal square root), then GELU
+                            for (uint32_t i = 0; i < 16; ++i) v[i] = gelu_fast(v[i] + s.b1s[c0 + i]);
+                        } else {
+                            // BatchNorm (eval, with the reciprocal square root), then GELU
 #pragma unroll
-                        for (uint32_t i = 0; i < 32; ++i) {
-                            const uint32_t lc = c0 + cc + i;
-                            float t = v[i] + s.b1s[lc];
-                            if (bn_w) t = (t - s.bns[2][lc]) * rsqrtf(s.bns[3][lc] + 1e-5f) * s.bns[0][lc] + s.bns[1][lc];
-                            v[i] = gelu_fast(t);
+                            for (uint32_t i = 0; i < 16; ++i) {
+                                const uint32_t lc = c0 + i;
+                                float t = v[i] + s.b1s[lc];
+                                if (bn_w)
+                                    t = (t - s.bns[2][lc]) * rsqrtf(s.bns[3][lc] + 1e-5f) * s.bns[0][lc] + s.bns[1][lc];
+                                v[i] = gelu_fast(t);
+                            }
                         }
-                    }
-                    // 32 columns = 64 bytes of the row, four 16-byte pieces
-                    const uint32_t col = c0 + cc, kb = col / kKB, kc = col % kKB;
-                    uint8_t* blk = s.H[kb];
+                        // 16 columns = 32 bytes of the row, two 16-byte pieces
+                        uint8_t* blk = s.H[kb];
 #pragma unroll
-                    for (uint32_t q8 = 0; q8 < 4; ++q8) {
-                        uint32_t pk[4];
+                        for (uint32_t q8 = 0; q8 < 2; ++q8) {
+                            uint32_t pk[4];
 #pragma unroll
-                        for (uint32_t k = 0; k < 4; ++k)
-                            pk[k] = static_cast<uint32_t>(bf16_bits(v[8 * q8 + 2 * k])) |
-                                    (static_cast<uint32_t>(bf16_bits(v[8 * q8 + 2 * k + 1])) << 16);
-                        *reinterpret_cast<uint4*>(blk + tc::sw128_offset(row, kc + 8 * q8)) =
-                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            for (uint32_t k = 0; k < 4; ++k)
+                                pk[k] = static_cast<uint32_t>(bf16_bits(v[8 * q8 + 2 * k])) |
+                                        (static_cast<uint32_t>(bf16_bits(v[8 * q8 + 2 * k + 1])) << 16);
+                            *reinterpret_cast<uint4*>(blk + tc::sw128_offset(row, part * 16 + 8 * q8)) =
+                                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        }
+                        tc::fence_async_smem();
                     }
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.h_ready[kb]);  // (blocks past n1: no data, phase kept in step)
                 }
             }
-            tc::fence_async_smem();
             tc::fence_before();
             __syncwarp();
-            if (lane == 0) {
-                tc::mbar_arrive(&s.h_ready);
-                tc::mbar_arrive(&s.d1_drained);
-            }
+            if (lane == 0) tc::mbar_arrive(&s.d1_drained);
             // ---- second GEMM's partial -> the exchange, rows grouped by owner
             if (!(ok = comp_all(tc::mbar_wait(&s.d2_full, ph, err, 12, g, lim)))) break;
             tc::fence_after();
