@@ -96,6 +96,50 @@ __global__ void __launch_bounds__(256) sample_elem_kernel(SampleArgs a) {
     a.out[e] = v;
 }
 
+// The same for 4 consecutive actions per thread (A a multiple of 4, the
+// stream offset too): the 4 draws of one step come from one Philox block,
+// so each block is evaluated once, and the row is stored as one float4.
+__global__ void __launch_bounds__(256) sample_quad_kernel(SampleArgs a) {
+    const uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t TA = a.T * a.A;
+    if (q >= static_cast<uint64_t>(a.B) * a.S * TA / 4) return;
+    const uint64_t e = q * 4;
+    const uint32_t act = static_cast<uint32_t>(e % a.A);
+    const uint32_t t = static_cast<uint32_t>((e / a.A) % a.T);
+    const uint64_t row = e / TA;  // b * S + s
+    const uint32_t s = static_cast<uint32_t>(row % a.S);
+    const uint32_t b = static_cast<uint32_t>(row / a.S);
+    const uint32_t g = a.sample_base + s;
+    float v[4];
+    if (a.carried && g >= 1 && g <= a.inject) {
+        const float* src = a.carried + ((static_cast<size_t>(b) * a.carried_count + (g - 1)) * a.T + t) * a.A + act;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = src[i];
+    } else {
+        const size_t mi = (static_cast<size_t>(b) * a.T + t) * a.A + act;
+        if (g == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = a.mean[mi + i];
+        } else {
+            float eps[4];
+            if (a.noise) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) eps[i] = a.noise[e + i];
+            } else {
+                const uint64_t gi = global_row(b, s, a.sample_base, a.sample_total, a.S) * TA +
+                                    static_cast<uint64_t>(t) * a.A + act;
+                const float4 n = normal_quad(a.seed, (a.offset + gi) >> 2);
+                eps[0] = n.x; eps[1] = n.y; eps[2] = n.z; eps[3] = n.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __fadd_rn(a.mean[mi + i], __fmul_rn(eps[i], a.std[mi + i]));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = cmin(cmax(v[i], a.low[act + i]), a.high[act + i]);
+    }
+    *reinterpret_cast<float4*>(a.out + e) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
 // --------------------------------------------------- MPPI reduce (generic)
 __global__ void __launch_bounds__(256) mppi_reduce_kernel(MppiArgs m, const float* cand,
                                                           const float* scores, uint32_t S) {
@@ -426,6 +470,8 @@ cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream) {
     const uint64_t lanes = static_cast<uint64_t>(a.B) * a.S * a.A;
     if (a.smooth > 0.0f && a.T > 1)
         sample_kernel<<<ceil_div(lanes, 256), 256, 0, stream>>>(a);
+    else if (a.A % 4 == 0 && a.offset % 4 == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0)
+        sample_quad_kernel<<<ceil_div(lanes * a.T / 4, 256), 256, 0, stream>>>(a);
     else
         sample_elem_kernel<<<ceil_div(lanes * a.T, 256), 256, 0, stream>>>(a);
     return cudaGetLastError();

@@ -13,13 +13,15 @@
 //     D[128 x 128] = X_t[128 x 16] . Wx_c^T          (r | z | n_h | n_x cols)
 //     D[:, 0:96]  += H_t[128 x 256] . Whh_c^T         (16 MMAs, K = 256)
 //   then the GRU gates of those 32 units for the 128 rows (f32), with h_t in
-//   TMEM (f32) and in shared memory (bf16, the next step's A operand).
+//   TMEM twice: f32 (the recurrent state) and bf16 (the A operand of the
+//   h-block MMAs, read by the tensor core straight from TMEM, so that shared
+//   memory bandwidth goes to the weights alone).
 //   The prober's first layer is one more MMA per step (A = h_{t+1}).
 //
-// Before it, sample_kernel draws the candidates and skyjepa_tc_inputs_kernel
-// computes every candidate's action-TCN input x_t for every step (all
-// threads of the GPU), written as bf16 K-major tiles with a constant 1 at
-// k = E that carries the GRU biases through the x-block MMA.
+// Before it, the sampler draws the candidates and skyjepa_tc_inputs_seq_kernel
+// computes every candidate's action-TCN input x_t for every step (one thread
+// per candidate), written as bf16 K-major tiles with a constant 1 at k = E
+// that carries the GRU biases through the x-block MMA.
 //
 // Roles (448 threads): warp 0 streams the weight chunks and the x tiles
 // (bulk copies); warp 1 issues the MMAs and owns TMEM; warps 2-9 run the GRU
@@ -29,11 +31,13 @@
 // with bounded waits; a wait that gives up records where and the kernel
 // unwinds.
 //
-// TMEM (512 columns): two accumulator slots of 128 columns = [0,256); h_t
-// (f32) = [256,512).  (A tcgen05.mma of M = 128, K = 16 costs the issuing
-// thread about the same below N ~ 128, so chunks are as wide as TMEM allows.)  Weights are bf16 (packed once
-// per scorer by pack_tc_weights_kernel; the GRU biases ride in the x block);
-// the prober's later layers, the TCN and the integrator stay f32.
+// TMEM (512 columns): one accumulator slot of 128 columns = [0,128); h_t as
+// bf16 pairs = [128,256); h_t (f32) = [256,512).  The slot's consumers (GRU
+// epilogue, prober) load it into registers and hand it back before their
+// math, so the next chunk's MMAs overlap the gates of this one.  Weight
+// chunks stream through a 3-deep shared-memory ring.  Weights are bf16
+// (packed once per scorer by pack_tc_weights_kernel; the GRU biases ride in
+// the x block); the prober's later layers, the TCN and the integrator stay f32.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -56,12 +60,13 @@ constexpr uint32_t kXRows = 4 * kUnits;           // B rows of the x part: r, z,
 constexpr uint32_t kChunkHBytes = 4 * kHRows * 128;  // 4 K-blocks x 96 rows x 128 B (SW128)
 constexpr uint32_t kChunkXBytes = kXRows * 32;       // 128 rows x 16 k (SW32)
 constexpr uint32_t kChunkBytes = kChunkHBytes + kChunkXBytes;  // 52 KB, 1024-aligned
-constexpr uint32_t kWStages = 2;                  // weight-chunk ring
-constexpr uint32_t kSlots = 2, kSlotCols = kXRows; // accumulator ring: 2 x 128 TMEM columns
+constexpr uint32_t kWStages = 3;                  // weight-chunk ring
+constexpr uint32_t kSlots = 1, kSlotCols = kXRows; // accumulator: one slot of 128 TMEM columns
 constexpr uint32_t kUPW = kUnits / 2;             // units per epilogue warp and chunk
-constexpr uint32_t kHCol = kSlots * kSlotCols;    // h (f32) lives in TMEM columns [256, 512)
+constexpr uint32_t kACol = kSlots * kSlotCols;    // h_t as bf16 (the MMAs' A operand): TMEM columns [128, 256)
+constexpr uint32_t kHCol = kACol + kH / 2;        // h (f32) lives in TMEM columns [256, 512)
+static_assert(kHCol + kH == 512, "TMEM holds the slot, A and h");
 constexpr uint32_t kEntries = kChunks + 1;        // accumulator-ring entries per step (chunks + prober)
-constexpr uint32_t kABytes = 4 * 128 * 128;
 constexpr uint32_t kXBytes = 128 * 32;
 constexpr uint32_t kMaxHid = 32, kMaxLayers = 3;
 constexpr uint32_t kP1Bytes = 4 * kMaxHid * 128;
@@ -74,11 +79,11 @@ constexpr uint32_t kAuxBarrier = 3, kAuxThreads = 128;
 constexpr uint32_t kMaxHistTc = 16;
 
 struct __align__(1024) TcSmem {
-    uint8_t A[kABytes];
     uint8_t W[kWStages][kChunkBytes];
     uint8_t X[2][kXBytes];
     uint8_t P1[kP1Bytes];
     float pw[kPwFloats];  // prober: b1, hidden layers (W, b), output (W, b)
+    float hst[kRows * (kMaxHid + 1)];  // prober hidden-layer outputs, one padded row per candidate
     float red_w[kRows];
     uint64_t red_key[4];
     float red_f[4];
@@ -114,20 +119,12 @@ __device__ __forceinline__ bool aux_all(bool v) {
 // sigmoid(v) = 0.5 + 0.5 tanh(v / 2).
 __device__ __forceinline__ float sigmoid_f(float v) { return fmaf(0.5f, tanh_fast(0.5f * v), 0.5f); }
 
-struct FastGelu {
-    __device__ __forceinline__ float operator()(float v) const { return gelu_fast(v); }
-};
-
 // Two f32 -> packed bf16x2 (the first value at the lower address).
 __device__ __forceinline__ uint32_t bf2(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 8 f32 values as bf16 into one 16-byte chunk of a K-major tile row.
-__device__ __forceinline__ void store_bf16x8(uint8_t* dst, const float (&v)[8]) {
-    *reinterpret_cast<uint4*>(dst) = make_uint4(bf2(v[0], v[1]), bf2(v[2], v[3]), bf2(v[4], v[5]), bf2(v[6], v[7]));
-}
 
 // The element (row, k) of the prober / recurrent weights in the packed layouts.
 __host__ __device__ inline uint32_t packed_h_offset(uint32_t j, uint32_t k, uint32_t rows) {
@@ -505,41 +502,121 @@ struct TcnConst {
     float v[kTcnParamFloats];  // per level: conv1 weight [4][4][3], bias [4], conv2 weight, bias
 };
 
-__global__ void __launch_bounds__(256) skyjepa_tc_inputs_kernel(SkyjepaArgs a, const __grid_constant__ TcnConst tw,
-                                                                uint8_t* xtiles) {
-    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const uint64_t total = static_cast<uint64_t>(a.B) * a.S * a.T;
-    if (i >= total) return;
-    const uint32_t t = static_cast<uint32_t>(i % a.T);
-    const uint64_t grow = i / a.T;  // b * S + s
-    const uint32_t b = static_cast<uint32_t>(grow / a.S);
+// The same inputs, one thread per candidate walking its steps in order.
+// The window of step t is the sequence positions t .. t + 9; a block-1
+// value at window position p >= 2 (conv1) or p >= 4 (block output) reads no
+// zero padding, so it is a function of its sequence position alone and is
+// computed once, when it first enters a window (at p = 9), then slides down
+// with the window.  Only the padded edge values (conv1 at p = 0, 1; block 1
+// at p = 1, 3) and blocks 2 and 3 are evaluated per window.  Every
+// convolution sums its taps in conv_at's order (with the fast GELU), so x_t
+// is tcn_last's value for the window.
+template <bool kTap0, bool kTap1>
+__device__ __forceinline__ void conv3(const float* W, const float* B, const float (&x0)[kTcnC], const float (&x1)[kTcnC],
+                                      const float (&x2)[kTcnC], float (&out)[kTcnC]) {
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kTcnC; ++i) {
+            if (kTap0) acc = fmaf(W[(o * kTcnC + i) * kTcnK + 0], x0[i], acc);
+            if (kTap1) acc = fmaf(W[(o * kTcnC + i) * kTcnK + 1], x1[i], acc);
+            acc = fmaf(W[(o * kTcnC + i) * kTcnK + 2], x2[i], acc);
+        }
+        out[o] = gelu_fast(acc + B[o]);
+    }
+}
+
+// gelu(conv2(taps) + residual): a block's output at one position
+template <bool kTap0, bool kTap1>
+__device__ __forceinline__ void block3(const TcnBlockW& w, const float (&h0)[kTcnC], const float (&h1)[kTcnC],
+                                       const float (&h2)[kTcnC], const float (&res)[kTcnC], float (&out)[kTcnC]) {
+    float c[kTcnC];
+    conv3<kTap0, kTap1>(w.w2, w.b2, h0, h1, h2, c);
+#pragma unroll
+    for (int o = 0; o < kTcnC; ++o) out[o] = gelu_fast(c[o] + res[o]);
+}
+
+__global__ void __launch_bounds__(128) skyjepa_tc_inputs_seq_kernel(SkyjepaArgs a, const __grid_constant__ TcnConst tw,
+                                                                    uint8_t* xtiles) {
+    const uint64_t grow = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // b * S + s
+    if (grow >= static_cast<uint64_t>(a.B) * a.S) return;
+    const uint32_t b = static_cast<uint32_t>(grow / a.S), T = a.T;
     TcnBlockW w[3];
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
         const float* blk = tw.v + l * kTcnBlockFloats;
         w[l] = {blk, blk + 48, blk + 52, blk + 100};
     }
-    const float* cand_row = a.cand_out + grow * a.T * 4;
-    float x0[kTcnC][kTcnHs];
+    const float* cand = a.cand_out + grow * T * 4;
+    const float* hist = a.action_hist + static_cast<size_t>(b) * (kTcnHs - 1) * 4;
+    float mean[4], inv[4];
 #pragma unroll
-    for (int q = 0; q < kTcnHs; ++q) {
-        const uint32_t pos = t + q;
-        const float* src = pos < kTcnHs - 1 ? a.action_hist + (static_cast<size_t>(b) * (kTcnHs - 1) + pos) * 4
-                                            : cand_row + (pos - (kTcnHs - 1)) * 4;
-        const float4 v = *reinterpret_cast<const float4*>(src);
-        x0[0][q] = (v.x - a.action_mean[0]) / a.action_std[0];
-        x0[1][q] = (v.y - a.action_mean[1]) / a.action_std[1];
-        x0[2][q] = (v.z - a.action_mean[2]) / a.action_std[2];
-        x0[3][q] = (v.w - a.action_mean[3]) / a.action_std[3];
-    }
-    float x[kTcnC];
-    tcn_last<FastGelu>(w, x0, x);
+    for (int c = 0; c < 4; ++c) { mean[c] = a.action_mean[c]; inv[c] = a.action_std[c]; }
+    auto load = [&](uint32_t pos, float (&v)[kTcnC]) {
+        const float4 f = *reinterpret_cast<const float4*>(pos < kTcnHs - 1 ? hist + pos * 4 : cand + (pos - (kTcnHs - 1)) * 4);
+        v[0] = (f.x - mean[0]) / inv[0];
+        v[1] = (f.y - mean[1]) / inv[1];
+        v[2] = (f.z - mean[2]) / inv[2];
+        v[3] = (f.w - mean[3]) / inv[3];
+    };
+    // window of step 0; block-1 values that read no padding: conv1 at 2..8, output at 4..8
+    float x[kTcnHs][kTcnC], c1[kTcnHs][kTcnC], y1[kTcnHs][kTcnC];
+#pragma unroll
+    for (int q = 0; q < kTcnHs; ++q) load(q, x[q]);
+#pragma unroll
+    for (int q = 2; q < kTcnHs - 1; ++q) conv3<true, true>(w[0].w1, w[0].b1, x[q - 2], x[q - 1], x[q], c1[q]);
+#pragma unroll
+    for (int q = 4; q < kTcnHs - 1; ++q) block3<true, true>(w[0], c1[q - 2], c1[q - 1], c1[q], x[q], y1[q]);
     const uint64_t tile = grow / kRows;
     const uint32_t row = static_cast<uint32_t>(grow % kRows);
-    uint8_t* xt = xtiles + (tile * a.T + t) * kXBytes;
-    *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 0)) =
-        make_uint4(bf2(x[0], x[1]), bf2(x[2], x[3]), bf2(1.0f, 0.0f), 0u);
-    *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
+    for (uint32_t t = 0; t < T; ++t) {
+        if (t > 0) {
+#pragma unroll
+            for (int q = 0; q + 1 < kTcnHs; ++q)
+#pragma unroll
+                for (int c = 0; c < kTcnC; ++c) x[q][c] = x[q + 1][c];
+#pragma unroll
+            for (int q = 2; q + 1 < kTcnHs; ++q)
+#pragma unroll
+                for (int c = 0; c < kTcnC; ++c) c1[q][c] = c1[q + 1][c];
+#pragma unroll
+            for (int q = 4; q + 1 < kTcnHs; ++q)
+#pragma unroll
+                for (int c = 0; c < kTcnC; ++c) y1[q][c] = y1[q + 1][c];
+            load(t + kTcnHs - 1, x[kTcnHs - 1]);
+        }
+        // the window's new position 9
+        conv3<true, true>(w[0].w1, w[0].b1, x[7], x[8], x[9], c1[9]);
+        block3<true, true>(w[0], c1[7], c1[8], c1[9], x[9], y1[9]);
+        // block 1 at the padded edge: conv1 at 0, 1; output at 1, 3
+        float e0[kTcnC], e1[kTcnC], y1_1[kTcnC], y1_3[kTcnC];
+        conv3<false, false>(w[0].w1, w[0].b1, x[0], x[0], x[0], e0);
+        conv3<false, true>(w[0].w1, w[0].b1, x[0], x[0], x[1], e1);
+        block3<false, true>(w[0], e0, e0, e1, x[1], y1_1);
+        block3<true, true>(w[0], e1, c1[2], c1[3], x[3], y1_3);
+        // block 2 (dilation 2): conv1 at odd positions, output at 1, 5, 9
+        float h1[kTcnC], h3[kTcnC], h5[kTcnC], h7[kTcnC], h9[kTcnC];
+        conv3<false, false>(w[1].w1, w[1].b1, y1_1, y1_1, y1_1, h1);
+        conv3<false, true>(w[1].w1, w[1].b1, y1_1, y1_1, y1_3, h3);
+        conv3<true, true>(w[1].w1, w[1].b1, y1_1, y1_3, y1[5], h5);
+        conv3<true, true>(w[1].w1, w[1].b1, y1_3, y1[5], y1[7], h7);
+        conv3<true, true>(w[1].w1, w[1].b1, y1[5], y1[7], y1[9], h9);
+        float y2_1[kTcnC], y2_5[kTcnC], y2_9[kTcnC];
+        block3<false, false>(w[1], h1, h1, h1, y1_1, y2_1);
+        block3<true, true>(w[1], h1, h3, h5, y1[5], y2_5);
+        block3<true, true>(w[1], h5, h7, h9, y1[9], y2_9);
+        // block 3 (dilation 4): conv1 at 1, 5, 9, output at 9
+        float g1[kTcnC], g5[kTcnC], g9[kTcnC], xo[kTcnC];
+        conv3<false, false>(w[2].w1, w[2].b1, y2_1, y2_1, y2_1, g1);
+        conv3<false, true>(w[2].w1, w[2].b1, y2_1, y2_1, y2_5, g5);
+        conv3<true, true>(w[2].w1, w[2].b1, y2_1, y2_5, y2_9, g9);
+        block3<true, true>(w[2], g1, g5, g9, y2_9, xo);
+        uint8_t* xt = xtiles + (tile * T + t) * kXBytes;
+        *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 0)) =
+            make_uint4(bf2(xo[0], xo[1]), bf2(xo[2], xo[3]), bf2(1.0f, 0.0f), 0u);
+        *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
+    }
 }
 
 // ------------------------------------------------------------ main kernel
@@ -648,91 +725,99 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 }
         }
     } else if (warp == 1) {
-        // ================= MMA issuer
-        if (lane == 0) {
+        // ================= MMA issuer (the whole warp, converged; one elected lane issues)
+        {
             const uint32_t id_gru_x = tc::idesc_bf16_f32(128, kXRows), id_gru_h = tc::idesc_bf16_f32(128, kHRows);
             const uint32_t id_prob = tc::idesc_bf16_f32(128, hid);
-            const uint32_t a_base = tc::smem_u32(s.A), p_base = tc::smem_u32(s.P1);
-            uint32_t j = 0, K = 0, xs = 0, hq = 0;
-            uint32_t uses[2][kSlots] = {};
-            int last[kSlots];
-            for (uint32_t i = 0; i < kSlots; ++i) last[i] = -1;
+            const uint32_t a_tmem = tmem + kACol;
+            // every lane waits; the outcome is the warp's (a diverged lane would leave elect.sync short)
+            auto wwait = [&](uint64_t* bar, uint32_t parity, volatile int* e, int site, uint32_t detail,
+                             uint32_t limit) -> bool {
+                return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, e, site, static_cast<int>(detail), limit));
+            };
+            // descriptors built once; a K step or a ring slot only adds to the start-address
+            // field (address >> 4, every address of the ring stays below 2^18)
+            const uint64_t p_desc = tc::smem_desc(tc::smem_u32(s.P1), 16, 1024, tc::kSwizzle128);
+            const uint64_t wh_desc = tc::smem_desc(tc::smem_u32(s.W[0]), 16, 1024, tc::kSwizzle128);
+            const uint64_t wx_desc = tc::smem_desc(tc::smem_u32(s.W[0]) + kChunkHBytes, 16, 256, tc::kSwizzle32);
+            const uint64_t x_desc = tc::smem_desc(tc::smem_u32(s.X[0]), 16, 256, tc::kSwizzle32);
+            uint32_t j = 0, K = 0, xs = 0, hq = 0, wslot = 0, wphase = 0;
+            // per (group g, slot) the parity of its publications, bit 2 g + slot; per slot
+            // whether it was published (bit slot of `used`) and to which group (bit slot of
+            // `last_g`).  Bit masks rather than small arrays: a runtime index into an array
+            // would place it in local memory.
+            uint32_t uses = 0, used = 0, last_g = 0;
             // entry K goes to slot K % kSlots: wait until the slot's previous consumer group released it
             auto acc_slot = [&](uint32_t k, uint32_t& col) -> bool {
                 const uint32_t slot = k % kSlots;
                 col = slot * kSlotCols;
-                if (last[slot] < 0) return true;
-                const int g = last[slot];
-                return tc::mbar_wait(&s.empty[g][slot], (uses[g][slot] - 1u) & 1u, err, 5, k, lim);
+                if (!((used >> slot) & 1u)) return true;
+                const uint32_t g = (last_g >> slot) & 1u;
+                return wwait(&s.empty[g][slot], ((uses >> (2u * g + slot)) & 1u) ^ 1u, err, 5, k, lim);
             };
-            auto publish = [&](uint32_t k, int g) {
+            auto publish = [&](uint32_t k, uint32_t g) {
                 const uint32_t slot = k % kSlots;
-                tc::commit(&s.full[g][slot]);
-                ++uses[g][slot];
-                last[slot] = g;
+                tc::commit_w(&s.full[g][slot]);
+                uses ^= 1u << (2u * g + slot);
+                used |= 1u << slot;
+                last_g = (last_g & ~(1u << slot)) | (g << slot);
             };
             auto prober = [&](bool real) -> bool {
                 uint32_t col;
                 if (!acc_slot(K, col)) return false;
                 tc::fence_after();
-                if (real)
-                    for (uint32_t ks = 0; ks < 16; ++ks) {
-                        const uint32_t kb = ks >> 2, jj = ks & 3u;
-                        tc::mma_bf16(tmem + col, tc::smem_desc(a_base + kb * 128 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
-                                     tc::smem_desc(p_base + kb * hid * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
-                                     id_prob, ks > 0);
-                    }
-                publish(K, 1);
+                if (real) {
+#pragma unroll
+                    for (uint32_t ks = 0; ks < 16; ++ks)
+                        tc::mma_bf16_ta_w(tmem + col, a_tmem + ks * 8,
+                                        p_desc + (((ks >> 2) * kMaxHid * 128 + (ks & 3u) * 32) >> 4), id_prob, ks > 0);
+                }
+                publish(K, 1u);
                 ++K;
                 return true;
             };
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
                 for (uint32_t t = 0; ok && t < T; ++t) {
-                    ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_t
+                    ok = wwait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_t
                     ++hq;
                     const uint32_t xslot = xs & 1u;
-                    if (ok) ok = tc::mbar_wait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs, lim);
+                    if (ok) ok = wwait(&s.x_full[xslot], (xs >> 1) & 1u, err, 3, xs, lim);
                     for (uint32_t c = 0; ok && c < kChunks; ++c, ++j) {
                         if (c == 1 && !(ok = prober(t > 0))) break;  // prober of step t-1 (A = h_t)
-                        const uint32_t wslot = j % kWStages;
-                        if (!(ok = tc::mbar_wait(&s.w_full[wslot], (j / kWStages) & 1u, err, 4, j, lim))) break;
+                        if (!(ok = wwait(&s.w_full[wslot], wphase, err, 4, j, lim))) break;
                         uint32_t col;
                         if (!(ok = acc_slot(K, col))) break;
                         tc::fence_after();
-                        const uint32_t w_base = tc::smem_u32(s.W[wslot]);
-                        tc::mma_bf16(tmem + col, tc::smem_desc(tc::smem_u32(s.X[xslot]), 16, 256, tc::kSwizzle32),
-                                     tc::smem_desc(w_base + kChunkHBytes, 16, 256, tc::kSwizzle32), id_gru_x, 0);
-                        for (uint32_t ks = 0; ks < 16; ++ks) {
-                            const uint32_t kb = ks >> 2, jj = ks & 3u;
-                            tc::mma_bf16(tmem + col,
-                                         tc::smem_desc(a_base + kb * 128 * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
-                                         tc::smem_desc(w_base + kb * kHRows * 128 + jj * 32, 16, 1024, tc::kSwizzle128),
-                                         id_gru_h, 1);
-                        }
-                        publish(K, 0);
-                        tc::commit(&s.w_empty[wslot]);
-                        if (c == kChunks - 1) tc::commit(&s.x_empty[xslot]);
+                        const uint64_t wo = static_cast<uint64_t>(wslot * (kChunkBytes >> 4));
+                        tc::mma_bf16_w(tmem + col, x_desc + xslot * (kXBytes >> 4), wx_desc + wo, id_gru_x, 0);
+#pragma unroll
+                        for (uint32_t ks = 0; ks < 16; ++ks)
+                            tc::mma_bf16_ta_w(tmem + col, a_tmem + ks * 8,
+                                            wh_desc + wo + (((ks >> 2) * kHRows * 128 + (ks & 3u) * 32) >> 4), id_gru_h, 1);
+                        publish(K, 0u);
+                        tc::commit_w(&s.w_empty[wslot]);
+                        if (c == kChunks - 1) tc::commit_w(&s.x_empty[xslot]);
                         ++K;
+                        if (++wslot == kWStages) { wslot = 0; wphase ^= 1u; }
                     }
                     ++xs;
                 }
-                if (ok) ok = tc::mbar_wait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_T
+                if (ok) ok = wwait(&s.h_full, hq & 1u, err, 2, hq, lim);  // A holds h_T
                 ++hq;
                 if (ok) ok = prober(true);                           // prober of step T-1
-                if (ok) tc::commit(&s.a_read);                       // A is no longer read in this tile
+                if (ok) tc::commit_w(&s.a_read);                       // A is no longer read in this tile
             }
             // every MMA issued has completed before TMEM is released
-            tc::commit(&s.done);
+            tc::commit_w(&s.done);
             tc::mbar_wait_landing(&s.done, 0, lim);
         }
     } else if (warp < kAuxWarp0) {
         // ================= GRU epilogue: quadrant q, units [kUPW half, kUPW (half + 1)) of each chunk
         const uint32_t q = warp & 3u, half = (warp - kEpiWarp0) >> 2;
-        const uint32_t row = q * 32 + lane;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         uint32_t K0 = 0;  // acc-ring entry index of the tile's first entry
-        uint32_t eu[kSlots] = {}, tiles_done = 0;
+        uint32_t eu = 0, tiles_done = 0;  // bit slot: phase parity of full[0][slot]
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
             const uint32_t b = tile / p.tiles_per_vehicle;
@@ -750,11 +835,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) hv[i] = __ldg(p.h0 + static_cast<size_t>(b) * kH + u0 + i);
                     tc::tmem_st8(lane_base + kHCol + u0, hv);
-                    uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
-                    store_bf16x8(blk + tc::sw128_offset(row, u0 & 63u), hv);
+                    const uint32_t hb[4] = {bf2(hv[0], hv[1]), bf2(hv[2], hv[3]), bf2(hv[4], hv[5]), bf2(hv[6], hv[7])};
+                    tc::tmem_st4u(lane_base + kACol + u0 / 2, hb);
                 }
             tc::tmem_st_wait();
-            tc::fence_async_smem();
             tc::fence_before();
             __syncwarp();
             const bool skip = p.skip_h_arrive && blockIdx.x == 0 && warp == kEpiWarp0 && tiles_done == 0;
@@ -763,8 +847,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 for (uint32_t c = 0; c < kChunks; ++c) {
                     const uint32_t k = K0 + kEntries * t + (c == 0 ? 0u : c + 1u);
                     const uint32_t slot = k % kSlots;
-                    if (!(ok = tc::mbar_wait(&s.full[0][slot], eu[slot] & 1u, err, 6, k, lim))) break;
-                    ++eu[slot];
+                    if (!(ok = tc::mbar_wait(&s.full[0][slot], (eu >> slot) & 1u, err, 6, k, lim))) break;
+                    eu ^= 1u << slot;
                     tc::fence_after();
                     static_assert(kUPW == 16, "the gate loop loads 16 units per warp");
                     {
@@ -777,6 +861,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     tc::tmem_ld16(acol + 3 * kUnits, nx);
                     tc::tmem_ld16(lane_base + kHCol + u0, hv);
                     tc::tmem_ld_wait();
+                    // the accumulator is in registers: the slot goes back to the MMA issuer
+                    // before the gates are computed
+                    tc::fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&s.empty[0][slot]);
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float rg = sigmoid_f(r[i]);
@@ -787,22 +876,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     tc::tmem_st16(lane_base + kHCol + u0, hv);
                     }
                     tc::tmem_st_wait();
-                    tc::fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&s.empty[0][slot]);
                 }
                 if (!ok) break;
-                // all MMAs of step t are done (the last chunk's completed): h_{t+1} -> A
-                for (uint32_t c = 0; c < kChunks; ++c)
-                    for (uint32_t g8 = 0; g8 < kUPW; g8 += 8) {
-                        const uint32_t u0 = c * kUnits + half * kUPW + g8;
-                        float hv[8];
-                        tc::tmem_ld8(lane_base + kHCol + u0, hv);
-                        tc::tmem_ld_wait();
-                        uint8_t* blk = s.A + (u0 >> 6) * 128 * 128;
-                        store_bf16x8(blk + tc::sw128_offset(row, u0 & 63u), hv);
+                // all MMAs of step t are done (the last chunk's completed): h_{t+1} -> A,
+                // four chunks' units per TMEM round trip
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < kChunks; c0 += 4) {
+                    float hv[4][16];
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) tc::tmem_ld16(lane_base + kHCol + (c0 + i) * kUnits + half * kUPW, hv[i]);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) {
+                        uint32_t hb[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) hb[e] = bf2(hv[i][2 * e], hv[i][2 * e + 1]);
+                        tc::tmem_st8u(lane_base + kACol + ((c0 + i) * kUnits + half * kUPW) / 2, hb);
                     }
-                tc::fence_async_smem();
+                }
+                tc::tmem_st_wait();
                 tc::fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&s.h_full);
@@ -815,7 +907,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
         const uint32_t q = warp & 3u, row = q * 32 + lane, atid = tid - kAuxWarp0 * 32;
         const uint32_t lane_base = tmem + ((q * 32) << 16);
         const uint32_t TA = T * 4u;
-        uint32_t K0 = 0, au[kSlots] = {};
+        uint32_t K0 = 0, au = 0;  // bit slot: phase parity of full[1][slot]
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
             const uint32_t b = tile / p.tiles_per_vehicle, tv = tile % p.tiles_per_vehicle;
@@ -831,31 +923,38 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                 // prober of step t-1 (entry kEntries t + 1; at t = 0 an empty entry; the last at kEntries T)
                 const uint32_t k = K0 + (t < T ? kEntries * t + 1 : kEntries * T);
                 const uint32_t slot = k % kSlots;
-                ok = aux_all(tc::mbar_wait(&s.full[1][slot], au[slot] & 1u, err, 9, k, lim));
+                ok = aux_all(tc::mbar_wait(&s.full[1][slot], (au >> slot) & 1u, err, 9, k, lim));
                 if (!ok) break;
-                ++au[slot];
+                au ^= 1u << slot;
                 tc::fence_after();
                 if (t > 0) {
                     constexpr uint32_t hid = kMaxHid;  // the tensor-core path takes prober hidden_dim 32
                     float h1[kMaxHid];
                     const float* pw = s.pw;
-#pragma unroll
-                    for (uint32_t c0 = 0; c0 < kMaxHid; c0 += 16) {
-                        float v[16];
-                        tc::tmem_ld16(lane_base + slot * kSlotCols + c0, v);
+                    {
+                        float v0[16], v1[16];
+                        tc::tmem_ld16(lane_base + slot * kSlotCols, v0);
+                        tc::tmem_ld16(lane_base + slot * kSlotCols + 16, v1);
                         tc::tmem_ld_wait();
+                        // the slot goes back to the MMA issuer before the prober's layers run
+                        tc::fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&s.empty[1][slot]);
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) h1[c0 + i] = gelu_fast(v[i] + pw[c0 + i]);
+                        for (int i = 0; i < 16; ++i) {
+                            h1[i] = gelu_fast(v0[i] + pw[i]);
+                            h1[16 + i] = gelu_fast(v1[i] + pw[16 + i]);
+                        }
                     }
-                    tc::fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&s.empty[1][slot]);
                     uint32_t off = hid;
-                    float h2[kMaxHid];
+                    // a hidden layer's outputs go to this row's shared staging as they are
+                    // produced and come back once the layer is done (h1 and the next h1
+                    // are never held in registers together)
+                    float* hrow = s.hst + row * (kMaxHid + 1);
                     for (uint32_t l = 0; l + 1 < a.prober_layers; ++l) {
                         const float* W = pw + off;
                         const float* bb = pw + off + hid * hid;
-#pragma unroll
+#pragma unroll 4
                         for (uint32_t o = 0; o < hid; ++o) {
                             float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
@@ -863,14 +962,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                                 s0 = fmaf(h1[i], W[o * hid + i], s0);
                                 s1 = fmaf(h1[i + 1], W[o * hid + i + 1], s1);
                             }
-                            h2[o] = gelu_fast((s0 + s1) + bb[o]);
+                            hrow[o] = gelu_fast((s0 + s1) + bb[o]);
                         }
 #pragma unroll
-                        for (uint32_t o = 0; o < hid; ++o) h1[o] = h2[o];
+                        for (uint32_t o = 0; o < hid; ++o) h1[o] = hrow[o];
                         off += hid * hid + hid;
                     }
-                    float po[15];
-#pragma unroll
+#pragma unroll 4
                     for (uint32_t o = 0; o < 15; ++o) {
                         float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
@@ -878,8 +976,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                             s0 = fmaf(h1[i], pw[off + o * hid + i], s0);
                             s1 = fmaf(h1[i + 1], pw[off + o * hid + i + 1], s1);
                         }
-                        po[o] = (s0 + s1) + pw[off + 15 * hid + o];
+                        hrow[o] = (s0 + s1) + pw[off + 15 * hid + o];
                     }
+                    float po[15];
+#pragma unroll
+                    for (uint32_t o = 0; o < 15; ++o) po[o] = hrow[o];
                     // integrator step t-1 (lewm_skyjepa_integrate_f32, kinematics.rs:377-484) + cost
                     const uint32_t ts = t - 1;
                     const float* act = cand_row + ts * 4;
@@ -1138,11 +1239,11 @@ cudaError_t launch_skyjepa_tc(const SkyjepaArgs& a, const uint8_t* packed, float
     e = launch_sample(sa, stream);
     if (e != cudaSuccess) return e;
     // 2. per-step inputs of every candidate; then the join with the latent
-    const uint64_t n_in = static_cast<uint64_t>(a.B) * a.S * a.T;
     if (!a.action_tcn_host || tcn_weight_floats(a.action_tcn) != kTcnParamFloats) return cudaErrorInvalidValue;
     TcnConst tw;
     for (uint32_t q = 0; q < kTcnParamFloats; ++q) tw.v[q] = a.action_tcn_host[q];
-    skyjepa_tc_inputs_kernel<<<static_cast<uint32_t>((n_in + 255) / 256), 256, 0, stream>>>(a, tw, xtiles);
+    const uint64_t rows = static_cast<uint64_t>(a.B) * a.S;
+    skyjepa_tc_inputs_seq_kernel<<<static_cast<uint32_t>((rows + 127) / 128), 128, 0, stream>>>(a, tw, xtiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = join_h0(stream, side)) != cudaSuccess) return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

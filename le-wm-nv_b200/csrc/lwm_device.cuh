@@ -44,6 +44,18 @@ __device__ __forceinline__ float normal_at(uint64_t seed, uint64_t index) {
     return (lane & 1u) ? r * s : r * c;
 }
 
+// Draws 4i .. 4i + 3 of the stream (one Philox block, both Box-Muller pairs):
+// the values normal_at gives for those indices.
+__device__ __forceinline__ float4 normal_quad(uint64_t seed, uint64_t block) {
+    const uint4 w = philox4x32_10(block, seed);
+    const float r0 = sqrtf(-2.0f * logf(unit_open(w.x)));
+    const float r1 = sqrtf(-2.0f * logf(unit_open(w.z)));
+    float s0, c0, s1, c1;
+    sincospif(2.0f * unit_open(w.y), &s0, &c0);
+    sincospif(2.0f * unit_open(w.w), &s1, &c1);
+    return make_float4(r0 * c0, r0 * s0, r1 * c1, r1 * s1);
+}
+
 // Candle's f32 maximum / minimum: (a < b) ? b : a and (a > b) ? b : a.
 __device__ __forceinline__ float cmax(float a, float b) { return a < b ? b : a; }
 __device__ __forceinline__ float cmin(float a, float b) { return a > b ? b : a; }
