@@ -265,57 +265,62 @@ __global__ void __launch_bounds__(kThreads, 1) lewm_pred_kernel(const __grid_con
             if (g > 0) tc::mbar_wait_landing(&s.a_full, (g - 1) & 1u, lim);
         }
     } else if (warp == 1) {
-        // ================= MMA issuer
-        if (lane == 0) {
+        // ================= MMA issuer (the whole warp, converged; one elected lane issues)
+        {
             const uint32_t xb = tc::smem_u32(s.X[0]), hb = tc::smem_u32(s.H[0]), wb = tc::smem_u32(s.W[0]);
+            // every lane waits; the outcome is the warp's (a diverged lane would leave elect.sync short)
+            auto wwait = [&](uint64_t* bar, uint32_t parity, volatile int* e, int site, uint32_t detail,
+                             uint32_t limit) -> bool {
+                return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, e, site, static_cast<int>(detail), limit));
+            };
             uint32_t n = 0;
             bool ok = true;
             for (uint32_t g = 0; ok && g < G; ++g) {
                 const PredHalf& hf = p.half[g % p.halves];
                 const uint32_t ph = g & 1u, nkb2 = hf.n1 / kKB;
                 // first GEMM: D1 = X W1^T ([128 x 192] x [192 x n1])
-                if (g > 0 && !(ok = tc::mbar_wait(&s.d1_drained, (g - 1) & 1u, err, 4, g, lim))) break;
-                if (!(ok = tc::mbar_wait(&s.a_full, ph, err, 5, g, lim))) break;
+                if (g > 0 && !(ok = wwait(&s.d1_drained, (g - 1) & 1u, err, 4, g, lim))) break;
+                if (!(ok = wwait(&s.a_full, ph, err, 5, g, lim))) break;
                 tc::fence_after();
                 const uint32_t id1 = tc::idesc_bf16_f32(kM, hf.n1);
                 for (uint32_t kb = 0; ok && kb < kDKB; ++kb, ++n) {
                     const uint32_t slot = n % kStages;
-                    if (!(ok = tc::mbar_wait(&s.w_full[slot], (n / kStages) & 1u, err, 6, n, lim))) break;
+                    if (!(ok = wwait(&s.w_full[slot], (n / kStages) & 1u, err, 6, n, lim))) break;
                     tc::fence_after();
                     const uint64_t da = tc::smem_desc(xb + kb * kBlk, 16, 1024, tc::kSwizzle128);
                     const uint64_t db = tc::smem_desc(wb + slot * kStage, 16, 1024, tc::kSwizzle128);
 #pragma unroll
                     for (uint32_t k = 0; k < kKB / 16; ++k)
-                        tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, id1, (kb | k) ? 1u : 0u);
-                    tc::commit(&s.w_empty[slot]);
+                        tc::mma_bf16_w(tmem, da + 2 * k, db + 2 * k, id1, (kb | k) ? 1u : 0u);
+                    tc::commit_w(&s.w_empty[slot]);
                 }
                 if (!ok) break;
-                tc::commit(&s.x_free);
-                tc::commit(&s.d1_full);
+                tc::commit_w(&s.x_free);
+                tc::commit_w(&s.d1_full);
                 // second GEMM: D2 = H W2^T ([128 x n1] x [n1 x 192]), this CTA's K slice
-                if (g > 0 && !(ok = tc::mbar_wait(&s.d2_drained, (g - 1) & 1u, err, 7, g, lim))) break;
+                if (g > 0 && !(ok = wwait(&s.d2_drained, (g - 1) & 1u, err, 7, g, lim))) break;
                 const uint32_t id2 = tc::idesc_bf16_f32(kM, kD);
                 for (uint32_t kb = 0; ok && kb < nkb2; ++kb, ++n) {
                     // each K block as soon as the drains have written it
-                    if (!(ok = tc::mbar_wait(&s.h_ready[kb], ph, err, 8, g, lim))) break;
+                    if (!(ok = wwait(&s.h_ready[kb], ph, err, 8, g, lim))) break;
                     tc::fence_after();
                     const uint32_t slot = n % kStages;
-                    if (!(ok = tc::mbar_wait(&s.w_full[slot], (n / kStages) & 1u, err, 9, n, lim))) break;
+                    if (!(ok = wwait(&s.w_full[slot], (n / kStages) & 1u, err, 9, n, lim))) break;
                     tc::fence_after();
                     const uint64_t da = tc::smem_desc(hb + kb * kBlk, 16, 1024, tc::kSwizzle128);
                     const uint64_t db = tc::smem_desc(wb + slot * kStage, 16, 1024, tc::kSwizzle128);
 #pragma unroll
                     for (uint32_t k = 0; k < kKB / 16; ++k)
-                        tc::mma_bf16(tmem + kColD2, da + 2 * k, db + 2 * k, id2, (kb | k) ? 1u : 0u);
-                    tc::commit(&s.w_empty[slot]);
+                        tc::mma_bf16_w(tmem + kColD2, da + 2 * k, db + 2 * k, id2, (kb | k) ? 1u : 0u);
+                    tc::commit_w(&s.w_empty[slot]);
                 }
                 if (!ok) break;
-                tc::commit(&s.h_free);
-                tc::commit(&s.d2_full);
+                tc::commit_w(&s.h_free);
+                tc::commit_w(&s.d2_full);
             }
             failed = !ok;
             // every MMA issued has completed before TMEM is released
-            tc::commit(&s.done);
+            tc::commit_w(&s.done);
             tc::mbar_wait_landing(&s.done, 0, lim);
         }
     } else {

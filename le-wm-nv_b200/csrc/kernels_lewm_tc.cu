@@ -122,14 +122,14 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err, u
     const uint32_t idesc = tc::idesc_bf16_f32(kTM, n_mma);
     for (uint32_t i = 0; i < nblk; ++i) {
         const uint32_t s = i & 1u, k0 = kb + i * kTK;
-        if (tid == 0) {
+        if (warp == 0) {  // the whole warp, converged; one elected lane issues
             tc::fence_after();
             const uint32_t a0 = tc::smem_u32(sA + s * kStageA), b0 = tc::smem_u32(sB + s * kStageB);
             const uint32_t steps = min(4u, (ke - k0) / 16u);
             for (uint32_t j = 0; j < steps; ++j)
-                tc::mma_bf16(tmem, tc::smem_desc(a0 + j * 32u, 16, 1024, tc::kSwizzle128),
-                             tc::smem_desc(b0 + j * 32u, 16, 1024, tc::kSwizzle128), idesc, (i | j) != 0u);
-            tc::commit(&bars[s]);
+                tc::mma_bf16_w(tmem, tc::smem_desc(a0 + j * 32u, 16, 1024, tc::kSwizzle128),
+                               tc::smem_desc(b0 + j * 32u, 16, 1024, tc::kSwizzle128), idesc, (i | j) != 0u);
+            tc::commit_w(&bars[s]);
         }
         if (i + 1 < nblk) {
             const uint32_t s2 = s ^ 1u, k1 = k0 + kTK;
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err, u
             __syncthreads();
         }
     }
-    if (tid == 0) tc::commit(&bars[2]);
+    if (warp == 0) tc::commit_w(&bars[2]);
     tc::mbar_wait(&bars[2], 0, err, kSiteFinal, static_cast<int>(nblk));
     tc::fence_after();
 

@@ -454,22 +454,27 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 }
         }
     } else if (warp == 1) {
-        // ================= MMA issuer
-        if (lane == 0) {
+        // ================= MMA issuer (the whole warp, converged; one elected lane issues)
+        {
             const uint32_t id128 = idesc_f16_f32(kRowsM, 2 * kNh), id64 = idesc_f16_f32(kRowsM, kNh);
             const uint32_t id32 = idesc_f16_f32(kRowsM, 32), id16 = idesc_f16_f32(kRowsM, 16);
             const uint32_t w_base = tc::smem_u32(s.W);
+            // every lane waits; the outcome is the warp's (a diverged lane would leave elect.sync short)
+            auto wwait = [&](uint64_t* bar, uint32_t parity, volatile int* e, int site, uint32_t detail,
+                             uint32_t limit) -> bool {
+                return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, e, site, static_cast<int>(detail), limit));
+            };
             // descriptors of the operand bases; an offset of n bytes adds n >> 4
             // to the start-address field (all addresses below 256 KB)
             const uint64_t da = tc::smem_desc(tc::smem_u32(s.A), 16, 256, tc::kSwizzle32);
             const uint64_t dbh = tc::smem_desc(w_base, 16, 1024, tc::kSwizzle128);
             const uint64_t dbx = tc::smem_desc(w_base + kBhBytes, 16, 256, tc::kSwizzle32);
-            bool ok = tc::mbar_wait(&s.w_full, 0, err, 2, 0, lim);
+            bool ok = wwait(&s.w_full, 0, err, 2, 0, lim);
             for (uint32_t t = 0; ok && t <= T; ++t) {
                 const uint32_t slot = t & 1u;
-                ok = tc::mbar_wait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds the own slice of h_t
-                if (ok && t >= 2) ok = tc::mbar_wait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
-                if (ok && t < T) ok = tc::mbar_wait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
+                ok = wwait(&s.h_full, t & 1u, err, 3, t, lim);  // A holds the own slice of h_t
+                if (ok && t >= 2) ok = wwait(&s.empty[slot], ((t >> 1) - 1u) & 1u, err, 4, t, lim);
+                if (ok && t < T) ok = wwait(&s.x_full[slot], (t >> 1) & 1u, err, 5, t, lim);
                 if (!ok) break;
                 tc::fence_after();
                 const uint32_t d = tmem + slot * kSlotCols;
@@ -479,24 +484,24 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                 if (t < T) {
                     const uint64_t dx = tc::smem_desc(tc::smem_u32(s.X[slot]), 16, 256, tc::kSwizzle32);
                     constexpr uint64_t x1 = kSliceBytes >> 4, nx = (2 * kNh * 32) >> 4;
-                    tc::mma_f16(d, dx, dbx, id128, 0);
-                    tc::mma_f16(d, dx + x1, dbx, id64, 1);
-                    tc::mma_f16(d + kColNx, dx, dbx + nx, id32, 0);
-                    tc::mma_f16(d + kColNx, dx + x1, dbx + nx, id16, 1);
+                    tc::mma_f16_w(d, dx, dbx, id128, 0);
+                    tc::mma_f16_w(d, dx + x1, dbx, id64, 1);
+                    tc::mma_f16_w(d + kColNx, dx, dbx + nx, id32, 0);
+                    tc::mma_f16_w(d + kColNx, dx + x1, dbx + nx, id16, 1);
                     acc = 1;
                 }
                 auto slice = [&](uint32_t j) {
                     const uint64_t a0 = da + ((j * kSlicePair) >> 4), a1 = a0 + (kSliceBytes >> 4);
                     const uint64_t b = dbh + (((j >> 2) * kBhBlock + (j & 3u) * 32) >> 4);
-                    tc::mma_f16(d, a0, b, id128, acc);
-                    tc::mma_f16(d, a1, b, id64, 1);
+                    tc::mma_f16_w(d, a0, b, id128, acc);
+                    tc::mma_f16_w(d, a1, b, id64, 1);
                     acc = 1;
                 };
                 // the own slice first, then the peers' group by group as they land
                 slice(c);
                 for (uint32_t g = 0; ok && g < kGroups; ++g) {
                     if (t > 0) {
-                        if (!(ok = tc::mbar_wait(&s.h_grp[g], (t - 1u) & 1u, err, 13, t, lim))) break;
+                        if (!(ok = wwait(&s.h_grp[g], (t - 1u) & 1u, err, 13, t, lim))) break;
                         tc::fence_after();
                     }
 #pragma unroll
@@ -506,12 +511,12 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     }
                 }
                 if (!ok) break;
-                tc::commit(&s.mma_done[slot]);
-                if (t < T) tc::commit(&s.x_empty[slot]);
+                tc::commit_w(&s.mma_done[slot]);
+                if (t < T) tc::commit_w(&s.x_empty[slot]);
             }
             failed = !ok;
             // every MMA issued has completed before TMEM is released
-            tc::commit(&s.done);
+            tc::commit_w(&s.done);
             tc::mbar_wait_landing(&s.done, 0, lim);
         }
     } else if (warp < kAuxWarp0) {

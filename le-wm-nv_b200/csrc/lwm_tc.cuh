@@ -92,6 +92,11 @@ __device__ __forceinline__ void mma_bf16_ta_w(uint32_t d_tmem, uint32_t a_tmem, 
         : "memory");
 }
 
+__device__ __forceinline__ void mma_f16_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    mma_bf16_w(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
 // The same instruction with fp16 operands (the instruction descriptor names
 // the operand types).
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
