@@ -866,6 +866,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
                     tc::fence_before();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&s.empty[0][slot]);
+                    // A lane-divergent branch that is never taken (tiles_done never reaches
+                    // 2^32 - 1, which the compiler cannot know): the divergent region it
+                    // opens and closes keeps the gate arithmetic below from being scheduled
+                    // ahead of the release above.  Measured on the 256-vehicle fleet: the
+                    // rollout takes 15.5 ms with it and 18.9 ms without (written out here:
+                    // the same test in a separate inline function did not keep the order).
+                    if (lane == 0 && tiles_done == 0xFFFFFFFFu) p.err[3] = 0;
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float rg = sigmoid_f(r[i]);
