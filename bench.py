@@ -54,21 +54,20 @@ ROLLOUT_FLOP_PER_CANDIDATE_STEP = 2 * (4 * 768 + 256 * 768 + 256 * 32 + 32 * 32 
 ROLLOUT_DRAM_BYTES = {"skyjepa": 1847040}
 
 
-NCCL_LOG = None  # this process's NCCL communicator log (multi-GPU runs)
+NCCL_LOG = None  # where this process's NCCL communicator log goes (multi-GPU runs)
 
 
 def nccl_log_setup():
-    """Route NCCL's communicator log (INIT lines: ranks, devices, NVLS) to a
-    per-process file, so stdout keeps the one JSON line; returns the path.
-    Called before torch (and NCCL) are loaded, so NCCL reads the settings."""
-    import tempfile
+    """Turn on NCCL's communicator log (INIT lines: ranks, devices, NVLS) on
+    stderr, so stdout keeps the one JSON line (NCCL's own default is
+    stdout); returns where it goes.  Called before torch (and NCCL) are
+    loaded, so NCCL reads the settings.  A caller's own NCCL_DEBUG wins."""
     if "NCCL_DEBUG" in os.environ:
-        return None
-    path = os.path.join(tempfile.gettempdir(), f"lewm_nccl_{os.getpid()}.log")
+        return os.environ.get("NCCL_DEBUG_FILE", "stdout") + f" (NCCL_DEBUG={os.environ['NCCL_DEBUG']}, caller's)"
     os.environ["NCCL_DEBUG"] = "INFO"
     os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
-    os.environ["NCCL_DEBUG_FILE"] = path
-    return path
+    os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
+    return "stderr (NCCL_DEBUG=INFO, NCCL_DEBUG_SUBSYS=INIT)"
 
 
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
@@ -343,18 +342,6 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
-def nccl_log_lines(path, limit=6):
-    """The communicator lines of this rank's NCCL log (rank count, NVLS)."""
-    if not path or not os.path.exists(path):
-        return []
-    keep = []
-    with open(path, errors="replace") as f:
-        for line in f:
-            if "Init COMPLETE" in line or "nRanks" in line or "NVLS" in line:
-                keep.append(line.strip()[-200:])
-    return keep[:limit]
-
-
 def fleet_collective_record(args, rank, world, local_rank, ctx):
     """The fleet across every rank by candidate shards: 256 vehicles x 4096
     candidates x 30 steps, bf16 rollout on the tensor cores, each rank scoring
@@ -471,7 +458,7 @@ def fleet_collective_record(args, rank, world, local_rank, ctx):
                      "peak_source": "MEASURED_PEAKS bf16_tflops_sustained (of measured) x n_gpus"},
         "timing": "CUDA events on the planner's stream, L2 flushed between plans, max over ranks",
         "nccl": {"version": ".".join(str(v) for v in torch.cuda.nccl.version()) if world > 1 else None,
-                 "log": nccl_log_lines(NCCL_LOG)},
+                 "ranks": dist.get_world_size() if world > 1 else 1, "log": NCCL_LOG},
         "clocks": clocks.summary(),
     }
 
