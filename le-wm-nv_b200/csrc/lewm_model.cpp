@@ -215,6 +215,7 @@ LewmModel::~LewmModel() {
     g_score.reset();
     g_enc.reset();
     if (blob_bf16) cudaFree(blob_bf16);
+    if (vit_qkv) cudaFree(vit_qkv);
     if (pred_w) cudaFree(pred_w);
     if (split.tc_err) cudaFree(split.tc_err);
     if (split.partial) cudaFree(split.partial);
@@ -506,9 +507,7 @@ cudaError_t LewmModel::encode_patches_body(uint32_t n, float* out, cudaStream_t 
     for (uint32_t l = 0; l < c.vit_layers; ++l) {
         const VitBlockW& b = w.vit[l];
         LWM_CU(launch_layernorm(f_x, f_y, rows, vh, 1, 0, b.ln1.w, b.ln1.b, c.vit_eps, s));
-        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.q, f_qkv, 3 * vh, rows), s));
-        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.k, f_qkv + vh, 3 * vh, rows), s));
-        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.v, f_qkv + 2 * vh, 3 * vh, rows), s));
+        LWM_CU(gemm_f32(sp, gemm(f_y, vh, b.qkv, f_qkv, 3 * vh, rows), s));
         LWM_CU(launch_attention(f_qkv, f_att, n, t, H, dh, scale, 0, 0, s));
         GemmArgs go = gemm(f_att, vh, b.o, f_x, vh, rows);
         go.residual = 1;
@@ -518,7 +517,7 @@ cudaError_t LewmModel::encode_patches_body(uint32_t n, float* out, cudaStream_t 
         GemmArgs g2 = gemm(f_f, c.vit_mlp, b.fc2, f_x, vh, rows);
         g2.residual = 1;
         LWM_CU(gemm_f32(sp, g2, s));
-        k += 9;
+        k += 7;
     }
     LWM_CU(launch_layernorm(f_x, f_cls, n, vh, t, 0, w.vit_norm.w, w.vit_norm.b, c.vit_eps, s));
     ++k;
@@ -531,6 +530,33 @@ void GraphCache::reset() {
     if (exec) cudaGraphExecDestroy(exec);
     exec = nullptr;
     seen = false;
+}
+
+// The ViT's query, key and value projections as one Linear of 3 x vit_hidden
+// outputs (weight rows q, then k, then v; the biases alike), so each layer
+// runs one GEMM into the [rows, 3 vit_hidden] buffer that the three filled
+// column range by column range (HfVitEncoder's SelfAttention: three Linears
+// of the same input).
+cudaError_t LewmModel::fuse_vit_qkv() {
+    if (c.encoder != LWM_ENCODER_VIT || w.vit.empty() || vit_qkv) return cudaSuccess;
+    const size_t vh = c.vit_hidden, per = 3 * vh * vh + 3 * vh;
+    LWM_CU(cudaMalloc(&vit_qkv, per * w.vit.size() * sizeof(float)));
+    for (size_t l = 0; l < w.vit.size(); ++l) {
+        VitBlockW& b = w.vit[l];
+        float* dst = vit_qkv + l * per;
+        const Lin* src[3] = {&b.q, &b.k, &b.v};
+        for (int i = 0; i < 3; ++i) {
+            LWM_CU(cudaMemcpy(dst + i * vh * vh, src[i]->w, vh * vh * sizeof(float), cudaMemcpyDeviceToDevice));
+            if (src[i]->b)
+                LWM_CU(cudaMemcpy(dst + 3 * vh * vh + i * vh, src[i]->b, vh * sizeof(float), cudaMemcpyDeviceToDevice));
+        }
+        b.qkv.w = dst;
+        b.qkv.b = b.q.b ? dst + 3 * vh * vh : nullptr;
+        b.qkv.out = static_cast<uint32_t>(3 * vh);
+        b.qkv.in = static_cast<uint32_t>(vh);
+        b.qkv.wb = nullptr;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t LewmModel::ensure_split() {
@@ -558,7 +584,7 @@ void for_each_lin(LewmWeights& w, F f) {
         for (Lin* l : {&b.qkv, &b.to_out, &b.fc1, &b.fc2, &b.ada}) f(*l);
     for (Lin& l : w.enc_lin) f(l);
     for (VitBlockW& b : w.vit)
-        for (Lin* l : {&b.q, &b.k, &b.v, &b.o, &b.fc1, &b.fc2}) f(*l);
+        for (Lin* l : {&b.qkv, &b.o, &b.fc1, &b.fc2}) f(*l);
 }
 
 }  // namespace

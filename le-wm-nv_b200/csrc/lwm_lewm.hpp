@@ -154,6 +154,7 @@ struct BlockW {
 struct VitBlockW {
     Norm ln1, ln2;
     Lin q, k, v, o, fc1, fc2;
+    Lin qkv;  // q, k and v as one Linear of 3 x vit_hidden outputs (LewmModel::fuse_vit_qkv)
 };
 
 // Tensor views into one weight blob (host walk of the documented order); with
@@ -207,6 +208,7 @@ struct LewmModel {
     LewmWeights w;
     float* blob = nullptr;  // device weights
     uint16_t* blob_bf16 = nullptr;  // bf16 copies of the GEMM weights, each 256-byte aligned
+    float* vit_qkv = nullptr;       // the ViT layers' fused query/key/value weights and biases
     int precision = LWM_PRECISION_F32;
     // bf16 with the image model's predictor shape: the whole rollout in one
     // launch (lewm_pred_kernel) with its weights packed per CTA rank
@@ -230,6 +232,7 @@ struct LewmModel {
     cudaError_t encode_patches_body(uint32_t n, float* out, cudaStream_t s);
     size_t encoder_layout(uint32_t n, EncoderOffsets* o) const;
     cudaError_t ensure_split();
+    cudaError_t fuse_vit_qkv();
     // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
     // GEMM inputs on the tensor cores, f32 accumulation and activations.
     cudaError_t set_precision(int p, cudaStream_t s);
