@@ -468,11 +468,12 @@ cudaError_t launch_h0_batched(const SkyjepaArgs& a, float* h0, cudaStream_t stre
 // history))[last position] (SkyJepaModel::encode_history, model.rs:52-66).
 cudaError_t launch_skyjepa_h0(const SkyjepaArgs& a, float* h0, cudaStream_t stream) {
     if (a.Hs > kH0MaxHist) return cudaErrorInvalidValue;
+    // the default encoder: one 16-CTA cluster per vehicle, pruned to what the
+    // last output depends on (one launch; 256 vehicles in 0.21 ms, against
+    // 1.07 ms for the batched per-layer kernels below)
+    if (skyjepa_h0_pruned_supported(a)) return launch_skyjepa_h0_pruned(a, h0, stream);
     if (a.h0_work && a.B >= kH0BatchedMinVehicles && a.Hs == kH0BatchedHist && a.state_tcn.k == 3)
         return launch_h0_batched(a, h0, stream);
-    // few vehicles, the default encoder: one 16-CTA cluster per vehicle,
-    // pruned to what the last output depends on
-    if (skyjepa_h0_pruned_supported(a)) return launch_skyjepa_h0_pruned(a, h0, stream);
     // few vehicles, wide encoder: one 8-CTA cluster per vehicle (weights
     // staged in shared memory, output channels split over the cluster)
     if (a.state_tcn.max_ch >= 64) return launch_skyjepa_h0_cluster(a, h0, stream);
