@@ -66,6 +66,12 @@ namespace lwm {
 // expf / tanhf on the rollout's critical path (plan 0.118 -> 0.110 ms).
 __device__ __forceinline__ float sigmoid_e(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
 __device__ __forceinline__ float tanh_e(float v) { return 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * v)); }
+// Candle's tanh-form GELU (gelu_tanh's products and their order) with tanh_e.
+__device__ __forceinline__ float gelu_e(float v) {
+    const float k = 0.7978845608028654f;
+    return __fmul_rn(__fmul_rn(0.5f, v),
+                     1.0f + tanh_e(__fmul_rn(__fmul_rn(k, v), 1.0f + __fmul_rn(__fmul_rn(0.044715f, v), v))));
+}
 
 namespace {
 
@@ -665,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
             // layer 1 activation, hidden layers, output (SkyJepaProber::forward, prober.rs:84-102)
             for (uint32_t e = atid; e < kOwnRows * kHid; e += kAuxThreads) {
                 const uint32_t rr = e / kHid, o = e % kHid;
-                s.a1[rr][o] = gelu_tanh(s.pre[par][rr][o] + __ldg(a.p_in_b + o));
+                s.a1[rr][o] = gelu_e(s.pre[par][rr][o] + __ldg(a.p_in_b + o));
             }
             aux_sync();
             float(*pin)[kHid] = s.a1;
@@ -685,8 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
                     s1b = fmaf(pin[rb][i + 1], w1, s1b);
                 }
                 const float bias = __ldg(a.p_hid_b[l] + lane);
-                pout[ra][lane] = gelu_tanh((s0a + s1a) + bias);
-                pout[rb][lane] = gelu_tanh((s0b + s1b) + bias);
+                pout[ra][lane] = gelu_e((s0a + s1a) + bias);
+                pout[rb][lane] = gelu_e((s0b + s1b) + bias);
                 aux_sync();
                 float(*tmp)[kHid] = pin;
                 pin = pout;
