@@ -133,6 +133,7 @@ __device__ __forceinline__ float pick(const float (&acc)[NP], uint32_t lane) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1) skyjepa_h0_pruned_kernel(SkyjepaArgs a, float* h0) {
+    pdl_trigger();  // the input kernel after it in the stream needs nothing from it
     extern __shared__ __align__(16) float sm[];
     const uint32_t c = cta_rank(), b = blockIdx.x / kCl;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;

@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, 
     // at step t (white noise, as sample_elem_kernel) and, with the other three
     // lanes of its group, encodes the window of step t (lane o: channel o)
     __shared__ float cand_s[kMaxHorizon][4];
+    pdl_trigger();  // the rollout after it may start its prologue (it waits for this kernel before its inputs)
     if (blockIdx.x == 0 && threadIdx.x < 4) err[threadIdx.x] = 0;  // the rollout's error word starts clear
     const uint64_t grow = blockIdx.x;  // b * S + s
     const uint32_t b = static_cast<uint32_t>(grow / a.S), sidx = static_cast<uint32_t>(grow % a.S);
@@ -366,6 +367,9 @@ __global__ void __launch_bounds__(256) skyjepa_mma_inputs_kernel(SkyjepaArgs a, 
     *reinterpret_cast<uint4*>(xt + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(xt + kSliceBytes + tc::sw32_offset(row, 0)) = make_uint4(l01, l23, l4, 0u);
     *reinterpret_cast<uint4*>(xt + kSliceBytes + tc::sw32_offset(row, 8)) = make_uint4(0u, 0u, 0u, 0u);
+    // this kernel completes only after the history encoder before it: the
+    // rollout's wait for this kernel then covers h0 as well
+    pdl_wait();
 }
 
 // ------------------------------------------------------------ main kernel
@@ -424,12 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1) skyjepa_mma_kernel(MmaArgs p) {
     tc::fence_after();
     const uint32_t tmem = s.tmem;
     bool failed = false;
+    // the weights do not come from the kernels before this one in the stream:
+    // their copy starts before the wait for those kernels (h0, x tiles, the
+    // cleared error word)
+    if (warp == 0 && lane == 0) {
+        tc::mbar_expect_tx(&s.w_full, kWBytes);
+        tc::bulk_g2s(s.W, p.w + static_cast<size_t>(c) * kWBytes, kWBytes, &s.w_full);
+    }
+    pdl_wait();
 
     if (warp == 0) {
-        // ================= producer: the CTA's weights once, then one x tile per step
+        // ================= producer: the CTA's weights once (issued above), then one x tile per step
         if (lane == 0) {
-            tc::mbar_expect_tx(&s.w_full, kWBytes);
-            tc::bulk_g2s(s.W, p.w + static_cast<size_t>(c) * kWBytes, kWBytes, &s.w_full);
             const uint8_t* xg = p.xchg + static_cast<size_t>(tile) * 2 * kABytes;
             uint32_t t = 0;  // x tiles issued
             auto load_x = [&](uint32_t k) -> bool {
@@ -971,16 +981,30 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     if (e != cudaSuccess) return e;
     if (!mma_configure(dev)) return cudaErrorNotSupported;
     if (!a.action_tcn_host) return cudaErrorInvalidValue;
-    // 0. initial latent per vehicle (on the side stream when given)
-    if ((e = fork_h0(a, h0, stream, side)) != cudaSuccess) return e;
-    // 1. the candidates (white noise) and the action encoder of every
-    // (candidate, step) as split-fp16 x tiles, one block per candidate
+    (void)side;
+    // 0. initial latent per vehicle; 1. the candidates (white noise) and the
+    // action encoder of every (candidate, step) as split-fp16 x tiles, one
+    // block per candidate; 2. the rollout.  One stream with programmatic
+    // dependent launch: the input kernel runs beside the history encoder
+    // (which triggers at its start) and finishes after it; the rollout starts
+    // its prologue (barriers, TMEM, the weight copy) beside the input kernel
+    // and waits for it before touching h0 and the x tiles.
+    if ((e = launch_skyjepa_h0(a, h0, stream)) != cudaSuccess) return e;
     MmaTcnConst tw;
     for (uint32_t q = 0; q < 3 * 104; ++q) tw.v[q] = a.action_tcn_host[q];
     const uint32_t threads = (4 * a.T + 31) / 32 * 32;
-    skyjepa_mma_inputs_kernel<<<a.B * a.S, threads, 0, stream>>>(a, tw, xtiles, err);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = join_h0(stream, side)) != cudaSuccess) return e;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t ic{};
+        ic.gridDim = dim3(a.B * a.S, 1, 1);
+        ic.blockDim = dim3(threads, 1, 1);
+        ic.stream = stream;
+        ic.attrs = pdl;
+        ic.numAttrs = 1;
+        if ((e = cudaLaunchKernelEx(&ic, skyjepa_mma_inputs_kernel, a, tw, xtiles, err)) != cudaSuccess) return e;
+    }
     // 3. the rollout: one 16-CTA cluster per 128 rows
     MmaArgs p;
     p.a = a;
@@ -997,13 +1021,14 @@ cudaError_t launch_skyjepa_mma(const SkyjepaArgs& a, const uint8_t* packed, floa
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = sizeof(MmaSmem) + 1024;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kCl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1] = pdl[0];
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (a.time_begin) cudaEventRecord(a.time_begin, stream);
     e = cudaLaunchKernelEx(&cfg, skyjepa_mma_kernel, p);
     if (a.time_end) cudaEventRecord(a.time_end, stream);

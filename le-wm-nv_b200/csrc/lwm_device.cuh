@@ -56,6 +56,14 @@ __device__ __forceinline__ float4 normal_quad(uint64_t seed, uint64_t block) {
     return make_float4(r0 * c0, r0 * s0, r1 * c1, r1 * s1);
 }
 
+// Programmatic dependent launch (griddepcontrol): a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start once every
+// CTA of the kernel before it in the stream has called pdl_trigger (or
+// exited); pdl_wait returns once that kernel has completed and its writes
+// are visible.  Both are no-ops in a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Candle's f32 maximum / minimum: (a < b) ? b : a and (a > b) ? b : a.
 __device__ __forceinline__ float cmax(float a, float b) { return a < b ? b : a; }
 __device__ __forceinline__ float cmin(float a, float b) { return a > b ? b : a; }
