@@ -36,6 +36,8 @@ namespace lwm {
 constexpr int kBM = 64, kBN = 64, kBK = 32;
 
 __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     __shared__ __align__(16) float As[2][kBK][kBM + 4];
     __shared__ __align__(16) float Ws[2][kBK][kBN + 4];
     const int tid = threadIdx.x;
@@ -160,7 +162,7 @@ cudaError_t gemm_f32(const GemmArgs& in, cudaStream_t stream, const SplitScratch
         g.counters = sp->counters;
     }
     dim3 grid(tx, ty, g.splits);
-    gemm_f32_kernel<<<grid, 256, 0, stream>>>(g);
+    if (cudaError_t e = launch_pdl(gemm_f32_kernel, grid, dim3(256), 0, stream, g); e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -257,6 +259,8 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
 // LayerNorm (affine, eps) of rows gathered from src row (r * t_in + pick).
 __global__ void layernorm_kernel(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
                                  const float* w, const float* b, float eps) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
     if (r >= rows) return;
@@ -271,6 +275,8 @@ __global__ void layernorm_kernel(const float* x, float* y, uint32_t rows, uint32
 // MLP hidden layer (Mlp::forward, modules.rs:108-115; VectorMlpEncoder).
 __global__ void norm_act_kernel(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
                                 const float* rm, const float* rv) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
     if (r >= rows) return;
@@ -303,6 +309,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __global__ void __launch_bounds__(kNaThreads) norm_act_row_kernel(float* x, uint32_t d, int kind, const float* w,
                                                                   const float* b, const float* rm, const float* rv) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     __shared__ float red[kNaThreads >> 5];
     float* xr = x + static_cast<size_t>(blockIdx.x) * d;
     float v[kNaPer];
@@ -385,6 +393,8 @@ __global__ void frames_put_kernel(const float* src, float* frames, uint32_t nfra
 // reference does (q * scale).
 __global__ void attention_kernel(const float* qkv, float* out, uint32_t seqs, uint32_t t, uint32_t H, uint32_t dh,
                                  float scale, int causal, int scale_q_first) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t gw = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
     const size_t total = static_cast<size_t>(seqs) * H * t;
@@ -442,6 +452,8 @@ constexpr uint32_t kAttnQ = 32, kAttnMaxT = 256;
 
 __global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, float* out, uint32_t t, uint32_t H,
                                                              uint32_t dh, float scale, int causal, int scale_q_first) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     extern __shared__ float sm[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t h = blockIdx.y, q0 = blockIdx.x * kAttnQ;
@@ -534,6 +546,8 @@ __host__ __device__ inline size_t at_smem_floats(uint32_t t) {
 
 __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, float* out, uint32_t t, uint32_t H,
                                                               float scale, int causal, int scale_q_first) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     extern __shared__ __align__(16) float sm[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t h = blockIdx.y, q0 = blockIdx.x * kAtQ, tp = at_tpad(t);
@@ -679,6 +693,8 @@ __global__ void patchify_kernel(const float* pix, float* patches, uint32_t n, ui
 // tokens [n, 1 + np, vh] = [cls ; patch embeddings] + position embeddings.
 __global__ void vit_assemble_kernel(const float* patch_out, const float* cls, const float* pos, float* x, uint32_t n,
                                     uint32_t np, uint32_t vh) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t total = static_cast<size_t>(n) * (np + 1) * vh;
     if (i >= total) return;
@@ -714,7 +730,10 @@ cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, c
 cudaError_t launch_layernorm(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
                              const float* w, const float* b, float eps, cudaStream_t s) {
     if (!rows) return cudaSuccess;
-    layernorm_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, y, rows, d, t_in, pick, w, b, eps);
+    if (cudaError_t e = launch_pdl(layernorm_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, s, x, y, rows, d, t_in, pick,
+                                   w, b, eps);
+        e != cudaSuccess)
+        return e;
     return cudaGetLastError();
 }
 
@@ -722,10 +741,9 @@ cudaError_t launch_norm_act(float* x, uint32_t rows, uint32_t d, int kind, const
                             const float* rm, const float* rv, cudaStream_t s) {
     if (!rows) return cudaSuccess;
     if (d >= 512 && d <= kNaThreads * kNaPer)
-        norm_act_row_kernel<<<rows, kNaThreads, 0, s>>>(x, d, kind, w, b, rm, rv);
+        return launch_pdl(norm_act_row_kernel, dim3(rows), dim3(kNaThreads), 0, s, x, d, kind, w, b, rm, rv);
     else
-        norm_act_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, rows, d, kind, w, b, rm, rv);
-    return cudaGetLastError();
+        return launch_pdl(norm_act_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, s, x, rows, d, kind, w, b, rm, rv);
 }
 
 cudaError_t launch_silu(const float* x, float* y, size_t n, cudaStream_t s) {
@@ -768,21 +786,19 @@ cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32
         cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(tsmem));
         if (e != cudaSuccess) return e;
-        attention_tiled_kernel<<<dim3((t + kAtQ - 1) / kAtQ, H, seqs), 256, tsmem, s>>>(qkv, out, t, H, scale, causal,
-                                                                                      scale_q_first);
-        return cudaGetLastError();
+        return launch_pdl(attention_tiled_kernel, dim3((t + kAtQ - 1) / kAtQ, H, seqs), dim3(256), tsmem, s, qkv, out, t,
+                          H, scale, causal, scale_q_first);
     }
     const size_t smem = (static_cast<size_t>(t) * (2 * dh + 1) + 8 * t + 8 * dh) * sizeof(float);
     if (t > 32 && t <= kAttnMaxT && dh <= 128 && smem <= 200 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        attention_smem_kernel<<<dim3((t + kAttnQ - 1) / kAttnQ, H, seqs), 256, smem, s>>>(qkv, out, t, H, dh, scale,
-                                                                                          causal, scale_q_first);
-        return cudaGetLastError();
+        return launch_pdl(attention_smem_kernel, dim3((t + kAttnQ - 1) / kAttnQ, H, seqs), dim3(256), smem, s, qkv, out,
+                          t, H, dh, scale, causal, scale_q_first);
     }
-    attention_kernel<<<blocks_for(warps, 8), 256, 0, s>>>(qkv, out, seqs, t, H, dh, scale, causal, scale_q_first);
-    return cudaGetLastError();
+    return launch_pdl(attention_kernel, dim3(blocks_for(warps, 8)), dim3(256), 0, s, qkv, out, seqs, t, H, dh, scale,
+                      causal, scale_q_first);
 }
 
 cudaError_t launch_goal_cost(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
@@ -804,8 +820,8 @@ cudaError_t launch_vit_assemble(const float* patch_out, const float* cls, const 
                                 uint32_t np, uint32_t vh, cudaStream_t s) {
     const size_t total = static_cast<size_t>(n) * (np + 1) * vh;
     if (!total) return cudaSuccess;
-    vit_assemble_kernel<<<blocks_for(total, 256), 256, 0, s>>>(patch_out, cls, pos, x, n, np, vh);
-    return cudaGetLastError();
+    return launch_pdl(vit_assemble_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, s, patch_out, cls, pos, x, n, np,
+                      vh);
 }
 
 }  // namespace lwm

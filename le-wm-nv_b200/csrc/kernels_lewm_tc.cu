@@ -27,6 +27,7 @@
 #include <atomic>
 #include <cstdint>
 
+#include "lwm_device.cuh"
 #include "lwm_lewm.hpp"
 #include "lwm_lewm_epi.cuh"
 #include "lwm_tc.cuh"
@@ -113,8 +114,10 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err, u
         }
     };
 
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    load_b(0, kb);  // the weights are not written by the kernels before this one
+    pdl_wait();     // the activations are: they are complete and visible from here
     load_a(kb);
-    load_b(0, kb);
     store_a(0);
     cp_async_wait_all();
     tc::fence_async_smem();
@@ -216,6 +219,8 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(GemmArgs g, int* err, u
 // The partials of an output are all loaded before they are added (in split
 // order); indices are 32-bit (the partial buffer holds under 2^32 floats).
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(GemmArgs g) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
     constexpr uint32_t kMaxSplits = 16;
     const uint32_t total = g.M * g.N, plane = total;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -273,10 +278,12 @@ cudaError_t gemm_tc(const GemmArgs& in, cudaStream_t stream, const SplitScratch*
         g.partial = sp->partial;
     }
     dim3 grid(tx, ty, g.splits);
-    gemm_tc_kernel<<<grid, 256, kTcSmem, stream>>>(g, err, tn);
-    if ((e = cudaGetLastError()) != cudaSuccess || g.splits <= 1) return e;
+    if ((e = launch_pdl(gemm_tc_kernel, grid, dim3(256), kTcSmem, stream, g, err, tn)) != cudaSuccess || g.splits <= 1)
+        return e;
     const uint64_t total = static_cast<uint64_t>(g.M) * g.N;
-    splitk_reduce_kernel<<<static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 8)), 256, 0, stream>>>(g);
+    e = launch_pdl(splitk_reduce_kernel, dim3(static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 8))),
+                   dim3(256), 0, stream, g);
+    if (e != cudaSuccess) return e;
     if (sp->extra_launches) ++*sp->extra_launches;
     return cudaGetLastError();
 }

@@ -11,6 +11,7 @@
 #include <string>
 
 #include "lwm_host.hpp"
+#include "lwm_pdl.hpp"
 #include "lwm_lewm.hpp"
 
 namespace lwm {
@@ -489,6 +490,7 @@ cudaError_t LewmModel::encode_pixels_body(const float* pix, uint32_t n, float* o
 // embedding GEMM, [CLS] + position embeddings, the encoder layers, the final
 // norm of the CLS token, then the projector.
 cudaError_t LewmModel::encode_patches_body(uint32_t n, float* out, cudaStream_t s) {
+    const PdlScope pdl;  // the encoder's launches overlap each other's prologues
     const SplitScratch* sp = &split;
     const uint32_t vh = c.vit_hidden, p = c.patch_size, side = c.image_size / p, np = side * side, t = np + 1;
     const uint32_t kdim = c.channels * p * p, H = c.vit_heads, dh = vh / H;

@@ -9,6 +9,9 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
+
+#include "lwm_pdl.hpp"
 #include <cuda_runtime.h>
 
 namespace lwm {
@@ -63,6 +66,28 @@ __device__ __forceinline__ float4 normal_quad(uint64_t seed, uint64_t block) {
 // are visible.  Both are no-ops in a kernel launched without the attribute.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launches `kernel`, with programmatic stream serialization while a PdlScope
+// is open on the launching thread (the kernel calls pdl_wait before it reads
+// what the kernels before it wrote, and before it completes; without the
+// attribute both are no-ops).  The ViT encoder's chain of short launches
+// gains from it; a chain that interleaves with launches made without it
+// (the vector model's predictor) measured slower, so it stays off there.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_pdl_launch ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Candle's f32 maximum / minimum: (a < b) ? b : a and (a > b) ? b : a.
 __device__ __forceinline__ float cmax(float a, float b) { return a < b ? b : a; }
