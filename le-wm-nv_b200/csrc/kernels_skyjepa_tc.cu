@@ -510,8 +510,18 @@ struct TcnConst {
 // computed once, when it first enters a window (at p = 9), then slides down
 // with the window.  Only the padded edge values (conv1 at p = 0, 1; block 1
 // at p = 1, 3) and blocks 2 and 3 are evaluated per window.  Every
-// convolution sums its taps in conv_at's order (with the fast GELU), so x_t
-// is tcn_last's value for the window.
+// convolution sums its taps in conv_at's order and the GELU is the fast
+// GELU with its operations regrouped (gelu_fast5), so x_t is tcn_last's
+// value for the window up to the last bits of each GELU.
+// The fast GELU in five arithmetic operations and one MUFU: 0.5 v (1 + tanh(u))
+// = h + h tanh(u) with h = v / 2 and u = v (c0 + c1 v^2), c0 = sqrt(2 / pi),
+// c1 = 0.044715 c0 (gelu_fast's function, operations regrouped).
+__device__ __forceinline__ float gelu_fast5(float v) {
+    const float u = v * fmaf(0.7978845608028654f * 0.044715f, v * v, 0.7978845608028654f);
+    const float h = 0.5f * v;
+    return fmaf(h, tanh_fast(u), h);
+}
+
 template <bool kTap0, bool kTap1>
 __device__ __forceinline__ void conv3(const float* W, const float* B, const float (&x0)[kTcnC], const float (&x1)[kTcnC],
                                       const float (&x2)[kTcnC], float (&out)[kTcnC]) {
@@ -524,7 +534,7 @@ __device__ __forceinline__ void conv3(const float* W, const float* B, const floa
             if (kTap1) acc = fmaf(W[(o * kTcnC + i) * kTcnK + 1], x1[i], acc);
             acc = fmaf(W[(o * kTcnC + i) * kTcnK + 2], x2[i], acc);
         }
-        out[o] = gelu_fast(acc + B[o]);
+        out[o] = gelu_fast5(acc + B[o]);
     }
 }
 
@@ -535,7 +545,7 @@ __device__ __forceinline__ void block3(const TcnBlockW& w, const float (&h0)[kTc
     float c[kTcnC];
     conv3<kTap0, kTap1>(w.w2, w.b2, h0, h1, h2, c);
 #pragma unroll
-    for (int o = 0; o < kTcnC; ++o) out[o] = gelu_fast(c[o] + res[o]);
+    for (int o = 0; o < kTcnC; ++o) out[o] = gelu_fast5(c[o] + res[o]);
 }
 
 __global__ void __launch_bounds__(128) skyjepa_tc_inputs_seq_kernel(SkyjepaArgs a, const __grid_constant__ TcnConst tw,
