@@ -10,9 +10,12 @@
 //      other activation stay f32);
 //   W  bf16 weights [N, K] (converted once per scorer), 16-byte cp.async
 //      copies into the same layout;
-//   one thread issues tcgen05.mma (M 128, N <= 128, K 16) into a TMEM
-//   accumulator and commits each stage to an mbarrier that releases it; the
-//   next block's loads run while the tensor core works on this one.
+//   warp 0 (converged, one elected lane) issues tcgen05.mma (M 128, N <= 128,
+//   K 16) into a TMEM accumulator and commits each stage to an mbarrier that
+//   releases it; the next block's loads run while the tensor core works on
+//   this one.  Launched with programmatic dependent launch inside the ViT
+//   encoder: the weights of the first block load before the wait for the
+//   kernel that wrote the activations.
 // The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
 // 32 (w % 4) .. +31 = rows, w / 4 picks the column half) into a shared-memory
 // tile, then writes it a warp per row so that C, the gate table and the

@@ -33,16 +33,19 @@
 // finishes the prober, integrates and accumulates the cost.
 //
 // Roles (448 threads): warp 0 loads the weights once and streams the x tiles;
-// warp 1 allocates TMEM and issues the MMAs; warps 2-9 run the gates (two
+// warp 1 allocates TMEM and issues the MMAs (the whole warp, one elected
+// lane per instruction); warps 2-9 run the gates (two
 // warps per TMEM lane quadrant, 8 units each); warps 10-13 read the prober
 // columns, then finish the prober, the integrator, the cost and the MPPI
 // partial of the CTA's 8 rows.  Every hand-off is an mbarrier with a bounded
 // wait; a wait that gives up records its site and the kernel unwinds.
 //
-// Before it, per plan: skyjepa_mma_inputs_kernel (the candidates, sampled as
+// Before it, per plan and in the same stream: the history encoder (h0 per
+// vehicle) and skyjepa_mma_inputs_kernel (the candidates, sampled as
 // sample_elem_kernel does, and the action encoder of every (candidate, step)
-// as split-fp16 x tiles with a constant-1 column that carries the GRU biases)
-// and the history encoder (h0 per vehicle, on a side stream).
+// as split-fp16 x tiles with a constant-1 column that carries the GRU
+// biases), chained by programmatic dependent launch: the input kernel runs
+// beside the encoder and the rollout's prologue beside the input kernel.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
