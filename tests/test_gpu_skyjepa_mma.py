@@ -5,6 +5,8 @@ tolerances: per-candidate costs within 1e-4 relative, the MPPI sequence
 within 1e-4, the best index up to ties — several vehicles with their own
 masses, horizons that are odd and long, more 128-row clusters than one wave,
 the seeded Philox path, and agreement with the CUDA-core f32 rollout."""
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -86,3 +88,27 @@ def test_split_fp16_seeded_plan_matches_cuda_core_rollout(ctx):
         res[prec] = p.plan(_scorer(ctx, w, precision=prec))
     assert_costs_close(res["f32"].scores, res["f32-cuda-core"].scores)
     assert_actions_close(res["f32"].sequence, res["f32-cuda-core"].sequence)
+
+
+def test_split_fp16_context_changes_between_back_to_back_plans(ctx):
+    # One scorer and planner, the context replaced between plans that run back
+    # to back on one stream: the history encoder, the input kernel and the
+    # rollout are chained by programmatic dependent launch, and each plan must
+    # read the h0 and x tiles of its own context (not the previous plan's).
+    wa = W.skyjepa(seed=53, batch=2, samples=256, horizon=8)
+    other = W.skyjepa(seed=54, batch=2, samples=256, horizon=8)
+    # the same model, weights and normalisation; another state / action
+    # history and reference window
+    wb = dataclasses.replace(wa, state_history=other.state_history, action_history=other.action_history,
+                             reference_states=other.reference_states, reference_actions=other.reference_actions,
+                             initial=other.initial)
+    noise = normals(84, (1, 2, 256, 8, 4))
+    p = L.MppiPlanner(ctx, wa.mppi)
+    sc = _scorer(ctx, wa)
+    for w in (wa, wb, wa):
+        sc.set_context(w.state_history, w.action_history, w.reference_states, w.reference_actions)
+        p.set_warm_start_sequence(w.warm_start)
+        r = p.plan(sc, injected_noise=noise)
+        ref = _oracle_plan(w, noise)
+        assert_costs_close(r.scores, ref["scores"])
+        assert_actions_close(r.sequence, ref["sequence"])
