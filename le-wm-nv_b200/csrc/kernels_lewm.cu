@@ -529,13 +529,13 @@ __global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, f
 }
 
 // The same attention for 64-wide heads, register-tiled: a block per
-// (sequence, head, 32 queries), K (rows padded to 68 floats: 16-byte rows
+// (sequence, head, 8 QW queries), K (rows padded to 68 floats: 16-byte rows
 // that eight lanes read from eight different bank quads), V and the block's
-// queries in shared memory.  Warp w scores its 4 queries against keys
-// lane + 32 u (u < 8), 4 x 8 accumulators a thread, 16-byte operand loads;
-// the softmax weights go to a per-warp [key][4] table, and the lanes then
-// accumulate output dimensions lane and lane + 32 of the 4 queries over the
-// keys.  Every dot product, the softmax and the weighted sums run in the
+// queries in shared memory.  Warp w scores its QW (4, or 2 when the grid is
+// small) queries against keys lane + 32 u (u < 8), QW x 8 accumulators a
+// thread, 16-byte operand loads; the softmax weights go to a per-warp
+// [key][4] table, and the lanes then accumulate output dimensions lane and
+// lane + 32 of the QW queries over the keys.  Every dot product, the softmax and the weighted sums run in the
 // same order as attention_smem_kernel's, so the outputs are identical.
 constexpr uint32_t kAtQ = 32, kAtDh = 64, kAtKld = 68;
 __host__ __device__ inline uint32_t at_tpad(uint32_t t) { return (t + 31u) & ~31u; }
@@ -544,13 +544,14 @@ __host__ __device__ inline size_t at_smem_floats(uint32_t t) {
     return static_cast<size_t>(tp) * kAtKld + static_cast<size_t>(tp) * kAtDh + kAtQ * kAtKld + 8u * tp * 4u;
 }
 
+template <uint32_t QW>
 __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, float* out, uint32_t t, uint32_t H,
                                                               float scale, int causal, int scale_q_first) {
     pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
     pdl_wait();     // the kernels before this one are complete and their writes visible
     extern __shared__ __align__(16) float sm[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t h = blockIdx.y, q0 = blockIdx.x * kAtQ, tp = at_tpad(t);
+    const uint32_t h = blockIdx.y, q0 = blockIdx.x * (8u * QW), tp = at_tpad(t);
     const size_t s = blockIdx.z;
     const uint32_t inner = H * kAtDh;
     float* Ks = sm;                    // [tp][68]
@@ -569,7 +570,7 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
         *reinterpret_cast<float4*>(Ks + j * kAtKld + c) = k;
         *reinterpret_cast<float4*>(Vs + j * kAtDh + c) = v;
     }
-    for (uint32_t idx = threadIdx.x; idx < kAtQ * 16u; idx += blockDim.x) {
+    for (uint32_t idx = threadIdx.x; idx < 8u * QW * 16u; idx += blockDim.x) {
         const uint32_t qi = idx >> 4, c = (idx & 15u) * 4u, i = q0 + qi;
         float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < t) {
@@ -579,25 +580,25 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
         *reinterpret_cast<float4*>(Qs + qi * kAtKld + c) = q;
     }
     __syncthreads();
-    const uint32_t ql = warp * 4u;  // the warp's first query, block-local
+    const uint32_t ql = warp * QW;  // the warp's first query, block-local
     if (q0 + ql >= t) return;
-    float acc[4][8];
+    float acc[QW][8];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < static_cast<int>(QW); ++a)
 #pragma unroll
         for (int u = 0; u < 8; ++u) acc[a][u] = 0.0f;
     const uint32_t nu = tp / 32u;  // key rounds that hold real keys (the rest of the 8 stay unused)
 #pragma unroll 1
     for (uint32_t d = 0; d < kAtDh; d += 4) {
-        float4 q[4];
+        float4 q[QW];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) q[a] = *reinterpret_cast<const float4*>(Qs + (ql + a) * kAtKld + d);
+        for (int a = 0; a < static_cast<int>(QW); ++a) q[a] = *reinterpret_cast<const float4*>(Qs + (ql + a) * kAtKld + d);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             if (static_cast<uint32_t>(u) >= nu) break;
             const float4 k = *reinterpret_cast<const float4*>(Ks + (u * 32u + lane) * kAtKld + d);
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
+            for (int a = 0; a < static_cast<int>(QW); ++a) {
                 acc[a][u] = fmaf(q[a].x, k.x, acc[a][u]);
                 acc[a][u] = fmaf(q[a].y, k.y, acc[a][u]);
                 acc[a][u] = fmaf(q[a].z, k.z, acc[a][u]);
@@ -605,10 +606,10 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
             }
         }
     }
-    float inv[4];
+    float inv[QW];
     uint32_t jend = 0;
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < static_cast<int>(QW); ++a) {
         const uint32_t i = q0 + ql + a;
         const uint32_t jmax = i >= t ? 0u : (causal ? i + 1 : t);
         jend = jmax > jend ? jmax : jend;
@@ -637,19 +638,21 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
         inv[a] = warp_sum(sum);
     }
     __syncwarp();
-    float o[4][2];
+    float o[QW][2];
 #pragma unroll
-    for (int a = 0; a < 4; ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
+    for (int a = 0; a < static_cast<int>(QW); ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
     for (uint32_t j = 0; j < jend; ++j) {
         const float4 p = *reinterpret_cast<const float4*>(Pt + j * 4u);
+        const float pw[4] = {p.x, p.y, p.z, p.w};
         const float v0 = Vs[j * kAtDh + lane], v1 = Vs[j * kAtDh + lane + 32u];
-        o[0][0] = fmaf(p.x, v0, o[0][0]); o[0][1] = fmaf(p.x, v1, o[0][1]);
-        o[1][0] = fmaf(p.y, v0, o[1][0]); o[1][1] = fmaf(p.y, v1, o[1][1]);
-        o[2][0] = fmaf(p.z, v0, o[2][0]); o[2][1] = fmaf(p.z, v1, o[2][1]);
-        o[3][0] = fmaf(p.w, v0, o[3][0]); o[3][1] = fmaf(p.w, v1, o[3][1]);
+#pragma unroll
+        for (int a = 0; a < static_cast<int>(QW); ++a) {
+            o[a][0] = fmaf(pw[a], v0, o[a][0]);
+            o[a][1] = fmaf(pw[a], v1, o[a][1]);
+        }
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < static_cast<int>(QW); ++a) {
         const uint32_t i = q0 + ql + a;
         if (i >= t) break;
         float* orow = out + (s * t + i) * inner + h * kAtDh;
@@ -783,10 +786,19 @@ cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32
     const size_t tsmem = at_smem_floats(t) * sizeof(float);
     const bool aligned = (reinterpret_cast<uintptr_t>(qkv) & 15u) == 0 && (H * kAtDh * 3u) % 4u == 0;
     if (t > 32 && t <= kAttnMaxT && dh == kAtDh && aligned && tsmem <= 200 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(tsmem));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attention_tiled_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(tsmem));
         if (e != cudaSuccess) return e;
-        return launch_pdl(attention_tiled_kernel, dim3((t + kAtQ - 1) / kAtQ, H, seqs), dim3(256), tsmem, s, qkv, out, t,
+        // 4 queries a warp (32 a block); 2 (16 a block) when that leaves SMs
+        // without a block (the ViT's 197 tokens x 3 heads x a few frames)
+        const size_t blocks4 = static_cast<size_t>((t + kAtQ - 1) / kAtQ) * H * seqs;
+        if (blocks4 < 148)
+            return launch_pdl(attention_tiled_kernel<2>, dim3((t + 15) / 16, H, seqs), dim3(256), tsmem, s, qkv, out, t,
+                              H, scale, causal, scale_q_first);
+        return launch_pdl(attention_tiled_kernel<4>, dim3((t + kAtQ - 1) / kAtQ, H, seqs), dim3(256), tsmem, s, qkv, out, t,
                           H, scale, causal, scale_q_first);
     }
     const size_t smem = (static_cast<size_t>(t) * (2 * dh + 1) + 8 * t + 8 * dh) * sizeof(float);
