@@ -271,6 +271,41 @@ __global__ void layernorm_kernel(const float* x, float* y, uint32_t rows, uint32
     for (uint32_t i = lane; i < d; i += 32) yr[i] = (xr[i] - mean) / den * w[i] + b[i];
 }
 
+// The same for rows of exactly NQ x 32 values (the ViT's 192: NQ = 6): the
+// row is read once into registers; the sums run in row_stats' order, so the
+// outputs are layernorm_kernel's.
+template <int NQ>
+__global__ void layernorm_reg_kernel(const float* x, float* y, uint32_t rows, uint32_t t_in, uint32_t pick,
+                                     const float* w, const float* b, float eps) {
+    pdl_trigger();  // launched with programmatic serialization (launch_pdl): the next kernel may start
+    pdl_wait();     // the kernels before this one are complete and their writes visible
+    constexpr uint32_t d = NQ * 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    const float* xr = x + (static_cast<size_t>(r) * t_in + pick) * d;
+    float v[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) v[q] = xr[lane + 32 * q];
+    float sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) sum += v[q];
+    const float mean = warp_sum(sum) / static_cast<float>(d);
+    float var = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+        const float c = v[q] - mean;
+        var += c * c;
+    }
+    const float den = sqrtf(warp_sum(var) / static_cast<float>(d) + eps);
+    float* yr = y + static_cast<size_t>(r) * d;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+        const uint32_t i = lane + 32 * q;
+        yr[i] = (v[q] - mean) / den * w[i] + b[i];
+    }
+}
+
 // In place: norm (BatchNorm eval / LayerNorm / none) then GELU (tanh) of an
 // MLP hidden layer (Mlp::forward, modules.rs:108-115; VectorMlpEncoder).
 __global__ void norm_act_kernel(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
@@ -733,11 +768,11 @@ cudaError_t launch_ada_ln(const float* x, float* y, uint32_t rows, uint32_t d, c
 cudaError_t launch_layernorm(const float* x, float* y, uint32_t rows, uint32_t d, uint32_t t_in, uint32_t pick,
                              const float* w, const float* b, float eps, cudaStream_t s) {
     if (!rows) return cudaSuccess;
-    if (cudaError_t e = launch_pdl(layernorm_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, s, x, y, rows, d, t_in, pick,
-                                   w, b, eps);
-        e != cudaSuccess)
-        return e;
-    return cudaGetLastError();
+    if (d == 192)
+        return launch_pdl(layernorm_reg_kernel<6>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, x, y, rows, t_in, pick, w,
+                          b, eps);
+    return launch_pdl(layernorm_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, s, x, y, rows, d, t_in, pick, w, b,
+                      eps);
 }
 
 cudaError_t launch_norm_act(float* x, uint32_t rows, uint32_t d, int kind, const float* w, const float* b,
