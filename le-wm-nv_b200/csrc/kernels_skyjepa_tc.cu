@@ -703,7 +703,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) skyjepa_tc_kernel(TcArgs p) {
     const uint32_t entries = kEntries * T + 1;  // acc-ring entries per tile
 
     if (warp == 0) {
-        // ================= producer: weight chunks, 2 slots
+        // ================= producer: weight chunks (kWStages-deep ring), x tiles (2 slots)
         if (lane == 0) {
             uint32_t j = 0, xs = 0;
             for (uint32_t tile = blockIdx.x; tile < p.tiles && !err[0]; tile += gridDim.x)
