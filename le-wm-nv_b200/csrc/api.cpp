@@ -93,16 +93,20 @@ struct DevBuf {
 // device allocation laid out like the pinned staging they are copied to, so
 // that lwm_plan reads all of them back with one copy.
 struct ResultLayout {
-    size_t fa, seq, sc, best, total;
+    size_t fa, seq, sc, best, err, total;
 };
 inline size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+// first action, sequence, scores, best indices, then the tensor-core
+// rollouts' error word (4 ints: site, block, detail, parity), so that one
+// device-to-host copy brings back the results and the error word together
 inline ResultLayout result_layout(size_t B, size_t T, size_t A, size_t S) {
     ResultLayout l;
     l.fa = 0;
     l.seq = round256(B * A * 4);
     l.sc = round256(l.seq + B * T * A * 4);
     l.best = round256(l.sc + B * S * 4);
-    l.total = l.best + B * 4;
+    l.err = (l.best + B * 4 + 15) & ~static_cast<size_t>(15);
+    l.total = l.err + 4 * sizeof(int);
     return l;
 }
 
@@ -191,7 +195,7 @@ struct lwm_scorer {
     std::unique_ptr<lwm::LewmModel> lewm;
     // learned scorer on tensor cores (bf16): packed weights, per-vehicle h0, wait-timeout flag
     int32_t precision = LWM_PRECISION_F32;
-    DevBuf tc_packed, tc_h0, tc_err, tc_x, h0_work;
+    DevBuf tc_packed, tc_h0, tc_x, h0_work;
     bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
     DevBuf small_x;
     lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
@@ -217,7 +221,8 @@ struct lwm_planner {
     uint32_t cap_b = 0;
     DevBuf bounds, zeros, std_init, mean, stdv, cand, scores, partials, counters, sequence, first_action, warm,
         best, best_score, carried, noise_tmp;
-    DevBuf results;  // holds first_action, sequence, scores and best (views into it)
+    DevBuf results;  // holds first_action, sequence, scores, best (views into it) and the error word
+    uint32_t results_batch = 0;  // the batch the views were laid out for
     HostBuf staging;
     uint32_t last_batch = 0, last_cols = 0;
     // iCEM trace: [iterations][4][B] scores and the elite mean of an iteration
@@ -235,6 +240,11 @@ struct lwm_planner {
     uint32_t elite_iterations = 0;
     bool has_result = false;
 };
+
+// The tensor-core rollouts' error word in the planner's result block.
+static int* result_err(lwm_planner* p, uint32_t B) {
+    return reinterpret_cast<int*>(static_cast<char*>(p->results.ptr) + result_layout(B, p->T, p->A, p->S).err);
+}
 
 namespace {
 
@@ -417,11 +427,18 @@ lwm_status ensure_planner_buffers(lwm_planner* p, uint32_t B) {
     const ResultLayout rl = result_layout(B, p->T, p->A, p->S);
     if (p->results.bytes < rl.total) {
         LWM_TRY(p->results.ensure(rl.total));
-        p->first_action.set_view(p->results.ptr, rl.fa, static_cast<size_t>(B) * p->A * 4);
-        p->sequence.set_view(p->results.ptr, rl.seq, seq * 4);
-        p->scores.set_view(p->results.ptr, rl.sc, static_cast<size_t>(B) * p->S * 4);
-        p->best.set_view(p->results.ptr, rl.best, static_cast<size_t>(B) * 4);
+        LWM_CUDA(cudaMemset(p->results.ptr, 0, rl.total));  // the error word starts clear
     }
+    if (p->results_batch != B) {
+        // the views move with the batch (the error word is zero wherever it lands:
+        // every plan that can set it clears it first, and a reported error clears it)
+        LWM_CUDA(cudaMemset(static_cast<char*>(p->results.ptr) + rl.err, 0, 4 * sizeof(int)));
+        p->results_batch = B;
+    }
+    p->first_action.set_view(p->results.ptr, rl.fa, static_cast<size_t>(B) * p->A * 4);
+    p->sequence.set_view(p->results.ptr, rl.seq, seq * 4);
+    p->scores.set_view(p->results.ptr, rl.sc, static_cast<size_t>(B) * p->S * 4);
+    p->best.set_view(p->results.ptr, rl.best, static_cast<size_t>(B) * 4);
     LWM_TRY(p->partials.ensure(static_cast<size_t>(B) * P * pw * 4));
     LWM_TRY(p->counters.ensure(static_cast<size_t>(B) * 4));
 
@@ -514,7 +531,6 @@ lwm_status ensure_tc(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uint
     if (!sc->tc_ready) {
         LWM_TRY(sc->tc_packed.ensure(lwm::skyjepa_tc_packed_bytes()));
         LWM_CUDA(lwm::skyjepa_tc_pack(a, sc->tc_packed.as<uint8_t>(), sc->ctx->stream));
-        LWM_TRY(sc->tc_err.ensure(256));
         sc->tc_ready = true;
     }
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
@@ -530,7 +546,6 @@ lwm_status ensure_mma(lwm_scorer* sc, const lwm::SkyjepaArgs& a, uint32_t B, uin
         LWM_CUDA(lwm::skyjepa_mma_pack(a, sc->mma_packed.as<uint8_t>(), sc->ctx->stream));
         sc->mma_ready = true;
     }
-    LWM_TRY(sc->tc_err.ensure(256));
     LWM_TRY(sc->tc_h0.ensure(static_cast<size_t>(B) * a.H * sizeof(float)));
     LWM_TRY(sc->h0_work.ensure(lwm::skyjepa_h0_work_bytes(a, B)));
     LWM_TRY(sc->tc_x.ensure(lwm::skyjepa_mma_xtile_bytes(B, S, T)));
@@ -807,11 +822,11 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     a.m.P = lwm::skyjepa_tc_partials_per_vehicle(p->S);
                     a.low_dev = low;
                     a.high_dev = high;
-                    LWM_CUDA(cudaMemsetAsync(sc->tc_err.ptr, 0, 4 * sizeof(int), stream));
+                    int* err_word = result_err(p, B);
+                    LWM_CUDA(cudaMemsetAsync(err_word, 0, 4 * sizeof(int), stream));
                     p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa_tc(a, sc->tc_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
-                                                    sc->tc_x.as<uint8_t>(), sc->tc_err.as<int>(), stream,
-                                                    &launched, &sc->side));
+                                                    sc->tc_x.as<uint8_t>(), err_word, stream, &launched, &sc->side));
                 } else if (sc->precision == LWM_PRECISION_F32 && lwm::skyjepa_mma_supported(a, &why) &&
                            lwm::skyjepa_mma_fits_device()) {
                     // f32-class accuracy on the tensor cores (split-fp16 operands)
@@ -825,8 +840,7 @@ lwm_status plan_device_locked(lwm_planner* p, lwm_scorer* sc, const float* injec
                     p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa_mma(a, sc->mma_packed.as<uint8_t>(), sc->tc_h0.as<float>(),
                                                      sc->tc_x.as<uint8_t>(), sc->mma_xchg.as<uint8_t>(),
-                                                     sc->tc_err.as<int>(), stream,
-                                                     &launched, &sc->side));
+                                                     result_err(p, B), stream, &launched, &sc->side));
                 } else {
                     p->ctx->kernel_timing(a);
                     LWM_CUDA(lwm::launch_skyjepa(a, stream, &launched));
@@ -1678,7 +1692,6 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     s->mma_xchg.release();
     s->tc_h0.release();
     s->h0_work.release();
-    s->tc_err.release();
     s->tc_x.release();
     s->small_x.release();
     if (s->side.stream) cudaStreamDestroy(s->side.stream);
@@ -1845,12 +1858,17 @@ lwm_status lwm_plan(lwm_planner* p, lwm_scorer* sc, const float* injected, lwm_p
         if (out->scores) LWM_CUDA(cudaMemcpyAsync(h + off_sc, d.scores, nsc * 4, cudaMemcpyDeviceToHost, stream));
         if (out->best_indices) LWM_CUDA(cudaMemcpyAsync(h + off_best, d.best_indices, B * 4, cudaMemcpyDeviceToHost, stream));
     }
+    // the error word: the SkyJEPA tensor-core rollouts write theirs into the
+    // result block (in the copy above when it is one copy); the LeWM GEMMs
+    // keep theirs with the model
     int tc_err[4] = {0, 0, 0, 0};
-    int* err_dev = sc->tc_err.ptr ? sc->tc_err.as<int>()
-                   : (sc->kind == ScorerKind::Lewm ? sc->lewm->split.tc_err : nullptr);
-    if (err_dev) LWM_CUDA(cudaMemcpyAsync(tc_err, err_dev, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
+    int* err_dev = sc->kind == ScorerKind::Lewm ? sc->lewm->split.tc_err : result_err(p, static_cast<uint32_t>(B));
+    const bool err_in_copy = one_copy && sc->kind != ScorerKind::Lewm;
+    if (err_dev && !err_in_copy)
+        LWM_CUDA(cudaMemcpyAsync(tc_err, err_dev, sizeof tc_err, cudaMemcpyDeviceToHost, stream));
     LWM_CUDA(cudaStreamSynchronize(stream));
-    if (tc_err[0] && sc->kind == ScorerKind::Lewm) LWM_CUDA(cudaMemset(err_dev, 0, sizeof tc_err));
+    if (err_in_copy) std::memcpy(tc_err, h + rl.err, sizeof tc_err);
+    if (tc_err[0]) LWM_CUDA(cudaMemset(err_dev, 0, sizeof tc_err));
     if (tc_err[0] && p->counters.ptr) {
         // the blocks that gave up never arrived: clear the per-vehicle
         // arrival counters so the planner's next plan starts clean
