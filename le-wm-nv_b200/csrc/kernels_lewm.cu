@@ -848,6 +848,56 @@ cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32
                       causal, scale_q_first);
 }
 
+// The ActionEmbedder's first two layers for every (sample, time) token in
+// one launch (modules.rs:150-158: patch_embed, a kernel-1 Conv1d over the
+// action dim, then embed.0 with SiLU): y = silu(W1 (Wc a + bc) + b1).  Their
+// K (the action dim, the smoothed dim) is too small for the tensor-core GEMM
+// and the work is a few MFLOP, so two GEMM launches were all latency.  A
+// block takes 4 tokens: the smoothed vectors go to shared memory, then each
+// thread computes output columns tid, tid + 256, ... of the 4 tokens (sums in
+// k order from 0, bias after, as the GEMM kernels do).
+constexpr uint32_t kAeTok = 4, kAeMaxA = 8, kAeMaxSm = 64;
+__global__ void __launch_bounds__(256) action_embed_kernel(const float* cand, uint32_t A, const float* wc,
+                                                           const float* bc, uint32_t sm, const float* w1,
+                                                           const float* b1, uint32_t ah, float* out, uint32_t rows) {
+    __shared__ float s_sm[kAeTok][kAeMaxSm];
+    const uint32_t r0 = blockIdx.x * kAeTok;
+    {
+        const uint32_t t = threadIdx.x / kAeMaxSm, k = threadIdx.x % kAeMaxSm;
+        if (t < kAeTok && k < sm && r0 + t < rows) {
+            const float* a = cand + static_cast<size_t>(r0 + t) * A;
+            float acc = 0.0f;
+            for (uint32_t i = 0; i < A; ++i) acc = fmaf(a[i], wc[static_cast<size_t>(k) * A + i], acc);
+            s_sm[t][k] = bc ? acc + bc[k] : acc;
+        }
+    }
+    __syncthreads();
+    for (uint32_t j = threadIdx.x; j < ah; j += blockDim.x) {
+        const float* wr = w1 + static_cast<size_t>(j) * sm;
+        float acc[kAeTok] = {};
+        for (uint32_t k = 0; k < sm; ++k) {
+            const float wv = __ldg(wr + k);
+#pragma unroll
+            for (uint32_t t = 0; t < kAeTok; ++t) acc[t] = fmaf(s_sm[t][k], wv, acc[t]);
+        }
+        const float bias = b1 ? __ldg(b1 + j) : 0.0f;
+#pragma unroll
+        for (uint32_t t = 0; t < kAeTok; ++t)
+            if (r0 + t < rows) out[static_cast<size_t>(r0 + t) * ah + j] = apply_act(kActSilu, b1 ? acc[t] + bias : acc[t]);
+    }
+}
+
+bool action_embed_supported(uint32_t A, uint32_t sm) { return A >= 1 && A <= kAeMaxA && sm >= 1 && sm <= kAeMaxSm; }
+
+cudaError_t launch_action_embed(const float* cand, uint32_t A, const float* wc, const float* bc, uint32_t sm,
+                                const float* w1, const float* b1, uint32_t ah, float* out, uint32_t rows,
+                                cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    if (!action_embed_supported(A, sm)) return cudaErrorInvalidValue;
+    action_embed_kernel<<<(rows + kAeTok - 1) / kAeTok, 256, 0, s>>>(cand, A, wc, bc, sm, w1, b1, ah, out, rows);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_goal_cost(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
                              float* scores, cudaStream_t s) {
     if (!rows) return cudaSuccess;

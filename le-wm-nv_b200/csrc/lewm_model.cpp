@@ -297,11 +297,19 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
     int n = 0;
     split_launches = 0;
     const uint32_t rows_all = static_cast<uint32_t>(all);
-    // ActionEmbedder over every (sample, time) token (modules.rs:150-158)
-    LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
-    LWM_CU(gemm_f32(sp, gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
+    // ActionEmbedder over every (sample, time) token (modules.rs:150-158): the
+    // small-K first two layers in one kernel, the last as a GEMM
+    if (action_embed_supported(A, sm) && w.act_conv.in == A && w.act_fc1.in == sm) {
+        LWM_CU(launch_action_embed(cand, A, w.act_conv.w, w.act_conv.b, sm, w.act_fc1.w, w.act_fc1.b, ah, f_ah,
+                                   rows_all, s));
+        n += 1;
+    } else {
+        LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
+        LWM_CU(gemm_f32(sp, gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
+        n += 2;
+    }
     LWM_CU(gemm_f32(sp, gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
-    n += 3;
+    n += 1;
     // cond -> SiLU -> AdaLN table of every layer (ConditionalBlock::forward, modules.rs:317-320);
     // the condition of a token depends only on its action, so the table is
     // built once per scoring call for all (sample, time) tokens.

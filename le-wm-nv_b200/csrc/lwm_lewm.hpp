@@ -76,6 +76,12 @@ cudaError_t launch_frames_put(const float* src, float* frames, uint32_t nframes,
                               uint32_t d, cudaStream_t s);
 cudaError_t launch_attention(const float* qkv, float* out, uint32_t seqs, uint32_t t, uint32_t H, uint32_t dh,
                              float scale, int causal, int scale_q_first, cudaStream_t s);
+// silu(W1 (Wc a + bc) + b1) for every row of `cand` [rows, A] (the action
+// embedder's first two layers); A <= 8, sm <= 64 (action_embed_supported).
+bool action_embed_supported(uint32_t A, uint32_t sm);
+cudaError_t launch_action_embed(const float* cand, uint32_t A, const float* wc, const float* bc, uint32_t sm,
+                                const float* w1, const float* b1, uint32_t ah, float* out, uint32_t rows,
+                                cudaStream_t s);
 cudaError_t launch_goal_cost(const float* pred, const float* goal, uint32_t S, size_t rows, uint32_t d,
                              float* scores, cudaStream_t s);
 cudaError_t launch_patchify(const float* pix, float* patches, uint32_t n, uint32_t C, uint32_t img, uint32_t p,
