@@ -728,17 +728,18 @@ def run_lewm(args, rank, world, local_rank):
     ctx.synchronize()
 
     def encode_and_plan(upload: bool):
-        with torch.cuda.stream(stream):
-            if image:
-                if upload:
+        if image:
+            if upload:
+                with torch.cuda.stream(stream):
                     dev_y.copy_(host_y, non_blocking=True)
                     dev_uv.copy_(host_uv, non_blocking=True)
-                # NV12 preprocessing written straight into the ViT's patch matrix
-                emb = sc.encode_nv12(dev_y, dev_uv, 2, s_img, s_img, "bt601-video", prep)
-            else:
-                if upload:
-                    dev_obs.copy_(host_obs, non_blocking=True)
-                emb = sc.encode_vector(dev_obs)
+            # one control step: NV12 preprocessing straight into the ViT's patch
+            # matrix, the encoder beside sampling and the AdaLN tables, then the plan
+            return planner.plan_nv12_device(sc, dev_y, dev_uv, w.batch, 1, s_img, s_img, "bt601-video", prep)
+        with torch.cuda.stream(stream):
+            if upload:
+                dev_obs.copy_(host_obs, non_blocking=True)
+            emb = sc.encode_vector(dev_obs)
             sc.set_context_device(emb[:1, None, :].contiguous(), emb[1:].contiguous())
         return planner.plan_device(sc)
 

@@ -714,6 +714,22 @@ lwm_status lwm_lewm_encode_nv12_device(lwm_scorer* scorer, const uint8_t* y_plan
 lwm_status lwm_lewm_encode_packed_device(lwm_scorer* scorer, const uint8_t* input, uint32_t n, uint32_t height,
                                          uint32_t width, int32_t format, const lwm_image_preprocess* cfg,
                                          float* out);
+/* One control step of LeWmSession (src/session.rs:31-40 reset_pixels and
+ * encode_pixels, :46-65 score_candidates) under a planner (plan_device,
+ * src/planner.rs:450): device NV12 frames -> embeddings -> scorer context ->
+ * plan.  Frames [0, batch*history) are the observation history (batch-major,
+ * `history` frames a row; the rollout window is `history`), frames
+ * [batch*history, batch*(history+1)) the goals.  Results equal
+ * lwm_lewm_encode_nv12_device + lwm_scorer_lewm_set_context_device (window
+ * = history) + lwm_plan_device.  The encoder runs on a high-priority stream of
+ * the scorer, beside the planner's sampling and the candidate-only part of
+ * scoring (action embedding, AdaLN tables) on the context stream; the rollout
+ * waits for it, and the context stream is ordered after it on return.
+ * Asynchronous like lwm_plan_device; whole planners only (no shards). */
+lwm_status lwm_lewm_plan_nv12_device(lwm_planner* planner, lwm_scorer* scorer, const uint8_t* y_plane,
+                                     const uint8_t* uv_plane, uint32_t batch, uint32_t history, uint32_t height,
+                                     uint32_t width, int32_t color_space, const lwm_image_preprocess* cfg,
+                                     const float* injected_noise, lwm_plan_device_result* out);
 
 /* ---------------------------------------------------------------- allocation-free iteration */
 

@@ -199,6 +199,7 @@ struct lwm_scorer {
     bool sky_small = false;  // latent <= 64: the warp-per-candidate path (h0 in tc_h0, inputs in small_x)
     DevBuf small_x;
     lwm::SideStream side;    // the history encoding runs here, beside sampling and the inputs
+    lwm::SideStream enc_side;  // LeWM: the frame encoder of lwm_lewm_plan_nv12_device (high priority)
     std::vector<float> action_tcn_host;  // the action encoder's weights, for kernel-parameter packing
     bool tc_ready = false;
     DevBuf mma_packed;       // split-fp16 weights of the f32 tensor-core path (per CTA rank)
@@ -1573,17 +1574,7 @@ static lwm_status lewm_set_context(lwm_scorer* s, uint32_t B, uint32_t h, uint32
     LWM_CUDA(cudaSetDevice(s->ctx->device));
     const size_t D = m.c.embed_dim;
     const size_t need = static_cast<size_t>(B) * h * D;
-    if (need > m.ctx_cap || static_cast<size_t>(B) * D > m.ctx_cap) {
-        LWM_CUDA(cudaStreamSynchronize(s->ctx->stream));
-        if (m.emb) cudaFree(m.emb);
-        if (m.goal) cudaFree(m.goal);
-        m.emb = m.goal = nullptr;
-        m.ctx_cap = 0;
-        const size_t cap = std::max(need, static_cast<size_t>(B) * D);
-        LWM_CUDA(cudaMalloc(&m.emb, cap * sizeof(float)));
-        LWM_CUDA(cudaMalloc(&m.goal, cap * sizeof(float)));
-        m.ctx_cap = cap;
-    }
+    LWM_CUDA(m.ensure_context(B, h, false, s->ctx->stream));
     LWM_CUDA(cudaMemcpyAsync(m.emb, emb, need * sizeof(float), kind, s->ctx->stream));
     LWM_CUDA(cudaMemcpyAsync(m.goal, goal, static_cast<size_t>(B) * D * sizeof(float), kind, s->ctx->stream));
     if (kind == cudaMemcpyHostToDevice) LWM_CUDA(cudaStreamSynchronize(s->ctx->stream));  // host arrays may go away
@@ -1697,6 +1688,9 @@ lwm_status lwm_scorer_destroy(lwm_scorer* s) {
     if (s->side.stream) cudaStreamDestroy(s->side.stream);
     if (s->side.fork) cudaEventDestroy(s->side.fork);
     if (s->side.join) cudaEventDestroy(s->side.join);
+    if (s->enc_side.stream) cudaStreamDestroy(s->enc_side.stream);
+    if (s->enc_side.fork) cudaEventDestroy(s->enc_side.fork);
+    if (s->enc_side.join) cudaEventDestroy(s->enc_side.join);
     s->ctx_dev.release();
     s->ctx_host.release();
     delete s;
@@ -2010,7 +2004,8 @@ lwm_status preprocess_packed(lwm_ctx* ctx, const uint8_t* input, uint32_t B, uin
 
 lwm_status preprocess_nv12(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* uv_plane, uint32_t B, uint32_t H,
                            uint32_t W, int32_t color_space, const lwm_image_preprocess* cfg, uint32_t history_len,
-                           uint32_t slot, uint32_t patch, int32_t out_bf16, void* output) {
+                           uint32_t slot, uint32_t patch, int32_t out_bf16, void* output,
+                           cudaStream_t stream = nullptr) {
     if (!cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
     if (color_space < 0 || color_space > 3)
         return fail(LWM_INVALID_ARGUMENT, "unknown NV12 color space " + std::to_string(color_space) +
@@ -2032,9 +2027,9 @@ lwm_status preprocess_nv12(lwm_ctx* ctx, const uint8_t* y_plane, const uint8_t* 
     a.test_wait_polls = ctx->faults.wait_polls;
     if (lwm::nv12_staged_eligible(a)) {
         LWM_TRY(ensure_media_err(ctx));
-        LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, ctx->stream));
+        LWM_CUDA(lwm::launch_nv12_staged(a, ctx->media_err_dev, stream ? stream : ctx->stream));
     } else {
-        LWM_CUDA(lwm::launch_media(a, true, ctx->stream));
+        LWM_CUDA(lwm::launch_media(a, true, stream ? stream : ctx->stream));
     }
     ctx->launches += 1;
     return LWM_OK;
@@ -2050,9 +2045,7 @@ lwm_status check_patch(const lwm_image_preprocess* cfg, uint32_t patch) {
 }
 
 // The image encoder's patch size and frame size must be the output's.
-lwm_status check_vit_frames(lwm_scorer* s, const lwm_image_preprocess* cfg, uint32_t n, float* out) {
-    if (!s || s->kind != ScorerKind::Lewm || !cfg || !out || n == 0)
-        return fail(LWM_INVALID_ARGUMENT, "invalid encode arguments");
+lwm_status check_vit_encoder(lwm_scorer* s, const lwm_image_preprocess* cfg) {
     const lwm_lewm_config& c = s->lewm->c;
     if (c.encoder != LWM_ENCODER_VIT) return fail(LWM_INVALID_ARGUMENT, "encode_pixels called on non-image observation encoder");
     if (c.channels != 3) return fail(LWM_INVALID_ARGUMENT, "frame encoding needs a 3-channel image encoder");
@@ -2061,6 +2054,12 @@ lwm_status check_vit_frames(lwm_scorer* s, const lwm_image_preprocess* cfg, uint
                                               std::to_string(cfg->output_width) + " does not match the encoder's image size " +
                                               std::to_string(c.image_size));
     return LWM_OK;
+}
+
+lwm_status check_vit_frames(lwm_scorer* s, const lwm_image_preprocess* cfg, uint32_t n, float* out) {
+    if (!s || s->kind != ScorerKind::Lewm || !cfg || !out || n == 0)
+        return fail(LWM_INVALID_ARGUMENT, "invalid encode arguments");
+    return check_vit_encoder(s, cfg);
 }
 
 }  // namespace
@@ -2120,6 +2119,70 @@ lwm_status lwm_lewm_encode_packed_device(lwm_scorer* s, const uint8_t* input, ui
     LWM_CUDA(s->lewm->encode_patches(n, out, s->ctx->stream));
     s->ctx->launches += static_cast<uint64_t>(s->lewm->launches);
     return LWM_OK;
+}
+
+// LeWmSession::reset_pixels + encode_pixels of the goal + plan
+// (src/session.rs:31-40, 46-65; planner.rs:450): the frames' encoder runs on
+// the scorer's high-priority encoder stream, beside the planner's sampling and
+// the candidate-only part of scoring on the context stream; the rollout waits
+// for it.  The context stream is ordered after the encoder on every return.
+lwm_status lwm_lewm_plan_nv12_device(lwm_planner* p, lwm_scorer* s, const uint8_t* y_plane, const uint8_t* uv_plane,
+                                     uint32_t B, uint32_t h, uint32_t H, uint32_t W, int32_t color_space,
+                                     const lwm_image_preprocess* cfg, const float* injected,
+                                     lwm_plan_device_result* out) {
+    if (!p || !s || !out || !y_plane || !uv_plane || !cfg) return fail(LWM_INVALID_ARGUMENT, "null argument");
+    if (s->kind != ScorerKind::Lewm) return fail(LWM_INVALID_ARGUMENT, "not a LeWM scorer");
+    if (s->ctx != p->ctx) return fail(LWM_INVALID_ARGUMENT, "planner and scorer belong to different contexts");
+    if (p->shard_total) return fail(LWM_INVALID_ARGUMENT, "planner is a candidate shard: encode, set the context and plan");
+    if (B == 0 || h == 0) return fail(LWM_INVALID_ARGUMENT, "invalid LeWM context shapes");
+    lwm::LewmModel& m = *s->lewm;
+    if (h > m.c.num_frames)
+        return fail(LWM_INVALID_ARGUMENT, "rollout window " + std::to_string(h) + " exceeds predictor.num_frames " +
+                                              std::to_string(m.c.num_frames));
+    const uint64_t frames = static_cast<uint64_t>(B) * (static_cast<uint64_t>(h) + 1);
+    if (frames > 65536) return fail(LWM_INVALID_ARGUMENT, "too many frames: " + std::to_string(frames));
+    const uint32_t n = static_cast<uint32_t>(frames);
+    LWM_TRY(check_vit_encoder(s, cfg));
+    std::lock_guard<std::mutex> lock(p->mu);
+    std::lock_guard<std::mutex> lock2(s->mu);
+    LWM_CUDA(cudaSetDevice(p->ctx->device));
+    cudaStream_t stream = p->ctx->stream;
+    lwm::SideStream& side = s->enc_side;
+    if (!side.stream) {
+        int least = 0, greatest = 0;
+        LWM_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        LWM_CUDA(cudaStreamCreateWithPriority(&side.stream, cudaStreamNonBlocking, greatest));
+        LWM_CUDA(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming));
+        LWM_CUDA(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming));
+    }
+    // observation frames [B, h] then the B goals: one encoder output fills emb and goal
+    LWM_CUDA(m.ensure_context(B, h, true, stream));
+    float* patches = nullptr;
+    LWM_CUDA(m.patch_buffer(n, &patches));
+    // the frames and the context buffers were last touched in stream order
+    LWM_CUDA(cudaEventRecord(side.fork, stream));
+    LWM_CUDA(cudaStreamWaitEvent(side.stream, side.fork, 0));
+    struct Join {  // on every return: the context stream waits for the encoder stream
+        lwm::LewmModel& m;
+        lwm::SideStream& side;
+        cudaStream_t stream;
+        ~Join() {
+            m.join_ev = nullptr;
+            if (cudaEventRecord(side.join, side.stream) == cudaSuccess) cudaStreamWaitEvent(stream, side.join, 0);
+        }
+    } join{m, side, stream};
+    LWM_TRY(preprocess_nv12(s->ctx, y_plane, uv_plane, n, H, W, color_space, cfg, 0, 0, m.c.patch_size, 0, patches,
+                            side.stream));
+    LWM_CUDA(m.encode_patches(n, m.emb, side.stream));
+    s->ctx->launches += static_cast<uint64_t>(m.launches);
+    LWM_CUDA(cudaEventRecord(side.join, side.stream));
+    m.B = B;
+    m.h = h;
+    m.history = h;
+    s->batch = B;
+    s->has_context = true;
+    m.join_ev = side.join;
+    return plan_device_locked(p, s, injected, out);
 }
 
 lwm_status lwm_normal_device(lwm_ctx* ctx, uint64_t seed, uint64_t offset, size_t count, float* out) {

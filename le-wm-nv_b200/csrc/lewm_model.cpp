@@ -215,17 +215,20 @@ void Arena::release() {
 LewmModel::~LewmModel() {
     g_score.reset();
     g_enc.reset();
+    g_score_cand.reset();
+    g_score_roll.reset();
     if (blob_bf16) cudaFree(blob_bf16);
     if (vit_qkv) cudaFree(vit_qkv);
     if (pred_w) cudaFree(pred_w);
     if (split.tc_err) cudaFree(split.tc_err);
     if (split.partial) cudaFree(split.partial);
     if (split.counters) cudaFree(split.counters);
+    if (split_cand.partial) cudaFree(split_cand.partial);
+    if (split_cand.counters) cudaFree(split_cand.counters);
     ws.release();
     enc.release();
     if (blob) cudaFree(blob);
-    if (emb) cudaFree(emb);
-    if (goal) cudaFree(goal);
+    if (emb) cudaFree(emb);  // goal lives in the same allocation
 }
 
 namespace {
@@ -268,8 +271,8 @@ cudaError_t mlp(const SplitScratch* sp, const MlpW& m, const float* x, uint32_t 
 }  // namespace
 
 cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb,
-                                  cudaStream_t s) {
-    const SplitScratch* sp = &split;
+                                  cudaStream_t s, int part) {
+    const SplitScratch* sp = part == 1 ? &split_cand : &split;
     const uint32_t D = c.embed_dim, hid = c.pred_hidden_dim, inner = c.heads * c.dim_head, A = c.action_dim;
     const uint32_t sm = c.smoothed_dim, ah = c.action_mlp_scale * D, ph = c.pred_proj_hidden;
     const size_t bs = static_cast<size_t>(B) * S, all = bs * T;
@@ -297,34 +300,40 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
     int n = 0;
     split_launches = 0;
     const uint32_t rows_all = static_cast<uint32_t>(all);
-    // ActionEmbedder over every (sample, time) token (modules.rs:150-158): the
-    // small-K first two layers in one kernel, the last as a GEMM
-    if (action_embed_supported(A, sm) && w.act_conv.in == A && w.act_fc1.in == sm) {
-        LWM_CU(launch_action_embed(cand, A, w.act_conv.w, w.act_conv.b, sm, w.act_fc1.w, w.act_fc1.b, ah, f_ah,
-                                   rows_all, s));
+    if (part != 2) {
+        // ActionEmbedder over every (sample, time) token (modules.rs:150-158): the
+        // small-K first two layers in one kernel, the last as a GEMM
+        if (action_embed_supported(A, sm) && w.act_conv.in == A && w.act_fc1.in == sm) {
+            LWM_CU(launch_action_embed(cand, A, w.act_conv.w, w.act_conv.b, sm, w.act_fc1.w, w.act_fc1.b, ah, f_ah,
+                                       rows_all, s));
+            n += 1;
+        } else {
+            LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
+            LWM_CU(gemm_f32(sp, gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
+            n += 2;
+        }
+        LWM_CU(gemm_f32(sp, gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
         n += 1;
-    } else {
-        LWM_CU(gemm_f32(sp, gemm(cand, A, w.act_conv, f_sm, sm, rows_all), s));
-        LWM_CU(gemm_f32(sp, gemm(f_sm, sm, w.act_fc1, f_ah, ah, rows_all, kActSilu), s));
-        n += 2;
-    }
-    LWM_CU(gemm_f32(sp, gemm(f_ah, ah, w.act_fc2, f_act, D, rows_all), s));
-    n += 1;
-    // cond -> SiLU -> AdaLN table of every layer (ConditionalBlock::forward, modules.rs:317-320);
-    // the condition of a token depends only on its action, so the table is
-    // built once per scoring call for all (sample, time) tokens.
-    const float* cond = f_act;
-    if (w.has_proj) {
-        LWM_CU(gemm_f32(sp, gemm(f_act, D, w.cond_proj, f_cond, hid, rows_all), s));
+        // cond -> SiLU -> AdaLN table of every layer (ConditionalBlock::forward, modules.rs:317-320);
+        // the condition of a token depends only on its action, so the table is
+        // built once per scoring call for all (sample, time) tokens.
+        const float* cond = f_act;
+        if (w.has_proj) {
+            LWM_CU(gemm_f32(sp, gemm(f_act, D, w.cond_proj, f_cond, hid, rows_all), s));
+            ++n;
+            cond = f_cond;
+        }
+        LWM_CU(launch_silu(cond, f_cond, all * hid, s));
         ++n;
-        cond = f_cond;
-    }
-    LWM_CU(launch_silu(cond, f_cond, all * hid, s));
-    ++n;
-    for (uint32_t l = 0; l < c.depth; ++l) {
-        LWM_CU(gemm_f32(sp, gemm(f_cond, hid, w.blocks[l].ada, f_ada + static_cast<size_t>(l) * all * 6 * hid, 6 * hid,
-                             rows_all), s));
-        ++n;
+        for (uint32_t l = 0; l < c.depth; ++l) {
+            float* table = f_ada + static_cast<size_t>(l) * all * 6 * hid;
+            LWM_CU(gemm_f32(sp, gemm(f_cond, hid, w.blocks[l].ada, table, 6 * hid, rows_all), s));
+            ++n;
+        }
+        if (part == 1) {
+            launches = n + split_launches;
+            return cudaSuccess;
+        }
     }
     if (fused) {
         // the whole rollout in one launch
@@ -569,16 +578,30 @@ cudaError_t LewmModel::fuse_vit_qkv() {
     return cudaSuccess;
 }
 
-cudaError_t LewmModel::ensure_split() {
-    // 4 M floats of partial tiles (16 splits of 64 tiles) and 64 K tile counters
-    if (split.partial) return cudaSuccess;
+namespace {
+
+// 4 M floats of partial tiles (16 splits of 64 tiles) and 64 K tile counters
+cudaError_t alloc_split(SplitScratch& sp, int* extra_launches) {
+    if (sp.partial) return cudaSuccess;
     constexpr size_t kPartial = static_cast<size_t>(4) << 20, kCounters = 65536;
-    LWM_CU(cudaMalloc(&split.partial, kPartial * sizeof(float)));
-    LWM_CU(cudaMalloc(&split.counters, kCounters * sizeof(unsigned int)));
-    LWM_CU(cudaMemset(split.counters, 0, kCounters * sizeof(unsigned int)));
-    split.floats = kPartial;
-    split.n_counters = kCounters;
-    split.extra_launches = &split_launches;
+    LWM_CU(cudaMalloc(&sp.partial, kPartial * sizeof(float)));
+    LWM_CU(cudaMalloc(&sp.counters, kCounters * sizeof(unsigned int)));
+    LWM_CU(cudaMemset(sp.counters, 0, kCounters * sizeof(unsigned int)));
+    sp.floats = kPartial;
+    sp.n_counters = kCounters;
+    sp.extra_launches = extra_launches;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t LewmModel::ensure_split() { return alloc_split(split, &split_launches); }
+
+// Same sizes as `split`, the same tensor-core error word: the candidate-only
+// part of scoring sums its split-K partials in the same order as on `split`.
+cudaError_t LewmModel::ensure_split_cand() {
+    LWM_CU(alloc_split(split_cand, &split_launches));
+    split_cand.tc_err = split.tc_err;
     return cudaSuccess;
 }
 
@@ -748,7 +771,38 @@ cudaError_t LewmModel::score(const float* cand, uint32_t S, uint32_t T, float* s
     LWM_CU(ensure_split());
     const uint64_t key[GraphCache::kKey] = {u(cand), u(scores), u(last_emb), S, T, B, u(emb), u(goal), h, history,
                                             u(ws.ptr), ws.floats, u(s), 1};
-    return run_graphed(g_score, key, s, launches, [&] { return score_body(cand, S, T, scores, last_emb, s); });
+    if (!join_ev)
+        return run_graphed(g_score, key, s, launches, [&] { return score_body(cand, S, T, scores, last_emb, s); });
+    // the encoder that writes emb / goal runs on another stream until join_ev
+    LWM_CU(ensure_split_cand());
+    uint64_t key1[GraphCache::kKey], key2[GraphCache::kKey];
+    std::memcpy(key1, key, sizeof key);
+    std::memcpy(key2, key, sizeof key);
+    key1[GraphCache::kKey - 1] = 4;
+    key2[GraphCache::kKey - 1] = 5;
+    LWM_CU(run_graphed(g_score_cand, key1, s, launches,
+                       [&] { return score_body(cand, S, T, scores, last_emb, s, 1); }));
+    const int n1 = launches;
+    LWM_CU(cudaStreamWaitEvent(s, join_ev, 0));
+    LWM_CU(run_graphed(g_score_roll, key2, s, launches,
+                       [&] { return score_body(cand, S, T, scores, last_emb, s, 2); }));
+    launches += n1;
+    return cudaSuccess;
+}
+
+cudaError_t LewmModel::ensure_context(uint32_t B_, uint32_t h_, bool packed, cudaStream_t s) {
+    const size_t D = c.embed_dim;
+    const size_t need = static_cast<size_t>(B_) * h_ * D, need_goal = static_cast<size_t>(B_) * D;
+    const size_t cap = std::max(need, need_goal);
+    if (emb && (packed ? ctx_cap == need && need >= need_goal : ctx_cap >= cap)) return cudaSuccess;
+    LWM_CU(cudaStreamSynchronize(s));
+    if (emb) cudaFree(emb);
+    emb = goal = nullptr;
+    ctx_cap = 0;
+    LWM_CU(cudaMalloc(&emb, 2 * cap * sizeof(float)));
+    goal = emb + cap;
+    ctx_cap = cap;
+    return cudaSuccess;
 }
 
 cudaError_t LewmModel::encode_pixels(const float* pix, uint32_t n, float* out, cudaStream_t s) {

@@ -223,21 +223,33 @@ struct LewmModel {
     bool pred_ready = false;
     // per-plan context
     uint32_t B = 0, h = 0, history = 0;
-    float* emb = nullptr;   // [B, h, D]
-    float* goal = nullptr;  // [B, D]
+    float* emb = nullptr;   // [B, h, D], at the start of one allocation
+    float* goal = nullptr;  // [B, D], ctx_cap floats after emb (same allocation)
     size_t ctx_cap = 0;
+    // Set while an observation encoding that writes emb / goal runs on
+    // another stream: scoring then builds the candidate-only part (action
+    // embedding, AdaLN tables) first, waits for this event, then rolls out.
+    cudaEvent_t join_ev = nullptr;
     Arena ws;               // rollout workspace
     Arena enc;              // encoder workspace
     SplitScratch split;     // split-K partial tiles
-    GraphCache g_score, g_enc;
+    SplitScratch split_cand;  // the candidate-only part's own, while an encoder uses `split`
+    GraphCache g_score, g_enc, g_score_cand, g_score_roll;
     int launches = 0;
     int split_launches = 0;  // split-K reduce kernels of the current launch sequence
     ~LewmModel();
-    cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s);
+    // part 0: all of scoring; 1: the candidate-only part (on split_cand, so
+    // it may run beside an encoder that uses `split`); 2: the rest
+    cudaError_t score_body(const float* cand, uint32_t S, uint32_t T, float* scores, float* last_emb, cudaStream_t s,
+                           int part = 0);
+    // emb and goal for [B, h] observation embeddings and B goals; `packed`:
+    // goal directly behind emb's B h D floats (one encoder output fills both)
+    cudaError_t ensure_context(uint32_t B, uint32_t h, bool packed, cudaStream_t s);
     cudaError_t encode_pixels_body(const float* pixels, uint32_t n, float* out, cudaStream_t s);
     cudaError_t encode_patches_body(uint32_t n, float* out, cudaStream_t s);
     size_t encoder_layout(uint32_t n, EncoderOffsets* o) const;
     cudaError_t ensure_split();
+    cudaError_t ensure_split_cand();
     cudaError_t fuse_vit_qkv();
     // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
     // GEMM inputs on the tensor cores, f32 accumulation and activations.

@@ -398,6 +398,8 @@ _sig("lwm_preprocess_packed_patches_device", C.c_int, VP, VP, U32, U32, U32, I32
 _sig("lwm_preprocess_nv12_patches_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), U32,
      I32, VP)
 _sig("lwm_lewm_encode_nv12_device", C.c_int, VP, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), VP)
+_sig("lwm_lewm_plan_nv12_device", C.c_int, VP, VP, VP, VP, U32, U32, U32, U32, I32, C.POINTER(ImagePreprocess), VP,
+     C.POINTER(_PlanDeviceResult))
 _sig("lwm_lewm_encode_packed_device", C.c_int, VP, VP, U32, U32, U32, I32, C.POINTER(ImagePreprocess), VP)
 
 
@@ -927,6 +929,24 @@ class _Planner:
         r = _PlanDeviceResult()
         _check(lib.lwm_plan_device(self.handle, scorer.handle, VP(injected_noise_ptr) if injected_noise_ptr else None,
                                    C.byref(r)))
+        return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
+                                r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
+                                _OUTCOME[r.deadline_outcome])
+
+    def plan_nv12_device(self, scorer: "LewmScorer", y_plane, uv_plane, batch: int, history: int, height: int,
+                         width: int, color_space, cfg: "ImagePreprocess",
+                         injected_noise_ptr: Optional[int] = None) -> PlanDeviceResult:
+        """One LeWmSession control step (src/session.rs:31-65) on device NV12
+        frames: frames [0, batch*history) are the observation history,
+        [batch*history, batch*(history+1)) the goals.  Equal to encode_nv12 +
+        set_context_device + plan_device, with the frames' encoder running
+        beside sampling and the candidate-only part of scoring."""
+        cs = NV12_COLOR_SPACES[color_space] if isinstance(color_space, str) else int(color_space)
+        r = _PlanDeviceResult()
+        _check(lib.lwm_lewm_plan_nv12_device(self.handle, scorer.handle, VP(_ptr(y_plane)), VP(_ptr(uv_plane)), batch,
+                                             history, height, width, cs, C.byref(cfg),
+                                             VP(injected_noise_ptr) if injected_noise_ptr else None, C.byref(r)))
+        scorer.batch = batch
         return PlanDeviceResult(r.first_action or 0, r.sequence or 0, r.scores or 0, r.best_indices or 0, r.batch,
                                 r.scores_cols, r.iterations_completed, r.elapsed_ns * 1e-9, bool(r.deadline_reached),
                                 _OUTCOME[r.deadline_outcome])
