@@ -564,7 +564,7 @@ __global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, f
 }
 
 // The same attention for 64-wide heads, register-tiled: a block per
-// (sequence, head, 8 QW queries), K (rows padded to 68 floats: 16-byte rows
+// (sequence, head, 8 QW queries), K (staged by cp.async; rows padded to 68 floats: 16-byte rows
 // that eight lanes read from eight different bank quads), V and the block's
 // queries in shared memory.  Warp w scores its QW (4, or 2 when the grid is
 // small) queries against keys lane + 32 u (u < 8), QW x 8 accumulators a
@@ -573,6 +573,15 @@ __global__ void __launch_bounds__(256) attention_smem_kernel(const float* qkv, f
 // lane + 32 of the QW queries over the keys.  Every dot product, the softmax and the weighted sums run in the
 // same order as attention_smem_kernel's, so the outputs are identical.
 constexpr uint32_t kAtQ = 32, kAtDh = 64, kAtKld = 68;
+
+// 16 bytes global -> shared without a register round trip (zero-filled when
+// `bytes` is 0); all of a thread's copies are in flight until the wait.
+__device__ __forceinline__ void at_copy16(float* dst, const float* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
 __host__ __device__ inline uint32_t at_tpad(uint32_t t) { return (t + 31u) & ~31u; }
 __host__ __device__ inline size_t at_smem_floats(uint32_t t) {
     const uint32_t tp = at_tpad(t);
@@ -594,16 +603,14 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
     float* Qs = Vs + tp * kAtDh;       // [32][68]
     float* Pt = Qs + kAtQ * kAtKld + warp * tp * 4u;  // this warp's [tp][4]
     const float* base = qkv + s * t * 3 * inner;
+    // K and V rows by asynchronous copies (every row in flight at once; the
+    // padding rows j >= t zero-filled)
     for (uint32_t idx = threadIdx.x; idx < tp * 16u; idx += blockDim.x) {
         const uint32_t j = idx >> 4, c = (idx & 15u) * 4u;
-        float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
-        if (j < t) {
-            const float* row = base + static_cast<size_t>(j) * 3 * inner + h * kAtDh + c;
-            k = *reinterpret_cast<const float4*>(row + inner);
-            v = *reinterpret_cast<const float4*>(row + 2 * inner);
-        }
-        *reinterpret_cast<float4*>(Ks + j * kAtKld + c) = k;
-        *reinterpret_cast<float4*>(Vs + j * kAtDh + c) = v;
+        const float* row = base + static_cast<size_t>(j < t ? j : 0u) * 3 * inner + h * kAtDh + c;
+        const uint32_t bytes = j < t ? 16u : 0u;
+        at_copy16(Ks + j * kAtKld + c, row + inner, bytes);
+        at_copy16(Vs + j * kAtDh + c, row + 2 * inner, bytes);
     }
     for (uint32_t idx = threadIdx.x; idx < 8u * QW * 16u; idx += blockDim.x) {
         const uint32_t qi = idx >> 4, c = (idx & 15u) * 4u, i = q0 + qi;
@@ -614,6 +621,7 @@ __global__ void __launch_bounds__(256) attention_tiled_kernel(const float* qkv, 
         }
         *reinterpret_cast<float4*>(Qs + qi * kAtKld + c) = q;
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     const uint32_t ql = warp * QW;  // the warp's first query, block-local
     if (q0 + ql >= t) return;
