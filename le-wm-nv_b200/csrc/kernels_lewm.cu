@@ -90,7 +90,27 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
         __syncthreads();
         buf ^= 1;
     }
-    if (g.splits <= 1) {
+    // epilogue_value's arithmetic on the thread's 4 x 4 outputs, with every
+    // bias / residual / gate operand loaded before the first store (loads
+    // after a store to C would each wait for it: C might alias them)
+    auto finish = [&](const float (&val)[4][4]) {
+        float bv[4], cv[4][4], gv[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t n = n0 + tx * 4 + j;
+            bv[j] = (g.bias && n < g.N) ? g.bias[n] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t m = m0 + ty * 4 + i;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t n = n0 + tx * 4 + j;
+                const bool in = g.residual && m < g.M && n < g.N;
+                cv[i][j] = in ? g.C[static_cast<size_t>(m) * g.ldc + n] : 0.0f;
+                gv[i][j] = (in && g.gate) ? g.gate[g.map.row(m) * g.ldg + n] : 0.0f;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint32_t m = m0 + ty * 4 + i;
@@ -99,10 +119,20 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
             for (int j = 0; j < 4; ++j) {
                 const uint32_t n = n0 + tx * 4 + j;
                 if (n >= g.N) continue;
-                float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
-                *c = epilogue_value(g, m, n, acc[i][j], c);
+                float v = val[i][j];
+                if (g.bias) v = v + bv[j];
+                if (g.residual) {
+                    if (g.gate) v = gv[i][j] * v;
+                    v = cv[i][j] + v;
+                } else {
+                    v = apply_act(g.act, v);
+                }
+                g.C[static_cast<size_t>(m) * g.ldc + n] = v;
             }
         }
+    };
+    if (g.splits <= 1) {
+        finish(acc);
         return;
     }
     // split-K: park this split's tile, the last split of the tile to arrive
@@ -121,21 +151,22 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
     if (!s_last) return;
     __threadfence();
     const float* parts = g.partial + tile * g.splits * (kBM * kBN);
+    float sum[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t m = m0 + ty * 4 + i;
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t n = n0 + tx * 4 + j;
-            float v = 0.0f;
-            for (uint32_t z = 0; z < g.splits; ++z)
-                v += __ldcg(parts + z * (kBM * kBN) + (ty * 4 + i) * kBN + tx * 4 + j);
-            if (m < g.M && n < g.N) {
-                float* c = g.C + static_cast<size_t>(m) * g.ldc + n;
-                *c = epilogue_value(g, m, n, v, c);
-            }
+        for (int j = 0; j < 4; ++j) sum[i][j] = 0.0f;
+    for (uint32_t z = 0; z < g.splits; ++z) {  // split order: sum += partial_z
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(parts + z * (kBM * kBN) + (ty * 4 + i) * kBN + tx * 4));
+            sum[i][0] += p.x;
+            sum[i][1] += p.y;
+            sum[i][2] += p.z;
+            sum[i][3] += p.w;
         }
     }
+    finish(sum);
     if (tid == 0) g.counters[tile] = 0u;
 }
 
