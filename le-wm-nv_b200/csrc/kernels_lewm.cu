@@ -243,7 +243,8 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
     if (r >= rows) return;
     const float* xr = x + static_cast<size_t>(r) * d;
     const float* a = ada + map.row(r) * ld_ada;
-    float v[NQ], sh[NQ], sc[NQ];
+    // the affine weights too, so that no load waits behind the stores at the end
+    float v[NQ], sh[NQ], sc[NQ], wv[NQ], bv[NQ];
     float s = 0.0f;
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
@@ -252,6 +253,8 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
         v[q] = in ? xr[i] : 0.0f;
         sh[q] = in ? a[shift_off + i] : 0.0f;
         sc[q] = in ? a[scale_off + i] : 0.0f;
+        wv[q] = in ? w[i] : 0.0f;
+        bv[q] = in ? b[i] : 0.0f;
         s += v[q];
     }
     float mean = warp_sum(s) / static_cast<float>(d);
@@ -283,7 +286,7 @@ __global__ void ada_ln_kernel(const float* x, float* y, uint32_t rows, uint32_t 
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
         const uint32_t i = lane + 32 * q;
-        if (i < d) yr[i] = (v[q] - mean) / den * w[i] + b[i];
+        if (i < d) yr[i] = (v[q] - mean) / den * wv[q] + bv[q];
     }
 }
 
