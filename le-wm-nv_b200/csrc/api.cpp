@@ -1555,6 +1555,7 @@ lwm_status lwm_scorer_lewm_create(lwm_ctx* ctx, const lwm_lewm_config* cfg, cons
     LWM_CUDA(cudaMemcpy(model->blob, weights, n * sizeof(float), cudaMemcpyHostToDevice));
     lwm::lewm_walk(*cfg, model->blob, &model->w);
     LWM_CUDA(model->fuse_vit_qkv());
+    LWM_CUDA(model->fold_v_out());
     lwm_scorer* s = new_scorer(ctx, ScorerKind::Lewm);
     s->lewm = std::move(model);
     *out = s;

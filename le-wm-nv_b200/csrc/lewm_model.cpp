@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "lwm_host.hpp"
 #include "lwm_pdl.hpp"
@@ -219,6 +220,7 @@ LewmModel::~LewmModel() {
     g_score_roll.reset();
     if (blob_bf16) cudaFree(blob_bf16);
     if (vit_qkv) cudaFree(vit_qkv);
+    if (vo_blob) cudaFree(vo_blob);
     if (pred_w) cudaFree(pred_w);
     if (split.tc_err) cudaFree(split.tc_err);
     if (split.partial) cudaFree(split.partial);
@@ -382,9 +384,20 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
             const BlockW& b = w.blocks[l];
             const float* ada = f_ada + static_cast<size_t>(l) * all * 6 * hid;
             LWM_CU(launch_ada_ln(x, f_y, rows, hid, ada, 6 * hid, 0, hid, map, b.attn_norm.w, b.attn_norm.b, s));
-            const float* att;
-            uint32_t ld_att;
-            if (wl == 1) {
+            const float* att = f_att;
+            uint32_t ld_att = inner;
+            const bool folded = wl == 1 && b.vo.w && !b.qkv.wb;
+            if (folded) {
+                // one-token window, f32 weights: V and the out-projection as
+                // the one folded map vo (x += g1 * (y Wvo^T + bvo))
+                GemmArgs gv = gemm(f_y, hid, b.vo, x, hid, rows);
+                gv.residual = 1;
+                gv.gate = ada + 2 * hid;
+                gv.ldg = 6 * hid;
+                gv.map = map;
+                LWM_CU(gemm_f32(sp, gv, s));
+                n += 2;
+            } else if (wl == 1) {
                 // softmax over a single key is exactly 1: the attention output is V
                 Lin v = b.qkv;
                 v.w = b.qkv.w + static_cast<size_t>(2) * inner * hid;
@@ -392,22 +405,21 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
                 v.out = inner;
                 LWM_CU(gemm_f32(sp, gemm(f_y, hid, v, f_att, inner, rows), s));
                 n += 2;
-                att = f_att;
-                ld_att = inner;
             } else {
                 LWM_CU(gemm_f32(sp, gemm(f_y, hid, b.qkv, f_qkv, 3 * inner, rows), s));
                 LWM_CU(launch_attention(f_qkv, f_att, static_cast<uint32_t>(bs), wl, c.heads, c.dim_head, scale, 1, 1,
                                         s));
                 n += 3;
-                att = f_att;
-                ld_att = inner;
             }
-            GemmArgs go = gemm(att, ld_att, b.to_out, x, hid, rows);
-            go.residual = 1;
-            go.gate = ada + 2 * hid;
-            go.ldg = 6 * hid;
-            go.map = map;
-            LWM_CU(gemm_f32(sp, go, s));
+            if (!folded) {
+                GemmArgs go = gemm(att, ld_att, b.to_out, x, hid, rows);
+                go.residual = 1;
+                go.gate = ada + 2 * hid;
+                go.ldg = 6 * hid;
+                go.map = map;
+                LWM_CU(gemm_f32(sp, go, s));
+                ++n;
+            }
             LWM_CU(launch_ada_ln(x, f_y, rows, hid, ada, 6 * hid, 3 * hid, 4 * hid, map, b.mlp_norm.w, b.mlp_norm.b,
                                  s));
             LWM_CU(gemm_f32(sp, gemm(f_y, hid, b.fc1, f_f, c.mlp_dim, rows, kActGeluTanh), s));
@@ -417,7 +429,7 @@ cudaError_t LewmModel::score_body(const float* cand, uint32_t S, uint32_t T, flo
             g2.ldg = 6 * hid;
             g2.map = map;
             LWM_CU(gemm_f32(sp, g2, s));
-            n += 4;
+            n += 3;
         }
         // last token -> norm -> output_proj -> pred_proj (Transformer::forward_last, modules.rs:369-380)
         LWM_CU(launch_layernorm(x, f_last, static_cast<uint32_t>(bs), hid, wl, wl - 1, w.final_norm.w, w.final_norm.b,
@@ -556,6 +568,52 @@ void GraphCache::reset() {
 // runs one GEMM into the [rows, 3 vit_hidden] buffer that the three filled
 // column range by column range (HfVitEncoder's SelfAttention: three Linears
 // of the same input).
+// One-token windows make the attention output V itself, so the attention
+// half-layer is two chained linear maps: y -> V = y Wv^T + bv -> V Wo^T + bo.
+// Their product, Wvo = Wo Wv and bvo = Wo bv + bo, is formed once here (in
+// double, rounded to f32) and replaces both GEMMs on the f32 path; results
+// differ from the two-GEMM order by f32 rounding only.
+cudaError_t LewmModel::fold_v_out() {
+    if (vo_blob || w.blocks.empty()) return cudaSuccess;
+    const size_t hid = c.pred_hidden_dim, inner = static_cast<size_t>(c.heads) * c.dim_head;
+    const size_t per = hid * hid + hid;
+    std::vector<float> wv(inner * hid), bv(inner), wo(hid * inner), bo(hid), out(per * w.blocks.size());
+    std::vector<double> acc(hid);
+    for (size_t l = 0; l < w.blocks.size(); ++l) {
+        const BlockW& b = w.blocks[l];
+        if (b.qkv.in != hid || b.qkv.out != 3 * inner || b.to_out.in != inner || b.to_out.out != hid) return cudaSuccess;
+        LWM_CU(cudaMemcpy(wv.data(), b.qkv.w + 2 * inner * hid, wv.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        LWM_CU(cudaMemcpy(wo.data(), b.to_out.w, wo.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        std::fill(bv.begin(), bv.end(), 0.0f);
+        std::fill(bo.begin(), bo.end(), 0.0f);
+        if (b.qkv.b) LWM_CU(cudaMemcpy(bv.data(), b.qkv.b + 2 * inner, inner * sizeof(float), cudaMemcpyDeviceToHost));
+        if (b.to_out.b) LWM_CU(cudaMemcpy(bo.data(), b.to_out.b, hid * sizeof(float), cudaMemcpyDeviceToHost));
+        float* dst = out.data() + l * per;
+        for (size_t o = 0; o < hid; ++o) {
+            std::fill(acc.begin(), acc.end(), 0.0);
+            double bias = bo[o];
+            for (size_t k = 0; k < inner; ++k) {
+                const double a = wo[o * inner + k];
+                const float* row = wv.data() + k * hid;
+                for (size_t i = 0; i < hid; ++i) acc[i] += a * row[i];
+                bias += a * bv[k];
+            }
+            for (size_t i = 0; i < hid; ++i) dst[o * hid + i] = static_cast<float>(acc[i]);
+            dst[hid * hid + o] = static_cast<float>(bias);
+        }
+    }
+    LWM_CU(cudaMalloc(&vo_blob, out.size() * sizeof(float)));
+    LWM_CU(cudaMemcpy(vo_blob, out.data(), out.size() * sizeof(float), cudaMemcpyHostToDevice));
+    for (size_t l = 0; l < w.blocks.size(); ++l) {
+        Lin& vo = w.blocks[l].vo;
+        vo.w = vo_blob + l * per;
+        vo.b = vo_blob + l * per + hid * hid;
+        vo.in = vo.out = static_cast<uint32_t>(hid);
+        vo.wb = nullptr;
+    }
+    return cudaSuccess;
+}
+
 cudaError_t LewmModel::fuse_vit_qkv() {
     if (c.encoder != LWM_ENCODER_VIT || w.vit.empty() || vit_qkv) return cudaSuccess;
     const size_t vh = c.vit_hidden, per = 3 * vh * vh + 3 * vh;

@@ -156,6 +156,7 @@ struct MlpW {
 struct BlockW {
     Norm attn_norm, mlp_norm;
     Lin qkv, to_out, fc1, fc2, ada;
+    Lin vo;  // V rows of qkv folded into to_out (LewmModel::fold_v_out; f32 path, one-token windows)
 };
 struct VitBlockW {
     Norm ln1, ln2;
@@ -215,6 +216,7 @@ struct LewmModel {
     float* blob = nullptr;  // device weights
     uint16_t* blob_bf16 = nullptr;  // bf16 copies of the GEMM weights, each 256-byte aligned
     float* vit_qkv = nullptr;       // the ViT layers' fused query/key/value weights and biases
+    float* vo_blob = nullptr;       // the predictor layers' folded V / out-projection maps
     int precision = LWM_PRECISION_F32;
     // bf16 with the image model's predictor shape: the whole rollout in one
     // launch (lewm_pred_kernel) with its weights packed per CTA rank
@@ -251,6 +253,7 @@ struct LewmModel {
     cudaError_t ensure_split();
     cudaError_t ensure_split_cand();
     cudaError_t fuse_vit_qkv();
+    cudaError_t fold_v_out();
     // LWM_PRECISION_F32: f32 GEMMs; LWM_PRECISION_BF16: bf16 weights and
     // GEMM inputs on the tensor cores, f32 accumulation and activations.
     cudaError_t set_precision(int p, cudaStream_t s);
