@@ -93,6 +93,15 @@ def test_valid_config_then_requires_context():
     assert status == 1 and msg == "null argument"
 
 
+def test_image_control_step_rejects_null_handles():
+    # lwm_lewm_plan_nv12_device checks its arguments before any device work
+    cfg = L.ImagePreprocess.imagenet_224()
+    r = L._PlanDeviceResult()
+    status = L.lib.lwm_lewm_plan_nv12_device(None, None, None, None, 1, 1, 224, 224, 0, C.byref(cfg), None,
+                                              C.byref(r))
+    assert status == 1 and L.lib.lwm_last_error().decode() == "null argument"
+
+
 def test_unsupported_sizes_are_rejected_loudly():
     status, msg = _create_error("mppi", L.MppiConfig(65, 4, 2))
     assert status == 6 and "horizon 65" in msg
